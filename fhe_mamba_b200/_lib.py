@@ -1,0 +1,130 @@
+"""ctypes binding of libfhe_b200.so (the C ABI in include/fhe_b200.h).
+
+The shared library is the product: every call here goes to CUDA kernels.  If
+the library is missing it is built with nvcc; if it cannot be loaded the import
+fails loudly — there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import threading
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libfhe_b200.so")
+HEADER = os.path.join(os.path.dirname(_PKG), "include", "fhe_b200.h")
+
+FHE_OK = 0
+FHE_ERR_INVALID = -1
+FHE_ERR_CUDA = -2
+FHE_ERR_ALLOC = -3
+FHE_ERR_STATE = -4
+FHE_ERR_INTERNAL = -5
+FHE_MEM_HOST = 0
+FHE_MEM_DEVICE = 1
+
+u32 = ctypes.c_uint32
+i32 = ctypes.c_int32
+u64 = ctypes.c_uint64
+f64 = ctypes.c_double
+vp = ctypes.c_void_p
+P64 = ctypes.POINTER(ctypes.c_uint64)
+P32 = ctypes.POINTER(ctypes.c_uint32)
+PD = ctypes.POINTER(ctypes.c_double)
+PI32 = ctypes.POINTER(ctypes.c_int32)
+
+
+class FheError(RuntimeError):
+    """Raised when an fhe_* call returns a negative status."""
+
+    def __init__(self, code: int, fn: str, msg: str):
+        super().__init__(f"{fn} failed ({code}): {msg}")
+        self.code = code
+
+
+class InvalidArgument(FheError, ValueError):
+    pass
+
+
+class StateError(FheError):
+    pass
+
+
+class Params(ctypes.Structure):
+    _fields_ = [
+        ("log_n", u32),
+        ("mult_depth", u32),
+        ("scaling_mod_size", u32),
+        ("first_mod_size", u32),
+        ("num_large_digits", u32),
+        ("batch_size", u32),
+        ("device", i32),
+        ("reserved", u32),
+    ]
+
+
+# name -> (argtypes); all return int status.
+SIGNATURES = {
+    "fhe_last_error": [ctypes.c_char_p, ctypes.c_size_t],
+    "fhe_ctx_create": [ctypes.POINTER(Params), ctypes.POINTER(vp)],
+    "fhe_ctx_create_ntt": [u32, P64, u32, i32, ctypes.POINTER(vp)],
+    "fhe_ctx_destroy": [vp],
+    "fhe_ctx_moduli": [vp, P64, P32, P64, P32],
+    "fhe_gen_ckks_moduli": [u32, u32, u32, u32, u32, P64, P32, P64, P32],
+    "fhe_gen_ntt_primes": [u32, u32, u32, P64],
+    "fhe_ctx_roots": [vp, P64, u32],
+    "fhe_ctx_stream": [vp, ctypes.POINTER(vp)],
+    "fhe_ctx_synchronize": [vp],
+    "fhe_ntt": [vp, P64, u32, u32, u32, ctypes.c_int],
+    "fhe_intt": [vp, P64, u32, u32, u32, ctypes.c_int],
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def header_symbols() -> list[str]:
+    """Names of every function declared in include/fhe_b200.h."""
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*int\s+(fhe_\w+)\s*\(", text, flags=re.M)))
+
+
+def load(build_if_missing: bool = True):
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            if not build_if_missing:
+                raise OSError(f"{LIB_PATH} is missing; run fhe_mamba_b200.build.build()")
+            from . import build as _build
+            _build.build()
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, args in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = ctypes.c_int
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(4096)
+    load().fhe_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(code: int, fn: str) -> None:
+    if code == FHE_OK:
+        return
+    msg = last_error()
+    if code == FHE_ERR_INVALID:
+        raise InvalidArgument(code, fn, msg)
+    if code == FHE_ERR_STATE:
+        raise StateError(code, fn, msg)
+    raise FheError(code, fn, msg)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args), name)

@@ -1,0 +1,460 @@
+// Negacyclic NTT / inverse NTT over RNS limbs for sm_100a.
+//
+// Convention (OpenFHE ChineseRemainderTransformFTTNat, used by FIDESlib's
+// NTT_ / INTT_ kernels): the forward transform takes natural-order
+// coefficients and returns evaluations in bit-reversed order,
+//   out[i] = sum_j a[j] * psi^{(2*brv(i)+1)*j}  (mod q),
+// psi the minimal primitive 2N-th root of unity mod q.  The inverse undoes it
+// exactly, including the 1/N factor.  Outputs are fully reduced to [0, q).
+//
+// Layout: one transform = one limb = N contiguous u64 words; a batch is
+// u64[n_polys][limb_stride][N] where the launch covers limbs
+// [limb0, limb0 + n_limbs) of each poly and limb l uses prime prime0 + l.
+//
+// Structure: N = 2^LA * 2^LB.  The forward transform runs as two passes over
+// HBM.  Pass "cols" performs the first LA Cooley-Tukey stages, which only
+// couple words whose indices agree mod 2^LB (2^LB independent columns of
+// height 2^LA).  Pass "rows" performs the last LB stages, which only couple
+// words inside one contiguous row of 2^LB.  Inside a pass each thread holds
+// R = 2^LR words in registers and runs LR stages there, the block exchanges
+// words once through shared memory, and each thread runs the remaining
+// LS - LR stages on a contiguous run of R words.  The inverse mirrors this
+// (rows first, then columns, Gentleman-Sande butterflies, 1/N folded into the
+// last stage).  Twiddles are read as (w, w') 16-byte pairs.
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "modarith.cuh"
+#include "ntt.h"
+
+namespace fhe {
+namespace {
+
+constexpr int kColsPerCta = 32;  // one column per lane in the column pass
+
+template <int LS>
+struct PassShape {
+  static constexpr int LR = (LS + 1) / 2;  // stages in round 1
+  static constexpr int R = 1 << LR;        // words per thread
+  static constexpr int LT = LS - LR;       // stages in round 2
+  static constexpr int T = 1 << LT;        // threads per sub-problem
+  static constexpr int S = 1 << LS;        // sub-problem size
+};
+
+// Forward Cooley-Tukey (Harvey) butterfly on lazy residues in [0, 4q).
+__device__ __forceinline__ void ct_bfly(uint64_t& x, uint64_t& y, const Twiddle tw, uint64_t q,
+                                        uint64_t q2) {
+  x = csub(x, q2);
+  const uint64_t t = shoup_lazy(y, tw.w, tw.wp, q);
+  y = x + q2 - t;
+  x = x + t;
+}
+
+// Inverse Gentleman-Sande (Harvey) butterfly on residues in [0, 2q).
+__device__ __forceinline__ void gs_bfly(uint64_t& x, uint64_t& y, const Twiddle tw, uint64_t q,
+                                        uint64_t q2) {
+  const uint64_t s = csub(x + y, q2);
+  const uint64_t d = x + q2 - y;
+  x = s;
+  y = shoup_lazy(d, tw.w, tw.wp, q);
+}
+
+__device__ __forceinline__ Twiddle ld_tw(const Twiddle* t, uint32_t i) {
+  const ulonglong2 v = __ldg(reinterpret_cast<const ulonglong2*>(t) + i);
+  return Twiddle{v.x, v.y};
+}
+
+// ---------------------------------------------------------------------------
+// Forward, pass 1: columns.  Column c of the tile (lane) holds words
+// j = col0 + c + 2^LB * k for k in [0, 2^LA).  Warp w is thread t of each
+// column.  Round 1: k = t + T*u.  Round 2: k = R*t + u.
+template <int LA>
+__global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T)
+    ntt_fwd_cols(uint64_t* __restrict__ data, const Twiddle* __restrict__ tw_all,
+                 const uint64_t* __restrict__ primes, int log_n, uint32_t limb_stride,
+                 uint32_t prime0) {
+  using P = PassShape<LA>;
+  extern __shared__ uint64_t smem[];
+  const int LB = log_n - LA;
+  const uint32_t n = 1u << log_n;
+  const uint32_t limb = blockIdx.y;
+  const uint32_t pidx = prime0 + limb;
+  const uint64_t q = primes[pidx], q2 = 2 * q;
+  const Twiddle* tw = tw_all + (size_t)pidx * n;
+  uint64_t* a = data + ((size_t)blockIdx.z * limb_stride + limb) * n;
+  const int c = threadIdx.x & 31;
+  const int t = threadIdx.x >> 5;
+  const uint32_t col = blockIdx.x * kColsPerCta + c;
+
+  uint64_t x[P::R];
+#pragma unroll
+  for (int u = 0; u < P::R; ++u) x[u] = a[col + ((size_t)(t + P::T * u) << LB)];
+
+  // Round 1: register half-distance h <-> k half-distance d = h*T.
+  // Stage m = S/(2d); group i = k/(2d) = u/(2h) (thread independent).
+#pragma unroll
+  for (int h = P::R / 2; h >= 1; h >>= 1) {
+    const int m = P::S / (2 * h * P::T);
+#pragma unroll
+    for (int g = 0; g < P::R; g += 2 * h) {
+      const Twiddle w = ld_tw(tw, m + g / (2 * h));
+#pragma unroll
+      for (int v = 0; v < h; ++v) ct_bfly(x[g + v], x[g + v + h], w, q, q2);
+    }
+  }
+  if constexpr (P::LT > 0) {
+    // Exchange: smem[k][c].
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) smem[(t + P::T * u) * kColsPerCta + c] = x[u];
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) x[u] = smem[(P::R * t + u) * kColsPerCta + c];
+    // Round 2: half-distance h (k units), m = S/(2h), group i = (R*t + g)/(2h).
+#pragma unroll
+    for (int h = P::T / 2; h >= 1; h >>= 1) {
+      const int m = P::S / (2 * h);
+#pragma unroll
+      for (int g = 0; g < P::R; g += 2 * h) {
+        const Twiddle w = ld_tw(tw, m + (P::R * t + g) / (2 * h));
+#pragma unroll
+        for (int v = 0; v < h; ++v) ct_bfly(x[g + v], x[g + v + h], w, q, q2);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) a[col + ((size_t)(P::R * t + u) << LB)] = x[u];
+  } else {
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) a[col + ((size_t)(t + P::T * u) << LB)] = x[u];
+  }
+}
+
+// Padded shared index for the row passes: one spare word per 16 keeps the
+// stride-R reads of round 2 free of bank conflicts.
+__device__ __forceinline__ int rpad(int k) { return k + (k >> 4); }
+
+// ---------------------------------------------------------------------------
+// Forward, pass 2: rows.  A CTA owns ROWS rows of 2^LB contiguous words.  The
+// tile is staged through shared memory in both directions so global loads and
+// stores are contiguous.  Thread t of a row: round 1 k = t + T*u, round 2
+// k = R*t + u.  Final output reduced from [0, 4q) to [0, q).
+template <int LB, int ROWS>
+__global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
+    ntt_fwd_rows(uint64_t* __restrict__ data, const Twiddle* __restrict__ tw_all,
+                 const uint64_t* __restrict__ primes, int log_n, uint32_t limb_stride,
+                 uint32_t prime0) {
+  using P = PassShape<LB>;
+  extern __shared__ uint64_t smem[];
+  constexpr int kRowWords = P::S + P::S / 16;
+  const uint32_t n = 1u << log_n;
+  const uint32_t limb = blockIdx.y;
+  const uint32_t pidx = prime0 + limb;
+  const uint64_t q = primes[pidx], q2 = 2 * q;
+  const Twiddle* tw = tw_all + (size_t)pidx * n;
+  uint64_t* a = data + ((size_t)blockIdx.z * limb_stride + limb) * n +
+                (size_t)blockIdx.x * ROWS * P::S;
+  const int t = threadIdx.x % P::T;
+  const int rr = threadIdx.x / P::T;
+  const uint32_t row = blockIdx.x * ROWS + rr;
+
+  // Coalesced tile load: ROWS*S contiguous words.
+  constexpr int kThreads = ROWS * P::T;
+  for (int i = threadIdx.x; i < ROWS * P::S / 2; i += kThreads) {
+    const ulonglong2 v = reinterpret_cast<const ulonglong2*>(a)[i];
+    const int w = 2 * i, r = w / P::S, k = w % P::S;
+    smem[r * kRowWords + rpad(k)] = v.x;
+    smem[r * kRowWords + rpad(k + 1)] = v.y;
+  }
+  __syncthreads();
+  uint64_t x[P::R];
+  uint64_t* srow = smem + rr * kRowWords;
+#pragma unroll
+  for (int u = 0; u < P::R; ++u) x[u] = srow[rpad(t + P::T * u)];
+
+  // Global stage for k-half-distance d: m = N/(2d); i = row*S/(2d) + k/(2d).
+#pragma unroll
+  for (int h = P::R / 2; h >= 1; h >>= 1) {
+    const int d = h * P::T;
+    const uint32_t m = n / (2 * d);
+    const uint32_t base = m + row * (P::S / (2 * d));
+#pragma unroll
+    for (int g = 0; g < P::R; g += 2 * h) {
+      const Twiddle w = ld_tw(tw, base + g / (2 * h));
+#pragma unroll
+      for (int v = 0; v < h; ++v) ct_bfly(x[g + v], x[g + v + h], w, q, q2);
+    }
+  }
+  if constexpr (P::LT > 0) {
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) srow[rpad(t + P::T * u)] = x[u];
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) x[u] = srow[rpad(P::R * t + u)];
+#pragma unroll
+    for (int h = P::T / 2; h >= 1; h >>= 1) {
+      const uint32_t m = n / (2 * h);
+      const uint32_t base = m + row * (P::S / (2 * h));
+#pragma unroll
+      for (int g = 0; g < P::R; g += 2 * h) {
+        const Twiddle w = ld_tw(tw, base + (P::R * t + g) / (2 * h));
+#pragma unroll
+        for (int v = 0; v < h; ++v) ct_bfly(x[g + v], x[g + v + h], w, q, q2);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) srow[rpad(P::R * t + u)] = csub(csub(x[u], q2), q);
+  } else {
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) srow[rpad(t + P::T * u)] = csub(csub(x[u], q2), q);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < ROWS * P::S / 2; i += kThreads) {
+    const int w = 2 * i, r = w / P::S, k = w % P::S;
+    ulonglong2 v;
+    v.x = smem[r * kRowWords + rpad(k)];
+    v.y = smem[r * kRowWords + rpad(k + 1)];
+    reinterpret_cast<ulonglong2*>(a)[i] = v;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Inverse, pass 1: rows (stages with half-distance 1 .. 2^(LB-1)).
+// Round 1 on contiguous runs k = R*t + u (half-distances 1 .. T/2), exchange,
+// round 2 on k = t + T*u (half-distances T .. S/2).  Input in [0, q).
+template <int LB, int ROWS>
+__global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
+    ntt_inv_rows(uint64_t* __restrict__ data, const Twiddle* __restrict__ tw_all,
+                 const uint64_t* __restrict__ primes, int log_n, uint32_t limb_stride,
+                 uint32_t prime0) {
+  using P = PassShape<LB>;
+  extern __shared__ uint64_t smem[];
+  constexpr int kRowWords = P::S + P::S / 16;
+  const uint32_t n = 1u << log_n;
+  const uint32_t limb = blockIdx.y;
+  const uint32_t pidx = prime0 + limb;
+  const uint64_t q = primes[pidx], q2 = 2 * q;
+  const Twiddle* tw = tw_all + (size_t)pidx * n;
+  uint64_t* a = data + ((size_t)blockIdx.z * limb_stride + limb) * n +
+                (size_t)blockIdx.x * ROWS * P::S;
+  const int t = threadIdx.x % P::T;
+  const int rr = threadIdx.x / P::T;
+  const uint32_t row = blockIdx.x * ROWS + rr;
+  constexpr int kThreads = ROWS * P::T;
+
+  for (int i = threadIdx.x; i < ROWS * P::S / 2; i += kThreads) {
+    const ulonglong2 v = reinterpret_cast<const ulonglong2*>(a)[i];
+    const int w = 2 * i, r = w / P::S, k = w % P::S;
+    smem[r * kRowWords + rpad(k)] = v.x;
+    smem[r * kRowWords + rpad(k + 1)] = v.y;
+  }
+  __syncthreads();
+  uint64_t x[P::R];
+  uint64_t* srow = smem + rr * kRowWords;
+  if constexpr (P::LT > 0) {
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) x[u] = srow[rpad(P::R * t + u)];
+#pragma unroll
+    for (int h = 1; h <= P::T / 2; h <<= 1) {
+      const uint32_t m = n / (2 * h);
+      const uint32_t base = m + row * (P::S / (2 * h));
+#pragma unroll
+      for (int g = 0; g < P::R; g += 2 * h) {
+        const Twiddle w = ld_tw(tw, base + (P::R * t + g) / (2 * h));
+#pragma unroll
+        for (int v = 0; v < h; ++v) gs_bfly(x[g + v], x[g + v + h], w, q, q2);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) srow[rpad(P::R * t + u)] = x[u];
+    __syncthreads();
+  }
+#pragma unroll
+  for (int u = 0; u < P::R; ++u) x[u] = srow[rpad(t + P::T * u)];
+#pragma unroll
+  for (int h = 1; h <= P::R / 2; h <<= 1) {
+    const int d = h * P::T;
+    const uint32_t m = n / (2 * d);
+    const uint32_t base = m + row * (P::S / (2 * d));
+#pragma unroll
+    for (int g = 0; g < P::R; g += 2 * h) {
+      const Twiddle w = ld_tw(tw, base + g / (2 * h));
+#pragma unroll
+      for (int v = 0; v < h; ++v) gs_bfly(x[g + v], x[g + v + h], w, q, q2);
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int u = 0; u < P::R; ++u) srow[rpad(t + P::T * u)] = x[u];
+  __syncthreads();
+  for (int i = threadIdx.x; i < ROWS * P::S / 2; i += kThreads) {
+    const int w = 2 * i, r = w / P::S, k = w % P::S;
+    ulonglong2 v;
+    v.x = smem[r * kRowWords + rpad(k)];
+    v.y = smem[r * kRowWords + rpad(k + 1)];
+    reinterpret_cast<ulonglong2*>(a)[i] = v;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Inverse, pass 2: columns (half-distances 2^LB .. N/2).  Round 1 on
+// k = R*t + u (k half-distances 1 .. T/2), exchange, round 2 on k = t + T*u.
+// The last stage (m = 1) folds in N^{-1}: x' = (x+y)/N, y' = (x-y)*w/N, with
+// tw_last = (N^{-1}, N^{-1}') and tw_last2 = (w_1 N^{-1}, ...).
+template <int LA>
+__global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T)
+    ntt_inv_cols(uint64_t* __restrict__ data, const Twiddle* __restrict__ tw_all,
+                 const uint64_t* __restrict__ primes, const Twiddle* __restrict__ ninv_all,
+                 int log_n, uint32_t limb_stride, uint32_t prime0) {
+  using P = PassShape<LA>;
+  extern __shared__ uint64_t smem[];
+  const int LB = log_n - LA;
+  const uint32_t n = 1u << log_n;
+  const uint32_t limb = blockIdx.y;
+  const uint32_t pidx = prime0 + limb;
+  const uint64_t q = primes[pidx], q2 = 2 * q;
+  const Twiddle* tw = tw_all + (size_t)pidx * n;
+  uint64_t* a = data + ((size_t)blockIdx.z * limb_stride + limb) * n;
+  const int c = threadIdx.x & 31;
+  const int t = threadIdx.x >> 5;
+  const uint32_t col = blockIdx.x * kColsPerCta + c;
+  uint64_t x[P::R];
+
+  if constexpr (P::LT > 0) {
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) x[u] = a[col + ((size_t)(P::R * t + u) << LB)];
+#pragma unroll
+    for (int h = 1; h <= P::T / 2; h <<= 1) {
+      const int m = P::S / (2 * h);
+#pragma unroll
+      for (int g = 0; g < P::R; g += 2 * h) {
+        const Twiddle w = ld_tw(tw, m + (P::R * t + g) / (2 * h));
+#pragma unroll
+        for (int v = 0; v < h; ++v) gs_bfly(x[g + v], x[g + v + h], w, q, q2);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) smem[(P::R * t + u) * kColsPerCta + c] = x[u];
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) x[u] = smem[(t + P::T * u) * kColsPerCta + c];
+  } else {
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) x[u] = a[col + ((size_t)(t + P::T * u) << LB)];
+  }
+#pragma unroll
+  for (int h = 1; h < P::R / 2; h <<= 1) {
+    const int m = P::S / (2 * h * P::T);
+#pragma unroll
+    for (int g = 0; g < P::R; g += 2 * h) {
+      const Twiddle w = ld_tw(tw, m + g / (2 * h));
+#pragma unroll
+      for (int v = 0; v < h; ++v) gs_bfly(x[g + v], x[g + v + h], w, q, q2);
+    }
+  }
+  {  // last stage, m = 1, half-distance R/2 in registers, 1/N folded in.
+    const Twiddle ni = ninv_all[2 * pidx];
+    const Twiddle wn = ninv_all[2 * pidx + 1];
+    constexpr int h = P::R / 2;
+#pragma unroll
+    for (int v = 0; v < h; ++v) {
+      const uint64_t s = x[v] + x[v + h];  // < 4q
+      const uint64_t d = x[v] + q2 - x[v + h];
+      x[v] = csub(shoup_lazy(s, ni.w, ni.wp, q), q);
+      x[v + h] = csub(shoup_lazy(d, wn.w, wn.wp, q), q);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < P::R; ++u) a[col + ((size_t)(t + P::T * u) << LB)] = x[u];
+}
+
+constexpr int kRowsPerCta = 32;
+
+template <int LB>
+size_t rows_smem() {
+  using P = PassShape<LB>;
+  return (size_t)kRowsPerCta * (P::S + P::S / 16) * sizeof(uint64_t);
+}
+template <int LA>
+size_t cols_smem() {
+  using P = PassShape<LA>;
+  return P::LT > 0 ? (size_t)kColsPerCta * P::S * sizeof(uint64_t) : 0;
+}
+
+template <int LA, int LB>
+cudaError_t launch_fwd(const NttArgs& g) {
+  using PA = PassShape<LA>;
+  using PB = PassShape<LB>;
+  const int log_n = LA + LB;
+  const size_t sa = cols_smem<LA>(), sb = rows_smem<LB>();
+  cudaError_t e;
+  e = cudaFuncSetAttribute(ntt_fwd_cols<LA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(ntt_fwd_rows<LB, kRowsPerCta>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
+  if (e != cudaSuccess) return e;
+  dim3 ga((1u << LB) / kColsPerCta, g.n_limbs, g.n_polys);
+  ntt_fwd_cols<LA><<<ga, kColsPerCta * PA::T, sa, g.stream>>>(g.data, g.tw, g.primes, log_n,
+                                                              g.limb_stride, g.prime0);
+  dim3 gb((1u << LA) / kRowsPerCta, g.n_limbs, g.n_polys);
+  ntt_fwd_rows<LB, kRowsPerCta><<<gb, kRowsPerCta * PB::T, sb, g.stream>>>(
+      g.data, g.tw, g.primes, log_n, g.limb_stride, g.prime0);
+  return cudaGetLastError();
+}
+
+template <int LA, int LB>
+cudaError_t launch_inv(const NttArgs& g) {
+  using PA = PassShape<LA>;
+  using PB = PassShape<LB>;
+  const int log_n = LA + LB;
+  const size_t sa = cols_smem<LA>(), sb = rows_smem<LB>();
+  cudaError_t e;
+  e = cudaFuncSetAttribute(ntt_inv_cols<LA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(ntt_inv_rows<LB, kRowsPerCta>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
+  if (e != cudaSuccess) return e;
+  dim3 gb((1u << LA) / kRowsPerCta, g.n_limbs, g.n_polys);
+  ntt_inv_rows<LB, kRowsPerCta><<<gb, kRowsPerCta * PB::T, sb, g.stream>>>(
+      g.data, g.tw_inv, g.primes, log_n, g.limb_stride, g.prime0);
+  dim3 ga((1u << LB) / kColsPerCta, g.n_limbs, g.n_polys);
+  ntt_inv_cols<LA><<<ga, kColsPerCta * PA::T, sa, g.stream>>>(
+      g.data, g.tw_inv, g.primes, g.ninv, log_n, g.limb_stride, g.prime0);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// log N = LA + LB with LA = floor(logN/2) >= 5 so both passes have >= 32
+// columns / rows per CTA tile.
+cudaError_t ntt_forward(const NttArgs& g) {
+  if (g.n_limbs == 0 || g.n_polys == 0) return cudaSuccess;
+  switch (g.log_n) {
+    case 10: return launch_fwd<5, 5>(g);
+    case 11: return launch_fwd<5, 6>(g);
+    case 12: return launch_fwd<6, 6>(g);
+    case 13: return launch_fwd<6, 7>(g);
+    case 14: return launch_fwd<7, 7>(g);
+    case 15: return launch_fwd<7, 8>(g);
+    case 16: return launch_fwd<8, 8>(g);
+    case 17: return launch_fwd<8, 9>(g);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t ntt_inverse(const NttArgs& g) {
+  if (g.n_limbs == 0 || g.n_polys == 0) return cudaSuccess;
+  switch (g.log_n) {
+    case 10: return launch_inv<5, 5>(g);
+    case 11: return launch_inv<5, 6>(g);
+    case 12: return launch_inv<6, 6>(g);
+    case 13: return launch_inv<6, 7>(g);
+    case 14: return launch_inv<7, 7>(g);
+    case 15: return launch_inv<7, 8>(g);
+    case 16: return launch_inv<8, 8>(g);
+    case 17: return launch_inv<8, 9>(g);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace fhe

@@ -1,0 +1,27 @@
+// Launch interface of the RNS NTT kernels (ntt.cu).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "modarith.cuh"
+
+namespace fhe {
+
+struct NttArgs {
+  uint64_t* data;          // u64[n_polys][limb_stride][N], first launched limb at data
+  const Twiddle* tw;       // forward tables, Twiddle[n_primes][N]: psi^{brv(i)}
+  const Twiddle* tw_inv;   // inverse tables: psi^{-brv(i)}
+  const uint64_t* primes;  // u64[n_primes]
+  const Twiddle* ninv;     // per prime: (N^{-1}, .), (psi^{-brv(1)} N^{-1}, .)
+  int log_n;
+  uint32_t n_polys;
+  uint32_t n_limbs;
+  uint32_t limb_stride;    // limbs between consecutive polys
+  uint32_t prime0;         // prime index of the first launched limb
+  cudaStream_t stream;
+};
+
+cudaError_t ntt_forward(const NttArgs& args);
+cudaError_t ntt_inverse(const NttArgs& args);
+
+}  // namespace fhe

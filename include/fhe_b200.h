@@ -1,0 +1,120 @@
+/*
+ * fhe_b200 — C ABI of the B200-native RNS-CKKS evaluation backend.
+ *
+ * This is the drop-in boundary for the reference's native FIDESlib/OpenFHE
+ * stage (fhe-mamba: native/fideslib_stage0).  Every entry point:
+ *   - returns int status: FHE_OK (0) or a negative FHE_ERR_* code; the message
+ *     of the last failure on the calling thread is read with fhe_last_error();
+ *   - never throws across the ABI;
+ *   - takes plain pointers and sizes (no C++ or torch types);
+ *   - is single-threaded per context: one context owns one CUDA stream on one
+ *     device, and all device work of the context is ordered on that stream.
+ * Handles are opaque, owned by the caller and freed explicitly.
+ *
+ * Residue layout (device and host buffers alike): limb-major
+ * u64[n_polys][n_limbs][N], each limb a full length-N residue polynomial.
+ */
+#ifndef FHE_B200_H
+#define FHE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FHE_OK 0
+#define FHE_ERR_INVALID (-1)   /* bad argument, shape or handle */
+#define FHE_ERR_CUDA (-2)      /* CUDA runtime or kernel launch failure */
+#define FHE_ERR_ALLOC (-3)     /* device or host allocation failure */
+#define FHE_ERR_STATE (-4)     /* missing key, level underflow, scale mismatch */
+#define FHE_ERR_INTERNAL (-5)  /* unexpected exception */
+
+#define FHE_MEM_HOST 0         /* pointer is host memory (pageable or pinned) */
+#define FHE_MEM_DEVICE 1       /* pointer is device memory of the context's GPU */
+
+typedef struct fhe_ctx fhe_ctx;
+
+/* CKKS context parameters.  Mirrors the reference's CCParams calls
+ * (native/fideslib_stage0/src/packed_fideslib.cpp:1060-1068:
+ *  SetRingDim, SetMultiplicativeDepth, SetScalingModSize, SetFirstModSize,
+ *  SetScalingTechnique(FLEXIBLEAUTO), SetKeySwitchTechnique(HYBRID),
+ *  SetNumLargeDigits, SetBatchSize, SetSecretKeyDist(UNIFORM_TERNARY)). */
+typedef struct fhe_params {
+  uint32_t log_n;             /* ring dimension N = 2^log_n, 10 <= log_n <= 17 */
+  uint32_t mult_depth;        /* number of Q primes = mult_depth + 1 */
+  uint32_t scaling_mod_size;  /* bits of the scaling primes */
+  uint32_t first_mod_size;    /* bits of q_0 (must differ from scaling_mod_size) */
+  uint32_t num_large_digits;  /* dnum of HYBRID key switching */
+  uint32_t batch_size;        /* slots (<= N/2, power of two) */
+  int32_t device;             /* CUDA device ordinal */
+  uint32_t reserved;
+} fhe_params;
+
+/* --- context ------------------------------------------------------------ */
+
+/* Replaces GenCryptoContext(CCParams) + LoadContext (packed_fideslib.cpp:1068,1090):
+ * generates the FLEXIBLEAUTO Q chain and HYBRID P primes the way OpenFHE
+ * v1.4.2 does, their minimal primitive 2N-th roots, and uploads all NTT,
+ * basis-conversion and rescale tables to the device. */
+int fhe_ctx_create(const fhe_params* params, fhe_ctx** out);
+
+/* NTT-only context on an explicit prime list (q_i = 1 mod 2N, q_i < 2^62);
+ * replaces the FIDESlib Context the NTT probe builds
+ * (experiments/ntt_warp_tail/probe.cu:93-104) for raw limb transforms. */
+int fhe_ctx_create_ntt(uint32_t log_n, const uint64_t* primes, uint32_t n_primes,
+                       int32_t device, fhe_ctx** out);
+
+int fhe_ctx_destroy(fhe_ctx* ctx);
+
+/* Copies the Q primes (n_q written) and P primes (n_p written); either array
+ * may be NULL to query only the counts.  Replaces the probe's
+ * gpu->prime[i].p / gpu->specialPrime[i].p reads (probe.cu:124-140). */
+int fhe_ctx_moduli(const fhe_ctx* ctx, uint64_t* q, uint32_t* n_q, uint64_t* p, uint32_t* n_p);
+
+/* Host-only parameter generation (no device work).  Writes the FLEXIBLEAUTO Q
+ * chain (mult_depth + 1 primes) and the HYBRID P primes that fhe_ctx_create
+ * would use; q/p may be NULL to query counts (q needs >= mult_depth + 1 slots,
+ * p >= 64).  Same rule as OpenFHE v1.4.2 ParamsGenCKKSRNS, as the reference's
+ * context set-up invokes it (packed_fideslib.cpp:1060-1068). */
+int fhe_gen_ckks_moduli(uint32_t log_n, uint32_t mult_depth, uint32_t scaling_mod_size,
+                        uint32_t first_mod_size, uint32_t num_large_digits,
+                        uint64_t* q, uint32_t* n_q, uint64_t* p, uint32_t* n_p);
+
+/* Host-only: the `count` largest primes q < 2^bits with q = 1 mod 2N, in
+ * descending order (the NTT microbench prime set of BASELINE config 2). */
+int fhe_gen_ntt_primes(uint32_t log_n, uint32_t bits, uint32_t count, uint64_t* out);
+
+/* Minimal primitive 2N-th roots of unity, one per prime (Q then P). */
+int fhe_ctx_roots(const fhe_ctx* ctx, uint64_t* roots, uint32_t n);
+
+/* The context's cudaStream_t (as void*), for callers that time or order work. */
+int fhe_ctx_stream(const fhe_ctx* ctx, void** stream);
+
+/* Blocks until all work queued on the context's stream has finished. */
+int fhe_ctx_synchronize(fhe_ctx* ctx);
+
+/* Copies the calling thread's last error message (NUL-terminated). */
+int fhe_last_error(char* buf, size_t len);
+
+/* --- raw limb transforms (BASELINE config 2 microbench) ------------------ */
+
+/* Forward negacyclic NTT, OpenFHE order (natural coefficients in, bit-reversed
+ * evaluations out, minimal psi), in place on u64[n_polys][n_limbs][N]; limb l
+ * uses prime limb0 + l.  Inputs must be reduced (< q).  mem = FHE_MEM_HOST
+ * copies the buffer to the device and back inside the call.  Replaces FIDESlib
+ * NTT_<*, ALGO_SHOUP, NTT_NONE> launched as in probe.cu:57-64 and
+ * RNSPoly::NTT (src/fideslib_plaintext_encoder.cpp:264,410). */
+int fhe_ntt(fhe_ctx* ctx, uint64_t* data, uint32_t n_polys, uint32_t limb0,
+            uint32_t n_limbs, int mem);
+
+/* Inverse of fhe_ntt (bit-reversed evaluations in, coefficients out, 1/N
+ * applied).  Replaces FIDESlib INTT_ / RNSPoly::INTT. */
+int fhe_intt(fhe_ctx* ctx, uint64_t* data, uint32_t n_polys, uint32_t limb0,
+             uint32_t n_limbs, int mem);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
