@@ -69,7 +69,7 @@ __device__ __forceinline__ Twiddle ld_tw(const Twiddle* t, uint32_t i) {
 // j = col0 + c + 2^LB * k for k in [0, 2^LA).  Warp w is thread t of each
 // column.  Round 1: k = t + T*u.  Round 2: k = R*t + u.
 template <int LA>
-__global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T)
+__global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA >= 8 ? 1 : 2)
     ntt_fwd_cols(uint64_t* __restrict__ data, const Twiddle* __restrict__ tw_all,
                  const uint64_t* __restrict__ primes, int log_n, uint32_t limb_stride,
                  uint32_t prime0) {
@@ -77,11 +77,11 @@ __global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T)
   extern __shared__ uint64_t smem[];
   const int LB = log_n - LA;
   const uint32_t n = 1u << log_n;
-  const uint32_t limb = blockIdx.y;
+  const uint32_t limb = blockIdx.z;
   const uint32_t pidx = prime0 + limb;
   const uint64_t q = primes[pidx], q2 = 2 * q;
   const Twiddle* tw = tw_all + (size_t)pidx * n;
-  uint64_t* a = data + ((size_t)blockIdx.z * limb_stride + limb) * n;
+  uint64_t* a = data + ((size_t)blockIdx.y * limb_stride + limb) * n;
   const int c = threadIdx.x & 31;
   const int t = threadIdx.x >> 5;
   const uint32_t col = blockIdx.x * kColsPerCta + c;
@@ -146,11 +146,11 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
   extern __shared__ uint64_t smem[];
   constexpr int kRowWords = P::S + P::S / 16;
   const uint32_t n = 1u << log_n;
-  const uint32_t limb = blockIdx.y;
+  const uint32_t limb = blockIdx.z;
   const uint32_t pidx = prime0 + limb;
   const uint64_t q = primes[pidx], q2 = 2 * q;
   const Twiddle* tw = tw_all + (size_t)pidx * n;
-  uint64_t* a = data + ((size_t)blockIdx.z * limb_stride + limb) * n +
+  uint64_t* a = data + ((size_t)blockIdx.y * limb_stride + limb) * n +
                 (size_t)blockIdx.x * ROWS * P::S;
   const int t = threadIdx.x % P::T;
   const int rr = threadIdx.x / P::T;
@@ -231,11 +231,11 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
   extern __shared__ uint64_t smem[];
   constexpr int kRowWords = P::S + P::S / 16;
   const uint32_t n = 1u << log_n;
-  const uint32_t limb = blockIdx.y;
+  const uint32_t limb = blockIdx.z;
   const uint32_t pidx = prime0 + limb;
   const uint64_t q = primes[pidx], q2 = 2 * q;
   const Twiddle* tw = tw_all + (size_t)pidx * n;
-  uint64_t* a = data + ((size_t)blockIdx.z * limb_stride + limb) * n +
+  uint64_t* a = data + ((size_t)blockIdx.y * limb_stride + limb) * n +
                 (size_t)blockIdx.x * ROWS * P::S;
   const int t = threadIdx.x % P::T;
   const int rr = threadIdx.x / P::T;
@@ -302,7 +302,7 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
 // The last stage (m = 1) folds in N^{-1}: x' = (x+y)/N, y' = (x-y)*w/N, with
 // tw_last = (N^{-1}, N^{-1}') and tw_last2 = (w_1 N^{-1}, ...).
 template <int LA>
-__global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T)
+__global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA >= 8 ? 1 : 2)
     ntt_inv_cols(uint64_t* __restrict__ data, const Twiddle* __restrict__ tw_all,
                  const uint64_t* __restrict__ primes, const Twiddle* __restrict__ ninv_all,
                  int log_n, uint32_t limb_stride, uint32_t prime0) {
@@ -310,11 +310,11 @@ __global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T)
   extern __shared__ uint64_t smem[];
   const int LB = log_n - LA;
   const uint32_t n = 1u << log_n;
-  const uint32_t limb = blockIdx.y;
+  const uint32_t limb = blockIdx.z;
   const uint32_t pidx = prime0 + limb;
   const uint64_t q = primes[pidx], q2 = 2 * q;
   const Twiddle* tw = tw_all + (size_t)pidx * n;
-  uint64_t* a = data + ((size_t)blockIdx.z * limb_stride + limb) * n;
+  uint64_t* a = data + ((size_t)blockIdx.y * limb_stride + limb) * n;
   const int c = threadIdx.x & 31;
   const int t = threadIdx.x >> 5;
   const uint32_t col = blockIdx.x * kColsPerCta + c;
@@ -393,10 +393,10 @@ cudaError_t launch_fwd(const NttArgs& g) {
   e = cudaFuncSetAttribute(ntt_fwd_rows<LB, kRowsPerCta>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
   if (e != cudaSuccess) return e;
-  dim3 ga((1u << LB) / kColsPerCta, g.n_limbs, g.n_polys);
+  dim3 ga((1u << LB) / kColsPerCta, g.n_polys, g.n_limbs);
   ntt_fwd_cols<LA><<<ga, kColsPerCta * PA::T, sa, g.stream>>>(g.data, g.tw, g.primes, log_n,
                                                               g.limb_stride, g.prime0);
-  dim3 gb((1u << LA) / kRowsPerCta, g.n_limbs, g.n_polys);
+  dim3 gb((1u << LA) / kRowsPerCta, g.n_polys, g.n_limbs);
   ntt_fwd_rows<LB, kRowsPerCta><<<gb, kRowsPerCta * PB::T, sb, g.stream>>>(
       g.data, g.tw, g.primes, log_n, g.limb_stride, g.prime0);
   return cudaGetLastError();
@@ -414,10 +414,10 @@ cudaError_t launch_inv(const NttArgs& g) {
   e = cudaFuncSetAttribute(ntt_inv_rows<LB, kRowsPerCta>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
   if (e != cudaSuccess) return e;
-  dim3 gb((1u << LA) / kRowsPerCta, g.n_limbs, g.n_polys);
+  dim3 gb((1u << LA) / kRowsPerCta, g.n_polys, g.n_limbs);
   ntt_inv_rows<LB, kRowsPerCta><<<gb, kRowsPerCta * PB::T, sb, g.stream>>>(
       g.data, g.tw_inv, g.primes, log_n, g.limb_stride, g.prime0);
-  dim3 ga((1u << LB) / kColsPerCta, g.n_limbs, g.n_polys);
+  dim3 ga((1u << LB) / kColsPerCta, g.n_polys, g.n_limbs);
   ntt_inv_cols<LA><<<ga, kColsPerCta * PA::T, sa, g.stream>>>(
       g.data, g.tw_inv, g.primes, g.ninv, log_n, g.limb_stride, g.prime0);
   return cudaGetLastError();
