@@ -3,12 +3,11 @@
  * and the counter-based sampler.  TEST INFRASTRUCTURE ONLY (see ckks_oracle.h).
  */
 #include "ckks_oracle.h"
+#include "oracle_internal.h"
 
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
-
-typedef unsigned __int128 u128;
 
 uint64_t oc_mulmod(uint64_t a, uint64_t b, uint64_t q) {
   return (uint64_t)(((u128)a * b) % q);
@@ -194,25 +193,20 @@ uint64_t oc_root_of_unity(uint64_t m, uint64_t q) {
   return best;
 }
 
-static uint32_t bitrev(uint32_t x, uint32_t bits) {
+uint32_t oi_bitrev(uint32_t x, uint32_t bits) {
   uint32_t r = 0;
   for (uint32_t i = 0; i < bits; ++i) { r = (r << 1) | (x & 1); x >>= 1; }
   return r;
 }
 
-typedef struct {
-  uint64_t* w;   /* w[i] = root^{bitrev(i)} */
-  uint64_t* wp;  /* Shoup companion floor(w * 2^64 / q) */
-} twiddles_t;
-
-static twiddles_t make_table(uint32_t log_n, uint64_t q, uint64_t root) {
+twiddles_t oi_make_table(uint32_t log_n, uint64_t q, uint64_t root) {
   const uint32_t n = 1u << log_n;
   twiddles_t t;
   t.w = (uint64_t*)malloc(sizeof(uint64_t) * n);
   t.wp = (uint64_t*)malloc(sizeof(uint64_t) * n);
   uint64_t x = 1;
   for (uint32_t i = 0; i < n; ++i) {
-    uint32_t r = bitrev(i, log_n);
+    uint32_t r = oi_bitrev(i, log_n);
     t.w[r] = x;
     t.wp[r] = (uint64_t)(((u128)x << 64) / q);
     x = oc_mulmod(x, root, q);
@@ -220,25 +214,20 @@ static twiddles_t make_table(uint32_t log_n, uint64_t q, uint64_t root) {
   return t;
 }
 
-static void free_table(twiddles_t* t) { free(t->w); free(t->wp); }
+void oi_free_table(twiddles_t* t) { free(t->w); free(t->wp); }
 
-static inline uint64_t mul_shoup(uint64_t x, uint64_t w, uint64_t wp, uint64_t q) {
-  uint64_t hi = (uint64_t)(((u128)x * wp) >> 64);
-  uint64_t r = x * w - hi * q;
-  return r >= q ? r - q : r;
-}
 
 /* OpenFHE ChineseRemainderTransformFTTNat::ForwardTransformToBitReverseInPlace:
  * Cooley-Tukey, natural-order input, bit-reversed output, table psi^{brv(i)}.
  * Output word i is a(psi^{2*brv(i)+1}) mod q. */
-static void ntt_fwd_table(uint64_t* a, uint32_t log_n, uint64_t q, const twiddles_t* t) {
+void oi_ntt_fwd_table(uint64_t* a, uint32_t log_n, uint64_t q, const twiddles_t* t) {
   const uint32_t n = 1u << log_n;
   for (uint32_t m = 1, h = n >> 1; m < n; m <<= 1, h >>= 1) {
     for (uint32_t i = 0; i < m; ++i) {
       const uint64_t w = t->w[m + i], wp = t->wp[m + i];
       for (uint32_t j = 2 * i * h; j < 2 * i * h + h; ++j) {
         uint64_t u = a[j];
-        uint64_t v = mul_shoup(a[j + h], w, wp, q);
+        uint64_t v = oi_mul_shoup(a[j + h], w, wp, q);
         uint64_t s = u + v;
         a[j] = s >= q ? s - q : s;
         a[j + h] = u >= v ? u - v : u + q - v;
@@ -249,7 +238,7 @@ static void ntt_fwd_table(uint64_t* a, uint32_t log_n, uint64_t q, const twiddle
 
 /* OpenFHE InverseTransformFromBitReverseInPlace: Gentleman-Sande with
  * psi^{-brv(i)}, then a multiply by N^{-1}. */
-static void ntt_inv_table(uint64_t* a, uint32_t log_n, uint64_t q, const twiddles_t* t) {
+void oi_ntt_inv_table(uint64_t* a, uint32_t log_n, uint64_t q, const twiddles_t* t) {
   const uint32_t n = 1u << log_n;
   for (uint32_t m = n >> 1, h = 1; m >= 1; m >>= 1, h <<= 1) {
     for (uint32_t i = 0; i < m; ++i) {
@@ -258,25 +247,25 @@ static void ntt_inv_table(uint64_t* a, uint32_t log_n, uint64_t q, const twiddle
         uint64_t u = a[j], v = a[j + h];
         uint64_t s = u + v;
         a[j] = s >= q ? s - q : s;
-        a[j + h] = mul_shoup(u >= v ? u - v : u + q - v, w, wp, q);
+        a[j + h] = oi_mul_shoup(u >= v ? u - v : u + q - v, w, wp, q);
       }
     }
   }
   const uint64_t ninv = oc_invmod(n % q, q);
   const uint64_t ninvp = (uint64_t)(((u128)ninv << 64) / q);
-  for (uint32_t j = 0; j < n; ++j) a[j] = mul_shoup(a[j], ninv, ninvp, q);
+  for (uint32_t j = 0; j < n; ++j) a[j] = oi_mul_shoup(a[j], ninv, ninvp, q);
 }
 
 void oc_ntt_forward(uint64_t* a, uint32_t log_n, uint64_t q, uint64_t psi) {
-  twiddles_t t = make_table(log_n, q, psi);
-  ntt_fwd_table(a, log_n, q, &t);
-  free_table(&t);
+  twiddles_t t = oi_make_table(log_n, q, psi);
+  oi_ntt_fwd_table(a, log_n, q, &t);
+  oi_free_table(&t);
 }
 
 void oc_ntt_inverse(uint64_t* a, uint32_t log_n, uint64_t q, uint64_t psi) {
-  twiddles_t t = make_table(log_n, q, oc_invmod(psi, q));
-  ntt_inv_table(a, log_n, q, &t);
-  free_table(&t);
+  twiddles_t t = oi_make_table(log_n, q, oc_invmod(psi, q));
+  oi_ntt_inv_table(a, log_n, q, &t);
+  oi_free_table(&t);
 }
 
 void oc_ntt_batch(uint64_t* data, uint32_t n_polys, uint32_t n_limbs,
@@ -285,16 +274,16 @@ void oc_ntt_batch(uint64_t* data, uint32_t n_polys, uint32_t n_limbs,
   const uint64_t n = (uint64_t)1 << log_n;
   twiddles_t* tabs = (twiddles_t*)malloc(sizeof(twiddles_t) * n_limbs);
   for (uint32_t l = 0; l < n_limbs; ++l)
-    tabs[l] = make_table(log_n, q[l], inverse ? oc_invmod(psi[l], q[l]) : psi[l]);
+    tabs[l] = oi_make_table(log_n, q[l], inverse ? oc_invmod(psi[l], q[l]) : psi[l]);
   const long total = (long)n_polys * n_limbs;
 #pragma omp parallel for schedule(dynamic, 1) num_threads(threads > 0 ? threads : 1)
   for (long k = 0; k < total; ++k) {
     const uint32_t l = (uint32_t)(k % n_limbs);
     uint64_t* a = data + (uint64_t)k * n;
-    if (inverse) ntt_inv_table(a, log_n, q[l], &tabs[l]);
-    else ntt_fwd_table(a, log_n, q[l], &tabs[l]);
+    if (inverse) oi_ntt_inv_table(a, log_n, q[l], &tabs[l]);
+    else oi_ntt_fwd_table(a, log_n, q[l], &tabs[l]);
   }
-  for (uint32_t l = 0; l < n_limbs; ++l) free_table(&tabs[l]);
+  for (uint32_t l = 0; l < n_limbs; ++l) oi_free_table(&tabs[l]);
   free(tabs);
 }
 
