@@ -5,6 +5,8 @@ libfhe_b200.so (hand-written sm_100a CUDA); this package only marshals
 arguments and raises on error statuses.
 """
 from ._lib import FheError, InvalidArgument, StateError, load  # noqa: F401
+from .ckks import CCParams, Ciphertext, CryptoContext, GenCryptoContext, Plaintext  # noqa: F401
 from .ntt import NttContext  # noqa: F401
 
-__all__ = ["FheError", "InvalidArgument", "StateError", "NttContext", "load"]
+__all__ = ["FheError", "InvalidArgument", "StateError", "NttContext", "load", "CCParams", "CryptoContext",
+           "GenCryptoContext", "Ciphertext", "Plaintext"]

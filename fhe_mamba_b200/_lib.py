@@ -78,6 +78,44 @@ SIGNATURES = {
     "fhe_ctx_synchronize": [vp],
     "fhe_ntt": [vp, P64, u32, u32, u32, ctypes.c_int],
     "fhe_intt": [vp, P64, u32, u32, u32, ctypes.c_int],
+    # CKKS
+    "fhe_ctx_info": [vp, ctypes.c_void_p],
+    "fhe_level_scale": [vp, u32, ctypes.POINTER(f64)],
+    "fhe_keygen": [vp, u64],
+    "fhe_galois_element": [vp, i32, P64],
+    "fhe_rotation_keygen": [vp, PI32, u32],
+    "fhe_conjugation_keygen": [vp],
+    "fhe_key_download": [vp, ctypes.c_int, u64, P64, ctypes.c_size_t],
+    "fhe_encode": [vp, PD, PD, u32, u32, f64, ctypes.POINTER(vp)],
+    "fhe_decode": [vp, vp, PD, PD, u32],
+    "fhe_encrypt": [vp, vp, ctypes.POINTER(vp)],
+    "fhe_decrypt": [vp, vp, ctypes.POINTER(vp)],
+    "fhe_ct_free": [vp],
+    "fhe_pt_free": [vp],
+    "fhe_ct_info": [vp, P32, P32, P32, ctypes.POINTER(f64)],
+    "fhe_pt_info": [vp, P32, ctypes.POINTER(f64)],
+    "fhe_ct_download": [vp, vp, P64],
+    "fhe_ct_upload": [vp, P64, u32, u32, u32, f64, ctypes.POINTER(vp)],
+    "fhe_pt_download": [vp, vp, P64],
+    "fhe_pt_upload": [vp, P64, u32, f64, ctypes.POINTER(vp)],
+    "fhe_ct_clone": [vp, vp, ctypes.POINTER(vp)],
+    "fhe_add": [vp, vp, vp, ctypes.POINTER(vp)],
+    "fhe_sub": [vp, vp, vp, ctypes.POINTER(vp)],
+    "fhe_negate": [vp, vp, ctypes.POINTER(vp)],
+    "fhe_add_plain": [vp, vp, vp, ctypes.POINTER(vp)],
+    "fhe_sub_plain": [vp, vp, vp, ctypes.POINTER(vp)],
+    "fhe_mul_plain": [vp, vp, vp, ctypes.POINTER(vp)],
+    "fhe_add_scalar": [vp, vp, f64, ctypes.POINTER(vp)],
+    "fhe_mul_scalar": [vp, vp, f64, ctypes.POINTER(vp)],
+    "fhe_mul_int": [vp, vp, ctypes.c_int64, ctypes.POINTER(vp)],
+    "fhe_tensor": [vp, vp, vp, ctypes.POINTER(vp)],
+    "fhe_relinearize": [vp, vp, ctypes.POINTER(vp)],
+    "fhe_mul": [vp, vp, vp, ctypes.POINTER(vp)],
+    "fhe_rescale": [vp, vp],
+    "fhe_level_reduce": [vp, vp, u32],
+    "fhe_rotate": [vp, vp, i32, ctypes.POINTER(vp)],
+    "fhe_conjugate": [vp, vp, ctypes.POINTER(vp)],
+    "fhe_rotate_hoisted": [vp, vp, PI32, u32, ctypes.POINTER(vp)],
 }
 
 _lock = threading.Lock()

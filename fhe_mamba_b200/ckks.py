@@ -1,0 +1,331 @@
+"""OpenFHE-style CKKS API over the C ABI.
+
+Mirrors the CryptoContext calls the reference's native executor makes
+(native/fideslib_stage0/src/packed_fideslib.cpp:117-281, 1060-1090):
+GenCryptoContext, KeyGen, EvalMultKeyGen, EvalRotateKeyGen,
+MakeCKKSPackedPlaintext, Encrypt, Decrypt, EvalAdd/EvalSub/EvalMult,
+RescaleInPlace, EvalRotate, EvalFastRotationPrecompute/EvalFastRotation.
+Every operation runs on the GPU through libfhe_b200.so; errors surface as
+FheError (InvalidArgument / StateError) the way OpenFHE throws.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from ._lib import P32, P64, PD, PI32, call
+
+vp = ctypes.c_void_p
+
+
+@dataclass
+class CCParams:
+    """CCParams<CryptoContextCKKSRNS> fields the reference sets."""
+
+    ring_dim: int = 1 << 16
+    multiplicative_depth: int = 44
+    scaling_mod_size: int = 59
+    first_mod_size: int = 60
+    num_large_digits: int = 3
+    batch_size: int = 0  # 0 -> ring_dim / 2
+    device: int = 0
+
+    def SetRingDim(self, n):
+        self.ring_dim = n
+
+    def SetMultiplicativeDepth(self, d):
+        self.multiplicative_depth = d
+
+    def SetScalingModSize(self, b):
+        self.scaling_mod_size = b
+
+    def SetFirstModSize(self, b):
+        self.first_mod_size = b
+
+    def SetNumLargeDigits(self, d):
+        self.num_large_digits = d
+
+    def SetBatchSize(self, s):
+        self.batch_size = s
+
+
+class Plaintext:
+    def __init__(self, cc: "CryptoContext", h):
+        self.cc, self._h = cc, h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def info(self):
+        nl, sc = ctypes.c_uint32(), ctypes.c_double()
+        call("fhe_pt_info", self._h, ctypes.byref(nl), ctypes.byref(sc))
+        return nl.value, sc.value
+
+    def GetLevel(self):
+        return self.cc.n_q - self.info()[0]
+
+    def GetScalingFactor(self):
+        return self.info()[1]
+
+    def GetCKKSPackedValue(self, count=None):
+        n = self.cc.slots if count is None else count
+        re = np.zeros(n)
+        im = np.zeros(n)
+        call("fhe_decode", self.cc.h, self._h, re.ctypes.data_as(PD), im.ctypes.data_as(PD), n)
+        return re + 1j * im
+
+    def GetRealPackedValue(self, count=None):
+        return self.GetCKKSPackedValue(count).real
+
+    def residues(self):
+        nl, _ = self.info()
+        out = np.zeros((nl, self.cc.n), dtype=np.uint64)
+        call("fhe_pt_download", self.cc.h, self._h, out.ctypes.data_as(P64))
+        return out
+
+    def __del__(self):
+        try:
+            if self._h and self._h.value:
+                call("fhe_pt_free", self._h)
+        except Exception:
+            pass
+
+
+class Ciphertext:
+    def __init__(self, cc: "CryptoContext", h):
+        self.cc, self._h = cc, h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def info(self):
+        nc, nl, nd, sc = ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_double()
+        call("fhe_ct_info", self._h, ctypes.byref(nc), ctypes.byref(nl), ctypes.byref(nd), ctypes.byref(sc))
+        return nc.value, nl.value, nd.value, sc.value
+
+    def GetLevel(self):
+        return self.cc.n_q - self.info()[1]
+
+    def GetNoiseScaleDeg(self):
+        return self.info()[2]
+
+    def GetScalingFactor(self):
+        return self.info()[3]
+
+    def n_limbs(self):
+        return self.info()[1]
+
+    def Clone(self):
+        return self.cc._ct("fhe_ct_clone", self._h)
+
+    def residues(self):
+        nc, nl, _, _ = self.info()
+        out = np.zeros((nc, nl, self.cc.n), dtype=np.uint64)
+        call("fhe_ct_download", self.cc.h, self._h, out.ctypes.data_as(P64))
+        return out
+
+    def __del__(self):
+        try:
+            if self._h and self._h.value:
+                call("fhe_ct_free", self._h)
+        except Exception:
+            pass
+
+
+class CryptoContext:
+    """GenCryptoContext(params) + LoadContext on one GPU."""
+
+    def __init__(self, params: CCParams):
+        log_n = int(params.ring_dim).bit_length() - 1
+        if 1 << log_n != params.ring_dim:
+            raise _lib.InvalidArgument(-1, "GenCryptoContext", "ring dimension must be a power of two")
+        p = _lib.Params(log_n, params.multiplicative_depth, params.scaling_mod_size, params.first_mod_size,
+                        params.num_large_digits, params.batch_size or params.ring_dim // 2, params.device, 0)
+        h = vp()
+        call("fhe_ctx_create", ctypes.byref(p), ctypes.byref(h))
+        self.h = h
+        info = (ctypes.c_uint32 * 8)()
+        call("fhe_ctx_info", h, ctypes.cast(info, vp))
+        self.log_n, self.n_q, self.n_p, self.dnum, self.alpha, self.slots = list(info)[:6]
+        self.n = 1 << self.log_n
+        q = np.zeros(self.n_q, dtype=np.uint64)
+        pp = np.zeros(max(self.n_p, 1), dtype=np.uint64)
+        call("fhe_ctx_moduli", h, q.ctypes.data_as(P64), None, pp.ctypes.data_as(P64), None)
+        self.q = [int(x) for x in q]
+        self.p = [int(x) for x in pp[: self.n_p]]
+
+    # -- context queries
+    def GetRingDimension(self):
+        return self.n
+
+    def GetBatchSize(self):
+        return self.slots
+
+    def level_scale(self, n_limbs=None):
+        out = ctypes.c_double()
+        call("fhe_level_scale", self.h, self.n_q if n_limbs is None else n_limbs, ctypes.byref(out))
+        return out.value
+
+    def stream_ptr(self):
+        s = vp()
+        call("fhe_ctx_stream", self.h, ctypes.byref(s))
+        return int(s.value or 0)
+
+    def synchronize(self):
+        call("fhe_ctx_synchronize", self.h)
+
+    # -- keys
+    def KeyGen(self, seed: int = 0):
+        call("fhe_keygen", self.h, seed)
+
+    def EvalMultKeyGen(self, *_):
+        """The relinearisation key is generated by KeyGen."""
+
+    def EvalRotateKeyGen(self, steps):
+        arr = np.ascontiguousarray(np.asarray(list(steps), dtype=np.int32))
+        call("fhe_rotation_keygen", self.h, arr.ctypes.data_as(PI32), len(arr))
+
+    def EvalConjugateKeyGen(self):
+        call("fhe_conjugation_keygen", self.h)
+
+    def galois_element(self, step: int) -> int:
+        g = ctypes.c_uint64()
+        call("fhe_galois_element", self.h, step, ctypes.byref(g))
+        return g.value
+
+    def key(self, kind: int, galois: int = 0):
+        D = (self.n_q + self.alpha - 1) // self.alpha
+        words = {0: (self.n_q + self.n_p) * self.n, 1: 2 * self.n_q * self.n}.get(
+            kind, D * 2 * (self.n_q + self.n_p) * self.n)
+        out = np.zeros(words, dtype=np.uint64)
+        call("fhe_key_download", self.h, kind, galois, out.ctypes.data_as(P64), words)
+        return out
+
+    # -- encoding / encryption
+    def MakeCKKSPackedPlaintext(self, values, noise_scale_deg=1, level=0, params=None, slots=None,
+                                scale=0.0):
+        v = np.ascontiguousarray(np.asarray(values, dtype=np.complex128))
+        re = np.ascontiguousarray(v.real)
+        im = np.ascontiguousarray(v.imag)
+        h = vp()
+        call("fhe_encode", self.h, re.ctypes.data_as(PD), im.ctypes.data_as(PD), len(v), self.n_q - level,
+             float(scale), ctypes.byref(h))
+        return Plaintext(self, h)
+
+    def Encrypt(self, pt: Plaintext, _unused=None):
+        if isinstance(_unused, Plaintext):  # Encrypt(publicKey, pt) call order
+            pt = _unused
+        return self._ct("fhe_encrypt", pt.handle)
+
+    def Decrypt(self, ct: Ciphertext, _unused=None):
+        if isinstance(ct, Ciphertext):
+            c = ct
+        else:
+            c = _unused
+        h = vp()
+        call("fhe_decrypt", self.h, c.handle, ctypes.byref(h))
+        return Plaintext(self, h)
+
+    def upload(self, residues: np.ndarray, noise_deg=1, scale=1.0):
+        r = np.ascontiguousarray(residues, dtype=np.uint64)
+        h = vp()
+        call("fhe_ct_upload", self.h, r.ctypes.data_as(P64), r.shape[0], r.shape[1], noise_deg, scale,
+             ctypes.byref(h))
+        return Ciphertext(self, h)
+
+    def upload_plain(self, residues: np.ndarray, scale=1.0):
+        r = np.ascontiguousarray(residues, dtype=np.uint64)
+        h = vp()
+        call("fhe_pt_upload", self.h, r.ctypes.data_as(P64), r.shape[0], scale, ctypes.byref(h))
+        return Plaintext(self, h)
+
+    # -- arithmetic
+    def _ct(self, fn, *args):
+        h = vp()
+        call(fn, self.h, *args, ctypes.byref(h))
+        return Ciphertext(self, h)
+
+    def EvalAdd(self, a, b):
+        if isinstance(b, Ciphertext):
+            return self._ct("fhe_add", a.handle, b.handle)
+        if isinstance(b, Plaintext):
+            return self._ct("fhe_add_plain", a.handle, b.handle)
+        return self._ct("fhe_add_scalar", a.handle, float(b))
+
+    def EvalSub(self, a, b):
+        if isinstance(b, Ciphertext):
+            return self._ct("fhe_sub", a.handle, b.handle)
+        if isinstance(b, Plaintext):
+            return self._ct("fhe_sub_plain", a.handle, b.handle)
+        return self._ct("fhe_add_scalar", a.handle, -float(b))
+
+    def EvalNegate(self, a):
+        return self._ct("fhe_negate", a.handle)
+
+    def EvalMult(self, a, b):
+        if isinstance(b, Ciphertext):
+            return self._ct("fhe_mul", a.handle, b.handle)
+        if isinstance(b, Plaintext):
+            return self._ct("fhe_mul_plain", a.handle, b.handle)
+        return self._ct("fhe_mul_scalar", a.handle, float(b))
+
+    def EvalSquare(self, a):
+        return self._ct("fhe_mul", a.handle, a.handle)
+
+    def EvalMultNoRelin(self, a, b):
+        return self._ct("fhe_tensor", a.handle, b.handle)
+
+    def Relinearize(self, a):
+        return self._ct("fhe_relinearize", a.handle)
+
+    def MultByInteger(self, a, v: int):
+        return self._ct("fhe_mul_int", a.handle, int(v))
+
+    def RescaleInPlace(self, a):
+        call("fhe_rescale", self.h, a.handle)
+
+    def Rescale(self, a):
+        c = a.Clone()
+        self.RescaleInPlace(c)
+        return c
+
+    def LevelReduceInPlace(self, a, levels: int):
+        call("fhe_level_reduce", self.h, a.handle, levels)
+
+    def EvalRotate(self, a, step: int):
+        return self._ct("fhe_rotate", a.handle, int(step))
+
+    def EvalConjugate(self, a):
+        return self._ct("fhe_conjugate", a.handle)
+
+    def EvalFastRotationPrecompute(self, a):
+        """Hoisting handle: the ModUp is shared inside EvalFastRotation's batch call."""
+        return a
+
+    def EvalFastRotation(self, a, steps, m=None, precomp=None):
+        steps = list(steps) if hasattr(steps, "__iter__") else [steps]
+        arr = np.ascontiguousarray(np.asarray(steps, dtype=np.int32))
+        outs = (vp * len(arr))()
+        call("fhe_rotate_hoisted", self.h, a.handle, arr.ctypes.data_as(PI32), len(arr), outs)
+        res = [Ciphertext(self, vp(o)) for o in outs]
+        return res
+
+    def close(self):
+        if getattr(self, "h", None) and self.h.value:
+            call("fhe_ctx_destroy", self.h)
+            self.h = vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def GenCryptoContext(params: CCParams) -> CryptoContext:
+    return CryptoContext(params)

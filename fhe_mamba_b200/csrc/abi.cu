@@ -5,10 +5,19 @@
 #include <string>
 
 #include "../../include/fhe_b200.h"
+#include "ckks.h"
 #include "context.h"
 
+// Member order matters: ck refers to c and is destroyed first.
 struct fhe_ctx {
   fhe::Context c;
+  std::unique_ptr<fhe::Ckks> ck;
+};
+struct fhe_ct {
+  std::unique_ptr<fhe::Ct> p;
+};
+struct fhe_pt {
+  std::unique_ptr<fhe::Pt> p;
 };
 
 namespace {
@@ -106,6 +115,7 @@ int fhe_ctx_create(const fhe_params* p, fhe_ctx** out) {
     c.primes = q;
     c.primes.insert(c.primes.end(), pp.begin(), pp.end());
     c.build_tables();
+    h->ck = std::make_unique<fhe::Ckks>(c);
     *out = h.release();
   });
 }
@@ -214,6 +224,284 @@ int fhe_ntt(fhe_ctx* ctx, uint64_t* data, uint32_t n_polys, uint32_t limb0, uint
 
 int fhe_intt(fhe_ctx* ctx, uint64_t* data, uint32_t n_polys, uint32_t limb0, uint32_t n_limbs, int mem) {
   return guarded([&] { raw_transform(ctx, data, n_polys, limb0, n_limbs, mem, true); });
+}
+
+// ---------------------------------------------------------------------------
+// CKKS
+
+namespace {
+fhe::Ckks& ckks(fhe_ctx* ctx) {
+  fhe::require(ctx != nullptr, "null context");
+  fhe::require(ctx->ck != nullptr, "not a CKKS context (created with fhe_ctx_create_ntt)");
+  ctx->c.make_current();
+  return *ctx->ck;
+}
+const fhe::Ct& ct_of(const fhe_ct* c) {
+  fhe::require(c != nullptr && c->p != nullptr, "null ciphertext handle");
+  return *c->p;
+}
+const fhe::Pt& pt_of(const fhe_pt* p) {
+  fhe::require(p != nullptr && p->p != nullptr, "null plaintext handle");
+  return *p->p;
+}
+void put_ct(fhe_ct** out, std::unique_ptr<fhe::Ct> c) {
+  fhe::require(out != nullptr, "null output handle");
+  *out = new fhe_ct{std::move(c)};
+}
+void put_pt(fhe_pt** out, std::unique_ptr<fhe::Pt> p) {
+  fhe::require(out != nullptr, "null output handle");
+  *out = new fhe_pt{std::move(p)};
+}
+}  // namespace
+
+int fhe_ctx_info(const fhe_ctx* ctx, fhe_ctx_info_t* info) {
+  return guarded([&] {
+    fhe::require(ctx != nullptr && info != nullptr, "null context or output");
+    const fhe::Context& c = ctx->c;
+    info->log_n = c.log_n;
+    info->n_q = c.L;
+    info->n_p = c.K;
+    info->dnum = c.dnum;
+    info->alpha = c.alpha;
+    info->slots = c.slots;
+    info->ckks = ctx->ck ? 1 : 0;
+    info->reserved = 0;
+  });
+}
+
+int fhe_level_scale(fhe_ctx* ctx, uint32_t n_limbs, double* scale) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(scale != nullptr && n_limbs >= 1 && n_limbs <= ctx->c.L, "bad limb count or output");
+    *scale = k.level_scale(n_limbs);
+  });
+}
+
+int fhe_keygen(fhe_ctx* ctx, uint64_t seed) {
+  return guarded([&] { ckks(ctx).keygen(seed); });
+}
+
+int fhe_galois_element(fhe_ctx* ctx, int32_t step, uint64_t* g) {
+  return guarded([&] {
+    fhe::require(g != nullptr, "null output");
+    *g = ckks(ctx).galois_for_step(step);
+  });
+}
+
+int fhe_rotation_keygen(fhe_ctx* ctx, const int32_t* steps, uint32_t n) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(steps != nullptr || n == 0, "null steps");
+    for (uint32_t i = 0; i < n; ++i) k.rotation_keygen(k.galois_for_step(steps[i]));
+  });
+}
+
+int fhe_conjugation_keygen(fhe_ctx* ctx) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    k.rotation_keygen(2ull * ctx->c.n - 1);
+  });
+}
+
+int fhe_key_download(fhe_ctx* ctx, int kind, uint64_t galois, uint64_t* host, size_t words) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(kind >= 0 && kind <= 3, "key kind must be 0..3");
+    fhe::require(host != nullptr && words == k.key_words(kind),
+                 "host buffer must hold exactly " + std::to_string(k.key_words(kind)) + " words");
+    k.download_key(kind, galois, host);
+  });
+}
+
+int fhe_encode(fhe_ctx* ctx, const double* re, const double* im, uint32_t count, uint32_t n_limbs, double scale,
+               fhe_pt** out) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(re != nullptr || count == 0, "null values");
+    const uint32_t nq = n_limbs ? n_limbs : ctx->c.L;
+    fhe::require(nq <= ctx->c.L, "n_limbs above the number of Q primes");
+    put_pt(out, k.encode(re, im, count, nq, scale > 0 ? scale : k.level_scale(nq)));
+  });
+}
+
+int fhe_decode(fhe_ctx* ctx, const fhe_pt* pt, double* re, double* im, uint32_t count) {
+  return guarded([&] { ckks(ctx).decode(pt_of(pt), re, im, count); });
+}
+
+int fhe_encrypt(fhe_ctx* ctx, const fhe_pt* pt, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).encrypt(pt_of(pt))); });
+}
+
+int fhe_decrypt(fhe_ctx* ctx, const fhe_ct* ct, fhe_pt** out) {
+  return guarded([&] { put_pt(out, ckks(ctx).decrypt(ct_of(ct))); });
+}
+
+int fhe_ct_free(fhe_ct* ct) {
+  return guarded([&] { delete ct; });
+}
+
+int fhe_pt_free(fhe_pt* pt) {
+  return guarded([&] { delete pt; });
+}
+
+int fhe_ct_info(const fhe_ct* ct, uint32_t* ncomp, uint32_t* n_limbs, uint32_t* noise_deg, double* scale) {
+  return guarded([&] {
+    const fhe::Ct& c = ct_of(ct);
+    if (ncomp) *ncomp = c.ncomp;
+    if (n_limbs) *n_limbs = c.nq;
+    if (noise_deg) *noise_deg = c.noise_deg;
+    if (scale) *scale = c.scale;
+  });
+}
+
+int fhe_pt_info(const fhe_pt* pt, uint32_t* n_limbs, double* scale) {
+  return guarded([&] {
+    const fhe::Pt& p = pt_of(pt);
+    if (n_limbs) *n_limbs = p.nq;
+    if (scale) *scale = p.scale;
+  });
+}
+
+int fhe_ct_download(fhe_ctx* ctx, const fhe_ct* ct, uint64_t* host) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    const fhe::Ct& c = ct_of(ct);
+    fhe::require(host != nullptr, "null host buffer");
+    const size_t n = ctx->c.n;
+    FHE_CUDA(cudaMemcpy2DAsync(host, (size_t)c.nq * n * 8, c.data(), (size_t)c.cap * n * 8, (size_t)c.nq * n * 8,
+                               c.ncomp, cudaMemcpyDeviceToHost, k.ctx.stream));
+    FHE_CUDA(cudaStreamSynchronize(k.ctx.stream));
+  });
+}
+
+int fhe_ct_upload(fhe_ctx* ctx, const uint64_t* host, uint32_t ncomp, uint32_t n_limbs, uint32_t noise_deg,
+                  double scale, fhe_ct** out) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(host != nullptr, "null host buffer");
+    fhe::require(ncomp >= 2 && ncomp <= 3 && n_limbs >= 1 && n_limbs <= ctx->c.L, "bad ciphertext shape");
+    auto c = k.alloc(n_limbs, ncomp);
+    c->noise_deg = noise_deg;
+    c->scale = scale;
+    FHE_CUDA(cudaMemcpyAsync(c->data(), host, (size_t)ncomp * n_limbs * ctx->c.n * 8, cudaMemcpyHostToDevice,
+                             k.ctx.stream));
+    FHE_CUDA(cudaStreamSynchronize(k.ctx.stream));
+    put_ct(out, std::move(c));
+  });
+}
+
+int fhe_pt_download(fhe_ctx* ctx, const fhe_pt* pt, uint64_t* host) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    const fhe::Pt& p = pt_of(pt);
+    fhe::require(host != nullptr, "null host buffer");
+    FHE_CUDA(cudaMemcpyAsync(host, p.data(), (size_t)p.nq * ctx->c.n * 8, cudaMemcpyDeviceToHost, k.ctx.stream));
+    FHE_CUDA(cudaStreamSynchronize(k.ctx.stream));
+  });
+}
+
+int fhe_pt_upload(fhe_ctx* ctx, const uint64_t* host, uint32_t n_limbs, double scale, fhe_pt** out) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(host != nullptr && n_limbs >= 1 && n_limbs <= ctx->c.L, "bad plaintext shape");
+    auto p = std::make_unique<fhe::Pt>();
+    p->buf = fhe::DevMem((size_t)n_limbs * ctx->c.n * 8);
+    p->nq = n_limbs;
+    p->scale = scale;
+    FHE_CUDA(cudaMemcpyAsync(p->data(), host, (size_t)n_limbs * ctx->c.n * 8, cudaMemcpyHostToDevice, k.ctx.stream));
+    FHE_CUDA(cudaStreamSynchronize(k.ctx.stream));
+    put_pt(out, std::move(p));
+  });
+}
+
+int fhe_ct_clone(fhe_ctx* ctx, const fhe_ct* ct, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).clone(ct_of(ct))); });
+}
+
+int fhe_add(fhe_ctx* ctx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).add(ct_of(a), ct_of(b), false)); });
+}
+
+int fhe_sub(fhe_ctx* ctx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).add(ct_of(a), ct_of(b), true)); });
+}
+
+int fhe_negate(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).negate(ct_of(a))); });
+}
+
+int fhe_add_plain(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* p, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).add_plain(ct_of(a), pt_of(p), false)); });
+}
+
+int fhe_sub_plain(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* p, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).add_plain(ct_of(a), pt_of(p), true)); });
+}
+
+int fhe_mul_plain(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* p, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).mul_plain(ct_of(a), pt_of(p))); });
+}
+
+int fhe_add_scalar(fhe_ctx* ctx, const fhe_ct* a, double v, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).add_scalar(ct_of(a), v)); });
+}
+
+int fhe_mul_scalar(fhe_ctx* ctx, const fhe_ct* a, double v, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).mul_scalar(ct_of(a), v)); });
+}
+
+int fhe_mul_int(fhe_ctx* ctx, const fhe_ct* a, int64_t v, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).mul_int(ct_of(a), v)); });
+}
+
+int fhe_tensor(fhe_ctx* ctx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).tensor(ct_of(a), ct_of(b))); });
+}
+
+int fhe_relinearize(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).relinearize(ct_of(a))); });
+}
+
+int fhe_mul(fhe_ctx* ctx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).mul(ct_of(a), ct_of(b))); });
+}
+
+int fhe_rescale(fhe_ctx* ctx, fhe_ct* ct) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(ct != nullptr && ct->p != nullptr, "null ciphertext handle");
+    k.rescale_inplace(*ct->p);
+  });
+}
+
+int fhe_level_reduce(fhe_ctx* ctx, fhe_ct* ct, uint32_t levels) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(ct != nullptr && ct->p != nullptr, "null ciphertext handle");
+    k.level_reduce_inplace(*ct->p, levels);
+  });
+}
+
+int fhe_rotate(fhe_ctx* ctx, const fhe_ct* a, int32_t step, fhe_ct** out) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    put_ct(out, k.rotate(ct_of(a), k.galois_for_step(step)));
+  });
+}
+
+int fhe_conjugate(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).rotate(ct_of(a), 2ull * ctx->c.n - 1)); });
+}
+
+int fhe_rotate_hoisted(fhe_ctx* ctx, const fhe_ct* a, const int32_t* steps, uint32_t n, fhe_ct** outs) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(outs != nullptr && (steps != nullptr || n == 0), "null steps or outputs");
+    std::vector<uint64_t> gs(n);
+    for (uint32_t i = 0; i < n; ++i) gs[i] = k.galois_for_step(steps[i]);
+    auto r = k.rotate_hoisted(ct_of(a), gs);
+    for (uint32_t i = 0; i < n; ++i) outs[i] = new fhe_ct{std::move(r[i])};
+  });
 }
 
 }  // extern "C"

@@ -1,0 +1,739 @@
+// RNS-CKKS evaluator: key generation, encoding, encryption, HYBRID key
+// switching, rescale, rotations and FLEXIBLEAUTO scale bookkeeping.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "ckks.h"
+
+namespace fhe {
+
+namespace {
+typedef unsigned __int128 u128;
+
+// Randomness streams (same definition as the CPU oracle's OC_STREAM_*).
+constexpr uint64_t kStreamSecret = 1ull << 56;
+constexpr uint64_t kStreamPkA = 2ull << 56;
+constexpr uint64_t kStreamPkE = 3ull << 56;
+inline uint64_t stream_enc(uint64_t kind, uint64_t nonce) { return (kind << 56) | (nonce & 0xFFFFFFFFFFFFFFull); }
+inline uint64_t stream_key(uint64_t kind, uint64_t id, uint64_t digit) {
+  return (kind << 56) | ((id & 0xFFFFFFFFFFull) << 8) | digit;
+}
+
+Shoup mk_shoup(uint64_t w, uint64_t q) { return Shoup{w, nt::shoup(w, q)}; }
+
+template <class T>
+DevMem upload(const std::vector<T>& v) {
+  DevMem m(std::max<size_t>(v.size() * sizeof(T), 16));
+  if (!v.empty()) FHE_CUDA(cudaMemcpy(m.p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice));
+  return m;
+}
+}  // namespace
+
+Ckks::Ckks(Context& c) : ctx(c) {
+  const uint32_t L = c.L;
+  sf_.assign(L, 0.0);
+  sf_[0] = (double)c.primes[L - 1];
+  for (uint32_t k = 1; k < L; ++k) sf_[k] = sf_[k - 1] * sf_[k - 1] / (double)c.primes[L - k];
+  mods_host_.resize(c.n_primes());
+  FHE_CUDA(cudaMemcpy(mods_host_.data(), c.d_mod.p, mods_host_.size() * sizeof(Modulus), cudaMemcpyDeviceToHost));
+  build_static_tables();
+  status_ = DevMem(sizeof(unsigned));
+}
+
+// Context-owned scratch buffers, reused across calls (one stream orders all use).
+uint64_t* Ckks::ws(size_t idx, size_t words) {
+  if (ws_.size() <= idx) ws_.resize(idx + 1);
+  if (ws_[idx].bytes < words * 8) {
+    FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+    ws_[idx] = DevMem(words * 8);
+  }
+  return ws_[idx].as<uint64_t>();
+}
+
+void Ckks::ntt_dense(uint64_t* d, uint32_t polys, uint32_t limbs, uint32_t stride, uint32_t prime0, bool inv) {
+  if (!polys || !limbs) return;
+  NttArgs a = ctx.ntt_args(d, polys, prime0, limbs, stride);
+  FHE_CUDA(inv ? ntt_inverse(a) : ntt_forward(a));
+}
+
+void Ckks::build_static_tables() {
+  const uint32_t L = ctx.L, K = ctx.K;
+  const auto& P = ctx.primes;
+  std::vector<Shoup> pinv(L), pmod(L + K), qinv((size_t)L * L);
+  for (uint32_t i = 0; i < L + K; ++i) {
+    const uint64_t q = P[i];
+    uint64_t pm = 1 % q;
+    for (uint32_t k = 0; k < K; ++k) pm = nt::mulmod(pm, P[L + k] % q, q);
+    pmod[i] = mk_shoup(i < L ? pm : 0, q);
+    if (i < L) pinv[i] = mk_shoup(nt::invmod(pm, q), q);
+  }
+  for (uint32_t last = 1; last < L; ++last)
+    for (uint32_t i = 0; i < last; ++i) {
+      const uint64_t q = P[i];
+      qinv[(size_t)last * L + i] = mk_shoup(nt::invmod(P[last] % q, q), q);
+    }
+  pinv_ = upload(pinv);
+  pmod_ = upload(pmod);
+  qinv_ = upload(qinv);
+  // P -> Q conversion arrays: sources p_0..p_{K-1}, targets q_0..q_{L-1}.
+  if (K) {
+    std::vector<uint32_t> srcp(K), dstp(L);
+    std::vector<Shoup> hatinv(K), hat((size_t)L * K);
+    for (uint32_t k = 0; k < K; ++k) {
+      srcp[k] = L + k;
+      const uint64_t pk = P[L + k];
+      uint64_t h = 1 % pk;
+      for (uint32_t j = 0; j < K; ++j)
+        if (j != k) h = nt::mulmod(h, P[L + j] % pk, pk);
+      hatinv[k] = mk_shoup(nt::invmod(h, pk), pk);
+    }
+    for (uint32_t t = 0; t < L; ++t) {
+      dstp[t] = t;
+      const uint64_t q = P[t];
+      for (uint32_t k = 0; k < K; ++k) {
+        uint64_t h = 1 % q;
+        for (uint32_t j = 0; j < K; ++j)
+          if (j != k) h = nt::mulmod(h, P[L + j] % q, q);
+        hat[(size_t)t * K + k] = mk_shoup(h, q);
+      }
+    }
+    auto a16 = [](size_t x) { return (x + 15) & ~size_t(15); };
+    const size_t b1 = a16(K * 4), b2 = a16(b1 + L * 4), b3 = b2 + K * sizeof(Shoup);
+    std::vector<char> blob(b3 + hat.size() * sizeof(Shoup));
+    std::memcpy(blob.data(), srcp.data(), K * 4);
+    std::memcpy(blob.data() + b1, dstp.data(), L * 4);
+    std::memcpy(blob.data() + b2, hatinv.data(), K * sizeof(Shoup));
+    std::memcpy(blob.data() + b3, hat.data(), hat.size() * sizeof(Shoup));
+    mdtab_blob_ = upload(blob);
+  }
+  // Special FFT twiddles: inverse in OpenFHE FFTSpecialInv order, forward in
+  // FFTSpecialForward order, computed with the host C library's cos/sin.
+  const uint32_t slots = ctx.slots, M = 4 * slots;
+  std::vector<uint32_t> rot(slots);
+  uint32_t p = 1;
+  for (uint32_t j = 0; j < slots; ++j) { rot[j] = p; p = (uint32_t)((uint64_t)p * 5 % M); }
+  std::vector<double2> ti(std::max(1u, slots)), tf(std::max(1u, slots));
+  for (uint32_t len = 2; len <= slots; len *= 2)
+    for (uint32_t j = 0; j < len / 2; ++j) {
+      const uint32_t ii = (4 * len - rot[j] % (4 * len)) * (M / (4 * len));
+      const double ai = 2.0 * M_PI * ii / M;
+      ti[len / 2 - 1 + j] = make_double2(std::cos(ai), std::sin(ai));
+      const uint32_t fi = (rot[j] % (4 * len)) * (M / (4 * len));
+      const double af = 2.0 * M_PI * fi / M;
+      tf[len / 2 - 1 + j] = make_double2(std::cos(af), std::sin(af));
+    }
+  fft_inv_tw_ = upload(ti);
+  fft_fwd_tw_ = upload(tf);
+}
+
+LevelTables& Ckks::level(uint32_t nq) {
+  auto it = levels_.find(nq);
+  if (it != levels_.end()) return it->second;
+  LevelTables& T = levels_[nq];
+  const uint32_t L = ctx.L, K = ctx.K, a = ctx.alpha;
+  const auto& P = ctx.primes;
+  T.nq = nq;
+  T.D = (nq + a - 1) / a;
+  T.w = nq + K;
+  const PrimeMap pm{nq, L};
+  // One blob per level; per digit: src_prime[ns] | dst_prime[nt] | hatinv[ns] | hat[nt][ns].
+  struct Off { size_t sp, dp, hi, h; uint32_t ns, nt, lo, hil; };
+  std::vector<Off> offs(T.D);
+  size_t cur = 0;
+  auto a16 = [](size_t x) { return (x + 15) & ~size_t(15); };
+  for (uint32_t j = 0; j < T.D; ++j) {
+    Off& o = offs[j];
+    o.lo = j * a;
+    o.hil = std::min(o.lo + a, nq);
+    o.ns = o.hil - o.lo;
+    o.nt = T.w - o.ns;
+    require(o.ns <= 24, "digits of more than 24 limbs are not supported", -1);
+    o.sp = cur; cur += 4 * o.ns;
+    o.dp = cur; cur += 4 * o.nt;
+    cur = a16(cur);
+    o.hi = cur; cur += sizeof(Shoup) * o.ns;
+    o.h = cur; cur += sizeof(Shoup) * o.ns * o.nt;
+  }
+  std::vector<char> blob(std::max<size_t>(cur, 16));
+  std::vector<uint2> list;
+  for (uint32_t j = 0; j < T.D; ++j) {
+    const Off& o = offs[j];
+    uint32_t* sp = reinterpret_cast<uint32_t*>(blob.data() + o.sp);
+    uint32_t* dp = reinterpret_cast<uint32_t*>(blob.data() + o.dp);
+    Shoup* hinv = reinterpret_cast<Shoup*>(blob.data() + o.hi);
+    Shoup* hat = reinterpret_cast<Shoup*>(blob.data() + o.h);
+    for (uint32_t i = 0; i < o.ns; ++i) {
+      sp[i] = o.lo + i;
+      const uint64_t qi = P[o.lo + i];
+      uint64_t h = 1 % qi;
+      for (uint32_t m = 0; m < o.ns; ++m)
+        if (m != i) h = nt::mulmod(h, P[o.lo + m] % qi, qi);
+      hinv[i] = mk_shoup(nt::invmod(h, qi), qi);
+    }
+    uint32_t tt = 0;
+    for (uint32_t l = 0; l < T.w; ++l) {
+      if (l >= o.lo && l < o.hil) continue;
+      const uint32_t pr = pm(l);
+      dp[tt] = pr;
+      const uint64_t t = P[pr];
+      for (uint32_t i = 0; i < o.ns; ++i) {
+        uint64_t h = 1 % t;
+        for (uint32_t m = 0; m < o.ns; ++m)
+          if (m != i) h = nt::mulmod(h, P[o.lo + m] % t, t);
+        hat[(size_t)tt * o.ns + i] = mk_shoup(h, t);
+      }
+      list.push_back(make_uint2(j * T.w + l, pr));
+      ++tt;
+    }
+  }
+  T.blob = upload(blob);
+  std::vector<ModUpDigit> digs(T.D);
+  const char* base = T.blob.as<char>();
+  for (uint32_t j = 0; j < T.D; ++j) {
+    const Off& o = offs[j];
+    digs[j].lo = o.lo;
+    digs[j].hi = o.hil;
+    digs[j].conv = ConvTable{o.ns, o.nt, reinterpret_cast<const uint32_t*>(base + o.sp),
+                             reinterpret_cast<const uint32_t*>(base + o.dp),
+                             reinterpret_cast<const Shoup*>(base + o.hi), reinterpret_cast<const Shoup*>(base + o.h)};
+  }
+  T.digits = upload(digs);
+  T.ntt_list = upload(list);
+  T.ntt_list_len = (uint32_t)list.size();
+  if (K) {
+    const char* mb = mdtab_blob_.as<char>();
+    auto a16b = [](size_t x) { return (x + 15) & ~size_t(15); };
+    const size_t b1 = a16b(K * 4), b2 = a16b(b1 + L * 4), b3 = b2 + K * sizeof(Shoup);
+    ConvTable md{K, nq, reinterpret_cast<const uint32_t*>(mb), reinterpret_cast<const uint32_t*>(mb + b1),
+                 reinterpret_cast<const Shoup*>(mb + b2), reinterpret_cast<const Shoup*>(mb + b3)};
+    T.moddown = upload(std::vector<ConvTable>{md});
+  }
+  return T;
+}
+
+// ---------------------------------------------------------------------------
+// keys
+
+uint64_t Ckks::galois_for_step(int64_t step) const {
+  const uint64_t m = 2ull * ctx.n;
+  const int64_t order = (int64_t)(ctx.n / 2);
+  int64_t e = step % order;
+  if (e < 0) e += order;
+  return nt::powmod(5, (uint64_t)e, m);
+}
+
+// HYBRID switching key: digit j has a_j uniform over Q_L P and
+// b_j = -a_j s_new + e_j + [l in digit j] (P mod q_l) s_old.
+void Ckks::switch_keygen(uint64_t key_id, const uint64_t* s_new, const uint64_t* s_old, DevMem& out) {
+  const uint32_t L = ctx.L, K = ctx.K, n = ctx.n, lk = L + K;
+  const uint32_t D = (L + ctx.alpha - 1) / ctx.alpha;
+  out = DevMem((size_t)D * 2 * lk * n * 8);
+  uint64_t* tmp = ws(9, (size_t)lk * n);
+  int64_t* e = reinterpret_cast<int64_t*>(ws(10, n));
+  const Modulus* mods = ctx.d_mod.as<Modulus>();
+  const uint64_t* primes = ctx.d_primes.as<uint64_t>();
+  const PrimeMap full{lk, L};
+  for (uint32_t j = 0; j < D; ++j) {
+    uint64_t* b = out.as<uint64_t>() + (size_t)j * 2 * lk * n;
+    uint64_t* a = b + (size_t)lk * n;
+    launch_sample_uniform(seed_, stream_key(0x10, key_id, j), a, n, lk, full, mods, ctx.stream);
+    launch_sample_small(1, seed_, stream_key(0x11, key_id, j), e, n, ctx.stream);
+    launch_lift_small(e, tmp, n, lk, full, primes, ctx.stream);
+    ntt_dense(tmp, 1, lk, lk, 0, false);
+    launch_ew(Ew::Mul, a, 0, s_new, 0, b, 0, 1, lk, n, full, mods, ctx.stream);
+    launch_ew(Ew::SubFrom, b, 0, tmp, 0, b, 0, 1, lk, n, full, mods, ctx.stream);
+    const uint32_t lo = j * ctx.alpha, hi = std::min(lo + ctx.alpha, L);
+    launch_mul_const(s_old + (size_t)lo * n, 0, pmod_.as<Shoup>() + lo, b + (size_t)lo * n, 0, b + (size_t)lo * n,
+                     0, 1, hi - lo, n, primes + lo, ctx.stream);
+  }
+  FHE_CUDA(cudaGetLastError());
+}
+
+void Ckks::keygen(uint64_t seed) {
+  const uint32_t L = ctx.L, K = ctx.K, n = ctx.n, lk = L + K;
+  seed_ = seed;
+  const Modulus* mods = ctx.d_mod.as<Modulus>();
+  const uint64_t* primes = ctx.d_primes.as<uint64_t>();
+  int64_t* small = reinterpret_cast<int64_t*>(ws(10, n));
+  s_ntt_ = DevMem((size_t)lk * n * 8);
+  launch_sample_small(0, seed, kStreamSecret, small, n, ctx.stream);
+  launch_lift_small(small, s_ntt_.as<uint64_t>(), n, lk, PrimeMap{lk, L}, primes, ctx.stream);
+  ntt_dense(s_ntt_.as<uint64_t>(), 1, lk, lk, 0, false);
+  pk_ = DevMem((size_t)2 * L * n * 8);
+  uint64_t* b = pk_.as<uint64_t>();
+  uint64_t* a = b + (size_t)L * n;
+  uint64_t* tmp = ws(9, (size_t)lk * n);
+  const PrimeMap q{L, L};
+  launch_sample_uniform(seed, kStreamPkA, a, n, L, q, mods, ctx.stream);
+  launch_sample_small(1, seed, kStreamPkE, small, n, ctx.stream);
+  launch_lift_small(small, tmp, n, L, q, primes, ctx.stream);
+  ntt_dense(tmp, 1, L, L, 0, false);
+  launch_ew(Ew::Mul, a, 0, s_ntt_.as<uint64_t>(), 0, b, 0, 1, L, n, q, mods, ctx.stream);
+  launch_ew(Ew::SubFrom, b, 0, tmp, 0, b, 0, 1, L, n, q, mods, ctx.stream);
+  uint64_t* s2 = ws(11, (size_t)lk * n);
+  launch_ew(Ew::Mul, s_ntt_.as<uint64_t>(), 0, s_ntt_.as<uint64_t>(), 0, s2, 0, 1, lk, n, PrimeMap{lk, L}, mods,
+            ctx.stream);
+  switch_keygen(0, s_ntt_.as<uint64_t>(), s2, rlk_);
+  rot_.clear();
+  keyed_ = true;
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+}
+
+// Rotation key for Galois element g: switches s -> sigma_g^{-1}(s), so that a
+// rotation is KS(c1) followed by sigma_g on (c0 + u0, u1).
+void Ckks::rotation_keygen(uint64_t g) {
+  require(keyed_, "rotation key generation before keygen", -4);
+  if (rot_.count(g)) return;
+  const uint32_t lk = ctx.L + ctx.K, n = ctx.n;
+  const uint64_t m = 2ull * n;
+  require(g % 2 == 1 && g < m, "Galois element must be odd and below 2N", -1);
+  const uint64_t ginv = nt::powmod(g, n - 1, m);  // (Z/2N)^* has order N
+  require((u128)g * ginv % m == 1, "internal: Galois inverse", -5);
+  uint64_t* snew = ws(12, (size_t)lk * n);
+  launch_automorphism(s_ntt_.as<uint64_t>(), 0, snew, 0, 1, lk, ctx.log_n, ginv, ctx.stream);
+  DevMem key;
+  switch_keygen(g, snew, s_ntt_.as<uint64_t>(), key);
+  rot_.emplace(g, std::move(key));
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+}
+
+size_t Ckks::key_words(int kind) const {
+  const size_t n = ctx.n, L = ctx.L, K = ctx.K;
+  const size_t D = (L + ctx.alpha - 1) / ctx.alpha;
+  switch (kind) {
+    case 0: return (L + K) * n;
+    case 1: return 2 * L * n;
+    default: return D * 2 * (L + K) * n;
+  }
+}
+
+void Ckks::download_key(int kind, uint64_t g, uint64_t* host) const {
+  require(keyed_, "no keys generated", -4);
+  const DevMem* m = nullptr;
+  if (kind == 0) m = &s_ntt_;
+  else if (kind == 1) m = &pk_;
+  else if (kind == 2) m = &rlk_;
+  else {
+    auto it = rot_.find(g);
+    require(it != rot_.end(), "no rotation key for Galois element " + std::to_string(g), -4);
+    m = &it->second;
+  }
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  FHE_CUDA(cudaMemcpy(host, m->p, key_words(kind) * 8, cudaMemcpyDeviceToHost));
+}
+
+// ---------------------------------------------------------------------------
+// encode / encrypt
+
+std::unique_ptr<Pt> Ckks::encode(const double* re, const double* im, uint32_t count, uint32_t nq, double scale) {
+  const uint32_t slots = ctx.slots, n = ctx.n;
+  require(count <= slots, "more values than slots", -1);
+  require(nq >= 1 && nq <= ctx.L, "limb count out of range", -1);
+  std::vector<double2> v(slots, make_double2(0.0, 0.0));
+  for (uint32_t i = 0; i < count; ++i) v[i] = make_double2(re ? re[i] : 0.0, im ? im[i] : 0.0);
+  double2* dv = reinterpret_cast<double2*>(ws(13, 2 * (size_t)slots));
+  FHE_CUDA(cudaMemcpyAsync(dv, v.data(), slots * sizeof(double2), cudaMemcpyHostToDevice, ctx.stream));
+  launch_fft_special_inv(dv, fft_inv_tw_.as<double2>(), slots, 1, ctx.stream);
+  int64_t* coef = reinterpret_cast<int64_t*>(ws(14, n));
+  FHE_CUDA(cudaMemsetAsync(coef, 0, (size_t)n * 8, ctx.stream));
+  FHE_CUDA(cudaMemsetAsync(status_.p, 0, sizeof(unsigned), ctx.stream));
+  launch_encode_round(dv, coef, slots, n, scale, status_.as<unsigned>(), ctx.stream);
+  auto p = std::make_unique<Pt>();
+  p->buf = DevMem((size_t)nq * n * 8);
+  p->nq = nq;
+  p->scale = scale;
+  launch_lift_small(coef, p->data(), n, nq, PrimeMap{nq, ctx.L}, ctx.d_primes.as<uint64_t>(), ctx.stream);
+  ntt_dense(p->data(), 1, nq, nq, 0, false);
+  unsigned st = 0;
+  FHE_CUDA(cudaMemcpyAsync(&st, status_.p, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx.stream));
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  require(st == 0, "encode: a scaled value is not finite or exceeds 2^62", -1);
+  return p;
+}
+
+void Ckks::decode(const Pt& p, double* re, double* im, uint32_t count) {
+  const uint32_t slots = ctx.slots, n = ctx.n;
+  require(count <= slots, "more values than slots", -1);
+  const uint32_t nl = std::min<uint32_t>(p.nq, 2);
+  uint64_t* c = ws(15, (size_t)nl * n);
+  FHE_CUDA(cudaMemcpyAsync(c, p.data(), (size_t)nl * n * 8, cudaMemcpyDeviceToDevice, ctx.stream));
+  ntt_dense(c, 1, nl, nl, 0, true);
+  double2* dv = reinterpret_cast<double2*>(ws(13, 2 * (size_t)slots));
+  const uint64_t q0 = ctx.primes[0], q1 = ctx.primes[1];
+  const uint64_t q0inv = nt::invmod(q0 % q1, q1);
+  launch_decode_crt(c, nl, slots, n, p.scale, q0, q1, q0inv, nt::shoup(q0inv, q1), mods_host_[1], dv, ctx.stream);
+  launch_fft_special_fwd(dv, fft_fwd_tw_.as<double2>(), slots, 1, ctx.stream);
+  std::vector<double2> v(slots);
+  FHE_CUDA(cudaMemcpyAsync(v.data(), dv, slots * sizeof(double2), cudaMemcpyDeviceToHost, ctx.stream));
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  for (uint32_t i = 0; i < count; ++i) {
+    if (re) re[i] = v[i].x;
+    if (im) im[i] = v[i].y;
+  }
+}
+
+std::unique_ptr<Ct> Ckks::alloc(uint32_t nq, uint32_t ncomp) {
+  auto c = std::make_unique<Ct>();
+  c->buf = DevMem((size_t)ncomp * nq * ctx.n * 8);
+  c->cap = nq;
+  c->nq = nq;
+  c->ncomp = ncomp;
+  return c;
+}
+
+std::unique_ptr<Ct> Ckks::clone(const Ct& a) {
+  auto c = alloc(a.nq, a.ncomp);
+  c->noise_deg = a.noise_deg;
+  c->scale = a.scale;
+  const size_t n = ctx.n;
+  FHE_CUDA(cudaMemcpy2DAsync(c->data(), (size_t)c->cap * n * 8, a.data(), (size_t)a.cap * n * 8,
+                             (size_t)a.nq * n * 8, a.ncomp, cudaMemcpyDeviceToDevice, ctx.stream));
+  return c;
+}
+
+std::unique_ptr<Ct> Ckks::encrypt(const Pt& p) {
+  require(keyed_, "encrypt before keygen", -4);
+  const uint32_t nq = p.nq, n = ctx.n, L = ctx.L;
+  const Modulus* mods = ctx.d_mod.as<Modulus>();
+  const uint64_t* primes = ctx.d_primes.as<uint64_t>();
+  const uint64_t nonce = enc_nonce++;
+  int64_t* small = reinterpret_cast<int64_t*>(ws(10, n));
+  uint64_t* v = ws(16, (size_t)nq * n);
+  uint64_t* e = ws(17, (size_t)2 * nq * n);
+  const PrimeMap q{nq, L};
+  launch_sample_small(0, seed_, stream_enc(4, nonce), small, n, ctx.stream);
+  launch_lift_small(small, v, n, nq, q, primes, ctx.stream);
+  launch_sample_small(1, seed_, stream_enc(5, nonce), small, n, ctx.stream);
+  launch_lift_small(small, e, n, nq, q, primes, ctx.stream);
+  launch_sample_small(1, seed_, stream_enc(6, nonce), small, n, ctx.stream);
+  launch_lift_small(small, e + (size_t)nq * n, n, nq, q, primes, ctx.stream);
+  ntt_dense(v, 1, nq, nq, 0, false);
+  ntt_dense(e, 2, nq, nq, 0, false);
+  auto c = alloc(nq, 2);
+  const size_t s = (size_t)nq * n;
+  // c0 = b v + e0 + m ;  c1 = a v + e1
+  launch_ew(Ew::Mul, pk_.as<uint64_t>(), (size_t)L * n, v, 0, c->data(), s, 2, nq, n, q, mods, ctx.stream);
+  launch_ew(Ew::Add, c->data(), s, e, s, c->data(), s, 2, nq, n, q, mods, ctx.stream);
+  launch_ew(Ew::Add, c->data(), 0, p.data(), 0, c->data(), 0, 1, nq, n, q, mods, ctx.stream);
+  c->scale = p.scale;
+  c->noise_deg = p.noise_deg;
+  return c;
+}
+
+std::unique_ptr<Pt> Ckks::decrypt(const Ct& c) {
+  require(keyed_, "decrypt before keygen", -4);
+  const uint32_t nq = c.nq, n = ctx.n;
+  const Modulus* mods = ctx.d_mod.as<Modulus>();
+  const PrimeMap q{nq, ctx.L};
+  auto p = std::make_unique<Pt>();
+  p->buf = DevMem((size_t)nq * n * 8);
+  p->nq = nq;
+  p->scale = c.scale;
+  p->noise_deg = c.noise_deg;
+  const size_t cs = (size_t)c.cap * n;
+  const uint64_t* s = s_ntt_.as<uint64_t>();
+  FHE_CUDA(cudaMemcpyAsync(p->data(), c.data(), (size_t)nq * n * 8, cudaMemcpyDeviceToDevice, ctx.stream));
+  launch_ew(Ew::MulAdd, c.data() + cs, 0, s, 0, p->data(), 0, 1, nq, n, q, mods, ctx.stream);
+  if (c.ncomp == 3) {
+    uint64_t* s2 = ws(11, (size_t)(ctx.L + ctx.K) * n);
+    launch_ew(Ew::Mul, s, 0, s, 0, s2, 0, 1, nq, n, q, mods, ctx.stream);
+    launch_ew(Ew::MulAdd, c.data() + 2 * cs, 0, s2, 0, p->data(), 0, 1, nq, n, q, mods, ctx.stream);
+  }
+  return p;
+}
+
+// ---------------------------------------------------------------------------
+// key switching
+
+void Ckks::modup(const uint64_t* d, uint32_t nq, uint64_t* ext) {
+  const uint32_t n = ctx.n;
+  LevelTables& T = level(nq);
+  uint64_t* coef = ws(1, (size_t)ctx.L * n);
+  FHE_CUDA(cudaMemcpyAsync(coef, d, (size_t)nq * n * 8, cudaMemcpyDeviceToDevice, ctx.stream));
+  ntt_dense(coef, 1, nq, nq, 0, true);
+  launch_modup(coef, d, ext, nq, ctx.K, n, T.digits.as<ModUpDigit>(), T.D, ctx.d_primes.as<uint64_t>(), ctx.stream);
+  if (T.ntt_list_len) {
+    NttArgs a = ctx.ntt_args(ext, 1, 0, T.ntt_list_len, 0);
+    a.list = T.ntt_list.as<uint2>();
+    FHE_CUDA(ntt_forward(a));
+  }
+}
+
+// acc = [2][w][N] (NTT form, clobbered) -> out[c] = ModDown(acc[c]) (+ add_c0 on component 0).
+void Ckks::moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, const uint64_t* add_c0) {
+  const uint32_t n = ctx.n, K = ctx.K, w = nq + K;
+  LevelTables& T = level(nq);
+  ntt_dense(acc + (size_t)nq * n, 2, K, w, ctx.L, true);
+  uint64_t* conv = ws(3, (size_t)2 * ctx.L * n);
+  launch_convert(acc + (size_t)nq * n, (size_t)w * n, conv, (size_t)nq * n, 2, T.moddown.as<ConvTable>(), n,
+                 ctx.d_primes.as<uint64_t>(), ctx.stream);
+  ntt_dense(conv, 2, nq, nq, 0, false);
+  launch_moddown_combine(acc, (size_t)w * n, conv, (size_t)nq * n, pinv_.as<Shoup>(), add_c0, out, so, 2, nq, n,
+                         ctx.d_primes.as<uint64_t>(), ctx.stream);
+}
+
+void Ckks::keyswitch(const uint64_t* d, uint32_t nq, const uint64_t* evk, uint64_t* out, size_t so,
+                     const uint64_t* add_c0) {
+  const uint32_t n = ctx.n, K = ctx.K, w = nq + K;
+  LevelTables& T = level(nq);
+  uint64_t* ext = ws(0, (size_t)T.D * w * n);
+  uint64_t* acc = ws(2, (size_t)2 * (ctx.L + K) * n);
+  modup(d, nq, ext);
+  launch_key_inner(ext, T.D, w, evk, ctx.L + K, PrimeMap{nq, ctx.L}, acc, n, ctx.d_mod.as<Modulus>(), ctx.stream);
+  moddown_pair(acc, nq, out, so, add_c0);
+}
+
+std::unique_ptr<Ct> Ckks::relinearize(const Ct& d) {
+  require(keyed_, "relinearize before keygen", -4);
+  require(d.ncomp == 3, "relinearize expects a 3-component ciphertext", -1);
+  const uint32_t nq = d.nq, n = ctx.n;
+  const size_t cs = (size_t)d.cap * n;
+  auto out = alloc(nq, 2);
+  const size_t so = (size_t)nq * n;
+  keyswitch(d.data() + 2 * cs, nq, rlk_.as<uint64_t>(), out->data(), so, nullptr);
+  launch_ew(Ew::Add, out->data(), so, d.data(), cs, out->data(), so, 2, nq, n, PrimeMap{nq, ctx.L},
+            ctx.d_mod.as<Modulus>(), ctx.stream);
+  out->scale = d.scale;
+  out->noise_deg = d.noise_deg;
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::rotate(const Ct& a, uint64_t g) {
+  require(a.ncomp == 2, "rotate expects a 2-component ciphertext", -1);
+  auto it = rot_.find(g);
+  require(it != rot_.end(), "missing rotation key for Galois element " + std::to_string(g), -4);
+  const uint32_t nq = a.nq, n = ctx.n;
+  const size_t cs = (size_t)a.cap * n, so = (size_t)nq * n;
+  uint64_t* u = ws(4, 2 * so);
+  keyswitch(a.data() + cs, nq, it->second.as<uint64_t>(), u, so, a.data());
+  auto out = alloc(nq, 2);
+  launch_automorphism(u, so, out->data(), so, 2, nq, ctx.log_n, g, ctx.stream);
+  out->scale = a.scale;
+  out->noise_deg = a.noise_deg;
+  return out;
+}
+
+std::vector<std::unique_ptr<Ct>> Ckks::rotate_hoisted(const Ct& a, const std::vector<uint64_t>& gs) {
+  require(a.ncomp == 2, "rotate expects a 2-component ciphertext", -1);
+  for (uint64_t g : gs) require(rot_.count(g) != 0, "missing rotation key for Galois element " + std::to_string(g), -4);
+  const uint32_t nq = a.nq, n = ctx.n, K = ctx.K, w = nq + K;
+  const size_t cs = (size_t)a.cap * n, so = (size_t)nq * n;
+  LevelTables& T = level(nq);
+  uint64_t* ext = ws(5, (size_t)T.D * w * n);  // one ModUp shared by every rotation
+  modup(a.data() + cs, nq, ext);
+  std::vector<std::unique_ptr<Ct>> outs;
+  uint64_t* acc = ws(2, (size_t)2 * (ctx.L + K) * n);
+  uint64_t* u = ws(4, 2 * so);
+  for (uint64_t g : gs) {
+    launch_key_inner(ext, T.D, w, rot_.at(g).as<uint64_t>(), ctx.L + K, PrimeMap{nq, ctx.L}, acc, n,
+                     ctx.d_mod.as<Modulus>(), ctx.stream);
+    moddown_pair(acc, nq, u, so, a.data());
+    auto out = alloc(nq, 2);
+    launch_automorphism(u, so, out->data(), so, 2, nq, ctx.log_n, g, ctx.stream);
+    out->scale = a.scale;
+    out->noise_deg = a.noise_deg;
+    outs.push_back(std::move(out));
+  }
+  return outs;
+}
+
+// ---------------------------------------------------------------------------
+// arithmetic
+
+std::unique_ptr<Ct> Ckks::tensor(const Ct& a, const Ct& b) {
+  require(a.ncomp == 2 && b.ncomp == 2, "tensor expects 2-component ciphertexts", -1);
+  require(a.nq == b.nq, "tensor operands must have the same number of limbs", -1);
+  const uint32_t nq = a.nq, n = ctx.n;
+  auto d = alloc(nq, 3);
+  launch_tensor(a.data(), (size_t)a.cap * n, b.data(), (size_t)b.cap * n, d->data(), (size_t)nq * n, nq, n,
+                ctx.d_mod.as<Modulus>(), ctx.stream);
+  d->scale = a.scale * b.scale;
+  d->noise_deg = a.noise_deg + b.noise_deg;
+  return d;
+}
+
+// OpenFHE DropLastElementAndScale: x_i <- (x_i - [lift(x_last)]_{q_i}) q_last^{-1}.
+void Ckks::rescale_inplace(Ct& a) {
+  require(a.nq >= 2, "rescale: no limb left to drop (level underflow)", -4);
+  const uint32_t nq = a.nq, n = ctx.n, nc = a.ncomp;
+  const size_t cs = (size_t)a.cap * n;
+  uint64_t* last = ws(6, (size_t)nc * n);
+  FHE_CUDA(cudaMemcpy2DAsync(last, (size_t)n * 8, a.data() + (size_t)(nq - 1) * n, cs * 8, (size_t)n * 8, nc,
+                             cudaMemcpyDeviceToDevice, ctx.stream));
+  ntt_dense(last, nc, 1, 1, nq - 1, true);
+  uint64_t* lifted = ws(7, (size_t)nc * (nq - 1) * n);
+  const size_t ls = (size_t)(nq - 1) * n;
+  launch_rescale_lift(last, n, lifted, ls, nc, nq - 1, n, ctx.primes[nq - 1], ctx.d_mod.as<Modulus>(), ctx.stream);
+  ntt_dense(lifted, nc, nq - 1, nq - 1, 0, false);
+  launch_moddown_combine(a.data(), cs, lifted, ls, qinv_.as<Shoup>() + (size_t)(nq - 1) * ctx.L, nullptr, a.data(),
+                         cs, nc, nq - 1, n, ctx.d_primes.as<uint64_t>(), ctx.stream);
+  a.scale /= (double)ctx.primes[nq - 1];
+  a.nq -= 1;
+  a.noise_deg = a.noise_deg > 1 ? a.noise_deg - 1 : 1;
+}
+
+void Ckks::level_reduce_inplace(Ct& a, uint32_t levels) {
+  require(levels < a.nq, "level reduce would drop every limb", -4);
+  a.nq -= levels;
+}
+
+std::vector<uint64_t> Ckks::scalar_residues(long double v, uint32_t nq) const {
+  const long double r = roundl(v);
+  const bool neg = r < 0;
+  const long double mag = neg ? -r : r;
+  require(mag < 1.7e38L, "scalar constant too large", -1);
+  const long double two64 = 18446744073709551616.0L;
+  const uint64_t hi = (uint64_t)(mag / two64);
+  const uint64_t lo = (uint64_t)(mag - (long double)hi * two64);
+  std::vector<uint64_t> out(nq);
+  for (uint32_t i = 0; i < nq; ++i) {
+    const uint64_t q = ctx.primes[i];
+    const uint64_t x = (uint64_t)((((u128)hi << 64) | lo) % q);
+    out[i] = neg && x ? q - x : x;
+  }
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::mul_int(const Ct& a, int64_t v) {
+  auto r = scalar_residues((long double)v, a.nq);
+  std::vector<Shoup> sh(a.nq);
+  for (uint32_t i = 0; i < a.nq; ++i) sh[i] = mk_shoup(r[i], ctx.primes[i]);
+  DevMem d = upload(sh);
+  auto out = alloc(a.nq, a.ncomp);
+  launch_mul_const(a.data(), (size_t)a.cap * ctx.n, d.as<Shoup>(), nullptr, 0, out->data(), (size_t)a.nq * ctx.n,
+                   a.ncomp, a.nq, ctx.n, ctx.d_primes.as<uint64_t>(), ctx.stream);
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  out->scale = a.scale;
+  out->noise_deg = a.noise_deg;
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::adjust(const Ct& a, uint32_t nq, double scale) {
+  require(nq <= a.nq, "adjust: target level is above the ciphertext", -1);
+  auto c = clone(a);
+  if (c->noise_deg == 2 && c->nq > nq) rescale_inplace(*c);
+  if (std::fabs(c->scale / scale - 1.0) > 1e-12) {
+    require(c->nq > nq, "adjust: scales differ at the same level", -4);
+    // times round(scale * q_last / s), then rescale: new scale = s * C / q_last ~ scale
+    const long double C = (long double)scale * (long double)ctx.primes[c->nq - 1] / (long double)c->scale;
+    require(C >= 1.0L && C < 9.2e18L, "adjust: scale ratio out of range", -4);
+    auto m = mul_int(*c, (int64_t)roundl(C));
+    m->noise_deg = c->noise_deg + 1;
+    c = std::move(m);
+    rescale_inplace(*c);
+    c->scale = scale;
+  }
+  if (c->nq > nq) level_reduce_inplace(*c, c->nq - nq);
+  return c;
+}
+
+std::unique_ptr<Ct> Ckks::add(const Ct& a, const Ct& b, bool subtract) {
+  require(a.ncomp == b.ncomp, "add: component counts differ", -1);
+  const Ct* x = &a;
+  const Ct* y = &b;
+  std::unique_ptr<Ct> tx, ty;
+  const bool same_scale = std::fabs(a.scale / b.scale - 1.0) <= 1e-12;
+  if (a.nq != b.nq) {
+    // FLEXIBLEAUTO level alignment: the operand with more limbs is brought to
+    // the other's level and scale.
+    if (a.nq > b.nq) { tx = adjust(a, b.nq, b.scale); x = tx.get(); }
+    else { ty = adjust(b, a.nq, a.scale); y = ty.get(); }
+  } else if (!same_scale) {
+    // Same level, different scale (degree 1 + degree 2): raise the smaller
+    // scale by an exact integer multiple.
+    const bool a_small = a.scale < b.scale;
+    const Ct& sm = a_small ? a : b;
+    const Ct& bg = a_small ? b : a;
+    const long double C = (long double)bg.scale / (long double)sm.scale;
+    require(C >= 1.0L && C < 4.6e18L, "add: scale ratio out of range", -4);
+    auto m = mul_int(sm, (int64_t)roundl(C));
+    m->scale = bg.scale;
+    m->noise_deg = bg.noise_deg;
+    if (a_small) { tx = std::move(m); x = tx.get(); } else { ty = std::move(m); y = ty.get(); }
+  }
+  const uint32_t nq = std::min(x->nq, y->nq), n = ctx.n;
+  auto out = alloc(nq, a.ncomp);
+  launch_ew(subtract ? Ew::Sub : Ew::Add, x->data(), (size_t)x->cap * n, y->data(), (size_t)y->cap * n, out->data(),
+            (size_t)nq * n, a.ncomp, nq, n, PrimeMap{nq, ctx.L}, ctx.d_mod.as<Modulus>(), ctx.stream);
+  out->scale = x->scale;
+  out->noise_deg = std::max(x->noise_deg, y->noise_deg);
+  if (tx || ty) FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::negate(const Ct& a) {
+  const uint32_t n = ctx.n;
+  auto out = alloc(a.nq, a.ncomp);
+  launch_ew(Ew::Neg, a.data(), (size_t)a.cap * n, a.data(), (size_t)a.cap * n, out->data(), (size_t)a.nq * n, a.ncomp,
+            a.nq, n, PrimeMap{a.nq, ctx.L}, ctx.d_mod.as<Modulus>(), ctx.stream);
+  out->scale = a.scale;
+  out->noise_deg = a.noise_deg;
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::add_plain(const Ct& a, const Pt& p, bool subtract) {
+  require(p.nq >= a.nq, "add_plain: plaintext has fewer limbs than the ciphertext", -1);
+  require(std::fabs(a.scale / p.scale - 1.0) < 1e-9, "add_plain: scale mismatch", -4);
+  auto out = clone(a);
+  launch_ew(subtract ? Ew::Sub : Ew::Add, out->data(), 0, p.data(), 0, out->data(), 0, 1, a.nq, ctx.n,
+            PrimeMap{a.nq, ctx.L}, ctx.d_mod.as<Modulus>(), ctx.stream);
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::mul_plain(const Ct& a, const Pt& p) {
+  require(p.nq >= a.nq, "mul_plain: plaintext has fewer limbs than the ciphertext", -1);
+  const uint32_t n = ctx.n;
+  auto out = alloc(a.nq, a.ncomp);
+  launch_ew(Ew::Mul, a.data(), (size_t)a.cap * n, p.data(), 0, out->data(), (size_t)a.nq * n, a.ncomp, a.nq, n,
+            PrimeMap{a.nq, ctx.L}, ctx.d_mod.as<Modulus>(), ctx.stream);
+  out->scale = a.scale * p.scale;
+  out->noise_deg = a.noise_deg + p.noise_deg;
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::add_scalar(const Ct& a, double v) {
+  auto r = scalar_residues((long double)v * (long double)a.scale, a.nq);
+  DevMem d = upload(r);
+  auto out = clone(a);
+  launch_add_const(out->data(), 0, d.as<uint64_t>(), out->data(), 0, 1, a.nq, ctx.n, ctx.d_primes.as<uint64_t>(),
+                   ctx.stream);
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::prepare_mult_input(const Ct& a) {
+  auto c = clone(a);
+  if (c->noise_deg >= 2) rescale_inplace(*c);
+  return c;
+}
+
+std::unique_ptr<Ct> Ckks::mul_scalar(const Ct& a, double v) {
+  auto c = prepare_mult_input(a);
+  const double sf = level_scale(c->nq);
+  auto r = scalar_residues((long double)v * (long double)sf, c->nq);
+  std::vector<Shoup> sh(c->nq);
+  for (uint32_t i = 0; i < c->nq; ++i) sh[i] = mk_shoup(r[i], ctx.primes[i]);
+  DevMem d = upload(sh);
+  auto out = alloc(c->nq, c->ncomp);
+  launch_mul_const(c->data(), (size_t)c->cap * ctx.n, d.as<Shoup>(), nullptr, 0, out->data(), (size_t)c->nq * ctx.n,
+                   c->ncomp, c->nq, ctx.n, ctx.d_primes.as<uint64_t>(), ctx.stream);
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  out->scale = c->scale * sf;
+  out->noise_deg = c->noise_deg + 1;
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::mul(const Ct& a, const Ct& b) {
+  require(keyed_, "mul before keygen", -4);
+  auto x = prepare_mult_input(a);
+  auto y = prepare_mult_input(b);
+  if (x->nq > y->nq) level_reduce_inplace(*x, x->nq - y->nq);
+  if (y->nq > x->nq) level_reduce_inplace(*y, y->nq - x->nq);
+  auto d = tensor(*x, *y);
+  auto out = relinearize(*d);
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  return out;
+}
+
+}  // namespace fhe

@@ -1,0 +1,124 @@
+// RNS-CKKS evaluator on the device (host orchestration of ckks_kernels + ntt).
+//
+// Semantics follow the OpenFHE CryptoContext the reference drives
+// (packed_fideslib.cpp:117-281): FLEXIBLEAUTO scaling (level scaling factors
+// sf_k = sf_{k-1}^2 / q_{L-k}, automatic rescale of degree-2 inputs before a
+// multiplication), HYBRID key switching with dnum digits, rotations by
+// key-switch-then-automorphism, hoisted rotations sharing one ModUp.
+#pragma once
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <vector>
+
+#include "ckks_kernels.h"
+#include "context.h"
+
+namespace fhe {
+
+// Device ciphertext: ncomp components of cap limbs each; the first nq limbs of
+// every component are live.  Component c, limb l at data + (c*cap + l)*N.
+struct Ct {
+  DevMem buf;
+  uint32_t cap = 0, nq = 0, ncomp = 2, noise_deg = 1;
+  double scale = 1.0;
+  uint64_t* data() const { return buf.as<uint64_t>(); }
+};
+
+// Device plaintext in NTT form over nq limbs.
+struct Pt {
+  DevMem buf;
+  uint32_t nq = 0, noise_deg = 1;
+  double scale = 1.0;
+  uint64_t* data() const { return buf.as<uint64_t>(); }
+};
+
+// Per-level key-switching tables (built on first use of a level).
+struct LevelTables {
+  uint32_t nq = 0, D = 0, w = 0;
+  DevMem digits;    // ModUpDigit[D]
+  DevMem blob;      // backing store of all ConvTable arrays of this level
+  DevMem ntt_list;  // uint2[]: ext limbs that need a forward NTT after ModUp
+  uint32_t ntt_list_len = 0;
+  DevMem moddown;   // ConvTable (P -> Q_nq)
+};
+
+class Ckks {
+ public:
+  explicit Ckks(Context& c);
+  Context& ctx;
+
+  // FLEXIBLEAUTO scaling factor of a fresh ciphertext with nq live limbs.
+  double level_scale(uint32_t nq) const { return sf_[ctx.L - nq]; }
+
+  // keys
+  void keygen(uint64_t seed);
+  bool has_keys() const { return keyed_; }
+  uint64_t galois_for_step(int64_t step) const;
+  void rotation_keygen(uint64_t g);
+  bool has_rotation_key(uint64_t g) const { return rot_.count(g) != 0; }
+  void download_key(int kind, uint64_t g, uint64_t* host) const;
+  size_t key_words(int kind) const;
+
+  // encode / encryption
+  std::unique_ptr<Pt> encode(const double* re, const double* im, uint32_t count, uint32_t nq, double scale);
+  void decode(const Pt& p, double* re, double* im, uint32_t count);
+  std::unique_ptr<Ct> encrypt(const Pt& p);
+  std::unique_ptr<Pt> decrypt(const Ct& c);
+
+  // arithmetic (all outputs are new handles)
+  std::unique_ptr<Ct> alloc(uint32_t nq, uint32_t ncomp);
+  std::unique_ptr<Ct> clone(const Ct& a);
+  std::unique_ptr<Ct> add(const Ct& a, const Ct& b, bool subtract);
+  std::unique_ptr<Ct> add_plain(const Ct& a, const Pt& p, bool subtract);
+  std::unique_ptr<Ct> mul_plain(const Ct& a, const Pt& p);
+  std::unique_ptr<Ct> add_scalar(const Ct& a, double v);
+  std::unique_ptr<Ct> mul_scalar(const Ct& a, double v);
+  std::unique_ptr<Ct> mul_int(const Ct& a, int64_t v);  // exact integer multiple, scale unchanged
+  std::unique_ptr<Ct> negate(const Ct& a);
+  std::unique_ptr<Ct> tensor(const Ct& a, const Ct& b);
+  std::unique_ptr<Ct> relinearize(const Ct& d);
+  std::unique_ptr<Ct> mul(const Ct& a, const Ct& b);
+  void rescale_inplace(Ct& a);
+  void level_reduce_inplace(Ct& a, uint32_t levels);
+  std::unique_ptr<Ct> rotate(const Ct& a, uint64_t g);
+  std::vector<std::unique_ptr<Ct>> rotate_hoisted(const Ct& a, const std::vector<uint64_t>& gs);
+
+  // Brings `a` to (nq, scale): FLEXIBLEAUTO adjustment by an integer multiple
+  // and a rescale, then dropping limbs.
+  std::unique_ptr<Ct> adjust(const Ct& a, uint32_t nq, double scale);
+
+  uint64_t enc_nonce = 1;
+
+ private:
+  void build_static_tables();
+  LevelTables& level(uint32_t nq);
+  // Key switch of d (NTT form, nq limbs) with evk: out = (u0 [+ add_c0], u1),
+  // component stride so.
+  void keyswitch(const uint64_t* d, uint32_t nq, const uint64_t* evk, uint64_t* out, size_t so,
+                 const uint64_t* add_c0);
+  void modup(const uint64_t* d, uint32_t nq, uint64_t* ext);
+  void moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, const uint64_t* add_c0);
+  void switch_keygen(uint64_t key_id, const uint64_t* s_new, const uint64_t* s_old, DevMem& out);
+  void ntt_dense(uint64_t* d, uint32_t polys, uint32_t limbs, uint32_t stride, uint32_t prime0, bool inv);
+  uint64_t* ws(size_t idx, size_t words);
+  std::vector<uint64_t> scalar_residues(long double v, uint32_t nq) const;
+  std::unique_ptr<Ct> prepare_mult_input(const Ct& a);
+
+  std::vector<double> sf_;
+  std::map<uint32_t, LevelTables> levels_;
+  DevMem pinv_;        // Shoup[L]: P^{-1} mod q_i
+  DevMem qinv_;        // Shoup[L][L]: q_last^{-1} mod q_i
+  DevMem pmod_;        // Shoup[L+K]: P mod q_i (0 for P primes)
+  DevMem mdtab_blob_;  // P -> Q conversion arrays (shared by all levels)
+  std::vector<Modulus> mods_host_;
+  DevMem fft_inv_tw_, fft_fwd_tw_;
+  bool keyed_ = false;
+  uint64_t seed_ = 0;
+  DevMem s_ntt_, pk_, rlk_;
+  std::map<uint64_t, DevMem> rot_;
+  std::vector<DevMem> ws_;
+  DevMem status_;
+};
+
+}  // namespace fhe

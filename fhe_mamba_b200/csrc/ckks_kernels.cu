@@ -1,0 +1,487 @@
+// RNS-CKKS device kernels for sm_100a (elementwise limb arithmetic, sampling,
+// automorphisms, HYBRID key-switching basis conversions, rescale lift,
+// special-FFT encode/decode).  The NTT lives in ntt.cu.
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "ckks_kernels.h"
+
+namespace fhe {
+namespace {
+
+constexpr int kTpb = 256;
+
+// ---------------------------------------------------------------------------
+// ChaCha20 block (RFC 8439 rounds), key = (seed, fixed words), 64-bit block
+// counter, 64-bit stream nonce.  Word w of the keystream for (seed, stream)
+// is 64-bit word (w & 7) of block (w >> 3), little-endian 32-bit halves.
+__device__ __forceinline__ uint32_t rotl(uint32_t v, int c) { return (v << c) | (v >> (32 - c)); }
+#define QR(a, b, c, d)             \
+  a += b; d ^= a; d = rotl(d, 16); \
+  c += d; b ^= c; b = rotl(b, 12); \
+  a += b; d ^= a; d = rotl(d, 8);  \
+  c += d; b ^= c; b = rotl(b, 7);
+
+__device__ void chacha_block(uint64_t seed, uint64_t stream, uint64_t counter, uint64_t out[8]) {
+  uint32_t s[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u,
+                    (uint32_t)seed, (uint32_t)(seed >> 32), 0x243f6a88u, 0x85a308d3u,
+                    0x13198a2eu, 0x03707344u, 0xa4093822u, 0x299f31d0u,
+                    (uint32_t)counter, (uint32_t)(counter >> 32), (uint32_t)stream,
+                    (uint32_t)(stream >> 32)};
+  uint32_t x[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = s[i];
+#pragma unroll 1
+  for (int r = 0; r < 10; ++r) {
+    QR(x[0], x[4], x[8], x[12]);
+    QR(x[1], x[5], x[9], x[13]);
+    QR(x[2], x[6], x[10], x[14]);
+    QR(x[3], x[7], x[11], x[15]);
+    QR(x[0], x[5], x[10], x[15]);
+    QR(x[1], x[6], x[11], x[12]);
+    QR(x[2], x[7], x[8], x[13]);
+    QR(x[3], x[4], x[9], x[14]);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    out[i] = (uint64_t)(x[2 * i] + s[2 * i]) | ((uint64_t)(x[2 * i + 1] + s[2 * i + 1]) << 32);
+}
+#undef QR
+
+__global__ void k_sample_small(int kind, uint64_t seed, uint64_t stream, int64_t* out, uint32_t n) {
+  const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;  // one block = 8 coefficients
+  if (8 * b >= n) return;
+  uint64_t w[8];
+  chacha_block(seed, stream, b, w);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int64_t v;
+    if (kind == 0) {
+      const uint64_t r = w[i] % 3;
+      v = r == 2 ? -1 : (int64_t)r;
+    } else {
+      v = (int64_t)__popcll(w[i] & 0x1FFFFFull) - (int64_t)__popcll((w[i] >> 21) & 0x1FFFFFull);
+    }
+    out[8 * b + i] = v;
+  }
+}
+
+__global__ void k_lift_small(const int64_t* src, uint64_t* out, uint32_t n, PrimeMap pm,
+                             const uint64_t* primes) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y;
+  const uint64_t q = primes[pm(l)];
+  const int64_t v = src[k];
+  uint64_t r;
+  if (v >= 0) {
+    r = (uint64_t)v % q;
+  } else {
+    const uint64_t m = ((uint64_t)(-(v + 1)) + 1) % q;
+    r = m ? q - m : 0;
+  }
+  out[(size_t)l * n + k] = r;
+}
+
+// Uniform residue from two keystream words: (hi * 2^64 + lo) mod q.
+__global__ void k_sample_uniform(uint64_t seed, uint64_t stream, uint64_t* out, uint32_t n, PrimeMap pm,
+                                 const Modulus* mods) {
+  const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;  // 4 coefficients per thread
+  if (4 * t >= n) return;
+  const uint32_t l = blockIdx.y;
+  const uint32_t p = pm(l);
+  const Modulus m = mods[p];
+  const uint64_t r64 = barrett_reduce(1, 0, m);  // 2^64 mod q
+  uint64_t w[8];
+  chacha_block(seed, stream, ((uint64_t)p * n + 4 * t) / 4, w);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t hi = barrett_reduce(0, w[2 * i], m);
+    const uint64_t lo = barrett_reduce(0, w[2 * i + 1], m);
+    out[(size_t)l * n + 4 * t + i] = add_mod(mul_mod(hi, r64, m), lo, m.q);
+  }
+}
+
+// ---------------------------------------------------------------------------
+__global__ void k_ew(Ew op, const uint64_t* a, size_t sa, const uint64_t* b, size_t sb, uint64_t* out,
+                     size_t so, uint32_t n, PrimeMap pm, const Modulus* mods) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y, c = blockIdx.z;
+  const Modulus m = mods[pm(l)];
+  const size_t off = (size_t)l * n + k;
+  const uint64_t x = a[c * sa + off];
+  uint64_t r;
+  switch (op) {
+    case Ew::Add: r = add_mod(x, b[c * sb + off], m.q); break;
+    case Ew::Sub: r = sub_mod(x, b[c * sb + off], m.q); break;
+    case Ew::Mul: r = mul_mod(x, b[c * sb + off], m); break;
+    case Ew::Neg: r = neg_mod(x, m.q); break;
+    case Ew::MulAdd: r = add_mod(out[c * so + off], mul_mod(x, b[c * sb + off], m), m.q); break;
+    default: r = sub_mod(b[c * sb + off], x, m.q); break;  // SubFrom
+  }
+  out[c * so + off] = r;
+}
+
+__global__ void k_mul_const(const uint64_t* a, size_t sa, const Shoup* cst, const uint64_t* b, size_t sb,
+                            uint64_t* out, size_t so, uint32_t n, const uint64_t* primes) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y, c = blockIdx.z;
+  const uint64_t q = primes[l];
+  const size_t off = (size_t)l * n + k;
+  const Shoup w = cst[l];
+  uint64_t r = shoup_mul(a[c * sa + off], w.w, w.wp, q);
+  if (b) r = add_mod(r, b[c * sb + off], q);
+  out[c * so + off] = r;
+}
+
+__global__ void k_add_const(const uint64_t* a, size_t sa, const uint64_t* cst, uint64_t* out, size_t so,
+                            uint32_t n, const uint64_t* primes) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y, c = blockIdx.z;
+  const size_t off = (size_t)l * n + k;
+  out[c * so + off] = add_mod(a[c * sa + off], cst[l], primes[l]);
+}
+
+__global__ void k_tensor(const uint64_t* a, size_t sa, const uint64_t* b, size_t sb, uint64_t* d, size_t sd,
+                         uint32_t n, const Modulus* mods) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y;
+  const Modulus m = mods[l];
+  const size_t off = (size_t)l * n + k;
+  const uint64_t a0 = a[off], a1 = a[sa + off], b0 = b[off], b1 = b[sb + off];
+  d[off] = mul_mod(a0, b0, m);
+  d[sd + off] = add_mod(mul_mod(a0, b1, m), mul_mod(a1, b0, m), m.q);
+  d[2 * sd + off] = mul_mod(a1, b1, m);
+}
+
+__global__ void k_automorphism(const uint64_t* in, size_t si, uint64_t* out, size_t so, uint32_t log_n,
+                               uint64_t g) {
+  const uint32_t n = 1u << log_n;
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t l = blockIdx.y, c = blockIdx.z;
+  const uint64_t mask = 2ull * n - 1;
+  const uint64_t e = ((2ull * (__brev(i) >> (32 - log_n)) + 1) * g) & mask;
+  const uint32_t j = __brev((uint32_t)((e - 1) >> 1)) >> (32 - log_n);
+  out[c * so + (size_t)l * n + i] = __ldg(in + c * si + (size_t)l * n + j);
+}
+
+// ---------------------------------------------------------------------------
+constexpr int kMaxSrc = 24;  // largest digit / special basis handled by the conversions
+
+__global__ void k_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t w, uint32_t n,
+                        const ModUpDigit* digits, const uint64_t* primes) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t j = blockIdx.y;
+  const ModUpDigit dg = digits[j];
+  uint64_t* e = ext + (size_t)j * w * n;
+  const uint32_t ns = dg.hi - dg.lo;
+  uint64_t y[kMaxSrc];
+#pragma unroll
+  for (int i = 0; i < kMaxSrc; ++i) {
+    if (i < (int)ns) {
+      const uint32_t l = dg.lo + i;
+      const Shoup h = dg.conv.hatinv[i];
+      y[i] = shoup_mul(coef[(size_t)l * n + k], h.w, h.wp, primes[dg.conv.src_prime[i]]);
+      e[(size_t)l * n + k] = dntt[(size_t)l * n + k];
+    }
+  }
+  for (uint32_t tt = 0; tt < dg.conv.nt; ++tt) {
+    const uint32_t l = tt < dg.lo ? tt : tt + ns;
+    const uint64_t t = primes[dg.conv.dst_prime[tt]], t2 = 2 * t;
+    const Shoup* hrow = dg.conv.hat + (size_t)tt * ns;
+    uint64_t acc = 0;
+#pragma unroll
+    for (int i = 0; i < kMaxSrc; ++i) {
+      if (i < (int)ns) {
+        const Shoup h = hrow[i];
+        acc = csub(acc + shoup_lazy(y[i], h.w, h.wp, t), t2);
+      }
+    }
+    e[(size_t)l * n + k] = csub(acc, t);
+  }
+}
+
+__global__ void k_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_t* evk,
+                            uint32_t key_limbs, PrimeMap pm, uint64_t* acc, uint32_t n,
+                            const Modulus* mods) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y;
+  const uint32_t p = pm(l);
+  const Modulus m = mods[p];
+  uint64_t s0 = 0, s1 = 0;
+  for (uint32_t j = 0; j < D; ++j) {
+    const uint64_t x = ext[((size_t)j * w + l) * n + k];
+    const uint64_t* kb = evk + (size_t)j * 2 * key_limbs * n;
+    s0 = add_mod(s0, mul_mod(x, kb[(size_t)p * n + k], m), m.q);
+    s1 = add_mod(s1, mul_mod(x, kb[((size_t)key_limbs + p) * n + k], m), m.q);
+  }
+  acc[(size_t)l * n + k] = s0;
+  acc[((size_t)w + l) * n + k] = s1;
+}
+
+__global__ void k_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp,
+                          const ConvTable* tab, uint32_t n, const uint64_t* primes) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t c = blockIdx.y;
+  const ConvTable t = *tab;
+  const uint64_t* s = src + c * s_comp;
+  uint64_t* d = dst + c * d_comp;
+  uint64_t y[kMaxSrc];
+#pragma unroll
+  for (int i = 0; i < kMaxSrc; ++i) {
+    if (i < (int)t.ns) {
+      const Shoup h = t.hatinv[i];
+      y[i] = shoup_mul(s[(size_t)i * n + k], h.w, h.wp, primes[t.src_prime[i]]);
+    }
+  }
+  for (uint32_t tt = 0; tt < t.nt; ++tt) {
+    const uint64_t q = primes[t.dst_prime[tt]], q2 = 2 * q;
+    const Shoup* hrow = t.hat + (size_t)tt * t.ns;
+    uint64_t acc = 0;
+#pragma unroll
+    for (int i = 0; i < kMaxSrc; ++i) {
+      if (i < (int)t.ns) {
+        const Shoup h = hrow[i];
+        acc = csub(acc + shoup_lazy(y[i], h.w, h.wp, q), q2);
+      }
+    }
+    d[(size_t)tt * n + k] = csub(acc, q);
+  }
+}
+
+__global__ void k_moddown_combine(const uint64_t* x, size_t sx, const uint64_t* conv, size_t sc,
+                                  const Shoup* pinv, const uint64_t* add, uint64_t* out, size_t so, uint32_t n,
+                                  const uint64_t* primes) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y, c = blockIdx.z;
+  const uint64_t q = primes[l];
+  const size_t off = (size_t)l * n + k;
+  const Shoup w = pinv[l];
+  uint64_t r = shoup_mul(sub_mod(x[c * sx + off], conv[c * sc + off], q), w.w, w.wp, q);
+  if (add && c == 0) r = add_mod(r, add[off], q);
+  out[c * so + off] = r;
+}
+
+__global__ void k_rescale_lift(const uint64_t* last, size_t sl, uint64_t* lifted, size_t sd, uint32_t n,
+                               uint64_t q_last, const Modulus* mods) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y, c = blockIdx.z;
+  const Modulus m = mods[l];
+  const uint64_t v = last[c * sl + k];
+  uint64_t r;
+  if (v > q_last / 2) {
+    const uint64_t mag = barrett_reduce(0, q_last - v, m);
+    r = mag ? m.q - mag : 0;
+  } else {
+    r = barrett_reduce(0, v, m);
+  }
+  lifted[c * sd + (size_t)l * n + k] = r;
+}
+
+// ---------------------------------------------------------------------------
+// Special FFT (OpenFHE FFTSpecialInv / FFTSpecialForward) stages.  Explicit
+// round-to-nearest intrinsics keep every product and sum unfused so that the
+// result matches a plain C evaluation of the same expressions.
+__global__ void k_fft_inv_stage(double2* v, const double2* tw, uint32_t slots, uint32_t len) {
+  const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= slots / 2) return;
+  double2* x = v + (size_t)blockIdx.y * slots;
+  const uint32_t half = len / 2, j = t % half, i = (t / half) * len + j;
+  const double2 a = x[i], b = x[i + half], w = tw[half - 1 + j];
+  const double vr = __dsub_rn(a.x, b.x), vi = __dsub_rn(a.y, b.y);
+  x[i] = make_double2(__dadd_rn(a.x, b.x), __dadd_rn(a.y, b.y));
+  x[i + half] = make_double2(__dsub_rn(__dmul_rn(vr, w.x), __dmul_rn(vi, w.y)),
+                             __dadd_rn(__dmul_rn(vi, w.x), __dmul_rn(vr, w.y)));
+}
+
+__global__ void k_fft_fwd_stage(double2* v, const double2* tw, uint32_t slots, uint32_t len) {
+  const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= slots / 2) return;
+  double2* x = v + (size_t)blockIdx.y * slots;
+  const uint32_t lenh = len / 2, j = t % lenh, i = (t / lenh) * len + j;
+  const double2 u = x[i], b = x[i + lenh], w = tw[lenh - 1 + j];
+  const double tr = __dsub_rn(__dmul_rn(b.x, w.x), __dmul_rn(b.y, w.y));
+  const double ti = __dadd_rn(__dmul_rn(b.x, w.y), __dmul_rn(b.y, w.x));
+  x[i] = make_double2(__dadd_rn(u.x, tr), __dadd_rn(u.y, ti));
+  x[i + lenh] = make_double2(__dsub_rn(u.x, tr), __dsub_rn(u.y, ti));
+}
+
+__global__ void k_encode_round(const double2* v, int64_t* coef, uint32_t slots, uint32_t log_slots,
+                               uint32_t n, double scale, unsigned* status) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= slots) return;
+  const uint32_t gap = n / (2 * slots);
+  const uint32_t src = log_slots ? (__brev(i) >> (32 - log_slots)) : 0;
+  const double2 x = v[src];
+  const double r = __dmul_rn(__ddiv_rn(x.x, (double)slots), scale);
+  const double s = __dmul_rn(__ddiv_rn(x.y, (double)slots), scale);
+  const double lim = 4611686018427387904.0;  // 2^62
+  if (!isfinite(r) || !isfinite(s) || fabs(r) >= lim || fabs(s) >= lim) {
+    atomicOr(status, 1u);
+    return;
+  }
+  coef[(size_t)i * gap] = llround(r);
+  coef[(size_t)i * gap + n / 2] = llround(s);
+}
+
+__device__ __forceinline__ double u128_to_double(uint64_t hi, uint64_t lo) {
+  return __dadd_rn(__dmul_rn((double)hi, 18446744073709551616.0), (double)lo);
+}
+
+__global__ void k_decode_crt(const uint64_t* coef, uint32_t nlimbs, uint32_t slots, uint32_t log_slots,
+                             uint32_t n, double scale, uint64_t q0, uint64_t q1, uint64_t q0inv,
+                             uint64_t q0inv_sh, Modulus m1, double2* v) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= slots) return;
+  const uint32_t gap = n / (2 * slots);
+  double part[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const size_t idx = (size_t)i * gap + (h ? n / 2 : 0);
+    const uint64_t a0 = coef[idx];
+    double val;
+    if (nlimbs == 1) {
+      val = a0 > q0 / 2 ? -(double)(q0 - a0) : (double)a0;
+    } else {
+      const uint64_t a1 = coef[(size_t)n + idx];
+      const uint64_t a0m = barrett_reduce(0, a0, m1);
+      const uint64_t d = sub_mod(a1, a0m, q1);
+      const uint64_t t = shoup_mul(d, q0inv, q0inv_sh, q1);
+      // x = a0 + q0 * t  < q0 q1 (128-bit)
+      uint64_t lo = q0 * t, hi = __umul64hi(q0, t);
+      lo += a0;
+      hi += lo < a0;
+      const uint64_t Qlo = q0 * q1, Qhi = __umul64hi(q0, q1);
+      const uint64_t hlo = (Qlo >> 1) | (Qhi << 63), hhi = Qhi >> 1;  // floor(Q/2)
+      const bool neg = hi > hhi || (hi == hhi && lo > hlo);
+      if (neg) {  // -(Q - x)
+        const uint64_t rlo = Qlo - lo;
+        const uint64_t rhi = Qhi - hi - (Qlo < lo);
+        val = -u128_to_double(rhi, rlo);
+      } else {
+        val = u128_to_double(hi, lo);
+      }
+    }
+    part[h] = __ddiv_rn(val, scale);
+  }
+  const uint32_t dst = log_slots ? (__brev(i) >> (32 - log_slots)) : 0;
+  v[dst] = make_double2(part[0], part[1]);
+}
+
+inline dim3 grid1(uint32_t n, uint32_t y = 1, uint32_t z = 1) { return dim3((n + kTpb - 1) / kTpb, y, z); }
+
+uint32_t log2u(uint32_t x) {
+  uint32_t l = 0;
+  while ((1u << l) < x) ++l;
+  return l;
+}
+
+}  // namespace
+
+void launch_sample_small(int kind, uint64_t seed, uint64_t stream, int64_t* out, uint32_t n, cudaStream_t s) {
+  k_sample_small<<<grid1(n / 8), kTpb, 0, s>>>(kind, seed, stream, out, n);
+}
+
+void launch_lift_small(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
+                       const uint64_t* primes, cudaStream_t s) {
+  if (!nlimbs) return;
+  k_lift_small<<<grid1(n, nlimbs), kTpb, 0, s>>>(src, out, n, pm, primes);
+}
+
+void launch_sample_uniform(uint64_t seed, uint64_t stream, uint64_t* out, uint32_t n, uint32_t nlimbs,
+                           PrimeMap pm, const Modulus* mods, cudaStream_t s) {
+  if (!nlimbs) return;
+  k_sample_uniform<<<grid1(n / 4, nlimbs), kTpb, 0, s>>>(seed, stream, out, n, pm, mods);
+}
+
+void launch_ew(Ew op, const uint64_t* a, size_t sa, const uint64_t* b, size_t sb, uint64_t* out, size_t so,
+               uint32_t ncomp, uint32_t nlimbs, uint32_t n, PrimeMap pm, const Modulus* mods, cudaStream_t s) {
+  if (!nlimbs || !ncomp) return;
+  k_ew<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(op, a, sa, b, sb, out, so, n, pm, mods);
+}
+
+void launch_mul_const(const uint64_t* a, size_t sa, const Shoup* c, const uint64_t* b, size_t sb, uint64_t* out,
+                      size_t so, uint32_t ncomp, uint32_t nlimbs, uint32_t n, const uint64_t* primes,
+                      cudaStream_t s) {
+  if (!nlimbs || !ncomp) return;
+  k_mul_const<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, b, sb, out, so, n, primes);
+}
+
+void launch_add_const(const uint64_t* a, size_t sa, const uint64_t* c, uint64_t* out, size_t so, uint32_t ncomp,
+                      uint32_t nlimbs, uint32_t n, const uint64_t* primes, cudaStream_t s) {
+  if (!nlimbs || !ncomp) return;
+  k_add_const<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, out, so, n, primes);
+}
+
+void launch_tensor(const uint64_t* a, size_t sa, const uint64_t* b, size_t sb, uint64_t* d, size_t sd,
+                   uint32_t nq, uint32_t n, const Modulus* mods, cudaStream_t s) {
+  k_tensor<<<grid1(n, nq), kTpb, 0, s>>>(a, sa, b, sb, d, sd, n, mods);
+}
+
+void launch_automorphism(const uint64_t* in, size_t si, uint64_t* out, size_t so, uint32_t ncomp,
+                         uint32_t nlimbs, uint32_t log_n, uint64_t g, cudaStream_t s) {
+  if (!nlimbs || !ncomp) return;
+  k_automorphism<<<grid1(1u << log_n, nlimbs, ncomp), kTpb, 0, s>>>(in, si, out, so, log_n, g);
+}
+
+void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t nq, uint32_t K, uint32_t n,
+                  const ModUpDigit* digits_dev, uint32_t D, const uint64_t* primes, cudaStream_t s) {
+  k_modup<<<grid1(n, D), kTpb, 0, s>>>(coef, dntt, ext, nq + K, n, digits_dev, primes);
+}
+
+void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_t* evk, uint32_t key_limbs,
+                      PrimeMap pm, uint64_t* acc, uint32_t n, const Modulus* mods, cudaStream_t s) {
+  k_key_inner<<<grid1(n, w), kTpb, 0, s>>>(ext, D, w, evk, key_limbs, pm, acc, n, mods);
+}
+
+void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp, uint32_t ncomp,
+                    const ConvTable* t_dev, uint32_t n, const uint64_t* primes, cudaStream_t s) {
+  k_convert<<<grid1(n, ncomp), kTpb, 0, s>>>(src, s_comp, dst, d_comp, t_dev, n, primes);
+}
+
+void launch_moddown_combine(const uint64_t* x, size_t sx, const uint64_t* conv, size_t sc, const Shoup* pinv,
+                            const uint64_t* add, uint64_t* out, size_t so, uint32_t ncomp, uint32_t nq,
+                            uint32_t n, const uint64_t* primes, cudaStream_t s) {
+  if (!nq || !ncomp) return;
+  k_moddown_combine<<<grid1(n, nq, ncomp), kTpb, 0, s>>>(x, sx, conv, sc, pinv, add, out, so, n, primes);
+}
+
+void launch_rescale_lift(const uint64_t* last, size_t sl, uint64_t* lifted, size_t sd, uint32_t ncomp,
+                         uint32_t nlimbs, uint32_t n, uint64_t q_last, const Modulus* mods, cudaStream_t s) {
+  if (!nlimbs) return;
+  k_rescale_lift<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(last, sl, lifted, sd, n, q_last, mods);
+}
+
+void launch_fft_special_inv(double2* v, const double2* tw, uint32_t slots, uint32_t batch, cudaStream_t s) {
+  for (uint32_t len = slots; len >= 2; len >>= 1)
+    k_fft_inv_stage<<<grid1(slots / 2, batch), kTpb, 0, s>>>(v, tw, slots, len);
+}
+
+void launch_fft_special_fwd(double2* v, const double2* tw, uint32_t slots, uint32_t batch, cudaStream_t s) {
+  for (uint32_t len = 2; len <= slots; len <<= 1)
+    k_fft_fwd_stage<<<grid1(slots / 2, batch), kTpb, 0, s>>>(v, tw, slots, len);
+}
+
+void launch_encode_round(const double2* v, int64_t* coef, uint32_t slots, uint32_t n, double scale,
+                         unsigned* status, cudaStream_t s) {
+  k_encode_round<<<grid1(slots), kTpb, 0, s>>>(v, coef, slots, log2u(slots), n, scale, status);
+}
+
+void launch_decode_crt(const uint64_t* coef, uint32_t nlimbs, uint32_t slots, uint32_t n, double scale,
+                       uint64_t q0, uint64_t q1, uint64_t q0inv_mod_q1, uint64_t q0inv_shoup, Modulus m1,
+                       double2* v, cudaStream_t s) {
+  k_decode_crt<<<grid1(slots), kTpb, 0, s>>>(coef, nlimbs, slots, log2u(slots), n, scale, q0, q1, q0inv_mod_q1,
+                                             q0inv_shoup, m1, v);
+}
+
+}  // namespace fhe

@@ -1,0 +1,108 @@
+// Launchers of the RNS-CKKS device kernels (ckks_kernels.cu).
+//
+// Polynomials are limb-major u64[limbs][N].  A polynomial "over Q_l (+P)"
+// maps limb l to prime l for l < nq and to prime p_base + (l - nq) beyond
+// (p_base = L, the first special prime), described by a PrimeMap.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "modarith.cuh"
+
+namespace fhe {
+
+struct PrimeMap {
+  uint32_t nq;      // limbs [0, nq) sit on primes [0, nq)
+  uint32_t p_base;  // limb nq + k sits on prime p_base + k
+  __host__ __device__ uint32_t operator()(uint32_t l) const { return l < nq ? l : p_base + (l - nq); }
+};
+
+// Constant multiplier with its Shoup companion (same layout as Twiddle).
+using Shoup = Twiddle;
+
+// Fast basis conversion (OpenFHE ApproxSwitchCRTBasis) from `ns` source limbs
+// to `nt` target limbs:  out_t = sum_i [x_i * hatinv_i]_{s_i} * hat_{i,t}  mod t.
+struct ConvTable {
+  uint32_t ns, nt;
+  const uint32_t* src_prime;  // [ns]
+  const uint32_t* dst_prime;  // [nt]
+  const Shoup* hatinv;        // [ns]
+  const Shoup* hat;           // [nt][ns]
+};
+
+// ---- randomness (ChaCha20, same streams as the oracle) ----
+void launch_sample_small(int kind, uint64_t seed, uint64_t stream, int64_t* out, uint32_t n,
+                         cudaStream_t s);  // kind 0: ternary, 1: CBD(21)
+void launch_lift_small(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
+                       const uint64_t* primes, cudaStream_t s);
+void launch_sample_uniform(uint64_t seed, uint64_t stream, uint64_t* out, uint32_t n, uint32_t nlimbs,
+                           PrimeMap pm, const Modulus* mods, cudaStream_t s);
+
+// ---- elementwise on [ncomp][limbs][N] with per-operand component strides (words) ----
+enum class Ew { Add, Sub, Mul, Neg, MulAdd /*out += a*b*/, SubFrom /*out = b - a*/ };
+void launch_ew(Ew op, const uint64_t* a, size_t sa, const uint64_t* b, size_t sb, uint64_t* out,
+               size_t so, uint32_t ncomp, uint32_t nlimbs, uint32_t n, PrimeMap pm,
+               const Modulus* mods, cudaStream_t s);
+// out[comp][l] = a[comp][l] * c_l (Shoup constant per limb, prime primes[l]) (+ b[comp][l] if b)
+void launch_mul_const(const uint64_t* a, size_t sa, const Shoup* c, const uint64_t* b, size_t sb,
+                      uint64_t* out, size_t so, uint32_t ncomp, uint32_t nlimbs, uint32_t n,
+                      const uint64_t* primes, cudaStream_t s);
+// out[comp][l] = a[comp][l] + c_l
+void launch_add_const(const uint64_t* a, size_t sa, const uint64_t* c, uint64_t* out, size_t so,
+                      uint32_t ncomp, uint32_t nlimbs, uint32_t n, const uint64_t* primes,
+                      cudaStream_t s);
+// Tensor product of two 2-component ciphertexts into d = [3][nq] (component stride sd).
+void launch_tensor(const uint64_t* a, size_t sa, const uint64_t* b, size_t sb, uint64_t* d, size_t sd,
+                   uint32_t nq, uint32_t n, const Modulus* mods, cudaStream_t s);
+
+// ---- automorphism in NTT (bit-reversed evaluation) order ----
+// out[l][i] = in[l][j], 2 brv(j) + 1 = (2 brv(i) + 1) g mod 2N.
+void launch_automorphism(const uint64_t* in, size_t si, uint64_t* out, size_t so, uint32_t ncomp,
+                         uint32_t nlimbs, uint32_t log_n, uint64_t g, cudaStream_t s);
+
+// ---- key switching ----
+// ModUp for all digits at once.  coef = INTT(d) [nq][N]; dntt = d [nq][N];
+// ext = [D][w][N], w = nq + K.  Digit j's own limbs are copied from dntt, the
+// others receive the basis conversion (coefficient form, NTT'd afterwards).
+struct ModUpDigit {
+  uint32_t lo, hi;  // own limbs [lo, hi)
+  ConvTable conv;   // sources lo..hi-1, targets = all other limbs of ext (in limb order)
+};
+void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t nq, uint32_t K,
+                  uint32_t n, const ModUpDigit* digits_dev, uint32_t D, const uint64_t* primes,
+                  cudaStream_t s);
+// acc[2][w][N] = sum_j ext[j] * evk[j][0/1][key limb]; key limb of ext limb l is pm(l).
+void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_t* evk,
+                      uint32_t key_limbs, PrimeMap pm, uint64_t* acc, uint32_t n, const Modulus* mods,
+                      cudaStream_t s);
+// Basis conversion of ncomp polys: src limbs (coefficient form) -> dst (coefficient form).
+void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp, uint32_t ncomp,
+                    const ConvTable* t_dev, uint32_t n, const uint64_t* primes, cudaStream_t s);
+// out[c][i] = (x[c][i] - conv[c][i]) * pinv_i  (+ add[i] on component 0 when add != null).
+void launch_moddown_combine(const uint64_t* x, size_t sx, const uint64_t* conv, size_t sc,
+                            const Shoup* pinv, const uint64_t* add, uint64_t* out, size_t so,
+                            uint32_t ncomp, uint32_t nq, uint32_t n, const uint64_t* primes,
+                            cudaStream_t s);
+// Rescale lift: lifted[c][i] = centred(last[c]) mod q_i for i < nlimbs.
+void launch_rescale_lift(const uint64_t* last, size_t sl, uint64_t* lifted, size_t sd, uint32_t ncomp,
+                         uint32_t nlimbs, uint32_t n, uint64_t q_last, const Modulus* mods,
+                         cudaStream_t s);
+
+// ---- encode / decode ----
+void launch_fft_special_inv(double2* v, const double2* tw, uint32_t slots, uint32_t batch,
+                            cudaStream_t s);
+void launch_fft_special_fwd(double2* v, const double2* tw, uint32_t slots, uint32_t batch,
+                            cudaStream_t s);
+// Bit-reverse, divide by slots, scale, round half away from zero, place at
+// coefficient i*gap (real) and i*gap + N/2 (imag) of coef (zeroed elsewhere).
+// status bit 0: a coefficient was not finite or exceeded 2^62.
+void launch_encode_round(const double2* v, int64_t* coef, uint32_t slots, uint32_t n, double scale,
+                         unsigned* status, cudaStream_t s);
+// Centred CRT of limbs 0 and 1 (or limb 0 alone) of an INTT'd plaintext at the
+// slot positions, divided by scale -> complex values in bit-reversed order,
+// ready for the forward special FFT.  m1 = Barrett constants of q1.
+void launch_decode_crt(const uint64_t* coef, uint32_t nlimbs, uint32_t slots, uint32_t n, double scale,
+                       uint64_t q0, uint64_t q1, uint64_t q0inv_mod_q1, uint64_t q0inv_shoup,
+                       Modulus m1, double2* v, cudaStream_t s);
+
+}  // namespace fhe

@@ -59,6 +59,18 @@ __device__ __forceinline__ void gs_bfly(uint64_t& x, uint64_t& y, const Twiddle 
   y = shoup_lazy(d, tw.w, tw.wp, q);
 }
 
+// Limb addressed by this block: (poly = blockIdx.y, limb = blockIdx.z) in the
+// dense layout, or entry blockIdx.z of the explicit limb list.
+__device__ __forceinline__ uint64_t* block_limb(const NttArgs& g, uint32_t n, uint32_t& pidx) {
+  if (g.list) {
+    const uint2 e = g.list[blockIdx.z];
+    pidx = e.y;
+    return g.data + (size_t)e.x * n;
+  }
+  pidx = g.prime0 + blockIdx.z;
+  return g.data + ((size_t)blockIdx.y * g.limb_stride + blockIdx.z) * n;
+}
+
 __device__ __forceinline__ Twiddle ld_tw(const Twiddle* t, uint32_t i) {
   const ulonglong2 v = __ldg(reinterpret_cast<const ulonglong2*>(t) + i);
   return Twiddle{v.x, v.y};
@@ -70,18 +82,15 @@ __device__ __forceinline__ Twiddle ld_tw(const Twiddle* t, uint32_t i) {
 // column.  Round 1: k = t + T*u.  Round 2: k = R*t + u.
 template <int LA>
 __global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA >= 8 ? 1 : 2)
-    ntt_fwd_cols(uint64_t* __restrict__ data, const Twiddle* __restrict__ tw_all,
-                 const uint64_t* __restrict__ primes, int log_n, uint32_t limb_stride,
-                 uint32_t prime0) {
+    ntt_fwd_cols(const NttArgs g) {
   using P = PassShape<LA>;
   extern __shared__ uint64_t smem[];
-  const int LB = log_n - LA;
-  const uint32_t n = 1u << log_n;
-  const uint32_t limb = blockIdx.z;
-  const uint32_t pidx = prime0 + limb;
-  const uint64_t q = primes[pidx], q2 = 2 * q;
-  const Twiddle* tw = tw_all + (size_t)pidx * n;
-  uint64_t* a = data + ((size_t)blockIdx.y * limb_stride + limb) * n;
+  const int LB = g.log_n - LA;
+  const uint32_t n = 1u << g.log_n;
+  uint32_t pidx;
+  uint64_t* a = block_limb(g, n, pidx);
+  const uint64_t q = g.primes[pidx], q2 = 2 * q;
+  const Twiddle* tw = g.tw + (size_t)pidx * n;
   const int c = threadIdx.x & 31;
   const int t = threadIdx.x >> 5;
   const uint32_t col = blockIdx.x * kColsPerCta + c;
@@ -139,19 +148,15 @@ __device__ __forceinline__ int rpad(int k) { return k + (k >> 4); }
 // k = R*t + u.  Final output reduced from [0, 4q) to [0, q).
 template <int LB, int ROWS>
 __global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
-    ntt_fwd_rows(uint64_t* __restrict__ data, const Twiddle* __restrict__ tw_all,
-                 const uint64_t* __restrict__ primes, int log_n, uint32_t limb_stride,
-                 uint32_t prime0) {
+    ntt_fwd_rows(const NttArgs g) {
   using P = PassShape<LB>;
   extern __shared__ uint64_t smem[];
   constexpr int kRowWords = P::S + P::S / 16;
-  const uint32_t n = 1u << log_n;
-  const uint32_t limb = blockIdx.z;
-  const uint32_t pidx = prime0 + limb;
-  const uint64_t q = primes[pidx], q2 = 2 * q;
-  const Twiddle* tw = tw_all + (size_t)pidx * n;
-  uint64_t* a = data + ((size_t)blockIdx.y * limb_stride + limb) * n +
-                (size_t)blockIdx.x * ROWS * P::S;
+  const uint32_t n = 1u << g.log_n;
+  uint32_t pidx;
+  uint64_t* a = block_limb(g, n, pidx) + (size_t)blockIdx.x * ROWS * P::S;
+  const uint64_t q = g.primes[pidx], q2 = 2 * q;
+  const Twiddle* tw = g.tw + (size_t)pidx * n;
   const int t = threadIdx.x % P::T;
   const int rr = threadIdx.x / P::T;
   const uint32_t row = blockIdx.x * ROWS + rr;
@@ -224,19 +229,15 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
 // round 2 on k = t + T*u (half-distances T .. S/2).  Input in [0, q).
 template <int LB, int ROWS>
 __global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
-    ntt_inv_rows(uint64_t* __restrict__ data, const Twiddle* __restrict__ tw_all,
-                 const uint64_t* __restrict__ primes, int log_n, uint32_t limb_stride,
-                 uint32_t prime0) {
+    ntt_inv_rows(const NttArgs g) {
   using P = PassShape<LB>;
   extern __shared__ uint64_t smem[];
   constexpr int kRowWords = P::S + P::S / 16;
-  const uint32_t n = 1u << log_n;
-  const uint32_t limb = blockIdx.z;
-  const uint32_t pidx = prime0 + limb;
-  const uint64_t q = primes[pidx], q2 = 2 * q;
-  const Twiddle* tw = tw_all + (size_t)pidx * n;
-  uint64_t* a = data + ((size_t)blockIdx.y * limb_stride + limb) * n +
-                (size_t)blockIdx.x * ROWS * P::S;
+  const uint32_t n = 1u << g.log_n;
+  uint32_t pidx;
+  uint64_t* a = block_limb(g, n, pidx) + (size_t)blockIdx.x * ROWS * P::S;
+  const uint64_t q = g.primes[pidx], q2 = 2 * q;
+  const Twiddle* tw = g.tw_inv + (size_t)pidx * n;
   const int t = threadIdx.x % P::T;
   const int rr = threadIdx.x / P::T;
   const uint32_t row = blockIdx.x * ROWS + rr;
@@ -303,18 +304,15 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
 // tw_last = (N^{-1}, N^{-1}') and tw_last2 = (w_1 N^{-1}, ...).
 template <int LA>
 __global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA >= 8 ? 1 : 2)
-    ntt_inv_cols(uint64_t* __restrict__ data, const Twiddle* __restrict__ tw_all,
-                 const uint64_t* __restrict__ primes, const Twiddle* __restrict__ ninv_all,
-                 int log_n, uint32_t limb_stride, uint32_t prime0) {
+    ntt_inv_cols(const NttArgs g) {
   using P = PassShape<LA>;
   extern __shared__ uint64_t smem[];
-  const int LB = log_n - LA;
-  const uint32_t n = 1u << log_n;
-  const uint32_t limb = blockIdx.z;
-  const uint32_t pidx = prime0 + limb;
-  const uint64_t q = primes[pidx], q2 = 2 * q;
-  const Twiddle* tw = tw_all + (size_t)pidx * n;
-  uint64_t* a = data + ((size_t)blockIdx.y * limb_stride + limb) * n;
+  const int LB = g.log_n - LA;
+  const uint32_t n = 1u << g.log_n;
+  uint32_t pidx;
+  uint64_t* a = block_limb(g, n, pidx);
+  const uint64_t q = g.primes[pidx], q2 = 2 * q;
+  const Twiddle* tw = g.tw_inv + (size_t)pidx * n;
   const int c = threadIdx.x & 31;
   const int t = threadIdx.x >> 5;
   const uint32_t col = blockIdx.x * kColsPerCta + c;
@@ -353,8 +351,8 @@ __global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA >= 8 ? 1 : 
     }
   }
   {  // last stage, m = 1, half-distance R/2 in registers, 1/N folded in.
-    const Twiddle ni = ninv_all[2 * pidx];
-    const Twiddle wn = ninv_all[2 * pidx + 1];
+    const Twiddle ni = g.ninv[2 * pidx];
+    const Twiddle wn = g.ninv[2 * pidx + 1];
     constexpr int h = P::R / 2;
 #pragma unroll
     for (int v = 0; v < h; ++v) {
@@ -385,7 +383,6 @@ template <int LA, int LB>
 cudaError_t launch_fwd(const NttArgs& g) {
   using PA = PassShape<LA>;
   using PB = PassShape<LB>;
-  const int log_n = LA + LB;
   const size_t sa = cols_smem<LA>(), sb = rows_smem<LB>();
   cudaError_t e;
   e = cudaFuncSetAttribute(ntt_fwd_cols<LA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa);
@@ -393,12 +390,11 @@ cudaError_t launch_fwd(const NttArgs& g) {
   e = cudaFuncSetAttribute(ntt_fwd_rows<LB, kRowsPerCta>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
   if (e != cudaSuccess) return e;
-  dim3 ga((1u << LB) / kColsPerCta, g.n_polys, g.n_limbs);
-  ntt_fwd_cols<LA><<<ga, kColsPerCta * PA::T, sa, g.stream>>>(g.data, g.tw, g.primes, log_n,
-                                                              g.limb_stride, g.prime0);
-  dim3 gb((1u << LA) / kRowsPerCta, g.n_polys, g.n_limbs);
-  ntt_fwd_rows<LB, kRowsPerCta><<<gb, kRowsPerCta * PB::T, sb, g.stream>>>(
-      g.data, g.tw, g.primes, log_n, g.limb_stride, g.prime0);
+  const uint32_t polys = g.list ? 1 : g.n_polys;
+  dim3 ga((1u << LB) / kColsPerCta, polys, g.n_limbs);
+  ntt_fwd_cols<LA><<<ga, kColsPerCta * PA::T, sa, g.stream>>>(g);
+  dim3 gb((1u << LA) / kRowsPerCta, polys, g.n_limbs);
+  ntt_fwd_rows<LB, kRowsPerCta><<<gb, kRowsPerCta * PB::T, sb, g.stream>>>(g);
   return cudaGetLastError();
 }
 
@@ -406,7 +402,6 @@ template <int LA, int LB>
 cudaError_t launch_inv(const NttArgs& g) {
   using PA = PassShape<LA>;
   using PB = PassShape<LB>;
-  const int log_n = LA + LB;
   const size_t sa = cols_smem<LA>(), sb = rows_smem<LB>();
   cudaError_t e;
   e = cudaFuncSetAttribute(ntt_inv_cols<LA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa);
@@ -414,12 +409,11 @@ cudaError_t launch_inv(const NttArgs& g) {
   e = cudaFuncSetAttribute(ntt_inv_rows<LB, kRowsPerCta>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
   if (e != cudaSuccess) return e;
-  dim3 gb((1u << LA) / kRowsPerCta, g.n_polys, g.n_limbs);
-  ntt_inv_rows<LB, kRowsPerCta><<<gb, kRowsPerCta * PB::T, sb, g.stream>>>(
-      g.data, g.tw_inv, g.primes, log_n, g.limb_stride, g.prime0);
-  dim3 ga((1u << LB) / kColsPerCta, g.n_polys, g.n_limbs);
-  ntt_inv_cols<LA><<<ga, kColsPerCta * PA::T, sa, g.stream>>>(
-      g.data, g.tw_inv, g.primes, g.ninv, log_n, g.limb_stride, g.prime0);
+  const uint32_t polys = g.list ? 1 : g.n_polys;
+  dim3 gb((1u << LA) / kRowsPerCta, polys, g.n_limbs);
+  ntt_inv_rows<LB, kRowsPerCta><<<gb, kRowsPerCta * PB::T, sb, g.stream>>>(g);
+  dim3 ga((1u << LB) / kColsPerCta, polys, g.n_limbs);
+  ntt_inv_cols<LA><<<ga, kColsPerCta * PA::T, sa, g.stream>>>(g);
   return cudaGetLastError();
 }
 

@@ -18,6 +18,9 @@ struct NttArgs {
   uint32_t n_limbs;
   uint32_t limb_stride;    // limbs between consecutive polys
   uint32_t prime0;         // prime index of the first launched limb
+  // Optional explicit limb list (device array, n_limbs entries, n_polys must
+  // be 1): entry {x, y} transforms the limb at data + x*N with prime y.
+  const uint2* list = nullptr;
   cudaStream_t stream;
 };
 

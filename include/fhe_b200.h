@@ -114,6 +114,99 @@ int fhe_ntt(fhe_ctx* ctx, uint64_t* data, uint32_t n_polys, uint32_t limb0,
 int fhe_intt(fhe_ctx* ctx, uint64_t* data, uint32_t n_polys, uint32_t limb0,
              uint32_t n_limbs, int mem);
 
+/* --- CKKS evaluation (the API packed_fideslib.cpp:117-281 drives) --------- */
+
+typedef struct fhe_ct fhe_ct; /* device ciphertext: 2 or 3 components over n_limbs Q limbs */
+typedef struct fhe_pt fhe_pt; /* device plaintext, NTT form over n_limbs Q limbs */
+
+typedef struct fhe_ctx_info_t {
+  uint32_t log_n, n_q, n_p, dnum, alpha, slots, ckks, reserved;
+} fhe_ctx_info_t;
+
+int fhe_ctx_info(const fhe_ctx* ctx, fhe_ctx_info_t* info);
+
+/* FLEXIBLEAUTO scaling factor of a fresh ciphertext with n_limbs Q limbs
+ * (OpenFHE GetScalingFactorReal(level), level = n_q - n_limbs). */
+int fhe_level_scale(fhe_ctx* ctx, uint32_t n_limbs, double* scale);
+
+/* KeyGen + EvalMultKeyGen (packed_fideslib.cpp:1078): ternary secret, public
+ * key, HYBRID relinearisation key, all sampled on the device from ChaCha20
+ * streams keyed by `seed`. */
+int fhe_keygen(fhe_ctx* ctx, uint64_t seed);
+
+/* Galois element 5^step mod 2N of a slot rotation (FindAutomorphismIndex2n). */
+int fhe_galois_element(fhe_ctx* ctx, int32_t step, uint64_t* g);
+
+/* EvalRotateKeyGen(secretKey, steps) (packed_fideslib.cpp:1079-1083). */
+int fhe_rotation_keygen(fhe_ctx* ctx, const int32_t* steps, uint32_t n);
+
+/* Key for EvalConjugate (conjugate API patch, patches/fideslib-v2.1.0-*conjugate*). */
+int fhe_conjugation_keygen(fhe_ctx* ctx);
+
+/* Copies a key to host memory: kind 0 secret s (NTT form, [n_q+n_p][N]),
+ * 1 public key ([2][n_q][N]), 2 relinearisation key, 3 rotation key of
+ * Galois element `galois` ([digits][2][n_q+n_p][N]); `words` must equal the
+ * key's size.  For parity tests against an independent implementation. */
+int fhe_key_download(fhe_ctx* ctx, int kind, uint64_t galois, uint64_t* host, size_t words);
+
+/* MakeCKKSPackedPlaintext (packed_fideslib.cpp:163-179): special inverse FFT,
+ * scale, round half away from zero, RNS lift and NTT, all on the device.
+ * n_limbs = 0 means all Q limbs; scale <= 0 means the FLEXIBLEAUTO factor. */
+int fhe_encode(fhe_ctx* ctx, const double* re, const double* im, uint32_t count, uint32_t n_limbs,
+               double scale, fhe_pt** out);
+/* Decode (CKKSPackedEncoding::Decode): count <= slots values. */
+int fhe_decode(fhe_ctx* ctx, const fhe_pt* pt, double* re, double* im, uint32_t count);
+/* Encrypt(publicKey, pt) (packed_fideslib.cpp:185-189). */
+int fhe_encrypt(fhe_ctx* ctx, const fhe_pt* pt, fhe_ct** out);
+/* Decrypt(secretKey, ct) (client side, packed_fideslib.cpp:1195-1210). */
+int fhe_decrypt(fhe_ctx* ctx, const fhe_ct* ct, fhe_pt** out);
+
+int fhe_ct_free(fhe_ct* ct);
+int fhe_pt_free(fhe_pt* pt);
+/* GetLevel/GetNoiseScaleDeg/GetScalingFactor of a ciphertext. */
+int fhe_ct_info(const fhe_ct* ct, uint32_t* ncomp, uint32_t* n_limbs, uint32_t* noise_deg, double* scale);
+int fhe_pt_info(const fhe_pt* pt, uint32_t* n_limbs, double* scale);
+/* Raw residues, layout [ncomp][n_limbs][N] (host). */
+int fhe_ct_download(fhe_ctx* ctx, const fhe_ct* ct, uint64_t* host);
+int fhe_ct_upload(fhe_ctx* ctx, const uint64_t* host, uint32_t ncomp, uint32_t n_limbs, uint32_t noise_deg,
+                  double scale, fhe_ct** out);
+int fhe_pt_download(fhe_ctx* ctx, const fhe_pt* pt, uint64_t* host);
+int fhe_pt_upload(fhe_ctx* ctx, const uint64_t* host, uint32_t n_limbs, double scale, fhe_pt** out);
+/* Ciphertext::Clone. */
+int fhe_ct_clone(fhe_ctx* ctx, const fhe_ct* ct, fhe_ct** out);
+
+/* EvalAdd / EvalSub (FLEXIBLEAUTO level and scale alignment). */
+int fhe_add(fhe_ctx* ctx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out);
+int fhe_sub(fhe_ctx* ctx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out);
+int fhe_negate(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
+/* EvalAdd(ct, pt) / EvalSub(ct, pt) / EvalMult(ct, pt) (packed_fideslib.cpp:155-200). */
+int fhe_add_plain(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* p, fhe_ct** out);
+int fhe_sub_plain(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* p, fhe_ct** out);
+int fhe_mul_plain(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* p, fhe_ct** out);
+/* EvalAdd(ct, double) / EvalMult(ct, double). */
+int fhe_add_scalar(fhe_ctx* ctx, const fhe_ct* a, double v, fhe_ct** out);
+int fhe_mul_scalar(fhe_ctx* ctx, const fhe_ct* a, double v, fhe_ct** out);
+/* Exact integer multiple (multIntScalar, src/fideslib_refresh_correction.hpp:16-43). */
+int fhe_mul_int(fhe_ctx* ctx, const fhe_ct* a, int64_t v, fhe_ct** out);
+/* EvalMult without relinearisation (3-component result). */
+int fhe_tensor(fhe_ctx* ctx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out);
+/* Relinearize (HYBRID key switch of the third component). */
+int fhe_relinearize(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
+/* EvalMult(ct, ct) (packed_fideslib.cpp:128-154): rescale degree-2 inputs,
+ * align levels, tensor, relinearise. */
+int fhe_mul(fhe_ctx* ctx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out);
+/* RescaleInPlace (packed_fideslib.cpp:236) — OpenFHE DropLastElementAndScale. */
+int fhe_rescale(fhe_ctx* ctx, fhe_ct* ct);
+/* LevelReduceInPlace: drop limbs without scaling. */
+int fhe_level_reduce(fhe_ctx* ctx, fhe_ct* ct, uint32_t levels);
+/* EvalRotate(ct, step) (packed_fideslib.cpp:207-221): key switch, then automorphism. */
+int fhe_rotate(fhe_ctx* ctx, const fhe_ct* a, int32_t step, fhe_ct** out);
+/* EvalConjugate. */
+int fhe_conjugate(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
+/* EvalFastRotationPrecompute + EvalFastRotation (src/fideslib_rotation_batch.hpp:8-23):
+ * one ModUp shared by n rotations; outs receives n new handles. */
+int fhe_rotate_hoisted(fhe_ctx* ctx, const fhe_ct* a, const int32_t* steps, uint32_t n, fhe_ct** outs);
+
 #ifdef __cplusplus
 }
 #endif
