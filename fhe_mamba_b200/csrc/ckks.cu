@@ -614,15 +614,26 @@ std::unique_ptr<Ct> Ckks::adjust(const Ct& a, uint32_t nq, double scale) {
   auto c = clone(a);
   if (c->noise_deg == 2 && c->nq > nq) rescale_inplace(*c);
   if (std::fabs(c->scale / scale - 1.0) > 1e-12) {
-    require(c->nq > nq, "adjust: scales differ at the same level", -4);
-    // times round(scale * q_last / s), then rescale: new scale = s * C / q_last ~ scale
-    const long double C = (long double)scale * (long double)ctx.primes[c->nq - 1] / (long double)c->scale;
-    require(C >= 1.0L && C < 9.2e18L, "adjust: scale ratio out of range", -4);
-    auto m = mul_int(*c, (int64_t)roundl(C));
-    m->noise_deg = c->noise_deg + 1;
-    c = std::move(m);
-    rescale_inplace(*c);
-    c->scale = scale;
+    // Either times round(scale * q_last / s) and a rescale (consumes the
+    // level being dropped anyway), or, when the target carries a squared
+    // scale, drop limbs first and multiply by round(scale / s).
+    const long double C =
+        c->nq > nq ? (long double)scale * (long double)ctx.primes[c->nq - 1] / (long double)c->scale : 0.0L;
+    if (C >= 1.0L && C < 9.2e18L) {
+      auto m = mul_int(*c, (int64_t)roundl(C));
+      m->noise_deg = c->noise_deg + 1;
+      c = std::move(m);
+      rescale_inplace(*c);
+      c->scale = scale;
+    } else {
+      if (c->nq > nq) level_reduce_inplace(*c, c->nq - nq);
+      const long double R = (long double)scale / (long double)c->scale;
+      require(R >= 1.0L && R < 4.6e18L, "adjust: scale ratio out of range", -4);
+      auto m = mul_int(*c, (int64_t)roundl(R));
+      m->noise_deg = c->noise_deg + 1;
+      m->scale = scale;
+      c = std::move(m);
+    }
   }
   if (c->nq > nq) level_reduce_inplace(*c, c->nq - nq);
   return c;
