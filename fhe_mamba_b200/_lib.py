@@ -116,6 +116,7 @@ SIGNATURES = {
     "fhe_rotate": [vp, vp, i32, ctypes.POINTER(vp)],
     "fhe_conjugate": [vp, vp, ctypes.POINTER(vp)],
     "fhe_rotate_hoisted": [vp, vp, PI32, u32, ctypes.POINTER(vp)],
+    "fhe_rescale_noalloc": [vp, vp, u32, u32, vp],
 }
 
 _lock = threading.Lock()

@@ -8,6 +8,10 @@
 #include "ckks.h"
 #include "context.h"
 
+namespace fhe {
+void rescale_noalloc(Context& c, const uint64_t* in, uint32_t ncomp, uint32_t nq, uint64_t* out);
+}
+
 // Member order matters: ck refers to c and is destroyed first.
 struct fhe_ctx {
   fhe::Context c;
@@ -224,6 +228,13 @@ int fhe_ntt(fhe_ctx* ctx, uint64_t* data, uint32_t n_polys, uint32_t limb0, uint
 
 int fhe_intt(fhe_ctx* ctx, uint64_t* data, uint32_t n_polys, uint32_t limb0, uint32_t n_limbs, int mem) {
   return guarded([&] { raw_transform(ctx, data, n_polys, limb0, n_limbs, mem, true); });
+}
+
+int fhe_rescale_noalloc(fhe_ctx* ctx, const uint64_t* in, uint32_t ncomp, uint32_t n_limbs, uint64_t* out) {
+  return guarded([&] {
+    fhe::require(ctx != nullptr, "null context");
+    fhe::rescale_noalloc(ctx->c, in, ncomp, n_limbs, out);
+  });
 }
 
 // ---------------------------------------------------------------------------

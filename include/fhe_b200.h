@@ -207,6 +207,22 @@ int fhe_conjugate(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
  * one ModUp shared by n rotations; outs receives n new handles. */
 int fhe_rotate_hoisted(fhe_ctx* ctx, const fhe_ct* a, const int32_t* steps, uint32_t n, fhe_ct** outs);
 
+/* Rescale that allocates nothing.  This entry point has no counterpart in the
+ * reference; it exists for callers that cannot let the library allocate
+ * device memory when they rescale — code working inside a memory budget
+ * reserved in advance, or a host framework that owns every device allocation.
+ * `in` holds device residues [ncomp][n_limbs][N] (NTT form), `out` receives
+ * [ncomp][n_limbs-1][N] (must not overlap `in`); the result equals
+ * fhe_rescale word for word.  Scratch comes from one fixed 32 MiB device
+ * array that every GPU loading this library keeps until the process exits;
+ * sizes needing more (2(n_limbs-1) + ncomp*N*n_limbs words) are rejected with
+ * FHE_ERR_INVALID.  The first call on each device looks up that array's
+ * device address, so make it before any stream capture.  All calls share the
+ * one array, so calls whose GPU work overlaps (other contexts, other streams)
+ * race; the array keeps the last call's contents, and every word a call reads
+ * was written earlier by the same call. */
+int fhe_rescale_noalloc(fhe_ctx* ctx, const uint64_t* in, uint32_t ncomp, uint32_t n_limbs, uint64_t* out);
+
 #ifdef __cplusplus
 }
 #endif
