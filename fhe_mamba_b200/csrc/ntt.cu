@@ -81,7 +81,7 @@ __device__ __forceinline__ Twiddle ld_tw(const Twiddle* t, uint32_t i) {
 // j = col0 + c + 2^LB * k for k in [0, 2^LA).  Warp w is thread t of each
 // column.  Round 1: k = t + T*u.  Round 2: k = R*t + u.
 template <int LA>
-__global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA >= 8 ? 1 : 2)
+__global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA <= 8 ? 2 : 1)
     ntt_fwd_cols(const NttArgs g) {
   using P = PassShape<LA>;
   extern __shared__ uint64_t smem[];
@@ -147,7 +147,7 @@ __device__ __forceinline__ int rpad(int k) { return k + (k >> 4); }
 // stores are contiguous.  Thread t of a row: round 1 k = t + T*u, round 2
 // k = R*t + u.  Final output reduced from [0, 4q) to [0, q).
 template <int LB, int ROWS>
-__global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
+__global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
     ntt_fwd_rows(const NttArgs g) {
   using P = PassShape<LB>;
   extern __shared__ uint64_t smem[];
@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
 // Round 1 on contiguous runs k = R*t + u (half-distances 1 .. T/2), exchange,
 // round 2 on k = t + T*u (half-distances T .. S/2).  Input in [0, q).
 template <int LB, int ROWS>
-__global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
+__global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
     ntt_inv_rows(const NttArgs g) {
   using P = PassShape<LB>;
   extern __shared__ uint64_t smem[];
@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T)
 // The last stage (m = 1) folds in N^{-1}: x' = (x+y)/N, y' = (x-y)*w/N, with
 // tw_last = (N^{-1}, N^{-1}') and tw_last2 = (w_1 N^{-1}, ...).
 template <int LA>
-__global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA >= 8 ? 1 : 2)
+__global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA <= 8 ? 2 : 1)
     ntt_inv_cols(const NttArgs g) {
   using P = PassShape<LA>;
   extern __shared__ uint64_t smem[];
