@@ -243,12 +243,45 @@ void Context::build_tables() {
     const uint32_t b = nt::bitlen(q);
     mods[i] = Modulus{q, (uint64_t)(((u128)1 << (2 * b)) / q), b, 0};
   };
+  // Row-pass round-2 twiddles: for row r, thread t and the j-th twiddle the
+  // thread uses (forward: half-distances T/2..1, inverse: 1..T/2, groups g in
+  // steps of 2h), entry = table[n/(2h) + r*(S/(2h)) + (R*t + g)/(2h)].
+  int rows = 0, R = 0, T = 0, J = 0;
+  ntt_row_shape((int)log_n, rows, R, T, J);
+  const uint32_t S = n / rows;
+  tw2_stride = (uint32_t)rows * J * T;
+  std::vector<Twiddle> tw2((size_t)np * tw2_stride), tw2i((size_t)np * tw2_stride);
+  auto work2 = [&](uint32_t i) {
+    const Twiddle* f = tw.data() + (size_t)i * n;
+    const Twiddle* g = twi.data() + (size_t)i * n;
+    for (int r = 0; r < rows; ++r) {
+      int j = 0;
+      for (int h = T / 2; h >= 1; h >>= 1)
+        for (int gg = 0; gg < R; gg += 2 * h, ++j)
+          for (int t = 0; t < T; ++t)
+            tw2[(size_t)i * tw2_stride + ((size_t)r * J + j) * T + t] =
+                f[n / (2 * h) + r * (S / (2 * h)) + (R * t + gg) / (2 * h)];
+      j = 0;
+      for (int h = 1; h <= T / 2; h <<= 1)
+        for (int gg = 0; gg < R; gg += 2 * h, ++j)
+          for (int t = 0; t < T; ++t)
+            tw2i[(size_t)i * tw2_stride + ((size_t)r * J + j) * T + t] =
+                g[n / (2 * h) + r * (S / (2 * h)) + (R * t + gg) / (2 * h)];
+    }
+  };
   const uint32_t nthreads = std::max(1u, std::min<uint32_t>(np, std::thread::hardware_concurrency()));
   std::vector<std::thread> pool;
   for (uint32_t t = 0; t < nthreads; ++t)
     pool.emplace_back([&, t] {
       for (uint32_t i = t; i < np; i += nthreads) work(i);
     });
+  for (auto& th : pool) th.join();
+  pool.clear();
+  if (tw2_stride)
+    for (uint32_t t = 0; t < nthreads; ++t)
+      pool.emplace_back([&, t] {
+        for (uint32_t i = t; i < np; i += nthreads) work2(i);
+      });
   for (auto& th : pool) th.join();
 
   d_primes = DevMem(np * sizeof(uint64_t));
@@ -261,6 +294,12 @@ void Context::build_tables() {
   FHE_CUDA(cudaMemcpy(d_tw.p, tw.data(), tw.size() * sizeof(Twiddle), cudaMemcpyHostToDevice));
   FHE_CUDA(cudaMemcpy(d_tw_inv.p, twi.data(), twi.size() * sizeof(Twiddle), cudaMemcpyHostToDevice));
   FHE_CUDA(cudaMemcpy(d_ninv.p, ninv.data(), ninv.size() * sizeof(Twiddle), cudaMemcpyHostToDevice));
+  if (tw2_stride) {
+    d_tw2 = DevMem(tw2.size() * sizeof(Twiddle));
+    d_tw2_inv = DevMem(tw2i.size() * sizeof(Twiddle));
+    FHE_CUDA(cudaMemcpy(d_tw2.p, tw2.data(), tw2.size() * sizeof(Twiddle), cudaMemcpyHostToDevice));
+    FHE_CUDA(cudaMemcpy(d_tw2_inv.p, tw2i.data(), tw2i.size() * sizeof(Twiddle), cudaMemcpyHostToDevice));
+  }
 }
 
 uint64_t* Context::stage(size_t words) {
@@ -279,12 +318,18 @@ NttArgs Context::ntt_args(uint64_t* data, uint32_t n_polys, uint32_t prime0, uin
   a.tw_inv = d_tw_inv.as<Twiddle>();
   a.primes = d_primes.as<uint64_t>();
   a.ninv = d_ninv.as<Twiddle>();
+  a.tw2 = d_tw2.as<Twiddle>();
+  a.tw2_inv = d_tw2_inv.as<Twiddle>();
+  a.tw2_stride = tw2_stride;
   a.log_n = (int)log_n;
   a.n_polys = n_polys;
   a.n_limbs = n_limbs;
   a.limb_stride = limb_stride;
   a.prime0 = prime0;
   a.stream = stream;
+  bool lazy = prime0 + n_limbs <= primes.size();
+  for (uint32_t i = prime0; lazy && i < prime0 + n_limbs; ++i) lazy = primes[i] < (uint64_t(1) << 59);
+  a.lazy = lazy;
   return a;
 }
 

@@ -75,6 +75,10 @@ struct Context {
   DevMem d_tw;      // Twiddle[L+K][N]
   DevMem d_tw_inv;  // Twiddle[L+K][N]
   DevMem d_ninv;    // Twiddle[L+K][2]
+  // Round-2 twiddles of the row passes re-laid out thread-fastest so every
+  // load of a warp is contiguous: [prime][row][j][t] (forward, inverse).
+  DevMem d_tw2, d_tw2_inv;
+  uint32_t tw2_stride = 0;  // entries per prime
 
   // Staging buffer for host-memory entry points.
   DevMem d_stage;

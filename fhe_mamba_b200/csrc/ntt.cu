@@ -39,12 +39,25 @@ struct PassShape {
   static constexpr int LT = LS - LR;       // stages in round 2
   static constexpr int T = 1 << LT;        // threads per sub-problem
   static constexpr int S = 1 << LS;        // sub-problem size
+  static constexpr int J = R * (T - 1) / T;  // round-2 twiddles per thread
 };
 
 // Forward Cooley-Tukey (Harvey) butterfly on lazy residues in [0, 4q).
 __device__ __forceinline__ void ct_bfly(uint64_t& x, uint64_t& y, const Twiddle tw, uint64_t q,
                                         uint64_t q2) {
   x = csub(x, q2);
+  const uint64_t t = shoup_lazy(y, tw.w, tw.wp, q);
+  y = x + q2 - t;
+  x = x + t;
+}
+
+// Forward butterfly without reducing x: every output grows by at most 2q.
+// Used while the running bound stays below 2^64 (all primes < 2^59, see the
+// schedule in ntt_fwd_rows).  With red16, x is first brought below 16q.
+template <bool kReduce16>
+__device__ __forceinline__ void ct_bfly_lazy(uint64_t& x, uint64_t& y, const Twiddle tw, uint64_t q,
+                                             uint64_t q2, uint64_t q16) {
+  if (kReduce16) x = csub(x, q16);
   const uint64_t t = shoup_lazy(y, tw.w, tw.wp, q);
   y = x + q2 - t;
   x = x + t;
@@ -80,7 +93,7 @@ __device__ __forceinline__ Twiddle ld_tw(const Twiddle* t, uint32_t i) {
 // Forward, pass 1: columns.  Column c of the tile (lane) holds words
 // j = col0 + c + 2^LB * k for k in [0, 2^LA).  Warp w is thread t of each
 // column.  Round 1: k = t + T*u.  Round 2: k = R*t + u.
-template <int LA>
+template <int LA, bool LAZY>
 __global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA <= 8 ? 2 : 1)
     ntt_fwd_cols(const NttArgs g) {
   using P = PassShape<LA>;
@@ -108,7 +121,10 @@ __global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA <= 8 ? 2 : 
     for (int g = 0; g < P::R; g += 2 * h) {
       const Twiddle w = ld_tw(tw, m + g / (2 * h));
 #pragma unroll
-      for (int v = 0; v < h; ++v) ct_bfly(x[g + v], x[g + v + h], w, q, q2);
+      for (int v = 0; v < h; ++v) {
+        if constexpr (LAZY) ct_bfly_lazy<false>(x[g + v], x[g + v + h], w, q, q2, 0);
+        else ct_bfly(x[g + v], x[g + v + h], w, q, q2);
+      }
     }
   }
   if constexpr (P::LT > 0) {
@@ -126,7 +142,10 @@ __global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA <= 8 ? 2 : 
       for (int g = 0; g < P::R; g += 2 * h) {
         const Twiddle w = ld_tw(tw, m + (P::R * t + g) / (2 * h));
 #pragma unroll
-        for (int v = 0; v < h; ++v) ct_bfly(x[g + v], x[g + v + h], w, q, q2);
+        for (int v = 0; v < h; ++v) {
+          if constexpr (LAZY) ct_bfly_lazy<false>(x[g + v], x[g + v + h], w, q, q2, 0);
+          else ct_bfly(x[g + v], x[g + v + h], w, q, q2);
+        }
       }
     }
 #pragma unroll
@@ -146,7 +165,13 @@ __device__ __forceinline__ int rpad(int k) { return k + (k >> 4); }
 // tile is staged through shared memory in both directions so global loads and
 // stores are contiguous.  Thread t of a row: round 1 k = t + T*u, round 2
 // k = R*t + u.  Final output reduced from [0, 4q) to [0, q).
-template <int LB, int ROWS>
+//
+// LAZY schedule (every prime of the launch below 2^59, so 32q < 2^64): the
+// column pass never reduces (outputs < (2 LA + 1) q <= 17q); here the first
+// stage of each round brings x below 16q and the others do not reduce, so
+// values stay below 18q + 2q * (stages - 1) <= 26q; the output is reduced
+// with one Shoup multiplication by 1 and a conditional subtraction.
+template <int LB, int ROWS, bool LAZY>
 __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
     ntt_fwd_rows(const NttArgs g) {
   using P = PassShape<LB>;
@@ -155,11 +180,16 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
   const uint32_t n = 1u << g.log_n;
   uint32_t pidx;
   uint64_t* a = block_limb(g, n, pidx) + (size_t)blockIdx.x * ROWS * P::S;
-  const uint64_t q = g.primes[pidx], q2 = 2 * q;
+  const uint64_t q = g.primes[pidx], q2 = 2 * q, q16 = 16 * q;
+  const uint64_t mu = LAZY ? ~0ull / q : 0;  // floor(2^64 / q), Shoup companion of 1
   const Twiddle* tw = g.tw + (size_t)pidx * n;
   const int t = threadIdx.x % P::T;
   const int rr = threadIdx.x / P::T;
   const uint32_t row = blockIdx.x * ROWS + rr;
+  auto fwd_final = [](uint64_t v, uint64_t q, uint64_t q2, uint64_t mu) {
+    if constexpr (LAZY) return csub(shoup_lazy(v, 1, mu, q), q);
+    else return csub(csub(v, q2), q);
+  };
 
   // Coalesced tile load: ROWS*S contiguous words.
   constexpr int kThreads = ROWS * P::T;
@@ -185,7 +215,14 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
     for (int g = 0; g < P::R; g += 2 * h) {
       const Twiddle w = ld_tw(tw, base + g / (2 * h));
 #pragma unroll
-      for (int v = 0; v < h; ++v) ct_bfly(x[g + v], x[g + v + h], w, q, q2);
+      for (int v = 0; v < h; ++v) {
+        if constexpr (LAZY) {
+          if (h == P::R / 2) ct_bfly_lazy<true>(x[g + v], x[g + v + h], w, q, q2, q16);
+          else ct_bfly_lazy<false>(x[g + v], x[g + v + h], w, q, q2, q16);
+        } else {
+          ct_bfly(x[g + v], x[g + v + h], w, q, q2);
+        }
+      }
     }
   }
   if constexpr (P::LT > 0) {
@@ -195,23 +232,30 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
     __syncthreads();
 #pragma unroll
     for (int u = 0; u < P::R; ++u) x[u] = srow[rpad(P::R * t + u)];
+    const Twiddle* t2 = g.tw2 + (size_t)pidx * g.tw2_stride + (size_t)row * (P::J * P::T) + t;
+    int j = 0;
 #pragma unroll
     for (int h = P::T / 2; h >= 1; h >>= 1) {
-      const uint32_t m = n / (2 * h);
-      const uint32_t base = m + row * (P::S / (2 * h));
 #pragma unroll
-      for (int g = 0; g < P::R; g += 2 * h) {
-        const Twiddle w = ld_tw(tw, base + (P::R * t + g) / (2 * h));
+      for (int g = 0; g < P::R; g += 2 * h, ++j) {
+        const Twiddle w = ld_tw(t2, j * P::T);
 #pragma unroll
-        for (int v = 0; v < h; ++v) ct_bfly(x[g + v], x[g + v + h], w, q, q2);
+        for (int v = 0; v < h; ++v) {
+          if constexpr (LAZY) {
+            if (h == P::T / 2) ct_bfly_lazy<true>(x[g + v], x[g + v + h], w, q, q2, q16);
+            else ct_bfly_lazy<false>(x[g + v], x[g + v + h], w, q, q2, q16);
+          } else {
+            ct_bfly(x[g + v], x[g + v + h], w, q, q2);
+          }
+        }
       }
     }
 #pragma unroll
-    for (int u = 0; u < P::R; ++u) srow[rpad(P::R * t + u)] = csub(csub(x[u], q2), q);
+    for (int u = 0; u < P::R; ++u) srow[rpad(P::R * t + u)] = fwd_final(x[u], q, q2, mu);
   } else {
     __syncthreads();
 #pragma unroll
-    for (int u = 0; u < P::R; ++u) srow[rpad(t + P::T * u)] = csub(csub(x[u], q2), q);
+    for (int u = 0; u < P::R; ++u) srow[rpad(t + P::T * u)] = fwd_final(x[u], q, q2, mu);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < ROWS * P::S / 2; i += kThreads) {
@@ -255,13 +299,13 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
   if constexpr (P::LT > 0) {
 #pragma unroll
     for (int u = 0; u < P::R; ++u) x[u] = srow[rpad(P::R * t + u)];
+    const Twiddle* t2 = g.tw2_inv + (size_t)pidx * g.tw2_stride + (size_t)row * (P::J * P::T) + t;
+    int j = 0;
 #pragma unroll
     for (int h = 1; h <= P::T / 2; h <<= 1) {
-      const uint32_t m = n / (2 * h);
-      const uint32_t base = m + row * (P::S / (2 * h));
 #pragma unroll
-      for (int g = 0; g < P::R; g += 2 * h) {
-        const Twiddle w = ld_tw(tw, base + (P::R * t + g) / (2 * h));
+      for (int g = 0; g < P::R; g += 2 * h, ++j) {
+        const Twiddle w = ld_tw(t2, j * P::T);
 #pragma unroll
         for (int v = 0; v < h; ++v) gs_bfly(x[g + v], x[g + v + h], w, q, q2);
       }
@@ -379,23 +423,28 @@ size_t cols_smem() {
   return P::LT > 0 ? (size_t)kColsPerCta * P::S * sizeof(uint64_t) : 0;
 }
 
-template <int LA, int LB>
-cudaError_t launch_fwd(const NttArgs& g) {
+template <int LA, int LB, bool LAZY>
+cudaError_t launch_fwd_impl(const NttArgs& g) {
   using PA = PassShape<LA>;
   using PB = PassShape<LB>;
   const size_t sa = cols_smem<LA>(), sb = rows_smem<LB>();
   cudaError_t e;
-  e = cudaFuncSetAttribute(ntt_fwd_cols<LA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa);
+  e = cudaFuncSetAttribute(ntt_fwd_cols<LA, LAZY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(ntt_fwd_rows<LB, kRowsPerCta>,
+  e = cudaFuncSetAttribute(ntt_fwd_rows<LB, kRowsPerCta, LAZY>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
   if (e != cudaSuccess) return e;
   const uint32_t polys = g.list ? 1 : g.n_polys;
   dim3 ga((1u << LB) / kColsPerCta, polys, g.n_limbs);
-  ntt_fwd_cols<LA><<<ga, kColsPerCta * PA::T, sa, g.stream>>>(g);
+  ntt_fwd_cols<LA, LAZY><<<ga, kColsPerCta * PA::T, sa, g.stream>>>(g);
   dim3 gb((1u << LA) / kRowsPerCta, polys, g.n_limbs);
-  ntt_fwd_rows<LB, kRowsPerCta><<<gb, kRowsPerCta * PB::T, sb, g.stream>>>(g);
+  ntt_fwd_rows<LB, kRowsPerCta, LAZY><<<gb, kRowsPerCta * PB::T, sb, g.stream>>>(g);
   return cudaGetLastError();
+}
+
+template <int LA, int LB>
+cudaError_t launch_fwd(const NttArgs& g) {
+  return g.lazy ? launch_fwd_impl<LA, LB, true>(g) : launch_fwd_impl<LA, LB, false>(g);
 }
 
 template <int LA, int LB>
@@ -418,6 +467,15 @@ cudaError_t launch_inv(const NttArgs& g) {
 }
 
 }  // namespace
+
+void ntt_row_shape(int log_n, int& rows, int& R, int& T, int& J) {
+  const int LA = log_n / 2, LB = log_n - LA;
+  const int LR = (LB + 1) / 2, LT = LB - LR;
+  rows = 1 << LA;
+  R = 1 << LR;
+  T = 1 << LT;
+  J = R * (T - 1) / T;
+}
 
 // log N = LA + LB with LA = floor(logN/2) >= 5 so both passes have >= 32
 // columns / rows per CTA tile.

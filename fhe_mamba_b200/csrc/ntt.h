@@ -21,8 +21,19 @@ struct NttArgs {
   // Optional explicit limb list (device array, n_limbs entries, n_polys must
   // be 1): entry {x, y} transforms the limb at data + x*N with prime y.
   const uint2* list = nullptr;
+  // Every prime the launch touches is below 2^59: the forward transform may
+  // skip most intermediate reductions (see ntt_fwd_rows).
+  bool lazy = false;
+  // Row-pass round-2 twiddles, thread-fastest layout (see Context::build_tables).
+  const Twiddle* tw2 = nullptr;
+  const Twiddle* tw2_inv = nullptr;
+  uint32_t tw2_stride = 0;
   cudaStream_t stream;
 };
+
+// Shape of the row pass for a ring of 2^log_n: rows of 2^LB words, R words per
+// thread, T threads per row; J round-2 twiddles per thread.
+void ntt_row_shape(int log_n, int& rows, int& R, int& T, int& J);
 
 cudaError_t ntt_forward(const NttArgs& args);
 cudaError_t ntt_inverse(const NttArgs& args);
