@@ -117,6 +117,8 @@ SIGNATURES = {
     "fhe_conjugate": [vp, vp, ctypes.POINTER(vp)],
     "fhe_rotate_hoisted": [vp, vp, PI32, u32, ctypes.POINTER(vp)],
     "fhe_rescale_noalloc": [vp, vp, u32, u32, vp],
+    "fhe_encode_batch": [vp, PD, PD, u32, u32, u32, f64, ctypes.POINTER(vp)],
+    "fhe_linear_transform": [vp, vp, ctypes.POINTER(vp), u32, u32, ctypes.POINTER(vp)],
 }
 
 _lock = threading.Lock()

@@ -217,6 +217,25 @@ class CryptoContext:
              float(scale), ctypes.byref(h))
         return Plaintext(self, h)
 
+    def MakeCKKSPackedPlaintexts(self, vectors, level=0, scale=0.0):
+        """Batched MakeCKKSPackedPlaintext (one device pass for many vectors)."""
+        arr = np.asarray(vectors, dtype=np.complex128)
+        if arr.ndim != 2:
+            raise _lib.InvalidArgument(-1, "MakeCKKSPackedPlaintexts", "expected a 2-D array of vectors")
+        re = np.ascontiguousarray(arr.real)
+        im = np.ascontiguousarray(arr.imag)
+        outs = (vp * arr.shape[0])()
+        call("fhe_encode_batch", self.h, re.ctypes.data_as(PD), im.ctypes.data_as(PD), arr.shape[0],
+             arr.shape[1], self.n_q - level, float(scale), outs)
+        return [Plaintext(self, vp(o)) for o in outs]
+
+    def EvalLinearTransform(self, ct, diagonals, baby: int, giant: int):
+        """out = sum_g rot(sum_j diagonals[g*baby+j] (.) rot(ct, j), g*baby); None = zero diagonal."""
+        if len(diagonals) != baby * giant:
+            raise _lib.InvalidArgument(-1, "EvalLinearTransform", "need baby*giant diagonals")
+        arr = (vp * len(diagonals))(*[d.handle if d is not None else None for d in diagonals])
+        return self._ct("fhe_linear_transform", ct.handle, arr, baby, giant)
+
     def Encrypt(self, pt: Plaintext, _unused=None):
         if isinstance(_unused, Plaintext):  # Encrypt(publicKey, pt) call order
             pt = _unused
@@ -329,3 +348,28 @@ class CryptoContext:
 
 def GenCryptoContext(params: CCParams) -> CryptoContext:
     return CryptoContext(params)
+
+
+def bsgs_diagonals(W: np.ndarray, baby: int, giant: int, slots: int):
+    """Diagonal layout for y = W x (W: m x n) with the input replicated twice
+    (slot s holds x[s mod n] for s < 2n).  Diagonal d = g*baby + j holds
+    W[i, (i + d) mod n] at slot i + g*baby (pre-rotated by the giant step), so
+    sum_g rot(sum_j diag (.) rot(x_rep, j), g*baby) puts y[i] in slot i.
+    Returns baby*giant arrays (None for diagonals d >= n)."""
+    m, n = W.shape
+    if baby * giant < n:
+        raise ValueError("baby*giant must cover every diagonal")
+    if (giant - 1) * baby + m > slots or 2 * n > slots:
+        raise ValueError("layout does not fit the slots")
+    rows = np.arange(m)
+    out = []
+    for g in range(giant):
+        for j in range(baby):
+            d = g * baby + j
+            if d >= n:
+                out.append(None)
+                continue
+            v = np.zeros(slots)
+            v[g * baby + rows] = W[rows, (rows + d) % n]
+            out.append(v)
+    return out

@@ -515,4 +515,27 @@ int fhe_rotate_hoisted(fhe_ctx* ctx, const fhe_ct* a, const int32_t* steps, uint
   });
 }
 
+int fhe_encode_batch(fhe_ctx* ctx, const double* re, const double* im, uint32_t batch, uint32_t count,
+                     uint32_t n_limbs, double scale, fhe_pt** outs) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(outs != nullptr && (re != nullptr || count == 0), "null values or outputs");
+    const uint32_t nq = n_limbs ? n_limbs : ctx->c.L;
+    fhe::require(nq <= ctx->c.L, "n_limbs above the number of Q primes");
+    auto v = k.encode_batch(re, im, batch, count, nq, scale > 0 ? scale : k.level_scale(nq));
+    for (uint32_t i = 0; i < batch; ++i) outs[i] = new fhe_pt{std::move(v[i])};
+  });
+}
+
+int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* diags, uint32_t baby,
+                         uint32_t giant, fhe_ct** out) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(diags != nullptr, "null diagonal array");
+    std::vector<const fhe::Pt*> d((size_t)baby * giant);
+    for (size_t i = 0; i < d.size(); ++i) d[i] = diags[i] ? diags[i]->p.get() : nullptr;
+    put_ct(out, k.linear_transform(ct_of(a), d, baby, giant));
+  });
+}
+
 }  // extern "C"

@@ -352,6 +352,49 @@ std::unique_ptr<Pt> Ckks::encode(const double* re, const double* im, uint32_t co
   return p;
 }
 
+std::vector<std::unique_ptr<Pt>> Ckks::encode_batch(const double* re, const double* im, uint32_t B, uint32_t count,
+                                                    uint32_t nq, double scale) {
+  const uint32_t slots = ctx.slots, n = ctx.n;
+  require(count <= slots, "more values than slots", -1);
+  require(nq >= 1 && nq <= ctx.L, "limb count out of range", -1);
+  std::vector<std::unique_ptr<Pt>> out;
+  const uint32_t chunk = std::max(1u, std::min(B, (uint32_t)((64u << 20) / (16ull * slots))));
+  std::vector<double2> v((size_t)chunk * slots);
+  for (uint32_t b0 = 0; b0 < B; b0 += chunk) {
+    const uint32_t nb = std::min(chunk, B - b0);
+    for (uint32_t b = 0; b < nb; ++b)
+      for (uint32_t i = 0; i < slots; ++i) {
+        const size_t src = (size_t)(b0 + b) * count + i;
+        v[(size_t)b * slots + i] =
+            i < count ? make_double2(re ? re[src] : 0.0, im ? im[src] : 0.0) : make_double2(0.0, 0.0);
+      }
+    double2* dv = reinterpret_cast<double2*>(ws(18, 2 * (size_t)nb * slots));
+    FHE_CUDA(cudaMemcpyAsync(dv, v.data(), (size_t)nb * slots * sizeof(double2), cudaMemcpyHostToDevice, ctx.stream));
+    launch_fft_special_inv(dv, fft_inv_tw_.as<double2>(), slots, nb, ctx.stream);
+    int64_t* coef = reinterpret_cast<int64_t*>(ws(19, (size_t)nb * n));
+    FHE_CUDA(cudaMemsetAsync(coef, 0, (size_t)nb * n * 8, ctx.stream));
+    FHE_CUDA(cudaMemsetAsync(status_.p, 0, sizeof(unsigned), ctx.stream));
+    launch_encode_round_batch(dv, coef, slots, n, scale, nb, status_.as<unsigned>(), ctx.stream);
+    uint64_t* res = ws(20, (size_t)nb * nq * n);
+    launch_lift_small_batch(coef, res, n, nq, PrimeMap{nq, ctx.L}, ctx.d_primes.as<uint64_t>(), nb, ctx.stream);
+    ntt_dense(res, nb, nq, nq, 0, false);
+    for (uint32_t b = 0; b < nb; ++b) {
+      auto p = std::make_unique<Pt>();
+      p->buf = DevMem((size_t)nq * n * 8);
+      p->nq = nq;
+      p->scale = scale;
+      FHE_CUDA(cudaMemcpyAsync(p->data(), res + (size_t)b * nq * n, (size_t)nq * n * 8, cudaMemcpyDeviceToDevice,
+                               ctx.stream));
+      out.push_back(std::move(p));
+    }
+    unsigned st = 0;
+    FHE_CUDA(cudaMemcpyAsync(&st, status_.p, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx.stream));
+    FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+    require(st == 0, "encode: a scaled value is not finite or exceeds 2^62", -1);
+  }
+  return out;
+}
+
 void Ckks::decode(const Pt& p, double* re, double* im, uint32_t count) {
   const uint32_t slots = ctx.slots, n = ctx.n;
   require(count <= slots, "more values than slots", -1);
@@ -423,6 +466,12 @@ std::unique_ptr<Ct> Ckks::encrypt(const Pt& p) {
 
 std::unique_ptr<Pt> Ckks::decrypt(const Ct& c) {
   require(keyed_, "decrypt before keygen", -4);
+  if (c.noise_deg >= 2 && c.nq >= 2 && c.ncomp == 2) {
+    // FLEXIBLEAUTO: a degree-2 ciphertext is rescaled before decryption.
+    auto t = clone(c);
+    rescale_inplace(*t);
+    return decrypt(*t);
+  }
   const uint32_t nq = c.nq, n = ctx.n;
   const Modulus* mods = ctx.d_mod.as<Modulus>();
   const PrimeMap q{nq, ctx.L};
@@ -536,6 +585,53 @@ std::vector<std::unique_ptr<Ct>> Ckks::rotate_hoisted(const Ct& a, const std::ve
     outs.push_back(std::move(out));
   }
   return outs;
+}
+
+std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a, const std::vector<const Pt*>& diags, uint32_t b,
+                                           uint32_t G) {
+  require(a.ncomp == 2, "linear transform expects a 2-component ciphertext", -1);
+  require(b >= 1 && b <= 32 && G >= 1, "baby step must be in [1, 32], giant step >= 1", -1);
+  require(diags.size() == (size_t)b * G, "need baby*giant diagonal entries", -1);
+  const uint32_t nq = a.nq, n = ctx.n;
+  double pscale = 0.0;
+  for (const Pt* p : diags)
+    if (p) {
+      require(p->nq >= nq, "a diagonal has fewer limbs than the ciphertext", -1);
+      if (pscale == 0.0) pscale = p->scale;
+      require(std::fabs(p->scale / pscale - 1.0) < 1e-12, "diagonals must share one scale", -1);
+    }
+  require(pscale != 0.0, "every diagonal is zero", -1);
+  // Babies: j = 0 is the input itself, 1..b-1 share one ModUp.
+  std::vector<uint64_t> gs;
+  for (uint32_t j = 1; j < b; ++j) gs.push_back(galois_for_step(j));
+  auto rot = rotate_hoisted(a, gs);
+  auto base = clone(a);  // cap == nq, component stride nq*N like the rotations
+  std::vector<const uint64_t*> bp{base->data()};
+  for (auto& r : rot) bp.push_back(r->data());
+  std::vector<const uint64_t*> dp(diags.size());
+  for (size_t i = 0; i < diags.size(); ++i) dp[i] = diags[i] ? diags[i]->data() : nullptr;
+  DevMem d_bp = upload(bp), d_dp = upload(dp);
+  const size_t cs = (size_t)nq * n;
+  uint64_t* inner = ws(21, (size_t)G * 2 * cs);
+  launch_bsgs_dot(d_bp.as<const uint64_t*>(), d_dp.as<const uint64_t*>(), inner, b, G, nq, n,
+                  ctx.d_mod.as<Modulus>(), ctx.stream);
+  auto out = alloc(nq, 2);
+  out->scale = a.scale * pscale;
+  out->noise_deg = a.noise_deg + 1;
+  FHE_CUDA(cudaMemcpyAsync(out->data(), inner, 2 * cs * 8, cudaMemcpyDeviceToDevice, ctx.stream));
+  for (uint32_t g = 1; g < G; ++g) {
+    auto it = rot_.find(galois_for_step((int64_t)g * b));
+    require(it != rot_.end(), "missing rotation key for giant step " + std::to_string(g * b), -4);
+    const uint64_t* ig = inner + (size_t)g * 2 * cs;
+    uint64_t* u = ws(4, 2 * cs);
+    keyswitch(ig + cs, nq, it->second.as<uint64_t>(), u, cs, ig);
+    uint64_t* r = ws(22, 2 * cs);
+    launch_automorphism(u, cs, r, cs, 2, nq, ctx.log_n, galois_for_step((int64_t)g * b), ctx.stream);
+    launch_ew(Ew::Add, out->data(), cs, r, cs, out->data(), cs, 2, nq, n, PrimeMap{nq, ctx.L},
+              ctx.d_mod.as<Modulus>(), ctx.stream);
+  }
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  return out;
 }
 
 // ---------------------------------------------------------------------------

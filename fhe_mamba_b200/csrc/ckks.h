@@ -63,6 +63,9 @@ class Ckks {
   // encode / encryption
   std::unique_ptr<Pt> encode(const double* re, const double* im, uint32_t count, uint32_t nq, double scale);
   void decode(const Pt& p, double* re, double* im, uint32_t count);
+  // Encodes B vectors of `count` values (values[b*count + i]) at nq limbs.
+  std::vector<std::unique_ptr<Pt>> encode_batch(const double* re, const double* im, uint32_t B, uint32_t count,
+                                                uint32_t nq, double scale);
   std::unique_ptr<Ct> encrypt(const Pt& p);
   std::unique_ptr<Pt> decrypt(const Ct& c);
 
@@ -83,6 +86,12 @@ class Ckks {
   void level_reduce_inplace(Ct& a, uint32_t levels);
   std::unique_ptr<Ct> rotate(const Ct& a, uint64_t g);
   std::vector<std::unique_ptr<Ct>> rotate_hoisted(const Ct& a, const std::vector<uint64_t>& gs);
+
+  // BSGS diagonal linear transform (the reference's PackedEvaluator::linear /
+  // LinearTransformInPlace): out = sum_g rot( sum_j diag[g*b+j] (.) rot(a, j), g*b ).
+  // diags has b*G entries (null = zero diagonal), each encoded at >= a.nq limbs
+  // with the same scale; babies share one ModUp.
+  std::unique_ptr<Ct> linear_transform(const Ct& a, const std::vector<const Pt*>& diags, uint32_t b, uint32_t G);
 
   // Brings `a` to (nq, scale): FLEXIBLEAUTO adjustment by an integer multiple
   // and a rescale, then dropping limbs.

@@ -378,6 +378,94 @@ __global__ void k_decode_crt(const uint64_t* coef, uint32_t nlimbs, uint32_t slo
   v[dst] = make_double2(part[0], part[1]);
 }
 
+__global__ void k_encode_round_batch(const double2* v, int64_t* coef, uint32_t slots, uint32_t log_slots,
+                                     uint32_t n, double scale, unsigned* status) {
+  const uint32_t b = blockIdx.y;
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= slots) return;
+  const uint32_t gap = n / (2 * slots);
+  const uint32_t src = log_slots ? (__brev(i) >> (32 - log_slots)) : 0;
+  const double2 x = v[(size_t)b * slots + src];
+  const double r = __dmul_rn(__ddiv_rn(x.x, (double)slots), scale);
+  const double s = __dmul_rn(__ddiv_rn(x.y, (double)slots), scale);
+  const double lim = 4611686018427387904.0;  // 2^62
+  if (!isfinite(r) || !isfinite(s) || fabs(r) >= lim || fabs(s) >= lim) {
+    atomicOr(status, 1u);
+    return;
+  }
+  int64_t* c = coef + (size_t)b * n;
+  c[(size_t)i * gap] = llround(r);
+  c[(size_t)i * gap + n / 2] = llround(s);
+}
+
+__global__ void k_lift_small_batch(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
+                                   const uint64_t* primes) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y, b = blockIdx.z;
+  const uint64_t q = primes[pm(l)];
+  const int64_t v = src[(size_t)b * n + k];
+  uint64_t r;
+  if (v >= 0) {
+    r = (uint64_t)v % q;
+  } else {
+    const uint64_t m = ((uint64_t)(-(v + 1)) + 1) % q;
+    r = m ? q - m : 0;
+  }
+  out[((size_t)b * nlimbs + l) * n + k] = r;
+}
+
+// 128-bit accumulator reduced mod q: (hi 2^64 + lo) mod q with hi < 2^62.
+__device__ __forceinline__ uint64_t reduce128(uint64_t hi, uint64_t lo, const Modulus& m, uint64_t r64) {
+  const uint64_t h = barrett_reduce(0, hi, m);
+  const uint64_t l = barrett_reduce(0, lo, m);
+  return add_mod(mul_mod(h, r64, m), l, m.q);
+}
+
+constexpr int kMaxBaby = 32;
+
+__global__ void __launch_bounds__(128) k_bsgs_dot(const uint64_t* const* babies, const uint64_t* const* diags,
+                                                  uint64_t* out, uint32_t b, uint32_t G, uint32_t nq, uint32_t n,
+                                                  const Modulus* mods) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y;
+  const Modulus m = mods[l];
+  const uint64_t r64 = barrett_reduce(1, 0, m);
+  const size_t off = (size_t)l * n + k, cs = (size_t)nq * n;
+  uint64_t x0[kMaxBaby], x1[kMaxBaby];
+#pragma unroll
+  for (int j = 0; j < kMaxBaby; ++j) {
+    if (j < (int)b) {
+      const uint64_t* bj = babies[j];
+      x0[j] = bj[off];
+      x1[j] = bj[cs + off];
+    }
+  }
+  for (uint32_t g = 0; g < G; ++g) {
+    uint64_t h0 = 0, l0 = 0, h1 = 0, l1 = 0;
+#pragma unroll
+    for (int j = 0; j < kMaxBaby; ++j) {
+      if (j < (int)b) {
+        const uint64_t* dp = diags[g * b + j];
+        if (dp) {
+          const uint64_t d = __ldcs(dp + off);  // streamed once: evict first
+          uint64_t lo = x0[j] * d, hi = __umul64hi(x0[j], d);
+          l0 += lo;
+          h0 += hi + (l0 < lo);
+          lo = x1[j] * d;
+          hi = __umul64hi(x1[j], d);
+          l1 += lo;
+          h1 += hi + (l1 < lo);
+        }
+      }
+    }
+    uint64_t* o = out + (size_t)g * 2 * cs;
+    o[off] = reduce128(h0, l0, m, r64);
+    o[cs + off] = reduce128(h1, l1, m, r64);
+  }
+}
+
 inline dim3 grid1(uint32_t n, uint32_t y = 1, uint32_t z = 1) { return dim3((n + kTpb - 1) / kTpb, y, z); }
 
 uint32_t log2u(uint32_t x) {
@@ -482,6 +570,23 @@ void launch_decode_crt(const uint64_t* coef, uint32_t nlimbs, uint32_t slots, ui
                        double2* v, cudaStream_t s) {
   k_decode_crt<<<grid1(slots), kTpb, 0, s>>>(coef, nlimbs, slots, log2u(slots), n, scale, q0, q1, q0inv_mod_q1,
                                              q0inv_shoup, m1, v);
+}
+
+void launch_encode_round_batch(const double2* v, int64_t* coef, uint32_t slots, uint32_t n, double scale,
+                               uint32_t batch, unsigned* status, cudaStream_t s) {
+  if (!batch) return;
+  k_encode_round_batch<<<grid1(slots, batch), kTpb, 0, s>>>(v, coef, slots, log2u(slots), n, scale, status);
+}
+
+void launch_lift_small_batch(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
+                             const uint64_t* primes, uint32_t batch, cudaStream_t s) {
+  if (!batch || !nlimbs) return;
+  k_lift_small_batch<<<grid1(n, nlimbs, batch), kTpb, 0, s>>>(src, out, n, nlimbs, pm, primes);
+}
+
+void launch_bsgs_dot(const uint64_t* const* babies, const uint64_t* const* diags, uint64_t* out, uint32_t b,
+                     uint32_t G, uint32_t nq, uint32_t n, const Modulus* mods, cudaStream_t s) {
+  k_bsgs_dot<<<dim3((n + 127) / 128, nq), 128, 0, s>>>(babies, diags, out, b, G, nq, n, mods);
 }
 
 }  // namespace fhe

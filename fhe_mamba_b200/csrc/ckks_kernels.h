@@ -105,4 +105,21 @@ void launch_decode_crt(const uint64_t* coef, uint32_t nlimbs, uint32_t slots, ui
                        uint64_t q0, uint64_t q1, uint64_t q0inv_mod_q1, uint64_t q0inv_shoup,
                        Modulus m1, double2* v, cudaStream_t s);
 
+// ---- batched encode ----
+// Batch versions over B vectors: v = [B][slots] double2, coef = [B][N] int64,
+// out = [B][nlimbs][N] u64.
+void launch_encode_round_batch(const double2* v, int64_t* coef, uint32_t slots, uint32_t n, double scale,
+                               uint32_t batch, unsigned* status, cudaStream_t s);
+void launch_lift_small_batch(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
+                             const uint64_t* primes, uint32_t batch, cudaStream_t s);
+
+// ---- BSGS inner products ----
+// For every giant g < G and component c < 2:
+//   out[g][c][l] = sum_{j < b} baby_j[c][l] * diag_{g*b+j}[l]   (mod q_l),
+// babies[j] = [2][nq][N] (component stride nq*N), diags[g*b+j] = [nq_d >= nq][N]
+// or null for an all-zero diagonal.  Products accumulate in 128 bits and are
+// reduced once per output word.  b <= 32.
+void launch_bsgs_dot(const uint64_t* const* babies, const uint64_t* const* diags, uint64_t* out, uint32_t b,
+                     uint32_t G, uint32_t nq, uint32_t n, const Modulus* mods, cudaStream_t s);
+
 }  // namespace fhe

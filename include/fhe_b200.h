@@ -207,6 +207,22 @@ int fhe_conjugate(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
  * one ModUp shared by n rotations; outs receives n new handles. */
 int fhe_rotate_hoisted(fhe_ctx* ctx, const fhe_ct* a, const int32_t* steps, uint32_t n, fhe_ct** outs);
 
+/* Batched MakeCKKSPackedPlaintext: encodes `batch` vectors of `count` values
+ * (re[b*count + i], im likewise or NULL) on the device in one pass; outs
+ * receives `batch` handles.  The device-side replacement of the reference's
+ * per-diagonal host encoding (src/fideslib_plaintext_encoder.cpp:264-410). */
+int fhe_encode_batch(fhe_ctx* ctx, const double* re, const double* im, uint32_t batch, uint32_t count,
+                     uint32_t n_limbs, double scale, fhe_pt** outs);
+
+/* BSGS plaintext-ciphertext matrix-vector product (PackedEvaluator::linear,
+ * packed_fideslib.cpp:447-532; LinearTransformInPlace of the reference's
+ * FIDESlib patch): out = sum_g rot( sum_j diags[g*baby+j] (.) rot(a, j), g*baby ).
+ * Baby rotations share one ModUp; one fused kernel forms every giant's inner
+ * sum; diags[i] may be NULL for an all-zero diagonal.  Needs rotation keys
+ * for steps 1..baby-1 and g*baby. */
+int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* diags, uint32_t baby,
+                         uint32_t giant, fhe_ct** out);
+
 /* Rescale that allocates nothing.  This entry point has no counterpart in the
  * reference; it exists for callers that cannot let the library allocate
  * device memory when they rescale — code working inside a memory budget
