@@ -150,6 +150,70 @@ def cpu_baseline(threads, sample_limbs=None):
     return 1.0 / (dt * scale), dt, f"fwd+inv of {POLYS} polys x {limbs} limbs x 2^16 (scaled x{scale:g})"
 
 
+def measure_ckks(local, reps=10):
+    """Key switching and the BSGS matvec at BASELINE config-3 shape
+    (N=2^16, 2^15 slots, 20 limbs, dnum 3), timed with CUDA events on the
+    context stream.  Returns the two report objects."""
+    import torch
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    from fhe_mamba_b200.ckks import bsgs_diagonals
+    cc = CryptoContext(CCParams(ring_dim=1 << 16, multiplicative_depth=19, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3, device=local))
+    cc.KeyGen(7)
+    stream = torch.cuda.ExternalStream(cc.stream_ptr(), device=torch.device("cuda", local))
+    n, L, K = cc.n, cc.n_q, cc.n_p
+    D = (L + cc.alpha - 1) // cc.alpha
+    rng = np.random.default_rng(3)
+    d3 = np.empty((3, L, n), dtype=np.uint64)
+    for l, q in enumerate(cc.q):
+        d3[:, l, :] = rng.integers(0, q, size=(3, n), dtype=np.uint64)
+    ct3 = cc.upload(d3, noise_deg=2)
+    for _ in range(3):
+        cc.Relinearize(ct3)
+    cc.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    outs = [cc.Relinearize(ct3) for _ in range(reps)]
+    e1.record(stream)
+    e1.synchronize()
+    ks_ms = e0.elapsed_time(e1) / reps
+    del outs
+    ks_bytes = (L + 2 * L + 2 * L) * n * 8 + D * 2 * (L + K) * n * 8
+    peak, kind = peaks()
+    ks = {"workload": "relinearisation (HYBRID key switch), N=2^16, 20 Q limbs, 7 P limbs, dnum 3",
+          "ms": ks_ms, "alg_bytes": ks_bytes, "achieved_gbs": ks_bytes / (ks_ms / 1e3) / 1e9,
+          "frac": ks_bytes / (ks_ms / 1e3) / 1e9 / peak, "peak_gbs": peak, "peak_source": kind}
+
+    m, k, baby, giant = 768, 1536, 32, 48
+    W = rng.normal(0, 0.02, size=(m, k))
+    x = rng.uniform(-1, 1, k)
+    cc.EvalRotateKeyGen(list(range(1, baby)) + [g * baby for g in range(1, giant)])
+    v = np.zeros(cc.slots)
+    v[:k] = x
+    v[k:2 * k] = x
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(v))
+    pts = cc.MakeCKKSPackedPlaintexts(np.array([d for d in bsgs_diagonals(W, baby, giant, cc.slots)]))
+    out = cc.EvalLinearTransform(ct, pts, baby, giant)
+    cc.synchronize()
+    e0.record(stream)
+    for _ in range(3):
+        out = cc.EvalLinearTransform(ct, pts, baby, giant)
+    e1.record(stream)
+    e1.synchronize()
+    mv_ms = e0.elapsed_time(e1) / 3
+    cc.RescaleInPlace(out)
+    y = cc.Decrypt(out).GetRealPackedValue()
+    err = float(np.max(np.abs(y[:m] - W @ x)))
+    diag_bytes = k * L * n * 8
+    mv = {"workload": "BASELINE configs[2]: 768x1536 BSGS matvec, N=2^16, 2^15 slots, 20 limbs, dnum 3, "
+                      "baby 32 / giant 48, diagonals pre-encoded in HBM",
+          "ms": mv_ms, "max_abs_err_vs_fp64": err, "rotations": (baby - 1) + (giant - 1),
+          "diagonal_bytes": diag_bytes, "diagonal_stream_gbs": diag_bytes / (mv_ms / 1e3) / 1e9}
+    del pts, ct, out, ct3
+    cc.close()
+    return ks, mv
+
+
 def host_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -196,6 +260,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ckks", action="store_true", help="skip the key-switch and matvec side measurements")
+    ap.add_argument("--ckks-only", action="store_true",
+                    help="print only the key-switch and matvec measurements (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("warmup must be >= 3")
@@ -212,6 +279,10 @@ def main():
     import torch.distributed as dist
 
     torch.cuda.set_device(local)
+    if args.ckks_only:
+        ks, mv = measure_ckks(local)
+        print(json.dumps({"keyswitch": ks, "bsgs_matvec": mv}), flush=True)
+        return
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
@@ -318,6 +389,10 @@ def main():
             "gpu_launches": 4 * args.steps,
             "clocks": clocks,
         }
+        if not args.no_ckks:
+            ks, mv = measure_ckks(local)
+            line["keyswitch"] = ks
+            line["bsgs_matvec"] = mv
         if not args.no_cpu_baseline:
             v, dt, sample = cpu_baseline(host_threads())
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",

@@ -54,7 +54,16 @@ void init_device(fhe::Context& c, int device) {
   fhe::require(device >= 0 && device < count, "device ordinal out of range");
   c.device = device;
   FHE_CUDA(cudaSetDevice(device));
-  FHE_CUDA(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+  c.sh = std::make_shared<fhe::StreamHolder>();
+  c.sh->device = device;
+  FHE_CUDA(cudaStreamCreateWithFlags(&c.sh->s, cudaStreamNonBlocking));
+  c.stream = c.sh->s;
+  // Keep freed ciphertext memory in the device pool instead of returning it
+  // to the driver at every synchronisation.
+  cudaMemPool_t pool;
+  FHE_CUDA(cudaDeviceGetDefaultMemPool(&pool, device));
+  uint64_t threshold = UINT64_MAX;
+  FHE_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold));
 }
 
 // Runs a raw transform on host or device memory.
@@ -416,7 +425,7 @@ int fhe_pt_upload(fhe_ctx* ctx, const uint64_t* host, uint32_t n_limbs, double s
     fhe::Ckks& k = ckks(ctx);
     fhe::require(host != nullptr && n_limbs >= 1 && n_limbs <= ctx->c.L, "bad plaintext shape");
     auto p = std::make_unique<fhe::Pt>();
-    p->buf = fhe::DevMem((size_t)n_limbs * ctx->c.n * 8);
+    p->buf = fhe::DevMem((size_t)n_limbs * ctx->c.n * 8, ctx->c.sh);
     p->nq = n_limbs;
     p->scale = scale;
     FHE_CUDA(cudaMemcpyAsync(p->data(), host, (size_t)n_limbs * ctx->c.n * 8, cudaMemcpyHostToDevice, k.ctx.stream));

@@ -41,6 +41,30 @@ Ckks::Ckks(Context& c) : ctx(c) {
   status_ = DevMem(sizeof(unsigned));
 }
 
+Ckks::~Ckks() {
+  if (ptr_event_) cudaEventDestroy(ptr_event_);
+  if (pinned_) cudaFreeHost(pinned_);
+}
+
+// Copies a small host table (pointers) to a device scratch buffer without
+// blocking the host: the data goes through pinned memory, reused once the
+// previous copy has finished.
+const void* Ckks::stage_pointers(const void* host, size_t bytes, size_t ws_idx) {
+  if (!ptr_event_) FHE_CUDA(cudaEventCreateWithFlags(&ptr_event_, cudaEventDisableTiming));
+  else FHE_CUDA(cudaEventSynchronize(ptr_event_));
+  if (pinned_bytes_ < bytes) {
+    if (pinned_) FHE_CUDA(cudaFreeHost(pinned_));
+    pinned_ = nullptr;
+    FHE_CUDA(cudaMallocHost(&pinned_, bytes));
+    pinned_bytes_ = bytes;
+  }
+  std::memcpy(pinned_, host, bytes);
+  uint64_t* d = ws(ws_idx, (bytes + 7) / 8);
+  FHE_CUDA(cudaMemcpyAsync(d, pinned_, bytes, cudaMemcpyHostToDevice, ctx.stream));
+  FHE_CUDA(cudaEventRecord(ptr_event_, ctx.stream));
+  return d;
+}
+
 // Context-owned scratch buffers, reused across calls (one stream orders all use).
 uint64_t* Ckks::ws(size_t idx, size_t words) {
   if (ws_.size() <= idx) ws_.resize(idx + 1);
@@ -340,7 +364,7 @@ std::unique_ptr<Pt> Ckks::encode(const double* re, const double* im, uint32_t co
   FHE_CUDA(cudaMemsetAsync(status_.p, 0, sizeof(unsigned), ctx.stream));
   launch_encode_round(dv, coef, slots, n, scale, status_.as<unsigned>(), ctx.stream);
   auto p = std::make_unique<Pt>();
-  p->buf = DevMem((size_t)nq * n * 8);
+  p->buf = DevMem((size_t)nq * n * 8, ctx.sh);
   p->nq = nq;
   p->scale = scale;
   launch_lift_small(coef, p->data(), n, nq, PrimeMap{nq, ctx.L}, ctx.d_primes.as<uint64_t>(), ctx.stream);
@@ -380,7 +404,7 @@ std::vector<std::unique_ptr<Pt>> Ckks::encode_batch(const double* re, const doub
     ntt_dense(res, nb, nq, nq, 0, false);
     for (uint32_t b = 0; b < nb; ++b) {
       auto p = std::make_unique<Pt>();
-      p->buf = DevMem((size_t)nq * n * 8);
+      p->buf = DevMem((size_t)nq * n * 8, ctx.sh);
       p->nq = nq;
       p->scale = scale;
       FHE_CUDA(cudaMemcpyAsync(p->data(), res + (size_t)b * nq * n, (size_t)nq * n * 8, cudaMemcpyDeviceToDevice,
@@ -418,7 +442,7 @@ void Ckks::decode(const Pt& p, double* re, double* im, uint32_t count) {
 
 std::unique_ptr<Ct> Ckks::alloc(uint32_t nq, uint32_t ncomp) {
   auto c = std::make_unique<Ct>();
-  c->buf = DevMem((size_t)ncomp * nq * ctx.n * 8);
+  c->buf = DevMem((size_t)ncomp * nq * ctx.n * 8, ctx.sh);
   c->cap = nq;
   c->nq = nq;
   c->ncomp = ncomp;
@@ -476,7 +500,7 @@ std::unique_ptr<Pt> Ckks::decrypt(const Ct& c) {
   const Modulus* mods = ctx.d_mod.as<Modulus>();
   const PrimeMap q{nq, ctx.L};
   auto p = std::make_unique<Pt>();
-  p->buf = DevMem((size_t)nq * n * 8);
+  p->buf = DevMem((size_t)nq * n * 8, ctx.sh);
   p->nq = nq;
   p->scale = c.scale;
   p->noise_deg = c.noise_deg;
@@ -606,15 +630,14 @@ std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a, const std::vector<const 
   for (uint32_t j = 1; j < b; ++j) gs.push_back(galois_for_step(j));
   auto rot = rotate_hoisted(a, gs);
   auto base = clone(a);  // cap == nq, component stride nq*N like the rotations
-  std::vector<const uint64_t*> bp{base->data()};
-  for (auto& r : rot) bp.push_back(r->data());
-  std::vector<const uint64_t*> dp(diags.size());
-  for (size_t i = 0; i < diags.size(); ++i) dp[i] = diags[i] ? diags[i]->data() : nullptr;
-  DevMem d_bp = upload(bp), d_dp = upload(dp);
+  std::vector<const uint64_t*> tab{base->data()};
+  for (auto& r : rot) tab.push_back(r->data());
+  for (size_t i = 0; i < diags.size(); ++i) tab.push_back(diags[i] ? diags[i]->data() : nullptr);
+  const uint64_t* const* d_tab =
+      static_cast<const uint64_t* const*>(stage_pointers(tab.data(), tab.size() * sizeof(void*), 23));
   const size_t cs = (size_t)nq * n;
   uint64_t* inner = ws(21, (size_t)G * 2 * cs);
-  launch_bsgs_dot(d_bp.as<const uint64_t*>(), d_dp.as<const uint64_t*>(), inner, b, G, nq, n,
-                  ctx.d_mod.as<Modulus>(), ctx.stream);
+  launch_bsgs_dot(d_tab, d_tab + b, inner, b, G, nq, n, ctx.d_mod.as<Modulus>(), ctx.stream);
   auto out = alloc(nq, 2);
   out->scale = a.scale * pscale;
   out->noise_deg = a.noise_deg + 1;
@@ -630,7 +653,6 @@ std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a, const std::vector<const 
     launch_ew(Ew::Add, out->data(), cs, r, cs, out->data(), cs, 2, nq, n, PrimeMap{nq, ctx.L},
               ctx.d_mod.as<Modulus>(), ctx.stream);
   }
-  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
   return out;
 }
 

@@ -128,6 +128,15 @@ class Ckks {
   std::map<uint64_t, DevMem> rot_;
   std::vector<DevMem> ws_;
   DevMem status_;
+  // Pinned staging for per-call pointer tables, reused once the previous
+  // copy (ptr_event_) has completed.
+  void* pinned_ = nullptr;
+  size_t pinned_bytes_ = 0;
+  cudaEvent_t ptr_event_ = nullptr;
+  const void* stage_pointers(const void* host, size_t bytes, size_t ws_idx);
+
+ public:
+  ~Ckks();
 };
 
 }  // namespace fhe

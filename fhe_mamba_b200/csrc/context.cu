@@ -19,6 +19,14 @@ void require(bool ok, const std::string& msg, int code) {
   if (!ok) throw Error(code, msg);
 }
 
+StreamHolder::~StreamHolder() {
+  if (s) {
+    cudaSetDevice(device);
+    cudaStreamSynchronize(s);
+    cudaStreamDestroy(s);
+  }
+}
+
 DevMem::DevMem(size_t b) : bytes(b) {
   if (b == 0) return;
   cudaError_t e = cudaMalloc(&p, b);
@@ -29,15 +37,34 @@ DevMem::DevMem(size_t b) : bytes(b) {
   }
 }
 
-DevMem::~DevMem() {
-  if (p) cudaFree(p);
+DevMem::DevMem(size_t b, const std::shared_ptr<StreamHolder>& stream) : bytes(b), sh(stream) {
+  if (b == 0) return;
+  cudaError_t e = cudaMallocAsync(&p, b, sh->s);
+  if (e != cudaSuccess) {
+    p = nullptr;
+    bytes = 0;
+    throw Error(-3, std::string("cudaMallocAsync(") + std::to_string(b) + "): " + cudaGetErrorString(e));
+  }
 }
+
+void DevMem::release() {
+  if (p) {
+    if (sh) cudaFreeAsync(p, sh->s);
+    else cudaFree(p);
+  }
+  p = nullptr;
+  bytes = 0;
+  sh.reset();
+}
+
+DevMem::~DevMem() { release(); }
 
 DevMem& DevMem::operator=(DevMem&& o) noexcept {
   if (this != &o) {
-    if (p) cudaFree(p);
+    release();
     p = o.p;
     bytes = o.bytes;
+    sh = std::move(o.sh);
     o.p = nullptr;
     o.bytes = 0;
   }
@@ -200,7 +227,6 @@ Context::~Context() {
   if (stream) {
     cudaSetDevice(device);
     cudaStreamSynchronize(stream);
-    cudaStreamDestroy(stream);
   }
 }
 

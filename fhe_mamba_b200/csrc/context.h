@@ -1,6 +1,7 @@
 // Host-side context of the fhe_b200 backend: moduli, device tables, stream.
 #pragma once
 #include <cstdint>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -22,17 +23,30 @@ void cuda_check(cudaError_t e, const char* what);
 #define FHE_CUDA(call) ::fhe::cuda_check((call), #call)
 void require(bool ok, const std::string& msg, int code = -1);
 
-// Owning device allocation.
+// CUDA stream shared by a context and every buffer allocated on it; the
+// stream is destroyed when the last owner goes away.
+struct StreamHolder {
+  int device = 0;
+  cudaStream_t s = nullptr;
+  ~StreamHolder();
+};
+
+// Owning device allocation.  With a StreamHolder the memory comes from the
+// device's stream-ordered pool (cudaMallocAsync / cudaFreeAsync on that
+// stream), so allocating and freeing ciphertexts never synchronises.
 struct DevMem {
   void* p = nullptr;
   size_t bytes = 0;
+  std::shared_ptr<StreamHolder> sh;
   DevMem() = default;
   explicit DevMem(size_t b);
+  DevMem(size_t b, const std::shared_ptr<StreamHolder>& stream);
   ~DevMem();
   DevMem(const DevMem&) = delete;
   DevMem& operator=(const DevMem&) = delete;
-  DevMem(DevMem&& o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr; o.bytes = 0; }
+  DevMem(DevMem&& o) noexcept : p(o.p), bytes(o.bytes), sh(std::move(o.sh)) { o.p = nullptr; o.bytes = 0; }
   DevMem& operator=(DevMem&& o) noexcept;
+  void release();
   template <class T>
   T* as() const { return static_cast<T*>(p); }
 };
@@ -57,6 +71,7 @@ void ckks_moduli(uint32_t log_n, uint32_t num_q, uint32_t scale_bits, uint32_t f
 struct Context {
   int device = 0;
   cudaStream_t stream = nullptr;
+  std::shared_ptr<StreamHolder> sh;  // owns `stream`
   uint32_t log_n = 0;
   uint32_t n = 0;
   bool ckks = false;
