@@ -263,7 +263,7 @@ void Ckks::switch_keygen(uint64_t key_id, const uint64_t* s_new, const uint64_t*
     uint64_t* a = b + (size_t)lk * n;
     launch_sample_uniform(seed_, stream_key(0x10, key_id, j), a, n, lk, full, mods, ctx.stream);
     launch_sample_small(1, seed_, stream_key(0x11, key_id, j), e, n, ctx.stream);
-    launch_lift_small(e, tmp, n, lk, full, primes, ctx.stream);
+    launch_lift_small(e, tmp, n, lk, full, mods, ctx.stream);
     ntt_dense(tmp, 1, lk, lk, 0, false);
     launch_ew(Ew::Mul, a, 0, s_new, 0, b, 0, 1, lk, n, full, mods, ctx.stream);
     launch_ew(Ew::SubFrom, b, 0, tmp, 0, b, 0, 1, lk, n, full, mods, ctx.stream);
@@ -282,7 +282,7 @@ void Ckks::keygen(uint64_t seed) {
   int64_t* small = reinterpret_cast<int64_t*>(ws(10, n));
   s_ntt_ = DevMem((size_t)lk * n * 8);
   launch_sample_small(0, seed, kStreamSecret, small, n, ctx.stream);
-  launch_lift_small(small, s_ntt_.as<uint64_t>(), n, lk, PrimeMap{lk, L}, primes, ctx.stream);
+  launch_lift_small(small, s_ntt_.as<uint64_t>(), n, lk, PrimeMap{lk, L}, mods, ctx.stream);
   ntt_dense(s_ntt_.as<uint64_t>(), 1, lk, lk, 0, false);
   pk_ = DevMem((size_t)2 * L * n * 8);
   uint64_t* b = pk_.as<uint64_t>();
@@ -291,7 +291,7 @@ void Ckks::keygen(uint64_t seed) {
   const PrimeMap q{L, L};
   launch_sample_uniform(seed, kStreamPkA, a, n, L, q, mods, ctx.stream);
   launch_sample_small(1, seed, kStreamPkE, small, n, ctx.stream);
-  launch_lift_small(small, tmp, n, L, q, primes, ctx.stream);
+  launch_lift_small(small, tmp, n, L, q, mods, ctx.stream);
   ntt_dense(tmp, 1, L, L, 0, false);
   launch_ew(Ew::Mul, a, 0, s_ntt_.as<uint64_t>(), 0, b, 0, 1, L, n, q, mods, ctx.stream);
   launch_ew(Ew::SubFrom, b, 0, tmp, 0, b, 0, 1, L, n, q, mods, ctx.stream);
@@ -367,7 +367,7 @@ std::unique_ptr<Pt> Ckks::encode(const double* re, const double* im, uint32_t co
   p->buf = DevMem((size_t)nq * n * 8, ctx.sh);
   p->nq = nq;
   p->scale = scale;
-  launch_lift_small(coef, p->data(), n, nq, PrimeMap{nq, ctx.L}, ctx.d_primes.as<uint64_t>(), ctx.stream);
+  launch_lift_small(coef, p->data(), n, nq, PrimeMap{nq, ctx.L}, ctx.d_mod.as<Modulus>(), ctx.stream);
   ntt_dense(p->data(), 1, nq, nq, 0, false);
   unsigned st = 0;
   FHE_CUDA(cudaMemcpyAsync(&st, status_.p, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx.stream));
@@ -400,7 +400,7 @@ std::vector<std::unique_ptr<Pt>> Ckks::encode_batch(const double* re, const doub
     FHE_CUDA(cudaMemsetAsync(status_.p, 0, sizeof(unsigned), ctx.stream));
     launch_encode_round_batch(dv, coef, slots, n, scale, nb, status_.as<unsigned>(), ctx.stream);
     uint64_t* res = ws(20, (size_t)nb * nq * n);
-    launch_lift_small_batch(coef, res, n, nq, PrimeMap{nq, ctx.L}, ctx.d_primes.as<uint64_t>(), nb, ctx.stream);
+    launch_lift_small_batch(coef, res, n, nq, PrimeMap{nq, ctx.L}, ctx.d_mod.as<Modulus>(), nb, ctx.stream);
     ntt_dense(res, nb, nq, nq, 0, false);
     for (uint32_t b = 0; b < nb; ++b) {
       auto p = std::make_unique<Pt>();
@@ -470,11 +470,11 @@ std::unique_ptr<Ct> Ckks::encrypt(const Pt& p) {
   uint64_t* e = ws(17, (size_t)2 * nq * n);
   const PrimeMap q{nq, L};
   launch_sample_small(0, seed_, stream_enc(4, nonce), small, n, ctx.stream);
-  launch_lift_small(small, v, n, nq, q, primes, ctx.stream);
+  launch_lift_small(small, v, n, nq, q, mods, ctx.stream);
   launch_sample_small(1, seed_, stream_enc(5, nonce), small, n, ctx.stream);
-  launch_lift_small(small, e, n, nq, q, primes, ctx.stream);
+  launch_lift_small(small, e, n, nq, q, mods, ctx.stream);
   launch_sample_small(1, seed_, stream_enc(6, nonce), small, n, ctx.stream);
-  launch_lift_small(small, e + (size_t)nq * n, n, nq, q, primes, ctx.stream);
+  launch_lift_small(small, e + (size_t)nq * n, n, nq, q, mods, ctx.stream);
   ntt_dense(v, 1, nq, nq, 0, false);
   ntt_dense(e, 2, nq, nq, 0, false);
   auto c = alloc(nq, 2);
@@ -539,7 +539,7 @@ void Ckks::moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, co
   LevelTables& T = level(nq);
   ntt_dense(acc + (size_t)nq * n, 2, K, w, ctx.L, true);
   uint64_t* conv = ws(3, (size_t)2 * ctx.L * n);
-  launch_convert(acc + (size_t)nq * n, (size_t)w * n, conv, (size_t)nq * n, 2, T.moddown.as<ConvTable>(), n,
+  launch_convert(acc + (size_t)nq * n, (size_t)w * n, conv, (size_t)nq * n, 2, T.moddown.as<ConvTable>(), nq, n,
                  ctx.d_primes.as<uint64_t>(), ctx.stream);
   ntt_dense(conv, 2, nq, nq, 0, false);
   launch_moddown_combine(acc, (size_t)w * n, conv, (size_t)nq * n, pinv_.as<Shoup>(), add_c0, out, so, 2, nq, n,

@@ -66,21 +66,18 @@ __global__ void k_sample_small(int kind, uint64_t seed, uint64_t stream, int64_t
   }
 }
 
-__global__ void k_lift_small(const int64_t* src, uint64_t* out, uint32_t n, PrimeMap pm,
-                             const uint64_t* primes) {
+// Signed 64-bit value -> residue mod q (Barrett; |v| < 2^63).
+__device__ __forceinline__ uint64_t lift_signed(int64_t v, const Modulus& m) {
+  if (v >= 0) return barrett_reduce(0, (uint64_t)v, m);
+  const uint64_t r = barrett_reduce(0, (uint64_t)(-(v + 1)) + 1, m);
+  return r ? m.q - r : 0;
+}
+
+__global__ void k_lift_small(const int64_t* src, uint64_t* out, uint32_t n, PrimeMap pm, const Modulus* mods) {
   const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
   if (k >= n) return;
   const uint32_t l = blockIdx.y;
-  const uint64_t q = primes[pm(l)];
-  const int64_t v = src[k];
-  uint64_t r;
-  if (v >= 0) {
-    r = (uint64_t)v % q;
-  } else {
-    const uint64_t m = ((uint64_t)(-(v + 1)) + 1) % q;
-    r = m ? q - m : 0;
-  }
-  out[(size_t)l * n + k] = r;
+  out[(size_t)l * n + k] = lift_signed(src[k], mods[pm(l)]);
 }
 
 // Uniform residue from two keystream words: (hi * 2^64 + lo) mod q.
@@ -173,14 +170,25 @@ __global__ void k_automorphism(const uint64_t* in, size_t si, uint64_t* out, siz
 // ---------------------------------------------------------------------------
 constexpr int kMaxSrc = 24;  // largest digit / special basis handled by the conversions
 
+constexpr int kTgtChunk = 8;  // target limbs per block in the basis conversions
+
+// Block (x = coefficient tile, y = digit, z = chunk of kTgtChunk target limbs).
 __global__ void k_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t w, uint32_t n,
                         const ModUpDigit* digits, const uint64_t* primes) {
-  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
-  if (k >= n) return;
+  __shared__ Shoup sh_hat[kTgtChunk * kMaxSrc];
+  __shared__ uint64_t sh_t[kTgtChunk];
   const uint32_t j = blockIdx.y;
   const ModUpDigit dg = digits[j];
-  uint64_t* e = ext + (size_t)j * w * n;
   const uint32_t ns = dg.hi - dg.lo;
+  const uint32_t t0 = blockIdx.z * kTgtChunk;
+  if (t0 >= dg.conv.nt) return;  // uniform across the block
+  const uint32_t nt = min((uint32_t)kTgtChunk, dg.conv.nt - t0);
+  for (uint32_t i = threadIdx.x; i < nt * ns; i += blockDim.x) sh_hat[i] = dg.conv.hat[(size_t)t0 * ns + i];
+  if (threadIdx.x < nt) sh_t[threadIdx.x] = primes[dg.conv.dst_prime[t0 + threadIdx.x]];
+  __syncthreads();
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  uint64_t* e = ext + (size_t)j * w * n;
   uint64_t y[kMaxSrc];
 #pragma unroll
   for (int i = 0; i < kMaxSrc; ++i) {
@@ -188,13 +196,14 @@ __global__ void k_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ex
       const uint32_t l = dg.lo + i;
       const Shoup h = dg.conv.hatinv[i];
       y[i] = shoup_mul(coef[(size_t)l * n + k], h.w, h.wp, primes[dg.conv.src_prime[i]]);
-      e[(size_t)l * n + k] = dntt[(size_t)l * n + k];
+      if (blockIdx.z == 0) e[(size_t)l * n + k] = dntt[(size_t)l * n + k];
     }
   }
-  for (uint32_t tt = 0; tt < dg.conv.nt; ++tt) {
+  for (uint32_t u = 0; u < nt; ++u) {
+    const uint32_t tt = t0 + u;
     const uint32_t l = tt < dg.lo ? tt : tt + ns;
-    const uint64_t t = primes[dg.conv.dst_prime[tt]], t2 = 2 * t;
-    const Shoup* hrow = dg.conv.hat + (size_t)tt * ns;
+    const uint64_t t = sh_t[u], t2 = 2 * t;
+    const Shoup* hrow = sh_hat + u * ns;
     uint64_t acc = 0;
 #pragma unroll
     for (int i = 0; i < kMaxSrc; ++i) {
@@ -226,12 +235,21 @@ __global__ void k_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const u
   acc[((size_t)w + l) * n + k] = s1;
 }
 
+// Block (x = coefficient tile, y = component, z = chunk of kTgtChunk targets).
 __global__ void k_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp,
                           const ConvTable* tab, uint32_t n, const uint64_t* primes) {
+  __shared__ Shoup sh_hat[kTgtChunk * kMaxSrc];
+  __shared__ uint64_t sh_t[kTgtChunk];
+  const ConvTable t = *tab;
+  const uint32_t t0 = blockIdx.z * kTgtChunk;
+  if (t0 >= t.nt) return;
+  const uint32_t nt = min((uint32_t)kTgtChunk, t.nt - t0);
+  for (uint32_t i = threadIdx.x; i < nt * t.ns; i += blockDim.x) sh_hat[i] = t.hat[(size_t)t0 * t.ns + i];
+  if (threadIdx.x < nt) sh_t[threadIdx.x] = primes[t.dst_prime[t0 + threadIdx.x]];
+  __syncthreads();
   const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
   if (k >= n) return;
   const uint32_t c = blockIdx.y;
-  const ConvTable t = *tab;
   const uint64_t* s = src + c * s_comp;
   uint64_t* d = dst + c * d_comp;
   uint64_t y[kMaxSrc];
@@ -242,9 +260,9 @@ __global__ void k_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, siz
       y[i] = shoup_mul(s[(size_t)i * n + k], h.w, h.wp, primes[t.src_prime[i]]);
     }
   }
-  for (uint32_t tt = 0; tt < t.nt; ++tt) {
-    const uint64_t q = primes[t.dst_prime[tt]], q2 = 2 * q;
-    const Shoup* hrow = t.hat + (size_t)tt * t.ns;
+  for (uint32_t u = 0; u < nt; ++u) {
+    const uint64_t q = sh_t[u], q2 = 2 * q;
+    const Shoup* hrow = sh_hat + u * t.ns;
     uint64_t acc = 0;
 #pragma unroll
     for (int i = 0; i < kMaxSrc; ++i) {
@@ -253,7 +271,7 @@ __global__ void k_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, siz
         acc = csub(acc + shoup_lazy(y[i], h.w, h.wp, q), q2);
       }
     }
-    d[(size_t)tt * n + k] = csub(acc, q);
+    d[(size_t)(t0 + u) * n + k] = csub(acc, q);
   }
 }
 
@@ -399,20 +417,11 @@ __global__ void k_encode_round_batch(const double2* v, int64_t* coef, uint32_t s
 }
 
 __global__ void k_lift_small_batch(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
-                                   const uint64_t* primes) {
+                                   const Modulus* mods) {
   const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
   if (k >= n) return;
   const uint32_t l = blockIdx.y, b = blockIdx.z;
-  const uint64_t q = primes[pm(l)];
-  const int64_t v = src[(size_t)b * n + k];
-  uint64_t r;
-  if (v >= 0) {
-    r = (uint64_t)v % q;
-  } else {
-    const uint64_t m = ((uint64_t)(-(v + 1)) + 1) % q;
-    r = m ? q - m : 0;
-  }
-  out[((size_t)b * nlimbs + l) * n + k] = r;
+  out[((size_t)b * nlimbs + l) * n + k] = lift_signed(src[(size_t)b * n + k], mods[pm(l)]);
 }
 
 // 128-bit accumulator reduced mod q: (hi 2^64 + lo) mod q with hi < 2^62.
@@ -423,42 +432,37 @@ __device__ __forceinline__ uint64_t reduce128(uint64_t hi, uint64_t lo, const Mo
 }
 
 constexpr int kMaxBaby = 32;
+constexpr int kGiantChunk = 8;  // giants per CTA: neighbouring CTAs share the babies' tile in L1/L2
 
+// Block (x = giant chunk, y = coefficient tile, z = limb).  Each thread owns
+// one coefficient and accumulates every giant of its chunk in 128 bits; the
+// babies are re-read per giant from L1/L2, the diagonals stream from HBM once.
 __global__ void __launch_bounds__(128) k_bsgs_dot(const uint64_t* const* babies, const uint64_t* const* diags,
                                                   uint64_t* out, uint32_t b, uint32_t G, uint32_t nq, uint32_t n,
                                                   const Modulus* mods) {
-  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t k = blockIdx.y * blockDim.x + threadIdx.x;
   if (k >= n) return;
-  const uint32_t l = blockIdx.y;
+  const uint32_t l = blockIdx.z;
   const Modulus m = mods[l];
   const uint64_t r64 = barrett_reduce(1, 0, m);
   const size_t off = (size_t)l * n + k, cs = (size_t)nq * n;
-  uint64_t x0[kMaxBaby], x1[kMaxBaby];
-#pragma unroll
-  for (int j = 0; j < kMaxBaby; ++j) {
-    if (j < (int)b) {
-      const uint64_t* bj = babies[j];
-      x0[j] = bj[off];
-      x1[j] = bj[cs + off];
-    }
-  }
-  for (uint32_t g = 0; g < G; ++g) {
+  const uint32_t g0 = blockIdx.x * kGiantChunk, g1 = min(G, g0 + kGiantChunk);
+  for (uint32_t g = g0; g < g1; ++g) {
     uint64_t h0 = 0, l0 = 0, h1 = 0, l1 = 0;
-#pragma unroll
-    for (int j = 0; j < kMaxBaby; ++j) {
-      if (j < (int)b) {
-        const uint64_t* dp = diags[g * b + j];
-        if (dp) {
-          const uint64_t d = __ldcs(dp + off);  // streamed once: evict first
-          uint64_t lo = x0[j] * d, hi = __umul64hi(x0[j], d);
-          l0 += lo;
-          h0 += hi + (l0 < lo);
-          lo = x1[j] * d;
-          hi = __umul64hi(x1[j], d);
-          l1 += lo;
-          h1 += hi + (l1 < lo);
-        }
-      }
+#pragma unroll 4
+    for (uint32_t j = 0; j < b; ++j) {
+      const uint64_t* dp = diags[g * b + j];
+      if (!dp) continue;
+      const uint64_t d = __ldcs(dp + off);  // streamed once: evict first
+      const uint64_t* bj = babies[j];
+      const uint64_t x0 = __ldg(bj + off), x1 = __ldg(bj + cs + off);
+      uint64_t lo = x0 * d, hi = __umul64hi(x0, d);
+      l0 += lo;
+      h0 += hi + (l0 < lo);
+      lo = x1 * d;
+      hi = __umul64hi(x1, d);
+      l1 += lo;
+      h1 += hi + (l1 < lo);
     }
     uint64_t* o = out + (size_t)g * 2 * cs;
     o[off] = reduce128(h0, l0, m, r64);
@@ -481,9 +485,9 @@ void launch_sample_small(int kind, uint64_t seed, uint64_t stream, int64_t* out,
 }
 
 void launch_lift_small(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
-                       const uint64_t* primes, cudaStream_t s) {
+                       const Modulus* mods, cudaStream_t s) {
   if (!nlimbs) return;
-  k_lift_small<<<grid1(n, nlimbs), kTpb, 0, s>>>(src, out, n, pm, primes);
+  k_lift_small<<<grid1(n, nlimbs), kTpb, 0, s>>>(src, out, n, pm, mods);
 }
 
 void launch_sample_uniform(uint64_t seed, uint64_t stream, uint64_t* out, uint32_t n, uint32_t nlimbs,
@@ -524,7 +528,9 @@ void launch_automorphism(const uint64_t* in, size_t si, uint64_t* out, size_t so
 
 void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t nq, uint32_t K, uint32_t n,
                   const ModUpDigit* digits_dev, uint32_t D, const uint64_t* primes, cudaStream_t s) {
-  k_modup<<<grid1(n, D), kTpb, 0, s>>>(coef, dntt, ext, nq + K, n, digits_dev, primes);
+  // every digit has at most nq + K - 1 targets
+  const uint32_t chunks = (nq + K + kTgtChunk - 1) / kTgtChunk;
+  k_modup<<<grid1(n, D, chunks), kTpb, 0, s>>>(coef, dntt, ext, nq + K, n, digits_dev, primes);
 }
 
 void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_t* evk, uint32_t key_limbs,
@@ -533,8 +539,9 @@ void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_
 }
 
 void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp, uint32_t ncomp,
-                    const ConvTable* t_dev, uint32_t n, const uint64_t* primes, cudaStream_t s) {
-  k_convert<<<grid1(n, ncomp), kTpb, 0, s>>>(src, s_comp, dst, d_comp, t_dev, n, primes);
+                    const ConvTable* t_dev, uint32_t nt, uint32_t n, const uint64_t* primes, cudaStream_t s) {
+  const uint32_t chunks = (nt + kTgtChunk - 1) / kTgtChunk;
+  k_convert<<<grid1(n, ncomp, chunks), kTpb, 0, s>>>(src, s_comp, dst, d_comp, t_dev, n, primes);
 }
 
 void launch_moddown_combine(const uint64_t* x, size_t sx, const uint64_t* conv, size_t sc, const Shoup* pinv,
@@ -579,14 +586,15 @@ void launch_encode_round_batch(const double2* v, int64_t* coef, uint32_t slots, 
 }
 
 void launch_lift_small_batch(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
-                             const uint64_t* primes, uint32_t batch, cudaStream_t s) {
+                             const Modulus* mods, uint32_t batch, cudaStream_t s) {
   if (!batch || !nlimbs) return;
-  k_lift_small_batch<<<grid1(n, nlimbs, batch), kTpb, 0, s>>>(src, out, n, nlimbs, pm, primes);
+  k_lift_small_batch<<<grid1(n, nlimbs, batch), kTpb, 0, s>>>(src, out, n, nlimbs, pm, mods);
 }
 
 void launch_bsgs_dot(const uint64_t* const* babies, const uint64_t* const* diags, uint64_t* out, uint32_t b,
                      uint32_t G, uint32_t nq, uint32_t n, const Modulus* mods, cudaStream_t s) {
-  k_bsgs_dot<<<dim3((n + 127) / 128, nq), 128, 0, s>>>(babies, diags, out, b, G, nq, n, mods);
+  k_bsgs_dot<<<dim3((G + kGiantChunk - 1) / kGiantChunk, (n + 127) / 128, nq), 128, 0, s>>>(babies, diags, out, b,
+                                                                                           G, nq, n, mods);
 }
 
 }  // namespace fhe

@@ -34,7 +34,7 @@ struct ConvTable {
 void launch_sample_small(int kind, uint64_t seed, uint64_t stream, int64_t* out, uint32_t n,
                          cudaStream_t s);  // kind 0: ternary, 1: CBD(21)
 void launch_lift_small(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
-                       const uint64_t* primes, cudaStream_t s);
+                       const Modulus* mods, cudaStream_t s);
 void launch_sample_uniform(uint64_t seed, uint64_t stream, uint64_t* out, uint32_t n, uint32_t nlimbs,
                            PrimeMap pm, const Modulus* mods, cudaStream_t s);
 
@@ -76,8 +76,9 @@ void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_
                       uint32_t key_limbs, PrimeMap pm, uint64_t* acc, uint32_t n, const Modulus* mods,
                       cudaStream_t s);
 // Basis conversion of ncomp polys: src limbs (coefficient form) -> dst (coefficient form).
+// nt must equal the table's target count.
 void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp, uint32_t ncomp,
-                    const ConvTable* t_dev, uint32_t n, const uint64_t* primes, cudaStream_t s);
+                    const ConvTable* t_dev, uint32_t nt, uint32_t n, const uint64_t* primes, cudaStream_t s);
 // out[c][i] = (x[c][i] - conv[c][i]) * pinv_i  (+ add[i] on component 0 when add != null).
 void launch_moddown_combine(const uint64_t* x, size_t sx, const uint64_t* conv, size_t sc,
                             const Shoup* pinv, const uint64_t* add, uint64_t* out, size_t so,
@@ -111,7 +112,7 @@ void launch_decode_crt(const uint64_t* coef, uint32_t nlimbs, uint32_t slots, ui
 void launch_encode_round_batch(const double2* v, int64_t* coef, uint32_t slots, uint32_t n, double scale,
                                uint32_t batch, unsigned* status, cudaStream_t s);
 void launch_lift_small_batch(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
-                             const uint64_t* primes, uint32_t batch, cudaStream_t s);
+                             const Modulus* mods, uint32_t batch, cudaStream_t s);
 
 // ---- BSGS inner products ----
 // For every giant g < G and component c < 2:

@@ -179,8 +179,9 @@ void ckks_moduli(uint32_t log_n, uint32_t num_q, uint32_t scale_bits, uint32_t f
                  uint32_t dnum, std::vector<uint64_t>& q, std::vector<uint64_t>& p) {
   require(num_q >= 2 && num_q <= 64, "number of Q primes must be in [2, 64]");
   require(dnum >= 1, "num_large_digits must be >= 1");
-  require(scale_bits >= 20 && scale_bits <= 60 && first_bits >= 20 && first_bits <= 60,
-          "modulus sizes must be in [20, 60] bits");
+  // Barrett reductions of raw 64-bit words need primes of at least 33 bits.
+  require(scale_bits >= 33 && scale_bits <= 60 && first_bits >= 33 && first_bits <= 60,
+          "modulus sizes must be in [33, 60] bits");
   require(first_bits != scale_bits, "first_mod_size must differ from scaling_mod_size");
   const uint64_t m = uint64_t(2) << log_n;
   q.assign(num_q, 0);
