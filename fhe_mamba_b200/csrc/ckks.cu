@@ -172,7 +172,7 @@ LevelTables& Ckks::level(uint32_t nq) {
     o.hil = std::min(o.lo + a, nq);
     o.ns = o.hil - o.lo;
     o.nt = T.w - o.ns;
-    require(o.ns <= 24, "digits of more than 24 limbs are not supported", -1);
+    require(o.ns <= 24 && K <= 24, "digits or special bases of more than 24 limbs are not supported", -1);
     o.sp = cur; cur += 4 * o.ns;
     o.dp = cur; cur += 4 * o.nt;
     cur = a16(cur);
@@ -525,7 +525,8 @@ void Ckks::modup(const uint64_t* d, uint32_t nq, uint64_t* ext) {
   uint64_t* coef = ws(1, (size_t)ctx.L * n);
   FHE_CUDA(cudaMemcpyAsync(coef, d, (size_t)nq * n * 8, cudaMemcpyDeviceToDevice, ctx.stream));
   ntt_dense(coef, 1, nq, nq, 0, true);
-  launch_modup(coef, d, ext, nq, ctx.K, n, T.digits.as<ModUpDigit>(), T.D, ctx.d_primes.as<uint64_t>(), ctx.stream);
+  launch_modup(coef, d, ext, nq, ctx.K, n, T.digits.as<ModUpDigit>(), T.D, ctx.alpha, ctx.d_mod.as<Modulus>(),
+               ctx.stream);
   if (T.ntt_list_len) {
     NttArgs a = ctx.ntt_args(ext, 1, 0, T.ntt_list_len, 0);
     a.list = T.ntt_list.as<uint2>();
@@ -539,8 +540,8 @@ void Ckks::moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, co
   LevelTables& T = level(nq);
   ntt_dense(acc + (size_t)nq * n, 2, K, w, ctx.L, true);
   uint64_t* conv = ws(3, (size_t)2 * ctx.L * n);
-  launch_convert(acc + (size_t)nq * n, (size_t)w * n, conv, (size_t)nq * n, 2, T.moddown.as<ConvTable>(), nq, n,
-                 ctx.d_primes.as<uint64_t>(), ctx.stream);
+  launch_convert(acc + (size_t)nq * n, (size_t)w * n, conv, (size_t)nq * n, 2, T.moddown.as<ConvTable>(), K, nq, n,
+                 ctx.d_mod.as<Modulus>(), ctx.stream);
   ntt_dense(conv, 2, nq, nq, 0, false);
   launch_moddown_combine(acc, (size_t)w * n, conv, (size_t)nq * n, pinv_.as<Shoup>(), add_c0, out, so, 2, nq, n,
                          ctx.d_primes.as<uint64_t>(), ctx.stream);

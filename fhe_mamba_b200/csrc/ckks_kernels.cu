@@ -170,49 +170,51 @@ __global__ void k_automorphism(const uint64_t* in, size_t si, uint64_t* out, siz
 // ---------------------------------------------------------------------------
 constexpr int kMaxSrc = 24;  // largest digit / special basis handled by the conversions
 
+#define FHE_NS_CASES(X) \
+  X(1) X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11) X(12) X(13) X(14) X(15) X(16) X(17) X(18) \
+  X(19) X(20) X(21) X(22) X(23) X(24)
+
 constexpr int kTgtChunk = 8;  // target limbs per block in the basis conversions
 
-// Block (x = coefficient tile, y = digit, z = chunk of kTgtChunk target limbs).
+// Block (x = coefficient tile, y = digit - digit0, z = chunk of kTgtChunk
+// target limbs).  NS = source limbs of every digit in the launch.  The sum
+// sum_i y_i hat_{i,t} is formed exactly in 128 bits and reduced once.
+template <int NS>
 __global__ void k_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t w, uint32_t n,
-                        const ModUpDigit* digits, const uint64_t* primes) {
-  __shared__ Shoup sh_hat[kTgtChunk * kMaxSrc];
-  __shared__ uint64_t sh_t[kTgtChunk];
-  const uint32_t j = blockIdx.y;
+                        const ModUpDigit* digits, uint32_t digit0, const Modulus* mods) {
+  __shared__ uint64_t sh_hat[kTgtChunk * NS];
+  __shared__ Modulus sh_m[kTgtChunk];
+  const uint32_t j = digit0 + blockIdx.y;
   const ModUpDigit dg = digits[j];
-  const uint32_t ns = dg.hi - dg.lo;
   const uint32_t t0 = blockIdx.z * kTgtChunk;
   if (t0 >= dg.conv.nt) return;  // uniform across the block
   const uint32_t nt = min((uint32_t)kTgtChunk, dg.conv.nt - t0);
-  for (uint32_t i = threadIdx.x; i < nt * ns; i += blockDim.x) sh_hat[i] = dg.conv.hat[(size_t)t0 * ns + i];
-  if (threadIdx.x < nt) sh_t[threadIdx.x] = primes[dg.conv.dst_prime[t0 + threadIdx.x]];
+  for (uint32_t i = threadIdx.x; i < nt * NS; i += blockDim.x) sh_hat[i] = dg.conv.hat[(size_t)t0 * NS + i].w;
+  if (threadIdx.x < nt) sh_m[threadIdx.x] = mods[dg.conv.dst_prime[t0 + threadIdx.x]];
   __syncthreads();
   const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
   if (k >= n) return;
   uint64_t* e = ext + (size_t)j * w * n;
-  uint64_t y[kMaxSrc];
+  uint64_t y[NS];
 #pragma unroll
-  for (int i = 0; i < kMaxSrc; ++i) {
-    if (i < (int)ns) {
-      const uint32_t l = dg.lo + i;
-      const Shoup h = dg.conv.hatinv[i];
-      y[i] = shoup_mul(coef[(size_t)l * n + k], h.w, h.wp, primes[dg.conv.src_prime[i]]);
-      if (blockIdx.z == 0) e[(size_t)l * n + k] = dntt[(size_t)l * n + k];
-    }
+  for (int i = 0; i < NS; ++i) {
+    const uint32_t l = dg.lo + i;
+    const Shoup h = dg.conv.hatinv[i];
+    y[i] = shoup_mul(coef[(size_t)l * n + k], h.w, h.wp, mods[dg.conv.src_prime[i]].q);
+    if (blockIdx.z == 0) e[(size_t)l * n + k] = dntt[(size_t)l * n + k];
   }
   for (uint32_t u = 0; u < nt; ++u) {
     const uint32_t tt = t0 + u;
-    const uint32_t l = tt < dg.lo ? tt : tt + ns;
-    const uint64_t t = sh_t[u], t2 = 2 * t;
-    const Shoup* hrow = sh_hat + u * ns;
-    uint64_t acc = 0;
+    const uint32_t l = tt < dg.lo ? tt : tt + NS;
+    uint64_t hi = 0, lo = 0;
 #pragma unroll
-    for (int i = 0; i < kMaxSrc; ++i) {
-      if (i < (int)ns) {
-        const Shoup h = hrow[i];
-        acc = csub(acc + shoup_lazy(y[i], h.w, h.wp, t), t2);
-      }
+    for (int i = 0; i < NS; ++i) {
+      const uint64_t c = sh_hat[u * NS + i];
+      const uint64_t pl = y[i] * c;
+      lo += pl;
+      hi += __umul64hi(y[i], c) + (lo < pl);
     }
-    e[(size_t)l * n + k] = csub(acc, t);
+    e[(size_t)l * n + k] = reduce_u128(hi, lo, sh_m[u]);
   }
 }
 
@@ -236,42 +238,39 @@ __global__ void k_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const u
 }
 
 // Block (x = coefficient tile, y = component, z = chunk of kTgtChunk targets).
+template <int NS>
 __global__ void k_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp,
-                          const ConvTable* tab, uint32_t n, const uint64_t* primes) {
-  __shared__ Shoup sh_hat[kTgtChunk * kMaxSrc];
-  __shared__ uint64_t sh_t[kTgtChunk];
+                          const ConvTable* tab, uint32_t n, const Modulus* mods) {
+  __shared__ uint64_t sh_hat[kTgtChunk * NS];
+  __shared__ Modulus sh_m[kTgtChunk];
   const ConvTable t = *tab;
   const uint32_t t0 = blockIdx.z * kTgtChunk;
   if (t0 >= t.nt) return;
   const uint32_t nt = min((uint32_t)kTgtChunk, t.nt - t0);
-  for (uint32_t i = threadIdx.x; i < nt * t.ns; i += blockDim.x) sh_hat[i] = t.hat[(size_t)t0 * t.ns + i];
-  if (threadIdx.x < nt) sh_t[threadIdx.x] = primes[t.dst_prime[t0 + threadIdx.x]];
+  for (uint32_t i = threadIdx.x; i < nt * NS; i += blockDim.x) sh_hat[i] = t.hat[(size_t)t0 * NS + i].w;
+  if (threadIdx.x < nt) sh_m[threadIdx.x] = mods[t.dst_prime[t0 + threadIdx.x]];
   __syncthreads();
   const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
   if (k >= n) return;
   const uint32_t c = blockIdx.y;
   const uint64_t* s = src + c * s_comp;
   uint64_t* d = dst + c * d_comp;
-  uint64_t y[kMaxSrc];
+  uint64_t y[NS];
 #pragma unroll
-  for (int i = 0; i < kMaxSrc; ++i) {
-    if (i < (int)t.ns) {
-      const Shoup h = t.hatinv[i];
-      y[i] = shoup_mul(s[(size_t)i * n + k], h.w, h.wp, primes[t.src_prime[i]]);
-    }
+  for (int i = 0; i < NS; ++i) {
+    const Shoup h = t.hatinv[i];
+    y[i] = shoup_mul(s[(size_t)i * n + k], h.w, h.wp, mods[t.src_prime[i]].q);
   }
   for (uint32_t u = 0; u < nt; ++u) {
-    const uint64_t q = sh_t[u], q2 = 2 * q;
-    const Shoup* hrow = sh_hat + u * t.ns;
-    uint64_t acc = 0;
+    uint64_t hi = 0, lo = 0;
 #pragma unroll
-    for (int i = 0; i < kMaxSrc; ++i) {
-      if (i < (int)t.ns) {
-        const Shoup h = hrow[i];
-        acc = csub(acc + shoup_lazy(y[i], h.w, h.wp, q), q2);
-      }
+    for (int i = 0; i < NS; ++i) {
+      const uint64_t cst = sh_hat[u * NS + i];
+      const uint64_t pl = y[i] * cst;
+      lo += pl;
+      hi += __umul64hi(y[i], cst) + (lo < pl);
     }
-    d[(size_t)(t0 + u) * n + k] = csub(acc, q);
+    d[(size_t)(t0 + u) * n + k] = reduce_u128(hi, lo, sh_m[u]);
   }
 }
 
@@ -527,10 +526,24 @@ void launch_automorphism(const uint64_t* in, size_t si, uint64_t* out, size_t so
 }
 
 void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t nq, uint32_t K, uint32_t n,
-                  const ModUpDigit* digits_dev, uint32_t D, const uint64_t* primes, cudaStream_t s) {
-  // every digit has at most nq + K - 1 targets
-  const uint32_t chunks = (nq + K + kTgtChunk - 1) / kTgtChunk;
-  k_modup<<<grid1(n, D, chunks), kTpb, 0, s>>>(coef, dntt, ext, nq + K, n, digits_dev, primes);
+                  const ModUpDigit* digits_dev, uint32_t D, uint32_t alpha, const Modulus* mods, cudaStream_t s) {
+  // Full digits share one launch, a shorter last digit gets its own.
+  const uint32_t full = nq / alpha, rest = nq % alpha;
+  auto go = [&](uint32_t ns, uint32_t digit0, uint32_t count) {
+    if (!count) return;
+    const uint32_t chunks = (nq + K - ns + kTgtChunk - 1) / kTgtChunk;
+    const dim3 grid = grid1(n, count, chunks);
+    switch (ns) {
+#define FHE_CASE(NS) \
+  case NS: k_modup<NS><<<grid, kTpb, 0, s>>>(coef, dntt, ext, nq + K, n, digits_dev, digit0, mods); break;
+      FHE_NS_CASES(FHE_CASE)
+#undef FHE_CASE
+      default: break;
+    }
+  };
+  go(alpha, 0, full);
+  go(rest, full, rest ? 1 : 0);
+  (void)D;
 }
 
 void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_t* evk, uint32_t key_limbs,
@@ -539,9 +552,17 @@ void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_
 }
 
 void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp, uint32_t ncomp,
-                    const ConvTable* t_dev, uint32_t nt, uint32_t n, const uint64_t* primes, cudaStream_t s) {
+                    const ConvTable* t_dev, uint32_t ns, uint32_t nt, uint32_t n, const Modulus* mods,
+                    cudaStream_t s) {
   const uint32_t chunks = (nt + kTgtChunk - 1) / kTgtChunk;
-  k_convert<<<grid1(n, ncomp, chunks), kTpb, 0, s>>>(src, s_comp, dst, d_comp, t_dev, n, primes);
+  const dim3 grid = grid1(n, ncomp, chunks);
+  switch (ns) {
+#define FHE_CASE(NS) \
+  case NS: k_convert<NS><<<grid, kTpb, 0, s>>>(src, s_comp, dst, d_comp, t_dev, n, mods); break;
+    FHE_NS_CASES(FHE_CASE)
+#undef FHE_CASE
+    default: break;
+  }
 }
 
 void launch_moddown_combine(const uint64_t* x, size_t sx, const uint64_t* conv, size_t sc, const Shoup* pinv,

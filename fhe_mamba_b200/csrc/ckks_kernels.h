@@ -68,17 +68,19 @@ struct ModUpDigit {
   uint32_t lo, hi;  // own limbs [lo, hi)
   ConvTable conv;   // sources lo..hi-1, targets = all other limbs of ext (in limb order)
 };
+// Digits are [j*alpha, min((j+1)*alpha, nq)); at most 24 limbs each.
 void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t nq, uint32_t K,
-                  uint32_t n, const ModUpDigit* digits_dev, uint32_t D, const uint64_t* primes,
+                  uint32_t n, const ModUpDigit* digits_dev, uint32_t D, uint32_t alpha, const Modulus* mods,
                   cudaStream_t s);
 // acc[2][w][N] = sum_j ext[j] * evk[j][0/1][key limb]; key limb of ext limb l is pm(l).
 void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_t* evk,
                       uint32_t key_limbs, PrimeMap pm, uint64_t* acc, uint32_t n, const Modulus* mods,
                       cudaStream_t s);
 // Basis conversion of ncomp polys: src limbs (coefficient form) -> dst (coefficient form).
-// nt must equal the table's target count.
+// ns / nt must equal the table's source / target counts (ns <= 24).
 void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp, uint32_t ncomp,
-                    const ConvTable* t_dev, uint32_t nt, uint32_t n, const uint64_t* primes, cudaStream_t s);
+                    const ConvTable* t_dev, uint32_t ns, uint32_t nt, uint32_t n, const Modulus* mods,
+                    cudaStream_t s);
 // out[c][i] = (x[c][i] - conv[c][i]) * pinv_i  (+ add[i] on component 0 when add != null).
 void launch_moddown_combine(const uint64_t* x, size_t sx, const uint64_t* conv, size_t sc,
                             const Shoup* pinv, const uint64_t* add, uint64_t* out, size_t so,

@@ -268,7 +268,8 @@ void Context::build_tables() {
     ninv[2 * i] = Twiddle{ni, nt::shoup(ni, q)};
     ninv[2 * i + 1] = Twiddle{wn, nt::shoup(wn, q)};
     const uint32_t b = nt::bitlen(q);
-    mods[i] = Modulus{q, (uint64_t)(((u128)1 << (2 * b)) / q), b, 0};
+    const uint64_t r64 = (uint64_t)(((u128)1 << 64) % q);
+    mods[i] = Modulus{q, (uint64_t)(((u128)1 << (2 * b)) / q), b, 0, r64, nt::shoup(r64, q), nt::shoup(1, q)};
   };
   // Row-pass round-2 twiddles: for row r, thread t and the j-th twiddle the
   // thread uses (forward: half-distances T/2..1, inverse: 1..T/2, groups g in

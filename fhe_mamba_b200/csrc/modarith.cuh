@@ -25,6 +25,9 @@ struct Modulus {
   uint64_t mu;       // floor(2^(2n) / q)
   uint32_t n;        // bit length of q
   uint32_t pad;
+  uint64_t r64;      // 2^64 mod q
+  uint64_t r64p;     // Shoup companion of r64
+  uint64_t mu1;      // floor(2^64 / q), Shoup companion of 1
 };
 
 __device__ __forceinline__ uint64_t shoup_lazy(uint64_t x, uint64_t w, uint64_t wp, uint64_t q) {
@@ -59,6 +62,14 @@ __device__ __forceinline__ uint64_t barrett_reduce(uint64_t hi, uint64_t lo, con
   uint64_t r = lo - qhat * m.q;  // exact: r < 3q < 2^64
   r = csub(r, m.q);
   return csub(r, m.q);
+}
+
+// (hi * 2^64 + lo) mod q for any 128-bit value: two Shoup products by
+// constants (2^64 mod q and 1) and two conditional subtractions.
+__device__ __forceinline__ uint64_t reduce_u128(uint64_t hi, uint64_t lo, const Modulus& m) {
+  const uint64_t a = shoup_lazy(hi, m.r64, m.r64p, m.q);
+  const uint64_t b = shoup_lazy(lo, 1, m.mu1, m.q);
+  return csub(csub(a + b, 2 * m.q), m.q);
 }
 
 __device__ __forceinline__ uint64_t mul_mod(uint64_t a, uint64_t b, const Modulus& m) {
