@@ -530,6 +530,7 @@ void Ckks::modup(const uint64_t* d, uint32_t nq, uint64_t* ext) {
   if (T.ntt_list_len) {
     NttArgs a = ctx.ntt_args(ext, 1, 0, T.ntt_list_len, 0);
     a.list = T.ntt_list.as<uint2>();
+    a.lazy = ctx.max_prime() < (uint64_t(1) << 60) ? 16 : 0;  // the list spans Q and P primes
     FHE_CUDA(ntt_forward(a));
   }
 }

@@ -355,9 +355,9 @@ NttArgs Context::ntt_args(uint64_t* data, uint32_t n_polys, uint32_t prime0, uin
   a.limb_stride = limb_stride;
   a.prime0 = prime0;
   a.stream = stream;
-  bool lazy = prime0 + n_limbs <= primes.size();
-  for (uint32_t i = prime0; lazy && i < prime0 + n_limbs; ++i) lazy = primes[i] < (uint64_t(1) << 59);
-  a.lazy = lazy;
+  uint64_t qmax = 0;
+  for (uint32_t i = prime0; i < prime0 + n_limbs && i < primes.size(); ++i) qmax = std::max(qmax, primes[i]);
+  a.lazy = qmax < (uint64_t(1) << 59) ? 32 : qmax < (uint64_t(1) << 60) ? 16 : 0;
   return a;
 }
 

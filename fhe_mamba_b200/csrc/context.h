@@ -101,6 +101,7 @@ struct Context {
   ~Context();
   void make_current() const;
   uint32_t n_primes() const { return (uint32_t)primes.size(); }
+  uint64_t max_prime() const { uint64_t m = 0; for (uint64_t q : primes) m = q > m ? q : m; return m; }
   void build_tables();
   uint64_t* stage(size_t words);
   NttArgs ntt_args(uint64_t* data, uint32_t n_polys, uint32_t prime0, uint32_t n_limbs,

@@ -30,7 +30,6 @@
 namespace fhe {
 namespace {
 
-constexpr int kColsPerCta = 32;  // one column per lane in the column pass
 
 template <int LS>
 struct PassShape {
@@ -51,16 +50,34 @@ __device__ __forceinline__ void ct_bfly(uint64_t& x, uint64_t& y, const Twiddle 
   x = x + t;
 }
 
-// Forward butterfly without reducing x: every output grows by at most 2q.
-// Used while the running bound stays below 2^64 (all primes < 2^59, see the
-// schedule in ntt_fwd_rows).  With red16, x is first brought below 16q.
-template <bool kReduce16>
-__device__ __forceinline__ void ct_bfly_lazy(uint64_t& x, uint64_t& y, const Twiddle tw, uint64_t q,
-                                             uint64_t q2, uint64_t q16) {
-  if (kReduce16) x = csub(x, q16);
-  const uint64_t t = shoup_lazy(y, tw.w, tw.wp, q);
-  y = x + q2 - t;
-  x = x + t;
+// Greedy lazy schedule.  A forward pass starts with residues below b0 * q and
+// every butterfly that does not reduce x raises the bound by 2q.  Stage s
+// reduces x below (LZ/2) q (one conditional subtraction of (LZ/2) q) only
+// when skipping it would let the bound exceed LZ q, where LZ q < 2^64:
+// LZ = 32 needs every prime below 2^59, LZ = 16 below 2^60; LZ = 0 selects
+// the reducing Harvey butterfly at every stage.
+__host__ __device__ constexpr bool lz_reduce(int LZ, int b0, int s) {
+  int b = b0;
+  for (int i = 0; i < s; ++i) b = (b + 2 > LZ) ? LZ / 2 + 2 : b + 2;
+  return b + 2 > LZ;
+}
+__host__ __device__ constexpr int lz_bound_after(int LZ, int b0, int stages) {
+  int b = b0;
+  for (int i = 0; i < stages; ++i) b = (b + 2 > LZ) ? LZ / 2 + 2 : b + 2;
+  return b;
+}
+
+template <int LZ>
+__device__ __forceinline__ void fwd_bfly(bool reduce, uint64_t& x, uint64_t& y, const Twiddle w, uint64_t q,
+                                         uint64_t q2, uint64_t qh) {
+  if constexpr (LZ == 0) {
+    ct_bfly(x, y, w, q, q2);
+  } else {
+    if (reduce) x = csub(x, qh);
+    const uint64_t t = shoup_lazy(y, w.w, w.wp, q);
+    y = x + q2 - t;
+    x = x + t;
+  }
 }
 
 // Inverse Gentleman-Sande (Harvey) butterfly on residues in [0, 2q).
@@ -93,8 +110,8 @@ __device__ __forceinline__ Twiddle ld_tw(const Twiddle* t, uint32_t i) {
 // Forward, pass 1: columns.  Column c of the tile (lane) holds words
 // j = col0 + c + 2^LB * k for k in [0, 2^LA).  Warp w is thread t of each
 // column.  Round 1: k = t + T*u.  Round 2: k = R*t + u.
-template <int LA, bool LAZY>
-__global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA <= 8 ? 2 : 1)
+template <int LA, int LZ, int COLS>
+__global__ void __launch_bounds__(COLS * PassShape<LA>::T, LA <= 8 ? 64 / COLS : 32 / COLS)
     ntt_fwd_cols(const NttArgs g) {
   using P = PassShape<LA>;
   extern __shared__ uint64_t smem[];
@@ -102,50 +119,47 @@ __global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA <= 8 ? 2 : 
   const uint32_t n = 1u << g.log_n;
   uint32_t pidx;
   uint64_t* a = block_limb(g, n, pidx);
-  const uint64_t q = g.primes[pidx], q2 = 2 * q;
+  const uint64_t q = g.primes[pidx], q2 = 2 * q, qh = (uint64_t)(LZ / 2) * q;
   const Twiddle* tw = g.tw + (size_t)pidx * n;
-  const int c = threadIdx.x & 31;
-  const int t = threadIdx.x >> 5;
-  const uint32_t col = blockIdx.x * kColsPerCta + c;
+  const int c = threadIdx.x % COLS;
+  const int t = threadIdx.x / COLS;
+  const uint32_t col = blockIdx.x * COLS + c;
 
   uint64_t x[P::R];
 #pragma unroll
   for (int u = 0; u < P::R; ++u) x[u] = a[col + ((size_t)(t + P::T * u) << LB)];
+  int st = 0;  // stage index within the pass (compile-time after unrolling)
 
   // Round 1: register half-distance h <-> k half-distance d = h*T.
   // Stage m = S/(2d); group i = k/(2d) = u/(2h) (thread independent).
 #pragma unroll
-  for (int h = P::R / 2; h >= 1; h >>= 1) {
+  for (int h = P::R / 2; h >= 1; h >>= 1, ++st) {
     const int m = P::S / (2 * h * P::T);
+    const bool red = lz_reduce(LZ, 1, st);
 #pragma unroll
     for (int g = 0; g < P::R; g += 2 * h) {
       const Twiddle w = ld_tw(tw, m + g / (2 * h));
 #pragma unroll
-      for (int v = 0; v < h; ++v) {
-        if constexpr (LAZY) ct_bfly_lazy<false>(x[g + v], x[g + v + h], w, q, q2, 0);
-        else ct_bfly(x[g + v], x[g + v + h], w, q, q2);
-      }
+      for (int v = 0; v < h; ++v) fwd_bfly<LZ>(red, x[g + v], x[g + v + h], w, q, q2, qh);
     }
   }
   if constexpr (P::LT > 0) {
     // Exchange: smem[k][c].
 #pragma unroll
-    for (int u = 0; u < P::R; ++u) smem[(t + P::T * u) * kColsPerCta + c] = x[u];
+    for (int u = 0; u < P::R; ++u) smem[(t + P::T * u) * COLS + c] = x[u];
     __syncthreads();
 #pragma unroll
-    for (int u = 0; u < P::R; ++u) x[u] = smem[(P::R * t + u) * kColsPerCta + c];
+    for (int u = 0; u < P::R; ++u) x[u] = smem[(P::R * t + u) * COLS + c];
     // Round 2: half-distance h (k units), m = S/(2h), group i = (R*t + g)/(2h).
 #pragma unroll
-    for (int h = P::T / 2; h >= 1; h >>= 1) {
+    for (int h = P::T / 2; h >= 1; h >>= 1, ++st) {
       const int m = P::S / (2 * h);
+      const bool red = lz_reduce(LZ, 1, st);
 #pragma unroll
       for (int g = 0; g < P::R; g += 2 * h) {
         const Twiddle w = ld_tw(tw, m + (P::R * t + g) / (2 * h));
 #pragma unroll
-        for (int v = 0; v < h; ++v) {
-          if constexpr (LAZY) ct_bfly_lazy<false>(x[g + v], x[g + v + h], w, q, q2, 0);
-          else ct_bfly(x[g + v], x[g + v + h], w, q, q2);
-        }
+        for (int v = 0; v < h; ++v) fwd_bfly<LZ>(red, x[g + v], x[g + v + h], w, q, q2, qh);
       }
     }
 #pragma unroll
@@ -166,13 +180,11 @@ __device__ __forceinline__ int rpad(int k) { return k + (k >> 4); }
 // stores are contiguous.  Thread t of a row: round 1 k = t + T*u, round 2
 // k = R*t + u.  Final output reduced from [0, 4q) to [0, q).
 //
-// LAZY schedule (every prime of the launch below 2^59, so 32q < 2^64): the
-// column pass never reduces (outputs < (2 LA + 1) q <= 17q); here the first
-// stage of each round brings x below 16q and the others do not reduce, so
-// values stay below 18q + 2q * (stages - 1) <= 26q; the output is reduced
-// with one Shoup multiplication by 1 and a conditional subtraction.
-template <int LB, int ROWS, bool LAZY>
-__global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
+// With LZ > 0 the column pass leaves values below lz_bound_after(LZ, 1, LA) q;
+// this pass continues the greedy schedule and reduces the output with one
+// Shoup multiplication by 1 and a conditional subtraction.
+template <int LA, int LB, int ROWS, int LZ>
+__global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 64 / ROWS : 32 / ROWS)
     ntt_fwd_rows(const NttArgs g) {
   using P = PassShape<LB>;
   extern __shared__ uint64_t smem[];
@@ -180,14 +192,15 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
   const uint32_t n = 1u << g.log_n;
   uint32_t pidx;
   uint64_t* a = block_limb(g, n, pidx) + (size_t)blockIdx.x * ROWS * P::S;
-  const uint64_t q = g.primes[pidx], q2 = 2 * q, q16 = 16 * q;
-  const uint64_t mu = LAZY ? ~0ull / q : 0;  // floor(2^64 / q), Shoup companion of 1
+  const uint64_t q = g.primes[pidx], q2 = 2 * q, qh = (uint64_t)(LZ / 2) * q;
+  const uint64_t mu = LZ ? ~0ull / q : 0;  // floor(2^64 / q), Shoup companion of 1
+  constexpr int b0 = lz_bound_after(LZ, 1, LA);  // bound left by the column pass
   const Twiddle* tw = g.tw + (size_t)pidx * n;
   const int t = threadIdx.x % P::T;
   const int rr = threadIdx.x / P::T;
   const uint32_t row = blockIdx.x * ROWS + rr;
   auto fwd_final = [](uint64_t v, uint64_t q, uint64_t q2, uint64_t mu) {
-    if constexpr (LAZY) return csub(shoup_lazy(v, 1, mu, q), q);
+    if constexpr (LZ != 0) return csub(shoup_lazy(v, 1, mu, q), q);
     else return csub(csub(v, q2), q);
   };
 
@@ -206,23 +219,18 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
   for (int u = 0; u < P::R; ++u) x[u] = srow[rpad(t + P::T * u)];
 
   // Global stage for k-half-distance d: m = N/(2d); i = row*S/(2d) + k/(2d).
+  int st = 0;
 #pragma unroll
-  for (int h = P::R / 2; h >= 1; h >>= 1) {
+  for (int h = P::R / 2; h >= 1; h >>= 1, ++st) {
     const int d = h * P::T;
     const uint32_t m = n / (2 * d);
     const uint32_t base = m + row * (P::S / (2 * d));
+    const bool red = lz_reduce(LZ, b0, st);
 #pragma unroll
     for (int g = 0; g < P::R; g += 2 * h) {
       const Twiddle w = ld_tw(tw, base + g / (2 * h));
 #pragma unroll
-      for (int v = 0; v < h; ++v) {
-        if constexpr (LAZY) {
-          if (h == P::R / 2) ct_bfly_lazy<true>(x[g + v], x[g + v + h], w, q, q2, q16);
-          else ct_bfly_lazy<false>(x[g + v], x[g + v + h], w, q, q2, q16);
-        } else {
-          ct_bfly(x[g + v], x[g + v + h], w, q, q2);
-        }
-      }
+      for (int v = 0; v < h; ++v) fwd_bfly<LZ>(red, x[g + v], x[g + v + h], w, q, q2, qh);
     }
   }
   if constexpr (P::LT > 0) {
@@ -235,19 +243,13 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
     const Twiddle* t2 = g.tw2 + (size_t)pidx * g.tw2_stride + (size_t)row * (P::J * P::T) + t;
     int j = 0;
 #pragma unroll
-    for (int h = P::T / 2; h >= 1; h >>= 1) {
+    for (int h = P::T / 2; h >= 1; h >>= 1, ++st) {
+      const bool red = lz_reduce(LZ, b0, st);
 #pragma unroll
       for (int g = 0; g < P::R; g += 2 * h, ++j) {
         const Twiddle w = ld_tw(t2, j * P::T);
 #pragma unroll
-        for (int v = 0; v < h; ++v) {
-          if constexpr (LAZY) {
-            if (h == P::T / 2) ct_bfly_lazy<true>(x[g + v], x[g + v + h], w, q, q2, q16);
-            else ct_bfly_lazy<false>(x[g + v], x[g + v + h], w, q, q2, q16);
-          } else {
-            ct_bfly(x[g + v], x[g + v + h], w, q, q2);
-          }
-        }
+        for (int v = 0; v < h; ++v) fwd_bfly<LZ>(red, x[g + v], x[g + v + h], w, q, q2, qh);
       }
     }
 #pragma unroll
@@ -272,7 +274,7 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
 // Round 1 on contiguous runs k = R*t + u (half-distances 1 .. T/2), exchange,
 // round 2 on k = t + T*u (half-distances T .. S/2).  Input in [0, q).
 template <int LB, int ROWS>
-__global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
+__global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 64 / ROWS : 32 / ROWS)
     ntt_inv_rows(const NttArgs g) {
   using P = PassShape<LB>;
   extern __shared__ uint64_t smem[];
@@ -346,8 +348,8 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 2 : 1)
 // k = R*t + u (k half-distances 1 .. T/2), exchange, round 2 on k = t + T*u.
 // The last stage (m = 1) folds in N^{-1}: x' = (x+y)/N, y' = (x-y)*w/N, with
 // tw_last = (N^{-1}, N^{-1}') and tw_last2 = (w_1 N^{-1}, ...).
-template <int LA>
-__global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA <= 8 ? 2 : 1)
+template <int LA, int COLS>
+__global__ void __launch_bounds__(COLS * PassShape<LA>::T, LA <= 8 ? 64 / COLS : 32 / COLS)
     ntt_inv_cols(const NttArgs g) {
   using P = PassShape<LA>;
   extern __shared__ uint64_t smem[];
@@ -357,9 +359,9 @@ __global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA <= 8 ? 2 : 
   uint64_t* a = block_limb(g, n, pidx);
   const uint64_t q = g.primes[pidx], q2 = 2 * q;
   const Twiddle* tw = g.tw_inv + (size_t)pidx * n;
-  const int c = threadIdx.x & 31;
-  const int t = threadIdx.x >> 5;
-  const uint32_t col = blockIdx.x * kColsPerCta + c;
+  const int c = threadIdx.x % COLS;
+  const int t = threadIdx.x / COLS;
+  const uint32_t col = blockIdx.x * COLS + c;
   uint64_t x[P::R];
 
   if constexpr (P::LT > 0) {
@@ -376,10 +378,10 @@ __global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA <= 8 ? 2 : 
       }
     }
 #pragma unroll
-    for (int u = 0; u < P::R; ++u) smem[(P::R * t + u) * kColsPerCta + c] = x[u];
+    for (int u = 0; u < P::R; ++u) smem[(P::R * t + u) * COLS + c] = x[u];
     __syncthreads();
 #pragma unroll
-    for (int u = 0; u < P::R; ++u) x[u] = smem[(t + P::T * u) * kColsPerCta + c];
+    for (int u = 0; u < P::R; ++u) x[u] = smem[(t + P::T * u) * COLS + c];
   } else {
 #pragma unroll
     for (int u = 0; u < P::R; ++u) x[u] = a[col + ((size_t)(t + P::T * u) << LB)];
@@ -410,60 +412,78 @@ __global__ void __launch_bounds__(kColsPerCta * PassShape<LA>::T, LA <= 8 ? 2 : 
   for (int u = 0; u < P::R; ++u) a[col + ((size_t)(t + P::T * u) << LB)] = x[u];
 }
 
-constexpr int kRowsPerCta = 32;
-
-template <int LB>
+template <int LB, int ROWS>
 size_t rows_smem() {
   using P = PassShape<LB>;
-  return (size_t)kRowsPerCta * (P::S + P::S / 16) * sizeof(uint64_t);
+  return (size_t)ROWS * (P::S + P::S / 16) * sizeof(uint64_t);
 }
-template <int LA>
+template <int LA, int COLS>
 size_t cols_smem() {
   using P = PassShape<LA>;
-  return P::LT > 0 ? (size_t)kColsPerCta * P::S * sizeof(uint64_t) : 0;
+  return P::LT > 0 ? (size_t)COLS * P::S * sizeof(uint64_t) : 0;
 }
 
-template <int LA, int LB, bool LAZY>
+// Tile width: 32 columns / rows per CTA, or 16 when a launch would not fill
+// two waves of the 148 SMs (finer CTAs balance small batches better).
+inline int tile_width(uint32_t tiles32) { return tiles32 >= 2u * 2u * 148u ? 32 : 16; }
+
+template <int LA, int LB, int LZ, int TW>
 cudaError_t launch_fwd_impl(const NttArgs& g) {
   using PA = PassShape<LA>;
   using PB = PassShape<LB>;
-  const size_t sa = cols_smem<LA>(), sb = rows_smem<LB>();
+  const size_t sa = cols_smem<LA, TW>(), sb = rows_smem<LB, TW>();
   cudaError_t e;
-  e = cudaFuncSetAttribute(ntt_fwd_cols<LA, LAZY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa);
+  e = cudaFuncSetAttribute(ntt_fwd_cols<LA, LZ, TW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(ntt_fwd_rows<LB, kRowsPerCta, LAZY>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
+  e = cudaFuncSetAttribute(ntt_fwd_rows<LA, LB, TW, LZ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
   if (e != cudaSuccess) return e;
   const uint32_t polys = g.list ? 1 : g.n_polys;
-  dim3 ga((1u << LB) / kColsPerCta, polys, g.n_limbs);
-  ntt_fwd_cols<LA, LAZY><<<ga, kColsPerCta * PA::T, sa, g.stream>>>(g);
-  dim3 gb((1u << LA) / kRowsPerCta, polys, g.n_limbs);
-  ntt_fwd_rows<LB, kRowsPerCta, LAZY><<<gb, kRowsPerCta * PB::T, sb, g.stream>>>(g);
+  dim3 ga((1u << LB) / TW, polys, g.n_limbs);
+  ntt_fwd_cols<LA, LZ, TW><<<ga, TW * PA::T, sa, g.stream>>>(g);
+  dim3 gb((1u << LA) / TW, polys, g.n_limbs);
+  ntt_fwd_rows<LA, LB, TW, LZ><<<gb, TW * PB::T, sb, g.stream>>>(g);
   return cudaGetLastError();
+}
+
+template <int LA, int LB, int TW>
+cudaError_t launch_fwd_tw(const NttArgs& g) {
+  switch (g.lazy) {
+    case 32: return launch_fwd_impl<LA, LB, 32, TW>(g);
+    case 16: return launch_fwd_impl<LA, LB, 16, TW>(g);
+    default: return launch_fwd_impl<LA, LB, 0, TW>(g);
+  }
 }
 
 template <int LA, int LB>
 cudaError_t launch_fwd(const NttArgs& g) {
-  return g.lazy ? launch_fwd_impl<LA, LB, true>(g) : launch_fwd_impl<LA, LB, false>(g);
+  const uint32_t polys = g.list ? 1 : g.n_polys;
+  return tile_width(((1u << LB) / 32) * polys * g.n_limbs) == 32 ? launch_fwd_tw<LA, LB, 32>(g)
+                                                                   : launch_fwd_tw<LA, LB, 16>(g);
+}
+
+template <int LA, int LB, int TW>
+cudaError_t launch_inv_tw(const NttArgs& g) {
+  using PA = PassShape<LA>;
+  using PB = PassShape<LB>;
+  const size_t sa = cols_smem<LA, TW>(), sb = rows_smem<LB, TW>();
+  cudaError_t e;
+  e = cudaFuncSetAttribute(ntt_inv_cols<LA, TW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(ntt_inv_rows<LB, TW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
+  if (e != cudaSuccess) return e;
+  const uint32_t polys = g.list ? 1 : g.n_polys;
+  dim3 gb((1u << LA) / TW, polys, g.n_limbs);
+  ntt_inv_rows<LB, TW><<<gb, TW * PB::T, sb, g.stream>>>(g);
+  dim3 ga((1u << LB) / TW, polys, g.n_limbs);
+  ntt_inv_cols<LA, TW><<<ga, TW * PA::T, sa, g.stream>>>(g);
+  return cudaGetLastError();
 }
 
 template <int LA, int LB>
 cudaError_t launch_inv(const NttArgs& g) {
-  using PA = PassShape<LA>;
-  using PB = PassShape<LB>;
-  const size_t sa = cols_smem<LA>(), sb = rows_smem<LB>();
-  cudaError_t e;
-  e = cudaFuncSetAttribute(ntt_inv_cols<LA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(ntt_inv_rows<LB, kRowsPerCta>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
-  if (e != cudaSuccess) return e;
   const uint32_t polys = g.list ? 1 : g.n_polys;
-  dim3 gb((1u << LA) / kRowsPerCta, polys, g.n_limbs);
-  ntt_inv_rows<LB, kRowsPerCta><<<gb, kRowsPerCta * PB::T, sb, g.stream>>>(g);
-  dim3 ga((1u << LB) / kColsPerCta, polys, g.n_limbs);
-  ntt_inv_cols<LA><<<ga, kColsPerCta * PA::T, sa, g.stream>>>(g);
-  return cudaGetLastError();
+  return tile_width(((1u << LB) / 32) * polys * g.n_limbs) == 32 ? launch_inv_tw<LA, LB, 32>(g)
+                                                                   : launch_inv_tw<LA, LB, 16>(g);
 }
 
 }  // namespace

@@ -21,9 +21,10 @@ struct NttArgs {
   // Optional explicit limb list (device array, n_limbs entries, n_polys must
   // be 1): entry {x, y} transforms the limb at data + x*N with prime y.
   const uint2* list = nullptr;
-  // Every prime the launch touches is below 2^59: the forward transform may
-  // skip most intermediate reductions (see ntt_fwd_rows).
-  bool lazy = false;
+  // Lazy-reduction level of the forward transform: 32 when every prime the
+  // launch touches is below 2^59, 16 when below 2^60, else 0 (reduce at
+  // every butterfly).  See the schedule in ntt.cu.
+  int lazy = 0;
   // Row-pass round-2 twiddles, thread-fastest layout (see Context::build_tables).
   const Twiddle* tw2 = nullptr;
   const Twiddle* tw2_inv = nullptr;
