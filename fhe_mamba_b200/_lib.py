@@ -119,6 +119,7 @@ SIGNATURES = {
     "fhe_rescale_noalloc": [vp, vp, u32, u32, vp],
     "fhe_encode_batch": [vp, PD, PD, u32, u32, u32, f64, ctypes.POINTER(vp)],
     "fhe_linear_transform": [vp, vp, ctypes.POINTER(vp), u32, u32, ctypes.POINTER(vp)],
+    "fhe_chebyshev": [vp, vp, PD, u32, f64, f64, ctypes.POINTER(vp)],
 }
 
 _lock = threading.Lock()

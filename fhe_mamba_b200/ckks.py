@@ -236,6 +236,15 @@ class CryptoContext:
         arr = (vp * len(diagonals))(*[d.handle if d is not None else None for d in diagonals])
         return self._ct("fhe_linear_transform", ct.handle, arr, baby, giant)
 
+    def EvalChebyshevSeries(self, ct, coefficients, a: float, b: float):
+        """sum_i c_i T_i(u), u = (2x - a - b) / (b - a), Paterson-Stockmeyer on the device."""
+        c = np.ascontiguousarray(np.asarray(coefficients, dtype=np.float64))
+        return self._ct("fhe_chebyshev", ct.handle, c.ctypes.data_as(PD), len(c), float(a), float(b))
+
+    def EvalChebyshevFunction(self, func, ct, a: float, b: float, degree: int):
+        """Interpolates func at Chebyshev nodes on [a, b] and evaluates the series."""
+        return self.EvalChebyshevSeries(ct, chebyshev_coefficients(func, a, b, degree), a, b)
+
     def Encrypt(self, pt: Plaintext, _unused=None):
         if isinstance(_unused, Plaintext):  # Encrypt(publicKey, pt) call order
             pt = _unused
@@ -348,6 +357,18 @@ class CryptoContext:
 
 def GenCryptoContext(params: CCParams) -> CryptoContext:
     return CryptoContext(params)
+
+
+def chebyshev_coefficients(func, a: float, b: float, degree: int) -> np.ndarray:
+    """Chebyshev interpolation coefficients c_0..c_degree of func on [a, b]
+    (Chebyshev nodes of the first kind; the series is sum c_i T_i(u))."""
+    n = degree + 1
+    j = np.arange(n)
+    nodes = np.cos(np.pi * (j + 0.5) / n)
+    fx = np.asarray(func((b - a) / 2 * nodes + (a + b) / 2), dtype=np.float64)
+    c = np.array([2.0 / n * np.sum(fx * np.cos(np.pi * k * (j + 0.5) / n)) for k in range(n)])
+    c[0] /= 2
+    return c
 
 
 def bsgs_diagonals(W: np.ndarray, baby: int, giant: int, slots: int):

@@ -547,4 +547,13 @@ int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* dia
   });
 }
 
+int fhe_chebyshev(fhe_ctx* ctx, const fhe_ct* a, const double* coeffs, uint32_t n, double lo, double hi,
+                  fhe_ct** out) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(coeffs != nullptr && n >= 1, "need at least one coefficient");
+    put_ct(out, k.chebyshev(ct_of(a), std::vector<double>(coeffs, coeffs + n), lo, hi));
+  });
+}
+
 }  // extern "C"

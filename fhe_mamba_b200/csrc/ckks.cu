@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <functional>
 
 #include "ckks.h"
 
@@ -655,6 +656,65 @@ std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a, const std::vector<const 
     launch_ew(Ew::Add, out->data(), cs, r, cs, out->data(), cs, 2, nq, n, PrimeMap{nq, ctx.L},
               ctx.d_mod.as<Modulus>(), ctx.stream);
   }
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::chebyshev(const Ct& x, const std::vector<double>& coeffs, double lo, double hi) {
+  require(!coeffs.empty(), "no Chebyshev coefficients", -1);
+  require(hi > lo, "empty Chebyshev interval", -1);
+  // u = x * 2/(hi-lo) - (lo+hi)/(hi-lo)
+  std::unique_ptr<Ct> u = mul_scalar(x, 2.0 / (hi - lo));
+  u = add_scalar(*u, -(lo + hi) / (hi - lo));
+  std::map<int, std::unique_ptr<Ct>> cache;
+  int levels = 0;
+  while ((1 << levels) < (int)coeffs.size()) ++levels;
+  const int baby = 1 << ((std::max(1, levels) + 1) / 2);
+  std::function<const Ct&(int)> basis = [&](int i) -> const Ct& {
+    if (i == 1) return *u;
+    auto it = cache.find(i);
+    if (it != cache.end()) return *it->second;
+    std::unique_ptr<Ct> out;
+    if (i % 2 == 0) {
+      const Ct& h = basis(i / 2);
+      auto sq = mul(h, h);
+      auto dbl = add(*sq, *sq, false);
+      out = add_scalar(*dbl, -1.0);
+    } else {
+      const Ct& a = basis((i + 1) / 2);
+      const Ct& b = basis(i / 2);
+      auto pr = mul(a, b);
+      auto dbl = add(*pr, *pr, false);
+      out = add(*dbl, *u, true);
+    }
+    const Ct& ref = *out;
+    cache[i] = std::move(out);
+    return ref;
+  };
+  std::function<std::unique_ptr<Ct>(std::vector<double>)> evaluate =
+      [&](std::vector<double> c) -> std::unique_ptr<Ct> {
+    const int degree = (int)c.size() - 1;
+    if (degree < baby) {
+      std::unique_ptr<Ct> out;
+      for (int i = 1; i <= degree; ++i) {
+        if (std::fabs(c[i]) < 1e-14) continue;
+        auto term = mul_scalar(basis(i), c[i]);
+        out = out ? add(*out, *term, false) : std::move(term);
+      }
+      if (!out) out = mul_scalar(*u, 0.0);
+      return add_scalar(*out, c[0]);
+    }
+    int k = baby;
+    while (2 * k - 1 < degree) k *= 2;
+    std::vector<double> upper(c.begin() + k, c.end()), lower(c.begin(), c.begin() + k);
+    for (size_t i = 1; i < upper.size(); ++i) upper[i] *= 2;
+    for (int i = k + 1; i <= degree; ++i) lower[2 * k - i] -= c[i];
+    auto lo_part = evaluate(lower);
+    auto up_part = evaluate(upper);
+    auto prod = mul(basis(k), *up_part);
+    return add(*lo_part, *prod, false);
+  };
+  auto out = evaluate(coeffs);
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
   return out;
 }
 

@@ -93,6 +93,12 @@ class Ckks {
   // with the same scale; babies share one ModUp.
   std::unique_ptr<Ct> linear_transform(const Ct& a, const std::vector<const Pt*>& diags, uint32_t b, uint32_t G);
 
+  // Paterson-Stockmeyer evaluation of sum_i c_i T_i(u), u = (2x - lo - hi) / (hi - lo),
+  // following the reference's PackedEvaluator::chebyshev (packed_fideslib.cpp:533-599):
+  // T_{2k} = 2 T_k^2 - 1, T_{2k+1} = 2 T_k T_{k+1} - u, baby size
+  // 2^ceil(log2(deg+1)/2), recursive division by T_k for k a power of two.
+  std::unique_ptr<Ct> chebyshev(const Ct& x, const std::vector<double>& c, double lo, double hi);
+
   // Brings `a` to (nq, scale): FLEXIBLEAUTO adjustment by an integer multiple
   // and a rescale, then dropping limbs.
   std::unique_ptr<Ct> adjust(const Ct& a, uint32_t nq, double scale);

@@ -223,6 +223,12 @@ int fhe_encode_batch(fhe_ctx* ctx, const double* re, const double* im, uint32_t 
 int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* diags, uint32_t baby,
                          uint32_t giant, fhe_ct** out);
 
+/* EvalChebyshevSeries: sum_{i<n} coeffs[i] T_i((2a - lo - hi)/(hi - lo)) by
+ * Paterson-Stockmeyer with the reference's recursion
+ * (PackedEvaluator::chebyshev, packed_fideslib.cpp:533-599). */
+int fhe_chebyshev(fhe_ctx* ctx, const fhe_ct* a, const double* coeffs, uint32_t n, double lo, double hi,
+                  fhe_ct** out);
+
 /* Rescale that allocates nothing.  This entry point has no counterpart in the
  * reference; it exists for callers that cannot let the library allocate
  * device memory when they rescale — code working inside a memory budget
