@@ -214,6 +214,43 @@ def measure_ckks(local, reps=10):
     return ks, mv
 
 
+def measure_bootstrap(local, reps=3):
+    """One full-packing bootstrap at the reference's native parameters
+    (N=2^16, 2^15 slots, multiplicative depth 44, 59-bit scaling / 60-bit
+    first prime, dnum 3, level budget {4, 4}; packed_fideslib.cpp:1061-1089),
+    timed with CUDA events on the context stream; the input has 2 limbs left."""
+    import torch
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    cc = CryptoContext(CCParams(ring_dim=1 << 16, multiplicative_depth=44, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3, device=local))
+    cc.KeyGen(11)
+    cc.EvalBootstrapSetup((4, 4))
+    cc.EvalBootstrapKeyGen()
+    stream = torch.cuda.ExternalStream(cc.stream_ptr(), device=torch.device("cuda", local))
+    x = np.random.default_rng(5).uniform(-1, 1, cc.slots)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    cc.LevelReduceInPlace(ct, cc.n_q - 2)
+    out = cc.EvalBootstrap(ct)  # first call encodes the SlotToCoeff diagonals
+    cc.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        out = cc.EvalBootstrap(ct)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    err = float(np.max(np.abs(cc.Decrypt(out).GetRealPackedValue() - x)))
+    info = cc.bootstrap_info()
+    rep = {"workload": "full-packing bootstrap, N=2^16, 2^15 slots, depth 44 (45 Q limbs), 59/60-bit, dnum 3, "
+                       "level budget {4,4}, uniform ternary secret",
+           "ms": ms, "limbs_in": 2, "limbs_out": out.n_limbs(), "levels": cc.bootstrap_levels(),
+           "max_abs_err": err, "correction": info["correction"], "chebyshev_degree": info["chebyshev_degree"],
+           "rotation_keys": info["rotation_keys"]}
+    del out, ct
+    cc.close()
+    return rep
+
+
 def host_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -281,7 +318,8 @@ def main():
     torch.cuda.set_device(local)
     if args.ckks_only:
         ks, mv = measure_ckks(local)
-        print(json.dumps({"keyswitch": ks, "bsgs_matvec": mv}), flush=True)
+        bt = measure_bootstrap(local)
+        print(json.dumps({"keyswitch": ks, "bsgs_matvec": mv, "bootstrap": bt}), flush=True)
         return
     if world > 1:
         from datetime import timedelta
@@ -393,6 +431,7 @@ def main():
             ks, mv = measure_ckks(local)
             line["keyswitch"] = ks
             line["bsgs_matvec"] = mv
+            line["bootstrap"] = measure_bootstrap(local)
         if not args.no_cpu_baseline:
             v, dt, sample = cpu_baseline(host_threads())
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",

@@ -118,7 +118,16 @@ SIGNATURES = {
     "fhe_rotate_hoisted": [vp, vp, PI32, u32, ctypes.POINTER(vp)],
     "fhe_rescale_noalloc": [vp, vp, u32, u32, vp],
     "fhe_encode_batch": [vp, PD, PD, u32, u32, u32, f64, ctypes.POINTER(vp)],
-    "fhe_linear_transform": [vp, vp, ctypes.POINTER(vp), u32, u32, ctypes.POINTER(vp)],
+    "fhe_linear_transform": [vp, vp, ctypes.POINTER(vp), u32, u32, i32, i32, ctypes.POINTER(vp)],
+    "fhe_bootstrap_setup": [vp, u32, u32, u32, i32],
+    "fhe_bootstrap_keygen": [vp],
+    "fhe_bootstrap": [vp, vp, ctypes.POINTER(vp)],
+    "fhe_bootstrap_stage": [vp, i32, vp, ctypes.POINTER(vp)],
+    "fhe_bootstrap_info": [vp, ctypes.POINTER(i32), ctypes.POINTER(u32), ctypes.POINTER(u32)],
+    "fhe_bootstrap_levels": [vp, ctypes.POINTER(u32)],
+    "fhe_mod_raise": [vp, vp, ctypes.POINTER(vp)],
+    "fhe_mul_i": [vp, vp, ctypes.POINTER(vp)],
+    "fhe_ct_set_scale": [vp, vp, f64],
     "fhe_chebyshev": [vp, vp, PD, u32, f64, f64, ctypes.POINTER(vp)],
 }
 

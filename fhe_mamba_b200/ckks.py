@@ -229,12 +229,49 @@ class CryptoContext:
              arr.shape[1], self.n_q - level, float(scale), outs)
         return [Plaintext(self, vp(o)) for o in outs]
 
-    def EvalLinearTransform(self, ct, diagonals, baby: int, giant: int):
-        """out = sum_g rot(sum_j diagonals[g*baby+j] (.) rot(ct, j), g*baby); None = zero diagonal."""
+    def EvalLinearTransform(self, ct, diagonals, baby: int, giant: int, stride: int = 1, giant_offset: int = 0):
+        """out = sum_g rot(sum_j diagonals[g*baby+j] (.) rot(ct, j*stride), (g*baby - giant_offset)*stride);
+        None = zero diagonal."""
         if len(diagonals) != baby * giant:
             raise _lib.InvalidArgument(-1, "EvalLinearTransform", "need baby*giant diagonals")
         arr = (vp * len(diagonals))(*[d.handle if d is not None else None for d in diagonals])
-        return self._ct("fhe_linear_transform", ct.handle, arr, baby, giant)
+        return self._ct("fhe_linear_transform", ct.handle, arr, baby, giant, int(stride), int(giant_offset))
+
+    def EvalBootstrapSetup(self, level_budget=(4, 4), dim1=(0, 0), slots: int = 0, correction_factor: int = 0):
+        """OpenFHE EvalBootstrapSetup(levelBudget, dim1, slots, correctionFactor); dim1 is
+        accepted for signature compatibility (the BSGS split is chosen per group)."""
+        call("fhe_bootstrap_setup", self.h, int(level_budget[0]), int(level_budget[1]), int(slots),
+             int(correction_factor))
+
+    def EvalBootstrapKeyGen(self, secret_key=None, slots: int = 0):
+        call("fhe_bootstrap_keygen", self.h)
+
+    def EvalBootstrap(self, ct):
+        return self._ct("fhe_bootstrap", ct.handle)
+
+    def EvalBootstrapStage(self, stage: int, ct):
+        """0 = scale down and ModRaise, 1 = CoeffToSlot, 2 = EvalMod, 3 = SlotToCoeff."""
+        return self._ct("fhe_bootstrap_stage", int(stage), ct.handle)
+
+    def bootstrap_info(self):
+        c, d, k = ctypes.c_int32(), ctypes.c_uint32(), ctypes.c_uint32()
+        call("fhe_bootstrap_info", self.h, ctypes.byref(c), ctypes.byref(d), ctypes.byref(k))
+        return {"correction": c.value, "chebyshev_degree": d.value, "rotation_keys": k.value}
+
+    def bootstrap_levels(self):
+        """Limb counts of the last bootstrap after ModRaise, CoeffToSlot, EvalMod, SlotToCoeff."""
+        a = (ctypes.c_uint32 * 4)()
+        call("fhe_bootstrap_levels", self.h, a)
+        return list(a)
+
+    def ModRaise(self, ct):
+        return self._ct("fhe_mod_raise", ct.handle)
+
+    def MultByI(self, ct):
+        return self._ct("fhe_mul_i", ct.handle)
+
+    def SetScalingFactor(self, ct, scale: float):
+        call("fhe_ct_set_scale", self.h, ct.handle, float(scale))
 
     def EvalChebyshevSeries(self, ct, coefficients, a: float, b: float):
         """sum_i c_i T_i(u), u = (2x - a - b) / (b - a), Paterson-Stockmeyer on the device."""

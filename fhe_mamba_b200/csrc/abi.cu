@@ -5,6 +5,7 @@
 #include <string>
 
 #include "../../include/fhe_b200.h"
+#include "bootstrap.h"
 #include "ckks.h"
 #include "context.h"
 
@@ -16,6 +17,7 @@ void rescale_noalloc(Context& c, const uint64_t* in, uint32_t ncomp, uint32_t nq
 struct fhe_ctx {
   fhe::Context c;
   std::unique_ptr<fhe::Ckks> ck;
+  std::unique_ptr<fhe::Bootstrapper> boot;
 };
 struct fhe_ct {
   std::unique_ptr<fhe::Ct> p;
@@ -537,13 +539,91 @@ int fhe_encode_batch(fhe_ctx* ctx, const double* re, const double* im, uint32_t 
 }
 
 int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* diags, uint32_t baby,
-                         uint32_t giant, fhe_ct** out) {
+                         uint32_t giant, int32_t stride, int32_t giant_offset, fhe_ct** out) {
   return guarded([&] {
     fhe::Ckks& k = ckks(ctx);
     fhe::require(diags != nullptr, "null diagonal array");
     std::vector<const fhe::Pt*> d((size_t)baby * giant);
     for (size_t i = 0; i < d.size(); ++i) d[i] = diags[i] ? diags[i]->p.get() : nullptr;
-    put_ct(out, k.linear_transform(ct_of(a), d, baby, giant));
+    put_ct(out, k.linear_transform(ct_of(a), d, baby, giant, stride, giant_offset));
+  });
+}
+
+int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, uint32_t slots,
+                        int32_t correction) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(slots == 0 || slots == ctx->c.slots, "bootstrap slots must equal the context's slot count", -1);
+    fhe::BootParams p;
+    p.budget_cts = budget_cts;
+    p.budget_stc = budget_stc;
+    p.correction = correction;
+    ctx->boot = std::make_unique<fhe::Bootstrapper>(k, p);
+  });
+}
+
+int fhe_bootstrap_keygen(fhe_ctx* ctx) {
+  return guarded([&] {
+    ckks(ctx);
+    fhe::require(ctx->boot != nullptr, "bootstrap keygen before bootstrap setup", -4);
+    ctx->boot->keygen();
+  });
+}
+
+int fhe_bootstrap(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out) {
+  return guarded([&] {
+    ckks(ctx);
+    fhe::require(ctx->boot != nullptr, "bootstrap before bootstrap setup", -4);
+    put_ct(out, ctx->boot->bootstrap(ct_of(a)));
+  });
+}
+
+int fhe_bootstrap_stage(fhe_ctx* ctx, int32_t stage, const fhe_ct* a, fhe_ct** out) {
+  return guarded([&] {
+    ckks(ctx);
+    fhe::require(ctx->boot != nullptr, "bootstrap before bootstrap setup", -4);
+    fhe::Bootstrapper& b = *ctx->boot;
+    switch (stage) {
+      case 0: put_ct(out, b.raise(ct_of(a))); break;
+      case 1: put_ct(out, b.coeff_to_slot(ct_of(a))); break;
+      case 2: put_ct(out, b.eval_mod_full(ct_of(a))); break;
+      case 3: put_ct(out, b.slot_to_coeff(ct_of(a))); break;
+      default: fhe::require(false, "bootstrap stage must be 0..3", -1);
+    }
+  });
+}
+
+int fhe_bootstrap_info(fhe_ctx* ctx, int32_t* correction, uint32_t* cheb_degree, uint32_t* n_rotation_keys) {
+  return guarded([&] {
+    ckks(ctx);
+    fhe::require(ctx->boot != nullptr, "no bootstrap setup", -4);
+    if (correction) *correction = ctx->boot->correction();
+    if (cheb_degree) *cheb_degree = (uint32_t)ctx->boot->eval_mod_coefficients().size() - 1;
+    if (n_rotation_keys) *n_rotation_keys = (uint32_t)ctx->boot->rotation_steps().size() + 1;
+  });
+}
+
+int fhe_bootstrap_levels(fhe_ctx* ctx, uint32_t* levels) {
+  return guarded([&] {
+    ckks(ctx);
+    fhe::require(ctx->boot != nullptr && levels != nullptr, "no bootstrap setup or null output", -4);
+    for (int i = 0; i < 4; ++i) levels[i] = ctx->boot->last_levels()[i];
+  });
+}
+
+int fhe_mod_raise(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).mod_raise(ct_of(a))); });
+}
+
+int fhe_mul_i(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out) {
+  return guarded([&] { put_ct(out, ckks(ctx).mul_i(ct_of(a))); });
+}
+
+int fhe_ct_set_scale(fhe_ctx* ctx, fhe_ct* ct, double scale) {
+  return guarded([&] {
+    ckks(ctx);
+    fhe::require(ct != nullptr && ct->p != nullptr && scale > 0, "null ciphertext or non-positive scale");
+    ct->p->scale = scale;
   });
 }
 

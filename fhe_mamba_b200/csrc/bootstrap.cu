@@ -1,0 +1,311 @@
+// CKKS bootstrapping (host orchestration; every step runs on the device
+// through the Ckks evaluator).
+#include "bootstrap.h"
+
+#include <algorithm>
+#include <cmath>
+#include <functional>
+
+namespace fhe {
+namespace {
+
+using cd = std::complex<double>;
+// Sparse matrix over n slots by diagonals: d -> v, (M x)[r] = sum_d v_d[r] x[(r + d) mod n].
+using Sparse = std::map<uint32_t, std::vector<cd>>;
+
+// exp(2 pi i k / m) with the angle reduced exactly first.
+cd unit_root(uint64_t k, uint64_t m) {
+  const double a = 2.0 * M_PI * (double)(k % m) / (double)m;
+  return {std::cos(a), std::sin(a)};
+}
+
+void put(Sparse& s, uint32_t n, int64_t d, uint32_t r, cd v) {
+  const uint32_t k = (uint32_t)(((d % (int64_t)n) + n) % n);
+  auto& row = s[k];
+  if (row.empty()) row.assign(n, cd(0, 0));
+  row[r] += v;
+}
+
+// One butterfly stage of the special FFT with half-distance h (block 2h):
+// forward  out[i+j] = u + xi_j v, out[i+j+h] = u - xi_j v;
+// inverse  out[i+j] = (u + v)/2,  out[i+j+h] = (u - v) conj(xi_j)/2,
+// xi_j = exp(2 pi i (5^j mod 8h) / 8h) (the slot order of the encoder).
+Sparse stage(uint32_t n, uint32_t h, bool inverse) {
+  Sparse s;
+  const uint64_t m = 8ull * h;
+  std::vector<cd> xi(h);
+  uint64_t p = 1;
+  for (uint32_t j = 0; j < h; ++j, p = p * 5 % m) xi[j] = unit_root(p, m);
+  for (uint32_t i = 0; i < n; i += 2 * h)
+    for (uint32_t j = 0; j < h; ++j) {
+      const uint32_t r = i + j, r2 = i + j + h;
+      if (!inverse) {
+        put(s, n, 0, r, 1.0);
+        put(s, n, h, r, xi[j]);
+        put(s, n, -(int64_t)h, r2, 1.0);
+        put(s, n, 0, r2, -xi[j]);
+      } else {
+        const cd c = std::conj(xi[j]) * 0.5;
+        put(s, n, 0, r, 0.5);
+        put(s, n, h, r, 0.5);
+        put(s, n, -(int64_t)h, r2, c);
+        put(s, n, 0, r2, -c);
+      }
+    }
+  return s;
+}
+
+// y = A (B x)
+Sparse compose(const Sparse& A, const Sparse& B, uint32_t n) {
+  Sparse C;
+  for (const auto& [d1, a] : A)
+    for (const auto& [d2, b] : B) {
+      auto& c = C[(uint32_t)(((uint64_t)d1 + d2) % n)];
+      if (c.empty()) c.assign(n, cd(0, 0));
+      for (uint32_t r = 0; r < n; ++r) c[r] += a[r] * b[(r + d1) % n];
+    }
+  return C;
+}
+
+uint32_t ceil_log2(uint64_t x) {
+  uint32_t k = 0;
+  while ((1ull << k) < x) ++k;
+  return k;
+}
+
+// Chebyshev interpolant of f on [-1, 1] at degree d (nodes cos(pi (k + 1/2) / (d + 1))):
+// p = c_0 + sum_j c_j T_j.  The cosine arguments are reduced exactly in integers.
+std::vector<double> cheb_fit(const std::function<double(double)>& f, int d) {
+  const int64_t m = 4 * (int64_t)(d + 1);  // angle pi j (2k+1) / (2(d+1)) = 2 pi [j (2k+1) mod m] / m
+  std::vector<double> fx(d + 1), c(d + 1);
+  for (int k = 0; k <= d; ++k) fx[k] = f(unit_root(2 * k + 1, m).real());
+  for (int j = 0; j <= d; ++j) {
+    long double s = 0;
+    for (int k = 0; k <= d; ++k) s += (long double)fx[k] * unit_root((uint64_t)j * (2 * k + 1), m).real();
+    c[j] = (double)(2.0L * s / (d + 1));
+  }
+  c[0] *= 0.5;
+  return c;
+}
+
+}  // namespace
+
+Bootstrapper::Bootstrapper(Ckks& ck, const BootParams& p) : ck_(ck), p_(p) {
+  Context& ctx = ck.ctx;
+  const uint32_t n = ctx.slots;
+  require(n == ctx.n / 2, "bootstrapping supports fully packed slots (N/2) only", -1);
+  const uint32_t logn = ceil_log2(n);
+  require(p_.budget_cts >= 1 && p_.budget_stc >= 1, "level budgets must be >= 1", -1);
+  p_.budget_cts = std::min(p_.budget_cts, logn);
+  p_.budget_stc = std::min(p_.budget_stc, logn);
+  require(p_.K >= 1 && p_.double_angles >= 0 && p_.double_angles <= 12, "bad EvalMod parameters", -1);
+  // Default pre-scaling: the sine approximation error shrinks by 4x per step
+  // while the amplified noise grows by 2x; 8 balances them for uniform
+  // ternary secrets at N = 2^16 with 59-bit scaling primes, 9 below.
+  corr_ = p_.correction > 0 ? p_.correction : (ctx.log_n >= 16 ? 8 : 9);
+  require(corr_ <= 40, "correction must be <= 40", -1);
+  require(ctx.L > p_.budget_cts + p_.budget_stc + 2, "the modulus chain is too short for bootstrapping", -1);
+
+  // CoeffToSlot: raised slots (q0 / S) U0 w  ->  BR(w) / (2K), where S is the
+  // FLEXIBLEAUTO scale of the level CoeffToSlot ends on (kept exactly through
+  // the transform by encoding each group at the scale of the prime it drops).
+  const double S = ck.level_scale(ctx.L - p_.budget_cts);
+  const double alpha = S / (2.0 * p_.K * (double)ctx.primes[0]);
+  std::vector<uint32_t> halves;
+  for (uint32_t h = n / 2; h >= 1; h /= 2) halves.push_back(h);
+  build_groups(cts_, halves, p_.budget_cts, true, std::pow(alpha, 1.0 / p_.budget_cts));
+  // SlotToCoeff: BR(w') -> U0 w' / (2 pi); the 2^correction factor is an exact
+  // integer multiplication afterwards.
+  std::reverse(halves.begin(), halves.end());
+  build_groups(stc_, halves, p_.budget_stc, false, std::pow(1.0 / (2.0 * M_PI), 1.0 / p_.budget_stc));
+
+  // EvalMod cosine: p(u) ~ cos(2 pi (K u - 1/4) / 2^r) on [-1, 1], truncated
+  // where every remaining coefficient is below 2^-48.
+  const double K = p_.K, R = std::ldexp(1.0, p_.double_angles);
+  auto f = [K, R](double u) { return std::cos(2.0 * M_PI * (K * u - 0.25) / R); };
+  std::vector<double> c = cheb_fit(f, 191);
+  int deg = (int)c.size() - 1;
+  while (deg > 1 && std::fabs(c[deg]) < 0x1p-48) --deg;
+  c.resize(deg + 1);
+  cheb_ = std::move(c);
+}
+
+void Bootstrapper::build_groups(std::vector<Group>& out, const std::vector<uint32_t>& halves, uint32_t budget,
+                                bool inverse, double factor) {
+  const uint32_t n = ck_.ctx.slots;
+  const uint32_t stages = (uint32_t)halves.size();
+  size_t pos = 0;
+  for (uint32_t gi = 0; gi < budget; ++gi) {
+    const uint32_t k = stages / budget + (gi < stages % budget ? 1 : 0);
+    Sparse M;
+    uint32_t hmin = n, hmax = 0;
+    for (uint32_t s = 0; s < k; ++s) {
+      const uint32_t h = halves[pos + s];
+      Sparse st = stage(n, h, inverse);
+      M = M.empty() ? std::move(st) : compose(st, M, n);
+      hmin = std::min(hmin, h);
+      hmax = std::max(hmax, h);
+    }
+    pos += k;
+    for (auto& [d, v] : M)
+      for (auto& x : v) x *= factor;
+    Group g;
+    g.stride = hmin;
+    const bool top = hmax == n / 2;
+    // diagonal index t (diagonal t*hmin): t in [0, 2^k) for the top group,
+    // [-T, T] with T = 2^k - 1 otherwise.
+    const int64_t count = top ? (int64_t)1 << k : ((int64_t)1 << (k + 1)) - 1;
+    const int64_t T = ((int64_t)1 << k) - 1;
+    g.b = 1u << ((ceil_log2((uint64_t)count) + 1) / 2);
+    // giant offset: a multiple of b, so one giant step is the identity
+    g.offset = top ? 0 : ((T + g.b - 1) / g.b) * g.b;
+    g.G = top ? (uint32_t)((count + g.b - 1) / g.b) : (uint32_t)((g.offset + T + g.b) / g.b);
+    g.diags.resize((size_t)g.b * g.G);
+    for (uint32_t gg = 0; gg < g.G; ++gg)
+      for (uint32_t j = 0; j < g.b; ++j) {
+        const int64_t t = (int64_t)gg * g.b + j - g.offset;
+        if (top ? (t < 0 || t >= count) : (t < -T || t > T)) continue;
+        const uint32_t d = (uint32_t)(((t * (int64_t)hmin) % (int64_t)n + n) % n);
+        auto it = M.find(d);
+        if (it == M.end()) continue;
+        const auto& v = it->second;
+        if (std::all_of(v.begin(), v.end(), [](const cd& x) { return x == cd(0, 0); })) continue;
+        // pre-rotate by the giant amount r: D'[i] = D[(i - r) mod n]
+        const int64_t r = ((((int64_t)gg * g.b - g.offset) * (int64_t)hmin) % (int64_t)n + n) % n;
+        std::vector<cd> rv(n);
+        for (uint32_t i = 0; i < n; ++i) rv[i] = v[(i + n - (uint32_t)r) % n];
+        g.diags[(size_t)gg * g.b + j] = std::move(rv);
+      }
+    out.push_back(std::move(g));
+  }
+}
+
+std::vector<int64_t> Bootstrapper::rotation_steps() const {
+  std::vector<int64_t> s;
+  const int64_t n = ck_.ctx.slots;
+  for (const auto* gs : {&cts_, &stc_})
+    for (const Group& g : *gs) {
+      for (uint32_t j = 1; j < g.b; ++j) s.push_back(((int64_t)j * g.stride) % n);
+      for (uint32_t gg = 0; gg < g.G; ++gg) {
+        const int64_t r = ((((int64_t)gg * g.b - g.offset) * g.stride) % n + n) % n;
+        if (r) s.push_back(r);
+      }
+    }
+  std::sort(s.begin(), s.end());
+  s.erase(std::unique(s.begin(), s.end()), s.end());
+  return s;
+}
+
+void Bootstrapper::keygen() {
+  require(ck_.has_keys(), "bootstrap keygen before keygen", -4);
+  for (int64_t st : rotation_steps()) {
+    const uint64_t g = ck_.galois_for_step(st);
+    if (!ck_.has_rotation_key(g)) ck_.rotation_keygen(g);
+  }
+  const uint64_t conj = 2ull * ck_.ctx.n - 1;
+  if (!ck_.has_rotation_key(conj)) ck_.rotation_keygen(conj);
+}
+
+std::unique_ptr<Ct> Bootstrapper::transform(std::vector<Group>& groups, std::unique_ptr<Ct> x) {
+  Context& ctx = ck_.ctx;
+  const uint32_t n = ctx.slots;
+  for (Group& g : groups) {
+    const uint32_t nq = x->nq;
+    require(nq >= 2, "bootstrapping ran out of levels", -4);
+    auto it = g.enc.find(nq);
+    if (it == g.enc.end()) {
+      std::vector<double> re, im;
+      std::vector<size_t> which;
+      for (size_t i = 0; i < g.diags.size(); ++i)
+        if (!g.diags[i].empty()) {
+          which.push_back(i);
+          for (const cd& v : g.diags[i]) {
+            re.push_back(v.real());
+            im.push_back(v.imag());
+          }
+        }
+      // each group is encoded at the scale of the prime its rescale drops, so
+      // the ciphertext's scale passes through the transform unchanged
+      auto pts = ck_.encode_batch(re.data(), im.data(), (uint32_t)which.size(), n, nq, (double)ctx.primes[nq - 1]);
+      std::vector<std::unique_ptr<Pt>> enc(g.diags.size());
+      for (size_t i = 0; i < which.size(); ++i) enc[which[i]] = std::move(pts[i]);
+      it = g.enc.emplace(nq, std::move(enc)).first;
+    }
+    std::vector<const Pt*> d(g.diags.size());
+    for (size_t i = 0; i < d.size(); ++i) d[i] = it->second[i].get();
+    auto y = ck_.linear_transform(*x, d, g.b, g.G, g.stride, g.offset);
+    ck_.rescale_inplace(*y);
+    x = std::move(y);
+  }
+  return x;
+}
+
+// sin(2 pi y) for y = K u: the Chebyshev cosine at (y - 1/4) / 2^r, then r double angles.
+std::unique_ptr<Ct> Bootstrapper::eval_mod(const Ct& u) {
+  auto c = ck_.chebyshev(u, cheb_, -1.0, 1.0);
+  for (int i = 0; i < p_.double_angles; ++i) {
+    auto sq = ck_.mul(*c, *c);
+    auto dbl = ck_.add(*sq, *sq, false);
+    c = ck_.add_scalar(*dbl, -1.0);
+  }
+  return c;
+}
+
+std::unique_ptr<Ct> Bootstrapper::raise(const Ct& a) {
+  Context& ctx = ck_.ctx;
+  require(a.ncomp == 2, "bootstrap expects a 2-component ciphertext", -1);
+  auto in = ck_.clone(a);
+  if (in->noise_deg > 1 && in->nq > 1) ck_.rescale_inplace(*in);
+  require(in->nq >= 2, "bootstrap input needs at least 2 limbs after its pending rescale", -4);
+  // Scale the message down to q0 2^-correction on one limb (adjust records
+  // exactly that scale), then raise.
+  auto low = ck_.adjust(*in, 1, std::ldexp((double)ctx.primes[0], -corr_));
+  in.reset();
+  auto raised = ck_.mod_raise(*low);
+  raised->scale = ck_.level_scale(ctx.L - p_.budget_cts);
+  levels_[0] = raised->nq;
+  return raised;
+}
+
+std::unique_ptr<Ct> Bootstrapper::coeff_to_slot(const Ct& raised) {
+  require(raised.nq == ck_.ctx.L, "coeff_to_slot expects a raised ciphertext", -1);
+  auto x = transform(cts_, ck_.clone(raised));
+  levels_[1] = x->nq;
+  return x;
+}
+
+std::unique_ptr<Ct> Bootstrapper::eval_mod_full(const Ct& x) {
+  // real / imaginary split: re = x + conj(x), im = -i (x - conj(x))
+  auto cj = ck_.rotate(x, 2ull * ck_.ctx.n - 1);
+  auto re = ck_.add(x, *cj, false);
+  auto diff = ck_.add(*cj, x, true);
+  auto im = ck_.mul_i(*diff);
+  cj.reset();
+  diff.reset();
+  auto mre = eval_mod(*re);
+  auto mim = eval_mod(*im);
+  re.reset();
+  im.reset();
+  auto imi = ck_.mul_i(*mim);
+  auto w = ck_.add(*mre, *imi, false);
+  if (w->noise_deg > 1) ck_.rescale_inplace(*w);
+  levels_[2] = w->nq;
+  return w;
+}
+
+std::unique_ptr<Ct> Bootstrapper::slot_to_coeff(const Ct& w) {
+  auto y = transform(stc_, ck_.clone(w));
+  levels_[3] = y->nq;
+  return ck_.mul_int(*y, (int64_t)1 << corr_);
+}
+
+std::unique_ptr<Ct> Bootstrapper::bootstrap(const Ct& a) {
+  auto raised = raise(a);
+  auto x = coeff_to_slot(*raised);
+  raised.reset();
+  auto w = eval_mod_full(*x);
+  x.reset();
+  return slot_to_coeff(*w);
+}
+
+}  // namespace fhe

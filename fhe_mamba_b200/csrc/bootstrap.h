@@ -1,0 +1,86 @@
+// CKKS bootstrapping for fully packed ciphertexts: ModRaise -> CoeffToSlot ->
+// EvalMod -> SlotToCoeff, the pipeline of OpenFHE's FHECKKSRNS that the
+// reference drives through EvalBootstrapSetup({4,4},{0,0},slots,0) /
+// EvalBootstrapKeyGen / EvalBootstrap (packed_fideslib.cpp:1084-1089, :245, :259).
+//
+// CoeffToSlot and SlotToCoeff are the special inverse / forward FFT of the
+// slot encoding without its bit reversal (EvalMod is slot-wise, so the two
+// reversals cancel), split into `budget` groups of consecutive butterfly
+// stages.  A group of k stages with smallest half-distance h is a matrix with
+// diagonals at multiples of h (2^{k+1}-1 of them, 2^k for the group holding
+// the top stage) and runs as one strided BSGS linear transform, one level.
+// EvalMod evaluates sin(2 pi y)/(2 pi) ~ y - round(y) as a Chebyshev
+// approximation of cos(2 pi (y - 1/4) / 2^r) followed by r double-angle steps.
+#pragma once
+#include <complex>
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <vector>
+
+#include "ckks.h"
+
+namespace fhe {
+
+struct BootParams {
+  uint32_t budget_cts = 4, budget_stc = 4;
+  // log2 of the extra down-scaling applied before ModRaise; 0 picks the default.
+  int correction = 0;
+  double K = 512.0;       // bound on |I| in the raised plaintext m + q0*I (uniform ternary secret)
+  int double_angles = 6;  // r
+};
+
+class Bootstrapper {
+ public:
+  Bootstrapper(Ckks& ck, const BootParams& p);
+
+  // Rotation steps (slot amounts) the transforms need; keygen() generates
+  // them and the conjugation key.
+  std::vector<int64_t> rotation_steps() const;
+  void keygen();
+
+  // Refreshes a ciphertext with >= 2 limbs whose slots are bounded by 1 in
+  // magnitude.  The output decrypts to the same slots with fresh levels.
+  std::unique_ptr<Ct> bootstrap(const Ct& a);
+
+  // The four steps of bootstrap(), each on its own (the pieces that
+  // EvalCoeffsToSlots / EvalSlotsToCoeffs expose in OpenFHE):
+  //   raise:          adjust to one limb at scale q0 2^-correction, ModRaise,
+  //                   scale attribute set to the level scale CoeffToSlot ends on;
+  //   coeff_to_slot:  BR(w) / (2K), w = (t_lo + i t_hi) / q0 of the raised plaintext t;
+  //   eval_mod:       BR(w mod 1) * 2 pi (real and imaginary parts separately);
+  //   slot_to_coeff:  the inverse of coeff_to_slot back to the input's slots.
+  std::unique_ptr<Ct> raise(const Ct& a);
+  std::unique_ptr<Ct> coeff_to_slot(const Ct& raised);
+  std::unique_ptr<Ct> eval_mod_full(const Ct& x);
+  std::unique_ptr<Ct> slot_to_coeff(const Ct& w);
+
+  const BootParams& params() const { return p_; }
+  int correction() const { return corr_; }
+  // Chebyshev coefficients of the EvalMod cosine.
+  const std::vector<double>& eval_mod_coefficients() const { return cheb_; }
+  // Limb counts seen by the last bootstrap: after ModRaise, CoeffToSlot,
+  // EvalMod and SlotToCoeff.
+  const uint32_t* last_levels() const { return levels_; }
+
+ private:
+  struct Group {
+    uint32_t b = 0, G = 0;
+    int64_t stride = 0, offset = 0;
+    std::vector<std::vector<std::complex<double>>> diags;       // [b*G], pre-rotated; empty = zero
+    std::map<uint32_t, std::vector<std::unique_ptr<Pt>>> enc;  // encodings by limb count
+  };
+  void build_groups(std::vector<Group>& out, const std::vector<uint32_t>& halves, uint32_t budget, bool inverse,
+                    double factor);
+  std::unique_ptr<Ct> transform(std::vector<Group>& groups, std::unique_ptr<Ct> x);
+  std::unique_ptr<Ct> eval_mod(const Ct& x);
+
+  Ckks& ck_;
+  BootParams p_;
+  int corr_ = 0;
+  std::vector<Group> cts_, stc_;
+  std::vector<double> cheb_;
+  uint32_t levels_[4] = {0, 0, 0, 0};
+};
+
+}  // namespace fhe

@@ -615,10 +615,11 @@ std::vector<std::unique_ptr<Ct>> Ckks::rotate_hoisted(const Ct& a, const std::ve
 }
 
 std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a, const std::vector<const Pt*>& diags, uint32_t b,
-                                           uint32_t G) {
+                                           uint32_t G, int64_t stride, int64_t giant_offset) {
   require(a.ncomp == 2, "linear transform expects a 2-component ciphertext", -1);
   require(b >= 1 && b <= 32 && G >= 1, "baby step must be in [1, 32], giant step >= 1", -1);
   require(diags.size() == (size_t)b * G, "need baby*giant diagonal entries", -1);
+  require(stride != 0, "stride must be non-zero", -1);
   const uint32_t nq = a.nq, n = ctx.n;
   double pscale = 0.0;
   for (const Pt* p : diags)
@@ -628,9 +629,9 @@ std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a, const std::vector<const 
       require(std::fabs(p->scale / pscale - 1.0) < 1e-12, "diagonals must share one scale", -1);
     }
   require(pscale != 0.0, "every diagonal is zero", -1);
-  // Babies: j = 0 is the input itself, 1..b-1 share one ModUp.
+  // Babies: j = 0 is the input itself, 1..b-1 (rotations by j*stride) share one ModUp.
   std::vector<uint64_t> gs;
-  for (uint32_t j = 1; j < b; ++j) gs.push_back(galois_for_step(j));
+  for (uint32_t j = 1; j < b; ++j) gs.push_back(galois_for_step((int64_t)j * stride));
   auto rot = rotate_hoisted(a, gs);
   auto base = clone(a);  // cap == nq, component stride nq*N like the rotations
   std::vector<const uint64_t*> tab{base->data()};
@@ -644,27 +645,68 @@ std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a, const std::vector<const 
   auto out = alloc(nq, 2);
   out->scale = a.scale * pscale;
   out->noise_deg = a.noise_deg + 1;
-  FHE_CUDA(cudaMemcpyAsync(out->data(), inner, 2 * cs * 8, cudaMemcpyDeviceToDevice, ctx.stream));
-  for (uint32_t g = 1; g < G; ++g) {
-    auto it = rot_.find(galois_for_step((int64_t)g * b));
-    require(it != rot_.end(), "missing rotation key for giant step " + std::to_string(g * b), -4);
+  const PrimeMap pm{nq, ctx.L};
+  for (uint32_t g = 0; g < G; ++g) {
     const uint64_t* ig = inner + (size_t)g * 2 * cs;
-    uint64_t* u = ws(4, 2 * cs);
-    keyswitch(ig + cs, nq, it->second.as<uint64_t>(), u, cs, ig);
-    uint64_t* r = ws(22, 2 * cs);
-    launch_automorphism(u, cs, r, cs, 2, nq, ctx.log_n, galois_for_step((int64_t)g * b), ctx.stream);
-    launch_ew(Ew::Add, out->data(), cs, r, cs, out->data(), cs, 2, nq, n, PrimeMap{nq, ctx.L},
-              ctx.d_mod.as<Modulus>(), ctx.stream);
+    const int64_t amount = ((int64_t)g * b - giant_offset) * stride;
+    const uint64_t gal = galois_for_step(amount);
+    const uint64_t* term = ig;
+    if (gal != 1) {  // rotation by a non-zero amount: key switch, then automorphism
+      auto it = rot_.find(gal);
+      require(it != rot_.end(), "missing rotation key for giant step " + std::to_string(amount), -4);
+      uint64_t* u = ws(4, 2 * cs);
+      keyswitch(ig + cs, nq, it->second.as<uint64_t>(), u, cs, ig);
+      uint64_t* r = ws(22, 2 * cs);
+      launch_automorphism(u, cs, r, cs, 2, nq, ctx.log_n, gal, ctx.stream);
+      term = r;
+    }
+    if (g == 0)
+      FHE_CUDA(cudaMemcpyAsync(out->data(), term, 2 * cs * 8, cudaMemcpyDeviceToDevice, ctx.stream));
+    else
+      launch_ew(Ew::Add, out->data(), cs, term, cs, out->data(), cs, 2, nq, n, pm, ctx.d_mod.as<Modulus>(),
+                ctx.stream);
   }
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::mod_raise(const Ct& a) {
+  require(a.ncomp == 2, "mod_raise expects a 2-component ciphertext", -1);
+  const uint32_t n = ctx.n, L = ctx.L;
+  const size_t cs = (size_t)a.cap * n;
+  // coefficients of limb 0 of both components
+  uint64_t* c0 = ws(6, 2 * (size_t)n);
+  FHE_CUDA(cudaMemcpy2DAsync(c0, (size_t)n * 8, a.data(), cs * 8, (size_t)n * 8, 2, cudaMemcpyDeviceToDevice,
+                             ctx.stream));
+  ntt_dense(c0, 2, 1, 1, 0, true);
+  auto out = alloc(L, 2);
+  launch_rescale_lift(c0, n, out->data(), (size_t)L * n, 2, L, n, ctx.primes[0], ctx.d_mod.as<Modulus>(),
+                      ctx.stream);
+  ntt_dense(out->data(), 2, L, L, 0, false);
+  out->scale = a.scale;
+  out->noise_deg = 1;
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::mul_i(const Ct& a) {
+  auto out = alloc(a.nq, a.ncomp);
+  launch_mul_monomial_half(a.data(), (size_t)a.cap * ctx.n, out->data(), (size_t)a.nq * ctx.n, a.ncomp, a.nq, ctx.n,
+                           ctx.d_tw.as<Twiddle>(), ctx.d_primes.as<uint64_t>(), ctx.stream);
+  out->scale = a.scale;
+  out->noise_deg = a.noise_deg;
   return out;
 }
 
 std::unique_ptr<Ct> Ckks::chebyshev(const Ct& x, const std::vector<double>& coeffs, double lo, double hi) {
   require(!coeffs.empty(), "no Chebyshev coefficients", -1);
   require(hi > lo, "empty Chebyshev interval", -1);
-  // u = x * 2/(hi-lo) - (lo+hi)/(hi-lo)
-  std::unique_ptr<Ct> u = mul_scalar(x, 2.0 / (hi - lo));
-  u = add_scalar(*u, -(lo + hi) / (hi - lo));
+  // u = x * 2/(hi-lo) - (lo+hi)/(hi-lo); no level is spent when [lo, hi] = [-1, 1].
+  std::unique_ptr<Ct> u;
+  if (lo == -1.0 && hi == 1.0) {
+    u = clone(x);
+  } else {
+    u = mul_scalar(x, 2.0 / (hi - lo));
+    u = add_scalar(*u, -(lo + hi) / (hi - lo));
+  }
   std::map<int, std::unique_ptr<Ct>> cache;
   int levels = 0;
   while ((1 << levels) < (int)coeffs.size()) ++levels;
@@ -838,6 +880,11 @@ std::unique_ptr<Ct> Ckks::add(const Ct& a, const Ct& b, bool subtract) {
     const Ct& bg = a_small ? b : a;
     const long double C = (long double)bg.scale / (long double)sm.scale;
     require(C >= 1.0L && C < 4.6e18L, "add: scale ratio out of range", -4);
+    // An integer multiple reconciles the scales only when the ratio is large
+    // (degree 1 + degree 2) or integral; anything else would silently add
+    // values at different scales.
+    require(C >= 0x1p30L || fabsl(C - roundl(C)) <= 1e-9L * C,
+            "add: operands on one level carry different scales that are not integer multiples", -4);
     auto m = mul_int(sm, (int64_t)roundl(C));
     m->scale = bg.scale;
     m->noise_deg = bg.noise_deg;
@@ -919,8 +966,12 @@ std::unique_ptr<Ct> Ckks::mul(const Ct& a, const Ct& b) {
   require(keyed_, "mul before keygen", -4);
   auto x = prepare_mult_input(a);
   auto y = prepare_mult_input(b);
-  if (x->nq > y->nq) level_reduce_inplace(*x, x->nq - y->nq);
-  if (y->nq > x->nq) level_reduce_inplace(*y, y->nq - x->nq);
+  // FLEXIBLEAUTO level alignment (AdjustLevelsAndDepth): the operand with more
+  // limbs is brought to the other's level AND scale, so that ciphertexts on one
+  // level keep one scale; dropping limbs alone would leave a nearby but
+  // different scale that later additions cannot reconcile exactly.
+  if (x->nq > y->nq) x = adjust(*x, y->nq, y->scale);
+  if (y->nq > x->nq) y = adjust(*y, x->nq, x->scale);
   auto d = tensor(*x, *y);
   auto out = relinearize(*d);
   FHE_CUDA(cudaStreamSynchronize(ctx.stream));

@@ -91,7 +91,16 @@ class Ckks {
   // LinearTransformInPlace): out = sum_g rot( sum_j diag[g*b+j] (.) rot(a, j), g*b ).
   // diags has b*G entries (null = zero diagonal), each encoded at >= a.nq limbs
   // with the same scale; babies share one ModUp.
-  std::unique_ptr<Ct> linear_transform(const Ct& a, const std::vector<const Pt*>& diags, uint32_t b, uint32_t G);
+  // General form: baby j rotates by j*stride, giant g by (g*b - giant_offset)*stride,
+  // so diagonal (g*b + j - giant_offset)*stride is pre-rotated by the giant amount.
+  std::unique_ptr<Ct> linear_transform(const Ct& a, const std::vector<const Pt*>& diags, uint32_t b, uint32_t G,
+                                       int64_t stride = 1, int64_t giant_offset = 0);
+
+  // ModRaise for bootstrapping: the centred coefficients of limb 0 lifted to
+  // every Q limb (the plaintext becomes m + q_0 I).
+  std::unique_ptr<Ct> mod_raise(const Ct& a);
+  // Exact multiplication of every slot by the imaginary unit (times X^{N/2}).
+  std::unique_ptr<Ct> mul_i(const Ct& a);
 
   // Paterson-Stockmeyer evaluation of sum_i c_i T_i(u), u = (2x - lo - hi) / (hi - lo),
   // following the reference's PackedEvaluator::chebyshev (packed_fideslib.cpp:533-599):

@@ -469,6 +469,17 @@ __global__ void __launch_bounds__(128) k_bsgs_dot(const uint64_t* const* babies,
   }
 }
 
+__global__ void k_mul_monomial_half(const uint64_t* a, size_t sa, uint64_t* out, size_t so, uint32_t n,
+                                    const Twiddle* tw, const uint64_t* primes) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y, c = blockIdx.z;
+  const uint64_t q = primes[l];
+  const Twiddle w = tw[(size_t)l * n + 1];  // psi^{N/2}, a primitive 4th root of unity
+  const uint64_t v = shoup_mul(a[c * sa + (size_t)l * n + k], w.w, w.wp, q);
+  out[c * so + (size_t)l * n + k] = k < n / 2 ? v : neg_mod(v, q);
+}
+
 inline dim3 grid1(uint32_t n, uint32_t y = 1, uint32_t z = 1) { return dim3((n + kTpb - 1) / kTpb, y, z); }
 
 uint32_t log2u(uint32_t x) {
@@ -610,6 +621,13 @@ void launch_lift_small_batch(const int64_t* src, uint64_t* out, uint32_t n, uint
                              const Modulus* mods, uint32_t batch, cudaStream_t s) {
   if (!batch || !nlimbs) return;
   k_lift_small_batch<<<grid1(n, nlimbs, batch), kTpb, 0, s>>>(src, out, n, nlimbs, pm, mods);
+}
+
+void launch_mul_monomial_half(const uint64_t* a, size_t sa, uint64_t* out, size_t so, uint32_t ncomp,
+                              uint32_t nlimbs, uint32_t n, const Twiddle* tw, const uint64_t* primes,
+                              cudaStream_t s) {
+  if (!nlimbs || !ncomp) return;
+  k_mul_monomial_half<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, out, so, n, tw, primes);
 }
 
 void launch_bsgs_dot(const uint64_t* const* babies, const uint64_t* const* diags, uint64_t* out, uint32_t b,

@@ -116,6 +116,13 @@ void launch_encode_round_batch(const double2* v, int64_t* coef, uint32_t slots, 
 void launch_lift_small_batch(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
                              const Modulus* mods, uint32_t batch, cudaStream_t s);
 
+// out = a * X^{N/2} in NTT form: the evaluation at psi^{2 brv(i) + 1} is scaled
+// by i_q = psi^{N/2} when brv(i) is even (i < N/2) and by -i_q otherwise.
+// tw = forward twiddle tables (entry 1 of prime l's table is psi_l^{N/2}).
+void launch_mul_monomial_half(const uint64_t* a, size_t sa, uint64_t* out, size_t so, uint32_t ncomp,
+                              uint32_t nlimbs, uint32_t n, const Twiddle* tw, const uint64_t* primes,
+                              cudaStream_t s);
+
 // ---- BSGS inner products ----
 // For every giant g < G and component c < 2:
 //   out[g][c][l] = sum_{j < b} baby_j[c][l] * diag_{g*b+j}[l]   (mod q_l),

@@ -216,12 +216,47 @@ int fhe_encode_batch(fhe_ctx* ctx, const double* re, const double* im, uint32_t 
 
 /* BSGS plaintext-ciphertext matrix-vector product (PackedEvaluator::linear,
  * packed_fideslib.cpp:447-532; LinearTransformInPlace of the reference's
- * FIDESlib patch): out = sum_g rot( sum_j diags[g*baby+j] (.) rot(a, j), g*baby ).
+ * FIDESlib patch):
+ *   out = sum_g rot( sum_j diags[g*baby+j] (.) rot(a, j*stride), (g*baby - giant_offset)*stride ).
  * Baby rotations share one ModUp; one fused kernel forms every giant's inner
  * sum; diags[i] may be NULL for an all-zero diagonal.  Needs rotation keys
- * for steps 1..baby-1 and g*baby. */
+ * for steps j*stride and the non-zero giant amounts (stride 1, offset 0 is
+ * the plain matvec). */
 int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* diags, uint32_t baby,
-                         uint32_t giant, fhe_ct** out);
+                         uint32_t giant, int32_t stride, int32_t giant_offset, fhe_ct** out);
+
+/* Bootstrapping of fully packed ciphertexts (slots = N/2), replacing OpenFHE's
+ * EvalBootstrapSetup({budget_cts, budget_stc}, {0, 0}, slots, correction) /
+ * EvalBootstrapKeyGen / EvalBootstrap as called at packed_fideslib.cpp:1084-1089,
+ * :245 and :259.  ModRaise -> CoeffToSlot (budget_cts levels) -> EvalMod
+ * (Chebyshev cosine + double angles) -> SlotToCoeff (budget_stc levels).
+ * correction <= 0 picks the default pre-scaling exponent.  The input needs at
+ * least 2 limbs and slots of magnitude <= 1. */
+int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, uint32_t slots,
+                        int32_t correction);
+int fhe_bootstrap_keygen(fhe_ctx* ctx);
+int fhe_bootstrap(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
+/* One step of fhe_bootstrap (EvalCoeffsToSlots / EvalSlotsToCoeffs and their
+ * neighbours in OpenFHE's FHECKKSRNS): stage 0 = scale down to one limb and
+ * ModRaise, 1 = CoeffToSlot, 2 = EvalMod (real and imaginary parts), 3 =
+ * SlotToCoeff.  Chaining 0..3 equals fhe_bootstrap. */
+int fhe_bootstrap_stage(fhe_ctx* ctx, int32_t stage, const fhe_ct* a, fhe_ct** out);
+/* Any pointer may be NULL. n_rotation_keys counts the conjugation key. */
+int fhe_bootstrap_info(fhe_ctx* ctx, int32_t* correction, uint32_t* cheb_degree, uint32_t* n_rotation_keys);
+/* Limb counts of the last bootstrap after ModRaise, CoeffToSlot, EvalMod and
+ * SlotToCoeff (levels[4]); the reference's trace_levels telemetry. */
+int fhe_bootstrap_levels(fhe_ctx* ctx, uint32_t* levels);
+
+/* Bootstrapping ModRaise (EvalBootstrap's first step): the centred
+ * coefficients of limb 0 lifted to every Q limb. */
+int fhe_mod_raise(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
+
+/* Multiplies every slot by the imaginary unit exactly (times X^{N/2}); used to
+ * split and merge real/imaginary parts in CoeffToSlot/SlotToCoeff. */
+int fhe_mul_i(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
+
+/* SetScalingFactor: reinterprets the ciphertext's scale without touching it. */
+int fhe_ct_set_scale(fhe_ctx* ctx, fhe_ct* ct, double scale);
 
 /* EvalChebyshevSeries: sum_{i<n} coeffs[i] T_i((2a - lo - hi)/(hi - lo)) by
  * Paterson-Stockmeyer with the reference's recursion

@@ -348,3 +348,38 @@ class Ckks:
         out = self.zeros(ncomp, nq - 1)
         self.L_.oc_rescale(self.h, _p64(np.ascontiguousarray(ct)), ncomp, nq, _p64(out))
         return out
+
+    # bootstrapping pieces
+    def mod_raise(self, ct):
+        """ModRaise of OpenFHE's FHECKKSRNS::EvalBootstrap (the raise step): limb 0
+        of each component in coefficient form, centred (NativePoly::SwitchModulus),
+        lifted to every Q prime, back to NTT form."""
+        ncomp = ct.shape[0]
+        q0 = np.int64(self.q[0])
+        out = self.zeros(ncomp, self.L)
+        for c in range(ncomp):
+            a = np.ascontiguousarray(ct[c, 0:1]).copy()
+            self.ntt(a, 1, 0, inverse=True)
+            v = a[0].astype(np.int64)
+            v = np.where(v > q0 // 2, v - q0, v)
+            for l in range(self.L):
+                out[c, l] = (v % np.int64(self.q[l])).astype(np.uint64)
+            comp = np.ascontiguousarray(out[c])
+            self.ntt(comp, self.L, 0, inverse=False)
+            out[c] = comp
+        return out
+
+    def mul_i(self, ct):
+        """ct * X^{N/2} in NTT form: evaluation point psi^{2 brv(k) + 1} gives the
+        factor psi^{N/2} for k < N/2 and -psi^{N/2} above."""
+        ncomp, nq = ct.shape[0], ct.shape[1]
+        out = np.empty_like(ct)
+        h = self.n // 2
+        for l in range(nq):
+            q = self.q[l]
+            iq = pow(self.psi(l), h, q)
+            for c in range(ncomp):
+                x = [int(v) for v in ct[c, l]]
+                out[c, l] = np.array([(v * iq) % q if k < h else (-(v * iq)) % q for k, v in enumerate(x)],
+                                     dtype=np.uint64)
+        return out

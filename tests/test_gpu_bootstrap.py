@@ -1,0 +1,177 @@
+"""Bootstrapping on the device.
+
+ModRaise and the exact multiplication by i are compared word for word with the
+oracle's restatement; the strided BSGS linear transform (the CoeffToSlot /
+SlotToCoeff shape: diagonals at multiples of a stride, giant steps offset so
+that negative diagonals are reached) is checked against the fp64 product; the
+full bootstrap (ModRaise -> CoeffToSlot -> EvalMod -> SlotToCoeff) is checked
+by decryption against its input.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+SEED = 4321
+
+
+@pytest.fixture(scope="module")
+def small(oracle):
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    log_n, depth, sb, fb, dnum = 12, 6, 45, 55, 2
+    cc = CryptoContext(CCParams(ring_dim=1 << log_n, multiplicative_depth=depth, scaling_mod_size=sb,
+                                first_mod_size=fb, num_large_digits=dnum))
+    oc = oracle.Ckks(log_n, cc.q, cc.p, dnum, cc.slots)
+    cc.KeyGen(SEED)
+    s, sn = oc.keygen_secret(SEED)
+    return cc, oc, s, sn
+
+
+def _rand_ct(oc, nq, seed, ncomp=2):
+    rng = np.random.default_rng(seed)
+    x = np.empty((ncomp, nq, oc.n), dtype=np.uint64)
+    for l in range(nq):
+        x[:, l, :] = rng.integers(0, oc.q[l], size=(ncomp, oc.n), dtype=np.uint64)
+    return x
+
+
+def test_mul_i_matches_oracle_and_decrypts(small):
+    cc, oc, s, sn = small
+    a = _rand_ct(oc, 3, 5)
+    assert np.array_equal(cc.MultByI(cc.upload(a)).residues(), oc.mul_i(a))
+    r = np.random.default_rng(6)
+    z = r.uniform(-1, 1, cc.slots) + 1j * r.uniform(-1, 1, cc.slots)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(z))
+    got = cc.Decrypt(cc.MultByI(ct)).GetCKKSPackedValue()
+    assert np.max(np.abs(got - 1j * z)) < 1e-6
+
+
+def test_mod_raise_matches_oracle(small):
+    cc, oc, s, sn = small
+    for nq in (1, 3):
+        a = _rand_ct(oc, nq, 7 + nq)
+        got = cc.ModRaise(cc.upload(a))
+        assert got.GetLevel() == 0 and got.residues().shape == (2, oc.L, oc.n)
+        assert np.array_equal(got.residues(), oc.mod_raise(a)), nq
+
+
+def test_mod_raise_keeps_message_mod_q0(small):
+    """Decrypting the raised ciphertext gives m + q0*I with small integer I."""
+    cc, oc, s, sn = small
+    r = np.random.default_rng(8)
+    z = r.uniform(-1, 1, cc.slots)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(z))
+    cc.LevelReduceInPlace(ct, cc.n_q - 1)
+    raised = cc.ModRaise(ct)
+    dec = oc.decrypt(sn, raised.residues())  # [L][N] NTT form
+    dec = oc.ntt(np.ascontiguousarray(dec).copy(), oc.L, 0, inverse=True)
+    q0, q1 = oc.q[0], oc.q[1]
+    # exact coefficients from the first two limbs (CRT): t = m + q0*I
+    inv = pow(q0, -1, q1)
+    t = [int(a) + q0 * (((int(b) - int(a)) * inv) % q1) for a, b in zip(dec[0], dec[1])]
+    t = [v - q0 * q1 if v > q0 * q1 // 2 else v for v in t]
+    I = np.array([round(v / q0) for v in t], dtype=np.float64)
+    assert np.max(np.abs(I)) <= oc.n  # |I| is bounded by the secret's weight
+    m = np.array([v - q0 * round(v / q0) for v in t], dtype=np.float64)
+    assert np.max(np.abs(m)) < q0 / 4
+
+
+def _strided_diags(W, b, G, stride, off, slots):
+    """Pre-rotated diagonal plaintext values for the strided BSGS schedule."""
+    out = []
+    k = np.arange(slots)
+    for g in range(G):
+        r = (g * b - off) * stride
+        for j in range(b):
+            t = g * b + j - off
+            d = W[k, (k + t * stride) % slots]
+            out.append(np.roll(d, r) if np.any(d) else None)
+    return out
+
+
+def test_strided_linear_transform(small):
+    cc, oc, s, sn = small
+    n = cc.slots
+    b, G, off, stride = 4, 4, 7, 8
+    rng = np.random.default_rng(9)
+    W = np.zeros((n, n), dtype=complex)
+    k = np.arange(n)
+    for t in range(-off, G * b - off):
+        if t == 5:
+            continue  # one all-zero diagonal
+        W[k, (k + t * stride) % n] = rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)
+    diags = _strided_diags(W, b, G, stride, off, n)
+    assert sum(d is None for d in diags) == 1
+    steps = sorted({j * stride for j in range(1, b)} | {(g * b - off) * stride for g in range(G)} - {0})
+    cc.EvalRotateKeyGen(steps)
+    x = rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    pts = [cc.MakeCKKSPackedPlaintext(d) if d is not None else None for d in diags]
+    out = cc.EvalLinearTransform(ct, pts, b, G, stride=stride, giant_offset=off)
+    got = cc.Decrypt(out).GetCKKSPackedValue()
+    assert np.max(np.abs(got - W @ x)) < 1e-4
+
+
+@pytest.fixture(scope="module")
+def boot_ctx():
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    cc = CryptoContext(CCParams(ring_dim=1 << 12, multiplicative_depth=25, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3))
+    cc.KeyGen(SEED)
+    cc.EvalBootstrapSetup((4, 4))
+    cc.EvalBootstrapKeyGen()
+    return cc
+
+
+@pytest.mark.parametrize("cplx", [False, True])
+def test_bootstrap_refreshes_levels(boot_ctx, cplx):
+    """A ciphertext with 2 limbs left comes back with fresh limbs and the same slots."""
+    cc = boot_ctx
+    r = np.random.default_rng(11 + cplx)
+    x = r.uniform(-1, 1, cc.slots)
+    if cplx:
+        x = x + 1j * r.uniform(-1, 1, cc.slots)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    cc.LevelReduceInPlace(ct, cc.n_q - 2)
+    out = cc.EvalBootstrap(ct)
+    lv = cc.bootstrap_levels()
+    # 4 CoeffToSlot levels, 7 Chebyshev + 6 double-angle levels, 4 SlotToCoeff levels
+    assert lv == [cc.n_q, cc.n_q - 4, cc.n_q - 17, cc.n_q - 21] and out.n_limbs() == cc.n_q - 21
+    y = cc.Decrypt(out).GetCKKSPackedValue()
+    if not cplx:
+        y = y.real
+    assert np.max(np.abs(y - x)) < 1e-4
+
+
+def test_bootstrap_stages_chain(boot_ctx):
+    """Stages 0..3 chained equal the one-call bootstrap's accuracy; a constant
+    vector (the worst case for the sine approximation) also comes back."""
+    cc = boot_ctx
+    x = np.full(cc.slots, 0.9)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    cc.LevelReduceInPlace(ct, cc.n_q - 2)
+    c = ct
+    for st in range(4):
+        c = cc.EvalBootstrapStage(st, c)
+    assert np.max(np.abs(cc.Decrypt(c).GetRealPackedValue() - x)) < 1e-4
+
+
+def test_bootstrap_rejects_one_limb(boot_ctx):
+    from fhe_mamba_b200 import StateError
+    cc = boot_ctx
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(np.zeros(4)))
+    cc.LevelReduceInPlace(ct, cc.n_q - 1)
+    with pytest.raises(StateError):
+        cc.EvalBootstrap(ct)
+
+
+def test_bootstrap_then_multiply(boot_ctx):
+    """The refreshed ciphertext supports further multiplications."""
+    cc = boot_ctx
+    x = np.random.default_rng(13).uniform(-1, 1, cc.slots)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    cc.LevelReduceInPlace(ct, cc.n_q - 3)
+    out = cc.EvalBootstrap(ct)
+    sq = cc.EvalMult(out, out)
+    y = cc.Decrypt(sq).GetRealPackedValue()
+    assert np.max(np.abs(y - x * x)) < 2e-4
