@@ -427,12 +427,12 @@ def main():
             "gpu_launches": 4 * args.steps,
             "clocks": clocks,
         }
-        if not args.no_ckks:
+        if not args.no_ckks and world == 1:
             ks, mv = measure_ckks(local)
             line["keyswitch"] = ks
             line["bsgs_matvec"] = mv
             line["bootstrap"] = measure_bootstrap(local)
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:
             v, dt, sample = cpu_baseline(host_threads())
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",
                                     "sample": sample + "; CPU oracle restating OpenFHE's NTT"}
