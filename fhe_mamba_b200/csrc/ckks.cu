@@ -614,9 +614,12 @@ std::vector<std::unique_ptr<Ct>> Ckks::rotate_hoisted(const Ct& a, const std::ve
   return outs;
 }
 
-std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a, const std::vector<const Pt*>& diags, uint32_t b,
+std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a_in, const std::vector<const Pt*>& diags, uint32_t b,
                                            uint32_t G, int64_t stride, int64_t giant_offset) {
-  require(a.ncomp == 2, "linear transform expects a 2-component ciphertext", -1);
+  require(a_in.ncomp == 2, "linear transform expects a 2-component ciphertext", -1);
+  std::unique_ptr<Ct> pre;
+  if (a_in.noise_deg >= 2) pre = prepare_mult_input(a_in);
+  const Ct& a = pre ? *pre : a_in;
   require(b >= 1 && b <= 32 && G >= 1, "baby step must be in [1, 32], giant step >= 1", -1);
   require(diags.size() == (size_t)b * G, "need baby*giant diagonal entries", -1);
   require(stride != 0, "stride must be non-zero", -1);
@@ -919,7 +922,11 @@ std::unique_ptr<Ct> Ckks::add_plain(const Ct& a, const Pt& p, bool subtract) {
   return out;
 }
 
-std::unique_ptr<Ct> Ckks::mul_plain(const Ct& a, const Pt& p) {
+std::unique_ptr<Ct> Ckks::mul_plain(const Ct& a_in, const Pt& p) {
+  // FLEXIBLEAUTO: a pending rescale happens before the product.
+  std::unique_ptr<Ct> pre;
+  if (a_in.noise_deg >= 2) pre = prepare_mult_input(a_in);
+  const Ct& a = pre ? *pre : a_in;
   require(p.nq >= a.nq, "mul_plain: plaintext has fewer limbs than the ciphertext", -1);
   const uint32_t n = ctx.n;
   auto out = alloc(a.nq, a.ncomp);

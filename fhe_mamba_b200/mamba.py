@@ -1,0 +1,280 @@
+"""Packed Mamba-2 decode pieces on CKKS ciphertexts: the recurrent-state
+update and readout, the causal-conv window and the gated RMSNorm.
+
+These follow the reference's native Mamba-2 decode
+(``native/fideslib_stage0/src/stage1_mamba2_decode_fideslib.cpp``):
+
+* state layout -- the (head, channel, state) tensor of one layer is split into
+  groups of ``group_heads`` whole heads; within a group, state coordinate
+  (h, p, k) sits at slot ``k * group_block + h_local * head_dim + p`` with
+  ``group_block = group_heads * head_dim`` (packing of ``update_state_group`` /
+  ``readout_state_group``, :3971-4057);
+* ``expand_x`` / ``place_heads`` / ``place_state_blocks`` / ``doubling_fill``
+  (:3271-3410, :1802) -- masks, rotations and the strided BSGS that move the
+  packed streams into that layout;
+* the update ``S <- decay * S + (dt * x) (x) B`` and the readout
+  ``y = sum_k S * C`` by a rotate-and-add over the state axis, a block mask and
+  a placement rotation;
+* the RMSNorm inverse square root as a Chebyshev seed refined by Newton steps
+  ``y <- 1.5 y - 0.5 V y^3`` (``newton_refine``, :2388-2400) on
+  ``V = sum(x^2) + width * eps``.
+
+The plaintext formulas they implement are ``mixer2_forward`` and
+``rms_normalize`` / ``ssm_update_readout`` (``src/fhemamba/reference.py:182-294``,
+``src/fhemamba/tensor_ops.py:53-118``).  Every operation runs on the device
+through the C ABI; this module only schedules them.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+
+
+def _log2(v: int) -> int:
+    if v <= 0 or v & (v - 1):
+        raise _lib.InvalidArgument(-1, "mamba", f"{v} is not a power of two")
+    return v.bit_length() - 1
+
+
+@dataclass(frozen=True)
+class StateLayout:
+    """Slot layout of one layer's recurrent state (heads x head_dim x state_size)."""
+
+    heads: int
+    head_dim: int
+    state_size: int
+    slots: int
+
+    def __post_init__(self):
+        for v in (self.heads, self.head_dim, self.state_size, self.slots):
+            _log2(v)
+        if self.head_dim * self.state_size > self.slots:
+            raise _lib.InvalidArgument(-1, "StateLayout", "one head's state does not fit the slots")
+
+    @property
+    def group_heads(self) -> int:
+        return min(self.heads, self.slots // (self.head_dim * self.state_size))
+
+    @property
+    def group_block(self) -> int:
+        return self.group_heads * self.head_dim
+
+    @property
+    def groups(self) -> int:
+        return self.heads // self.group_heads
+
+    def slot(self, h: int, p: int, k: int):
+        g, hl = divmod(h, self.group_heads)
+        return g, k * self.group_block + hl * self.head_dim + p
+
+    def pack(self, state: np.ndarray) -> np.ndarray:
+        """[heads, head_dim, state_size] -> [groups, slots] slot vectors."""
+        s = np.asarray(state).reshape(self.groups, self.group_heads, self.head_dim, self.state_size)
+        out = np.zeros((self.groups, self.slots), dtype=s.dtype)
+        blk = s.transpose(0, 3, 1, 2).reshape(self.groups, self.state_size * self.group_block)
+        out[:, :blk.shape[1]] = blk
+        return out
+
+    def unpack(self, vecs: np.ndarray) -> np.ndarray:
+        v = np.asarray(vecs)[:, :self.state_size * self.group_block]
+        v = v.reshape(self.groups, self.state_size, self.group_heads, self.head_dim).transpose(0, 2, 3, 1)
+        return v.reshape(self.heads, self.head_dim, self.state_size)
+
+
+class PackedMamba2:
+    """Encrypted Mamba-2 state update / readout / conv / RMSNorm over one CryptoContext.
+
+    Streams: ``xbc`` holds x (d_inner = heads * head_dim values) at [0, d_inner),
+    B at [b_base, b_base + state_size) and C at [c_base, c_base + state_size);
+    per-head vectors (dt, decay) sit at [head_base, head_base + heads).  Every
+    stream is zero outside its values.
+    """
+
+    def __init__(self, cc, layout: StateLayout, b_base: int, c_base: int, head_base: int = 0):
+        if cc.slots != layout.slots:
+            raise _lib.InvalidArgument(-1, "PackedMamba2", "layout slots differ from the context")
+        self.cc, self.L = cc, layout
+        self.b_base, self.c_base, self.head_base = b_base, c_base, head_base
+        L = layout
+        self._state_baby = L.group_heads if L.state_size >= L.group_heads else L.state_size
+        self._state_giant = L.state_size // self._state_baby
+        self._mask_cache = {}
+        self._state_diags = None
+
+    # ---- keys -------------------------------------------------------------
+    def rotation_steps(self, norm_width: int = 0) -> list[int]:
+        L = self.L
+        gb, n = L.group_block, L.slots
+        s = set()
+        s |= {-(gb << i) for i in range(_log2(L.state_size))}         # fill over the state axis
+        s |= {gb << i for i in range(_log2(L.state_size))}            # readout rotate-sum
+        s |= {-(1 << i) for i in range(_log2(L.head_dim))}            # fill over a head
+        s |= {-(1 << i) for i in range(_log2(gb))}                    # fill over a state block
+        s |= {g * gb for g in range(1, L.groups)} | {-g * gb for g in range(1, L.groups)}
+        s |= {self.head_base + L.group_heads * g for g in range(L.groups)}
+        s |= {-(L.head_dim - 1) * hl for hl in range(1, L.group_heads)}
+        s |= {self.b_base, self.c_base}
+        stride = -(gb - 1)
+        b, G = self._state_baby, self._state_giant
+        s |= {j * stride for j in range(1, b)} | {g * b * stride for g in range(1, G)}
+        if norm_width:
+            s |= {1 << i for i in range(_log2(norm_width))} | {-norm_width}
+        return sorted(v % n for v in s if v % n)
+
+    # ---- plaintext helpers ------------------------------------------------
+    def _block_mask(self, lo: int, hi: int):
+        key = (lo, hi)
+        if key not in self._mask_cache:
+            m = np.zeros(self.L.slots)
+            m[lo:hi] = 1.0
+            self._mask_cache[key] = m
+        return self._mask_cache[key]
+
+    def _plain_for(self, ct, values):
+        """Plaintext at the level `ct` multiplies on (after its pending rescale)."""
+        c = self.cc
+        nq = ct.n_limbs() - (1 if ct.GetNoiseScaleDeg() >= 2 else 0)
+        return c.MakeCKKSPackedPlaintext(np.asarray(values, dtype=float), level=c.n_q - nq)
+
+    def _mul_mask(self, ct, mask):
+        return self.cc.EvalMult(ct, self._plain_for(ct, mask))
+
+    def _fill(self, ct, stride: int, count: int):
+        """doubling_fill: copies [0, stride) to count consecutive blocks (needs zeros beyond)."""
+        c = self.cc
+        for i in range(_log2(count)):
+            ct = c.EvalAdd(ct, c.EvalRotate(ct, -(stride << i)))
+        return ct
+
+    # ---- expansions into the state layout ---------------------------------
+    def expand_x(self, xbc, group: int):
+        """x of the group's heads, replicated over the state axis."""
+        gb = self.L.group_block
+        m = self._mul_mask(xbc, self._block_mask(group * gb, (group + 1) * gb))
+        if group:
+            m = self.cc.EvalRotate(m, group * gb)
+        return self._fill(m, gb, self.L.state_size)
+
+    def expand_heads(self, v, group: int):
+        """Per-head values (dt, decay) of the group, repeated over channels and states."""
+        c, L = self.cc, self.L
+        gh, hd = L.group_heads, L.head_dim
+        shifted = c.EvalRotate(v, self.head_base + gh * group) if self.head_base + gh * group else v
+        steps = [-(hd - 1) * hl for hl in range(1, gh)]
+        rots = [shifted] + (c.EvalFastRotation(shifted, steps) if steps else [])
+        acc = None
+        for hl, r in enumerate(rots):
+            term = self._mul_mask(r, self._block_mask(hl * hd, hl * hd + 1))
+            acc = term if acc is None else c.EvalAdd(acc, term)
+        acc = self._fill(acc, 1, hd)
+        return self._fill(acc, L.group_block, L.state_size)
+
+    def _state_block_diagonals(self, nq: int):
+        """Unit diagonals of place_state_blocks: element k of the source lands at slot k * group_block."""
+        if self._state_diags is None or self._state_diags[0] != nq:
+            L = self.L
+            gb, n = L.group_block, L.slots
+            stride = -(gb - 1)
+            b, G = self._state_baby, self._state_giant
+            vals = []
+            for g in range(G):
+                for j in range(b):
+                    t = g * b + j
+                    d = np.zeros(n)
+                    d[t * gb] = 1.0
+                    vals.append(np.roll(d, (g * b * stride) % n))
+            pts = self.cc.MakeCKKSPackedPlaintexts(np.array(vals), level=self.cc.n_q - nq)
+            self._state_diags = (nq, pts)
+        return self._state_diags[1]
+
+    def expand_states(self, xbc, base: int):
+        """B or C (state_size values at `base` of the stream), each value filling one state block."""
+        c, L = self.cc, self.L
+        src = c.EvalRotate(xbc, base)
+        src = self._mul_mask(src, self._block_mask(0, L.state_size))
+        pts = self._state_block_diagonals(src.n_limbs() - (1 if src.GetNoiseScaleDeg() >= 2 else 0))
+        placed = c.EvalLinearTransform(src, pts, self._state_baby, self._state_giant, stride=-(L.group_block - 1))
+        return self._fill(placed, 1, L.group_block)
+
+    # ---- recurrence ---------------------------------------------------------
+    def update(self, state, decay, x_exp, dt_exp, b_exp):
+        """S <- decay * S + (dt * x) * B on one group (state None: first token)."""
+        c = self.cc
+        upd = c.EvalMult(c.EvalMult(x_exp, dt_exp), b_exp)
+        if state is None:
+            return upd
+        return c.EvalAdd(c.EvalMult(decay, state), upd)
+
+    def readout(self, state, c_exp, group: int):
+        """y[h, p] = sum_k S[h, p, k] C[k] for the group's heads, placed at the group's x block."""
+        c, L = self.cc, self.L
+        gb = L.group_block
+        prod = c.EvalMult(state, c_exp)
+        for i in range(_log2(L.state_size)):
+            prod = c.EvalAdd(prod, c.EvalRotate(prod, gb << i))
+        out = self._mul_mask(prod, self._block_mask(0, gb))
+        return c.EvalRotate(out, -gb * group) if group else out
+
+    def step(self, states, xbc, dt, decay):
+        """One token of the SSM: updates every group's state, returns (states, y stream)."""
+        c = self.cc
+        b_exp = self.expand_states(xbc, self.b_base)
+        c_exp = self.expand_states(xbc, self.c_base)
+        new_states, y = [], None
+        for g in range(self.L.groups):
+            x_g = self.expand_x(xbc, g)
+            dt_g = self.expand_heads(dt, g)
+            dec_g = self.expand_heads(decay, g) if states is not None else None
+            s = self.update(states[g] if states is not None else None, dec_g, x_g, dt_g, b_exp)
+            new_states.append(s)
+            r = self.readout(s, c_exp, g)
+            y = r if y is None else c.EvalAdd(y, r)
+        return new_states, y
+
+    # ---- causal conv ----------------------------------------------------------
+    def conv(self, window, weights, bias=None):
+        """Depthwise causal conv over a FIFO of stream ciphertexts (oldest first):
+        out = sum_i weights[i] (.) window[i] + bias, weights[i] a slot vector per tap."""
+        c = self.cc
+        if len(window) != len(weights):
+            raise _lib.InvalidArgument(-1, "conv", "one weight vector per window entry")
+        acc = None
+        for ct, w in zip(window, weights):
+            if ct is None:
+                continue
+            t = c.EvalMult(ct, self._plain_for(ct, w))
+            acc = t if acc is None else c.EvalAdd(acc, t)
+        if bias is not None:
+            if acc.GetNoiseScaleDeg() >= 2:
+                c.RescaleInPlace(acc)
+            acc = c.EvalAdd(acc, c.MakeCKKSPackedPlaintext(np.asarray(bias, dtype=float), level=c.n_q - acc.n_limbs(),
+                                                           scale=acc.GetScalingFactor()))
+        return acc
+
+    # ---- RMSNorm ----------------------------------------------------------
+    def rms_norm(self, x, width: int, weight, eps: float, domain, degree: int = 31, newton: int = 2):
+        """x * rsqrt(mean(x^2) + eps) * weight for x at [0, width) (zeros elsewhere).
+
+        V = sum(x^2) + width * eps by a copy and a rotate-and-add window sum;
+        rsqrt(V) from a Chebyshev seed on `domain` (bounds of V) and Newton
+        steps; the result is multiplied by sqrt(width) * weight."""
+        c = self.cc
+        sq = c.EvalMult(x, x)
+        sq = c.EvalAdd(sq, c.EvalRotate(sq, -width))
+        for i in range(_log2(width)):
+            sq = c.EvalAdd(sq, c.EvalRotate(sq, 1 << i))
+        v = c.EvalAdd(sq, width * eps)
+        lo, hi = domain
+        y = c.EvalChebyshevFunction(lambda t: 1.0 / np.sqrt(t), v, lo, hi, degree)
+        v_neg_half = c.EvalMult(v, -0.5)
+        for _ in range(newton):
+            y2 = c.EvalMult(y, y)
+            vy = c.EvalMult(v_neg_half, y)
+            y = c.EvalAdd(c.EvalMult(y, 1.5), c.EvalMult(vy, y2))
+        w = np.zeros(self.L.slots)
+        w[:width] = np.asarray(weight, dtype=float) * np.sqrt(width)
+        xy = c.EvalMult(x, y)
+        return c.EvalMult(xy, self._plain_for(xy, w))
