@@ -119,7 +119,7 @@ SIGNATURES = {
     "fhe_rescale_noalloc": [vp, vp, u32, u32, vp],
     "fhe_encode_batch": [vp, PD, PD, u32, u32, u32, f64, ctypes.POINTER(vp)],
     "fhe_linear_transform": [vp, vp, ctypes.POINTER(vp), u32, u32, i32, i32, ctypes.POINTER(vp)],
-    "fhe_bootstrap_setup": [vp, u32, u32, u32, i32],
+    "fhe_bootstrap_setup": [vp, u32, u32, u32, i32, i32],
     "fhe_bootstrap_keygen": [vp],
     "fhe_bootstrap": [vp, vp, ctypes.POINTER(vp)],
     "fhe_bootstrap_stage": [vp, i32, vp, ctypes.POINTER(vp)],

@@ -237,11 +237,57 @@ class CryptoContext:
         arr = (vp * len(diagonals))(*[d.handle if d is not None else None for d in diagonals])
         return self._ct("fhe_linear_transform", ct.handle, arr, baby, giant, int(stride), int(giant_offset))
 
-    def EvalBootstrapSetup(self, level_budget=(4, 4), dim1=(0, 0), slots: int = 0, correction_factor: int = 0):
-        """OpenFHE EvalBootstrapSetup(levelBudget, dim1, slots, correctionFactor); dim1 is
-        accepted for signature compatibility (the BSGS split is chosen per group)."""
+    def EvalBootstrapSetup(self, level_budget=(4, 4), dim1=(0, 0), slots: int = 0, correction_factor: int = 0,
+                           slots_to_coeffs_first: bool = False):
+        """OpenFHE EvalBootstrapSetup(levelBudget, dim1, slots, correctionFactor[, slotsToCoeffsFirst]);
+        dim1 is accepted for signature compatibility (the BSGS split is chosen per group)."""
         call("fhe_bootstrap_setup", self.h, int(level_budget[0]), int(level_budget[1]), int(slots),
-             int(correction_factor))
+             int(correction_factor), int(bool(slots_to_coeffs_first)))
+
+    def bootstrap_components(self, ct, passes: int = 2, merge: bool = False):
+        """The reference's two-pass refresh (PackedEvaluator::bootstrap_components,
+        packed_fideslib.cpp:235-270): first = bootstrap(x); the residual
+        (x - first) * 4096 is bootstrapped again as `second`.  With merge, the
+        pair becomes 4096 * first + second by an exact integer multiple
+        (merge_refresh_correction) and divisor = 4096.
+        Returns (first, second or None, divisor); x ~ (first + second / 4096) / divisor-corrected."""
+        x = ct.Clone()
+        while x.GetNoiseScaleDeg() > 1:
+            self.RescaleInPlace(x)
+        first = self.EvalBootstrap(x)
+        if passes == 1:
+            return first, None, 1.0
+        a, b = x.Clone(), first.Clone()
+        while b.GetNoiseScaleDeg() > 1:
+            self.RescaleInPlace(b)
+        target = max(a.GetLevel(), b.GetLevel())
+        for name in ("a", "b"):
+            v = a if name == "a" else b
+            while v.GetLevel() < target:
+                v = self.EvalMult(v, 1.0)
+                while v.GetNoiseScaleDeg() > 1:
+                    self.RescaleInPlace(v)
+            if name == "a":
+                a = v
+            else:
+                b = v
+        residual = self.EvalMult(self.EvalSub(a, b), 4096.0)
+        while residual.GetNoiseScaleDeg() > 1:
+            self.RescaleInPlace(residual)
+        second = self.EvalBootstrap(residual)
+        if merge and first.GetLevel() == second.GetLevel() and \
+                first.GetNoiseScaleDeg() == second.GetNoiseScaleDeg():
+            return self.EvalAdd(self.MultByInteger(first, 4096), second), None, 4096.0
+        return first, second, 1.0
+
+    def refresh(self, ct, bound: float = 1.0, passes: int = 2, merge: bool = False):
+        """PackedEvaluator::refresh (packed_fideslib.cpp:271-281): bootstrap x / bound
+        (one or two passes) and scale back by bound."""
+        scaled = self.EvalMult(ct, 1.0 / bound)
+        first, second, divisor = self.bootstrap_components(scaled, passes, merge)
+        if second is None:
+            return self.EvalMult(first, bound / divisor)
+        return self.EvalMult(self.EvalAdd(first, self.EvalMult(second, 1.0 / 4096.0)), bound)
 
     def EvalBootstrapKeyGen(self, secret_key=None, slots: int = 0):
         call("fhe_bootstrap_keygen", self.h)

@@ -550,7 +550,7 @@ int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* dia
 }
 
 int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, uint32_t slots,
-                        int32_t correction) {
+                        int32_t correction, int32_t s2c_first) {
   return guarded([&] {
     fhe::Ckks& k = ckks(ctx);
     fhe::require(slots == 0 || slots == ctx->c.slots, "bootstrap slots must equal the context's slot count", -1);
@@ -558,6 +558,7 @@ int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, 
     p.budget_cts = budget_cts;
     p.budget_stc = budget_stc;
     p.correction = correction;
+    p.s2c_first = s2c_first != 0;
     ctx->boot = std::make_unique<fhe::Bootstrapper>(k, p);
   });
 }

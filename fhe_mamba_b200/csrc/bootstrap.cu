@@ -300,6 +300,23 @@ std::unique_ptr<Ct> Bootstrapper::slot_to_coeff(const Ct& w) {
 }
 
 std::unique_ptr<Ct> Bootstrapper::bootstrap(const Ct& a) {
+  if (p_.s2c_first) {
+    // SlotToCoeff first: the slots z become the plaintext's coefficients
+    // (BR(z) / (2 pi) as lo + i hi); after ModRaise and CoeffToSlot the slots
+    // hold z 2^-c / (2 pi) + BR(I) in their original order, and EvalMod leaves
+    // z 2^-c.
+    auto in = ck_.clone(a);
+    if (in->noise_deg > 1 && in->nq > 1) ck_.rescale_inplace(*in);
+    require(in->nq >= p_.budget_stc + 2, "S2C-first bootstrap input needs budget_stc + 2 limbs", -4);
+    auto coeffs = transform(stc_, std::move(in));
+    levels_[3] = coeffs->nq;
+    auto raised = raise(*coeffs);
+    coeffs.reset();
+    auto x = coeff_to_slot(*raised);
+    raised.reset();
+    auto w = eval_mod_full(*x);
+    return ck_.mul_int(*w, (int64_t)1 << corr_);
+  }
   auto raised = raise(a);
   auto x = coeff_to_slot(*raised);
   raised.reset();

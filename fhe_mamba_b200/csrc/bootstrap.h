@@ -28,6 +28,9 @@ struct BootParams {
   int correction = 0;
   double K = 512.0;       // bound on |I| in the raised plaintext m + q0*I (uniform ternary secret)
   int double_angles = 6;  // r
+  // SlotToCoeff before ModRaise (the reference's S2C-first patch): the input's
+  // own levels pay for SlotToCoeff, so the output keeps budget_stc more limbs.
+  bool s2c_first = false;
 };
 
 class Bootstrapper {
@@ -39,8 +42,9 @@ class Bootstrapper {
   std::vector<int64_t> rotation_steps() const;
   void keygen();
 
-  // Refreshes a ciphertext with >= 2 limbs whose slots are bounded by 1 in
-  // magnitude.  The output decrypts to the same slots with fresh levels.
+  // Refreshes a ciphertext with >= 2 limbs (>= budget_stc + 2 with
+  // s2c_first) whose slots are bounded by 1 in magnitude.  The output
+  // decrypts to the same slots with fresh levels.
   std::unique_ptr<Ct> bootstrap(const Ct& a);
 
   // The four steps of bootstrap(), each on its own (the pieces that

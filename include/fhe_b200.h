@@ -231,9 +231,12 @@ int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* dia
  * :245 and :259.  ModRaise -> CoeffToSlot (budget_cts levels) -> EvalMod
  * (Chebyshev cosine + double angles) -> SlotToCoeff (budget_stc levels).
  * correction <= 0 picks the default pre-scaling exponent.  The input needs at
- * least 2 limbs and slots of magnitude <= 1. */
+ * least 2 limbs and slots of magnitude <= 1.  s2c_first != 0 selects the
+ * reference's S2C-first variant (patches/fideslib-v2.1.0-s2c-first-bootstrap.patch:27-60):
+ * SlotToCoeff runs on the input's own levels before ModRaise (input needs
+ * budget_stc + 2 limbs) and the output keeps budget_stc more limbs. */
 int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, uint32_t slots,
-                        int32_t correction);
+                        int32_t correction, int32_t s2c_first);
 int fhe_bootstrap_keygen(fhe_ctx* ctx);
 int fhe_bootstrap(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
 /* One step of fhe_bootstrap (EvalCoeffsToSlots / EvalSlotsToCoeffs and their

@@ -175,3 +175,52 @@ def test_bootstrap_then_multiply(boot_ctx):
     sq = cc.EvalMult(out, out)
     y = cc.Decrypt(sq).GetRealPackedValue()
     assert np.max(np.abs(y - x * x)) < 2e-4
+
+
+def test_two_pass_refresh_gains_precision(boot_ctx):
+    """bootstrap_components with two passes (residual * 4096 bootstrapped again)
+    beats one pass by orders of magnitude; merge gives the same value."""
+    cc = boot_ctx
+    x = np.random.default_rng(17).uniform(-1, 1, cc.slots)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    cc.LevelReduceInPlace(ct, cc.n_q - 4)  # the scaling and the residual each take a level
+    one = cc.Decrypt(cc.refresh(ct, 1.0, passes=1)).GetRealPackedValue()
+    two = cc.Decrypt(cc.refresh(ct, 1.0, passes=2)).GetRealPackedValue()
+    e1, e2 = np.max(np.abs(one - x)), np.max(np.abs(two - x))
+    assert e2 < 1e-6 and e2 < e1 / 30
+    first, second, div = cc.bootstrap_components(ct, passes=2, merge=True)
+    assert second is None and div == 4096.0
+    merged = cc.Decrypt(first).GetRealPackedValue() / 4096.0
+    assert np.max(np.abs(merged - x)) < 1e-6
+
+
+def test_refresh_with_bound(boot_ctx):
+    cc = boot_ctx
+    x = np.random.default_rng(19).uniform(-6, 6, cc.slots)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    cc.LevelReduceInPlace(ct, cc.n_q - 4)
+    y = cc.Decrypt(cc.refresh(ct, 8.0, passes=2)).GetRealPackedValue()
+    assert np.max(np.abs(y - x)) < 1e-5
+
+
+def test_s2c_first_bootstrap():
+    """SlotToCoeff before ModRaise: same values, budget_stc (4) more limbs left."""
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    cc = CryptoContext(CCParams(ring_dim=1 << 12, multiplicative_depth=25, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3))
+    cc.KeyGen(SEED)
+    cc.EvalBootstrapSetup((4, 4), slots_to_coeffs_first=True)
+    cc.EvalBootstrapKeyGen()
+    r = np.random.default_rng(23)
+    x = r.uniform(-1, 1, cc.slots) + 1j * r.uniform(-1, 1, cc.slots)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    cc.LevelReduceInPlace(ct, cc.n_q - 6)
+    out = cc.EvalBootstrap(ct)
+    assert out.n_limbs() == cc.n_q - 17
+    y = cc.Decrypt(out).GetCKKSPackedValue()
+    assert np.max(np.abs(y - x)) < 1e-4
+    short = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x.real))
+    cc.LevelReduceInPlace(short, cc.n_q - 5)
+    from fhe_mamba_b200 import StateError
+    with pytest.raises(StateError):
+        cc.EvalBootstrap(short)
