@@ -23,6 +23,20 @@ inline uint64_t stream_key(uint64_t kind, uint64_t id, uint64_t digit) {
 
 Shoup mk_shoup(uint64_t w, uint64_t q) { return Shoup{w, nt::shoup(w, q)}; }
 
+LimbShoup limb_shoup(const std::vector<uint64_t>& r, const std::vector<uint64_t>& primes) {
+  require(r.size() <= kMaxConstLimbs, "too many limbs for a constant product", -1);
+  LimbShoup c{};
+  for (size_t i = 0; i < r.size(); ++i) c.v[i] = mk_shoup(r[i], primes[i]);
+  return c;
+}
+
+LimbWords limb_words(const std::vector<uint64_t>& r) {
+  require(r.size() <= kMaxConstLimbs, "too many limbs for a constant sum", -1);
+  LimbWords c{};
+  for (size_t i = 0; i < r.size(); ++i) c.v[i] = r[i];
+  return c;
+}
+
 template <class T>
 DevMem upload(const std::vector<T>& v) {
   DevMem m(std::max<size_t>(v.size() * sizeof(T), 16));
@@ -735,18 +749,54 @@ std::unique_ptr<Ct> Ckks::chebyshev(const Ct& x, const std::vector<double>& coef
     cache[i] = std::move(out);
     return ref;
   };
+  // Leaf polynomials (degree < baby) are weighted sums of T_1..T_{baby-1}; the
+  // basis is brought once to the level and scale of its deepest member and
+  // each leaf is then one fused pass (linear_wsum) instead of a scalar product,
+  // an addition and a level alignment per term.
+  std::vector<std::unique_ptr<Ct>> aligned;
+  auto aligned_basis = [&](int i) -> const Ct& {
+    if (aligned.empty()) {
+      const int top = std::min<int>(baby - 1, (int)coeffs.size() - 1);
+      uint32_t nq_min = ~0u;
+      double sc = 0.0;
+      std::vector<std::unique_ptr<Ct>> ready_basis(top + 1);
+      for (int j = 1; j <= top; ++j) {
+        const Ct& b = basis(j);
+        ready_basis[j] = b.noise_deg >= 2 ? rescaled(b) : clone(b);
+        if (ready_basis[j]->nq < nq_min) {
+          nq_min = ready_basis[j]->nq;
+          sc = ready_basis[j]->scale;
+        }
+      }
+      aligned.resize(top + 1);
+      for (int j = 1; j <= top; ++j) {
+        Ct& b = *ready_basis[j];
+        if (b.nq == nq_min) {
+          require(std::fabs(b.scale / sc - 1.0) < 1e-9, "chebyshev: basis scales differ on one level", -4);
+          aligned[j] = std::move(ready_basis[j]);
+        } else {
+          aligned[j] = adjust(b, nq_min, sc);
+        }
+      }
+    }
+    return *aligned[i];
+  };
   std::function<std::unique_ptr<Ct>(std::vector<double>)> evaluate =
       [&](std::vector<double> c) -> std::unique_ptr<Ct> {
     const int degree = (int)c.size() - 1;
     if (degree < baby) {
-      std::unique_ptr<Ct> out;
+      std::vector<const Ct*> xs;
+      std::vector<double> ws_;
       for (int i = 1; i <= degree; ++i) {
-        if (std::fabs(c[i]) < 1e-14) continue;
-        auto term = mul_scalar(basis(i), c[i]);
-        out = out ? add(*out, *term, false) : std::move(term);
+        if (c[i] == 0.0) continue;
+        xs.push_back(&aligned_basis(i));
+        ws_.push_back(c[i]);
       }
-      if (!out) out = mul_scalar(*u, 0.0);
-      return add_scalar(*out, c[0]);
+      if (xs.empty()) {
+        xs.push_back(&aligned_basis(1));
+        ws_.push_back(0.0);
+      }
+      return linear_wsum(xs, ws_, c[0]);
     }
     int k = baby;
     while (2 * k - 1 < degree) k *= 2;
@@ -758,9 +808,7 @@ std::unique_ptr<Ct> Ckks::chebyshev(const Ct& x, const std::vector<double>& coef
     auto prod = mul(basis(k), *up_part);
     return add(*lo_part, *prod, false);
   };
-  auto out = evaluate(coeffs);
-  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
-  return out;
+  return evaluate(coeffs);
 }
 
 // ---------------------------------------------------------------------------
@@ -779,10 +827,21 @@ std::unique_ptr<Ct> Ckks::tensor(const Ct& a, const Ct& b) {
 }
 
 // OpenFHE DropLastElementAndScale: x_i <- (x_i - [lift(x_last)]_{q_i}) q_last^{-1}.
-void Ckks::rescale_inplace(Ct& a) {
+void Ckks::rescale_inplace(Ct& a) { rescale_into(a, a); }
+
+std::unique_ptr<Ct> Ckks::rescaled(const Ct& a) {
+  require(a.nq >= 2, "rescale: no limb left to drop (level underflow)", -4);
+  auto out = alloc(a.nq - 1, a.ncomp);
+  rescale_into(a, *out);
+  return out;
+}
+
+// OpenFHE DropLastElementAndScale from `a` into `o` (o may be a itself, or a
+// buffer with >= a.nq - 1 limbs per component).
+void Ckks::rescale_into(const Ct& a, Ct& o) {
   require(a.nq >= 2, "rescale: no limb left to drop (level underflow)", -4);
   const uint32_t nq = a.nq, n = ctx.n, nc = a.ncomp;
-  const size_t cs = (size_t)a.cap * n;
+  const size_t cs = (size_t)a.cap * n, os = (size_t)o.cap * n;
   uint64_t* last = ws(6, (size_t)nc * n);
   FHE_CUDA(cudaMemcpy2DAsync(last, (size_t)n * 8, a.data() + (size_t)(nq - 1) * n, cs * 8, (size_t)n * 8, nc,
                              cudaMemcpyDeviceToDevice, ctx.stream));
@@ -791,11 +850,12 @@ void Ckks::rescale_inplace(Ct& a) {
   const size_t ls = (size_t)(nq - 1) * n;
   launch_rescale_lift(last, n, lifted, ls, nc, nq - 1, n, ctx.primes[nq - 1], ctx.d_mod.as<Modulus>(), ctx.stream);
   ntt_dense(lifted, nc, nq - 1, nq - 1, 0, false);
-  launch_moddown_combine(a.data(), cs, lifted, ls, qinv_.as<Shoup>() + (size_t)(nq - 1) * ctx.L, nullptr, a.data(),
-                         cs, nc, nq - 1, n, ctx.d_primes.as<uint64_t>(), ctx.stream);
-  a.scale /= (double)ctx.primes[nq - 1];
-  a.nq -= 1;
-  a.noise_deg = a.noise_deg > 1 ? a.noise_deg - 1 : 1;
+  launch_moddown_combine(a.data(), cs, lifted, ls, qinv_.as<Shoup>() + (size_t)(nq - 1) * ctx.L, nullptr, o.data(),
+                         os, nc, nq - 1, n, ctx.d_primes.as<uint64_t>(), ctx.stream);
+  o.scale = a.scale / (double)ctx.primes[nq - 1];
+  o.nq = nq - 1;
+  o.ncomp = nc;
+  o.noise_deg = a.noise_deg > 1 ? a.noise_deg - 1 : 1;
 }
 
 void Ckks::level_reduce_inplace(Ct& a, uint32_t levels) {
@@ -821,14 +881,10 @@ std::vector<uint64_t> Ckks::scalar_residues(long double v, uint32_t nq) const {
 }
 
 std::unique_ptr<Ct> Ckks::mul_int(const Ct& a, int64_t v) {
-  auto r = scalar_residues((long double)v, a.nq);
-  std::vector<Shoup> sh(a.nq);
-  for (uint32_t i = 0; i < a.nq; ++i) sh[i] = mk_shoup(r[i], ctx.primes[i]);
-  DevMem d = upload(sh);
+  const LimbShoup c = limb_shoup(scalar_residues((long double)v, a.nq), ctx.primes);
   auto out = alloc(a.nq, a.ncomp);
-  launch_mul_const(a.data(), (size_t)a.cap * ctx.n, d.as<Shoup>(), nullptr, 0, out->data(), (size_t)a.nq * ctx.n,
-                   a.ncomp, a.nq, ctx.n, ctx.d_primes.as<uint64_t>(), ctx.stream);
-  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  launch_mul_const_v(a.data(), (size_t)a.cap * ctx.n, c, out->data(), (size_t)a.nq * ctx.n, a.ncomp, a.nq, ctx.n,
+                     ctx.d_primes.as<uint64_t>(), ctx.stream);
   out->scale = a.scale;
   out->noise_deg = a.noise_deg;
   return out;
@@ -899,7 +955,6 @@ std::unique_ptr<Ct> Ckks::add(const Ct& a, const Ct& b, bool subtract) {
             (size_t)nq * n, a.ncomp, nq, n, PrimeMap{nq, ctx.L}, ctx.d_mod.as<Modulus>(), ctx.stream);
   out->scale = x->scale;
   out->noise_deg = std::max(x->noise_deg, y->noise_deg);
-  if (tx || ty) FHE_CUDA(cudaStreamSynchronize(ctx.stream));
   return out;
 }
 
@@ -938,50 +993,87 @@ std::unique_ptr<Ct> Ckks::mul_plain(const Ct& a_in, const Pt& p) {
 }
 
 std::unique_ptr<Ct> Ckks::add_scalar(const Ct& a, double v) {
-  auto r = scalar_residues((long double)v * (long double)a.scale, a.nq);
-  DevMem d = upload(r);
-  auto out = clone(a);
-  launch_add_const(out->data(), 0, d.as<uint64_t>(), out->data(), 0, 1, a.nq, ctx.n, ctx.d_primes.as<uint64_t>(),
-                   ctx.stream);
-  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  const LimbWords c = limb_words(scalar_residues((long double)v * (long double)a.scale, a.nq));
+  auto out = alloc(a.nq, a.ncomp);
+  launch_add_const_v(a.data(), (size_t)a.cap * ctx.n, c, out->data(), (size_t)a.nq * ctx.n, a.ncomp, a.nq, ctx.n,
+                     ctx.d_primes.as<uint64_t>(), ctx.stream);
+  out->scale = a.scale;
+  out->noise_deg = a.noise_deg;
   return out;
 }
 
 std::unique_ptr<Ct> Ckks::prepare_mult_input(const Ct& a) {
-  auto c = clone(a);
-  if (c->noise_deg >= 2) rescale_inplace(*c);
-  return c;
+  if (a.noise_deg >= 2) return rescaled(a);
+  return clone(a);
+}
+
+const Ct& Ckks::ready(const Ct& a, std::unique_ptr<Ct>& hold) {
+  if (a.noise_deg < 2) return a;
+  hold = rescaled(a);
+  return *hold;
 }
 
 std::unique_ptr<Ct> Ckks::mul_scalar(const Ct& a, double v) {
-  auto c = prepare_mult_input(a);
-  const double sf = level_scale(c->nq);
-  auto r = scalar_residues((long double)v * (long double)sf, c->nq);
-  std::vector<Shoup> sh(c->nq);
-  for (uint32_t i = 0; i < c->nq; ++i) sh[i] = mk_shoup(r[i], ctx.primes[i]);
-  DevMem d = upload(sh);
-  auto out = alloc(c->nq, c->ncomp);
-  launch_mul_const(c->data(), (size_t)c->cap * ctx.n, d.as<Shoup>(), nullptr, 0, out->data(), (size_t)c->nq * ctx.n,
-                   c->ncomp, c->nq, ctx.n, ctx.d_primes.as<uint64_t>(), ctx.stream);
-  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
-  out->scale = c->scale * sf;
-  out->noise_deg = c->noise_deg + 1;
+  std::unique_ptr<Ct> hold;
+  const Ct& c = ready(a, hold);
+  const double sf = level_scale(c.nq);
+  const LimbShoup k = limb_shoup(scalar_residues((long double)v * (long double)sf, c.nq), ctx.primes);
+  auto out = alloc(c.nq, c.ncomp);
+  launch_mul_const_v(c.data(), (size_t)c.cap * ctx.n, k, out->data(), (size_t)c.nq * ctx.n, c.ncomp, c.nq, ctx.n,
+                     ctx.d_primes.as<uint64_t>(), ctx.stream);
+  out->scale = c.scale * sf;
+  out->noise_deg = c.noise_deg + 1;
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::linear_wsum(const std::vector<const Ct*>& xs, const std::vector<double>& w, double c0) {
+  require(!xs.empty() && xs.size() == w.size() && xs.size() <= kMaxWsum, "linear_wsum: 1..32 terms", -1);
+  const Ct& x0 = *xs[0];
+  const uint32_t nq = x0.nq, nc = x0.ncomp;
+  for (const Ct* x : xs)
+    require(x->nq == nq && x->ncomp == nc && x->noise_deg == x0.noise_deg &&
+                std::fabs(x->scale / x0.scale - 1.0) < 1e-12,
+            "linear_wsum: terms must share level, scale and degree", -4);
+  const double sf = level_scale(nq);
+  WsumArgs args{};
+  std::vector<uint64_t> wt((size_t)xs.size() * nq);
+  for (size_t i = 0; i < xs.size(); ++i) {
+    args.x[i] = xs[i]->data();
+    args.stride[i] = (uint64_t)xs[i]->cap * ctx.n;
+    const auto r = scalar_residues((long double)w[i] * (long double)sf, nq);
+    std::copy(r.begin(), r.end(), wt.begin() + i * nq);
+  }
+  const uint64_t* dw =
+      static_cast<const uint64_t*>(stage_pointers(wt.data(), wt.size() * sizeof(uint64_t), 24));
+  const double out_scale = x0.scale * sf;
+  const LimbWords add = limb_words(scalar_residues((long double)c0 * (long double)out_scale, nq));
+  auto out = alloc(nq, nc);
+  launch_linear_wsum(args, (uint32_t)xs.size(), dw, add, c0 != 0.0, out->data(), (size_t)nq * ctx.n, nc, nq, ctx.n,
+                     ctx.d_mod.as<Modulus>(), ctx.stream);
+  out->scale = out_scale;
+  out->noise_deg = x0.noise_deg + 1;
   return out;
 }
 
 std::unique_ptr<Ct> Ckks::mul(const Ct& a, const Ct& b) {
   require(keyed_, "mul before keygen", -4);
-  auto x = prepare_mult_input(a);
-  auto y = prepare_mult_input(b);
+  std::unique_ptr<Ct> hx, hy;
+  const Ct* x = &ready(a, hx);
+  const Ct* y = &ready(b, hy);
   // FLEXIBLEAUTO level alignment (AdjustLevelsAndDepth): the operand with more
   // limbs is brought to the other's level AND scale, so that ciphertexts on one
   // level keep one scale; dropping limbs alone would leave a nearby but
   // different scale that later additions cannot reconcile exactly.
-  if (x->nq > y->nq) x = adjust(*x, y->nq, y->scale);
-  if (y->nq > x->nq) y = adjust(*y, x->nq, x->scale);
+  if (x->nq > y->nq) {
+    hx = adjust(*x, y->nq, y->scale);
+    x = hx.get();
+  }
+  if (y->nq > x->nq) {
+    hy = adjust(*y, x->nq, x->scale);
+    y = hy.get();
+  }
   auto d = tensor(*x, *y);
   auto out = relinearize(*d);
-  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
   return out;
 }
 

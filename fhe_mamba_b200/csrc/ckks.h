@@ -83,6 +83,10 @@ class Ckks {
   std::unique_ptr<Ct> relinearize(const Ct& d);
   std::unique_ptr<Ct> mul(const Ct& a, const Ct& b);
   void rescale_inplace(Ct& a);
+  std::unique_ptr<Ct> rescaled(const Ct& a);
+  // OpenFHE EvalLinearWSum: sum_i w_i x_i + c0 for ciphertexts on one level with
+  // one scale, in one pass (the weights are encoded at the level's scale).
+  std::unique_ptr<Ct> linear_wsum(const std::vector<const Ct*>& xs, const std::vector<double>& w, double c0);
   void level_reduce_inplace(Ct& a, uint32_t levels);
   std::unique_ptr<Ct> rotate(const Ct& a, uint64_t g);
   std::vector<std::unique_ptr<Ct>> rotate_hoisted(const Ct& a, const std::vector<uint64_t>& gs);
@@ -128,6 +132,9 @@ class Ckks {
   uint64_t* ws(size_t idx, size_t words);
   std::vector<uint64_t> scalar_residues(long double v, uint32_t nq) const;
   std::unique_ptr<Ct> prepare_mult_input(const Ct& a);
+  // `a` itself, or its rescaled copy (kept in `hold`) when a rescale is pending.
+  const Ct& ready(const Ct& a, std::unique_ptr<Ct>& hold);
+  void rescale_into(const Ct& a, Ct& out);
 
   std::vector<double> sf_;
   std::map<uint32_t, LevelTables> levels_;

@@ -142,6 +142,45 @@ __global__ void k_add_const(const uint64_t* a, size_t sa, const uint64_t* cst, u
   out[c * so + off] = add_mod(a[c * sa + off], cst[l], primes[l]);
 }
 
+__global__ void k_mul_const_v(const uint64_t* a, size_t sa, const LimbShoup c, uint64_t* out, size_t so, uint32_t n,
+                              const uint64_t* primes) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y, comp = blockIdx.z;
+  const size_t off = (size_t)l * n + k;
+  out[comp * so + off] = shoup_mul(a[comp * sa + off], c.v[l].w, c.v[l].wp, primes[l]);
+}
+
+__global__ void k_add_const_v(const uint64_t* a, size_t sa, const LimbWords c, uint64_t* out, size_t so, uint32_t n,
+                              const uint64_t* primes) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y, comp = blockIdx.z;
+  const size_t off = (size_t)l * n + k;
+  const uint64_t x = a[comp * sa + off];
+  out[comp * so + off] = comp == 0 ? add_mod(x, c.v[l], primes[l]) : x;
+}
+
+__global__ void k_linear_wsum(const WsumArgs a, uint32_t m, const uint64_t* w, const LimbWords add, int has_add,
+                              uint64_t* out, size_t so, uint32_t nq, uint32_t n, const Modulus* mods) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y, comp = blockIdx.z;
+  const size_t off = (size_t)l * n + k;
+  uint64_t hi = 0, lo = 0;
+  for (uint32_t i = 0; i < m; ++i) {
+    const uint64_t x = a.x[i][comp * a.stride[i] + off];
+    const uint64_t wi = w[(size_t)i * nq + l];
+    const uint64_t plo = x * wi;
+    lo += plo;
+    hi += __umul64hi(x, wi) + (lo < plo);
+  }
+  const Modulus md = mods[l];
+  uint64_t r = reduce_u128(hi, lo, md);
+  if (has_add && comp == 0) r = add_mod(r, add.v[l], md.q);
+  out[comp * so + off] = r;
+}
+
 __global__ void k_tensor(const uint64_t* a, size_t sa, const uint64_t* b, size_t sb, uint64_t* d, size_t sd,
                          uint32_t n, const Modulus* mods) {
   const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
@@ -523,6 +562,25 @@ void launch_add_const(const uint64_t* a, size_t sa, const uint64_t* c, uint64_t*
                       uint32_t nlimbs, uint32_t n, const uint64_t* primes, cudaStream_t s) {
   if (!nlimbs || !ncomp) return;
   k_add_const<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, out, so, n, primes);
+}
+
+void launch_mul_const_v(const uint64_t* a, size_t sa, const LimbShoup& c, uint64_t* out, size_t so, uint32_t ncomp,
+                        uint32_t nlimbs, uint32_t n, const uint64_t* primes, cudaStream_t s) {
+  if (!nlimbs || !ncomp) return;
+  k_mul_const_v<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, out, so, n, primes);
+}
+
+void launch_add_const_v(const uint64_t* a, size_t sa, const LimbWords& c, uint64_t* out, size_t so, uint32_t ncomp,
+                        uint32_t nlimbs, uint32_t n, const uint64_t* primes, cudaStream_t s) {
+  if (!nlimbs || !ncomp) return;
+  k_add_const_v<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, out, so, n, primes);
+}
+
+void launch_linear_wsum(const WsumArgs& a, uint32_t m, const uint64_t* w, const LimbWords& add, int has_add,
+                        uint64_t* out, size_t so, uint32_t ncomp, uint32_t nq, uint32_t n, const Modulus* mods,
+                        cudaStream_t s) {
+  if (!nq || !ncomp) return;
+  k_linear_wsum<<<grid1(n, nq, ncomp), kTpb, 0, s>>>(a, m, w, add, has_add, out, so, nq, n, mods);
 }
 
 void launch_tensor(const uint64_t* a, size_t sa, const uint64_t* b, size_t sb, uint64_t* d, size_t sd,

@@ -51,6 +51,32 @@ void launch_mul_const(const uint64_t* a, size_t sa, const Shoup* c, const uint64
 void launch_add_const(const uint64_t* a, size_t sa, const uint64_t* c, uint64_t* out, size_t so,
                       uint32_t ncomp, uint32_t nlimbs, uint32_t n, const uint64_t* primes,
                       cudaStream_t s);
+// Per-limb constants passed by value in the kernel parameters (no device
+// upload, no host synchronisation); Q limbs only.
+constexpr uint32_t kMaxConstLimbs = 64;
+struct LimbShoup {
+  Shoup v[kMaxConstLimbs];
+};
+struct LimbWords {
+  uint64_t v[kMaxConstLimbs];
+};
+// out[comp][l] = a[comp][l] * c.v[l]
+void launch_mul_const_v(const uint64_t* a, size_t sa, const LimbShoup& c, uint64_t* out, size_t so, uint32_t ncomp,
+                        uint32_t nlimbs, uint32_t n, const uint64_t* primes, cudaStream_t s);
+// out[0][l] = a[0][l] + c.v[l]; out[comp > 0] = a[comp]
+void launch_add_const_v(const uint64_t* a, size_t sa, const LimbWords& c, uint64_t* out, size_t so, uint32_t ncomp,
+                        uint32_t nlimbs, uint32_t n, const uint64_t* primes, cudaStream_t s);
+// Weighted sum of up to kMaxWsum ciphertexts on one level (OpenFHE EvalLinearWSum):
+//   out[c][l] = sum_i w[i * nq + l] * x_i[c][l]  (+ add.v[l] on component 0)  mod q_l,
+// products accumulated in 128 bits and reduced once.  w = device array [m][nq].
+constexpr uint32_t kMaxWsum = 32;
+struct WsumArgs {
+  const uint64_t* x[kMaxWsum];
+  uint64_t stride[kMaxWsum];  // component stride of x_i (words)
+};
+void launch_linear_wsum(const WsumArgs& a, uint32_t m, const uint64_t* w, const LimbWords& add, int has_add,
+                        uint64_t* out, size_t so, uint32_t ncomp, uint32_t nq, uint32_t n, const Modulus* mods,
+                        cudaStream_t s);
 // Tensor product of two 2-component ciphertexts into d = [3][nq] (component stride sd).
 void launch_tensor(const uint64_t* a, size_t sa, const uint64_t* b, size_t sb, uint64_t* d, size_t sd,
                    uint32_t nq, uint32_t n, const Modulus* mods, cudaStream_t s);
