@@ -125,6 +125,8 @@ SIGNATURES = {
     "fhe_bootstrap_stage": [vp, i32, vp, ctypes.POINTER(vp)],
     "fhe_bootstrap_info": [vp, ctypes.POINTER(i32), ctypes.POINTER(u32), ctypes.POINTER(u32)],
     "fhe_bootstrap_levels": [vp, ctypes.POINTER(u32)],
+    "fhe_program_validate": [ctypes.c_char_p, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(i32)],
+    "fhe_program_run": [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, f64, f64, vp],
     "fhe_mod_raise": [vp, vp, ctypes.POINTER(vp)],
     "fhe_mul_i": [vp, vp, ctypes.POINTER(vp)],
     "fhe_ct_set_scale": [vp, vp, f64],

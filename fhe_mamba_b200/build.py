@@ -17,6 +17,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libfhe_b200.so")
+CLI = os.path.join(PKG, "packed_b200")
 ROOT = os.path.dirname(PKG)
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -74,7 +75,21 @@ def build(verbose: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    _build_cli()
     return LIB
+
+
+def _build_cli() -> None:
+    """packed_b200: the command-line drop-in for the reference's packed executor."""
+    src = os.path.join(CSRC, "packed_main.cpp")
+    hdr = os.path.join(ROOT, "include", "fhe_b200.h")
+    if os.path.exists(CLI) and os.path.getmtime(CLI) >= max(os.path.getmtime(p) for p in (src, hdr, LIB)):
+        return
+    cmd = [_host_cxx(), "-O2", "-std=c++17", "-I", os.path.join(ROOT, "include"), src, "-o", CLI,
+           "-L", PKG, "-lfhe_b200", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"packed_b200 link failed:\n{r.stdout}\n{r.stderr}")
 
 
 if __name__ == "__main__":

@@ -1,5 +1,10 @@
 // extern "C" entry points of libfhe_b200.so (declared in include/fhe_b200.h).
+#include <chrono>
+#include <cmath>
 #include <cstring>
+#include <fstream>
+#include <iomanip>
+#include <iostream>
 #include <memory>
 #include <new>
 #include <string>
@@ -8,6 +13,7 @@
 #include "bootstrap.h"
 #include "ckks.h"
 #include "context.h"
+#include "program.h"
 
 namespace fhe {
 void rescale_noalloc(Context& c, const uint64_t* in, uint32_t ncomp, uint32_t nq, uint64_t* out);
@@ -610,6 +616,156 @@ int fhe_bootstrap_levels(fhe_ctx* ctx, uint32_t* levels) {
     fhe::require(ctx->boot != nullptr && levels != nullptr, "no bootstrap setup or null output", -4);
     for (int i = 0; i < 4; ++i) levels[i] = ctx->boot->last_levels()[i];
   });
+}
+
+int fhe_program_validate(const char* program_path, int32_t* slots, int32_t* nodes, int32_t* outputs) {
+  return guarded([&] {
+    fhe::require(program_path != nullptr, "null program path");
+    std::ifstream in(program_path);
+    fhe::require((bool)in, std::string("cannot open program ") + program_path);
+    const fhe::PackedProgram prog = fhe::read_packed_program(in);
+    if (slots) *slots = prog.slots;
+    if (nodes) *nodes = (int32_t)prog.nodes.size();
+    if (outputs) *outputs = (int32_t)prog.outputs.size();
+  });
+}
+
+int fhe_program_run(const char* program_path, const char* client_head_path, const char* result_path,
+                    double poly_tol, double exact_tol, const fhe_program_options* options) {
+  int verdict = 0;
+  const int rc = guarded([&] {
+    fhe::require(program_path && result_path, "null program or result path");
+    fhe::require(std::isfinite(poly_tol) && std::isfinite(exact_tol) && poly_tol > 0 && exact_tol > 0,
+                 "invalid error tolerance");
+    fhe_program_options o{};
+    if (options) o = *options;
+    if (!o.depth) o.depth = 44;
+    if (!o.scale_bits) o.scale_bits = 59;
+    if (!o.first_bits) o.first_bits = 60;
+    if (!o.dnum) o.dnum = 3;
+    if (!o.bootstrap_passes) o.bootstrap_passes = 2;
+    fhe::require(o.bootstrap_passes == 1 || o.bootstrap_passes == 2, "bootstrap passes must be 1 or 2");
+    using Clock = std::chrono::steady_clock;
+    auto since = [](Clock::time_point t) { return std::chrono::duration<double>(Clock::now() - t).count(); };
+    std::ifstream in(program_path);
+    fhe::require((bool)in, std::string("cannot open program ") + program_path);
+    const fhe::PackedProgram prog = fhe::read_packed_program(in);
+    uint32_t log_n = o.log_n;
+    if (!log_n) {
+      log_n = 12;
+      while ((1u << (log_n - 1)) < (uint32_t)prog.slots) ++log_n;
+    }
+    fhe::require((1u << (log_n - 1)) >= (uint32_t)prog.slots, "ring too small for the program's slots");
+    fhe::GenerationClient client;
+    const bool with_client = client_head_path && *client_head_path;
+    if (with_client) {
+      client.load(client_head_path);
+      fhe::require(prog.nodes[prog.outputs.back().node].size == (int)client.width,
+                   "client head and final hidden width mismatch");
+    }
+    const auto setup0 = Clock::now();
+    fhe_params par{log_n, o.depth, o.scale_bits, o.first_bits, o.dnum, 1u << (log_n - 1), o.device, 0};
+    fhe_ctx* raw = nullptr;
+    fhe::require(fhe_ctx_create(&par, &raw) == FHE_OK, g_last_error);
+    std::unique_ptr<fhe_ctx, int (*)(fhe_ctx*)> ctx(raw, fhe_ctx_destroy);
+    fhe::Ckks& ck = *ctx->ck;
+    ck.keygen(o.seed ? o.seed : 1);
+    const bool can_boot = ctx->c.L > 4 + 4 + 2 + 21;
+    if (can_boot) {
+      fhe::BootParams bp;
+      bp.s2c_first = o.s2c_first != 0;
+      ctx->boot = std::make_unique<fhe::Bootstrapper>(ck, bp);
+      ctx->boot->keygen();
+    }
+    FHE_CUDA(cudaStreamSynchronize(ctx->c.stream));
+    const double setup_seconds = since(setup0);
+    fhe::ExecutorOptions eo;
+    eo.bootstrap_passes = o.bootstrap_passes;
+    eo.trace = o.trace != 0;
+    fhe::PackedExecutor ex(ck, ctx->boot.get(), prog, eo);
+    std::map<int, size_t> output_pos;
+    for (size_t i = 0; i < prog.outputs.size(); ++i) output_pos.emplace(prog.outputs[i].node, i);
+    std::vector<int> feedback_outputs;
+    for (const auto& nd : prog.nodes)
+      if (nd.op == "feedback") {
+        auto it = output_pos.find(nd.parents.at(0));
+        feedback_outputs.push_back(it == output_pos.end() ? -1 : (int)it->second);
+      }
+    auto checked_hidden = [&](const fhe::Ct& hidden, int out_index) {
+      auto values = ex.decrypt(hidden, (int)client.width);
+      if (out_index >= 0) {
+        const auto e = fhe::packed_output_errors(values, prog.outputs.at(out_index));
+        fhe::require(!e.non_finite && e.polynomial <= poly_tol && e.exact <= exact_tol,
+                     "client hidden fails reference tolerance before token " +
+                         std::to_string(client.tokens.size() + 1), -4);
+      }
+      return values;
+    };
+    if (with_client)
+      ex.client_feedback = [&](const fhe::Ct& hidden) {
+        return ex.encrypt(client.select(checked_hidden(hidden, feedback_outputs.at(client.tokens.size()))));
+      };
+    const auto eval0 = Clock::now();
+    auto outs = ex.evaluate();
+    FHE_CUDA(cudaStreamSynchronize(ctx->c.stream));
+    const double eval_seconds = since(eval0);
+    if (with_client) client.select(checked_hidden(*outs.back(), (int)prog.outputs.size() - 1));
+    double perr = 0, eerr = 0;
+    int non_finite = 0;
+    std::vector<double> per_poly, per_exact;
+    for (size_t i = 0; i < prog.outputs.size(); ++i) {
+      const auto values = ex.decrypt(*outs[i], (int)prog.outputs[i].polynomial.size());
+      const auto e = fhe::packed_output_errors(values, prog.outputs[i]);
+      non_finite += e.non_finite;
+      perr = std::max(perr, e.polynomial);
+      eerr = std::max(eerr, e.exact);
+      per_poly.push_back(e.polynomial);
+      per_exact.push_back(e.exact);
+    }
+    const bool passed = non_finite == 0 && perr <= poly_tol && eerr <= exact_tol;
+    std::ofstream r(result_path);
+    fhe::require((bool)r, std::string("cannot open result ") + result_path);
+    r << std::setprecision(12) << "{\n\"schema\":\"fhemamba-packed-result-v1\",\"backend\":\"fhe_b200\","
+      << "\"encrypted\":true,\"security\":\"not-set\",\"passed\":" << (passed ? "true" : "false")
+      << ",\"slots\":" << ctx->c.slots << ",\"payload_slots\":" << prog.slots
+      << ",\"ring_dimension\":" << ctx->c.n << ",\"depth\":" << o.depth << ",\"scale_bits\":" << o.scale_bits
+      << ",\"refresh_ring_dimension\":" << ctx->c.n << ",\"security_audit\":null"
+      << ",\"nodes\":" << prog.nodes.size() << ",\"setup_seconds\":" << setup_seconds
+      << ",\"s2c_first\":" << (o.s2c_first ? "true" : "false")
+      << ",\"refresh_ceiling\":" << ex.refresh_ceiling << ",\"refreshed_level\":" << ex.refreshed_level
+      << ",\"evaluated_nodes\":" << prog.nodes.size() << ",\"eval_seconds\":" << eval_seconds
+      << ",\"bootstrap_seconds\":" << ex.bootstrap_seconds << ",\"bootstraps\":" << ex.bootstraps
+      << ",\"ct_ct_mul\":" << ex.ct_ct << ",\"ct_pt_mul\":" << ex.ct_pt << ",\"rotations\":" << ex.rotations
+      << ",\"adds\":" << ex.adds << ",\"rotation_keys_generated\":" << ex.rotation_keys_generated
+      << ",\"rotation_keygen_seconds\":" << ex.keygen_seconds
+      << ",\"linear_method\":\"bsgs\",\"refresh_policy\":\"baseline\",\"bootstrap_passes\":" << o.bootstrap_passes
+      << ",\"logical_refreshes\":" << ex.logical_refreshes
+      << ",\"max_abs_error_vs_polynomial\":" << perr << ",\"max_abs_error_vs_exact\":" << eerr
+      << ",\"non_finite\":" << non_finite << ",\"polynomial_tolerance\":" << poly_tol
+      << ",\"exact_tolerance\":" << exact_tol << ",\"per_output_errors\":[";
+    for (size_t i = 0; i < per_poly.size(); ++i)
+      r << (i ? "," : "") << "{\"polynomial\":" << per_poly[i] << ",\"exact\":" << per_exact[i] << "}";
+    r << "],\"diagnostic_only\":false,\"evaluation_decryptions\":0,\"client_output_decrypt_count\":"
+      << client.tokens.size() << ",\"generated_token_ids\":[";
+    for (size_t i = 0; i < client.tokens.size(); ++i) r << (i ? "," : "") << client.tokens[i];
+    r << "],\"client_logit_margins\":[";
+    for (size_t i = 0; i < client.margins.size(); ++i) r << (i ? "," : "") << client.margins[i];
+    r << "],\"operation_stats\":{";
+    bool first = true;
+    for (const auto& [name, st] : ex.operation_stats) {
+      r << (first ? "" : ",") << "\"" << name << "\":{\"nodes\":" << st.nodes << ",\"seconds\":" << st.seconds
+        << ",\"bootstrap_seconds\":" << st.bootstrap_seconds << ",\"bootstraps\":" << st.bootstraps << "}";
+      first = false;
+    }
+    r << "},\"scope\":\"" << (with_client ? "encrypted backbone with inline client vocabulary head and actual greedy feedback"
+                                           : "packed feasibility; inline client fixture")
+      << "\"}\n";
+    fhe::require((bool)r, "could not write packed result");
+    std::cout << "passed=" << passed << " polynomial_error=" << perr << " exact_error=" << eerr
+              << " eval_seconds=" << eval_seconds << std::endl;
+    verdict = passed ? 0 : 1;
+  });
+  return rc != FHE_OK ? rc : verdict;
 }
 
 int fhe_mod_raise(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out) {

@@ -250,6 +250,40 @@ int fhe_bootstrap_info(fhe_ctx* ctx, int32_t* correction, uint32_t* cheb_degree,
  * SlotToCoeff (levels[4]); the reference's trace_levels telemetry. */
 int fhe_bootstrap_levels(fhe_ctx* ctx, uint32_t* levels);
 
+/* --- packed programs ------------------------------------------------------ */
+
+/* Options of fhe_program_run; zero fields take the defaults in brackets. */
+typedef struct fhe_program_options {
+  uint32_t log_n;             /* ring dimension 2^log_n [smallest >= 2^12 with N/2 >= program slots] */
+  uint32_t depth;             /* multiplicative depth [44] */
+  uint32_t scale_bits;        /* [59] */
+  uint32_t first_bits;        /* [60] */
+  uint32_t dnum;              /* [3] */
+  int32_t bootstrap_passes;   /* 1 or 2 [2] */
+  int32_t s2c_first;          /* S2C-first bootstrap variant [0] */
+  int32_t trace;              /* print per-node levels [0] */
+  int32_t device;             /* CUDA device ordinal [0] */
+  uint32_t reserved;
+  uint64_t seed;              /* key seed [1] */
+} fhe_program_options;
+
+/* Parses and validates a program with read_packed_program's admission rules
+ * (native/fideslib_stage0/include/packed_program.hpp:60-163) without touching a
+ * GPU; any output pointer may be NULL. */
+int fhe_program_validate(const char* program_path, int32_t* slots, int32_t* nodes, int32_t* outputs);
+
+/* The reference's packed_fideslib executable as one call
+ * (native/fideslib_stage0/src/packed_fideslib.cpp:882-1403): reads a
+ * fhemamba-packed-v1/v2 program, owns all crypto state (keys, bootstrapping),
+ * evaluates every node on the device (PackedEvaluator::evaluate, :600-836,
+ * baseline refresh policy), optionally runs the client vocabulary head for
+ * greedy feedback (client_head_path: u32 vocab, u32 width, f32[vocab*width];
+ * NULL for none), and writes the fhemamba-packed-result-v1 JSON.
+ * Returns 0 when every output is within both tolerances, 1 when a gate fails,
+ * a negative error code otherwise (fhe_last_error has the message). */
+int fhe_program_run(const char* program_path, const char* client_head_path, const char* result_path,
+                    double poly_tol, double exact_tol, const fhe_program_options* options);
+
 /* Bootstrapping ModRaise (EvalBootstrap's first step): the centred
  * coefficients of limb 0 lifted to every Q limb. */
 int fhe_mod_raise(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
