@@ -894,10 +894,12 @@ std::unique_ptr<Ct> Ckks::adjust(const Ct& a, uint32_t nq, double scale) {
   require(nq <= a.nq, "adjust: target level is above the ciphertext", -1);
   auto c = clone(a);
   if (c->noise_deg == 2 && c->nq > nq) rescale_inplace(*c);
-  if (std::fabs(c->scale / scale - 1.0) > 1e-12) {
+  if (c->scale != scale) {
     // Either times round(scale * q_last / s) and a rescale (consumes the
     // level being dropped anyway), or, when the target carries a squared
-    // scale, drop limbs first and multiply by round(scale / s).
+    // scale, drop limbs first and multiply by round(scale / s).  FLEXIBLEAUTO
+    // scales of neighbouring levels can agree to 1e-12, so "nearly equal" is
+    // not "equal": any difference is removed exactly when a level is dropped.
     const long double C =
         c->nq > nq ? (long double)scale * (long double)ctx.primes[c->nq - 1] / (long double)c->scale : 0.0L;
     if (C >= 1.0L && C < 9.2e18L) {
@@ -906,6 +908,8 @@ std::unique_ptr<Ct> Ckks::adjust(const Ct& a, uint32_t nq, double scale) {
       c = std::move(m);
       rescale_inplace(*c);
       c->scale = scale;
+    } else if (c->nq == nq && std::fabs(c->scale / scale - 1.0) < 1e-9) {
+      c->scale = scale;  // one level, one scale up to rounding of the scale itself
     } else {
       if (c->nq > nq) level_reduce_inplace(*c, c->nq - nq);
       const long double R = (long double)scale / (long double)c->scale;
@@ -925,7 +929,9 @@ std::unique_ptr<Ct> Ckks::add(const Ct& a, const Ct& b, bool subtract) {
   const Ct* x = &a;
   const Ct* y = &b;
   std::unique_ptr<Ct> tx, ty;
-  const bool same_scale = std::fabs(a.scale / b.scale - 1.0) <= 1e-12;
+  // scales that agree to 1e-9 are one FLEXIBLEAUTO scale up to the rounding
+  // of its own computation
+  const bool same_scale = std::fabs(a.scale / b.scale - 1.0) <= 1e-9;
   if (a.nq != b.nq) {
     // FLEXIBLEAUTO level alignment: the operand with more limbs is brought to
     // the other's level and scale.
@@ -1032,8 +1038,11 @@ std::unique_ptr<Ct> Ckks::linear_wsum(const std::vector<const Ct*>& xs, const st
   const uint32_t nq = x0.nq, nc = x0.ncomp;
   for (const Ct* x : xs)
     require(x->nq == nq && x->ncomp == nc && x->noise_deg == x0.noise_deg &&
-                std::fabs(x->scale / x0.scale - 1.0) < 1e-12,
-            "linear_wsum: terms must share level, scale and degree", -4);
+                std::fabs(x->scale / x0.scale - 1.0) < 1e-9,
+            "linear_wsum: terms must share level, scale and degree (limbs " + std::to_string(x->nq) + "/" +
+                std::to_string(nq) + ", degree " + std::to_string(x->noise_deg) + "/" +
+                std::to_string(x0.noise_deg) + ", scale ratio " + std::to_string(x->scale / x0.scale) + ")",
+            -4);
   const double sf = level_scale(nq);
   WsumArgs args{};
   std::vector<uint64_t> wt((size_t)xs.size() * nq);

@@ -17,7 +17,7 @@ These follow the reference's native Mamba-2 decode
   a placement rotation;
 * the RMSNorm inverse square root as a Chebyshev seed refined by Newton steps
   ``y <- 1.5 y - 0.5 V y^3`` (``newton_refine``, :2388-2400) on
-  ``V = sum(x^2) + width * eps``.
+  ``V = mean(x^2) + eps``.
 
 The plaintext formulas they implement are ``mixer2_forward`` and
 ``rms_normalize`` / ``ssm_update_readout`` (``src/fhemamba/reference.py:182-294``,
@@ -49,14 +49,19 @@ class StateLayout:
     slots: int
 
     def __post_init__(self):
-        for v in (self.heads, self.head_dim, self.state_size, self.slots):
+        for v in (self.head_dim, self.state_size, self.slots):
             _log2(v)
-        if self.head_dim * self.state_size > self.slots:
+        if self.heads < 1 or self.head_dim * self.state_size > self.slots:
             raise _lib.InvalidArgument(-1, "StateLayout", "one head's state does not fit the slots")
 
     @property
     def group_heads(self) -> int:
-        return min(self.heads, self.slots // (self.head_dim * self.state_size))
+        """Largest power of two that fits the slots and divides the head count."""
+        g = 1
+        cap = min(self.heads, self.slots // (self.head_dim * self.state_size))
+        while 2 * g <= cap and self.heads % (2 * g) == 0:
+            g *= 2
+        return g
 
     @property
     def group_block(self) -> int:
@@ -121,7 +126,8 @@ class PackedMamba2:
         b, G = self._state_baby, self._state_giant
         s |= {j * stride for j in range(1, b)} | {g * b * stride for g in range(1, G)}
         if norm_width:
-            s |= {1 << i for i in range(_log2(norm_width))} | {-norm_width}
+            win = 1 << max(0, (norm_width - 1).bit_length())
+            s |= {1 << i for i in range(_log2(win))} | {-win}
         return sorted(v % n for v in s if v % n)
 
     # ---- plaintext helpers ------------------------------------------------
@@ -254,20 +260,48 @@ class PackedMamba2:
                                                            scale=acc.GetScalingFactor()))
         return acc
 
+    # ---- polynomial gates -------------------------------------------------
+    def poly(self, x, coeffs, lo: float, hi: float, lo_slot: int, hi_slot: int):
+        """Chebyshev series sum c_i T_i(u) on the slots [lo_slot, hi_slot) only:
+        u = (2x - lo - hi) / (hi - lo) there and 0 elsewhere (so inactive slots
+        stay inside [-1, 1]); the result is masked back to the active slots."""
+        c = self.cc
+        a = np.zeros(self.L.slots)
+        b = np.zeros(self.L.slots)
+        a[lo_slot:hi_slot] = 2.0 / (hi - lo)
+        b[lo_slot:hi_slot] = -(lo + hi) / (hi - lo)
+        u = self._mul_mask(x, a)
+        if u.GetNoiseScaleDeg() >= 2:
+            c.RescaleInPlace(u)
+        u = c.EvalAdd(u, c.MakeCKKSPackedPlaintext(b, level=c.n_q - u.n_limbs(), scale=u.GetScalingFactor()))
+        out = c.EvalChebyshevSeries(u, coeffs, -1.0, 1.0)
+        return self._mul_mask(out, self._block_mask(lo_slot, hi_slot))
+
     # ---- RMSNorm ----------------------------------------------------------
     def rms_norm(self, x, width: int, weight, eps: float, domain, degree: int = 31, newton: int = 2):
         """x * rsqrt(mean(x^2) + eps) * weight for x at [0, width) (zeros elsewhere).
 
-        V = sum(x^2) + width * eps by a copy and a rotate-and-add window sum;
-        rsqrt(V) from a Chebyshev seed on `domain` (bounds of V) and Newton
-        steps; the result is multiplied by sqrt(width) * weight."""
+        V = mean(x^2) + eps by a copy, a rotate-and-add window sum over the next
+        power of two and a 1/width mask; slots outside [0, width) are set to the
+        middle of `domain` (the bounds of V) before the Chebyshev seed of rsqrt,
+        which Newton steps y <- 1.5 y - 0.5 V y^3 refine (the reference's
+        newton_refine works on sum + width * eps and rescales by sqrt(width);
+        the mean form keeps every constant small)."""
         c = self.cc
+        win = 1 << max(0, (width - 1).bit_length())
         sq = c.EvalMult(x, x)
-        sq = c.EvalAdd(sq, c.EvalRotate(sq, -width))
-        for i in range(_log2(width)):
+        sq = c.EvalAdd(sq, c.EvalRotate(sq, -win))
+        for i in range(_log2(win)):
             sq = c.EvalAdd(sq, c.EvalRotate(sq, 1 << i))
-        v = c.EvalAdd(sq, width * eps)
         lo, hi = domain
+        inv = np.zeros(self.L.slots)
+        inv[:width] = 1.0 / width
+        v = self._mul_mask(sq, inv)  # mean(x^2) on [0, width), 0 elsewhere
+        if v.GetNoiseScaleDeg() >= 2:
+            c.RescaleInPlace(v)
+        fill = np.full(self.L.slots, 0.5 * (lo + hi))
+        fill[:width] = eps
+        v = c.EvalAdd(v, c.MakeCKKSPackedPlaintext(fill, level=c.n_q - v.n_limbs(), scale=v.GetScalingFactor()))
         y = c.EvalChebyshevFunction(lambda t: 1.0 / np.sqrt(t), v, lo, hi, degree)
         v_neg_half = c.EvalMult(v, -0.5)
         for _ in range(newton):
@@ -275,6 +309,6 @@ class PackedMamba2:
             vy = c.EvalMult(v_neg_half, y)
             y = c.EvalAdd(c.EvalMult(y, 1.5), c.EvalMult(vy, y2))
         w = np.zeros(self.L.slots)
-        w[:width] = np.asarray(weight, dtype=float) * np.sqrt(width)
+        w[:width] = np.asarray(weight, dtype=float)
         xy = c.EvalMult(x, y)
         return c.EvalMult(xy, self._plain_for(xy, w))

@@ -79,7 +79,7 @@ def test_rms_norm(env):
     weight = rng.uniform(0.5, 1.5, D_INNER)
     eps = 1e-5
     ct = _stream(cc, [(0, x)])
-    out = pm.rms_norm(ct, D_INNER, weight, eps, domain=(16.0, 80.0), degree=31, newton=2)
+    out = pm.rms_norm(ct, D_INNER, weight, eps, domain=(0.125, 0.625), degree=31, newton=2)
     want = x / np.sqrt(np.mean(x * x) + eps) * weight
     got = cc.Decrypt(out).GetRealPackedValue()
     assert np.max(np.abs(got[:D_INNER] - want)) < 1e-4
