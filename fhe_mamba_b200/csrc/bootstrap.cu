@@ -106,10 +106,10 @@ Bootstrapper::Bootstrapper(Ckks& ck, const BootParams& p) : ck_(ck), p_(p) {
   require(corr_ <= 40, "correction must be <= 40", -1);
   require(ctx.L > p_.budget_cts + p_.budget_stc + 2, "the modulus chain is too short for bootstrapping", -1);
 
-  // CoeffToSlot: raised slots (q0 / S) U0 w  ->  BR(w) / (2K), where S is the
-  // FLEXIBLEAUTO scale of the level CoeffToSlot ends on (kept exactly through
-  // the transform by encoding each group at the scale of the prime it drops).
-  const double S = ck.level_scale(ctx.L - p_.budget_cts);
+  // CoeffToSlot: raised slots (q0 / S) U0 w  ->  BR(w) / (2K), S the scale
+  // attribute given to the raised ciphertext (the top level's); every group
+  // then lands exactly on the FLEXIBLEAUTO scale of its output level.
+  const double S = ck.level_scale(ctx.L);
   const double alpha = S / (2.0 * p_.K * (double)ctx.primes[0]);
   std::vector<uint32_t> halves;
   for (uint32_t h = n / 2; h >= 1; h /= 2) halves.push_back(h);
@@ -212,7 +212,16 @@ std::unique_ptr<Ct> Bootstrapper::transform(std::vector<Group>& groups, std::uni
   for (Group& g : groups) {
     const uint32_t nq = x->nq;
     require(nq >= 2, "bootstrapping ran out of levels", -4);
+    // Diagonals encoded at scale level_scale(nq-1) q_{nq-1} / scale(x): after
+    // the rescale the ciphertext carries exactly the FLEXIBLEAUTO scale of its
+    // new level, so bootstrapped values mix with any other ciphertext there.
+    const double target = ck_.level_scale(nq - 1);
+    const double dscale = target * (double)ctx.primes[nq - 1] / x->scale;
     auto it = g.enc.find(nq);
+    if (it != g.enc.end() && g.enc_scale[nq] != dscale) {
+      g.enc.erase(it);
+      it = g.enc.end();
+    }
     if (it == g.enc.end()) {
       std::vector<double> re, im;
       std::vector<size_t> which;
@@ -224,17 +233,17 @@ std::unique_ptr<Ct> Bootstrapper::transform(std::vector<Group>& groups, std::uni
             im.push_back(v.imag());
           }
         }
-      // each group is encoded at the scale of the prime its rescale drops, so
-      // the ciphertext's scale passes through the transform unchanged
-      auto pts = ck_.encode_batch(re.data(), im.data(), (uint32_t)which.size(), n, nq, (double)ctx.primes[nq - 1]);
+      auto pts = ck_.encode_batch(re.data(), im.data(), (uint32_t)which.size(), n, nq, dscale);
       std::vector<std::unique_ptr<Pt>> enc(g.diags.size());
       for (size_t i = 0; i < which.size(); ++i) enc[which[i]] = std::move(pts[i]);
       it = g.enc.emplace(nq, std::move(enc)).first;
+      g.enc_scale[nq] = dscale;
     }
     std::vector<const Pt*> d(g.diags.size());
     for (size_t i = 0; i < d.size(); ++i) d[i] = it->second[i].get();
     auto y = ck_.linear_transform(*x, d, g.b, g.G, g.stride, g.offset);
     ck_.rescale_inplace(*y);
+    y->scale = target;  // equal to the computed scale up to its last bit
     x = std::move(y);
   }
   return x;
@@ -262,7 +271,7 @@ std::unique_ptr<Ct> Bootstrapper::raise(const Ct& a) {
   auto low = ck_.adjust(*in, 1, std::ldexp((double)ctx.primes[0], -corr_));
   in.reset();
   auto raised = ck_.mod_raise(*low);
-  raised->scale = ck_.level_scale(ctx.L - p_.budget_cts);
+  raised->scale = ck_.level_scale(ctx.L);
   levels_[0] = raised->nq;
   return raised;
 }

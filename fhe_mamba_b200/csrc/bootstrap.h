@@ -50,7 +50,7 @@ class Bootstrapper {
   // The four steps of bootstrap(), each on its own (the pieces that
   // EvalCoeffsToSlots / EvalSlotsToCoeffs expose in OpenFHE):
   //   raise:          adjust to one limb at scale q0 2^-correction, ModRaise,
-  //                   scale attribute set to the level scale CoeffToSlot ends on;
+  //                   scale attribute set to the top level's scale;
   //   coeff_to_slot:  BR(w) / (2K), w = (t_lo + i t_hi) / q0 of the raised plaintext t;
   //   eval_mod:       BR(w mod 1) * 2 pi (real and imaginary parts separately);
   //   slot_to_coeff:  the inverse of coeff_to_slot back to the input's slots.
@@ -73,6 +73,7 @@ class Bootstrapper {
     int64_t stride = 0, offset = 0;
     std::vector<std::vector<std::complex<double>>> diags;       // [b*G], pre-rotated; empty = zero
     std::map<uint32_t, std::vector<std::unique_ptr<Pt>>> enc;  // encodings by limb count
+    std::map<uint32_t, double> enc_scale;                      // their encoding scale
   };
   void build_groups(std::vector<Group>& out, const std::vector<uint32_t>& halves, uint32_t budget, bool inverse,
                     double factor);

@@ -374,7 +374,7 @@ std::unique_ptr<Pt> Ckks::encode(const double* re, const double* im, uint32_t co
   double2* dv = reinterpret_cast<double2*>(ws(13, 2 * (size_t)slots));
   FHE_CUDA(cudaMemcpyAsync(dv, v.data(), slots * sizeof(double2), cudaMemcpyHostToDevice, ctx.stream));
   launch_fft_special_inv(dv, fft_inv_tw_.as<double2>(), slots, 1, ctx.stream);
-  int64_t* coef = reinterpret_cast<int64_t*>(ws(14, n));
+  double* coef = reinterpret_cast<double*>(ws(14, n));
   FHE_CUDA(cudaMemsetAsync(coef, 0, (size_t)n * 8, ctx.stream));
   FHE_CUDA(cudaMemsetAsync(status_.p, 0, sizeof(unsigned), ctx.stream));
   launch_encode_round(dv, coef, slots, n, scale, status_.as<unsigned>(), ctx.stream);
@@ -382,12 +382,12 @@ std::unique_ptr<Pt> Ckks::encode(const double* re, const double* im, uint32_t co
   p->buf = DevMem((size_t)nq * n * 8, ctx.sh);
   p->nq = nq;
   p->scale = scale;
-  launch_lift_small(coef, p->data(), n, nq, PrimeMap{nq, ctx.L}, ctx.d_mod.as<Modulus>(), ctx.stream);
+  launch_lift_double(coef, p->data(), n, nq, PrimeMap{nq, ctx.L}, ctx.d_mod.as<Modulus>(), 1, ctx.stream);
   ntt_dense(p->data(), 1, nq, nq, 0, false);
   unsigned st = 0;
   FHE_CUDA(cudaMemcpyAsync(&st, status_.p, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx.stream));
   FHE_CUDA(cudaStreamSynchronize(ctx.stream));
-  require(st == 0, "encode: a scaled value is not finite or exceeds 2^62", -1);
+  require(st == 0, "encode: a scaled value is not finite or reaches 2^126", -1);
   return p;
 }
 
@@ -410,12 +410,12 @@ std::vector<std::unique_ptr<Pt>> Ckks::encode_batch(const double* re, const doub
     double2* dv = reinterpret_cast<double2*>(ws(18, 2 * (size_t)nb * slots));
     FHE_CUDA(cudaMemcpyAsync(dv, v.data(), (size_t)nb * slots * sizeof(double2), cudaMemcpyHostToDevice, ctx.stream));
     launch_fft_special_inv(dv, fft_inv_tw_.as<double2>(), slots, nb, ctx.stream);
-    int64_t* coef = reinterpret_cast<int64_t*>(ws(19, (size_t)nb * n));
+    double* coef = reinterpret_cast<double*>(ws(19, (size_t)nb * n));
     FHE_CUDA(cudaMemsetAsync(coef, 0, (size_t)nb * n * 8, ctx.stream));
     FHE_CUDA(cudaMemsetAsync(status_.p, 0, sizeof(unsigned), ctx.stream));
     launch_encode_round_batch(dv, coef, slots, n, scale, nb, status_.as<unsigned>(), ctx.stream);
     uint64_t* res = ws(20, (size_t)nb * nq * n);
-    launch_lift_small_batch(coef, res, n, nq, PrimeMap{nq, ctx.L}, ctx.d_mod.as<Modulus>(), nb, ctx.stream);
+    launch_lift_double(coef, res, n, nq, PrimeMap{nq, ctx.L}, ctx.d_mod.as<Modulus>(), nb, ctx.stream);
     ntt_dense(res, nb, nq, nq, 0, false);
     for (uint32_t b = 0; b < nb; ++b) {
       auto p = std::make_unique<Pt>();
@@ -429,7 +429,7 @@ std::vector<std::unique_ptr<Pt>> Ckks::encode_batch(const double* re, const doub
     unsigned st = 0;
     FHE_CUDA(cudaMemcpyAsync(&st, status_.p, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx.stream));
     FHE_CUDA(cudaStreamSynchronize(ctx.stream));
-    require(st == 0, "encode: a scaled value is not finite or exceeds 2^62", -1);
+    require(st == 0, "encode: a scaled value is not finite or reaches 2^126", -1);
   }
   return out;
 }

@@ -372,7 +372,7 @@ __global__ void k_fft_fwd_stage(double2* v, const double2* tw, uint32_t slots, u
   x[i + lenh] = make_double2(__dsub_rn(u.x, tr), __dsub_rn(u.y, ti));
 }
 
-__global__ void k_encode_round(const double2* v, int64_t* coef, uint32_t slots, uint32_t log_slots,
+__global__ void k_encode_round(const double2* v, double* coef, uint32_t slots, uint32_t log_slots,
                                uint32_t n, double scale, unsigned* status) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= slots) return;
@@ -381,13 +381,33 @@ __global__ void k_encode_round(const double2* v, int64_t* coef, uint32_t slots, 
   const double2 x = v[src];
   const double r = __dmul_rn(__ddiv_rn(x.x, (double)slots), scale);
   const double s = __dmul_rn(__ddiv_rn(x.y, (double)slots), scale);
-  const double lim = 4611686018427387904.0;  // 2^62
+  const double lim = 0x1p126;
   if (!isfinite(r) || !isfinite(s) || fabs(r) >= lim || fabs(s) >= lim) {
     atomicOr(status, 1u);
     return;
   }
-  coef[(size_t)i * gap] = llround(r);
-  coef[(size_t)i * gap + n / 2] = llround(s);
+  coef[(size_t)i * gap] = round(r);
+  coef[(size_t)i * gap + n / 2] = round(s);
+}
+
+// Exact residue of an integer-valued double: below 2^63 through int64, above
+// as hi 2^64 + lo (both parts exact: power-of-two scaling and a difference
+// that fits the mantissa) reduced by the 128-bit reduction.
+__device__ __forceinline__ uint64_t lift_double(double d, const Modulus& m) {
+  if (fabs(d) < 0x1p63) return lift_signed((int64_t)d, m);
+  const double a = fabs(d);
+  const double hi = floor(a * 0x1p-64);
+  const double lo = a - hi * 0x1p64;
+  const uint64_t r = reduce_u128((uint64_t)hi, (uint64_t)lo, m);
+  return d < 0 ? (r ? m.q - r : 0) : r;
+}
+
+__global__ void k_lift_double(const double* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
+                              const Modulus* mods) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const uint32_t l = blockIdx.y, b = blockIdx.z;
+  out[((size_t)b * nlimbs + l) * n + k] = lift_double(src[(size_t)b * n + k], mods[pm(l)]);
 }
 
 __device__ __forceinline__ double u128_to_double(uint64_t hi, uint64_t lo) {
@@ -434,7 +454,7 @@ __global__ void k_decode_crt(const uint64_t* coef, uint32_t nlimbs, uint32_t slo
   v[dst] = make_double2(part[0], part[1]);
 }
 
-__global__ void k_encode_round_batch(const double2* v, int64_t* coef, uint32_t slots, uint32_t log_slots,
+__global__ void k_encode_round_batch(const double2* v, double* coef, uint32_t slots, uint32_t log_slots,
                                      uint32_t n, double scale, unsigned* status) {
   const uint32_t b = blockIdx.y;
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -444,14 +464,14 @@ __global__ void k_encode_round_batch(const double2* v, int64_t* coef, uint32_t s
   const double2 x = v[(size_t)b * slots + src];
   const double r = __dmul_rn(__ddiv_rn(x.x, (double)slots), scale);
   const double s = __dmul_rn(__ddiv_rn(x.y, (double)slots), scale);
-  const double lim = 4611686018427387904.0;  // 2^62
+  const double lim = 0x1p126;
   if (!isfinite(r) || !isfinite(s) || fabs(r) >= lim || fabs(s) >= lim) {
     atomicOr(status, 1u);
     return;
   }
-  int64_t* c = coef + (size_t)b * n;
-  c[(size_t)i * gap] = llround(r);
-  c[(size_t)i * gap + n / 2] = llround(s);
+  double* c = coef + (size_t)b * n;
+  c[(size_t)i * gap] = round(r);
+  c[(size_t)i * gap + n / 2] = round(s);
 }
 
 __global__ void k_lift_small_batch(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
@@ -657,7 +677,7 @@ void launch_fft_special_fwd(double2* v, const double2* tw, uint32_t slots, uint3
     k_fft_fwd_stage<<<grid1(slots / 2, batch), kTpb, 0, s>>>(v, tw, slots, len);
 }
 
-void launch_encode_round(const double2* v, int64_t* coef, uint32_t slots, uint32_t n, double scale,
+void launch_encode_round(const double2* v, double* coef, uint32_t slots, uint32_t n, double scale,
                          unsigned* status, cudaStream_t s) {
   k_encode_round<<<grid1(slots), kTpb, 0, s>>>(v, coef, slots, log2u(slots), n, scale, status);
 }
@@ -669,10 +689,16 @@ void launch_decode_crt(const uint64_t* coef, uint32_t nlimbs, uint32_t slots, ui
                                              q0inv_shoup, m1, v);
 }
 
-void launch_encode_round_batch(const double2* v, int64_t* coef, uint32_t slots, uint32_t n, double scale,
+void launch_encode_round_batch(const double2* v, double* coef, uint32_t slots, uint32_t n, double scale,
                                uint32_t batch, unsigned* status, cudaStream_t s) {
   if (!batch) return;
   k_encode_round_batch<<<grid1(slots, batch), kTpb, 0, s>>>(v, coef, slots, log2u(slots), n, scale, status);
+}
+
+void launch_lift_double(const double* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
+                        const Modulus* mods, uint32_t batch, cudaStream_t s) {
+  if (!nlimbs || !batch) return;
+  k_lift_double<<<grid1(n, nlimbs, batch), kTpb, 0, s>>>(src, out, n, nlimbs, pm, mods);
 }
 
 void launch_lift_small_batch(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,

@@ -124,9 +124,13 @@ void launch_fft_special_fwd(double2* v, const double2* tw, uint32_t slots, uint3
                             cudaStream_t s);
 // Bit-reverse, divide by slots, scale, round half away from zero, place at
 // coefficient i*gap (real) and i*gap + N/2 (imag) of coef (zeroed elsewhere).
-// status bit 0: a coefficient was not finite or exceeded 2^62.
-void launch_encode_round(const double2* v, int64_t* coef, uint32_t slots, uint32_t n, double scale,
+// Coefficients are integer-valued doubles (exact above 2^53 too).
+// status bit 0: a coefficient was not finite or reached 2^126.
+void launch_encode_round(const double2* v, double* coef, uint32_t slots, uint32_t n, double scale,
                          unsigned* status, cudaStream_t s);
+// out[l][k] = src[k] mod q_l for integer-valued doubles |src| < 2^126 (exact).
+void launch_lift_double(const double* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
+                        const Modulus* mods, uint32_t batch, cudaStream_t s);
 // Centred CRT of limbs 0 and 1 (or limb 0 alone) of an INTT'd plaintext at the
 // slot positions, divided by scale -> complex values in bit-reversed order,
 // ready for the forward special FFT.  m1 = Barrett constants of q1.
@@ -137,7 +141,7 @@ void launch_decode_crt(const uint64_t* coef, uint32_t nlimbs, uint32_t slots, ui
 // ---- batched encode ----
 // Batch versions over B vectors: v = [B][slots] double2, coef = [B][N] int64,
 // out = [B][nlimbs][N] u64.
-void launch_encode_round_batch(const double2* v, int64_t* coef, uint32_t slots, uint32_t n, double scale,
+void launch_encode_round_batch(const double2* v, double* coef, uint32_t slots, uint32_t n, double scale,
                                uint32_t batch, unsigned* status, cudaStream_t s);
 void launch_lift_small_batch(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
                              const Modulus* mods, uint32_t batch, cudaStream_t s);

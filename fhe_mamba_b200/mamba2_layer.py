@@ -101,44 +101,59 @@ def _rms(x, w, eps):
     return x / np.sqrt(np.mean(x * x) + eps) * w
 
 
+def exact_step(W: Mamba2Weights, h, conv, st, upd=lambda k, v: None):
+    """The layer with the exact nonlinearities (calibration); upd(site, values)
+    observes the inputs of every polynomial and inverse square root."""
+    E, S, H, K, Pd = W.d_inner, W.d_state, W.heads, W.conv_kernel, W.head_dim
+    upd("v1", [np.mean(h * h) + W.eps])
+    u = _rms(h, W["norm_w"], W.eps)
+    proj = W["w_in"] @ u
+    z, xbc, dt = proj[:E], proj[E:E + W.conv_dim], proj[E + W.conv_dim:]
+    window = list(conv) + [xbc]
+    xc = sum(W["conv_w"][:, k] * window[k] for k in range(K)) + W["conv_b"]
+    upd("xc", xc)
+    xa = _silu(xc)
+    upd("dt", dt + W["dt_bias"])
+    dts = _softplus(dt + W["dt_bias"])
+    upd("adt", W["a"] * dts)
+    upd("z", z)
+    x, B, C = xa[:E].reshape(H, Pd), xa[E:E + S], xa[E + S:]
+    st = np.exp(W["a"] * dts)[:, None, None] * st + (dts[:, None] * x)[:, :, None] * B[None, None, :]
+    y = (st * C[None, None, :]).sum(-1) + W["d"][:, None] * x
+    g = y.reshape(E) * _silu(z)
+    upd("v2", [np.mean(g * g) + W.eps])
+    out = W["w_out"] @ _rms(g, W["gn_w"], W.eps)
+    return h + out, window[1:], st
+
+
+def new_ranges():
+    return {k: [np.inf, -np.inf] for k in ("xc", "dt", "adt", "z", "v1", "v2")}
+
+
+def range_updater(ranges):
+    def upd(k, v):
+        ranges[k][0] = min(ranges[k][0], float(np.min(v)))
+        ranges[k][1] = max(ranges[k][1], float(np.max(v)))
+    return upd
+
+
 class Mamba2Polys:
     """Polynomial domains calibrated on exact-function trajectories (random
     residual inputs over a few tokens, recurrent state U[-1, 1]), widened by half
-    their span."""
+    their span.  `ranges` (site -> [lo, hi]) replaces the layer-local
+    calibration when the layer sits inside a model."""
 
     def __init__(self, W: Mamba2Weights, degree: int = 31, seed_degree: int = 15, samples: int = 16,
-                 tokens: int = 3, seed: int = 9):
-        r = np.random.default_rng(seed)
-        E, S, H, K, Pd = W.d_inner, W.d_state, W.heads, W.conv_kernel, W.head_dim
-        ranges = {k: [np.inf, -np.inf] for k in ("xc", "dt", "adt", "z", "v1", "v2")}
-
-        def upd(k, v):
-            ranges[k][0] = min(ranges[k][0], float(np.min(v)))
-            ranges[k][1] = max(ranges[k][1], float(np.max(v)))
-
-        for _ in range(samples):
-            conv = [np.zeros(W.conv_dim) for _ in range(K - 1)]
-            st = r.uniform(-1, 1, (H, Pd, S))
-            for _ in range(tokens):
-                h = r.normal(0, 1, W.d_model)
-                upd("v1", [np.mean(h * h) + W.eps])
-                u = _rms(h, W["norm_w"], W.eps)
-                proj = W["w_in"] @ u
-                z, xbc, dt = proj[:E], proj[E:E + W.conv_dim], proj[E + W.conv_dim:]
-                window = conv + [xbc]
-                xc = sum(W["conv_w"][:, k] * window[k] for k in range(K)) + W["conv_b"]
-                upd("xc", xc)
-                xa = _silu(xc)
-                upd("dt", dt + W["dt_bias"])
-                dts = _softplus(dt + W["dt_bias"])
-                upd("adt", W["a"] * dts)
-                upd("z", z)
-                x, B, C = xa[:E].reshape(H, Pd), xa[E:E + S], xa[E + S:]
-                st = np.exp(W["a"] * dts)[:, None, None] * st + (dts[:, None] * x)[:, :, None] * B[None, None, :]
-                y = (st * C[None, None, :]).sum(-1) + W["d"][:, None] * x
-                g = y.reshape(E) * _silu(z)
-                upd("v2", [np.mean(g * g) + W.eps])
-                conv = window[1:]
+                 tokens: int = 3, seed: int = 9, ranges=None):
+        if ranges is None:
+            r = np.random.default_rng(seed)
+            ranges = new_ranges()
+            upd = range_updater(ranges)
+            for _ in range(samples):
+                conv = [np.zeros(W.conv_dim) for _ in range(W.conv_kernel - 1)]
+                st = r.uniform(-1, 1, (W.heads, W.head_dim, W.d_state))
+                for _ in range(tokens):
+                    _, conv, st = exact_step(W, r.normal(0, 1, W.d_model), conv, st, upd)
 
         def widen(k, frac=0.5, floor=1.0):
             lo, hi = ranges[k]
@@ -212,40 +227,126 @@ def rect_diagonals(Wm: np.ndarray, baby: int, giant: int, slots: int):
     return out
 
 
+def rotation_sum_schedule(count: int):
+    """(offset, accumulated) steps whose sums give sum_{r < count} rot(x, r * stride)
+    with about log2(count) rotations (doubling, plus one step per set bit)."""
+    steps, bit, filled = [], 1, 1
+    while bit <= count // 2:
+        bit *= 2
+    bit //= 2
+    while bit > 0:
+        steps.append((filled, True))
+        filled *= 2
+        if count & bit:
+            steps.append((filled, False))
+            filled += 1
+        bit //= 2
+    return steps
+
+
+class ReplicatedLayout:
+    """Replicated BSGS layout of y = W x (W: m x n) in `slots` slots.
+
+    R windows of w = n/R + ceil(m/n) n slots each; window r accumulates the
+    diagonals d = r n/R + t (t < n/R) of rows i < m at slots r w + i.  The input
+    is replicated with period n over the whole span, which makes slot
+    r w + i + t hold x[(i + r n/R + t) mod n] (r w = r n/R mod n), so all windows
+    share one set of n/R diagonal plaintexts and one BSGS over t.  A rotate-and-
+    add over the windows then sums the R partial results into slots [0, m)."""
+
+    def __init__(self, m: int, n: int, slots: int):
+        k = -(-m // n)
+        R = 1
+        while n % (2 * R) == 0:
+            R2 = 2 * R
+            w2 = n // R2 + k * n
+            if (R2 - 1) * w2 + m + n // R2 > slots:
+                break
+            R = R2
+        self.m, self.n, self.R = m, n, R
+        self.T = n // R
+        self.w = self.T + k * n
+        self.span = (R - 1) * self.w + m + self.T
+        if self.span > slots:
+            raise ValueError("matrix does not fit the slots")
+        self.copies = -(-self.span // n)
+        b = 1
+        while b * b < self.T:
+            b *= 2
+        self.b = b
+        self.G = -(-self.T // b)
+
+    def diagonals(self, Wm: np.ndarray, slots: int):
+        m, n, R, T, w, b = self.m, self.n, self.R, self.T, self.w, self.b
+        rows = np.arange(m)
+        out = []
+        for g in range(self.G):
+            for j in range(b):
+                t = g * b + j
+                if t >= T:
+                    out.append(None)
+                    continue
+                v = np.zeros(slots)
+                for r in range(R):
+                    v[r * w + rows] = Wm[rows, (rows + r * T + t) % n]
+                out.append(np.roll(v, g * b))  # pre-rotated by the giant step
+        return out
+
+    def rotation_steps(self):
+        s = {j for j in range(1, self.b)} | {g * self.b for g in range(1, self.G)}
+        s |= {-o * self.n for o, _ in rotation_sum_schedule(self.copies)}
+        s |= {o * self.w for o, _ in rotation_sum_schedule(self.R)}
+        return s
+
+
+class PlaintextCache:
+    """Encoded diagonal plaintexts kept across tokens up to a byte budget (LRU)."""
+
+    def __init__(self, budget_bytes: float):
+        self.budget = budget_bytes
+        self.items = {}
+        self.bytes = 0
+        self.hits = self.misses = 0
+
+    def get(self, key, nbytes, build):
+        if key in self.items:
+            self.hits += 1
+            v = self.items.pop(key)
+            self.items[key] = v
+            return v[0]
+        self.misses += 1
+        value = build()
+        while self.items and self.bytes + nbytes > self.budget:
+            k0 = next(iter(self.items))
+            self.bytes -= self.items.pop(k0)[1]
+        if nbytes <= self.budget:
+            self.items[key] = (value, nbytes)
+            self.bytes += nbytes
+        return value
+
+
 class EncryptedMamba2Layer:
     """The layer on ciphertexts of one CryptoContext (full packing)."""
 
-    def __init__(self, cc, W: Mamba2Weights, P: Mamba2Polys, passes: int = 2, margin: int = 3):
+    def __init__(self, cc, W: Mamba2Weights, P: Mamba2Polys, passes: int = 2, margin: int = 3,
+                 cache: PlaintextCache | None = None):
         self.cc, self.W, self.P = cc, W, P
         self.passes, self.margin = passes, margin
+        self.cache = cache if cache is not None else PlaintextCache(0)
+        self.rep = {"w_in": ReplicatedLayout(W.proj_dim, W.d_model, cc.slots),
+                    "w_out": ReplicatedLayout(W.d_model, W.d_inner, cc.slots)}
         E, S, H = W.d_inner, W.d_state, W.heads
         self.layout = StateLayout(H, W.head_dim, S, cc.slots)
         self.pm = PackedMamba2(cc, self.layout, b_base=E, c_base=E + S, head_base=0)
         self.refreshes = 0
         self._lin = {}
         n = cc.slots
-        # BSGS shapes: baby 32 or sqrt(n_in); replicated inputs
-        self.lin_shapes = {}
-        for name, (m, k) in {"w_in": (W.proj_dim, W.d_model), "w_out": (W.d_model, E)}.items():
-            b = 1
-            while b * b < k and b < 32:
-                b *= 2
-            G = -(-k // b)
-            reps = 1
-            while reps * k < m + k:
-                reps *= 2
-            if reps * k > n:
-                raise ValueError("input replication does not fit the slots")
-            self.lin_shapes[name] = (b, G, reps)
-
     # ---- setup --------------------------------------------------------------
     def rotation_steps(self):
         W, n = self.W, self.cc.slots
         s = set(self.pm.rotation_steps())
-        for name, (b, G, reps) in self.lin_shapes.items():
-            k = W.d_model if name == "w_in" else W.d_inner
-            s |= {j for j in range(1, b)} | {g * b for g in range(1, G)}
-            s |= {-(k << i) for i in range(reps.bit_length() - 1)}
+        for lay in self.rep.values():
+            s |= lay.rotation_steps()
         for width in (W.d_model, W.d_inner):
             win = 1 << (width - 1).bit_length()
             s |= {1 << i for i in range(win.bit_length() - 1)} | {-win}
@@ -254,8 +355,7 @@ class EncryptedMamba2Layer:
 
     def _diags(self, name):
         if name not in self._lin:
-            b, G, _ = self.lin_shapes[name]
-            self._lin[name] = rect_diagonals(self.W[name], b, G, self.cc.slots)
+            self._lin[name] = self.rep[name].diagonals(self.W[name], self.cc.slots)
         return self._lin[name]
 
     # ---- helpers --------------------------------------------------------------
@@ -269,18 +369,32 @@ class EncryptedMamba2Layer:
         self.refreshes += 1
         return self.cc.refresh(ct, bound, passes=self.passes)
 
-    def _linear(self, x, name):
+    def _rotation_sum(self, x, count, stride):
         c = self.cc
-        b, G, reps = self.lin_shapes[name]
-        k = self.W[name].shape[1]
-        for i in range(reps.bit_length() - 1):
-            x = c.EvalAdd(x, c.EvalRotate(x, -(k << i)))
+        acc = x
+        for off, accumulated in rotation_sum_schedule(count):
+            acc = c.EvalAdd(acc, c.EvalRotate(acc if accumulated else x, off * stride))
+        return acc
+
+    def _linear(self, x, name):
+        """Replicated BSGS matvec: replicate, one BSGS over n/R diagonals shared by
+        R windows, rotate-and-add the windows, mask to the m outputs."""
+        c = self.cc
+        lay = self.rep[name]
+        x = self._rotation_sum(x, lay.copies, -lay.n)
         nq = x.n_limbs() - (1 if x.GetNoiseScaleDeg() >= 2 else 0)
         diags = self._diags(name)
-        dense = [d for d in diags if d is not None]
-        pts = iter(c.MakeCKKSPackedPlaintexts(np.array(dense), level=c.n_q - nq))
-        plist = [next(pts) if d is not None else None for d in diags]
-        return c.EvalLinearTransform(x, plist, b, G)
+
+        def build():
+            dense = [d for d in diags if d is not None]
+            pts = iter(c.MakeCKKSPackedPlaintexts(np.array(dense), level=c.n_q - nq))
+            return [next(pts) if d is not None else None for d in diags]
+
+        nbytes = sum(d is not None for d in diags) * nq * c.n * 8
+        plist = self.cache.get((id(self), name, nq), nbytes, build)
+        y = c.EvalLinearTransform(x, plist, lay.b, lay.G)
+        y = self._rotation_sum(y, lay.R, lay.w)
+        return self.pm._mul_mask(y, self.pm._block_mask(0, lay.m))
 
     def _poly(self, x, p: Poly, lo_slot, hi_slot):
         return self.pm.poly(x, p.coeffs, p.lo, p.hi, lo_slot, hi_slot)
@@ -352,6 +466,39 @@ class EncryptedMamba2Layer:
         return h_out, window[1:], states
 
 
+def poly_step_record(W: Mamba2Weights, P: Mamba2Polys, h, conv, st, rec):
+    """plain_step that reports the magnitude of every refreshed intermediate."""
+    E, S, H, Pd = W.d_inner, W.d_state, W.heads, W.head_dim
+    rec("h", h)
+    u = plain_rms(h, W["norm_w"], W.eps, P.rsqrt1)
+    rec("u", u)
+    proj = W["w_in"] @ u
+    z, xbc, dt = proj[:E], proj[E:E + W.conv_dim], proj[E + W.conv_dim:]
+    rec("xbc", xbc)
+    rec("z", z)
+    window = list(conv) + [xbc]
+    xc = sum(W["conv_w"][:, k] * window[k] for k in range(W.conv_kernel)) + W["conv_b"]
+    rec("xc", xc)
+    xa = P.silu_x(xc)
+    rec("xa", xa)
+    rec("dt", dt + W["dt_bias"])
+    dts = P.softplus(dt + W["dt_bias"])
+    rec("dts", dts)
+    rec("adt", W["a"] * dts)
+    x, B, C = xa[:E].reshape(H, Pd), xa[E:E + S], xa[E + S:]
+    upd_ = (dts[:, None] * x)[:, :, None] * B[None, None, :]
+    st = upd_ if st is None else P.exp(W["a"] * dts)[:, None, None] * st + upd_
+    rec("state", st)
+    y = (st * C[None, None, :]).sum(-1) + W["d"][:, None] * x
+    rec("y", y)
+    g = y.reshape(E) * P.silu_z(z)
+    rec("g", g)
+    gn = plain_rms(g, W["gn_w"], W.eps, P.rsqrt2)
+    rec("gn", gn)
+    out = W["w_out"] @ gn
+    return h + out, window[1:], st
+
+
 def calibrate_bounds(W: Mamba2Weights, P: Mamba2Polys, samples: int = 4, seed: int = 11, tokens: int = 3):
     """Refresh bounds (max |value| x 2, at least 1) of every refreshed intermediate,
     from plaintext runs of the polynomial path over a few tokens."""
@@ -367,29 +514,111 @@ def calibrate_bounds(W: Mamba2Weights, P: Mamba2Polys, samples: int = 4, seed: i
         st = r.uniform(-1, 1, (H, Pd, S))
         for _ in range(tokens):
             h = r.normal(0, 1, W.d_model)
-            rec("h", h)
-            u = plain_rms(h, W["norm_w"], W.eps, P.rsqrt1)
-            rec("u", u)
-            proj = W["w_in"] @ u
-            z, xbc, dt = proj[:E], proj[E:E + W.conv_dim], proj[E + W.conv_dim:]
-            rec("xbc", xbc)
-            rec("z", z)
-            window = conv + [xbc]
-            xc = sum(W["conv_w"][:, k] * window[k] for k in range(W.conv_kernel)) + W["conv_b"]
-            rec("xc", xc)
-            xa = P.silu_x(xc)
-            rec("xa", xa)
-            rec("dt", dt + W["dt_bias"])
-            dts = P.softplus(dt + W["dt_bias"])
-            rec("dts", dts)
-            rec("adt", W["a"] * dts)
-            x, B, C = xa[:E].reshape(H, Pd), xa[E:E + S], xa[E + S:]
-            st = P.exp(W["a"] * dts)[:, None, None] * st + (dts[:, None] * x)[:, :, None] * B[None, None, :]
-            rec("state", st)
-            y = (st * C[None, None, :]).sum(-1) + W["d"][:, None] * x
-            rec("y", y)
-            g = y.reshape(E) * P.silu_z(z)
-            rec("g", g)
-            rec("gn", plain_rms(g, W["gn_w"], W.eps, P.rsqrt2))
-            conv = window[1:]
+            h2, conv, st = poly_step_record(W, P, h, conv, st, rec)
     return {k: max(1.0, 2.0 * v) for k, v in m.items()}
+
+
+class Mamba2Model:
+    """A layers-deep Mamba-2 language model (tied embedding, final RMSNorm) with
+    synthetic weights, for the encrypted greedy token loop:
+    the client encrypts the embedding of the current token, the server runs
+    every layer on ciphertexts, the client decrypts the final hidden vector and
+    picks the argmax token (the reference's GenerationClient::select,
+    native/fideslib_stage0/src/packed_fideslib.cpp:842-880)."""
+
+    def __init__(self, layers: int, d_model: int, d_state: int, heads: int, vocab: int, std: float = 0.02,
+                 seed: int = 6, calib_sequences: int = 8):
+        self.layers = [Mamba2Weights(d_model=d_model, d_state=d_state, heads=heads, std=std, seed=seed * 1000 + i)
+                       for i in range(layers)]
+        r = np.random.default_rng(seed)
+        self.embedding = r.normal(0, 1.0, (vocab, d_model))
+        self.norm_f = 1.0 + r.normal(0, 0.02, d_model)
+        eps = self.layers[0].eps
+        self.d_model = d_model
+        # calibration through the whole stack: exact-function trajectories from
+        # random prompts give every layer's polynomial domains ...
+        ranges = [new_ranges() for _ in self.layers]
+        finals = []
+        seqs = [r.integers(0, vocab, 4) for _ in range(calib_sequences)]
+        for seq in seqs:
+            state = [([np.zeros(W.conv_dim) for _ in range(W.conv_kernel - 1)],
+                      np.zeros((W.heads, W.head_dim, W.d_state))) for W in self.layers]
+            for tok in seq:
+                h = self.embedding[tok]
+                for li, W in enumerate(self.layers):
+                    h, c_, s_ = exact_step(W, h, state[li][0], state[li][1], range_updater(ranges[li]))
+                    state[li] = (c_, s_)
+                finals.append(np.mean(h * h) + eps)
+        self.polys = [Mamba2Polys(W, ranges=rg) for W, rg in zip(self.layers, ranges)]
+        lo, hi = 0.25 * min(finals), 4.0 * max(finals)
+        self.rsqrt_f = Poly(cheb_fit(lambda t: 1 / np.sqrt(t), lo, hi, 15), lo, hi)
+        # ... and the polynomial path's magnitudes give the refresh bounds
+        mags = [{} for _ in self.layers]
+        for seq in seqs:
+            state = self.initial_state()
+            for tok in seq:
+                h = self.embedding[tok]
+                for li, (W, P) in enumerate(zip(self.layers, self.polys)):
+                    def rec(k, v, m=mags[li]):
+                        m[k] = max(m.get(k, 0.0), float(np.max(np.abs(v))))
+                    h, c_, s_ = poly_step_record(W, P, h, state[li][0], state[li][1], rec)
+                    state[li] = (c_, s_)
+        self.bounds = [{k: max(1.0, 2.0 * v) for k, v in m.items()} for m in mags]
+
+    def initial_state(self):
+        return [([np.zeros(W.conv_dim) for _ in range(W.conv_kernel - 1)], None) for W in self.layers]
+
+    def plain_token(self, token: int, state):
+        """One token on plaintext (polynomial path); returns (hidden, logits, state)."""
+        h = self.embedding[token].copy()
+        new = []
+        for W, P, (conv, st) in zip(self.layers, self.polys, state):
+            h, conv, st = plain_step(W, P, h, conv, st)
+            new.append((conv, st))
+        hf = plain_rms(h, self.norm_f, self.layers[0].eps, self.rsqrt_f)
+        return hf, self.embedding @ hf, new
+
+
+class EncryptedMamba2Model:
+    """The model's layers on one CryptoContext; client-side encryption and
+    selection around them."""
+
+    def __init__(self, cc, model: Mamba2Model, passes: int = 2, cache_gb: float = 40.0):
+        self.cc, self.m = cc, model
+        self.cache = PlaintextCache(cache_gb * 2 ** 30)
+        self.layers = [EncryptedMamba2Layer(cc, W, P, passes=passes, cache=self.cache)
+                       for W, P in zip(model.layers, model.polys)]
+        self.state = [([None] * (W.conv_kernel - 1), None) for W in model.layers]
+        self.tokens, self.margins = [], []
+
+    def rotation_steps(self):
+        s = set()
+        for layer in self.layers:
+            s |= set(layer.rotation_steps())
+        return sorted(s)
+
+    def step(self, token: int):
+        """Server pass for one token: returns the encrypted final hidden vector."""
+        c, m = self.cc, self.m
+        h = c.Encrypt(c.MakeCKKSPackedPlaintext(np.pad(m.embedding[token], (0, c.slots - m.d_model))))
+        new = []
+        for layer, (conv, st), bounds in zip(self.layers, self.state, m.bounds):
+            h, conv, st = layer.step(h, conv, st, bounds)
+            new.append((conv, st))
+        self.state = new
+        last = self.layers[-1]
+        h = last._fit(h, 14, m.bounds[-1]["h"] * 2)
+        return last.pm.rms_norm(h, m.d_model, m.norm_f, m.layers[0].eps, (m.rsqrt_f.lo, m.rsqrt_f.hi),
+                                degree=len(m.rsqrt_f.coeffs) - 1)
+
+    def select(self, hidden_ct):
+        """Client: decrypt the final hidden vector and pick the greedy token."""
+        hf = self.cc.Decrypt(hidden_ct).GetRealPackedValue()[:self.m.d_model]
+        logits = self.m.embedding @ hf
+        order = np.argsort(logits)[::-1]
+        self.tokens.append(int(order[0]))
+        self.margins.append(float(logits[order[0]] - logits[order[1]]))
+        return int(order[0]), hf
+
+    def refreshes(self):
+        return sum(layer.refreshes for layer in self.layers)

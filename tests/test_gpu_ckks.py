@@ -185,3 +185,16 @@ def test_config3_keyswitch_shape(oracle):
     for st, o in zip(steps, outs):
         g = cc.galois_element(st)
         assert np.array_equal(o.residues(), oc.rotate(b, g, oc.rot_key(SEED, s, sn, g)))
+
+
+def test_encode_values_beyond_2_62(cfg1):
+    """Scaled coefficients above 2^63 are encoded exactly (integer-valued doubles
+    split into 64-bit halves before the RNS lift)."""
+    cc, oc, s, sn = cfg1
+    r = np.random.default_rng(5)
+    big = r.uniform(-1, 1, cc.slots) * 3e6  # x 2^50 scale -> coefficients near 2^70
+    pt = cc.MakeCKKSPackedPlaintext(big)
+    assert np.max(np.abs(pt.GetRealPackedValue() - big)) < 1e-6 * 3e6
+    x = _msg(cc.slots, 6)
+    ct = cc.EvalAdd(cc.Encrypt(cc.MakeCKKSPackedPlaintext(x)), pt)
+    assert np.max(np.abs(cc.Decrypt(ct).GetRealPackedValue() - (x + big))) < 1e-5 * 3e6

@@ -35,3 +35,32 @@ def test_two_tokens_match_plaintext_polynomial_path():
         err = np.max(np.abs(got - want))
         assert err < 2e-3, (token, err)
     assert layer.refreshes >= 1
+
+
+def test_greedy_token_loop_matches_plaintext():
+    """Two-layer model: prompt of 2 tokens then 2 generated tokens; the
+    encrypted loop picks the same tokens as the plaintext polynomial path and
+    its final hidden vectors agree."""
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    from fhe_mamba_b200.mamba2_layer import EncryptedMamba2Model, Mamba2Model
+    m = Mamba2Model(layers=2, d_model=64, d_state=32, heads=16, vocab=128, std=0.1)
+    cc = CryptoContext(CCParams(ring_dim=1 << 12, multiplicative_depth=44, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3))
+    cc.KeyGen(41)
+    cc.EvalBootstrapSetup((4, 4))
+    cc.EvalBootstrapKeyGen()
+    em = EncryptedMamba2Model(cc, m)
+    cc.EvalRotateKeyGen(em.rotation_steps())
+    state = m.initial_state()
+    prompt, generated = [3, 17], 2
+    token, plain_tokens, enc_tokens = None, [], []
+    for i in range(len(prompt) + generated - 1):
+        tok = prompt[i] if i < len(prompt) else token
+        hf, logits, state = m.plain_token(tok, state)
+        token = int(np.argmax(logits))
+        enc_tok, ehf = em.select(em.step(tok))
+        assert np.max(np.abs(ehf - hf)) < 1e-3, i
+        if i >= len(prompt) - 1:
+            plain_tokens.append(token)
+            enc_tokens.append(enc_tok)
+    assert enc_tokens == plain_tokens
