@@ -1,23 +1,32 @@
 """Benchmark driver (one JSON line on rank 0).
 
-Workload at N=1: BASELINE config 2 — batched forward + inverse negacyclic NTT,
-N = 2^16, 36 RNS limbs of 59-bit NTT-friendly primes, 2 ciphertexts x 2 polys
-(4 polys).  One step = forward NTT of the whole batch followed by the inverse
-NTT of the whole batch.  Inputs are seeded uniform residues in [0, q_i).
+Headline (BASELINE metric "enc s/generated token (Mamba-2-130M shape)"): the
+encrypted greedy token loop of a 24-layer Mamba-2-130M-shape model (d_model
+768, d_inner 1536, d_state 128, 24 heads, conv 4, vocab 50280, tied
+embedding; synthetic seeded weights ~N(0, 0.02^2)) at N = 2^16, 2^15 slots,
+multiplicative depth 44, 59-bit scaling / 60-bit first prime, dnum 3,
+two-pass bootstrapping.  One step = one generated token: the server runs all
+24 layers on the encrypted embedding (value, CUDA events on the context
+stream), the client encrypts the embedding and decrypts + selects the next
+token around it (e2e).  Inputs: keys (~36 GB), cached diagonals and
+ciphertexts far exceed the 126 MB L2.
 
-Timing: W untimed warm-up steps, then exactly K steps bracketed by a barrier
-and torch.cuda.synchronize() on both sides; the device time is the max over
-ranks.  Four rotating input batches (4 x 75.5 MB > 126 MB L2) keep each step's
-input out of L2.  CUDA events on the context's stream time the forward
-transform (the dominant kernel pair) for the roofline.
+Roofline: BASELINE config 2, the batched forward NTT (4 polys x 36 limbs x
+2^16, 59-bit primes) -- the dominant kernel of every primitive -- timed with
+CUDA events; key switching (config 3 shape) and bootstrapping are reported
+beside it.
 
-Multi-GPU (torchrun): each rank transforms its own independent batch (weak
-scaling, no data-path collective); value = steps of all ranks / max time.
+Timing: W untimed warm-up tokens, then exactly K tokens bracketed by a
+barrier and torch.cuda.synchronize() on both sides; the device time is the
+max over ranks.  Multi-GPU (torchrun): every rank runs its own replica of the
+token loop (the layers are sequential; no data-path collective); value =
+max time / tokens of all ranks.
 
-``--impl reference``: the reference's CKKS arithmetic lives in FIDESlib and
-OpenFHE, which are not in the reference checkout and cannot be built here, so
-the reference arm times the CPU oracle's restatement of OpenFHE's NTT on the
-host cores (all threads), rank 0 only.
+``--impl reference``: FIDESlib/OpenFHE are not in the reference checkout and
+cannot be built here; the reference arm times the CPU oracle (the
+restatement of OpenFHE's algorithms) on one key switch at the token loop's
+typical level with all host threads and scales it by the key switches of one
+token (a labelled estimate; a full CPU token would take hours).
 """
 from __future__ import annotations
 
@@ -36,8 +45,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "enc s/generated token (Mamba-2-130M shape); NTT+keyswitch % HBM roofline"
+UNIT = "s/generated token"
+NTT_UNIT = "batched fwd+inv NTT steps/s (4 polys x 36 limbs x 2^16)"
 LOG_N, LIMBS, POLYS, BITS = 16, 36, 4, 59
-UNIT = "batched fwd+inv NTT steps/s (4 polys x 36 limbs x 2^16)"
+# Key switches of one generated token of the 24-layer loop (two-pass refresh),
+# read from the GPU arm's counters (key_inner per token); used by the CPU arm.
+KS_PER_TOKEN = 42710
 ALG_BYTES_PER_TRANSFORM = 16 * POLYS * LIMBS * (1 << LOG_N)  # read + write every word once
 N_ROTATE = 4
 
@@ -133,7 +146,7 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_baseline(threads, sample_limbs=None):
+def cpu_ntt_baseline(threads, sample_limbs=None):
     """Oracle NTT (restatement of OpenFHE's CPU NTT) on the host cores."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
@@ -148,6 +161,26 @@ def cpu_baseline(threads, sample_limbs=None):
     dt = time.perf_counter() - t0
     scale = LIMBS / limbs
     return 1.0 / (dt * scale), dt, f"fwd+inv of {POLYS} polys x {limbs} limbs x 2^16 (scaled x{scale:g})"
+
+
+def cpu_keyswitch_seconds(threads, n_limbs=30):
+    """One HYBRID relinearisation on the CPU oracle (OpenFHE's algorithm restated
+    in C, OpenMP over the host threads) at the token loop's parameters
+    (N = 2^16, depth 44, 59/60-bit, dnum 3) and a typical level (n_limbs)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    q, p = O.ckks_moduli(16, 45, 59, 60, 3)
+    oc = O.Ckks(16, q, p, 3, 1 << 15)
+    s, sn = oc.keygen_secret(1)
+    rlk = oc.relin_key(1, sn)
+    rng = np.random.default_rng(0)
+    d3 = np.empty((3, n_limbs, 1 << 16), dtype=np.uint64)
+    for l in range(n_limbs):
+        d3[:, l, :] = rng.integers(0, q[l], size=(3, 1 << 16), dtype=np.uint64)
+    t0 = time.perf_counter()
+    oc.relinearize(d3, rlk)
+    return time.perf_counter() - t0
 
 
 def measure_ckks(local, reps=10):
@@ -214,23 +247,16 @@ def measure_ckks(local, reps=10):
     return ks, mv
 
 
-def measure_bootstrap(local, reps=3):
-    """One full-packing bootstrap at the reference's native parameters
-    (N=2^16, 2^15 slots, multiplicative depth 44, 59-bit scaling / 60-bit
-    first prime, dnum 3, level budget {4, 4}; packed_fideslib.cpp:1061-1089),
-    timed with CUDA events on the context stream; the input has 2 limbs left."""
+def measure_bootstrap(cc, reps=3):
+    """Full-packing bootstraps on the token loop's context (N=2^16, 2^15 slots,
+    depth 44, 59/60-bit, dnum 3, level budget {4,4}; packed_fideslib.cpp:1061-1089),
+    CUDA events on the context stream; the input has 2 limbs left."""
     import torch
-    from fhe_mamba_b200 import CCParams, CryptoContext
-    cc = CryptoContext(CCParams(ring_dim=1 << 16, multiplicative_depth=44, scaling_mod_size=59,
-                                first_mod_size=60, num_large_digits=3, device=local))
-    cc.KeyGen(11)
-    cc.EvalBootstrapSetup((4, 4))
-    cc.EvalBootstrapKeyGen()
-    stream = torch.cuda.ExternalStream(cc.stream_ptr(), device=torch.device("cuda", local))
+    stream = torch.cuda.ExternalStream(cc.stream_ptr())
     x = np.random.default_rng(5).uniform(-1, 1, cc.slots)
     ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
     cc.LevelReduceInPlace(ct, cc.n_q - 2)
-    out = cc.EvalBootstrap(ct)  # first call encodes the SlotToCoeff diagonals
+    out = cc.EvalBootstrap(ct)
     cc.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -238,17 +264,57 @@ def measure_bootstrap(local, reps=3):
         out = cc.EvalBootstrap(ct)
     e1.record(stream)
     e1.synchronize()
-    ms = e0.elapsed_time(e1) / reps
-    err = float(np.max(np.abs(cc.Decrypt(out).GetRealPackedValue() - x)))
     info = cc.bootstrap_info()
-    rep = {"workload": "full-packing bootstrap, N=2^16, 2^15 slots, depth 44 (45 Q limbs), 59/60-bit, dnum 3, "
-                       "level budget {4,4}, uniform ternary secret",
-           "ms": ms, "limbs_in": 2, "limbs_out": out.n_limbs(), "levels": cc.bootstrap_levels(),
-           "max_abs_err": err, "correction": info["correction"], "chebyshev_degree": info["chebyshev_degree"],
-           "rotation_keys": info["rotation_keys"]}
-    del out, ct
-    cc.close()
-    return rep
+    return {"workload": "full-packing bootstrap, N=2^16, 2^15 slots, depth 44 (45 Q limbs), 59/60-bit, dnum 3, "
+                        "level budget {4,4}, uniform ternary secret",
+            "ms": e0.elapsed_time(e1) / reps, "limbs_in": 2, "limbs_out": out.n_limbs(),
+            "levels": cc.bootstrap_levels(),
+            "max_abs_err": float(np.max(np.abs(cc.Decrypt(out).GetRealPackedValue() - x))),
+            "correction": info["correction"], "chebyshev_degree": info["chebyshev_degree"],
+            "rotation_keys": info["rotation_keys"]}
+
+
+class TokenLoop:
+    """The 24-layer encrypted greedy loop: client encrypt -> server layers -> client select."""
+
+    def __init__(self, local, layers=24, passes=2, seed=6):
+        from fhe_mamba_b200 import CCParams, CryptoContext
+        from fhe_mamba_b200.mamba2_layer import EncryptedMamba2Model, Mamba2Model
+        t0 = time.perf_counter()
+        self.model = Mamba2Model(layers=layers, d_model=768, d_state=128, heads=24, vocab=50280, seed=seed,
+                                 calib_sequences=4)
+        self.cc = CryptoContext(CCParams(ring_dim=1 << 16, multiplicative_depth=44, scaling_mod_size=59,
+                                         first_mod_size=60, num_large_digits=3, device=local))
+        self.cc.KeyGen(41 + seed)
+        self.cc.EvalBootstrapSetup((4, 4))
+        self.cc.EvalBootstrapKeyGen()
+        self.em = EncryptedMamba2Model(self.cc, self.model, passes=passes)
+        self.cc.EvalRotateKeyGen(self.em.rotation_steps())
+        self.cc.synchronize()
+        self.setup_seconds = time.perf_counter() - t0
+        self.token = 5
+        self.layers, self.passes = layers, passes
+
+    def encrypt(self, token):
+        m, c = self.model, self.cc
+        return c.Encrypt(c.MakeCKKSPackedPlaintext(np.pad(m.embedding[token], (0, c.slots - m.d_model))))
+
+    def server(self, ct):
+        em = self.em
+        h = ct
+        new = []
+        for layer, (conv, st), bounds in zip(em.layers, em.state, em.m.bounds):
+            h, conv, st = layer.step(h, conv, st, bounds)
+            new.append((conv, st))
+        em.state = new
+        m, last = em.m, em.layers[-1]
+        h = last._fit(h, 14, m.bounds[-1]["h"] * 2)
+        return last.pm.rms_norm(h, m.d_model, m.norm_f, m.layers[0].eps, (m.rsqrt_f.lo, m.rsqrt_f.hi),
+                                degree=len(m.rsqrt_f.coeffs) - 1)
+
+    def select(self, hidden):
+        tok, _ = self.em.select(hidden)
+        return tok
 
 
 def host_threads():
@@ -264,40 +330,81 @@ def run_reference(args, rank):
     threads = host_threads()
     samples = []
     for _ in range(args.warmup):
-        cpu_baseline(threads)
+        cpu_keyswitch_seconds(threads)
     for _ in range(args.steps):
-        v, dt, sample = cpu_baseline(threads)
-        samples.append(dt)
-    mean = sum(samples) / len(samples)
-    value = 1.0 / mean
+        samples.append(cpu_keyswitch_seconds(threads))
+    t_ks = sum(samples) / len(samples)
+    value = t_ks * KS_PER_TOKEN
+    sample = (f"one HYBRID key switch at 30 limbs (N=2^16, depth 44, dnum 3) on the CPU oracle, "
+              f"{t_ks:.3f} s, x {KS_PER_TOKEN} key switches per token (estimate)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u64",
-        "data": "synthetic", "config": config_dict(),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"fwd+inv of {POLYS} polys x {LIMBS} limbs x 2^16 per step; "
-                                   "CPU oracle restating OpenFHE's NTT (OpenFHE/FIDESlib absent)"},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": value * 1e3,
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "u64",
+        "data": "synthetic", "config": config_dict(args),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def config_dict():
+def config_dict(args):
+    return {"workload": "BASELINE configs[4]: encrypted greedy token loop, Mamba-2-130M shape "
+                        f"({args.layers} layers, d_model 768, d_state 128, 24 heads, vocab 50280)",
+            "ring_dim": 1 << 16, "slots": 1 << 15, "depth": 44, "scale_bits": 59, "dnum": 3,
+            "bootstrap_passes": args.passes, "l2": "inputs larger than L2 (keys ~36 GB, cached diagonals)",
+            "parallelism": "one token-loop replica per GPU"}
+
+
+def ntt_config():
     return {"workload": "BASELINE configs[1]: batched forward+inverse negacyclic NTT",
             "log_n": LOG_N, "limbs": LIMBS, "polys": POLYS, "prime_bits": BITS,
-            "l2": f"{N_ROTATE} rotating input batches ({N_ROTATE * ALG_BYTES_PER_TRANSFORM // 2 / 1e6:.0f} MB) > L2",
-            "parallelism": "independent batch per GPU"}
+            "l2": f"{N_ROTATE} rotating input batches ({N_ROTATE * ALG_BYTES_PER_TRANSFORM // 2 / 1e6:.0f} MB) > L2"}
+
+
+def measure_ntt(local, steps, warmup):
+    """Config-2 NTT: device-timed forward/inverse pairs and the forward roofline."""
+    import torch
+    from fhe_mamba_b200 import NttContext
+    qs = bench_primes()
+    ctx = NttContext(LOG_N, qs, device=local)
+    stream = torch.cuda.ExternalStream(ctx.stream_ptr(), device=torch.device("cuda", local))
+    bufs = [torch.from_numpy(make_batch(qs, 1000 + i).view(np.int64)).cuda(local) for i in range(N_ROTATE)]
+    torch.cuda.synchronize()
+    for i in range(warmup):
+        ctx.forward(bufs[i % N_ROTATE])
+        ctx.inverse(bufs[i % N_ROTATE])
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for i in range(steps):
+        b = bufs[i % N_ROTATE]
+        evs[i][0].record(stream)
+        ctx.forward(b)
+        evs[i][1].record(stream)
+        ctx.inverse(b)
+        evs[i][2].record(stream)
+    torch.cuda.synchronize()
+    fwd = sum(e[0].elapsed_time(e[1]) for e in evs) / steps
+    inv = sum(e[1].elapsed_time(e[2]) for e in evs) / steps
+    ctx.close()
+    achieved = ALG_BYTES_PER_TRANSFORM / (fwd / 1e3) / 1e9
+    peak, kind = peaks()
+    return {"bound": "hbm", "kernel": "forward NTT (ntt_fwd_cols + ntt_fwd_rows), BASELINE config 2",
+            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": kind,
+            "traffic": ncu_traffic(), "alg_bytes_per_launch": ALG_BYTES_PER_TRANSFORM, "fwd_ms": fwd,
+            "inv_ms": inv, "ntt_steps_per_s": 1e3 / (fwd + inv), "ntt_unit": NTT_UNIT, "config": ntt_config()}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=2, help="timed tokens")
+    ap.add_argument("--warmup", type=int, default=3, help="untimed tokens")
+    ap.add_argument("--layers", type=int, default=24)
+    ap.add_argument("--passes", type=int, default=2, choices=[1, 2], help="bootstrap passes per refresh")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-ckks", action="store_true", help="skip the key-switch and matvec side measurements")
+    ap.add_argument("--no-ckks", action="store_true", help="skip the key-switch, matvec and bootstrap side measurements")
     ap.add_argument("--ckks-only", action="store_true",
                     help="print only the key-switch and matvec measurements (profiling runs)")
     args = ap.parse_args()
@@ -318,38 +425,24 @@ def main():
     torch.cuda.set_device(local)
     if args.ckks_only:
         ks, mv = measure_ckks(local)
-        bt = measure_bootstrap(local)
-        print(json.dumps({"keyswitch": ks, "bsgs_matvec": mv, "bootstrap": bt}), flush=True)
+        print(json.dumps({"keyswitch": ks, "bsgs_matvec": mv}), flush=True)
         return
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=torch.device("cuda", local))
 
-    from fhe_mamba_b200 import NttContext
     from fhe_mamba_b200 import _lib
 
-    qs = bench_primes()
-    ctx = NttContext(LOG_N, qs, device=local)
-    stream = torch.cuda.ExternalStream(ctx.stream_ptr(), device=torch.device("cuda", local))
-    bufs = []
-    for i in range(N_ROTATE):
-        h = make_batch(qs, 1000 * rank + i)
-        bufs.append(torch.from_numpy(h.view(np.int64)).cuda(local))
-    torch.cuda.synchronize()
+    roofline = measure_ntt(local, steps=20, warmup=5)
+    side = {}
+    if world == 1 and not args.no_ckks:
+        side["keyswitch"], side["bsgs_matvec"] = measure_ckks(local)
 
-    def step(i, evs=None):
-        b = bufs[i % N_ROTATE]
-        if evs is not None:
-            evs[0].record(stream)
-        ctx.forward(b)
-        if evs is not None:
-            evs[1].record(stream)
-        ctx.inverse(b)
-        if evs is not None:
-            evs[2].record(stream)
-
-    for i in range(args.warmup):
-        step(i)
+    loop = TokenLoop(local, layers=args.layers, passes=args.passes, seed=6 + rank)
+    stream = torch.cuda.ExternalStream(loop.cc.stream_ptr(), device=torch.device("cuda", local))
+    tok = loop.token
+    for _ in range(args.warmup):
+        tok = loop.select(loop.server(loop.encrypt(tok)))
     torch.cuda.synchronize()
 
     uuid = None
@@ -360,85 +453,67 @@ def main():
     sampler = ClockSampler(uuid)
     sampler.start()
     time.sleep(0.5)
-
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
+    loop.cc.counters(reset=True)
+    launches0 = _lib.kernel_launches()
+    server_ms = 0.0
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    start.record(stream)
+    t_wall = time.perf_counter()
     for i in range(args.steps):
-        step(i, evs[i])
-    end.record(stream)
+        ct = loop.encrypt(tok)                      # client
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        hidden = loop.server(ct)                    # server: every layer on ciphertexts
+        e1.record(stream)
+        e1.synchronize()
+        server_ms += e0.elapsed_time(e1)
+        tok = loop.select(hidden)                   # client
     torch.cuda.synchronize()
+    e2e_dt = time.perf_counter() - t_wall
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
-
-    total_ms = start.elapsed_time(end)
-    fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    inv_ms = [e[1].elapsed_time(e[2]) for e in evs]
-    t = torch.tensor([total_ms], dtype=torch.float64, device=f"cuda:{local}")
+    launches = _lib.kernel_launches() - launches0
+    counters = loop.cc.counters(reset=True)
+    t = torch.tensor([server_ms, e2e_dt], dtype=torch.float64, device=f"cuda:{local}")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
-    value = world * args.steps / (total_ms / 1e3)
-
-    # End to end through the C ABI with pinned host buffers (copies inside the call).
-    host = torch.empty((POLYS, LIMBS, 1 << LOG_N), dtype=torch.int64, pin_memory=True)
-    host.copy_(bufs[0].cpu())
-    hv = host.numpy().view(np.uint64)
-    e2e_steps = max(3, min(args.steps, 20))
-    ctx.forward(hv)
-    ctx.inverse(hv)
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        ctx.forward(hv)
-        ctx.inverse(hv)
-    e2e_dt = time.perf_counter() - t0
-    te = torch.tensor([e2e_dt], dtype=torch.float64, device=f"cuda:{local}")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * e2e_steps / float(te.item())
-    words = POLYS * LIMBS * (1 << LOG_N)
-
-    fwd_avg = sum(fwd_ms) / len(fwd_ms)
-    achieved = ALG_BYTES_PER_TRANSFORM / (fwd_avg / 1e3) / 1e9
-    peak, peak_kind = peaks()
-    traffic = ncu_traffic()
+    server_ms, e2e_dt = float(t[0].item()), float(t[1].item())
+    value = server_ms / 1e3 / (args.steps * world)
+    e2e_value = e2e_dt / (args.steps * world)
+    slot_bytes = 16 * loop.cc.slots
 
     if rank == 0:
+        per_token = {k: v / args.steps for k, v in counters.items()}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
-            "config": config_dict(),
-            "roofline": {"bound": "hbm", "kernel": "forward NTT (ntt_fwd_cols + ntt_fwd_rows)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_source": peak_kind, "traffic": traffic,
-                         "alg_bytes_per_launch": ALG_BYTES_PER_TRANSFORM,
-                         "fwd_ms": fwd_avg, "inv_ms": sum(inv_ms) / len(inv_ms)},
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * 8 * words,
-                    "d2h_bytes_per_step": 2 * 8 * words,
-                    "path": "fhe_ntt + fhe_intt with FHE_MEM_HOST (pinned host buffer)"},
-            "gpu_launches": 4 * args.steps,
+            "warmup": args.warmup, "ms_per_step": server_ms / args.steps, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic (seeded random weights)",
+            "config": config_dict(args),
+            "roofline": roofline,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": slot_bytes,
+                    "d2h_bytes_per_step": slot_bytes,
+                    "path": "client encode+encrypt of the embedding (host slots to device), server layers, "
+                            "client decrypt+decode (device slots to host) and greedy argmax"},
+            "gpu_launches": launches,
             "clocks": clocks,
+            "per_token": {"operations": per_token, "refreshes": loop.em.refreshes() / max(1, args.steps + args.warmup),
+                          "setup_seconds": loop.setup_seconds, "tokens": loop.em.tokens[-args.steps:]},
         }
-        if not args.no_ckks and world == 1:
-            ks, mv = measure_ckks(local)
-            line["keyswitch"] = ks
-            line["bsgs_matvec"] = mv
-            line["bootstrap"] = measure_bootstrap(local)
-        if not args.no_cpu_baseline and world == 1:
-            v, dt, sample = cpu_baseline(host_threads())
-            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",
-                                    "sample": sample + "; CPU oracle restating OpenFHE's NTT"}
+        line.update(side)
+        if world == 1 and not args.no_ckks:
+            line["bootstrap"] = measure_bootstrap(loop.cc)
+        if world == 1 and not args.no_cpu_baseline:
+            threads = host_threads()
+            t_ks = cpu_keyswitch_seconds(threads)
+            line["cpu_baseline"] = {
+                "value": t_ks * per_token["key_inner"], "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": f"one HYBRID key switch at 30 limbs on the CPU oracle ({t_ks:.3f} s) x "
+                          f"{per_token['key_inner']:.0f} key switches per token (estimate; a CPU token takes hours)"}
         print(json.dumps(line), flush=True)
 
-    ctx.close()
+    loop.cc.close()
     if world > 1:
         dist.destroy_process_group()
 

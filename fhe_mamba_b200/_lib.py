@@ -119,6 +119,8 @@ SIGNATURES = {
     "fhe_rescale_noalloc": [vp, vp, u32, u32, vp],
     "fhe_encode_batch": [vp, PD, PD, u32, u32, u32, f64, ctypes.POINTER(vp)],
     "fhe_linear_transform": [vp, vp, ctypes.POINTER(vp), u32, u32, i32, i32, ctypes.POINTER(vp)],
+    "fhe_ctx_counters": [vp, vp, i32],
+    "fhe_kernel_launches": [ctypes.POINTER(ctypes.c_uint64)],
     "fhe_bootstrap_setup": [vp, u32, u32, u32, i32, i32],
     "fhe_bootstrap_keygen": [vp],
     "fhe_bootstrap": [vp, vp, ctypes.POINTER(vp)],
@@ -181,3 +183,10 @@ def check(code: int, fn: str) -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args), name)
+
+
+def kernel_launches() -> int:
+    """Kernels launched by libfhe_b200 in this process so far."""
+    c = ctypes.c_uint64()
+    call("fhe_kernel_launches", ctypes.byref(c))
+    return c.value

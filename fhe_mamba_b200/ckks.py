@@ -299,6 +299,15 @@ class CryptoContext:
         """0 = scale down and ModRaise, 1 = CoeffToSlot, 2 = EvalMod, 3 = SlotToCoeff."""
         return self._ct("fhe_bootstrap_stage", int(stage), ct.handle)
 
+    _COUNTERS = ("tensor", "relin", "rotations", "modup", "moddown", "key_inner", "rescales", "ntt_limbs",
+                 "bootstraps")
+
+    def counters(self, reset: bool = False) -> dict:
+        """Operation counters since creation or the last reset."""
+        a = (ctypes.c_uint64 * len(self._COUNTERS))()
+        call("fhe_ctx_counters", self.h, ctypes.cast(a, vp), int(reset))
+        return dict(zip(self._COUNTERS, (int(v) for v in a)))
+
     def bootstrap_info(self):
         c, d, k = ctypes.c_int32(), ctypes.c_uint32(), ctypes.c_uint32()
         call("fhe_bootstrap_info", self.h, ctypes.byref(c), ctypes.byref(d), ctypes.byref(k))

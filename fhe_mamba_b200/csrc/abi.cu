@@ -14,6 +14,7 @@
 #include "ckks.h"
 #include "context.h"
 #include "program.h"
+#include "launch_count.h"
 
 namespace fhe {
 void rescale_noalloc(Context& c, const uint64_t* in, uint32_t ncomp, uint32_t nq, uint64_t* out);
@@ -552,6 +553,23 @@ int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* dia
     std::vector<const fhe::Pt*> d((size_t)baby * giant);
     for (size_t i = 0; i < d.size(); ++i) d[i] = diags[i] ? diags[i]->p.get() : nullptr;
     put_ct(out, k.linear_transform(ct_of(a), d, baby, giant, stride, giant_offset));
+  });
+}
+
+int fhe_kernel_launches(uint64_t* count) {
+  if (!count) return FHE_ERR_INVALID;
+  *count = fhe::g_kernel_launches.load();
+  return FHE_OK;
+}
+
+int fhe_ctx_counters(fhe_ctx* ctx, fhe_counters* out, int32_t reset) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(out != nullptr, "null counters");
+    const fhe::Counters& c = k.counters;
+    *out = fhe_counters{c.tensor, c.relin, c.rotations, c.modup, c.moddown, c.key_inner, c.rescales, c.ntt_limbs,
+                        c.bootstraps};
+    if (reset) k.counters = fhe::Counters{};
   });
 }
 

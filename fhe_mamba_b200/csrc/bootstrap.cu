@@ -309,6 +309,7 @@ std::unique_ptr<Ct> Bootstrapper::slot_to_coeff(const Ct& w) {
 }
 
 std::unique_ptr<Ct> Bootstrapper::bootstrap(const Ct& a) {
+  ++ck_.counters.bootstraps;
   if (p_.s2c_first) {
     // SlotToCoeff first: the slots z become the plaintext's coefficients
     // (BR(z) / (2 pi) as lo + i hi); after ModRaise and CoeffToSlot the slots

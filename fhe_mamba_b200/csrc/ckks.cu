@@ -92,6 +92,7 @@ uint64_t* Ckks::ws(size_t idx, size_t words) {
 
 void Ckks::ntt_dense(uint64_t* d, uint32_t polys, uint32_t limbs, uint32_t stride, uint32_t prime0, bool inv) {
   if (!polys || !limbs) return;
+  counters.ntt_limbs += (uint64_t)polys * limbs;
   NttArgs a = ctx.ntt_args(d, polys, prime0, limbs, stride);
   FHE_CUDA(inv ? ntt_inverse(a) : ntt_forward(a));
 }
@@ -542,7 +543,9 @@ void Ckks::modup(const uint64_t* d, uint32_t nq, uint64_t* ext) {
   ntt_dense(coef, 1, nq, nq, 0, true);
   launch_modup(coef, d, ext, nq, ctx.K, n, T.digits.as<ModUpDigit>(), T.D, ctx.alpha, ctx.d_mod.as<Modulus>(),
                ctx.stream);
+  ++counters.modup;
   if (T.ntt_list_len) {
+    counters.ntt_limbs += T.ntt_list_len;
     NttArgs a = ctx.ntt_args(ext, 1, 0, T.ntt_list_len, 0);
     a.list = T.ntt_list.as<uint2>();
     a.lazy = ctx.max_prime() < (uint64_t(1) << 60) ? 16 : 0;  // the list spans Q and P primes
@@ -554,6 +557,7 @@ void Ckks::modup(const uint64_t* d, uint32_t nq, uint64_t* ext) {
 void Ckks::moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, const uint64_t* add_c0) {
   const uint32_t n = ctx.n, K = ctx.K, w = nq + K;
   LevelTables& T = level(nq);
+  ++counters.moddown;
   ntt_dense(acc + (size_t)nq * n, 2, K, w, ctx.L, true);
   uint64_t* conv = ws(3, (size_t)2 * ctx.L * n);
   launch_convert(acc + (size_t)nq * n, (size_t)w * n, conv, (size_t)nq * n, 2, T.moddown.as<ConvTable>(), K, nq, n,
@@ -570,6 +574,7 @@ void Ckks::keyswitch(const uint64_t* d, uint32_t nq, const uint64_t* evk, uint64
   uint64_t* ext = ws(0, (size_t)T.D * w * n);
   uint64_t* acc = ws(2, (size_t)2 * (ctx.L + K) * n);
   modup(d, nq, ext);
+  ++counters.key_inner;
   launch_key_inner(ext, T.D, w, evk, ctx.L + K, PrimeMap{nq, ctx.L}, acc, n, ctx.d_mod.as<Modulus>(), ctx.stream);
   moddown_pair(acc, nq, out, so, add_c0);
 }
@@ -581,6 +586,7 @@ std::unique_ptr<Ct> Ckks::relinearize(const Ct& d) {
   const size_t cs = (size_t)d.cap * n;
   auto out = alloc(nq, 2);
   const size_t so = (size_t)nq * n;
+  ++counters.relin;
   keyswitch(d.data() + 2 * cs, nq, rlk_.as<uint64_t>(), out->data(), so, nullptr);
   launch_ew(Ew::Add, out->data(), so, d.data(), cs, out->data(), so, 2, nq, n, PrimeMap{nq, ctx.L},
             ctx.d_mod.as<Modulus>(), ctx.stream);
@@ -596,6 +602,7 @@ std::unique_ptr<Ct> Ckks::rotate(const Ct& a, uint64_t g) {
   const uint32_t nq = a.nq, n = ctx.n;
   const size_t cs = (size_t)a.cap * n, so = (size_t)nq * n;
   uint64_t* u = ws(4, 2 * so);
+  ++counters.rotations;
   keyswitch(a.data() + cs, nq, it->second.as<uint64_t>(), u, so, a.data());
   auto out = alloc(nq, 2);
   launch_automorphism(u, so, out->data(), so, 2, nq, ctx.log_n, g, ctx.stream);
@@ -616,6 +623,8 @@ std::vector<std::unique_ptr<Ct>> Ckks::rotate_hoisted(const Ct& a, const std::ve
   uint64_t* acc = ws(2, (size_t)2 * (ctx.L + K) * n);
   uint64_t* u = ws(4, 2 * so);
   for (uint64_t g : gs) {
+    ++counters.rotations;
+    ++counters.key_inner;
     launch_key_inner(ext, T.D, w, rot_.at(g).as<uint64_t>(), ctx.L + K, PrimeMap{nq, ctx.L}, acc, n,
                      ctx.d_mod.as<Modulus>(), ctx.stream);
     moddown_pair(acc, nq, u, so, a.data());
@@ -672,6 +681,7 @@ std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a_in, const std::vector<con
       auto it = rot_.find(gal);
       require(it != rot_.end(), "missing rotation key for giant step " + std::to_string(amount), -4);
       uint64_t* u = ws(4, 2 * cs);
+      ++counters.rotations;
       keyswitch(ig + cs, nq, it->second.as<uint64_t>(), u, cs, ig);
       uint64_t* r = ws(22, 2 * cs);
       launch_automorphism(u, cs, r, cs, 2, nq, ctx.log_n, gal, ctx.stream);
@@ -819,6 +829,7 @@ std::unique_ptr<Ct> Ckks::tensor(const Ct& a, const Ct& b) {
   require(a.nq == b.nq, "tensor operands must have the same number of limbs", -1);
   const uint32_t nq = a.nq, n = ctx.n;
   auto d = alloc(nq, 3);
+  ++counters.tensor;
   launch_tensor(a.data(), (size_t)a.cap * n, b.data(), (size_t)b.cap * n, d->data(), (size_t)nq * n, nq, n,
                 ctx.d_mod.as<Modulus>(), ctx.stream);
   d->scale = a.scale * b.scale;
@@ -842,6 +853,7 @@ void Ckks::rescale_into(const Ct& a, Ct& o) {
   require(a.nq >= 2, "rescale: no limb left to drop (level underflow)", -4);
   const uint32_t nq = a.nq, n = ctx.n, nc = a.ncomp;
   const size_t cs = (size_t)a.cap * n, os = (size_t)o.cap * n;
+  ++counters.rescales;
   uint64_t* last = ws(6, (size_t)nc * n);
   FHE_CUDA(cudaMemcpy2DAsync(last, (size_t)n * 8, a.data() + (size_t)(nq - 1) * n, cs * 8, (size_t)n * 8, nc,
                              cudaMemcpyDeviceToDevice, ctx.stream));

@@ -43,10 +43,18 @@ struct LevelTables {
   DevMem moddown;   // ConvTable (P -> Q_nq)
 };
 
+// Operation counters (the reference's native.json ct_ct / rotations /
+// bootstraps fields plus the key-switching work behind them).
+struct Counters {
+  uint64_t tensor = 0, relin = 0, rotations = 0, modup = 0, moddown = 0, key_inner = 0, rescales = 0,
+           ntt_limbs = 0, bootstraps = 0;
+};
+
 class Ckks {
  public:
   explicit Ckks(Context& c);
   Context& ctx;
+  Counters counters;
 
   // FLEXIBLEAUTO scaling factor of a fresh ciphertext with nq live limbs.
   double level_scale(uint32_t nq) const { return sf_[ctx.L - nq]; }

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include "ckks_kernels.h"
+#include "launch_count.h"
 
 namespace fhe {
 namespace {
@@ -550,68 +551,68 @@ uint32_t log2u(uint32_t x) {
 }  // namespace
 
 void launch_sample_small(int kind, uint64_t seed, uint64_t stream, int64_t* out, uint32_t n, cudaStream_t s) {
-  k_sample_small<<<grid1(n / 8), kTpb, 0, s>>>(kind, seed, stream, out, n);
+  k_sample_small<<<grid1(n / 8), kTpb, 0, s>>>(kind, seed, stream, out, n); note_launch();
 }
 
 void launch_lift_small(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
                        const Modulus* mods, cudaStream_t s) {
   if (!nlimbs) return;
-  k_lift_small<<<grid1(n, nlimbs), kTpb, 0, s>>>(src, out, n, pm, mods);
+  k_lift_small<<<grid1(n, nlimbs), kTpb, 0, s>>>(src, out, n, pm, mods); note_launch();
 }
 
 void launch_sample_uniform(uint64_t seed, uint64_t stream, uint64_t* out, uint32_t n, uint32_t nlimbs,
                            PrimeMap pm, const Modulus* mods, cudaStream_t s) {
   if (!nlimbs) return;
-  k_sample_uniform<<<grid1(n / 4, nlimbs), kTpb, 0, s>>>(seed, stream, out, n, pm, mods);
+  k_sample_uniform<<<grid1(n / 4, nlimbs), kTpb, 0, s>>>(seed, stream, out, n, pm, mods); note_launch();
 }
 
 void launch_ew(Ew op, const uint64_t* a, size_t sa, const uint64_t* b, size_t sb, uint64_t* out, size_t so,
                uint32_t ncomp, uint32_t nlimbs, uint32_t n, PrimeMap pm, const Modulus* mods, cudaStream_t s) {
   if (!nlimbs || !ncomp) return;
-  k_ew<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(op, a, sa, b, sb, out, so, n, pm, mods);
+  k_ew<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(op, a, sa, b, sb, out, so, n, pm, mods); note_launch();
 }
 
 void launch_mul_const(const uint64_t* a, size_t sa, const Shoup* c, const uint64_t* b, size_t sb, uint64_t* out,
                       size_t so, uint32_t ncomp, uint32_t nlimbs, uint32_t n, const uint64_t* primes,
                       cudaStream_t s) {
   if (!nlimbs || !ncomp) return;
-  k_mul_const<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, b, sb, out, so, n, primes);
+  k_mul_const<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, b, sb, out, so, n, primes); note_launch();
 }
 
 void launch_add_const(const uint64_t* a, size_t sa, const uint64_t* c, uint64_t* out, size_t so, uint32_t ncomp,
                       uint32_t nlimbs, uint32_t n, const uint64_t* primes, cudaStream_t s) {
   if (!nlimbs || !ncomp) return;
-  k_add_const<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, out, so, n, primes);
+  k_add_const<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, out, so, n, primes); note_launch();
 }
 
 void launch_mul_const_v(const uint64_t* a, size_t sa, const LimbShoup& c, uint64_t* out, size_t so, uint32_t ncomp,
                         uint32_t nlimbs, uint32_t n, const uint64_t* primes, cudaStream_t s) {
   if (!nlimbs || !ncomp) return;
-  k_mul_const_v<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, out, so, n, primes);
+  k_mul_const_v<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, out, so, n, primes); note_launch();
 }
 
 void launch_add_const_v(const uint64_t* a, size_t sa, const LimbWords& c, uint64_t* out, size_t so, uint32_t ncomp,
                         uint32_t nlimbs, uint32_t n, const uint64_t* primes, cudaStream_t s) {
   if (!nlimbs || !ncomp) return;
-  k_add_const_v<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, out, so, n, primes);
+  k_add_const_v<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, c, out, so, n, primes); note_launch();
 }
 
 void launch_linear_wsum(const WsumArgs& a, uint32_t m, const uint64_t* w, const LimbWords& add, int has_add,
                         uint64_t* out, size_t so, uint32_t ncomp, uint32_t nq, uint32_t n, const Modulus* mods,
                         cudaStream_t s) {
   if (!nq || !ncomp) return;
-  k_linear_wsum<<<grid1(n, nq, ncomp), kTpb, 0, s>>>(a, m, w, add, has_add, out, so, nq, n, mods);
+  k_linear_wsum<<<grid1(n, nq, ncomp), kTpb, 0, s>>>(a, m, w, add, has_add, out, so, nq, n, mods); note_launch();
 }
 
 void launch_tensor(const uint64_t* a, size_t sa, const uint64_t* b, size_t sb, uint64_t* d, size_t sd,
                    uint32_t nq, uint32_t n, const Modulus* mods, cudaStream_t s) {
-  k_tensor<<<grid1(n, nq), kTpb, 0, s>>>(a, sa, b, sb, d, sd, n, mods);
+  k_tensor<<<grid1(n, nq), kTpb, 0, s>>>(a, sa, b, sb, d, sd, n, mods); note_launch();
 }
 
 void launch_automorphism(const uint64_t* in, size_t si, uint64_t* out, size_t so, uint32_t ncomp,
                          uint32_t nlimbs, uint32_t log_n, uint64_t g, cudaStream_t s) {
   if (!nlimbs || !ncomp) return;
-  k_automorphism<<<grid1(1u << log_n, nlimbs, ncomp), kTpb, 0, s>>>(in, si, out, so, log_n, g);
+  k_automorphism<<<grid1(1u << log_n, nlimbs, ncomp), kTpb, 0, s>>>(in, si, out, so, log_n, g); note_launch();
 }
 
 void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t nq, uint32_t K, uint32_t n,
@@ -624,7 +625,7 @@ void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uin
     const dim3 grid = grid1(n, count, chunks);
     switch (ns) {
 #define FHE_CASE(NS) \
-  case NS: k_modup<NS><<<grid, kTpb, 0, s>>>(coef, dntt, ext, nq + K, n, digits_dev, digit0, mods); break;
+  case NS: k_modup<NS><<<grid, kTpb, 0, s>>>(coef, dntt, ext, nq + K, n, digits_dev, digit0, mods); break; note_launch();
       FHE_NS_CASES(FHE_CASE)
 #undef FHE_CASE
       default: break;
@@ -637,7 +638,7 @@ void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uin
 
 void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_t* evk, uint32_t key_limbs,
                       PrimeMap pm, uint64_t* acc, uint32_t n, const Modulus* mods, cudaStream_t s) {
-  k_key_inner<<<grid1(n, w), kTpb, 0, s>>>(ext, D, w, evk, key_limbs, pm, acc, n, mods);
+  k_key_inner<<<grid1(n, w), kTpb, 0, s>>>(ext, D, w, evk, key_limbs, pm, acc, n, mods); note_launch();
 }
 
 void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp, uint32_t ncomp,
@@ -647,7 +648,7 @@ void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_
   const dim3 grid = grid1(n, ncomp, chunks);
   switch (ns) {
 #define FHE_CASE(NS) \
-  case NS: k_convert<NS><<<grid, kTpb, 0, s>>>(src, s_comp, dst, d_comp, t_dev, n, mods); break;
+  case NS: k_convert<NS><<<grid, kTpb, 0, s>>>(src, s_comp, dst, d_comp, t_dev, n, mods); break; note_launch();
     FHE_NS_CASES(FHE_CASE)
 #undef FHE_CASE
     default: break;
@@ -658,66 +659,66 @@ void launch_moddown_combine(const uint64_t* x, size_t sx, const uint64_t* conv, 
                             const uint64_t* add, uint64_t* out, size_t so, uint32_t ncomp, uint32_t nq,
                             uint32_t n, const uint64_t* primes, cudaStream_t s) {
   if (!nq || !ncomp) return;
-  k_moddown_combine<<<grid1(n, nq, ncomp), kTpb, 0, s>>>(x, sx, conv, sc, pinv, add, out, so, n, primes);
+  k_moddown_combine<<<grid1(n, nq, ncomp), kTpb, 0, s>>>(x, sx, conv, sc, pinv, add, out, so, n, primes); note_launch();
 }
 
 void launch_rescale_lift(const uint64_t* last, size_t sl, uint64_t* lifted, size_t sd, uint32_t ncomp,
                          uint32_t nlimbs, uint32_t n, uint64_t q_last, const Modulus* mods, cudaStream_t s) {
   if (!nlimbs) return;
-  k_rescale_lift<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(last, sl, lifted, sd, n, q_last, mods);
+  k_rescale_lift<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(last, sl, lifted, sd, n, q_last, mods); note_launch();
 }
 
 void launch_fft_special_inv(double2* v, const double2* tw, uint32_t slots, uint32_t batch, cudaStream_t s) {
   for (uint32_t len = slots; len >= 2; len >>= 1)
-    k_fft_inv_stage<<<grid1(slots / 2, batch), kTpb, 0, s>>>(v, tw, slots, len);
+    { k_fft_inv_stage<<<grid1(slots / 2, batch), kTpb, 0, s>>>(v, tw, slots, len); note_launch(); }
 }
 
 void launch_fft_special_fwd(double2* v, const double2* tw, uint32_t slots, uint32_t batch, cudaStream_t s) {
   for (uint32_t len = 2; len <= slots; len <<= 1)
-    k_fft_fwd_stage<<<grid1(slots / 2, batch), kTpb, 0, s>>>(v, tw, slots, len);
+    { k_fft_fwd_stage<<<grid1(slots / 2, batch), kTpb, 0, s>>>(v, tw, slots, len); note_launch(); }
 }
 
 void launch_encode_round(const double2* v, double* coef, uint32_t slots, uint32_t n, double scale,
                          unsigned* status, cudaStream_t s) {
-  k_encode_round<<<grid1(slots), kTpb, 0, s>>>(v, coef, slots, log2u(slots), n, scale, status);
+  k_encode_round<<<grid1(slots), kTpb, 0, s>>>(v, coef, slots, log2u(slots), n, scale, status); note_launch();
 }
 
 void launch_decode_crt(const uint64_t* coef, uint32_t nlimbs, uint32_t slots, uint32_t n, double scale,
                        uint64_t q0, uint64_t q1, uint64_t q0inv_mod_q1, uint64_t q0inv_shoup, Modulus m1,
                        double2* v, cudaStream_t s) {
   k_decode_crt<<<grid1(slots), kTpb, 0, s>>>(coef, nlimbs, slots, log2u(slots), n, scale, q0, q1, q0inv_mod_q1,
-                                             q0inv_shoup, m1, v);
+                                             q0inv_shoup, m1, v); note_launch();
 }
 
 void launch_encode_round_batch(const double2* v, double* coef, uint32_t slots, uint32_t n, double scale,
                                uint32_t batch, unsigned* status, cudaStream_t s) {
   if (!batch) return;
-  k_encode_round_batch<<<grid1(slots, batch), kTpb, 0, s>>>(v, coef, slots, log2u(slots), n, scale, status);
+  k_encode_round_batch<<<grid1(slots, batch), kTpb, 0, s>>>(v, coef, slots, log2u(slots), n, scale, status); note_launch();
 }
 
 void launch_lift_double(const double* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
                         const Modulus* mods, uint32_t batch, cudaStream_t s) {
   if (!nlimbs || !batch) return;
-  k_lift_double<<<grid1(n, nlimbs, batch), kTpb, 0, s>>>(src, out, n, nlimbs, pm, mods);
+  k_lift_double<<<grid1(n, nlimbs, batch), kTpb, 0, s>>>(src, out, n, nlimbs, pm, mods); note_launch();
 }
 
 void launch_lift_small_batch(const int64_t* src, uint64_t* out, uint32_t n, uint32_t nlimbs, PrimeMap pm,
                              const Modulus* mods, uint32_t batch, cudaStream_t s) {
   if (!batch || !nlimbs) return;
-  k_lift_small_batch<<<grid1(n, nlimbs, batch), kTpb, 0, s>>>(src, out, n, nlimbs, pm, mods);
+  k_lift_small_batch<<<grid1(n, nlimbs, batch), kTpb, 0, s>>>(src, out, n, nlimbs, pm, mods); note_launch();
 }
 
 void launch_mul_monomial_half(const uint64_t* a, size_t sa, uint64_t* out, size_t so, uint32_t ncomp,
                               uint32_t nlimbs, uint32_t n, const Twiddle* tw, const uint64_t* primes,
                               cudaStream_t s) {
   if (!nlimbs || !ncomp) return;
-  k_mul_monomial_half<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, out, so, n, tw, primes);
+  k_mul_monomial_half<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(a, sa, out, so, n, tw, primes); note_launch();
 }
 
 void launch_bsgs_dot(const uint64_t* const* babies, const uint64_t* const* diags, uint64_t* out, uint32_t b,
                      uint32_t G, uint32_t nq, uint32_t n, const Modulus* mods, cudaStream_t s) {
   k_bsgs_dot<<<dim3((G + kGiantChunk - 1) / kGiantChunk, (n + 127) / 128, nq), 128, 0, s>>>(babies, diags, out, b,
-                                                                                           G, nq, n, mods);
+                                                                                           G, nq, n, mods); note_launch();
 }
 
 }  // namespace fhe

@@ -5,8 +5,12 @@
 #include <thread>
 
 #include "context.h"
+#include "launch_count.h"
 
 namespace fhe {
+
+std::atomic<uint64_t> g_kernel_launches{0};
+
 
 typedef unsigned __int128 u128;
 

@@ -26,6 +26,7 @@
 
 #include "modarith.cuh"
 #include "ntt.h"
+#include "launch_count.h"
 
 namespace fhe {
 namespace {
@@ -439,9 +440,9 @@ cudaError_t launch_fwd_impl(const NttArgs& g) {
   if (e != cudaSuccess) return e;
   const uint32_t polys = g.list ? 1 : g.n_polys;
   dim3 ga((1u << LB) / TW, polys, g.n_limbs);
-  ntt_fwd_cols<LA, LZ, TW><<<ga, TW * PA::T, sa, g.stream>>>(g);
+  ntt_fwd_cols<LA, LZ, TW><<<ga, TW * PA::T, sa, g.stream>>>(g); note_launch();
   dim3 gb((1u << LA) / TW, polys, g.n_limbs);
-  ntt_fwd_rows<LA, LB, TW, LZ><<<gb, TW * PB::T, sb, g.stream>>>(g);
+  ntt_fwd_rows<LA, LB, TW, LZ><<<gb, TW * PB::T, sb, g.stream>>>(g); note_launch();
   return cudaGetLastError();
 }
 
@@ -473,9 +474,9 @@ cudaError_t launch_inv_tw(const NttArgs& g) {
   if (e != cudaSuccess) return e;
   const uint32_t polys = g.list ? 1 : g.n_polys;
   dim3 gb((1u << LA) / TW, polys, g.n_limbs);
-  ntt_inv_rows<LB, TW><<<gb, TW * PB::T, sb, g.stream>>>(g);
+  ntt_inv_rows<LB, TW><<<gb, TW * PB::T, sb, g.stream>>>(g); note_launch();
   dim3 ga((1u << LB) / TW, polys, g.n_limbs);
-  ntt_inv_cols<LA, TW><<<ga, TW * PA::T, sa, g.stream>>>(g);
+  ntt_inv_cols<LA, TW><<<ga, TW * PA::T, sa, g.stream>>>(g); note_launch();
   return cudaGetLastError();
 }
 

@@ -98,11 +98,14 @@ class PackedMamba2:
     stream is zero outside its values.
     """
 
-    def __init__(self, cc, layout: StateLayout, b_base: int, c_base: int, head_base: int = 0):
+    def __init__(self, cc, layout: StateLayout, b_base: int, c_base: int, head_base: int = 0,
+                 decay_base: int | None = None):
         if cc.slots != layout.slots:
             raise _lib.InvalidArgument(-1, "PackedMamba2", "layout slots differ from the context")
         self.cc, self.L = cc, layout
         self.b_base, self.c_base, self.head_base = b_base, c_base, head_base
+        # decay may sit in the same ciphertext as dt, at its own offset
+        self.decay_base = head_base if decay_base is None else decay_base
         L = layout
         self._state_baby = L.group_heads if L.state_size >= L.group_heads else L.state_size
         self._state_giant = L.state_size // self._state_baby
@@ -119,7 +122,7 @@ class PackedMamba2:
         s |= {-(1 << i) for i in range(_log2(L.head_dim))}            # fill over a head
         s |= {-(1 << i) for i in range(_log2(gb))}                    # fill over a state block
         s |= {g * gb for g in range(1, L.groups)} | {-g * gb for g in range(1, L.groups)}
-        s |= {self.head_base + L.group_heads * g for g in range(L.groups)}
+        s |= {base + L.group_heads * g for g in range(L.groups) for base in (self.head_base, self.decay_base)}
         s |= {-(L.head_dim - 1) * hl for hl in range(1, L.group_heads)}
         s |= {self.b_base, self.c_base}
         stride = -(gb - 1)
@@ -164,11 +167,12 @@ class PackedMamba2:
             m = self.cc.EvalRotate(m, group * gb)
         return self._fill(m, gb, self.L.state_size)
 
-    def expand_heads(self, v, group: int):
+    def expand_heads(self, v, group: int, base: int | None = None):
         """Per-head values (dt, decay) of the group, repeated over channels and states."""
         c, L = self.cc, self.L
         gh, hd = L.group_heads, L.head_dim
-        shifted = c.EvalRotate(v, self.head_base + gh * group) if self.head_base + gh * group else v
+        base = self.head_base if base is None else base
+        shifted = c.EvalRotate(v, base + gh * group) if base + gh * group else v
         steps = [-(hd - 1) * hl for hl in range(1, gh)]
         rots = [shifted] + (c.EvalFastRotation(shifted, steps) if steps else [])
         acc = None
@@ -233,7 +237,7 @@ class PackedMamba2:
         for g in range(self.L.groups):
             x_g = self.expand_x(xbc, g)
             dt_g = self.expand_heads(dt, g)
-            dec_g = self.expand_heads(decay, g) if states is not None else None
+            dec_g = self.expand_heads(decay, g, self.decay_base) if states is not None else None
             s = self.update(states[g] if states is not None else None, dec_g, x_g, dt_g, b_exp)
             new_states.append(s)
             r = self.readout(s, c_exp, g)

@@ -328,7 +328,7 @@ class PlaintextCache:
 class EncryptedMamba2Layer:
     """The layer on ciphertexts of one CryptoContext (full packing)."""
 
-    def __init__(self, cc, W: Mamba2Weights, P: Mamba2Polys, passes: int = 2, margin: int = 3,
+    def __init__(self, cc, W: Mamba2Weights, P: Mamba2Polys, passes: int = 2, margin: int = 4,
                  cache: PlaintextCache | None = None):
         self.cc, self.W, self.P = cc, W, P
         self.passes, self.margin = passes, margin
@@ -337,7 +337,14 @@ class EncryptedMamba2Layer:
                     "w_out": ReplicatedLayout(W.d_model, W.d_inner, cc.slots)}
         E, S, H = W.d_inner, W.d_state, W.heads
         self.layout = StateLayout(H, W.head_dim, S, cc.slots)
-        self.pm = PackedMamba2(cc, self.layout, b_base=E, c_base=E + S, head_base=0)
+        # SSM inputs share one ciphertext: xa at [0, conv_dim), dt and decay per head
+        # at their own offsets, so a single refresh serves the whole update.
+        self.dt_base = -(-W.conv_dim // 64) * 64
+        self.decay_base = self.dt_base + -(-H // 64) * 64
+        if self.decay_base + H > cc.slots:
+            raise ValueError("packed SSM inputs do not fit the slots")
+        self.pm = PackedMamba2(cc, self.layout, b_base=E, c_base=E + S, head_base=self.dt_base,
+                               decay_base=self.decay_base)
         self.refreshes = 0
         self._lin = {}
         n = cc.slots
@@ -350,7 +357,7 @@ class EncryptedMamba2Layer:
         for width in (W.d_model, W.d_inner):
             win = 1 << (width - 1).bit_length()
             s |= {1 << i for i in range(win.bit_length() - 1)} | {-win}
-        s |= {W.d_inner, W.d_inner + W.conv_dim}
+        s |= {W.d_inner, W.d_inner + W.conv_dim, -self.dt_base, -self.decay_base}
         return sorted(v % n for v in s if v % n)
 
     def _diags(self, name):
@@ -363,7 +370,9 @@ class EncryptedMamba2Layer:
         return ct.n_limbs() - 1 - (1 if ct.GetNoiseScaleDeg() >= 2 else 0)
 
     def _fit(self, ct, need, bound):
-        """Refreshes ct when fewer than need (+ margin) levels remain."""
+        """Refreshes ct when fewer than need + margin levels remain; the margin keeps
+        every stage's output refreshable (a two-pass refresh spends two levels
+        before its second bootstrap, which needs two limbs)."""
         if self._left(ct) >= need + self.margin:
             return ct
         self.refreshes += 1
@@ -408,14 +417,20 @@ class EncryptedMamba2Layer:
     def step(self, h, conv_state, ssm_state, bounds):
         """h: ciphertext of the residual stream at [0, d_model); conv_state: list
         of conv_kernel-1 xBC ciphertexts (None for zeros); ssm_state: list of
-        group ciphertexts or None.  Returns (h_out, conv_state, ssm_state)."""
+        group ciphertexts or None.  Returns (h_out, conv_state, ssm_state).
+
+        Refresh points: the layer input (before the block norm), the in_proj
+        output (once for the conv, dt and gate branches), the packed SSM inputs
+        (xa, dt, decay in one ciphertext) and the gated value before its norm;
+        states are refreshed only when their own levels run out."""
         c, W, P = self.cc, self.W, self.P
         E, S, H, Dm = W.d_inner, W.d_state, W.heads, W.d_model
         cd = W.conv_dim
         u = self._rms(h, Dm, W["norm_w"], P.rsqrt1, bounds["h"])
-        u = self._fit(u, 1, bounds["u"])
+        u = self._fit(u, 2, bounds["u"])
         proj = self._linear(u, "w_in")
-        # xBC stream at [0, conv_dim)
+        proj = self._fit(proj, 19, bounds["proj"])
+        # xBC stream at [0, conv_dim) and the causal conv
         xbc = self.pm._mul_mask(c.EvalRotate(proj, E), self.pm._block_mask(0, cd))
         window = [self._fit(w, 2, bounds["xbc"]) if w is not None else None for w in conv_state] + [xbc]
         taps = []
@@ -438,21 +453,21 @@ class EncryptedMamba2Layer:
                                                         scale=dtv.GetScalingFactor()))
         dtv = self._fit(dtv, 8, bounds["dt"])
         dts = self._poly(dtv, P.softplus, 0, H)
-        avec = np.zeros(c.slots)
-        avec[:H] = W["a"]
-        adt = self.pm._mul_mask(dts, avec)
-        adt = self._fit(adt, 8, bounds["adt"])
-        decay = self._poly(adt, P.exp, 0, H) if ssm_state is not None else None
-        # state update and readout
-        xa = self._fit(xa, 8, bounds["xa"])
-        dts = self._fit(dts, 8, bounds["dts"])
+        pack = c.EvalAdd(xa, c.EvalRotate(dts, -self.dt_base))
         if ssm_state is not None:
-            decay = self._fit(decay, 6, 1.0)
-            ssm_state = [self._fit(s, 4, bounds["state"]) for s in ssm_state]
-        states, y = self.pm.step(ssm_state, xa, dts, decay)
+            avec = np.zeros(c.slots)
+            avec[:H] = W["a"]
+            adt = self._fit(self.pm._mul_mask(dts, avec), 8, bounds["adt"])
+            decay = self._poly(adt, P.exp, 0, H)
+            pack = c.EvalAdd(pack, c.EvalRotate(decay, -self.decay_base))
+        pack = self._fit(pack, 8, bounds["pack"])
+        # state update and readout from the packed inputs
+        if ssm_state is not None:
+            ssm_state = [self._fit(st, 4, bounds["state"]) for st in ssm_state]
+        states, y = self.pm.step(ssm_state, pack, pack, pack if ssm_state is not None else None)
         dvec = np.zeros(c.slots)
         dvec[:E] = np.repeat(W["d"], W.head_dim)
-        y = c.EvalAdd(y, self.pm._mul_mask(xa, dvec))
+        y = c.EvalAdd(y, self.pm._mul_mask(pack, dvec))
         # gate
         z = self.pm._mul_mask(proj, self.pm._block_mask(0, E))
         z = self._fit(z, 8, bounds["z"])
@@ -460,7 +475,7 @@ class EncryptedMamba2Layer:
         y = self._fit(y, 2, bounds["y"])
         g = c.EvalMult(y, sz)
         gn = self._rms(g, E, W["gn_w"], P.rsqrt2, bounds["g"])
-        gn = self._fit(gn, 1, bounds["gn"])
+        gn = self._fit(gn, 2, bounds["gn"])
         out = self._linear(gn, "w_out")
         h_out = c.EvalAdd(h, out)
         return h_out, window[1:], states
@@ -473,6 +488,7 @@ def poly_step_record(W: Mamba2Weights, P: Mamba2Polys, h, conv, st, rec):
     u = plain_rms(h, W["norm_w"], W.eps, P.rsqrt1)
     rec("u", u)
     proj = W["w_in"] @ u
+    rec("proj", proj)
     z, xbc, dt = proj[:E], proj[E:E + W.conv_dim], proj[E + W.conv_dim:]
     rec("xbc", xbc)
     rec("z", z)
@@ -485,6 +501,9 @@ def poly_step_record(W: Mamba2Weights, P: Mamba2Polys, h, conv, st, rec):
     dts = P.softplus(dt + W["dt_bias"])
     rec("dts", dts)
     rec("adt", W["a"] * dts)
+    rec("pack", xa)
+    rec("pack", dts)
+    rec("pack", [1.0])
     x, B, C = xa[:E].reshape(H, Pd), xa[E:E + S], xa[E + S:]
     upd_ = (dts[:, None] * x)[:, :, None] * B[None, None, :]
     st = upd_ if st is None else P.exp(W["a"] * dts)[:, None, None] * st + upd_

@@ -225,6 +225,20 @@ int fhe_encode_batch(fhe_ctx* ctx, const double* re, const double* im, uint32_t 
 int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* diags, uint32_t baby,
                          uint32_t giant, int32_t stride, int32_t giant_offset, fhe_ct** out);
 
+/* Number of kernels this library has launched in this process (all contexts). */
+int fhe_kernel_launches(uint64_t* count);
+
+/* Operation counters of a context since creation or the last reset (the
+ * reference reports ct_ct / rotations / bootstraps in native.json,
+ * packed_fideslib.cpp:1239-1396; the key-switching work behind them too):
+ * tensor products, relinearisations, rotations (plain and hoisted), ModUps,
+ * ModDowns, key inner products, rescales, limb NTTs (forward + inverse) and
+ * bootstraps.  reset != 0 zeroes them after reading. */
+typedef struct fhe_counters {
+  uint64_t tensor, relin, rotations, modup, moddown, key_inner, rescales, ntt_limbs, bootstraps;
+} fhe_counters;
+int fhe_ctx_counters(fhe_ctx* ctx, fhe_counters* out, int32_t reset);
+
 /* Bootstrapping of fully packed ciphertexts (slots = N/2), replacing OpenFHE's
  * EvalBootstrapSetup({budget_cts, budget_stc}, {0, 0}, slots, correction) /
  * EvalBootstrapKeyGen / EvalBootstrap as called at packed_fideslib.cpp:1084-1089,
