@@ -183,7 +183,7 @@ def cpu_keyswitch_seconds(threads, n_limbs=30):
     return time.perf_counter() - t0
 
 
-def measure_ckks(local, reps=10):
+def measure_ckks(local, reps=10, matvec=True):
     """Key switching and the BSGS matvec at BASELINE config-3 shape
     (N=2^16, 2^15 slots, 20 limbs, dnum 3), timed with CUDA events on the
     context stream.  Returns the two report objects."""
@@ -217,6 +217,10 @@ def measure_ckks(local, reps=10):
           "ms": ks_ms, "alg_bytes": ks_bytes, "achieved_gbs": ks_bytes / (ks_ms / 1e3) / 1e9,
           "frac": ks_bytes / (ks_ms / 1e3) / 1e9 / peak, "peak_gbs": peak, "peak_source": kind}
 
+    if not matvec:
+        del ct3
+        cc.close()
+        return ks, None
     m, k, baby, giant = 768, 1536, 32, 48
     W = rng.normal(0, 0.02, size=(m, k))
     x = rng.uniform(-1, 1, k)
@@ -277,7 +281,7 @@ def measure_bootstrap(cc, reps=3):
 class TokenLoop:
     """The 24-layer encrypted greedy loop: client encrypt -> server layers -> client select."""
 
-    def __init__(self, local, layers=24, passes=2, seed=6):
+    def __init__(self, local, layers=24, passes=2, seed=6, sparse_h=0):
         from fhe_mamba_b200 import CCParams, CryptoContext
         from fhe_mamba_b200.mamba2_layer import EncryptedMamba2Model, Mamba2Model
         t0 = time.perf_counter()
@@ -286,13 +290,14 @@ class TokenLoop:
         self.cc = CryptoContext(CCParams(ring_dim=1 << 16, multiplicative_depth=44, scaling_mod_size=59,
                                          first_mod_size=60, num_large_digits=3, device=local))
         self.cc.KeyGen(41 + seed)
-        self.cc.EvalBootstrapSetup((4, 4))
+        self.cc.EvalBootstrapSetup((4, 4), sparse_hamming_weight=sparse_h)
         self.cc.EvalBootstrapKeyGen()
         self.em = EncryptedMamba2Model(self.cc, self.model, passes=passes)
         self.cc.EvalRotateKeyGen(self.em.rotation_steps())
         self.cc.synchronize()
         self.setup_seconds = time.perf_counter() - t0
         self.token = 5
+        self.hidden = []
         self.layers, self.passes = layers, passes
 
     def encrypt(self, token):
@@ -313,8 +318,22 @@ class TokenLoop:
                                 degree=len(m.rsqrt_f.coeffs) - 1)
 
     def select(self, hidden):
-        tok, _ = self.em.select(hidden)
+        tok, hf = self.em.select(hidden)
+        self.hidden.append(hf)
         return tok
+
+    def plaintext_check(self):
+        """Replays the token sequence on the plaintext polynomial path (same
+        weights and polynomials, fp64): whether every greedy token agrees and
+        the largest deviation of the decrypted final hidden vector."""
+        m = self.model
+        state, tok, same, err = m.initial_state(), self.token, True, 0.0
+        for enc_tok, hf in zip(self.em.tokens, self.hidden):
+            want, logits, state = m.plain_token(tok, state)
+            same &= int(np.argmax(logits)) == enc_tok
+            err = max(err, float(np.max(np.abs(want - hf))))
+            tok = enc_tok
+        return {"tokens_equal_plaintext": bool(same), "max_hidden_error": err, "tokens": len(self.hidden)}
 
 
 def host_threads():
@@ -352,7 +371,9 @@ def config_dict(args):
     return {"workload": "BASELINE configs[4]: encrypted greedy token loop, Mamba-2-130M shape "
                         f"({args.layers} layers, d_model 768, d_state 128, 24 heads, vocab 50280)",
             "ring_dim": 1 << 16, "slots": 1 << 15, "depth": 44, "scale_bits": 59, "dnum": 3,
-            "bootstrap_passes": args.passes, "l2": "inputs larger than L2 (keys ~36 GB, cached diagonals)",
+            "bootstrap_passes": args.passes,
+            "secret_key_dist": f"sparse-encapsulated h={args.sparse_h}" if args.sparse_h else "uniform-ternary",
+            "l2": "inputs larger than L2 (keys ~36 GB, cached diagonals)",
             "parallelism": "one token-loop replica per GPU"}
 
 
@@ -402,11 +423,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=3, help="untimed tokens")
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--passes", type=int, default=2, choices=[1, 2], help="bootstrap passes per refresh")
+    ap.add_argument("--sparse-h", type=int, default=0,
+                    help="bootstrap by sparse-secret encapsulation with this Hamming weight (0: uniform ternary)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ckks", action="store_true", help="skip the key-switch, matvec and bootstrap side measurements")
     ap.add_argument("--ckks-only", action="store_true",
-                    help="print only the key-switch and matvec measurements (profiling runs)")
+                    help="print only the config-3 key-switch measurement (small profiling runs)")
+    ap.add_argument("--kernel-shares", action="store_true",
+                    help="after the warm-up, record one token's kernels (CUPTI) and print their time shares")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("warmup must be >= 3")
@@ -424,8 +449,8 @@ def main():
 
     torch.cuda.set_device(local)
     if args.ckks_only:
-        ks, mv = measure_ckks(local)
-        print(json.dumps({"keyswitch": ks, "bsgs_matvec": mv}), flush=True)
+        ks, _ = measure_ckks(local, matvec=False)
+        print(json.dumps({"keyswitch": ks}), flush=True)
         return
     if world > 1:
         from datetime import timedelta
@@ -438,12 +463,33 @@ def main():
     if world == 1 and not args.no_ckks:
         side["keyswitch"], side["bsgs_matvec"] = measure_ckks(local)
 
-    loop = TokenLoop(local, layers=args.layers, passes=args.passes, seed=6 + rank)
+    loop = TokenLoop(local, layers=args.layers, passes=args.passes, seed=6 + rank, sparse_h=args.sparse_h)
     stream = torch.cuda.ExternalStream(loop.cc.stream_ptr(), device=torch.device("cuda", local))
     tok = loop.token
     for _ in range(args.warmup):
         tok = loop.select(loop.server(loop.encrypt(tok)))
     torch.cuda.synchronize()
+
+    if args.kernel_shares:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            tok = loop.select(loop.server(loop.encrypt(tok)))
+            torch.cuda.synchronize()
+        agg = {}
+        for e in prof.events():
+            if e.device_type.name != "CUDA":
+                continue
+            name = e.name.replace("void ", "").replace("(anonymous namespace)::", "").split("(")[0]
+            a = agg.setdefault(name, [0, 0.0])
+            a[0] += 1
+            a[1] += getattr(e, "device_time_total", 0) or getattr(e, "cuda_time_total", 0)
+        total = sum(v[1] for v in agg.values())
+        rows = [{"kernel": k, "launches": c, "ms": t / 1e3, "share": t / total}
+                for k, (c, t) in sorted(agg.items(), key=lambda kv: -kv[1][1])]
+        if rank == 0:
+            print(json.dumps({"kernel_shares_one_token": rows, "total_ms": total / 1e3}), flush=True)
+        loop.cc.close()
+        return
 
     uuid = None
     try:
@@ -499,7 +545,8 @@ def main():
             "gpu_launches": launches,
             "clocks": clocks,
             "per_token": {"operations": per_token, "refreshes": loop.em.refreshes() / max(1, args.steps + args.warmup),
-                          "setup_seconds": loop.setup_seconds, "tokens": loop.em.tokens[-args.steps:]},
+                          "setup_seconds": loop.setup_seconds, "tokens": loop.em.tokens[-args.steps:],
+                          "check": loop.plaintext_check()},
         }
         line.update(side)
         if world == 1 and not args.no_ckks:

@@ -121,7 +121,7 @@ SIGNATURES = {
     "fhe_linear_transform": [vp, vp, ctypes.POINTER(vp), u32, u32, i32, i32, ctypes.POINTER(vp)],
     "fhe_ctx_counters": [vp, vp, i32],
     "fhe_kernel_launches": [ctypes.POINTER(ctypes.c_uint64)],
-    "fhe_bootstrap_setup": [vp, u32, u32, u32, i32, i32],
+    "fhe_bootstrap_setup": [vp, u32, u32, u32, i32, i32, u32],
     "fhe_bootstrap_keygen": [vp],
     "fhe_bootstrap": [vp, vp, ctypes.POINTER(vp)],
     "fhe_bootstrap_stage": [vp, i32, vp, ctypes.POINTER(vp)],

@@ -200,7 +200,7 @@ class CryptoContext:
 
     def key(self, kind: int, galois: int = 0):
         D = (self.n_q + self.alpha - 1) // self.alpha
-        words = {0: (self.n_q + self.n_p) * self.n, 1: 2 * self.n_q * self.n}.get(
+        words = {0: (self.n_q + self.n_p) * self.n, 4: (self.n_q + self.n_p) * self.n, 1: 2 * self.n_q * self.n}.get(
             kind, D * 2 * (self.n_q + self.n_p) * self.n)
         out = np.zeros(words, dtype=np.uint64)
         call("fhe_key_download", self.h, kind, galois, out.ctypes.data_as(P64), words)
@@ -238,11 +238,12 @@ class CryptoContext:
         return self._ct("fhe_linear_transform", ct.handle, arr, baby, giant, int(stride), int(giant_offset))
 
     def EvalBootstrapSetup(self, level_budget=(4, 4), dim1=(0, 0), slots: int = 0, correction_factor: int = 0,
-                           slots_to_coeffs_first: bool = False):
+                           slots_to_coeffs_first: bool = False, sparse_hamming_weight: int = 0):
         """OpenFHE EvalBootstrapSetup(levelBudget, dim1, slots, correctionFactor[, slotsToCoeffsFirst]);
-        dim1 is accepted for signature compatibility (the BSGS split is chosen per group)."""
+        dim1 is accepted for signature compatibility (the BSGS split is chosen per group).
+        sparse_hamming_weight > 0 selects sparse-secret encapsulation."""
         call("fhe_bootstrap_setup", self.h, int(level_budget[0]), int(level_budget[1]), int(slots),
-             int(correction_factor), int(bool(slots_to_coeffs_first)))
+             int(correction_factor), int(bool(slots_to_coeffs_first)), int(sparse_hamming_weight))
 
     def bootstrap_components(self, ct, passes: int = 2, merge: bool = False):
         """The reference's two-pass refresh (PackedEvaluator::bootstrap_components,

@@ -335,7 +335,7 @@ int fhe_conjugation_keygen(fhe_ctx* ctx) {
 int fhe_key_download(fhe_ctx* ctx, int kind, uint64_t galois, uint64_t* host, size_t words) {
   return guarded([&] {
     fhe::Ckks& k = ckks(ctx);
-    fhe::require(kind >= 0 && kind <= 3, "key kind must be 0..3");
+    fhe::require(kind >= 0 && kind <= 6, "key kind must be 0..6");
     fhe::require(host != nullptr && words == k.key_words(kind),
                  "host buffer must hold exactly " + std::to_string(k.key_words(kind)) + " words");
     k.download_key(kind, galois, host);
@@ -574,7 +574,7 @@ int fhe_ctx_counters(fhe_ctx* ctx, fhe_counters* out, int32_t reset) {
 }
 
 int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, uint32_t slots,
-                        int32_t correction, int32_t s2c_first) {
+                        int32_t correction, int32_t s2c_first, uint32_t sparse_h) {
   return guarded([&] {
     fhe::Ckks& k = ckks(ctx);
     fhe::require(slots == 0 || slots == ctx->c.slots, "bootstrap slots must equal the context's slot count", -1);
@@ -583,6 +583,7 @@ int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, 
     p.budget_stc = budget_stc;
     p.correction = correction;
     p.s2c_first = s2c_first != 0;
+    p.sparse_h = sparse_h;
     ctx->boot = std::make_unique<fhe::Bootstrapper>(k, p);
   });
 }
@@ -692,6 +693,7 @@ int fhe_program_run(const char* program_path, const char* client_head_path, cons
     if (can_boot) {
       fhe::BootParams bp;
       bp.s2c_first = o.s2c_first != 0;
+      bp.sparse_h = o.sparse_h;
       ctx->boot = std::make_unique<fhe::Bootstrapper>(ck, bp);
       ctx->boot->keygen();
     }

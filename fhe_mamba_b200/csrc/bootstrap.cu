@@ -98,6 +98,11 @@ Bootstrapper::Bootstrapper(Ckks& ck, const BootParams& p) : ck_(ck), p_(p) {
   require(p_.budget_cts >= 1 && p_.budget_stc >= 1, "level budgets must be >= 1", -1);
   p_.budget_cts = std::min(p_.budget_cts, logn);
   p_.budget_stc = std::min(p_.budget_stc, logn);
+  if (p_.sparse_h) {
+    require(p_.sparse_h <= ctx.n / 2, "sparse Hamming weight out of range", -1);
+    p_.K = std::ceil((p_.sparse_h + 1) / 2.0) + 2.0;  // |I| <= (h + 1) / 2
+    p_.double_angles = 3;
+  }
   require(p_.K >= 1 && p_.double_angles >= 0 && p_.double_angles <= 12, "bad EvalMod parameters", -1);
   // Default pre-scaling: the sine approximation error shrinks by 4x per step
   // while the amplified noise grows by 2x; 8 balances them for uniform
@@ -204,6 +209,7 @@ void Bootstrapper::keygen() {
   }
   const uint64_t conj = 2ull * ck_.ctx.n - 1;
   if (!ck_.has_rotation_key(conj)) ck_.rotation_keygen(conj);
+  if (p_.sparse_h) ck_.sparse_keygen(p_.sparse_h);
 }
 
 std::unique_ptr<Ct> Bootstrapper::transform(std::vector<Group>& groups, std::unique_ptr<Ct> x) {
@@ -270,7 +276,14 @@ std::unique_ptr<Ct> Bootstrapper::raise(const Ct& a) {
   // exactly that scale), then raise.
   auto low = ck_.adjust(*in, 1, std::ldexp((double)ctx.primes[0], -corr_));
   in.reset();
+  if (p_.sparse_h) {
+    require(ck_.sparse_weight() == p_.sparse_h, "bootstrap keys for the sparse secret are missing", -4);
+    low = ck_.switch_to_sparse(*low);
+  }
   auto raised = ck_.mod_raise(*low);
+  // The raised plaintext t = m + q0 I is fixed now; switching back to the
+  // dense secret keeps it (and I) unchanged.
+  if (p_.sparse_h) raised = ck_.switch_to_dense(*raised);
   raised->scale = ck_.level_scale(ctx.L);
   levels_[0] = raised->nq;
   return raised;

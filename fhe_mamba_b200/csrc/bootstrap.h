@@ -31,6 +31,12 @@ struct BootParams {
   // SlotToCoeff before ModRaise (the reference's S2C-first patch): the input's
   // own levels pay for SlotToCoeff, so the output keeps budget_stc more limbs.
   bool s2c_first = false;
+  // Sparse-secret encapsulation (FIDESlib's SPARSE_ENCAPSULATED key
+  // distribution): 0 keeps the uniform ternary secret; h > 0 switches the
+  // one-limb ciphertext to a sparse secret of Hamming weight h before
+  // ModRaise and back right after it, so |I| <= (h + 1) / 2 and EvalMod needs
+  // a far smaller interval, degree and depth.
+  uint32_t sparse_h = 0;
 };
 
 class Bootstrapper {

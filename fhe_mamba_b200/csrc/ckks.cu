@@ -338,11 +338,66 @@ void Ckks::rotation_keygen(uint64_t g) {
   FHE_CUDA(cudaStreamSynchronize(ctx.stream));
 }
 
+// Sparse ternary secret of Hamming weight h: h distinct coefficient positions
+// (Floyd's sampling) with random signs, from a splitmix64 stream keyed by the
+// key seed; then the two switching keys of the encapsulation.
+void Ckks::sparse_keygen(uint32_t h) {
+  require(keyed_, "sparse key generation before keygen", -4);
+  const uint32_t n = ctx.n, L = ctx.L, K = ctx.K, lk = L + K;
+  require(h >= 1 && h <= n / 2, "sparse Hamming weight out of range", -1);
+  if (sparse_h_ == h) return;
+  uint64_t st = seed_ ^ 0x9E3779B97F4A7C15ull ^ ((uint64_t)h << 32);
+  auto next = [&st]() {
+    uint64_t z = (st += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+  };
+  std::vector<int64_t> coef(n, 0);
+  for (uint32_t j = n - h; j < n; ++j) {
+    const uint32_t t = (uint32_t)(next() % (j + 1));
+    const uint32_t pos = coef[t] == 0 ? t : j;
+    coef[pos] = (next() & 1) ? 1 : -1;
+  }
+  int64_t* small = reinterpret_cast<int64_t*>(ws(10, n));
+  FHE_CUDA(cudaMemcpyAsync(small, coef.data(), (size_t)n * 8, cudaMemcpyHostToDevice, ctx.stream));
+  s_sparse_ = DevMem((size_t)lk * n * 8);
+  launch_lift_small(small, s_sparse_.as<uint64_t>(), n, lk, PrimeMap{lk, L}, ctx.d_mod.as<Modulus>(), ctx.stream);
+  ntt_dense(s_sparse_.as<uint64_t>(), 1, lk, lk, 0, false);
+  const uint64_t id = 2ull * n + 1;  // beyond every Galois element and the relinearisation key
+  switch_keygen(id, s_sparse_.as<uint64_t>(), s_ntt_.as<uint64_t>(), key_to_sparse_);
+  switch_keygen(id + 2, s_ntt_.as<uint64_t>(), s_sparse_.as<uint64_t>(), key_to_dense_);
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  sparse_h_ = h;
+}
+
+std::unique_ptr<Ct> Ckks::switch_with(const Ct& a, const DevMem& key) {
+  require(a.ncomp == 2, "key switch expects a 2-component ciphertext", -1);
+  std::unique_ptr<Ct> hold;
+  const Ct& x = ready(a, hold);
+  const uint32_t nq = x.nq, n = ctx.n;
+  auto out = alloc(nq, 2);
+  keyswitch(x.data() + (size_t)x.cap * n, nq, key.as<uint64_t>(), out->data(), (size_t)nq * n, x.data());
+  out->scale = x.scale;
+  out->noise_deg = x.noise_deg;
+  return out;
+}
+
+std::unique_ptr<Ct> Ckks::switch_to_sparse(const Ct& a) {
+  require(sparse_h_ != 0, "no sparse secret", -4);
+  return switch_with(a, key_to_sparse_);
+}
+
+std::unique_ptr<Ct> Ckks::switch_to_dense(const Ct& a) {
+  require(sparse_h_ != 0, "no sparse secret", -4);
+  return switch_with(a, key_to_dense_);
+}
+
 size_t Ckks::key_words(int kind) const {
   const size_t n = ctx.n, L = ctx.L, K = ctx.K;
   const size_t D = (L + ctx.alpha - 1) / ctx.alpha;
   switch (kind) {
-    case 0: return (L + K) * n;
+    case 0: case 4: return (L + K) * n;
     case 1: return 2 * L * n;
     default: return D * 2 * (L + K) * n;
   }
@@ -354,7 +409,10 @@ void Ckks::download_key(int kind, uint64_t g, uint64_t* host) const {
   if (kind == 0) m = &s_ntt_;
   else if (kind == 1) m = &pk_;
   else if (kind == 2) m = &rlk_;
-  else {
+  else if (kind >= 4 && kind <= 6) {
+    require(sparse_h_ != 0, "no sparse secret", -4);
+    m = kind == 4 ? &s_sparse_ : kind == 5 ? &key_to_sparse_ : &key_to_dense_;
+  } else {
     auto it = rot_.find(g);
     require(it != rot_.end(), "no rotation key for Galois element " + std::to_string(g), -4);
     m = &it->second;

@@ -66,6 +66,12 @@ class Ckks {
   void rotation_keygen(uint64_t g);
   bool has_rotation_key(uint64_t g) const { return rot_.count(g) != 0; }
   void download_key(int kind, uint64_t g, uint64_t* host) const;
+  // Sparse-secret encapsulation for bootstrapping: a sparse ternary secret s'
+  // of Hamming weight h and the switching keys s -> s' and s' -> s.
+  void sparse_keygen(uint32_t h);
+  uint32_t sparse_weight() const { return sparse_h_; }
+  std::unique_ptr<Ct> switch_to_sparse(const Ct& a);
+  std::unique_ptr<Ct> switch_to_dense(const Ct& a);
   size_t key_words(int kind) const;
 
   // encode / encryption
@@ -155,6 +161,9 @@ class Ckks {
   bool keyed_ = false;
   uint64_t seed_ = 0;
   DevMem s_ntt_, pk_, rlk_;
+  DevMem s_sparse_, key_to_sparse_, key_to_dense_;
+  uint32_t sparse_h_ = 0;
+  std::unique_ptr<Ct> switch_with(const Ct& a, const DevMem& key);
   std::map<uint64_t, DevMem> rot_;
   std::vector<DevMem> ws_;
   DevMem status_;

@@ -18,7 +18,7 @@ int main(int argc, char** argv) {
   if (argc < 5) {
     std::cerr << "usage: packed_b200 PROGRAM RESULT POLY_TOL EXACT_TOL [--bootstrap-passes 1|2] "
                  "[--client-head FILE] [--trace-levels] [--s2c-first] [--ring-log N] [--depth D] [--seed S] "
-                 "[--device D]"
+                 "[--device D] [--secret-key-dist uniform-ternary|sparse-encapsulated] [--sparse-h H]"
               << std::endl;
     return 2;
   }
@@ -61,6 +61,15 @@ int main(int argc, char** argv) {
         o.seed = std::stoull(value());
       } else if (a == "--device") {
         o.device = std::stoi(value());
+      } else if (a == "--secret-key-dist") {
+        // the decode driver's choices (stage1_mamba2_decode_fideslib.cpp:284-291);
+        // bootstrapping under a sparse secret of weight 32 by encapsulation
+        const std::string d = value();
+        if (d == "sparse-encapsulated") o.sparse_h = o.sparse_h ? o.sparse_h : 32;
+        else if (d == "uniform-ternary") o.sparse_h = 0;
+        else throw std::invalid_argument("secret key distribution must be uniform-ternary or sparse-encapsulated");
+      } else if (a == "--sparse-h") {
+        o.sparse_h = (uint32_t)std::stoul(value());
       } else if (a == "--security") {
         if (value() != "not-set") throw std::invalid_argument("only --security not-set is available");
       } else if (no_effect.count(a)) {

@@ -145,8 +145,10 @@ int fhe_conjugation_keygen(fhe_ctx* ctx);
 
 /* Copies a key to host memory: kind 0 secret s (NTT form, [n_q+n_p][N]),
  * 1 public key ([2][n_q][N]), 2 relinearisation key, 3 rotation key of
- * Galois element `galois` ([digits][2][n_q+n_p][N]); `words` must equal the
- * key's size.  For parity tests against an independent implementation. */
+ * Galois element `galois` ([digits][2][n_q+n_p][N]); after a bootstrap setup
+ * with sparse_h > 0: 4 the sparse secret s' (NTT form), 5 the switching key
+ * s -> s', 6 the key s' -> s.  `words` must equal the key's size.  For parity
+ * tests against an independent implementation. */
 int fhe_key_download(fhe_ctx* ctx, int kind, uint64_t galois, uint64_t* host, size_t words);
 
 /* MakeCKKSPackedPlaintext (packed_fideslib.cpp:163-179): special inverse FFT,
@@ -248,9 +250,17 @@ int fhe_ctx_counters(fhe_ctx* ctx, fhe_counters* out, int32_t reset);
  * least 2 limbs and slots of magnitude <= 1.  s2c_first != 0 selects the
  * reference's S2C-first variant (patches/fideslib-v2.1.0-s2c-first-bootstrap.patch:27-60):
  * SlotToCoeff runs on the input's own levels before ModRaise (input needs
- * budget_stc + 2 limbs) and the output keeps budget_stc more limbs. */
+ * budget_stc + 2 limbs) and the output keeps budget_stc more limbs.
+ * sparse_h > 0 selects sparse-secret encapsulation (FIDESlib's
+ * SPARSE_ENCAPSULATED key distribution, the "sparse-encapsulated" choice of
+ * native/fideslib_stage0/src/fideslib_ctpt_probe.cpp:130-137; the packed
+ * executable fixes UNIFORM_TERNARY at packed_fideslib.cpp:1062): the
+ * one-limb ciphertext is switched to a sparse secret of Hamming weight
+ * sparse_h for ModRaise and back, so EvalMod covers |I| <= (h+1)/2 with a
+ * lower degree and 4-5 fewer levels; 0 keeps the reference's uniform ternary
+ * secret throughout. */
 int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, uint32_t slots,
-                        int32_t correction, int32_t s2c_first);
+                        int32_t correction, int32_t s2c_first, uint32_t sparse_h);
 int fhe_bootstrap_keygen(fhe_ctx* ctx);
 int fhe_bootstrap(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
 /* One step of fhe_bootstrap (EvalCoeffsToSlots / EvalSlotsToCoeffs and their
@@ -277,7 +287,7 @@ typedef struct fhe_program_options {
   int32_t s2c_first;          /* S2C-first bootstrap variant [0] */
   int32_t trace;              /* print per-node levels [0] */
   int32_t device;             /* CUDA device ordinal [0] */
-  uint32_t reserved;
+  uint32_t sparse_h;          /* sparse-secret encapsulation weight for bootstrapping [0: off] */
   uint64_t seed;              /* key seed [1] */
 } fhe_program_options;
 

@@ -229,6 +229,40 @@ class Ckks:
         self.L_.oc_keygen_switch(self.h, seed, key_id, _p64(s_ntt), _p64(sp_ntt), _p64(evk))
         return evk
 
+    def sparse_secret(self, seed, h):
+        """Sparse ternary secret of Hamming weight h for bootstrapping's key
+        encapsulation (FIDESlib's SPARSE_ENCAPSULATED distribution, selected by
+        the reference's decode driver at
+        native/fideslib_stage0/src/stage1_mamba2_decode_fideslib.cpp:284-291).
+        FIDESlib itself is not vendored; the sampler here is this build's own
+        definition: a splitmix64 stream keyed by seed ^ golden ^ (h << 32) picks
+        h distinct positions by Floyd's algorithm and a sign for each.
+        Returns (coefficients, NTT form over all L+K primes)."""
+        m64 = (1 << 64) - 1
+        st = [(seed ^ 0x9E3779B97F4A7C15 ^ (h << 32)) & m64]
+
+        def nxt():
+            st[0] = (st[0] + 0x9E3779B97F4A7C15) & m64
+            z = st[0]
+            z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & m64
+            z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & m64
+            return z ^ (z >> 31)
+
+        coef = np.zeros(self.n, dtype=np.int64)
+        for j in range(self.n - h, self.n):
+            t = nxt() % (j + 1)
+            pos = t if coef[t] == 0 else j
+            coef[pos] = 1 if nxt() & 1 else -1
+        sn = self.zeros(self.L + self.K)
+        self.L_.oc_lift_small(self.h, _pi64(coef), _p64(sn), self.L, self.K, 1)
+        return coef, sn
+
+    def sparse_keys(self, seed, s_ntt, sp_ntt):
+        """Switching keys s -> s' and s' -> s of the encapsulation, under the
+        key ids 2N+1 and 2N+3 (past every Galois element)."""
+        return (self.keygen_switch(seed, 2 * self.n + 1, sp_ntt, s_ntt),
+                self.keygen_switch(seed, 2 * self.n + 3, s_ntt, sp_ntt))
+
     def relin_key(self, seed, s_ntt):
         # s^2 over all L+K limbs (limb l of a full-width array sits on prime l)
         sq = self._bin("oc_mul_pointwise", s_ntt, s_ntt, self.L + self.K)

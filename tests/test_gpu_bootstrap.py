@@ -224,3 +224,38 @@ def test_s2c_first_bootstrap():
     from fhe_mamba_b200 import StateError
     with pytest.raises(StateError):
         cc.EvalBootstrap(short)
+
+
+def test_sparse_encapsulated_bootstrap(oracle):
+    """Sparse-secret encapsulation: the sparse secret and both switching keys
+    equal the oracle's word for word; the bootstrap keeps more limbs than the
+    uniform-ternary one (smaller EvalMod interval, lower degree, 3 double
+    angles) and decrypts to its input."""
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    h = 32
+    cc = CryptoContext(CCParams(ring_dim=1 << 12, multiplicative_depth=25, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3))
+    cc.KeyGen(SEED)
+    cc.EvalBootstrapSetup((4, 4), sparse_hamming_weight=h)
+    cc.EvalBootstrapKeyGen()
+    oc = oracle.Ckks(12, cc.q, cc.p, 3, cc.slots)
+    coef, spn = oc.sparse_secret(SEED, h)
+    assert np.count_nonzero(coef) == h and set(np.unique(coef)) <= {-1, 0, 1}
+    assert np.array_equal(cc.key(4).reshape(spn.shape), spn)
+    s, sn = oc.keygen_secret(SEED)
+    to_sparse, to_dense = oc.sparse_keys(SEED, sn, spn)
+    assert np.array_equal(cc.key(5).reshape(to_sparse.shape), to_sparse)
+    assert np.array_equal(cc.key(6).reshape(to_dense.shape), to_dense)
+    info = cc.bootstrap_info()
+    assert info["chebyshev_degree"] < 60
+    r = np.random.default_rng(29)
+    for cplx in (False, True):
+        x = r.uniform(-1, 1, cc.slots) + (1j * r.uniform(-1, 1, cc.slots) if cplx else 0)
+        ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+        cc.LevelReduceInPlace(ct, cc.n_q - 2)
+        out = cc.EvalBootstrap(ct)
+        lv = cc.bootstrap_levels()
+        assert lv[0] == cc.n_q and lv[1] == cc.n_q - 4 and lv[2] - lv[3] == 4
+        assert out.n_limbs() > cc.n_q - 21 + 2  # at least 3 levels above uniform ternary
+        y = cc.Decrypt(out).GetCKKSPackedValue()
+        assert np.max(np.abs((y if cplx else y.real) - x)) < 1e-4
