@@ -278,6 +278,66 @@ def measure_bootstrap(cc, reps=3):
             "rotation_keys": info["rotation_keys"]}
 
 
+def measure_sharded_keyswitch(local, world, reps=20):
+    """Limb-sharded relinearisation over the ranks (round-robin limbs, two NCCL
+    all-gathers per key switch) at the token loop's top level (45 limbs) and at
+    the config-3 level (20 limbs), N=2^16, dnum 3: device time per key switch
+    (CUDA events on the context stream, max over ranks), the single-GPU time of
+    the same key switch on this box, and a word-for-word check of the own rows
+    against the single-GPU result."""
+    import torch
+    import torch.distributed as dist
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    from fhe_mamba_b200.shard import ShardedKeySwitch, to_device_rows, to_host_rows
+    dev = torch.device("cuda", local)
+    cc = CryptoContext(CCParams(ring_dim=1 << 16, multiplicative_depth=44, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3, device=local))
+    cc.KeyGen(7)
+    sk = ShardedKeySwitch(cc)
+    sk.load_key(2)
+    cases = []
+    for nq in (cc.n_q, 20):
+        rng = np.random.default_rng(nq)
+        d = np.empty((3, nq, cc.n), dtype=np.uint64)
+        for l in range(nq):
+            d[:, l, :] = rng.integers(0, cc.q[l], size=(3, cc.n), dtype=np.uint64)
+        full = cc.upload(d, noise_deg=2)
+        want = cc.Relinearize(full).residues()
+        own = to_device_rows(sk.plan.own_rows(d, nq), dev)
+        exact = np.array_equal(to_host_rows(sk.relinearize(own, nq)), sk.plan.own_rows(want, nq))
+        for _ in range(3):
+            sk.relinearize(own, nq)
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(sk.stream)
+        for _ in range(reps):
+            sk.relinearize(own, nq)
+        e1.record(sk.stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        for _ in range(3):
+            cc.Relinearize(full)
+        cc.synchronize()
+        e0.record(sk.stream)
+        for _ in range(reps):
+            cc.Relinearize(full)
+        e1.record(sk.stream)
+        e1.synchronize()
+        single = e0.elapsed_time(e1) / reps
+        t = torch.tensor([ms, single, 0.0 if exact else 1.0], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pl = sk.plan
+        gather = (world - 1) * (pl.q_chunk(nq) + 2 * pl.p_chunk) * cc.n * 8
+        cases.append({"limbs": nq, "ms": float(t[0]), "single_gpu_ms": float(t[1]),
+                      "speedup": float(t[1] / t[0]), "bit_exact_all_ranks": bool(t[2] == 0.0),
+                      "received_bytes_per_rank": gather})
+        del full
+    cc.close()
+    return {"world": world, "layout": "round-robin RNS limbs, NCCL all-gathers of the ModUp and ModDown limbs",
+            "cases": cases}
+
+
 class TokenLoop:
     """The 24-layer encrypted greedy loop: client encrypt -> server layers -> client select."""
 
@@ -462,6 +522,9 @@ def main():
     side = {}
     if world == 1 and not args.no_ckks:
         side["keyswitch"], side["bsgs_matvec"] = measure_ckks(local)
+
+    if world > 1 and not args.no_ckks:
+        side["sharded_keyswitch"] = measure_sharded_keyswitch(local, world)
 
     loop = TokenLoop(local, layers=args.layers, passes=args.passes, seed=6 + rank, sparse_h=args.sparse_h)
     stream = torch.cuda.ExternalStream(loop.cc.stream_ptr(), device=torch.device("cuda", local))

@@ -121,6 +121,13 @@ SIGNATURES = {
     "fhe_linear_transform": [vp, vp, ctypes.POINTER(vp), u32, u32, i32, i32, ctypes.POINTER(vp)],
     "fhe_ctx_counters": [vp, vp, i32],
     "fhe_kernel_launches": [ctypes.POINTER(ctypes.c_uint64)],
+    "fhe_shard_init": [vp, u32, u32],
+    "fhe_shard_plan_get": [vp, u32, vp],
+    "fhe_shard_load_key": [vp, i32, u64],
+    "fhe_shard_modup_prepare": [vp, u32, vp, vp],
+    "fhe_shard_inner": [vp, u32, i32, u64, vp, vp, vp, vp],
+    "fhe_shard_moddown": [vp, u32, vp, vp, vp, vp, vp],
+    "fhe_shard_automorphism": [vp, u32, u64, vp, vp],
     "fhe_bootstrap_setup": [vp, u32, u32, u32, i32, i32, u32],
     "fhe_bootstrap_keygen": [vp],
     "fhe_bootstrap": [vp, vp, ctypes.POINTER(vp)],

@@ -14,6 +14,7 @@
 #include "ckks.h"
 #include "context.h"
 #include "program.h"
+#include "shard.h"
 #include "launch_count.h"
 
 namespace fhe {
@@ -25,6 +26,7 @@ struct fhe_ctx {
   fhe::Context c;
   std::unique_ptr<fhe::Ckks> ck;
   std::unique_ptr<fhe::Bootstrapper> boot;
+  std::unique_ptr<fhe::ShardKeySwitch> shard;
 };
 struct fhe_ct {
   std::unique_ptr<fhe::Ct> p;
@@ -553,6 +555,78 @@ int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* dia
     std::vector<const fhe::Pt*> d((size_t)baby * giant);
     for (size_t i = 0; i < d.size(); ++i) d[i] = diags[i] ? diags[i]->p.get() : nullptr;
     put_ct(out, k.linear_transform(ct_of(a), d, baby, giant, stride, giant_offset));
+  });
+}
+
+// ---- limb-sharded key switching ----------------------------------------
+
+namespace {
+fhe::ShardKeySwitch& shard_of(fhe_ctx* ctx) {
+  ckks(ctx);
+  fhe::require(ctx->shard != nullptr, "no shard set up (fhe_shard_init)", FHE_ERR_STATE);
+  return *ctx->shard;
+}
+}  // namespace
+
+int fhe_shard_init(fhe_ctx* ctx, uint32_t rank, uint32_t world) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    ctx->shard.reset();
+    ctx->shard = std::make_unique<fhe::ShardKeySwitch>(k, rank, world);
+  });
+}
+
+int fhe_shard_plan_get(fhe_ctx* ctx, uint32_t n_limbs, fhe_shard_plan* out) {
+  return guarded([&] {
+    fhe::require(out != nullptr, "null plan");
+    const fhe::ShardPlan p = shard_of(ctx).plan(n_limbs);
+    out->n_limbs = p.nq;
+    out->q_own = p.q_own;
+    out->q_chunk = p.q_chunk;
+    out->p_own = p.p_own;
+    out->p_chunk = p.p_chunk;
+    out->rows = p.rows;
+    out->digits = p.digits;
+    out->reserved = 0;
+  });
+}
+
+int fhe_shard_load_key(fhe_ctx* ctx, int32_t kind, uint64_t galois) {
+  return guarded([&] { shard_of(ctx).load_key(kind, galois); });
+}
+
+int fhe_shard_modup_prepare(fhe_ctx* ctx, uint32_t n_limbs, const uint64_t* d_own, uint64_t* send) {
+  return guarded([&] {
+    fhe::require(send != nullptr && (d_own != nullptr || shard_of(ctx).plan(n_limbs).q_own == 0), "null buffer");
+    shard_of(ctx).modup_prepare(n_limbs, d_own, send);
+  });
+}
+
+int fhe_shard_inner(fhe_ctx* ctx, uint32_t n_limbs, int32_t kind, uint64_t galois, const uint64_t* gathered,
+                    const uint64_t* d_own, uint64_t* acc, uint64_t* p_send) {
+  return guarded([&] {
+    const fhe::ShardPlan p = shard_of(ctx).plan(n_limbs);
+    fhe::require(gathered != nullptr && (acc != nullptr || p.rows == 0) && (p_send != nullptr || p.p_chunk == 0) &&
+                     (d_own != nullptr || p.q_own == 0),
+                 "null buffer");
+    shard_of(ctx).inner(n_limbs, kind, galois, gathered, d_own, acc, p_send);
+  });
+}
+
+int fhe_shard_moddown(fhe_ctx* ctx, uint32_t n_limbs, const uint64_t* acc, const uint64_t* p_gathered,
+                      const uint64_t* add0, const uint64_t* add1, uint64_t* out) {
+  return guarded([&] {
+    const fhe::ShardPlan p = shard_of(ctx).plan(n_limbs);
+    fhe::require(p.q_own == 0 || (acc != nullptr && p_gathered != nullptr && out != nullptr), "null buffer");
+    shard_of(ctx).moddown(n_limbs, acc, p_gathered, add0, add1, out);
+  });
+}
+
+int fhe_shard_automorphism(fhe_ctx* ctx, uint32_t n_limbs, uint64_t galois, const uint64_t* in, uint64_t* out) {
+  return guarded([&] {
+    fhe::require(shard_of(ctx).plan(n_limbs).q_own == 0 || (in != nullptr && out != nullptr && in != out),
+                 "automorphism needs distinct buffers");
+    shard_of(ctx).automorphism(n_limbs, galois, in, out);
   });
 }
 

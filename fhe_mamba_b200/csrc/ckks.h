@@ -176,6 +176,7 @@ class Ckks {
 
  public:
   ~Ckks();
+  friend class ShardKeySwitch;
 };
 
 }  // namespace fhe

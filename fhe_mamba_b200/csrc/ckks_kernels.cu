@@ -299,7 +299,8 @@ __global__ void k_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, siz
 #pragma unroll
   for (int i = 0; i < NS; ++i) {
     const Shoup h = t.hatinv[i];
-    y[i] = shoup_mul(s[(size_t)i * n + k], h.w, h.wp, mods[t.src_prime[i]].q);
+    const size_t row = t.src_row ? t.src_row[i] : (uint32_t)i;
+    y[i] = shoup_mul(s[row * n + k], h.w, h.wp, mods[t.src_prime[i]].q);
   }
   for (uint32_t u = 0; u < nt; ++u) {
     uint64_t hi = 0, lo = 0;
@@ -310,7 +311,8 @@ __global__ void k_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, siz
       lo += pl;
       hi += __umul64hi(y[i], cst) + (lo < pl);
     }
-    d[(size_t)(t0 + u) * n + k] = reduce_u128(hi, lo, sh_m[u]);
+    const size_t row = t.dst_row ? t.dst_row[t0 + u] : t0 + u;
+    d[row * n + k] = reduce_u128(hi, lo, sh_m[u]);
   }
 }
 
@@ -625,7 +627,7 @@ void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uin
     const dim3 grid = grid1(n, count, chunks);
     switch (ns) {
 #define FHE_CASE(NS) \
-  case NS: k_modup<NS><<<grid, kTpb, 0, s>>>(coef, dntt, ext, nq + K, n, digits_dev, digit0, mods); break; note_launch();
+  case NS: k_modup<NS><<<grid, kTpb, 0, s>>>(coef, dntt, ext, nq + K, n, digits_dev, digit0, mods); note_launch(); break;
       FHE_NS_CASES(FHE_CASE)
 #undef FHE_CASE
       default: break;
@@ -648,7 +650,7 @@ void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_
   const dim3 grid = grid1(n, ncomp, chunks);
   switch (ns) {
 #define FHE_CASE(NS) \
-  case NS: k_convert<NS><<<grid, kTpb, 0, s>>>(src, s_comp, dst, d_comp, t_dev, n, mods); break; note_launch();
+  case NS: k_convert<NS><<<grid, kTpb, 0, s>>>(src, s_comp, dst, d_comp, t_dev, n, mods); note_launch(); break;
     FHE_NS_CASES(FHE_CASE)
 #undef FHE_CASE
     default: break;

@@ -28,6 +28,10 @@ struct ConvTable {
   const uint32_t* dst_prime;  // [nt]
   const Shoup* hatinv;        // [ns]
   const Shoup* hat;           // [nt][ns]
+  // Optional row maps (null: identity): source i is read from row src_row[i]
+  // of its component, target t is written to row dst_row[t].
+  const uint32_t* src_row = nullptr;
+  const uint32_t* dst_row = nullptr;
 };
 
 // ---- randomness (ChaCha20, same streams as the oracle) ----

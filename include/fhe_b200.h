@@ -227,6 +227,43 @@ int fhe_encode_batch(fhe_ctx* ctx, const double* re, const double* im, uint32_t 
 int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* diags, uint32_t baby,
                          uint32_t giant, int32_t stride, int32_t giant_offset, fhe_ct** out);
 
+/* --- limb-sharded key switching (one process per GPU) ----------------------
+ * The multi-GPU mode of the north star: RNS limbs dealt out round-robin, rank
+ * r of W owning Q limbs l % W == r and P limbs p % W == r, so every
+ * limb-local operation (NTT, products, rescale epilogue, automorphism) needs
+ * no communication and a HYBRID key switch (FIDESlib's KeySwitch behind
+ * EvalMult / EvalRotate, packed_fideslib.cpp:149,215-217) needs exactly two
+ * all-gathers, which the caller runs on the context stream (fhe_ctx_stream)
+ * with its own collective library:
+ *   fhe_shard_modup_prepare  -> all-gather send [q_chunk][N] into [W][q_chunk][N]
+ *   fhe_shard_inner          -> all-gather p_send [2][p_chunk][N] into [W][2][p_chunk][N]
+ *   fhe_shard_moddown        -> out [2][q_own][N] (+ add0 / add1 per component)
+ * Buffers are device pointers on the context's device, rows of N words, own
+ * rows in increasing limb order.  Results equal the single-GPU key switch
+ * word for word.  Keys are generated whole on every rank and their own rows
+ * copied out by fhe_shard_load_key. */
+typedef struct fhe_shard_plan {
+  uint32_t n_limbs;  /* live Q limbs */
+  uint32_t q_own;    /* own Q limbs: l = rank + i*world */
+  uint32_t q_chunk;  /* rows per rank in the first all-gather (ceil(n_limbs / world)) */
+  uint32_t p_own;    /* own P limbs */
+  uint32_t p_chunk;  /* rows per rank and component in the second all-gather */
+  uint32_t rows;     /* own extended rows: q_own + p_own (acc is [2][rows][N]) */
+  uint32_t digits;   /* HYBRID digits at this level */
+  uint32_t reserved;
+} fhe_shard_plan;
+int fhe_shard_init(fhe_ctx* ctx, uint32_t rank, uint32_t world);
+int fhe_shard_plan_get(fhe_ctx* ctx, uint32_t n_limbs, fhe_shard_plan* out);
+/* kind 2: relinearisation key; 3: rotation key of Galois element `galois`. */
+int fhe_shard_load_key(fhe_ctx* ctx, int32_t kind, uint64_t galois);
+int fhe_shard_modup_prepare(fhe_ctx* ctx, uint32_t n_limbs, const uint64_t* d_own, uint64_t* send);
+int fhe_shard_inner(fhe_ctx* ctx, uint32_t n_limbs, int32_t kind, uint64_t galois, const uint64_t* gathered,
+                    const uint64_t* d_own, uint64_t* acc, uint64_t* p_send);
+int fhe_shard_moddown(fhe_ctx* ctx, uint32_t n_limbs, const uint64_t* acc, const uint64_t* p_gathered,
+                      const uint64_t* add0, const uint64_t* add1, uint64_t* out);
+/* Slot permutation of both components of the own rows ([2][q_own][N]). */
+int fhe_shard_automorphism(fhe_ctx* ctx, uint32_t n_limbs, uint64_t galois, const uint64_t* in, uint64_t* out);
+
 /* Number of kernels this library has launched in this process (all contexts). */
 int fhe_kernel_launches(uint64_t* count);
 
