@@ -489,7 +489,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ckks", action="store_true", help="skip the key-switch, matvec and bootstrap side measurements")
     ap.add_argument("--ckks-only", action="store_true",
-                    help="print only the config-3 key-switch measurement (small profiling runs)")
+                    help="print only the key-switch measurement: config 3 on one GPU, limb-sharded under torchrun")
     ap.add_argument("--kernel-shares", action="store_true",
                     help="after the warm-up, record one token's kernels (CUPTI) and print their time shares")
     args = ap.parse_args()
@@ -508,13 +508,19 @@ def main():
     import torch.distributed as dist
 
     torch.cuda.set_device(local)
-    if args.ckks_only:
+    if args.ckks_only and world == 1:
         ks, _ = measure_ckks(local, matvec=False)
         print(json.dumps({"keyswitch": ks}), flush=True)
         return
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=torch.device("cuda", local))
+    if args.ckks_only:
+        sharded = measure_sharded_keyswitch(local, world)
+        if rank == 0:
+            print(json.dumps({"sharded_keyswitch": sharded}), flush=True)
+        dist.destroy_process_group()
+        return
 
     from fhe_mamba_b200 import _lib
 
