@@ -42,6 +42,14 @@ struct PassShape {
   static constexpr int J = R * (T - 1) / T;  // round-2 twiddles per thread
 };
 
+// Minimum resident CTAs per SM for a pass of 2^LS words per sub-problem and
+// TW sub-problems per CTA: ~100 registers per thread for LS <= 8 (R = 16
+// words in registers plus twiddles without spilling), ~170 for LS = 9.
+template <int LS, int TW>
+constexpr int min_blocks() {
+  return LS <= 8 ? 40 / TW : 24 / TW;
+}
+
 // Forward Cooley-Tukey (Harvey) butterfly on lazy residues in [0, 4q).
 __device__ __forceinline__ void ct_bfly(uint64_t& x, uint64_t& y, const Twiddle tw, uint64_t q,
                                         uint64_t q2) {
@@ -112,7 +120,7 @@ __device__ __forceinline__ Twiddle ld_tw(const Twiddle* t, uint32_t i) {
 // j = col0 + c + 2^LB * k for k in [0, 2^LA).  Warp w is thread t of each
 // column.  Round 1: k = t + T*u.  Round 2: k = R*t + u.
 template <int LA, int LZ, int COLS>
-__global__ void __launch_bounds__(COLS * PassShape<LA>::T, LA <= 8 ? 64 / COLS : 32 / COLS)
+__global__ void __launch_bounds__(COLS * PassShape<LA>::T, min_blocks<LA, COLS>())
     ntt_fwd_cols(const NttArgs g) {
   using P = PassShape<LA>;
   extern __shared__ uint64_t smem[];
@@ -176,16 +184,17 @@ __global__ void __launch_bounds__(COLS * PassShape<LA>::T, LA <= 8 ? 64 / COLS :
 __device__ __forceinline__ int rpad(int k) { return k + (k >> 4); }
 
 // ---------------------------------------------------------------------------
-// Forward, pass 2: rows.  A CTA owns ROWS rows of 2^LB contiguous words.  The
-// tile is staged through shared memory in both directions so global loads and
-// stores are contiguous.  Thread t of a row: round 1 k = t + T*u, round 2
-// k = R*t + u.  Final output reduced from [0, 4q) to [0, q).
+// Forward, pass 2: rows.  A CTA owns ROWS rows of 2^LB contiguous words.
+// Thread t of a row: round 1 k = t + T*u (loaded straight from HBM, each load
+// instruction covering 128-byte runs), round 2 k = R*t + u, then back through
+// shared memory to the k = t + T*u layout for the stores.  Final output
+// reduced to [0, q).
 //
 // With LZ > 0 the column pass leaves values below lz_bound_after(LZ, 1, LA) q;
 // this pass continues the greedy schedule and reduces the output with one
 // Shoup multiplication by 1 and a conditional subtraction.
 template <int LA, int LB, int ROWS, int LZ>
-__global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 64 / ROWS : 32 / ROWS)
+__global__ void __launch_bounds__(ROWS * PassShape<LB>::T, min_blocks<LB, ROWS>())
     ntt_fwd_rows(const NttArgs g) {
   using P = PassShape<LB>;
   extern __shared__ uint64_t smem[];
@@ -205,19 +214,13 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 64 / ROWS :
     else return csub(csub(v, q2), q);
   };
 
-  // Coalesced tile load: ROWS*S contiguous words.
-  constexpr int kThreads = ROWS * P::T;
-  for (int i = threadIdx.x; i < ROWS * P::S / 2; i += kThreads) {
-    const ulonglong2 v = reinterpret_cast<const ulonglong2*>(a)[i];
-    const int w = 2 * i, r = w / P::S, k = w % P::S;
-    smem[r * kRowWords + rpad(k)] = v.x;
-    smem[r * kRowWords + rpad(k + 1)] = v.y;
-  }
-  __syncthreads();
+  // Round-1 layout k = t + T*u: for each u the T threads of a row read T
+  // consecutive words, so every load instruction covers whole 128-byte runs.
   uint64_t x[P::R];
   uint64_t* srow = smem + rr * kRowWords;
+  uint64_t* grow = a + (size_t)rr * P::S;
 #pragma unroll
-  for (int u = 0; u < P::R; ++u) x[u] = srow[rpad(t + P::T * u)];
+  for (int u = 0; u < P::R; ++u) x[u] = grow[t + P::T * u];
 
   // Global stage for k-half-distance d: m = N/(2d); i = row*S/(2d) + k/(2d).
   int st = 0;
@@ -261,13 +264,8 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 64 / ROWS :
     for (int u = 0; u < P::R; ++u) srow[rpad(t + P::T * u)] = fwd_final(x[u], q, q2, mu);
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < ROWS * P::S / 2; i += kThreads) {
-    const int w = 2 * i, r = w / P::S, k = w % P::S;
-    ulonglong2 v;
-    v.x = smem[r * kRowWords + rpad(k)];
-    v.y = smem[r * kRowWords + rpad(k + 1)];
-    reinterpret_cast<ulonglong2*>(a)[i] = v;
-  }
+#pragma unroll
+  for (int u = 0; u < P::R; ++u) grow[t + P::T * u] = srow[rpad(t + P::T * u)];
 }
 
 // ---------------------------------------------------------------------------
@@ -275,7 +273,7 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 64 / ROWS :
 // Round 1 on contiguous runs k = R*t + u (half-distances 1 .. T/2), exchange,
 // round 2 on k = t + T*u (half-distances T .. S/2).  Input in [0, q).
 template <int LB, int ROWS>
-__global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 64 / ROWS : 32 / ROWS)
+__global__ void __launch_bounds__(ROWS * PassShape<LB>::T, min_blocks<LB, ROWS>())
     ntt_inv_rows(const NttArgs g) {
   using P = PassShape<LB>;
   extern __shared__ uint64_t smem[];
@@ -331,17 +329,10 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 64 / ROWS :
       for (int v = 0; v < h; ++v) gs_bfly(x[g + v], x[g + v + h], w, q, q2);
     }
   }
-  __syncthreads();
+  // Round-2 layout k = t + T*u stores whole 128-byte runs directly.
+  uint64_t* grow = a + (size_t)rr * P::S;
 #pragma unroll
-  for (int u = 0; u < P::R; ++u) srow[rpad(t + P::T * u)] = x[u];
-  __syncthreads();
-  for (int i = threadIdx.x; i < ROWS * P::S / 2; i += kThreads) {
-    const int w = 2 * i, r = w / P::S, k = w % P::S;
-    ulonglong2 v;
-    v.x = smem[r * kRowWords + rpad(k)];
-    v.y = smem[r * kRowWords + rpad(k + 1)];
-    reinterpret_cast<ulonglong2*>(a)[i] = v;
-  }
+  for (int u = 0; u < P::R; ++u) grow[t + P::T * u] = x[u];
 }
 
 // ---------------------------------------------------------------------------
@@ -350,7 +341,7 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, LB <= 8 ? 64 / ROWS :
 // The last stage (m = 1) folds in N^{-1}: x' = (x+y)/N, y' = (x-y)*w/N, with
 // tw_last = (N^{-1}, N^{-1}') and tw_last2 = (w_1 N^{-1}, ...).
 template <int LA, int COLS>
-__global__ void __launch_bounds__(COLS * PassShape<LA>::T, LA <= 8 ? 64 / COLS : 32 / COLS)
+__global__ void __launch_bounds__(COLS * PassShape<LA>::T, min_blocks<LA, COLS>())
     ntt_inv_cols(const NttArgs g) {
   using P = PassShape<LA>;
   extern __shared__ uint64_t smem[];
@@ -424,9 +415,9 @@ size_t cols_smem() {
   return P::LT > 0 ? (size_t)COLS * P::S * sizeof(uint64_t) : 0;
 }
 
-// Tile width: 32 columns / rows per CTA, or 16 when a launch would not fill
-// two waves of the 148 SMs (finer CTAs balance small batches better).
-inline int tile_width(uint32_t tiles32) { return tiles32 >= 2u * 2u * 148u ? 32 : 16; }
+// Tile width: 8 columns / rows per CTA (128 threads at 2^16).  Measured on
+// the config-2 batch against 16 and 32 with several register caps: small
+// CTAs with ~100 registers keep the integer pipes busiest.
 
 template <int LA, int LB, int LZ, int TW>
 cudaError_t launch_fwd_impl(const NttArgs& g) {
@@ -457,9 +448,7 @@ cudaError_t launch_fwd_tw(const NttArgs& g) {
 
 template <int LA, int LB>
 cudaError_t launch_fwd(const NttArgs& g) {
-  const uint32_t polys = g.list ? 1 : g.n_polys;
-  return tile_width(((1u << LB) / 32) * polys * g.n_limbs) == 32 ? launch_fwd_tw<LA, LB, 32>(g)
-                                                                   : launch_fwd_tw<LA, LB, 16>(g);
+  return launch_fwd_tw<LA, LB, 8>(g);
 }
 
 template <int LA, int LB, int TW>
@@ -482,9 +471,7 @@ cudaError_t launch_inv_tw(const NttArgs& g) {
 
 template <int LA, int LB>
 cudaError_t launch_inv(const NttArgs& g) {
-  const uint32_t polys = g.list ? 1 : g.n_polys;
-  return tile_width(((1u << LB) / 32) * polys * g.n_limbs) == 32 ? launch_inv_tw<LA, LB, 32>(g)
-                                                                   : launch_inv_tw<LA, LB, 16>(g);
+  return launch_inv_tw<LA, LB, 8>(g);
 }
 
 }  // namespace
@@ -498,8 +485,8 @@ void ntt_row_shape(int log_n, int& rows, int& R, int& T, int& J) {
   J = R * (T - 1) / T;
 }
 
-// log N = LA + LB with LA = floor(logN/2) >= 5 so both passes have >= 32
-// columns / rows per CTA tile.
+// log N = LA + LB with LA = floor(logN/2) >= 5 so both passes have at least
+// one full tile of 8 columns / rows.
 cudaError_t ntt_forward(const NttArgs& g) {
   if (g.n_limbs == 0 || g.n_polys == 0) return cudaSuccess;
   switch (g.log_n) {
