@@ -467,13 +467,20 @@ def measure_ntt(local, steps, warmup):
     torch.cuda.synchronize()
     fwd = sum(e[0].elapsed_time(e[1]) for e in evs) / steps
     inv = sum(e[1].elapsed_time(e[2]) for e in evs) / steps
+    ceiling = ctx.butterfly_ceiling()
     ctx.close()
+    butterflies = POLYS * LIMBS * (1 << (LOG_N - 1)) * LOG_N
     achieved = ALG_BYTES_PER_TRANSFORM / (fwd / 1e3) / 1e9
     peak, kind = peaks()
     return {"bound": "hbm", "kernel": "forward NTT (ntt_fwd_cols + ntt_fwd_rows), BASELINE config 2",
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": kind,
             "traffic": ncu_traffic(), "alg_bytes_per_launch": ALG_BYTES_PER_TRANSFORM, "fwd_ms": fwd,
-            "inv_ms": inv, "ntt_steps_per_s": 1e3 / (fwd + inv), "ntt_unit": NTT_UNIT, "config": ntt_config()}
+            "inv_ms": inv, "ntt_steps_per_s": 1e3 / (fwd + inv), "ntt_unit": NTT_UNIT, "config": ntt_config(),
+            "integer_pipe": {
+                "note": "the transform is bound by the 64-bit multiply pipe, not HBM: ceiling = the same lazy "
+                        "Shoup butterfly on registers only, measured live on this GPU",
+                "butterflies_per_launch": butterflies, "achieved": butterflies / (fwd / 1e3),
+                "ceiling": ceiling, "unit": "butterflies/s", "frac": butterflies / (fwd / 1e3) / ceiling}}
 
 
 def main():
@@ -490,6 +497,8 @@ def main():
     ap.add_argument("--no-ckks", action="store_true", help="skip the key-switch, matvec and bootstrap side measurements")
     ap.add_argument("--ckks-only", action="store_true",
                     help="print only the key-switch measurement: config 3 on one GPU, limb-sharded under torchrun")
+    ap.add_argument("--ntt-only", action="store_true",
+                    help="print only the config-2 NTT roofline measurement (profiling runs)")
     ap.add_argument("--kernel-shares", action="store_true",
                     help="after the warm-up, record one token's kernels (CUPTI) and print their time shares")
     args = ap.parse_args()
@@ -508,6 +517,9 @@ def main():
     import torch.distributed as dist
 
     torch.cuda.set_device(local)
+    if args.ntt_only:
+        print(json.dumps({"roofline": measure_ntt(local, steps=20, warmup=5)}), flush=True)
+        return
     if args.ckks_only and world == 1:
         ks, _ = measure_ckks(local, matvec=False)
         print(json.dumps({"keyswitch": ks}), flush=True)

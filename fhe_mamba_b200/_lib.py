@@ -121,6 +121,7 @@ SIGNATURES = {
     "fhe_linear_transform": [vp, vp, ctypes.POINTER(vp), u32, u32, i32, i32, ctypes.POINTER(vp)],
     "fhe_ctx_counters": [vp, vp, i32],
     "fhe_kernel_launches": [ctypes.POINTER(ctypes.c_uint64)],
+    "fhe_ntt_butterfly_ceiling": [vp, ctypes.POINTER(ctypes.c_double)],
     "fhe_shard_init": [vp, u32, u32],
     "fhe_shard_plan_get": [vp, u32, vp],
     "fhe_shard_load_key": [vp, i32, u64],

@@ -630,6 +630,42 @@ int fhe_shard_automorphism(fhe_ctx* ctx, uint32_t n_limbs, uint64_t galois, cons
   });
 }
 
+int fhe_ntt_butterfly_ceiling(fhe_ctx* ctx, double* butterflies_per_s) {
+  return guarded([&] {
+    fhe::require(ctx != nullptr && butterflies_per_s != nullptr, "null argument");
+    fhe::Context& c = ctx->c;
+    c.make_current();
+    int sms = 0;
+    FHE_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c.device));
+    const uint32_t blocks = (uint32_t)sms * 8;
+    const int rounds = 64;
+    fhe::DevMem out((size_t)blocks * 256 * 8), in(1024 * 8);
+    std::vector<uint64_t> h(1024);
+    for (size_t i = 0; i < h.size(); ++i) h[i] = 0x9E3779B97F4A7C15ull * (i + 1);
+    FHE_CUDA(cudaMemcpy(in.p, h.data(), h.size() * 8, cudaMemcpyHostToDevice));
+    const uint64_t q = c.primes[0];
+    const uint64_t wv = c.roots[0] % q;
+    const fhe::Twiddle w{wv, fhe::nt::shoup(wv, q)};
+    cudaEvent_t e0, e1;
+    FHE_CUDA(cudaEventCreate(&e0));
+    FHE_CUDA(cudaEventCreate(&e1));
+    for (int r = 0; r < 2; ++r)
+      FHE_CUDA(fhe::ntt_butterfly_ceiling(q, w, out.as<uint64_t>(), in.as<uint64_t>(), blocks, rounds, c.stream));
+    FHE_CUDA(cudaEventRecord(e0, c.stream));
+    const int reps = 5;
+    for (int r = 0; r < reps; ++r)
+      FHE_CUDA(fhe::ntt_butterfly_ceiling(q, w, out.as<uint64_t>(), in.as<uint64_t>(), blocks, rounds, c.stream));
+    FHE_CUDA(cudaEventRecord(e1, c.stream));
+    FHE_CUDA(cudaEventSynchronize(e1));
+    float ms = 0;
+    FHE_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    const double bfly = (double)blocks * 256 * rounds * 8 * 8 * reps;
+    *butterflies_per_s = bfly / (ms / 1e3);
+  });
+}
+
 int fhe_kernel_launches(uint64_t* count) {
   if (!count) return FHE_ERR_INVALID;
   *count = fhe::g_kernel_launches.load();

@@ -286,17 +286,17 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, min_blocks<LB, ROWS>(
   const int t = threadIdx.x % P::T;
   const int rr = threadIdx.x / P::T;
   const uint32_t row = blockIdx.x * ROWS + rr;
-  constexpr int kThreads = ROWS * P::T;
 
-  for (int i = threadIdx.x; i < ROWS * P::S / 2; i += kThreads) {
-    const ulonglong2 v = reinterpret_cast<const ulonglong2*>(a)[i];
-    const int w = 2 * i, r = w / P::S, k = w % P::S;
-    smem[r * kRowWords + rpad(k)] = v.x;
-    smem[r * kRowWords + rpad(k + 1)] = v.y;
-  }
-  __syncthreads();
+  // Coalesced load in the k = t + T*u layout, staged through shared memory
+  // for round 1's contiguous runs.
   uint64_t x[P::R];
   uint64_t* srow = smem + rr * kRowWords;
+  {
+    const uint64_t* grow = a + (size_t)rr * P::S;
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) srow[rpad(t + P::T * u)] = grow[t + P::T * u];
+  }
+  __syncthreads();
   if constexpr (P::LT > 0) {
 #pragma unroll
     for (int u = 0; u < P::R; ++u) x[u] = srow[rpad(P::R * t + u)];
@@ -474,7 +474,43 @@ cudaError_t launch_inv(const NttArgs& g) {
   return launch_inv_tw<LA, LB, 8>(g);
 }
 
+// Integer-pipe ceiling of the forward butterfly: the same lazy Shoup
+// butterfly and reduction schedule as the column pass (8 stages, LZ = 16),
+// on 16 words held in registers with no memory traffic, 2 x 8 butterflies per
+// stage.  Each thread stores one word (the XOR of its registers) so the work
+// cannot be removed; `in` holds 1024 words.
+__global__ void __launch_bounds__(256) k_butterfly_ceiling(uint64_t* out, const uint64_t* in, uint64_t q,
+                                                            Twiddle w, int rounds) {
+  const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+  uint64_t x[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = in[(tid * 16 + i) & 1023u] % q;
+  const uint64_t q2 = 2 * q, qh = 8 * q;
+  for (int r = 0; r < rounds; ++r) {
+#pragma unroll
+    for (int st = 0; st < 8; ++st) {
+      const bool red = lz_reduce(16, 1, st);
+      const int h = 1 << (st & 3);
+#pragma unroll
+      for (int g = 0; g < 16; g += 2 * h)
+#pragma unroll
+        for (int v = 0; v < h; ++v) fwd_bfly<16>(red, x[g + v], x[g + v + h], w, q, q2, qh);
+    }
+  }
+  uint64_t acc = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc ^= x[i];
+  out[tid] = acc;
+}
+
 }  // namespace
+
+cudaError_t ntt_butterfly_ceiling(uint64_t q, Twiddle w, uint64_t* scratch_out, const uint64_t* scratch_in,
+                                  uint32_t blocks, int rounds, cudaStream_t s) {
+  k_butterfly_ceiling<<<blocks, 256, 0, s>>>(scratch_out, scratch_in, q, w, rounds);
+  note_launch();
+  return cudaGetLastError();
+}
 
 void ntt_row_shape(int log_n, int& rows, int& R, int& T, int& J) {
   const int LA = log_n / 2, LB = log_n - LA;

@@ -37,6 +37,11 @@ struct NttArgs {
 void ntt_row_shape(int log_n, int& rows, int& R, int& T, int& J);
 
 cudaError_t ntt_forward(const NttArgs& args);
+// Register-only throughput probe of the forward butterfly (see ntt.cu):
+// blocks x 256 threads, each 128 butterflies per round; scratch_out holds
+// blocks*256 words, scratch_in 1024 words.
+cudaError_t ntt_butterfly_ceiling(uint64_t q, Twiddle w, uint64_t* scratch_out, const uint64_t* scratch_in,
+                                  uint32_t blocks, int rounds, cudaStream_t s);
 cudaError_t ntt_inverse(const NttArgs& args);
 
 }  // namespace fhe

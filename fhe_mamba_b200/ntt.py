@@ -48,6 +48,13 @@ class NttContext:
     def synchronize(self):
         call("fhe_ctx_synchronize", self._h)
 
+    def butterfly_ceiling(self) -> float:
+        """Butterflies/s of the forward butterfly run on registers only (the
+        integer-pipe roofline of the transform on this GPU)."""
+        out = ctypes.c_double()
+        call("fhe_ntt_butterfly_ceiling", self._h, ctypes.byref(out))
+        return out.value
+
     def _run(self, name, data, limb0):
         if _is_torch_cuda(data):
             if data.dim() != 3 or data.shape[-1] != self.n or not data.is_contiguous():

@@ -264,6 +264,12 @@ int fhe_shard_moddown(fhe_ctx* ctx, uint32_t n_limbs, const uint64_t* acc, const
 /* Slot permutation of both components of the own rows ([2][q_own][N]). */
 int fhe_shard_automorphism(fhe_ctx* ctx, uint32_t n_limbs, uint64_t galois, const uint64_t* in, uint64_t* out);
 
+/* Integer-pipe ceiling of the NTT: butterflies per second of the forward
+ * transform's lazy Shoup butterfly (same arithmetic and reduction schedule)
+ * run on registers only, all SMs, on the context's device and stream.  The
+ * roofline that bounds the NTT on this GPU besides HBM bandwidth. */
+int fhe_ntt_butterfly_ceiling(fhe_ctx* ctx, double* butterflies_per_s);
+
 /* Number of kernels this library has launched in this process (all contexts). */
 int fhe_kernel_launches(uint64_t* count);
 

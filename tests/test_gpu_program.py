@@ -59,3 +59,21 @@ def test_gate_failure_exit_code(tmp_path):
 def test_bad_arguments_exit_code(tmp_path):
     r, _ = _run_cli(tmp_path, "packed_linear_v2.txt", 1e-6, 1e-6, "--no-such-flag")
     assert r.returncode == 2 and "unknown packed option" in r.stderr
+
+
+def test_mamba3_siso_generation(tmp_path):
+    """A 2-layer Mamba-3 SISO model (random init, d_model 64, d_state 16)
+    compiled by the reference's exporter path (tests/golden/make_mamba3_program.py):
+    3 prompt tokens and 2 client-feedback steps, where the client decrypts the
+    final hidden vector, picks the greedy token with the tied head and feeds
+    its embedding back (three generated tokens).  The tokens must equal the
+    reference's polynomial and exact paths and every output must stay within
+    1e-2 of both references."""
+    with open(os.path.join(GOLDEN, "mamba3_tokens.json")) as f:
+        want = json.load(f)
+    r, rep = _run_cli(tmp_path, "packed_mamba3_siso_v2.txt", 1e-2, 1e-2, "--client-head",
+                      os.path.join(GOLDEN, "mamba3_client_head.f32"))
+    assert r.returncode == 0, r.stderr
+    assert rep["passed"] and rep["non_finite"] == 0
+    assert rep["generated_token_ids"] == want["polynomial_token_ids"] == want["exact_token_ids"]
+    assert rep["bootstraps"] > 0

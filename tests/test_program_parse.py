@@ -19,6 +19,7 @@ GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
     ("packed_all_ops_v2.txt", 256, 16, 2),
     ("packed_linear_v2.txt", 2048, 3, 2),
     ("packed_refresh_v2.txt", 256, 61, 1),
+    ("packed_mamba3_siso_v2.txt", 2048, 1335, 5),
 ])
 def test_fixtures_parse(name, slots, nodes, outputs):
     assert validate_program(os.path.join(GOLDEN, name)) == {"slots": slots, "nodes": nodes, "outputs": outputs}
