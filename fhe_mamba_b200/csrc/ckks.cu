@@ -175,6 +175,7 @@ LevelTables& Ckks::level(uint32_t nq) {
   const auto& P = ctx.primes;
   T.nq = nq;
   T.D = (nq + a - 1) / a;
+  require(T.D <= 15, "more than 15 key-switching digits (the 128-bit key inner product sums at most 15)", -1);
   T.w = nq + K;
   const PrimeMap pm{nq, L};
   // One blob per level; per digit: src_prime[ns] | dst_prime[nt] | hatinv[ns] | hat[nt][ns].
@@ -597,8 +598,13 @@ void Ckks::modup(const uint64_t* d, uint32_t nq, uint64_t* ext) {
   const uint32_t n = ctx.n;
   LevelTables& T = level(nq);
   uint64_t* coef = ws(1, (size_t)ctx.L * n);
-  FHE_CUDA(cudaMemcpyAsync(coef, d, (size_t)nq * n * 8, cudaMemcpyDeviceToDevice, ctx.stream));
-  ntt_dense(coef, 1, nq, nq, 0, true);
+  {  // coef = INTT(d), out of place
+    counters.ntt_limbs += nq;
+    NttArgs a = ctx.ntt_args(coef, 1, 0, nq, nq);
+    a.src = d;
+    a.src_limb_stride = nq;
+    FHE_CUDA(ntt_inverse(a));
+  }
   launch_modup(coef, d, ext, nq, ctx.K, n, T.digits.as<ModUpDigit>(), T.D, ctx.alpha, ctx.d_mod.as<Modulus>(),
                ctx.stream);
   ++counters.modup;
@@ -620,9 +626,17 @@ void Ckks::moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, co
   uint64_t* conv = ws(3, (size_t)2 * ctx.L * n);
   launch_convert(acc + (size_t)nq * n, (size_t)w * n, conv, (size_t)nq * n, 2, T.moddown.as<ConvTable>(), K, nq, n,
                  ctx.d_mod.as<Modulus>(), ctx.stream);
-  ntt_dense(conv, 2, nq, nq, 0, false);
-  launch_moddown_combine(acc, (size_t)w * n, conv, (size_t)nq * n, pinv_.as<Shoup>(), add_c0, out, so, 2, nq, n,
-                         ctx.d_primes.as<uint64_t>(), ctx.stream);
+  // NTT of the conversion with the combine fused into its last pass:
+  // out = (acc - NTT(conv)) * P^{-1} (+ c0 on component 0).
+  counters.ntt_limbs += 2ull * nq;
+  NttArgs a = ctx.ntt_args(conv, 2, 0, nq, nq);
+  a.epi_x = acc;
+  a.epi_x_comp = (size_t)w * n;
+  a.epi_out = out;
+  a.epi_out_comp = so;
+  a.epi_w = pinv_.as<Shoup>();
+  a.epi_add = add_c0;
+  FHE_CUDA(ntt_forward(a));
 }
 
 void Ckks::keyswitch(const uint64_t* d, uint32_t nq, const uint64_t* evk, uint64_t* out, size_t so,
@@ -913,12 +927,18 @@ void Ckks::rescale_into(const Ct& a, Ct& o) {
   const size_t cs = (size_t)a.cap * n, os = (size_t)o.cap * n;
   ++counters.rescales;
   uint64_t* last = ws(6, (size_t)nc * n);
-  FHE_CUDA(cudaMemcpy2DAsync(last, (size_t)n * 8, a.data() + (size_t)(nq - 1) * n, cs * 8, (size_t)n * 8, nc,
-                             cudaMemcpyDeviceToDevice, ctx.stream));
-  ntt_dense(last, nc, 1, 1, nq - 1, true);
+  {  // last[c] = INTT(limb nq-1 of component c), out of place
+    counters.ntt_limbs += nc;
+    NttArgs la = ctx.ntt_args(last, nc, nq - 1, 1, 1);
+    la.src = a.data() + (size_t)(nq - 1) * n;
+    la.src_limb_stride = a.cap;
+    FHE_CUDA(ntt_inverse(la));
+  }
   uint64_t* lifted = ws(7, (size_t)nc * (nq - 1) * n);
   const size_t ls = (size_t)(nq - 1) * n;
   launch_rescale_lift(last, n, lifted, ls, nc, nq - 1, n, ctx.primes[nq - 1], ctx.d_mod.as<Modulus>(), ctx.stream);
+  // (measured: fusing this combine into the NTT's last pass, as ModDown does,
+  // is 5% slower here; the separate combine streams at full bandwidth)
   ntt_dense(lifted, nc, nq - 1, nq - 1, 0, false);
   launch_moddown_combine(a.data(), cs, lifted, ls, qinv_.as<Shoup>() + (size_t)(nq - 1) * ctx.L, nullptr, o.data(),
                          os, nc, nq - 1, n, ctx.d_primes.as<uint64_t>(), ctx.stream);

@@ -266,15 +266,20 @@ __global__ void k_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const u
   const uint32_t l = blockIdx.y;
   const uint32_t p = pm(l);
   const Modulus m = mods[p];
-  uint64_t s0 = 0, s1 = 0;
+  // 128-bit sums of the D products (each < q^2 < 2^122 / D), one reduction each
+  uint64_t h0 = 0, l0 = 0, h1 = 0, l1 = 0;
   for (uint32_t j = 0; j < D; ++j) {
     const uint64_t x = ext[((size_t)j * w + l) * n + k];
     const uint64_t* kb = evk + (size_t)j * 2 * key_limbs * n;
-    s0 = add_mod(s0, mul_mod(x, kb[(size_t)p * n + k], m), m.q);
-    s1 = add_mod(s1, mul_mod(x, kb[((size_t)key_limbs + p) * n + k], m), m.q);
+    const uint64_t k0 = kb[(size_t)p * n + k], k1 = kb[((size_t)key_limbs + p) * n + k];
+    const uint64_t p0 = x * k0, p1 = x * k1;
+    l0 += p0;
+    h0 += __umul64hi(x, k0) + (l0 < p0);
+    l1 += p1;
+    h1 += __umul64hi(x, k1) + (l1 < p1);
   }
-  acc[(size_t)l * n + k] = s0;
-  acc[((size_t)w + l) * n + k] = s1;
+  acc[(size_t)l * n + k] = reduce_u128(h0, l0, m);
+  acc[((size_t)w + l) * n + k] = reduce_u128(h1, l1, m);
 }
 
 // Block (x = coefficient tile, y = component, z = chunk of kTgtChunk targets).

@@ -193,7 +193,7 @@ __device__ __forceinline__ int rpad(int k) { return k + (k >> 4); }
 // With LZ > 0 the column pass leaves values below lz_bound_after(LZ, 1, LA) q;
 // this pass continues the greedy schedule and reduces the output with one
 // Shoup multiplication by 1 and a conditional subtraction.
-template <int LA, int LB, int ROWS, int LZ>
+template <int LA, int LB, int ROWS, int LZ, bool EPI>
 __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, min_blocks<LB, ROWS>())
     ntt_fwd_rows(const NttArgs g) {
   using P = PassShape<LB>;
@@ -264,8 +264,24 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, min_blocks<LB, ROWS>(
     for (int u = 0; u < P::R; ++u) srow[rpad(t + P::T * u)] = fwd_final(x[u], q, q2, mu);
   }
   __syncthreads();
+  if constexpr (EPI) {
+    // combine epilogue: (x - v) * w (+ add on component 0), same coalesced layout
+    const size_t off = (size_t)blockIdx.z * n + ((size_t)blockIdx.x * ROWS + rr) * P::S;
+    const uint64_t* ex = g.epi_x + blockIdx.y * g.epi_x_comp + off;
+    uint64_t* eo = g.epi_out + blockIdx.y * g.epi_out_comp + off;
+    const uint64_t* ea = (g.epi_add && blockIdx.y == 0) ? g.epi_add + off : nullptr;
+    const Twiddle w = g.epi_w[pidx];
 #pragma unroll
-  for (int u = 0; u < P::R; ++u) grow[t + P::T * u] = srow[rpad(t + P::T * u)];
+    for (int u = 0; u < P::R; ++u) {
+      const int k = t + P::T * u;
+      uint64_t r = shoup_mul(sub_mod(ex[k], srow[rpad(k)], q), w.w, w.wp, q);
+      if (ea) r = add_mod(r, ea[k], q);
+      eo[k] = r;
+    }
+  } else {
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) grow[t + P::T * u] = srow[rpad(t + P::T * u)];
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -287,12 +303,16 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, min_blocks<LB, ROWS>(
   const int rr = threadIdx.x / P::T;
   const uint32_t row = blockIdx.x * ROWS + rr;
 
-  // Coalesced load in the k = t + T*u layout, staged through shared memory
-  // for round 1's contiguous runs.
+  // Coalesced load in the k = t + T*u layout (from the out-of-place source
+  // when one is given), staged through shared memory for round 1's runs.
   uint64_t x[P::R];
   uint64_t* srow = smem + rr * kRowWords;
   {
-    const uint64_t* grow = a + (size_t)rr * P::S;
+    const uint64_t* grow =
+        (g.src ? g.src + ((size_t)blockIdx.y * g.src_limb_stride + blockIdx.z) * n +
+                     (size_t)blockIdx.x * ROWS * P::S
+               : a) +
+        (size_t)rr * P::S;
 #pragma unroll
     for (int u = 0; u < P::R; ++u) srow[rpad(t + P::T * u)] = grow[t + P::T * u];
   }
@@ -419,7 +439,7 @@ size_t cols_smem() {
 // the config-2 batch against 16 and 32 with several register caps: small
 // CTAs with ~100 registers keep the integer pipes busiest.
 
-template <int LA, int LB, int LZ, int TW>
+template <int LA, int LB, int LZ, int TW, bool EPI>
 cudaError_t launch_fwd_impl(const NttArgs& g) {
   using PA = PassShape<LA>;
   using PB = PassShape<LB>;
@@ -427,23 +447,32 @@ cudaError_t launch_fwd_impl(const NttArgs& g) {
   cudaError_t e;
   e = cudaFuncSetAttribute(ntt_fwd_cols<LA, LZ, TW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(ntt_fwd_rows<LA, LB, TW, LZ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
+  e = cudaFuncSetAttribute(ntt_fwd_rows<LA, LB, TW, LZ, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
   if (e != cudaSuccess) return e;
   const uint32_t polys = g.list ? 1 : g.n_polys;
   dim3 ga((1u << LB) / TW, polys, g.n_limbs);
   ntt_fwd_cols<LA, LZ, TW><<<ga, TW * PA::T, sa, g.stream>>>(g); note_launch();
   dim3 gb((1u << LA) / TW, polys, g.n_limbs);
-  ntt_fwd_rows<LA, LB, TW, LZ><<<gb, TW * PB::T, sb, g.stream>>>(g); note_launch();
+  ntt_fwd_rows<LA, LB, TW, LZ, EPI><<<gb, TW * PB::T, sb, g.stream>>>(g); note_launch();
   return cudaGetLastError();
+}
+
+template <int LA, int LB, int TW, bool EPI>
+cudaError_t launch_fwd_lz(const NttArgs& g) {
+  switch (g.lazy) {
+    case 32: return launch_fwd_impl<LA, LB, 32, TW, EPI>(g);
+    case 16: return launch_fwd_impl<LA, LB, 16, TW, EPI>(g);
+    default: return launch_fwd_impl<LA, LB, 0, TW, EPI>(g);
+  }
 }
 
 template <int LA, int LB, int TW>
 cudaError_t launch_fwd_tw(const NttArgs& g) {
-  switch (g.lazy) {
-    case 32: return launch_fwd_impl<LA, LB, 32, TW>(g);
-    case 16: return launch_fwd_impl<LA, LB, 16, TW>(g);
-    default: return launch_fwd_impl<LA, LB, 0, TW>(g);
+  if (g.epi_out) {
+    if (g.list || !g.epi_x || !g.epi_w) return cudaErrorInvalidValue;
+    return launch_fwd_lz<LA, LB, TW, true>(g);
   }
+  return launch_fwd_lz<LA, LB, TW, false>(g);
 }
 
 template <int LA, int LB>
@@ -471,6 +500,7 @@ cudaError_t launch_inv_tw(const NttArgs& g) {
 
 template <int LA, int LB>
 cudaError_t launch_inv(const NttArgs& g) {
+  if (g.src && g.list) return cudaErrorInvalidValue;
   return launch_inv_tw<LA, LB, 8>(g);
 }
 

@@ -29,6 +29,22 @@ struct NttArgs {
   const Twiddle* tw2 = nullptr;
   const Twiddle* tw2_inv = nullptr;
   uint32_t tw2_stride = 0;
+  // Optional out-of-place input of the inverse transform (dense layout only):
+  // its first pass reads limb l of poly c from src + (c*src_limb_stride + l)*N
+  // and every pass writes to data.
+  const uint64_t* src = nullptr;
+  uint32_t src_limb_stride = 0;
+  // Optional combine epilogue of the forward transform (dense layout only),
+  // the last step of ModDown and of rescaling: for poly c and limb l (prime
+  // p = prime0 + l) the transform's output v is not stored; instead
+  //   epi_out[c][l] = (epi_x[c][l] - v) * epi_w[p]  (+ epi_add[l] when c == 0)
+  // with component strides epi_x_comp / epi_out_comp words and limb stride N.
+  const uint64_t* epi_x = nullptr;
+  size_t epi_x_comp = 0;
+  uint64_t* epi_out = nullptr;
+  size_t epi_out_comp = 0;
+  const Twiddle* epi_w = nullptr;
+  const uint64_t* epi_add = nullptr;
   cudaStream_t stream;
 };
 

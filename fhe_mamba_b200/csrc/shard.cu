@@ -22,15 +22,19 @@ __global__ void k_key_inner_rows(const uint64_t* ext, uint32_t D, uint32_t rows,
   const uint32_t l = blockIdx.y;
   const Modulus m = mods[row_prime[l]];
   const uint32_t kr = krow(l);
-  uint64_t s0 = 0, s1 = 0;
+  uint64_t h0 = 0, l0 = 0, h1 = 0, l1 = 0;
   for (uint32_t j = 0; j < D; ++j) {
     const uint64_t x = ext[((size_t)j * rows + l) * n + k];
     const uint64_t* kb = key + (size_t)j * 2 * key_rows * n;
-    s0 = add_mod(s0, mul_mod(x, kb[(size_t)kr * n + k], m), m.q);
-    s1 = add_mod(s1, mul_mod(x, kb[((size_t)key_rows + kr) * n + k], m), m.q);
+    const uint64_t k0 = kb[(size_t)kr * n + k], k1 = kb[((size_t)key_rows + kr) * n + k];
+    const uint64_t p0 = x * k0, p1 = x * k1;
+    l0 += p0;
+    h0 += __umul64hi(x, k0) + (l0 < p0);
+    l1 += p1;
+    h1 += __umul64hi(x, k1) + (l1 < p1);
   }
-  acc[(size_t)l * n + k] = s0;
-  acc[((size_t)rows + l) * n + k] = s1;
+  acc[(size_t)l * n + k] = reduce_u128(h0, l0, m);
+  acc[((size_t)rows + l) * n + k] = reduce_u128(h1, l1, m);
 }
 
 // out[c][l] = (acc[c][l] - conv[c][l]) * P^{-1} mod q_l  (+ add_c[l]).
