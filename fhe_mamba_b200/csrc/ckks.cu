@@ -806,11 +806,25 @@ std::unique_ptr<Ct> Ckks::chebyshev(const Ct& x, const std::vector<double>& coef
     u = mul_scalar(x, 2.0 / (hi - lo));
     u = add_scalar(*u, -(lo + hi) / (hi - lo));
   }
+  if (u->noise_deg >= 2 && u->nq >= 2) rescale_inplace(*u);  // once, not at every use of T_1
   std::map<int, std::unique_ptr<Ct>> cache;
   int levels = 0;
   while ((1 << levels) < (int)coeffs.size()) ++levels;
   const int baby = 1 << ((std::max(1, levels) + 1) / 2);
-  std::function<const Ct&(int)> basis = [&](int i) -> const Ct& {
+  // T_i brought down to (nq, scale), cached: odd products and the leaf basis
+  // ask for the same lowered copies.
+  std::map<std::pair<int, uint32_t>, std::unique_ptr<Ct>> lowered;
+  std::function<const Ct&(int)> basis;
+  auto at_level = [&](int i, uint32_t nq, double sc) -> const Ct& {
+    const Ct& b = basis(i);
+    if (b.nq == nq) return b;
+    auto& slot = lowered[{i, nq}];
+    if (!slot) slot = adjust(b, nq, sc);
+    return *slot;
+  };
+  // Each T_i is rescaled once, right after its product, and reused in that
+  // form (a lazily rescaled T_i would be rescaled again at every use).
+  basis = [&](int i) -> const Ct& {
     if (i == 1) return *u;
     auto it = cache.find(i);
     if (it != cache.end()) return *it->second;
@@ -821,12 +835,15 @@ std::unique_ptr<Ct> Ckks::chebyshev(const Ct& x, const std::vector<double>& coef
       auto dbl = add(*sq, *sq, false);
       out = add_scalar(*dbl, -1.0);
     } else {
-      const Ct& a = basis((i + 1) / 2);
-      const Ct& b = basis(i / 2);
-      auto pr = mul(a, b);
+      const Ct* a = &basis((i + 1) / 2);
+      const Ct* b = &basis(i / 2);
+      if (a->nq > b->nq) a = &at_level((i + 1) / 2, b->nq, b->scale);
+      else if (b->nq > a->nq) b = &at_level(i / 2, a->nq, a->scale);
+      auto pr = mul(*a, *b);
       auto dbl = add(*pr, *pr, false);
       out = add(*dbl, *u, true);
     }
+    if (out->noise_deg >= 2 && out->nq >= 2) rescale_inplace(*out);
     const Ct& ref = *out;
     cache[i] = std::move(out);
     return ref;
@@ -835,30 +852,25 @@ std::unique_ptr<Ct> Ckks::chebyshev(const Ct& x, const std::vector<double>& coef
   // basis is brought once to the level and scale of its deepest member and
   // each leaf is then one fused pass (linear_wsum) instead of a scalar product,
   // an addition and a level alignment per term.
-  std::vector<std::unique_ptr<Ct>> aligned;
+  std::vector<const Ct*> aligned;
   auto aligned_basis = [&](int i) -> const Ct& {
     if (aligned.empty()) {
       const int top = std::min<int>(baby - 1, (int)coeffs.size() - 1);
       uint32_t nq_min = ~0u;
       double sc = 0.0;
-      std::vector<std::unique_ptr<Ct>> ready_basis(top + 1);
       for (int j = 1; j <= top; ++j) {
         const Ct& b = basis(j);
-        ready_basis[j] = b.noise_deg >= 2 ? rescaled(b) : clone(b);
-        if (ready_basis[j]->nq < nq_min) {
-          nq_min = ready_basis[j]->nq;
-          sc = ready_basis[j]->scale;
+        require(b.noise_deg < 2, "chebyshev: basis left unrescaled", -5);
+        if (b.nq < nq_min) {
+          nq_min = b.nq;
+          sc = b.scale;
         }
       }
-      aligned.resize(top + 1);
+      aligned.assign(top + 1, nullptr);
       for (int j = 1; j <= top; ++j) {
-        Ct& b = *ready_basis[j];
-        if (b.nq == nq_min) {
-          require(std::fabs(b.scale / sc - 1.0) < 1e-9, "chebyshev: basis scales differ on one level", -4);
-          aligned[j] = std::move(ready_basis[j]);
-        } else {
-          aligned[j] = adjust(b, nq_min, sc);
-        }
+        const Ct& b = basis(j);
+        if (b.nq == nq_min) require(std::fabs(b.scale / sc - 1.0) < 1e-9, "chebyshev: basis scales differ on one level", -4);
+        aligned[j] = &at_level(j, nq_min, sc);
       }
     }
     return *aligned[i];
@@ -982,34 +994,39 @@ std::unique_ptr<Ct> Ckks::mul_int(const Ct& a, int64_t v) {
 
 std::unique_ptr<Ct> Ckks::adjust(const Ct& a, uint32_t nq, double scale) {
   require(nq <= a.nq, "adjust: target level is above the ciphertext", -1);
-  auto c = clone(a);
-  if (c->noise_deg == 2 && c->nq > nq) rescale_inplace(*c);
-  if (c->scale != scale) {
+  // Every branch writes a new ciphertext (a rescale or an integer multiple);
+  // the input is copied only for a pure limb drop or a scale relabel.
+  std::unique_ptr<Ct> c;
+  if (a.noise_deg == 2 && a.nq > nq) c = rescaled(a);
+  const Ct* cur = c ? c.get() : &a;
+  if (cur->scale != scale) {
     // Either times round(scale * q_last / s) and a rescale (consumes the
     // level being dropped anyway), or, when the target carries a squared
-    // scale, drop limbs first and multiply by round(scale / s).  FLEXIBLEAUTO
+    // scale, multiply by round(scale / s) and drop limbs.  FLEXIBLEAUTO
     // scales of neighbouring levels can agree to 1e-12, so "nearly equal" is
     // not "equal": any difference is removed exactly when a level is dropped.
-    const long double C =
-        c->nq > nq ? (long double)scale * (long double)ctx.primes[c->nq - 1] / (long double)c->scale : 0.0L;
+    const long double C = cur->nq > nq
+                              ? (long double)scale * (long double)ctx.primes[cur->nq - 1] / (long double)cur->scale
+                              : 0.0L;
     if (C >= 1.0L && C < 9.2e18L) {
-      auto m = mul_int(*c, (int64_t)roundl(C));
-      m->noise_deg = c->noise_deg + 1;
+      auto m = mul_int(*cur, (int64_t)roundl(C));
+      m->noise_deg = cur->noise_deg + 1;
+      rescale_inplace(*m);
+      m->scale = scale;
       c = std::move(m);
-      rescale_inplace(*c);
-      c->scale = scale;
-    } else if (c->nq == nq && std::fabs(c->scale / scale - 1.0) < 1e-9) {
+    } else if (cur->nq == nq && std::fabs(cur->scale / scale - 1.0) < 1e-9) {
+      if (!c) c = clone(*cur);
       c->scale = scale;  // one level, one scale up to rounding of the scale itself
     } else {
-      if (c->nq > nq) level_reduce_inplace(*c, c->nq - nq);
-      const long double R = (long double)scale / (long double)c->scale;
+      const long double R = (long double)scale / (long double)cur->scale;
       require(R >= 1.0L && R < 4.6e18L, "adjust: scale ratio out of range", -4);
-      auto m = mul_int(*c, (int64_t)roundl(R));
-      m->noise_deg = c->noise_deg + 1;
+      auto m = mul_int(*cur, (int64_t)roundl(R));  // limb-wise: equal to dropping first
+      m->noise_deg = cur->noise_deg + 1;
       m->scale = scale;
       c = std::move(m);
     }
   }
+  if (!c) c = clone(*cur);
   if (c->nq > nq) level_reduce_inplace(*c, c->nq - nq);
   return c;
 }
@@ -1158,7 +1175,7 @@ std::unique_ptr<Ct> Ckks::mul(const Ct& a, const Ct& b) {
   require(keyed_, "mul before keygen", -4);
   std::unique_ptr<Ct> hx, hy;
   const Ct* x = &ready(a, hx);
-  const Ct* y = &ready(b, hy);
+  const Ct* y = &b == &a ? x : &ready(b, hy);  // a square rescales its operand once
   // FLEXIBLEAUTO level alignment (AdjustLevelsAndDepth): the operand with more
   // limbs is brought to the other's level AND scale, so that ciphertexts on one
   // level keep one scale; dropping limbs alone would leave a nearby but
