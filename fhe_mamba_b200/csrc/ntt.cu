@@ -209,9 +209,15 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, min_blocks<LB, ROWS>(
   const int t = threadIdx.x % P::T;
   const int rr = threadIdx.x / P::T;
   const uint32_t row = blockIdx.x * ROWS + rr;
-  auto fwd_final = [](uint64_t v, uint64_t q, uint64_t q2, uint64_t mu) {
-    if constexpr (LZ != 0) return csub(shoup_lazy(v, 1, mu, q), q);
-    else return csub(csub(v, q2), q);
+  // Final reduction to [0, q): the lazy schedule leaves values below bf*q,
+  // removed by conditional subtractions of 2^k q (ALU pipe) rather than a
+  // Shoup product by 1 (the 64-bit multiply pipe is the transform's limit).
+  constexpr int bf = LZ ? lz_bound_after(LZ, b0, LB) : 4;
+  constexpr int top = bf > 16 ? 4 : bf > 8 ? 3 : bf > 4 ? 2 : 1;  // 2^top < bf <= 2^(top+1)
+  auto fwd_final = [](uint64_t v, uint64_t q, uint64_t, uint64_t) {
+#pragma unroll
+    for (int k = top; k >= 0; --k) v = csub(v, q << k);
+    return v;
   };
 
   // Round-1 layout k = t + T*u: for each u the T threads of a row read T
