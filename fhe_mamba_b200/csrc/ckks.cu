@@ -606,7 +606,7 @@ void Ckks::modup(const uint64_t* d, uint32_t nq, uint64_t* ext) {
     FHE_CUDA(ntt_inverse(a));
   }
   launch_modup(coef, d, ext, nq, ctx.K, n, T.digits.as<ModUpDigit>(), T.D, ctx.alpha, ctx.d_mod.as<Modulus>(),
-               ctx.stream);
+               ctx.stream, ctx.max_prime() < (uint64_t(1) << 60));
   ++counters.modup;
   if (T.ntt_list_len) {
     counters.ntt_limbs += T.ntt_list_len;
@@ -625,7 +625,7 @@ void Ckks::moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, co
   ntt_dense(acc + (size_t)nq * n, 2, K, w, ctx.L, true);
   uint64_t* conv = ws(3, (size_t)2 * ctx.L * n);
   launch_convert(acc + (size_t)nq * n, (size_t)w * n, conv, (size_t)nq * n, 2, T.moddown.as<ConvTable>(), K, nq, n,
-                 ctx.d_mod.as<Modulus>(), ctx.stream);
+                 ctx.d_mod.as<Modulus>(), ctx.stream, ctx.max_prime() < (uint64_t(1) << 60));
   // NTT of the conversion with the combine fused into its last pass:
   // out = (acc - NTT(conv)) * P^{-1} (+ c0 on component 0).
   counters.ntt_limbs += 2ull * nq;

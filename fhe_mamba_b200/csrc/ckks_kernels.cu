@@ -214,12 +214,64 @@ constexpr int kMaxSrc = 24;  // largest digit / special basis handled by the con
   X(1) X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11) X(12) X(13) X(14) X(15) X(16) X(17) X(18) \
   X(19) X(20) X(21) X(22) X(23) X(24)
 
+#define FHE_NS16_CASES(X) \
+  X(1) X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11) X(12) X(13) X(14) X(15) X(16)
+
 constexpr int kTgtChunk = 8;  // target limbs per block in the basis conversions
+
+// Conversion constants in shared memory: the word itself, or (SPLIT) its
+// 30-bit halves packed as lo | hi << 32.
+template <bool SPLIT>
+__device__ __forceinline__ uint64_t conv_const(uint64_t w) {
+  if constexpr (SPLIT) return (w & ((1ull << 30) - 1)) | ((w >> 30) << 32);
+  else return w;
+}
+
+// sum_i y_i h_i mod m, exact.  SPLIT (every y_i, h_i < 2^60, NS <= 16): with
+// 30-bit halves each partial product is below 2^60, so the four partial sums
+// of NS terms fit 64 bits and every term is one 32x32+64 multiply-add; the
+// 128-bit total a11 2^60 + (a01 + a10) 2^30 + a00 is reduced once.
+// Otherwise: 64x64 -> 128-bit products accumulated with carries.
+template <int NS, bool SPLIT>
+__device__ __forceinline__ uint64_t conv_dot(const uint64_t (&y)[NS], const uint64_t* h, const Modulus& m) {
+  if constexpr (SPLIT) {
+    static_assert(NS <= 16, "split accumulation holds at most 16 terms");
+    uint64_t a00 = 0, a01 = 0, a10 = 0, a11 = 0;
+#pragma unroll
+    for (int i = 0; i < NS; ++i) {
+      const uint64_t c = h[i];
+      const uint32_t h0 = (uint32_t)c, h1 = (uint32_t)(c >> 32);
+      const uint32_t y0 = (uint32_t)(y[i] & ((1ull << 30) - 1)), y1 = (uint32_t)(y[i] >> 30);
+      a00 += (uint64_t)y0 * h0;
+      a01 += (uint64_t)y0 * h1;
+      a10 += (uint64_t)y1 * h0;
+      a11 += (uint64_t)y1 * h1;
+    }
+    const uint64_t mid = a01 + a10;
+    const uint64_t midc = mid < a01;  // carry of the middle sum (< 2^65)
+    uint64_t lo = a00 + (mid << 30);
+    uint64_t hi = (mid >> 34) + (midc << 30) + (lo < a00);
+    const uint64_t t = a11 << 60;
+    lo += t;
+    hi += (a11 >> 4) + (lo < t);
+    return reduce_u128(hi, lo, m);
+  } else {
+    uint64_t hi = 0, lo = 0;
+#pragma unroll
+    for (int i = 0; i < NS; ++i) {
+      const uint64_t c = h[i];
+      const uint64_t pl = y[i] * c;
+      lo += pl;
+      hi += __umul64hi(y[i], c) + (lo < pl);
+    }
+    return reduce_u128(hi, lo, m);
+  }
+}
 
 // Block (x = coefficient tile, y = digit - digit0, z = chunk of kTgtChunk
 // target limbs).  NS = source limbs of every digit in the launch.  The sum
 // sum_i y_i hat_{i,t} is formed exactly in 128 bits and reduced once.
-template <int NS>
+template <int NS, bool SPLIT>
 __global__ void k_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t w, uint32_t n,
                         const ModUpDigit* digits, uint32_t digit0, const Modulus* mods) {
   __shared__ uint64_t sh_hat[kTgtChunk * NS];
@@ -229,7 +281,8 @@ __global__ void k_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ex
   const uint32_t t0 = blockIdx.z * kTgtChunk;
   if (t0 >= dg.conv.nt) return;  // uniform across the block
   const uint32_t nt = min((uint32_t)kTgtChunk, dg.conv.nt - t0);
-  for (uint32_t i = threadIdx.x; i < nt * NS; i += blockDim.x) sh_hat[i] = dg.conv.hat[(size_t)t0 * NS + i].w;
+  for (uint32_t i = threadIdx.x; i < nt * NS; i += blockDim.x)
+    sh_hat[i] = conv_const<SPLIT>(dg.conv.hat[(size_t)t0 * NS + i].w);
   if (threadIdx.x < nt) sh_m[threadIdx.x] = mods[dg.conv.dst_prime[t0 + threadIdx.x]];
   __syncthreads();
   const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
@@ -246,15 +299,7 @@ __global__ void k_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ex
   for (uint32_t u = 0; u < nt; ++u) {
     const uint32_t tt = t0 + u;
     const uint32_t l = tt < dg.lo ? tt : tt + NS;
-    uint64_t hi = 0, lo = 0;
-#pragma unroll
-    for (int i = 0; i < NS; ++i) {
-      const uint64_t c = sh_hat[u * NS + i];
-      const uint64_t pl = y[i] * c;
-      lo += pl;
-      hi += __umul64hi(y[i], c) + (lo < pl);
-    }
-    e[(size_t)l * n + k] = reduce_u128(hi, lo, sh_m[u]);
+    e[(size_t)l * n + k] = conv_dot<NS, SPLIT>(y, sh_hat + u * NS, sh_m[u]);
   }
 }
 
@@ -283,7 +328,7 @@ __global__ void k_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const u
 }
 
 // Block (x = coefficient tile, y = component, z = chunk of kTgtChunk targets).
-template <int NS>
+template <int NS, bool SPLIT>
 __global__ void k_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp,
                           const ConvTable* tab, uint32_t n, const Modulus* mods) {
   __shared__ uint64_t sh_hat[kTgtChunk * NS];
@@ -292,7 +337,7 @@ __global__ void k_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, siz
   const uint32_t t0 = blockIdx.z * kTgtChunk;
   if (t0 >= t.nt) return;
   const uint32_t nt = min((uint32_t)kTgtChunk, t.nt - t0);
-  for (uint32_t i = threadIdx.x; i < nt * NS; i += blockDim.x) sh_hat[i] = t.hat[(size_t)t0 * NS + i].w;
+  for (uint32_t i = threadIdx.x; i < nt * NS; i += blockDim.x) sh_hat[i] = conv_const<SPLIT>(t.hat[(size_t)t0 * NS + i].w);
   if (threadIdx.x < nt) sh_m[threadIdx.x] = mods[t.dst_prime[t0 + threadIdx.x]];
   __syncthreads();
   const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
@@ -308,16 +353,8 @@ __global__ void k_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, siz
     y[i] = shoup_mul(s[row * n + k], h.w, h.wp, mods[t.src_prime[i]].q);
   }
   for (uint32_t u = 0; u < nt; ++u) {
-    uint64_t hi = 0, lo = 0;
-#pragma unroll
-    for (int i = 0; i < NS; ++i) {
-      const uint64_t cst = sh_hat[u * NS + i];
-      const uint64_t pl = y[i] * cst;
-      lo += pl;
-      hi += __umul64hi(y[i], cst) + (lo < pl);
-    }
     const size_t row = t.dst_row ? t.dst_row[t0 + u] : t0 + u;
-    d[row * n + k] = reduce_u128(hi, lo, sh_m[u]);
+    d[row * n + k] = conv_dot<NS, SPLIT>(y, sh_hat + u * NS, sh_m[u]);
   }
 }
 
@@ -623,16 +660,27 @@ void launch_automorphism(const uint64_t* in, size_t si, uint64_t* out, size_t so
 }
 
 void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t nq, uint32_t K, uint32_t n,
-                  const ModUpDigit* digits_dev, uint32_t D, uint32_t alpha, const Modulus* mods, cudaStream_t s) {
+                  const ModUpDigit* digits_dev, uint32_t D, uint32_t alpha, const Modulus* mods, cudaStream_t s,
+                  bool primes_below_2_60) {
   // Full digits share one launch, a shorter last digit gets its own.
   const uint32_t full = nq / alpha, rest = nq % alpha;
   auto go = [&](uint32_t ns, uint32_t digit0, uint32_t count) {
     if (!count) return;
     const uint32_t chunks = (nq + K - ns + kTgtChunk - 1) / kTgtChunk;
     const dim3 grid = grid1(n, count, chunks);
+    if (primes_below_2_60 && ns <= 16) {
+      switch (ns) {
+#define FHE_CASE(NS) \
+  case NS: k_modup<NS, true><<<grid, kTpb, 0, s>>>(coef, dntt, ext, nq + K, n, digits_dev, digit0, mods); note_launch(); break;
+        FHE_NS16_CASES(FHE_CASE)
+#undef FHE_CASE
+        default: break;
+      }
+      return;
+    }
     switch (ns) {
 #define FHE_CASE(NS) \
-  case NS: k_modup<NS><<<grid, kTpb, 0, s>>>(coef, dntt, ext, nq + K, n, digits_dev, digit0, mods); note_launch(); break;
+  case NS: k_modup<NS, false><<<grid, kTpb, 0, s>>>(coef, dntt, ext, nq + K, n, digits_dev, digit0, mods); note_launch(); break;
       FHE_NS_CASES(FHE_CASE)
 #undef FHE_CASE
       default: break;
@@ -650,12 +698,22 @@ void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_
 
 void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp, uint32_t ncomp,
                     const ConvTable* t_dev, uint32_t ns, uint32_t nt, uint32_t n, const Modulus* mods,
-                    cudaStream_t s) {
+                    cudaStream_t s, bool primes_below_2_60) {
   const uint32_t chunks = (nt + kTgtChunk - 1) / kTgtChunk;
   const dim3 grid = grid1(n, ncomp, chunks);
+  if (primes_below_2_60 && ns <= 16) {
+    switch (ns) {
+#define FHE_CASE(NS) \
+  case NS: k_convert<NS, true><<<grid, kTpb, 0, s>>>(src, s_comp, dst, d_comp, t_dev, n, mods); note_launch(); break;
+      FHE_NS16_CASES(FHE_CASE)
+#undef FHE_CASE
+      default: break;
+    }
+    return;
+  }
   switch (ns) {
 #define FHE_CASE(NS) \
-  case NS: k_convert<NS><<<grid, kTpb, 0, s>>>(src, s_comp, dst, d_comp, t_dev, n, mods); note_launch(); break;
+  case NS: k_convert<NS, false><<<grid, kTpb, 0, s>>>(src, s_comp, dst, d_comp, t_dev, n, mods); note_launch(); break;
     FHE_NS_CASES(FHE_CASE)
 #undef FHE_CASE
     default: break;

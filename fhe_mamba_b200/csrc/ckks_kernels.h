@@ -99,9 +99,11 @@ struct ModUpDigit {
   ConvTable conv;   // sources lo..hi-1, targets = all other limbs of ext (in limb order)
 };
 // Digits are [j*alpha, min((j+1)*alpha, nq)); at most 24 limbs each.
+// primes_below_2_60: every source and target prime is below 2^60 (selects the
+// split 30-bit accumulation of the conversions, which needs it).
 void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t nq, uint32_t K,
                   uint32_t n, const ModUpDigit* digits_dev, uint32_t D, uint32_t alpha, const Modulus* mods,
-                  cudaStream_t s);
+                  cudaStream_t s, bool primes_below_2_60);
 // acc[2][w][N] = sum_j ext[j] * evk[j][0/1][key limb]; key limb of ext limb l is pm(l).
 void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_t* evk,
                       uint32_t key_limbs, PrimeMap pm, uint64_t* acc, uint32_t n, const Modulus* mods,
@@ -110,7 +112,7 @@ void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_
 // ns / nt must equal the table's source / target counts (ns <= 24).
 void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp, uint32_t ncomp,
                     const ConvTable* t_dev, uint32_t ns, uint32_t nt, uint32_t n, const Modulus* mods,
-                    cudaStream_t s);
+                    cudaStream_t s, bool primes_below_2_60);
 // out[c][i] = (x[c][i] - conv[c][i]) * pinv_i  (+ add[i] on component 0 when add != null).
 void launch_moddown_combine(const uint64_t* x, size_t sx, const uint64_t* conv, size_t sc,
                             const Shoup* pinv, const uint64_t* add, uint64_t* out, size_t so,

@@ -304,7 +304,7 @@ void ShardKeySwitch::inner(uint32_t nq, int kind, uint64_t g, const uint64_t* ga
                                cudaMemcpyDeviceToDevice, c.stream));
     if (T.digit_nt[j])
       launch_convert(gathered, 0, e, 0, 1, T.digit_tabs.as<ConvTable>() + j, T.digit_ns[j], T.digit_nt[j], n,
-                     c.d_mod.as<Modulus>(), c.stream);
+                     c.d_mod.as<Modulus>(), c.stream, c.max_prime() < (uint64_t(1) << 60));
   }
   ntt_list(ext, T.ext_list, T.ext_len, false);
   ++ck_.counters.key_inner;
@@ -340,7 +340,7 @@ void ShardKeySwitch::moddown(uint32_t nq, const uint64_t* acc, const uint64_t* p
   }
   uint64_t* conv = conv_.as<uint64_t>();
   launch_convert(p_gathered, (size_t)pl.p_chunk * n, conv, (size_t)pl.q_own * n, 2, T.md_tab.as<ConvTable>(), c.K,
-                 pl.q_own, n, c.d_mod.as<Modulus>(), c.stream);
+                 pl.q_own, n, c.d_mod.as<Modulus>(), c.stream, c.max_prime() < (uint64_t(1) << 60));
   ntt_list(conv, T.conv_list, 2 * pl.q_own, false);
   const dim3 grid((n + kThreads - 1) / kThreads, pl.q_own, 2);
   k_combine_rows<<<grid, kThreads, 0, c.stream>>>(acc, pl.rows, conv, pl.q_own, T.pinv_rows, T.q_rows, add0, add1,

@@ -198,3 +198,21 @@ def test_encode_values_beyond_2_62(cfg1):
     x = _msg(cc.slots, 6)
     ct = cc.EvalAdd(cc.Encrypt(cc.MakeCKKSPackedPlaintext(x)), pt)
     assert np.max(np.abs(cc.Decrypt(ct).GetRealPackedValue() - (x + big))) < 1e-5 * 3e6
+
+
+def test_wide_digit_keyswitch(oracle):
+    """Depth 44, dnum 3 (15-limb digits, 15 special primes: the token loop's
+    key-switching shape) at N=2^13: relinearisation and a rotation equal the
+    oracle word for word at the top level and two lower levels."""
+    cc, oc, s, sn = _setup(oracle, 13, 44, 59, 60, 3)
+    assert cc.alpha == 15 and cc.n_p == 15
+    rlk = oc.relin_key(SEED, sn)
+    cc.EvalRotateKeyGen([3])
+    g = cc.galois_element(3)
+    rk = oc.rot_key(SEED, s, sn, g)
+    for nq in (45, 31, 16):
+        a = _rand_ct(oc, nq, 300 + nq, ncomp=3)
+        got = cc.Relinearize(cc.upload(a, noise_deg=2)).residues()
+        assert np.array_equal(got, oc.relinearize(a, rlk)), nq
+        b = _rand_ct(oc, nq, 400 + nq)
+        assert np.array_equal(cc.EvalRotate(cc.upload(b), 3).residues(), oc.rotate(b, g, rk)), nq
