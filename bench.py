@@ -55,6 +55,28 @@ ALG_BYTES_PER_TRANSFORM = 16 * POLYS * LIMBS * (1 << LOG_N)  # read + write ever
 N_ROTATE = 4
 
 
+_JSON_OUT = None
+
+
+def json_stdout():
+    """Keeps file descriptor 1 for the JSON line alone: anything else written
+    to it (NCCL's version banner, library logs, Python prints) goes to
+    stderr from here on."""
+    global _JSON_OUT
+    if _JSON_OUT is None:
+        sys.stdout.flush()
+        _JSON_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+        sys.stdout = sys.stderr
+    return _JSON_OUT
+
+
+def emit(obj):
+    out = json_stdout()
+    out.write(json.dumps(obj) + "\n")
+    out.flush()
+
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -424,7 +446,7 @@ def run_reference(args, rank):
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def config_dict(args):
@@ -504,6 +526,7 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("warmup must be >= 3")
+    json_stdout()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -518,11 +541,11 @@ def main():
 
     torch.cuda.set_device(local)
     if args.ntt_only:
-        print(json.dumps({"roofline": measure_ntt(local, steps=20, warmup=5)}), flush=True)
+        emit({"roofline": measure_ntt(local, steps=20, warmup=5)})
         return
     if args.ckks_only and world == 1:
         ks, _ = measure_ckks(local, matvec=False)
-        print(json.dumps({"keyswitch": ks}), flush=True)
+        emit({"keyswitch": ks})
         return
     if world > 1:
         from datetime import timedelta
@@ -530,7 +553,7 @@ def main():
     if args.ckks_only:
         sharded = measure_sharded_keyswitch(local, world)
         if rank == 0:
-            print(json.dumps({"sharded_keyswitch": sharded}), flush=True)
+            emit({"sharded_keyswitch": sharded})
         dist.destroy_process_group()
         return
 
@@ -568,7 +591,7 @@ def main():
         rows = [{"kernel": k, "launches": c, "ms": t / 1e3, "share": t / total}
                 for k, (c, t) in sorted(agg.items(), key=lambda kv: -kv[1][1])]
         if rank == 0:
-            print(json.dumps({"kernel_shares_one_token": rows, "total_ms": total / 1e3}), flush=True)
+            emit({"kernel_shares_one_token": rows, "total_ms": total / 1e3})
         loop.cc.close()
         return
 
@@ -639,7 +662,7 @@ def main():
                 "value": t_ks * per_token["key_inner"], "unit": UNIT, "cores": threads, "kind": "port",
                 "sample": f"one HYBRID key switch at 30 limbs on the CPU oracle ({t_ks:.3f} s) x "
                           f"{per_token['key_inner']:.0f} key switches per token (estimate; a CPU token takes hours)"}
-        print(json.dumps(line), flush=True)
+        emit(line)
 
     loop.cc.close()
     if world > 1:
