@@ -236,24 +236,36 @@ template <int NS, bool SPLIT>
 __device__ __forceinline__ uint64_t conv_dot(const uint64_t (&y)[NS], const uint64_t* h, const Modulus& m) {
   if constexpr (SPLIT) {
     static_assert(NS <= 16, "split accumulation holds at most 16 terms");
-    uint64_t a00 = 0, a01 = 0, a10 = 0, a11 = 0;
+    // Karatsuba on 30-bit halves: y h = y1 h1 2^60 + ((y0+y1)(h0+h1) - y0 h0
+    // - y1 h1) 2^30 + y0 h0, three 32x32->64 multiply-adds per term.  The
+    // middle products are below 2^62, so they are summed in groups of four.
+    constexpr int G = (NS + 3) / 4;
+    uint64_t s00 = 0, s11 = 0, mid[G] = {};
 #pragma unroll
     for (int i = 0; i < NS; ++i) {
       const uint64_t c = h[i];
       const uint32_t h0 = (uint32_t)c, h1 = (uint32_t)(c >> 32);
       const uint32_t y0 = (uint32_t)(y[i] & ((1ull << 30) - 1)), y1 = (uint32_t)(y[i] >> 30);
-      a00 += (uint64_t)y0 * h0;
-      a01 += (uint64_t)y0 * h1;
-      a10 += (uint64_t)y1 * h0;
-      a11 += (uint64_t)y1 * h1;
+      s00 += (uint64_t)y0 * h0;
+      s11 += (uint64_t)y1 * h1;
+      mid[i / 4] += (uint64_t)(y0 + y1) * (h0 + h1);
     }
-    const uint64_t mid = a01 + a10;
-    const uint64_t midc = mid < a01;  // carry of the middle sum (< 2^65)
-    uint64_t lo = a00 + (mid << 30);
-    uint64_t hi = (mid >> 34) + (midc << 30) + (lo < a00);
-    const uint64_t t = a11 << 60;
+    // m = sum(mid) - s00 - s11 in 128 bits (exact, below 2^66)
+    uint64_t ml = mid[0], mh = 0;
+#pragma unroll
+    for (int g = 1; g < G; ++g) {
+      ml += mid[g];
+      mh += ml < mid[g];
+    }
+    mh -= ml < s00;
+    ml -= s00;
+    mh -= ml < s11;
+    ml -= s11;
+    uint64_t lo = s00 + (ml << 30);
+    uint64_t hi = ((mh << 30) | (ml >> 34)) + (lo < s00);
+    const uint64_t t = s11 << 60;
     lo += t;
-    hi += (a11 >> 4) + (lo < t);
+    hi += (s11 >> 4) + (lo < t);
     return reduce_u128(hi, lo, m);
   } else {
     uint64_t hi = 0, lo = 0;
