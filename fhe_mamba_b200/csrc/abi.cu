@@ -7,6 +7,7 @@
 #include <iostream>
 #include <memory>
 #include <new>
+#include <sstream>
 #include <string>
 
 #include "../../include/fhe_b200.h"
@@ -759,6 +760,83 @@ int fhe_program_validate(const char* program_path, int32_t* slots, int32_t* node
   });
 }
 
+namespace {
+// Classical-128 parameter audit (the reference's CkksSecurityAudit,
+// native/fideslib_stage0/src/fideslib_security.hpp:18-80): exact bit lengths
+// of Q, P and Q*P against the 2024 Security Guidelines Table 5.2 bound for
+// the ring (uniform ternary secret, error sigma >= 3.19).
+uint32_t product_bit_length(const std::vector<uint64_t>& m) {
+  std::vector<uint32_t> x{1};  // little-endian 32-bit words
+  for (uint64_t q : m) {
+    std::vector<uint32_t> y(x.size() + 2, 0);
+    for (size_t i = 0; i < x.size(); ++i) {
+      unsigned __int128 carry = 0;
+      for (size_t j = 0; j < 2; ++j) {
+        const uint64_t qj = j == 0 ? (uint32_t)q : (uint32_t)(q >> 32);
+        const unsigned __int128 t = (unsigned __int128)x[i] * qj + y[i + j] + carry;
+        y[i + j] = (uint32_t)t;
+        carry = t >> 32;
+      }
+      for (size_t k = i + 2; carry; ++k) {
+        const unsigned __int128 t = (unsigned __int128)y[k] + carry;
+        y[k] = (uint32_t)t;
+        carry = t >> 32;
+      }
+    }
+    while (y.size() > 1 && y.back() == 0) y.pop_back();
+    x.swap(y);
+  }
+  uint32_t bits = 32 * (uint32_t)(x.size() - 1), top = x.back();
+  while (top) { ++bits; top >>= 1; }
+  return bits;
+}
+
+uint32_t classical128_bound(uint32_t ring) {
+  switch (ring) {
+    case 1024: return 26;
+    case 2048: return 53;
+    case 4096: return 106;
+    case 8192: return 214;
+    case 16384: return 430;
+    case 32768: return 868;
+    case 65536: return 1747;
+    case 131072: return 3523;
+    default: return 0;
+  }
+}
+
+struct SecurityAudit {
+  uint32_t ring = 0, q_bits = 0, p_bits = 0, qp_bits = 0, q_towers = 0, p_towers = 0, digits = 0, bound = 0;
+  double sigma = 0;
+  bool passed() const { return bound && sigma >= 3.19 && q_towers && p_towers && qp_bits <= bound; }
+  std::string json() const {
+    std::ostringstream o;
+    o << "{\"ring_dimension\":" << ring << ",\"q_bits\":" << q_bits << ",\"p_bits\":" << p_bits
+      << ",\"qp_bits\":" << qp_bits << ",\"q_towers\":" << q_towers << ",\"p_towers\":" << p_towers
+      << ",\"hybrid_digits\":" << digits << ",\"error_sigma\":" << sigma
+      << ",\"guideline_max_qp_bits\":" << bound << ",\"library_classical128\":true"
+      << ",\"uniform_ternary\":true,\"hybrid\":true,\"passed\":" << (passed() ? "true" : "false")
+      << ",\"basis\":\"2024 Security Guidelines Table 5.2; classical RLWE parameter bound\"}";
+    return o.str();
+  }
+};
+
+SecurityAudit audit_parameters(const fhe::Context& c) {
+  SecurityAudit a;
+  a.ring = c.n;
+  const std::vector<uint64_t> q(c.primes.begin(), c.primes.begin() + c.L), p(c.primes.begin() + c.L, c.primes.end());
+  a.q_bits = product_bit_length(q);
+  a.p_bits = product_bit_length(p);
+  a.qp_bits = product_bit_length(c.primes);
+  a.q_towers = c.L;
+  a.p_towers = c.K;
+  a.digits = c.dnum;
+  a.sigma = std::sqrt(21.0 / 2.0);  // centred binomial error, eta = 21
+  a.bound = classical128_bound(c.n);
+  return a;
+}
+}  // namespace
+
 int fhe_program_run(const char* program_path, const char* client_head_path, const char* result_path,
                     double poly_tol, double exact_tol, const fhe_program_options* options) {
   int verdict = 0;
@@ -768,6 +846,16 @@ int fhe_program_run(const char* program_path, const char* client_head_path, cons
                  "invalid error tolerance");
     fhe_program_options o{};
     if (options) o = *options;
+    if (o.security128) {
+      // packed_fideslib.cpp:1060-1076: ring 2^17, dnum = security digits,
+      // batch size = the program's slots, uniform ternary secret
+      fhe::require(o.sparse_h == 0, "128-classic requires the uniform ternary secret");
+      if (!o.log_n) o.log_n = 17;
+      o.dnum = o.security_digits ? o.security_digits : 4;
+      fhe::require(o.dnum >= 1 && o.dnum <= 16, "security digits must be in [1, 16]");
+    } else {
+      fhe::require(o.security_digits == 0, "security digits apply to --security 128-classic only");
+    }
     if (!o.depth) o.depth = 44;
     if (!o.scale_bits) o.scale_bits = 59;
     if (!o.first_bits) o.first_bits = 60;
@@ -793,10 +881,23 @@ int fhe_program_run(const char* program_path, const char* client_head_path, cons
                    "client head and final hidden width mismatch");
     }
     const auto setup0 = Clock::now();
-    fhe_params par{log_n, o.depth, o.scale_bits, o.first_bits, o.dnum, 1u << (log_n - 1), o.device, 0};
+    const uint32_t batch = o.security128 ? (uint32_t)prog.slots : 1u << (log_n - 1);
+    fhe_params par{log_n, o.depth, o.scale_bits, o.first_bits, o.dnum, batch, o.device, 0};
     fhe_ctx* raw = nullptr;
     fhe::require(fhe_ctx_create(&par, &raw) == FHE_OK, g_last_error);
     std::unique_ptr<fhe_ctx, int (*)(fhe_ctx*)> ctx(raw, fhe_ctx_destroy);
+    std::string audit_json = "null";
+    if (o.security128) {
+      const SecurityAudit a = audit_parameters(ctx->c);
+      audit_json = a.json();
+      std::ofstream pj(std::string(result_path) + ".parameters.json");
+      fhe::require((bool)pj, "cannot write the parameters audit");
+      pj << audit_json << "\n";
+      std::cout << "classical128 ring=" << a.ring << " QP_bits=" << a.qp_bits << " bound=" << a.bound
+                << " digits=" << a.digits << std::endl;
+      fhe::require(a.passed(), "classical-128 CKKS audit failed: HYBRID Q*P (" + std::to_string(a.qp_bits) +
+                                   " bits) exceeds the published bound for ring " + std::to_string(a.ring));
+    }
     fhe::Ckks& ck = *ctx->ck;
     ck.keygen(o.seed ? o.seed : 1);
     const bool can_boot = ctx->c.L > 4 + 4 + 2 + 21;
@@ -856,10 +957,11 @@ int fhe_program_run(const char* program_path, const char* client_head_path, cons
     std::ofstream r(result_path);
     fhe::require((bool)r, std::string("cannot open result ") + result_path);
     r << std::setprecision(12) << "{\n\"schema\":\"fhemamba-packed-result-v1\",\"backend\":\"fhe_b200\","
-      << "\"encrypted\":true,\"security\":\"not-set\",\"passed\":" << (passed ? "true" : "false")
+      << "\"encrypted\":true,\"security\":\"" << (o.security128 ? "128-classic" : "not-set")
+      << "\",\"passed\":" << (passed ? "true" : "false")
       << ",\"slots\":" << ctx->c.slots << ",\"payload_slots\":" << prog.slots
       << ",\"ring_dimension\":" << ctx->c.n << ",\"depth\":" << o.depth << ",\"scale_bits\":" << o.scale_bits
-      << ",\"refresh_ring_dimension\":" << ctx->c.n << ",\"security_audit\":null"
+      << ",\"refresh_ring_dimension\":" << ctx->c.n << ",\"security_audit\":" << audit_json
       << ",\"nodes\":" << prog.nodes.size() << ",\"setup_seconds\":" << setup_seconds
       << ",\"s2c_first\":" << (o.s2c_first ? "true" : "false")
       << ",\"refresh_ceiling\":" << ex.refresh_ceiling << ",\"refreshed_level\":" << ex.refreshed_level

@@ -93,7 +93,14 @@ std::vector<double> cheb_fit(const std::function<double(double)>& f, int d) {
 Bootstrapper::Bootstrapper(Ckks& ck, const BootParams& p) : ck_(ck), p_(p) {
   Context& ctx = ck.ctx;
   const uint32_t n = ctx.slots;
-  require(n == ctx.n / 2, "bootstrapping supports fully packed slots (N/2) only", -1);
+  require(n >= 2 && n <= ctx.n / 2 && (n & (n - 1)) == 0, "bootstrapping needs a power-of-two slot count <= N/2",
+          -1);
+  // Sparse packing (n < N/2): the plaintext lives in Z[X^g'], g' = N/(2n);
+  // after ModRaise the trace over the g = N/(2n) automorphisms fixing that
+  // subring (rotations by multiples of n) keeps g times its part of
+  // m + q0 I, and CoeffToSlot divides by g.
+  trace_ = ctx.n / (2 * n);
+  require(!(p_.s2c_first && trace_ > 1), "SlotToCoeff-first bootstrapping needs fully packed slots", -1);
   const uint32_t logn = ceil_log2(n);
   require(p_.budget_cts >= 1 && p_.budget_stc >= 1, "level budgets must be >= 1", -1);
   p_.budget_cts = std::min(p_.budget_cts, logn);
@@ -115,7 +122,7 @@ Bootstrapper::Bootstrapper(Ckks& ck, const BootParams& p) : ck_(ck), p_(p) {
   // attribute given to the raised ciphertext (the top level's); every group
   // then lands exactly on the FLEXIBLEAUTO scale of its output level.
   const double S = ck.level_scale(ctx.L);
-  const double alpha = S / (2.0 * p_.K * (double)ctx.primes[0]);
+  const double alpha = S / (2.0 * p_.K * (double)ctx.primes[0] * (double)trace_);
   std::vector<uint32_t> halves;
   for (uint32_t h = n / 2; h >= 1; h /= 2) halves.push_back(h);
   build_groups(cts_, halves, p_.budget_cts, true, std::pow(alpha, 1.0 / p_.budget_cts));
@@ -191,11 +198,14 @@ std::vector<int64_t> Bootstrapper::rotation_steps() const {
   for (const auto* gs : {&cts_, &stc_})
     for (const Group& g : *gs) {
       for (uint32_t j = 1; j < g.b; ++j) s.push_back(((int64_t)j * g.stride) % n);
+      // giant steps exactly as linear_transform asks for them (signed): with
+      // sparse packing a step and its residue mod n are different keys
       for (uint32_t gg = 0; gg < g.G; ++gg) {
-        const int64_t r = ((((int64_t)gg * g.b - g.offset) * g.stride) % n + n) % n;
+        const int64_t r = ((int64_t)gg * g.b - g.offset) * g.stride;
         if (r) s.push_back(r);
       }
     }
+  for (uint32_t j = 1; j < trace_; j *= 2) s.push_back((int64_t)j * n);  // sparse-packing trace
   std::sort(s.begin(), s.end());
   s.erase(std::unique(s.begin(), s.end()), s.end());
   return s;
@@ -284,6 +294,11 @@ std::unique_ptr<Ct> Bootstrapper::raise(const Ct& a) {
   // The raised plaintext t = m + q0 I is fixed now; switching back to the
   // dense secret keeps it (and I) unchanged.
   if (p_.sparse_h) raised = ck_.switch_to_dense(*raised);
+  // Sparse packing: sum of the rotations by j*n, j < g (log2 g doublings).
+  for (uint32_t j = 1; j < trace_; j *= 2) {
+    auto r = ck_.rotate(*raised, ck_.galois_for_step((int64_t)j * ctx.slots));
+    raised = ck_.add(*raised, *r, false);
+  }
   raised->scale = ck_.level_scale(ctx.L);
   levels_[0] = raised->nq;
   return raised;

@@ -1,4 +1,5 @@
-// CKKS bootstrapping for fully packed ciphertexts: ModRaise -> CoeffToSlot ->
+// CKKS bootstrapping for fully or sparsely packed ciphertexts (slots a power
+// of two <= N/2): ModRaise (+ the sparse-packing trace) -> CoeffToSlot ->
 // EvalMod -> SlotToCoeff, the pipeline of OpenFHE's FHECKKSRNS that the
 // reference drives through EvalBootstrapSetup({4,4},{0,0},slots,0) /
 // EvalBootstrapKeyGen / EvalBootstrap (packed_fideslib.cpp:1084-1089, :245, :259).
@@ -89,6 +90,7 @@ class Bootstrapper {
   Ckks& ck_;
   BootParams p_;
   int corr_ = 0;
+  uint32_t trace_ = 1;  // N / (2 slots): automorphisms summed after ModRaise (sparse packing)
   std::vector<Group> cts_, stc_;
   std::vector<double> cheb_;
   uint32_t levels_[4] = {0, 0, 0, 0};

@@ -18,7 +18,8 @@ int main(int argc, char** argv) {
   if (argc < 5) {
     std::cerr << "usage: packed_b200 PROGRAM RESULT POLY_TOL EXACT_TOL [--bootstrap-passes 1|2] "
                  "[--client-head FILE] [--trace-levels] [--s2c-first] [--ring-log N] [--depth D] [--seed S] "
-                 "[--device D] [--secret-key-dist uniform-ternary|sparse-encapsulated] [--sparse-h H]"
+                 "[--device D] [--secret-key-dist uniform-ternary|sparse-encapsulated] [--sparse-h H] "
+                 "[--security not-set|128-classic] [--security-digits N]"
               << std::endl;
     return 2;
   }
@@ -33,7 +34,7 @@ int main(int argc, char** argv) {
       "--gpu-plaintext-fft", "--batch-plaintext-rns", "--fuse-plaintext-rns-ntt", "--hoist-rotations",
       "--share-chebyshev"};
   static const std::set<std::string> no_effect_with_value = {"--plaintext-cache-capacity", "--prefetch-workers",
-                                                             "--frontier-live-limit", "--security-digits"};
+                                                             "--frontier-live-limit"};
   fhe_program_options o{};
   std::string client;
   try {
@@ -71,7 +72,11 @@ int main(int argc, char** argv) {
       } else if (a == "--sparse-h") {
         o.sparse_h = (uint32_t)std::stoul(value());
       } else if (a == "--security") {
-        if (value() != "not-set") throw std::invalid_argument("only --security not-set is available");
+        const std::string v = value();
+        if (v == "128-classic") o.security128 = 1;
+        else if (v != "not-set") throw std::invalid_argument("security must be not-set or 128-classic");
+      } else if (a == "--security-digits") {
+        o.security_digits = (uint32_t)std::stoul(value());
       } else if (no_effect.count(a)) {
       } else if (no_effect_with_value.count(a)) {
         value();

@@ -19,7 +19,8 @@ class ProgramOptions(ctypes.Structure):
     _fields_ = [("log_n", ctypes.c_uint32), ("depth", ctypes.c_uint32), ("scale_bits", ctypes.c_uint32),
                 ("first_bits", ctypes.c_uint32), ("dnum", ctypes.c_uint32), ("bootstrap_passes", ctypes.c_int32),
                 ("s2c_first", ctypes.c_int32), ("trace", ctypes.c_int32), ("device", ctypes.c_int32),
-                ("sparse_h", ctypes.c_uint32), ("seed", ctypes.c_uint64)]
+                ("sparse_h", ctypes.c_uint32), ("seed", ctypes.c_uint64), ("security128", ctypes.c_int32),
+                ("security_digits", ctypes.c_uint32)]
 
 
 def validate_program(path: str) -> dict:

@@ -284,7 +284,10 @@ typedef struct fhe_counters {
 } fhe_counters;
 int fhe_ctx_counters(fhe_ctx* ctx, fhe_counters* out, int32_t reset);
 
-/* Bootstrapping of fully packed ciphertexts (slots = N/2), replacing OpenFHE's
+/* Bootstrapping of the context's slots (full packing N/2, or sparse packing:
+ * a power of two below N/2, where ModRaise is followed by the trace over the
+ * rotations by multiples of the slot count, as OpenFHE does for
+ * SetBatchSize(slots) < N/2), replacing OpenFHE's
  * EvalBootstrapSetup({budget_cts, budget_stc}, {0, 0}, slots, correction) /
  * EvalBootstrapKeyGen / EvalBootstrap as called at packed_fideslib.cpp:1084-1089,
  * :245 and :259.  ModRaise -> CoeffToSlot (budget_cts levels) -> EvalMod
@@ -332,6 +335,14 @@ typedef struct fhe_program_options {
   int32_t device;             /* CUDA device ordinal [0] */
   uint32_t sparse_h;          /* sparse-secret encapsulation weight for bootstrapping [0: off] */
   uint64_t seed;              /* key seed [1] */
+  /* --security 128-classic (packed_fideslib.cpp:1060-1076): ring 2^17 unless
+   * log_n is set, dnum = security_digits [4], slots = the program's slots
+   * (sparse packing, the reference's SetBatchSize), uniform ternary secret,
+   * and Q*P checked against the 2024 guidelines' classical-128 bound for the
+   * ring (fideslib_security.hpp:18-30); the audit goes to RESULT.parameters.json
+   * and native.json's security_audit. */
+  int32_t security128;        /* [0: not-set] */
+  uint32_t security_digits;   /* [4] */
 } fhe_program_options;
 
 /* Parses and validates a program with read_packed_program's admission rules

@@ -259,3 +259,29 @@ def test_sparse_encapsulated_bootstrap(oracle):
         assert out.n_limbs() > cc.n_q - 21 + 2  # at least 3 levels above uniform ternary
         y = cc.Decrypt(out).GetCKKSPackedValue()
         assert np.max(np.abs((y if cplx else y.real) - x)) < 1e-4
+
+
+@pytest.mark.parametrize("slots", [512, 1024])
+def test_sparse_packing_bootstrap(slots):
+    """Sparsely packed slots (n < N/2, the reference's 128-bit mode runs 2^15
+    slots at N = 2^17): ModRaise, the trace over the rotations by multiples of
+    n, then CoeffToSlot / EvalMod / SlotToCoeff on n slots; the slots come back
+    with fresh limbs."""
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    cc = CryptoContext(CCParams(ring_dim=1 << 12, multiplicative_depth=25, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3, batch_size=slots))
+    assert cc.slots == slots
+    cc.KeyGen(SEED)
+    cc.EvalBootstrapSetup((4, 4))
+    cc.EvalBootstrapKeyGen()
+    r = np.random.default_rng(31 + slots)
+    for cplx in (False, True):
+        x = r.uniform(-1, 1, slots) + (1j * r.uniform(-1, 1, slots) if cplx else 0)
+        ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+        cc.LevelReduceInPlace(ct, cc.n_q - 2)
+        out = cc.EvalBootstrap(ct)
+        assert out.n_limbs() == cc.n_q - 21
+        y = cc.Decrypt(out).GetCKKSPackedValue()[:slots]
+        assert np.max(np.abs((y if cplx else y.real) - x)) < 1e-4
+        sq = cc.Decrypt(cc.EvalMult(out, out)).GetCKKSPackedValue()[:slots]
+        assert np.max(np.abs(sq - x * x)) < 4e-4

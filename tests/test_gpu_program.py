@@ -77,3 +77,27 @@ def test_mamba3_siso_generation(tmp_path):
     assert rep["passed"] and rep["non_finite"] == 0
     assert rep["generated_token_ids"] == want["polynomial_token_ids"] == want["exact_token_ids"]
     assert rep["bootstraps"] > 0
+
+
+def test_classical128_mode(tmp_path):
+    """--security 128-classic as the reference's executable sets it up: ring
+    2^17, four HYBRID digits, the program's 256 slots sparsely packed (so
+    bootstrapping runs the sparse-packing trace), and the Q*P audit (45 Q + 12
+    P primes, 3376 bits, within the 3523-bit classical-128 bound for 2^17)
+    written beside the result."""
+    out = tmp_path / "native.json"
+    r = subprocess.run([CLI, os.path.join(GOLDEN, "packed_refresh_v2.txt"), str(out), "1e-3", "1e-3",
+                        "--security", "128-classic"], capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stderr
+    assert "classical128 ring=131072 QP_bits=3376 bound=3523 digits=4" in r.stdout
+    rep = json.loads(out.read_text())
+    audit = json.loads((tmp_path / "native.json.parameters.json").read_text())
+    assert rep["passed"] and rep["security"] == "128-classic" and rep["ring_dimension"] == 131072
+    assert rep["slots"] == 256 and rep["bootstraps"] >= 2
+    assert rep["security_audit"] == audit and audit["passed"] and audit["qp_bits"] == 3376
+    assert audit["q_towers"] == 45 and audit["p_towers"] == 12 and audit["hybrid_digits"] == 4
+
+
+def test_security_digits_need_classical128(tmp_path):
+    r, _ = _run_cli(tmp_path, "packed_linear_v2.txt", 1e-6, 1e-6, "--security-digits", "4")
+    assert r.returncode == 2
