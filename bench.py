@@ -363,14 +363,27 @@ def measure_sharded_keyswitch(local, world, reps=20):
 class TokenLoop:
     """The 24-layer encrypted greedy loop: client encrypt -> server layers -> client select."""
 
-    def __init__(self, local, layers=24, passes=2, seed=6, sparse_h=0):
+    def __init__(self, local, layers=24, passes=2, seed=6, sparse_h=0, classical128=False):
         from fhe_mamba_b200 import CCParams, CryptoContext
         from fhe_mamba_b200.mamba2_layer import EncryptedMamba2Model, Mamba2Model
         t0 = time.perf_counter()
         self.model = Mamba2Model(layers=layers, d_model=768, d_state=128, heads=24, vocab=50280, seed=seed,
                                  calib_sequences=4)
-        self.cc = CryptoContext(CCParams(ring_dim=1 << 16, multiplicative_depth=44, scaling_mod_size=59,
-                                         first_mod_size=60, num_large_digits=3, device=local))
+        # 128-classic as the reference's executable sets it up: ring 2^17, four
+        # digits, 2^15 slots sparsely packed (packed_fideslib.cpp:1060-1076)
+        ring, dnum = (1 << 17, 4) if classical128 else (1 << 16, 3)
+        self.cc = CryptoContext(CCParams(ring_dim=ring, multiplicative_depth=44, scaling_mod_size=59,
+                                         first_mod_size=60, num_large_digits=dnum, batch_size=1 << 15,
+                                         device=local))
+        self.audit = None
+        if classical128:
+            import math
+            qp = math.prod(self.cc.q + self.cc.p).bit_length()
+            if qp > 3523:
+                raise RuntimeError(f"Q*P has {qp} bits, above the classical-128 bound 3523 for ring 2^17")
+            self.audit = {"ring_dimension": ring, "qp_bits": qp, "guideline_max_qp_bits": 3523,
+                          "q_towers": self.cc.n_q, "p_towers": self.cc.n_p, "hybrid_digits": dnum,
+                          "uniform_ternary": not sparse_h}
         self.cc.KeyGen(41 + seed)
         self.cc.EvalBootstrapSetup((4, 4), sparse_hamming_weight=sparse_h)
         self.cc.EvalBootstrapKeyGen()
@@ -452,7 +465,8 @@ def run_reference(args, rank):
 def config_dict(args):
     return {"workload": "BASELINE configs[4]: encrypted greedy token loop, Mamba-2-130M shape "
                         f"({args.layers} layers, d_model 768, d_state 128, 24 heads, vocab 50280)",
-            "ring_dim": 1 << 16, "slots": 1 << 15, "depth": 44, "scale_bits": 59, "dnum": 3,
+            "ring_dim": 1 << 17 if args.security == "128-classic" else 1 << 16, "slots": 1 << 15, "depth": 44,
+            "scale_bits": 59, "dnum": 4 if args.security == "128-classic" else 3, "security": args.security,
             "bootstrap_passes": args.passes,
             "secret_key_dist": f"sparse-encapsulated h={args.sparse_h}" if args.sparse_h else "uniform-ternary",
             "l2": "inputs larger than L2 (keys ~36 GB, cached diagonals)",
@@ -514,6 +528,8 @@ def main():
     ap.add_argument("--passes", type=int, default=2, choices=[1, 2], help="bootstrap passes per refresh")
     ap.add_argument("--sparse-h", type=int, default=0,
                     help="bootstrap by sparse-secret encapsulation with this Hamming weight (0: uniform ternary)")
+    ap.add_argument("--security", default="not-set", choices=["not-set", "128-classic"],
+                    help="128-classic: ring 2^17, dnum 4, 2^15 sparsely packed slots, Q*P audited")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ckks", action="store_true", help="skip the key-switch, matvec and bootstrap side measurements")
@@ -567,7 +583,8 @@ def main():
     if world > 1 and not args.no_ckks:
         side["sharded_keyswitch"] = measure_sharded_keyswitch(local, world)
 
-    loop = TokenLoop(local, layers=args.layers, passes=args.passes, seed=6 + rank, sparse_h=args.sparse_h)
+    loop = TokenLoop(local, layers=args.layers, passes=args.passes, seed=6 + rank, sparse_h=args.sparse_h,
+                     classical128=args.security == "128-classic")
     stream = torch.cuda.ExternalStream(loop.cc.stream_ptr(), device=torch.device("cuda", local))
     tok = loop.token
     for _ in range(args.warmup):
@@ -651,6 +668,7 @@ def main():
             "per_token": {"operations": per_token, "refreshes": loop.em.refreshes() / max(1, args.steps + args.warmup),
                           "setup_seconds": loop.setup_seconds, "tokens": loop.em.tokens[-args.steps:],
                           "check": loop.plaintext_check()},
+            "security_audit": loop.audit,
         }
         line.update(side)
         if world == 1 and not args.no_ckks:

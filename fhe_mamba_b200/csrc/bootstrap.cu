@@ -205,7 +205,6 @@ std::vector<int64_t> Bootstrapper::rotation_steps() const {
         if (r) s.push_back(r);
       }
     }
-  for (uint32_t j = 1; j < trace_; j *= 2) s.push_back((int64_t)j * n);  // sparse-packing trace
   std::sort(s.begin(), s.end());
   s.erase(std::unique(s.begin(), s.end()), s.end());
   return s;
@@ -219,6 +218,10 @@ void Bootstrapper::keygen() {
   }
   const uint64_t conj = 2ull * ck_.ctx.n - 1;
   if (!ck_.has_rotation_key(conj)) ck_.rotation_keygen(conj);
+  for (uint32_t j = 1; j < trace_; j *= 2) {  // sparse-packing trace
+    const uint64_t g = ck_.galois_for_full_step((int64_t)j * ck_.ctx.slots);
+    if (!ck_.has_rotation_key(g)) ck_.rotation_keygen(g);
+  }
   if (p_.sparse_h) ck_.sparse_keygen(p_.sparse_h);
 }
 
@@ -296,7 +299,7 @@ std::unique_ptr<Ct> Bootstrapper::raise(const Ct& a) {
   if (p_.sparse_h) raised = ck_.switch_to_dense(*raised);
   // Sparse packing: sum of the rotations by j*n, j < g (log2 g doublings).
   for (uint32_t j = 1; j < trace_; j *= 2) {
-    auto r = ck_.rotate(*raised, ck_.galois_for_step((int64_t)j * ctx.slots));
+    auto r = ck_.rotate(*raised, ck_.galois_for_full_step((int64_t)j * ctx.slots));
     raised = ck_.add(*raised, *r, false);
   }
   raised->scale = ck_.level_scale(ctx.L);

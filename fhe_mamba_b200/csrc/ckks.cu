@@ -256,12 +256,24 @@ LevelTables& Ckks::level(uint32_t nq) {
 // ---------------------------------------------------------------------------
 // keys
 
+// Rotation by `step` slots: sigma_{5^e}, e = step mod slots.  With sparse
+// packing (slots < N/2) every plaintext lives in the subring the rotations by
+// multiples of `slots` fix, so one Galois element per residue serves every
+// caller (keys asked for as -768 or 32000 are the same key).
 uint64_t Ckks::galois_for_step(int64_t step) const {
-  const uint64_t m = 2ull * ctx.n;
+  const int64_t order = (int64_t)ctx.slots;
+  int64_t e = step % order;
+  if (e < 0) e += order;
+  return nt::powmod(5, (uint64_t)e, 2ull * ctx.n);
+}
+
+// sigma_{5^e} with e = step mod N/2 (distinct for steps that differ by a
+// multiple of the slot count): the sparse-packing trace in bootstrapping.
+uint64_t Ckks::galois_for_full_step(int64_t step) const {
   const int64_t order = (int64_t)(ctx.n / 2);
   int64_t e = step % order;
   if (e < 0) e += order;
-  return nt::powmod(5, (uint64_t)e, m);
+  return nt::powmod(5, (uint64_t)e, 2ull * ctx.n);
 }
 
 // HYBRID switching key: digit j has a_j uniform over Q_L P and

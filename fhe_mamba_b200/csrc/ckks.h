@@ -63,6 +63,7 @@ class Ckks {
   void keygen(uint64_t seed);
   bool has_keys() const { return keyed_; }
   uint64_t galois_for_step(int64_t step) const;
+  uint64_t galois_for_full_step(int64_t step) const;
   void rotation_keygen(uint64_t g);
   bool has_rotation_key(uint64_t g) const { return rot_.count(g) != 0; }
   void download_key(int kind, uint64_t g, uint64_t* host) const;
