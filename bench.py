@@ -387,7 +387,8 @@ class TokenLoop:
         self.cc.KeyGen(41 + seed)
         self.cc.EvalBootstrapSetup((4, 4), sparse_hamming_weight=sparse_h)
         self.cc.EvalBootstrapKeyGen()
-        self.em = EncryptedMamba2Model(self.cc, self.model, passes=passes)
+        # ring 2^17 doubles every key and ciphertext: a smaller diagonal cache
+        self.em = EncryptedMamba2Model(self.cc, self.model, passes=passes, cache_gb=8 if classical128 else 40)
         self.cc.EvalRotateKeyGen(self.em.rotation_steps())
         self.cc.synchronize()
         self.setup_seconds = time.perf_counter() - t0
