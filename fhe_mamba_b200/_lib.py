@@ -122,6 +122,10 @@ SIGNATURES = {
     "fhe_ctx_counters": [vp, vp, i32],
     "fhe_kernel_launches": [ctypes.POINTER(ctypes.c_uint64)],
     "fhe_ntt_butterfly_ceiling": [vp, ctypes.POINTER(ctypes.c_double)],
+    "fhe_ct_save": [vp, vp, ctypes.c_char_p],
+    "fhe_ct_load": [vp, ctypes.c_char_p, ctypes.POINTER(vp)],
+    "fhe_keys_save": [vp, ctypes.c_char_p, i32],
+    "fhe_keys_load": [vp, ctypes.c_char_p],
     "fhe_shard_init": [vp, u32, u32],
     "fhe_shard_plan_get": [vp, u32, vp],
     "fhe_shard_load_key": [vp, i32, u64],

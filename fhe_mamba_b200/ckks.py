@@ -11,6 +11,7 @@ FheError (InvalidArgument / StateError) the way OpenFHE throws.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -289,6 +290,23 @@ class CryptoContext:
         if second is None:
             return self.EvalMult(first, bound / divisor)
         return self.EvalMult(self.EvalAdd(first, self.EvalMult(second, 1.0 / 4096.0)), bound)
+
+    # -- files for a process-separated client and server
+    def SerializeCiphertext(self, ct, path):
+        """OpenFHE Serial::SerializeToFile(path, ct) (the reference's handoff)."""
+        call("fhe_ct_save", self.h, ct.handle, os.fsencode(str(path)))
+
+    def DeserializeCiphertext(self, path):
+        return self._ct("fhe_ct_load", os.fsencode(str(path)))
+
+    def SerializeKeys(self, path, include_secret: bool = False):
+        """Public, relinearisation and rotation keys (+ the secret key if asked)."""
+        call("fhe_keys_save", self.h, os.fsencode(str(path)), int(bool(include_secret)))
+
+    def DeserializeKeys(self, path):
+        """Installs a key bundle; without the secret the context evaluates but
+        cannot decrypt or generate keys (a server)."""
+        call("fhe_keys_load", self.h, os.fsencode(str(path)))
 
     def EvalBootstrapKeyGen(self, secret_key=None, slots: int = 0):
         call("fhe_bootstrap_keygen", self.h)

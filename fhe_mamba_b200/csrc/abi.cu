@@ -631,6 +631,34 @@ int fhe_shard_automorphism(fhe_ctx* ctx, uint32_t n_limbs, uint64_t galois, cons
   });
 }
 
+int fhe_ct_save(fhe_ctx* ctx, const fhe_ct* ct, const char* path) {
+  return guarded([&] {
+    fhe::require(path != nullptr, "null path");
+    fhe::save_ciphertext(ckks(ctx), ct_of(ct), path);
+  });
+}
+
+int fhe_ct_load(fhe_ctx* ctx, const char* path, fhe_ct** out) {
+  return guarded([&] {
+    fhe::require(path != nullptr, "null path");
+    put_ct(out, fhe::load_ciphertext(ckks(ctx), path));
+  });
+}
+
+int fhe_keys_save(fhe_ctx* ctx, const char* path, int32_t include_secret) {
+  return guarded([&] {
+    fhe::require(path != nullptr, "null path");
+    ckks(ctx).save_keys(path, include_secret != 0);
+  });
+}
+
+int fhe_keys_load(fhe_ctx* ctx, const char* path) {
+  return guarded([&] {
+    fhe::require(path != nullptr, "null path");
+    ckks(ctx).load_keys(path);
+  });
+}
+
 int fhe_ntt_butterfly_ceiling(fhe_ctx* ctx, double* butterflies_per_s) {
   return guarded([&] {
     fhe::require(ctx != nullptr && butterflies_per_s != nullptr, "null argument");

@@ -330,6 +330,7 @@ void Ckks::keygen(uint64_t seed) {
   switch_keygen(0, s_ntt_.as<uint64_t>(), s2, rlk_);
   rot_.clear();
   keyed_ = true;
+  has_secret_ = true;
   FHE_CUDA(cudaStreamSynchronize(ctx.stream));
 }
 
@@ -337,6 +338,7 @@ void Ckks::keygen(uint64_t seed) {
 // rotation is KS(c1) followed by sigma_g on (c0 + u0, u1).
 void Ckks::rotation_keygen(uint64_t g) {
   require(keyed_, "rotation key generation before keygen", -4);
+  require(has_secret_, "generating keys needs the secret key (this context holds evaluation keys only)", -4);
   if (rot_.count(g)) return;
   const uint32_t lk = ctx.L + ctx.K, n = ctx.n;
   const uint64_t m = 2ull * n;
@@ -356,6 +358,7 @@ void Ckks::rotation_keygen(uint64_t g) {
 // key seed; then the two switching keys of the encapsulation.
 void Ckks::sparse_keygen(uint32_t h) {
   require(keyed_, "sparse key generation before keygen", -4);
+  require(has_secret_, "generating keys needs the secret key (this context holds evaluation keys only)", -4);
   const uint32_t n = ctx.n, L = ctx.L, K = ctx.K, lk = L + K;
   require(h >= 1 && h <= n / 2, "sparse Hamming weight out of range", -1);
   if (sparse_h_ == h) return;
@@ -418,6 +421,7 @@ size_t Ckks::key_words(int kind) const {
 
 void Ckks::download_key(int kind, uint64_t g, uint64_t* host) const {
   require(keyed_, "no keys generated", -4);
+  require(kind != 0 || has_secret_, "this context holds no secret key", -4);
   const DevMem* m = nullptr;
   if (kind == 0) m = &s_ntt_;
   else if (kind == 1) m = &pk_;
@@ -577,6 +581,7 @@ std::unique_ptr<Ct> Ckks::encrypt(const Pt& p) {
 
 std::unique_ptr<Pt> Ckks::decrypt(const Ct& c) {
   require(keyed_, "decrypt before keygen", -4);
+  require(has_secret_, "decryption needs the secret key (this context holds evaluation keys only)", -4);
   if (c.noise_deg >= 2 && c.nq >= 2 && c.ncomp == 2) {
     // FLEXIBLEAUTO: a degree-2 ciphertext is rescaled before decryption.
     auto t = clone(c);

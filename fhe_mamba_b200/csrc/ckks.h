@@ -9,6 +9,7 @@
 #include <cstdint>
 #include <map>
 #include <memory>
+#include <string>
 #include <vector>
 
 #include "ckks_kernels.h"
@@ -62,6 +63,11 @@ class Ckks {
   // keys
   void keygen(uint64_t seed);
   bool has_keys() const { return keyed_; }
+  // false for an evaluation-only context loaded from a key bundle without
+  // the secret (see serialize.cu)
+  bool has_secret() const { return has_secret_; }
+  void save_keys(const std::string& path, bool with_secret);
+  void load_keys(const std::string& path);
   uint64_t galois_for_step(int64_t step) const;
   uint64_t galois_for_full_step(int64_t step) const;
   void rotation_keygen(uint64_t g);
@@ -160,6 +166,7 @@ class Ckks {
   std::vector<Modulus> mods_host_;
   DevMem fft_inv_tw_, fft_fwd_tw_;
   bool keyed_ = false;
+  bool has_secret_ = false;
   uint64_t seed_ = 0;
   DevMem s_ntt_, pk_, rlk_;
   DevMem s_sparse_, key_to_sparse_, key_to_dense_;
@@ -179,5 +186,9 @@ class Ckks {
   ~Ckks();
   friend class ShardKeySwitch;
 };
+
+// Ciphertext files for a process-separated client and server (serialize.cu).
+void save_ciphertext(Ckks& k, const Ct& c, const std::string& path);
+std::unique_ptr<Ct> load_ciphertext(Ckks& k, const std::string& path);
 
 }  // namespace fhe

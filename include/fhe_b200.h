@@ -264,6 +264,23 @@ int fhe_shard_moddown(fhe_ctx* ctx, uint32_t n_limbs, const uint64_t* acc, const
 /* Slot permutation of both components of the own rows ([2][q_own][N]). */
 int fhe_shard_automorphism(fhe_ctx* ctx, uint32_t n_limbs, uint64_t galois, const uint64_t* in, uint64_t* out);
 
+/* --- files for a process-separated client and server ----------------------
+ * The reference's handoff (src/fideslib_handoff.cpp:27-85: serialize_ciphertext,
+ * deserialize_ciphertext, serialize_context): the client saves its evaluation
+ * keys and encrypted inputs, the server loads them into a context created with
+ * the same parameters, evaluates, and saves the result for the client.  Files
+ * carry a parameter fingerprint and a checksum; loading into a context with
+ * other parameters fails.  A key bundle saved without the secret makes an
+ * evaluation-only context: it evaluates and encrypts, but decryption and key
+ * generation fail with FHE_ERR_STATE.  Sparse-secret bootstrapping keys are not
+ * saved. */
+int fhe_ct_save(fhe_ctx* ctx, const fhe_ct* ct, const char* path);
+int fhe_ct_load(fhe_ctx* ctx, const char* path, fhe_ct** out);
+/* Public, relinearisation and every rotation key (and the secret when
+ * include_secret != 0). */
+int fhe_keys_save(fhe_ctx* ctx, const char* path, int32_t include_secret);
+int fhe_keys_load(fhe_ctx* ctx, const char* path);
+
 /* Integer-pipe ceiling of the NTT: butterflies per second of the forward
  * transform's lazy Shoup butterfly (same arithmetic and reduction schedule)
  * run on registers only, all SMs, on the context's device and stream.  The
