@@ -849,21 +849,42 @@ struct SecurityAudit {
   }
 };
 
-SecurityAudit audit_parameters(const fhe::Context& c) {
+SecurityAudit audit_moduli(uint32_t ring, const std::vector<uint64_t>& q, const std::vector<uint64_t>& p,
+                           uint32_t dnum) {
   SecurityAudit a;
-  a.ring = c.n;
-  const std::vector<uint64_t> q(c.primes.begin(), c.primes.begin() + c.L), p(c.primes.begin() + c.L, c.primes.end());
+  a.ring = ring;
+  std::vector<uint64_t> qp(q);
+  qp.insert(qp.end(), p.begin(), p.end());
   a.q_bits = product_bit_length(q);
   a.p_bits = product_bit_length(p);
-  a.qp_bits = product_bit_length(c.primes);
-  a.q_towers = c.L;
-  a.p_towers = c.K;
-  a.digits = c.dnum;
+  a.qp_bits = product_bit_length(qp);
+  a.q_towers = (uint32_t)q.size();
+  a.p_towers = (uint32_t)p.size();
+  a.digits = dnum;
   a.sigma = std::sqrt(21.0 / 2.0);  // centred binomial error, eta = 21
-  a.bound = classical128_bound(c.n);
+  a.bound = classical128_bound(ring);
   return a;
 }
+
+SecurityAudit audit_parameters(const fhe::Context& c) {
+  const std::vector<uint64_t> q(c.primes.begin(), c.primes.begin() + c.L), p(c.primes.begin() + c.L, c.primes.end());
+  return audit_moduli(c.n, q, p, c.dnum);
+}
 }  // namespace
+
+int fhe_security_audit(uint32_t log_n, uint32_t depth, uint32_t scale_bits, uint32_t first_bits, uint32_t dnum,
+                       char* json, size_t len, int32_t* passed) {
+  return guarded([&] {
+    fhe::require(log_n >= 10 && log_n <= 17, "log_n must be in [10, 17]");
+    std::vector<uint64_t> q, p;
+    fhe::nt::ckks_moduli(log_n, depth + 1, scale_bits, first_bits, dnum, q, p);
+    const SecurityAudit a = audit_moduli(1u << log_n, q, p, dnum);
+    const std::string j = a.json();
+    fhe::require(json == nullptr || len > j.size(), "audit buffer too small");
+    if (json) std::memcpy(json, j.c_str(), j.size() + 1);
+    if (passed) *passed = a.passed() ? 1 : 0;
+  });
+}
 
 int fhe_program_run(const char* program_path, const char* client_head_path, const char* result_path,
                     double poly_tol, double exact_tol, const fhe_program_options* options) {

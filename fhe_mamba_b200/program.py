@@ -23,6 +23,16 @@ class ProgramOptions(ctypes.Structure):
                 ("security_digits", ctypes.c_uint32)]
 
 
+def security_audit(log_n: int, depth: int = 44, scale_bits: int = 59, first_bits: int = 60, dnum: int = 4) -> dict:
+    """Classical-128 audit of a parameter set (no GPU): the parameters.json
+    that --security 128-classic writes, with its `passed` verdict."""
+    import json
+    buf = ctypes.create_string_buffer(2048)
+    ok = ctypes.c_int32()
+    call("fhe_security_audit", log_n, depth, scale_bits, first_bits, dnum, buf, len(buf), ctypes.byref(ok))
+    return json.loads(buf.value.decode())
+
+
 def validate_program(path: str) -> dict:
     """Parses a fhemamba-packed-v1/v2 program (no GPU); raises InvalidArgument when malformed."""
     s, n, o = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()

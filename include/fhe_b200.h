@@ -362,6 +362,12 @@ typedef struct fhe_program_options {
   uint32_t security_digits;   /* [4] */
 } fhe_program_options;
 
+/* The classical-128 audit of a parameter set without a GPU (host prime
+ * generation only): the JSON of RESULT.parameters.json and whether Q*P meets
+ * the bound.  The reference's CkksSecurityAudit (src/fideslib_security.hpp:33-80). */
+int fhe_security_audit(uint32_t log_n, uint32_t depth, uint32_t scale_bits, uint32_t first_bits, uint32_t dnum,
+                       char* json, size_t len, int32_t* passed);
+
 /* Parses and validates a program with read_packed_program's admission rules
  * (native/fideslib_stage0/include/packed_program.hpp:60-163) without touching a
  * GPU; any output pointer may be NULL. */
