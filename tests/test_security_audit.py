@@ -30,5 +30,7 @@ def test_ring_2_16_depth_44_fails_the_bound():
 
 
 def test_small_chain_within_its_ring_bound():
-    a = security_audit(14, 6, 50, 55, 2)
-    assert a["guideline_max_qp_bits"] == 430 and a["qp_bits"] <= 430 and a["passed"]
+    a = security_audit(15, 8, 50, 55, 2)
+    assert a["guideline_max_qp_bits"] == 868 and a["qp_bits"] <= 868 and a["passed"]
+    b = security_audit(14, 6, 50, 55, 2)  # BASELINE config 1's chain exceeds 430 bits
+    assert b["qp_bits"] > 430 and not b["passed"]
