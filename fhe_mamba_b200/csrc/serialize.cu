@@ -190,6 +190,11 @@ void Ckks::load_keys(const std::string& path) {
   pk_ = std::move(pk);
   rlk_ = std::move(rlk);
   rot_ = std::move(rot);
+  // keys tied to a previous secret of this context no longer apply
+  s_sparse_.release();
+  key_to_sparse_.release();
+  key_to_dense_.release();
+  sparse_h_ = 0;
   has_secret_ = with_secret != 0;
   std::random_device rd;
   // With the secret the seed comes back (new keys equal the saving context's);
