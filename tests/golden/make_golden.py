@@ -1,8 +1,8 @@
 """Regenerate the golden fixtures in tests/golden/.
 
-Run in a container where the reference checkout is mounted (its path is the
-first argument, default ``/root/reference``).  The fixtures it writes are
-committed; tests never read the reference at run time.
+Run in a container where the reference checkout is mounted; its path is the
+first argument.  The fixtures it writes are committed; tests never read the
+reference at run time.
 
 1. ``prime_chain_n17_d44_s59_f60_dnum4.json`` — the 45 Q + 12 P primes that
    the reference recorded from OpenFHE v1.4.2 / FIDESlib for
@@ -106,4 +106,6 @@ def main(ref: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_golden.py REFERENCE_CHECKOUT")
+    main(sys.argv[1])
