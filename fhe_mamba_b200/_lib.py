@@ -122,6 +122,7 @@ SIGNATURES = {
     "fhe_ctx_counters": [vp, vp, i32],
     "fhe_kernel_launches": [ctypes.POINTER(ctypes.c_uint64)],
     "fhe_ntt_butterfly_ceiling": [vp, ctypes.POINTER(ctypes.c_double)],
+    "fhe_refresh": [vp, vp, f64, i32, ctypes.POINTER(vp)],
     "fhe_security_audit": [u32, u32, u32, u32, u32, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(i32)],
     "fhe_ct_save": [vp, vp, ctypes.c_char_p],
     "fhe_ct_load": [vp, ctypes.c_char_p, ctypes.POINTER(vp)],

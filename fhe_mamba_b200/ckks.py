@@ -308,6 +308,11 @@ class CryptoContext:
         cannot decrypt or generate keys (a server)."""
         call("fhe_keys_load", self.h, os.fsencode(str(path)))
 
+    def EvalRefresh(self, ct, bound: float = 1.0, passes: int = 2):
+        """One library call for the reference's refresh (fhe_refresh): the same
+        arithmetic as refresh() without the host round trips."""
+        return self._ct("fhe_refresh", ct.handle, float(bound), int(passes))
+
     def EvalBootstrapKeyGen(self, secret_key=None, slots: int = 0):
         call("fhe_bootstrap_keygen", self.h)
 

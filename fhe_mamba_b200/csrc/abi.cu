@@ -743,6 +743,33 @@ int fhe_bootstrap(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out) {
   });
 }
 
+int fhe_refresh(fhe_ctx* ctx, const fhe_ct* a, double bound, int32_t passes, fhe_ct** out) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(ctx->boot != nullptr, "refresh before bootstrap setup", -4);
+    fhe::require(passes == 1 || passes == 2, "refresh passes must be 1 or 2");
+    fhe::require(std::isfinite(bound) && bound > 0, "refresh bound must be positive");
+    fhe::Bootstrapper& b = *ctx->boot;
+    // PackedEvaluator::refresh / bootstrap_components (packed_fideslib.cpp:235-281):
+    // bootstrap x / bound; with two passes the residual (x - first) * 4096 is
+    // bootstrapped again and added back / 4096; the result is scaled by bound.
+    auto x = k.mul_scalar(ct_of(a), 1.0 / bound);
+    if (x->noise_deg > 1) x = k.rescaled(*x);
+    auto first = b.bootstrap(*x);
+    std::unique_ptr<fhe::Ct> r;
+    if (passes == 1) {
+      r = k.mul_scalar(*first, bound);
+    } else {
+      auto residual = k.mul_scalar(*k.add(*x, *first, true), 4096.0);
+      if (residual->noise_deg > 1) residual = k.rescaled(*residual);
+      auto second = b.bootstrap(*residual);
+      r = k.mul_scalar(*k.add(*first, *k.mul_scalar(*second, 1.0 / 4096.0), false), bound);
+    }
+    if (r->noise_deg > 1) r = k.rescaled(*r);
+    put_ct(out, std::move(r));
+  });
+}
+
 int fhe_bootstrap_stage(fhe_ctx* ctx, int32_t stage, const fhe_ct* a, fhe_ct** out) {
   return guarded([&] {
     ckks(ctx);

@@ -326,6 +326,11 @@ int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, 
                         int32_t correction, int32_t s2c_first, uint32_t sparse_h);
 int fhe_bootstrap_keygen(fhe_ctx* ctx);
 int fhe_bootstrap(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
+/* The reference's refresh (PackedEvaluator::refresh / bootstrap_components,
+ * packed_fideslib.cpp:235-281): bootstrap a / bound (slots within [-bound,
+ * bound]); with passes == 2 the residual (x - first) * 4096 is bootstrapped
+ * again and added back / 4096; the result is scaled by bound. */
+int fhe_refresh(fhe_ctx* ctx, const fhe_ct* a, double bound, int32_t passes, fhe_ct** out);
 /* One step of fhe_bootstrap (EvalCoeffsToSlots / EvalSlotsToCoeffs and their
  * neighbours in OpenFHE's FHECKKSRNS): stage 0 = scale down to one limb and
  * ModRaise, 1 = CoeffToSlot, 2 = EvalMod (real and imaginary parts), 3 =

@@ -285,3 +285,17 @@ def test_sparse_packing_bootstrap(slots):
         assert np.max(np.abs((y if cplx else y.real) - x)) < 1e-4
         sq = cc.Decrypt(cc.EvalMult(out, out)).GetCKKSPackedValue()[:slots]
         assert np.max(np.abs(sq - x * x)) < 4e-4
+
+
+def test_library_refresh_matches_host_refresh(boot_ctx):
+    """fhe_refresh (one call) against the host-side refresh: same values within
+    the two-pass precision; two passes beat one; values up to the bound."""
+    cc = boot_ctx
+    x = np.random.default_rng(37).uniform(-5, 5, cc.slots)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    cc.LevelReduceInPlace(ct, cc.n_q - 4)
+    one = cc.Decrypt(cc.EvalRefresh(ct, 8.0, passes=1)).GetRealPackedValue()
+    two = cc.Decrypt(cc.EvalRefresh(ct, 8.0, passes=2)).GetRealPackedValue()
+    host = cc.Decrypt(cc.refresh(ct, 8.0, passes=2)).GetRealPackedValue()
+    assert np.max(np.abs(two - x)) < 1e-5 and np.max(np.abs(two - x)) < np.max(np.abs(one - x)) / 10
+    assert np.max(np.abs(two - host)) < 1e-5
