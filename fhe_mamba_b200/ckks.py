@@ -284,7 +284,14 @@ class CryptoContext:
 
     def refresh(self, ct, bound: float = 1.0, passes: int = 2, merge: bool = False):
         """PackedEvaluator::refresh (packed_fideslib.cpp:271-281): bootstrap x / bound
-        (one or two passes) and scale back by bound."""
+        (one or two passes) and scale back by bound.  Without merge this is one
+        library call (fhe_refresh); the merge variant composes the host steps."""
+        if not merge:
+            return self.EvalRefresh(ct, bound, passes)
+        return self.host_refresh(ct, bound, passes, merge)
+
+    def host_refresh(self, ct, bound: float = 1.0, passes: int = 2, merge: bool = False):
+        """refresh() composed from host-side calls (bootstrap_components)."""
         scaled = self.EvalMult(ct, 1.0 / bound)
         first, second, divisor = self.bootstrap_components(scaled, passes, merge)
         if second is None:

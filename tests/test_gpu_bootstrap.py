@@ -296,6 +296,6 @@ def test_library_refresh_matches_host_refresh(boot_ctx):
     cc.LevelReduceInPlace(ct, cc.n_q - 4)
     one = cc.Decrypt(cc.EvalRefresh(ct, 8.0, passes=1)).GetRealPackedValue()
     two = cc.Decrypt(cc.EvalRefresh(ct, 8.0, passes=2)).GetRealPackedValue()
-    host = cc.Decrypt(cc.refresh(ct, 8.0, passes=2)).GetRealPackedValue()
+    host = cc.Decrypt(cc.host_refresh(ct, 8.0, passes=2)).GetRealPackedValue()
     assert np.max(np.abs(two - x)) < 1e-5 and np.max(np.abs(two - x)) < np.max(np.abs(one - x)) / 10
     assert np.max(np.abs(two - host)) < 1e-5
