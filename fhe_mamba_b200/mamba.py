@@ -265,10 +265,11 @@ class PackedMamba2:
         return acc
 
     # ---- polynomial gates -------------------------------------------------
-    def poly(self, x, coeffs, lo: float, hi: float, lo_slot: int, hi_slot: int):
+    def poly(self, x, coeffs, lo: float, hi: float, lo_slot: int, hi_slot: int, out_mask=None):
         """Chebyshev series sum c_i T_i(u) on the slots [lo_slot, hi_slot) only:
         u = (2x - lo - hi) / (hi - lo) there and 0 elsewhere (so inactive slots
-        stay inside [-1, 1]); the result is masked back to the active slots."""
+        stay inside [-1, 1]); the result is masked back to the active slots
+        (or multiplied by `out_mask`, a slot vector zero outside them)."""
         c = self.cc
         a = np.zeros(self.L.slots)
         b = np.zeros(self.L.slots)
@@ -279,40 +280,51 @@ class PackedMamba2:
             c.RescaleInPlace(u)
         u = c.EvalAdd(u, c.MakeCKKSPackedPlaintext(b, level=c.n_q - u.n_limbs(), scale=u.GetScalingFactor()))
         out = c.EvalChebyshevSeries(u, coeffs, -1.0, 1.0)
-        return self._mul_mask(out, self._block_mask(lo_slot, hi_slot))
+        return self._mul_mask(out, self._block_mask(lo_slot, hi_slot) if out_mask is None else out_mask)
 
     # ---- RMSNorm ----------------------------------------------------------
-    def rms_norm(self, x, width: int, weight, eps: float, domain, degree: int = 31, newton: int = 2):
-        """x * rsqrt(mean(x^2) + eps) * weight for x at [0, width) (zeros elsewhere).
-
-        V = mean(x^2) + eps by a copy, a rotate-and-add window sum over the next
-        power of two and a 1/width mask; slots outside [0, width) are set to the
-        middle of `domain` (the bounds of V) before the Chebyshev seed of rsqrt,
-        which Newton steps y <- 1.5 y - 0.5 V y^3 refine (the reference's
-        newton_refine works on sum + width * eps and rescales by sqrt(width);
-        the mean form keeps every constant small)."""
+    def mean_square(self, x, width: int, eps: float, fill: float):
+        """V = mean(x^2) + eps on [0, width) and `fill` on every other slot, for x
+        at [0, width) (zeros elsewhere): a copy, a rotate-and-add window sum over
+        the next power of two and a 1/width mask.  Two levels below x."""
         c = self.cc
         win = 1 << max(0, (width - 1).bit_length())
         sq = c.EvalMult(x, x)
         sq = c.EvalAdd(sq, c.EvalRotate(sq, -win))
         for i in range(_log2(win)):
             sq = c.EvalAdd(sq, c.EvalRotate(sq, 1 << i))
-        lo, hi = domain
         inv = np.zeros(self.L.slots)
         inv[:width] = 1.0 / width
         v = self._mul_mask(sq, inv)  # mean(x^2) on [0, width), 0 elsewhere
         if v.GetNoiseScaleDeg() >= 2:
             c.RescaleInPlace(v)
-        fill = np.full(self.L.slots, 0.5 * (lo + hi))
-        fill[:width] = eps
-        v = c.EvalAdd(v, c.MakeCKKSPackedPlaintext(fill, level=c.n_q - v.n_limbs(), scale=v.GetScalingFactor()))
+        shift = np.full(self.L.slots, fill)
+        shift[:width] = eps
+        return c.EvalAdd(v, c.MakeCKKSPackedPlaintext(shift, level=c.n_q - v.n_limbs(), scale=v.GetScalingFactor()))
+
+    def scale_rows(self, x, y, width: int, weight):
+        """x * y * weight on [0, width): the normalised, weighted vector."""
+        w = np.zeros(self.L.slots)
+        w[:width] = np.asarray(weight, dtype=float)
+        xy = self.cc.EvalMult(x, y)
+        return self.cc.EvalMult(xy, self._plain_for(xy, w))
+
+    def rms_norm(self, x, width: int, weight, eps: float, domain, degree: int = 31, newton: int = 2):
+        """x * rsqrt(mean(x^2) + eps) * weight for x at [0, width) (zeros elsewhere).
+
+        V = mean(x^2) + eps (`mean_square`, slots outside [0, width) set to the
+        middle of `domain`, the bounds of V, so that they stay inside it) is the
+        input of a Chebyshev seed of rsqrt, which Newton steps
+        y <- 1.5 y - 0.5 V y^3 refine (the reference's newton_refine works on
+        sum + width * eps and rescales by sqrt(width); the mean form keeps every
+        constant small)."""
+        c = self.cc
+        lo, hi = domain
+        v = self.mean_square(x, width, eps, 0.5 * (lo + hi))
         y = c.EvalChebyshevFunction(lambda t: 1.0 / np.sqrt(t), v, lo, hi, degree)
         v_neg_half = c.EvalMult(v, -0.5)
         for _ in range(newton):
             y2 = c.EvalMult(y, y)
             vy = c.EvalMult(v_neg_half, y)
             y = c.EvalAdd(c.EvalMult(y, 1.5), c.EvalMult(vy, y2))
-        w = np.zeros(self.L.slots)
-        w[:width] = np.asarray(weight, dtype=float)
-        xy = c.EvalMult(x, y)
-        return c.EvalMult(xy, self._plain_for(xy, w))
+        return self.scale_rows(x, y, width, weight)

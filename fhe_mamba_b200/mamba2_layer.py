@@ -176,8 +176,19 @@ class Mamba2Polys:
         return Poly(cheb_fit(fn, lo, hi, degree), lo, hi)
 
 
-def plain_rms(x, w, eps, seed: Poly, newton=2):
+def plain_rms(x, w, eps, seed, newton=2, rec=None, key=None):
+    """x * rsqrt(mean(x^2) + eps) * w.  `seed` is a Chebyshev seed refined by
+    `newton` Newton steps, or an inverse square root with its own refinement
+    (an object with ``inv_sqrt``, as a chain payload exports them); rec(key_*)
+    then observes the variance and every iterate, at the variance and at the
+    value that fills the slots outside the vector."""
     v = np.mean(x * x) + eps
+    if hasattr(seed, "inv_sqrt"):
+        if rec is not None:
+            probe = np.array([v, seed.fill])
+            rec(key + "_v", probe)
+            seed.inv_sqrt(probe, trace=lambda name, val: rec(key + "_" + name, val))
+        return x * seed.inv_sqrt(v) * w
     y = seed(v)
     for _ in range(newton):
         y = 1.5 * y - 0.5 * v * y ** 3
@@ -201,7 +212,7 @@ def plain_step(W: Mamba2Weights, P: Mamba2Polys, h, conv_state, ssm_state):
     st = upd if ssm_state is None else decay[:, None, None] * ssm_state + upd
     y = (st * C[None, None, :]).sum(-1) + W["d"][:, None] * x
     g = y.reshape(E) * P.silu_z(z)
-    gn = plain_rms(g, W["gn_w"], W.eps, P.rsqrt2)
+    gn = plain_rms(g, W["gn_w"], getattr(W, "gated_eps", W.eps), P.rsqrt2)
     out = W["w_out"] @ gn
     return h + out, window[1:], st
 
@@ -405,13 +416,32 @@ class EncryptedMamba2Layer:
         y = self._rotation_sum(y, lay.R, lay.w)
         return self.pm._mul_mask(y, self.pm._block_mask(0, lay.m))
 
-    def _poly(self, x, p: Poly, lo_slot, hi_slot):
+    def _poly(self, x, p, lo_slot, hi_slot):
+        """A Chebyshev Poly on the slots [lo_slot, hi_slot), or a payload
+        nonlinearity (an object with ``encrypted``) evaluated its own way."""
+        if hasattr(p, "encrypted"):
+            return p.encrypted(self.pm, x, lo_slot, hi_slot)
         return self.pm.poly(x, p.coeffs, p.lo, p.hi, lo_slot, hi_slot)
 
-    def _rms(self, x, width, weight, seed: Poly, bound):
-        c = self.cc
-        x = self._fit(x, 14, bound)
-        return self.pm.rms_norm(x, width, weight, self.W.eps, (seed.lo, seed.hi), degree=len(seed.coeffs) - 1)
+    @staticmethod
+    def _need(p):
+        """Levels a nonlinearity consumes from its input (8: a degree-31 Poly)."""
+        return getattr(p, "levels", 8)
+
+    def _rms(self, x, width, weight, seed, bounds, key, prefix, eps):
+        """RMSNorm of x at [0, width).  A Chebyshev Poly seed runs the fixed
+        seed + 2 Newton steps of ``rms_norm``; a payload inverse square root
+        (``encrypted_inv_sqrt``) runs its own iteration on the variance, which
+        refreshes its iterates through bounds[prefix_*] as their levels run out."""
+        if hasattr(seed, "encrypted_inv_sqrt"):
+            x = self._fit(x, 2 + seed.levels, bounds[key])
+            v = self.pm.mean_square(x, width, eps, seed.fill)
+            y = seed.encrypted_inv_sqrt(self.cc, v, lambda ct, need, name: self._fit(ct, need, bounds[prefix + "_" + name]))
+            x = self._fit(x, 2, bounds[key])
+            y = self._fit(y, 2, bounds[prefix + "_y"])
+            return self.pm.scale_rows(x, y, width, weight)
+        x = self._fit(x, 14, bounds[key])
+        return self.pm.rms_norm(x, width, weight, eps, (seed.lo, seed.hi), degree=len(seed.coeffs) - 1)
 
     # ---- one token ------------------------------------------------------------
     def step(self, h, conv_state, ssm_state, bounds):
@@ -426,7 +456,7 @@ class EncryptedMamba2Layer:
         c, W, P = self.cc, self.W, self.P
         E, S, H, Dm = W.d_inner, W.d_state, W.heads, W.d_model
         cd = W.conv_dim
-        u = self._rms(h, Dm, W["norm_w"], P.rsqrt1, bounds["h"])
+        u = self._rms(h, Dm, W["norm_w"], P.rsqrt1, bounds, "h", "n1", W.eps)
         u = self._fit(u, 2, bounds["u"])
         proj = self._linear(u, "w_in")
         proj = self._fit(proj, 19, bounds["proj"])
@@ -441,7 +471,7 @@ class EncryptedMamba2Layer:
         bias = np.zeros(c.slots)
         bias[:cd] = W["conv_b"]
         xc = self.pm.conv(window, taps, bias)
-        xc = self._fit(xc, 8, bounds["xc"])
+        xc = self._fit(xc, self._need(P.silu_x), bounds["xc"])
         xa = self._poly(xc, P.silu_x, 0, cd)
         # dt and decay at [0, heads)
         dtv = self.pm._mul_mask(c.EvalRotate(proj, E + cd), self.pm._block_mask(0, H))
@@ -451,13 +481,16 @@ class EncryptedMamba2Layer:
         bias_dt[:H] = W["dt_bias"]
         dtv = c.EvalAdd(dtv, c.MakeCKKSPackedPlaintext(bias_dt, level=c.n_q - dtv.n_limbs(),
                                                         scale=dtv.GetScalingFactor()))
-        dtv = self._fit(dtv, 8, bounds["dt"])
+        dtv = self._fit(dtv, self._need(P.softplus), bounds["dt"])
         dts = self._poly(dtv, P.softplus, 0, H)
         pack = c.EvalAdd(xa, c.EvalRotate(dts, -self.dt_base))
         if ssm_state is not None:
+            # heads a payload prunes (head mask 0) get input 0, inside the
+            # decay polynomial's domain; the polynomial's output mask zeroes them
+            mask = getattr(P.exp, "head_mask", None)
             avec = np.zeros(c.slots)
-            avec[:H] = W["a"]
-            adt = self._fit(self.pm._mul_mask(dts, avec), 8, bounds["adt"])
+            avec[:H] = W["a"] if mask is None else W["a"] * mask
+            adt = self._fit(self.pm._mul_mask(dts, avec), self._need(P.exp), bounds["adt"])
             decay = self._poly(adt, P.exp, 0, H)
             pack = c.EvalAdd(pack, c.EvalRotate(decay, -self.decay_base))
         pack = self._fit(pack, 8, bounds["pack"])
@@ -470,11 +503,11 @@ class EncryptedMamba2Layer:
         y = c.EvalAdd(y, self.pm._mul_mask(pack, dvec))
         # gate
         z = self.pm._mul_mask(proj, self.pm._block_mask(0, E))
-        z = self._fit(z, 8, bounds["z"])
+        z = self._fit(z, self._need(P.silu_z), bounds["z"])
         sz = self._poly(z, P.silu_z, 0, E)
         y = self._fit(y, 2, bounds["y"])
         g = c.EvalMult(y, sz)
-        gn = self._rms(g, E, W["gn_w"], P.rsqrt2, bounds["g"])
+        gn = self._rms(g, E, W["gn_w"], P.rsqrt2, bounds, "g", "n2", getattr(W, "gated_eps", W.eps))
         gn = self._fit(gn, 2, bounds["gn"])
         out = self._linear(gn, "w_out")
         h_out = c.EvalAdd(h, out)
@@ -485,7 +518,7 @@ def poly_step_record(W: Mamba2Weights, P: Mamba2Polys, h, conv, st, rec):
     """plain_step that reports the magnitude of every refreshed intermediate."""
     E, S, H, Pd = W.d_inner, W.d_state, W.heads, W.head_dim
     rec("h", h)
-    u = plain_rms(h, W["norm_w"], W.eps, P.rsqrt1)
+    u = plain_rms(h, W["norm_w"], W.eps, P.rsqrt1, rec=rec, key="n1")
     rec("u", u)
     proj = W["w_in"] @ u
     rec("proj", proj)
@@ -512,7 +545,7 @@ def poly_step_record(W: Mamba2Weights, P: Mamba2Polys, h, conv, st, rec):
     rec("y", y)
     g = y.reshape(E) * P.silu_z(z)
     rec("g", g)
-    gn = plain_rms(g, W["gn_w"], W.eps, P.rsqrt2)
+    gn = plain_rms(g, W["gn_w"], getattr(W, "gated_eps", W.eps), P.rsqrt2, rec=rec, key="n2")
     rec("gn", gn)
     out = W["w_out"] @ gn
     return h + out, window[1:], st

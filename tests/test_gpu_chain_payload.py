@@ -1,0 +1,49 @@
+"""The reference exporter's Mamba-2 chain payload (tests/golden/mamba2_chain:
+2 layers, d_model 64, 16 heads x 8, d_state 32, degree-96/64/24 activations,
+degree-47/31 Newton-refined inverse square roots) decoded on ciphertexts:
+the decrypted final hidden vectors against the exporter's polynomial-circuit
+references (chain_expected_poly_final), and the client loop's greedy ids.
+The tolerance is 50x the error the slot-level model of the same schedule
+predicts with the two-pass refresh's measured noise (test_chain_decode_sim)."""
+import json
+import os
+
+import pytest
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+CHAIN = os.path.join(GOLDEN, "mamba2_chain")
+TOL = 5e-3
+
+
+def test_chain_decode_matches_polynomial_circuit():
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    from fhe_mamba_b200.chain_payload import read_chain_payload, run_chain
+    p = read_chain_payload(CHAIN)
+    cc = CryptoContext(CCParams(ring_dim=1 << 12, multiplicative_depth=44, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3))
+    cc.KeyGen(53)
+    cc.EvalBootstrapSetup((4, 4))
+    cc.EvalBootstrapKeyGen()
+    r = run_chain(cc, p, 3, TOL)
+    m = r["measurements"]
+    print("chain decode", m["per_token_max_abs_error"], "refreshes", m["refreshes"],
+          "s/token", m["seconds_per_token"])
+    assert r["passed"], m
+    assert m["max_abs_error"] < TOL and m["refreshes"] >= 6
+
+
+def test_cli_client_loop(tmp_path):
+    from fhe_mamba_b200 import mamba2_decode
+    out = tmp_path / "result.json"
+    rc = mamba2_decode.main(["--input-chain", CHAIN, "--output-json", str(out), "--ring-dim", "4096",
+                             "--security", "not-set", "--bootstrap-level-budget-cts", "4",
+                             "--bootstrap-level-budget-stc", "4", "--autoregressive-client-loop", "1",
+                             "--tokens", "3", "--tolerance", str(TOL), "--seed", "59"])
+    r = json.loads(out.read_text())
+    print("client loop", r.get("measurements", r))
+    assert rc == 0 and r["passed"], r
+    assert r["measurements"]["autoregressive_selected_ids"] == [80, 117]
+    assert r["parameters"]["num_large_digits"] == 3
