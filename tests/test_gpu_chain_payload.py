@@ -3,8 +3,10 @@
 degree-47/31 Newton-refined inverse square roots) decoded on ciphertexts:
 the decrypted final hidden vectors against the exporter's polynomial-circuit
 references (chain_expected_poly_final), and the client loop's greedy ids.
-The tolerance is 50x the error the slot-level model of the same schedule
-predicts with the two-pass refresh's measured noise (test_chain_decode_sim)."""
+Measured on a B200: 2.5e-6, the float32 rounding of the references
+themselves; the tolerance is the error the slot-level model of the same
+schedule predicts with the two-pass refresh's noise bound (1e-6 x the refresh
+bound, test_chain_decode_sim)."""
 import json
 import os
 
@@ -15,7 +17,7 @@ from conftest import GOLDEN
 pytestmark = pytest.mark.gpu
 
 CHAIN = os.path.join(GOLDEN, "mamba2_chain")
-TOL = 5e-3
+TOL = 1e-4
 
 
 def test_chain_decode_matches_polynomial_circuit():
