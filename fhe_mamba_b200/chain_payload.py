@@ -732,6 +732,35 @@ def chain_bounds(payload: ChainPayload, sequences=None):
 # encrypted decode
 
 
+CARRIED_SITES = ("xbc", "state")
+
+
+def meta_bts_policy(layer: int, enabled: bool, residual_layers=(), scheduled: bool = False):
+    """Refresh pass count per site of one layer under the reference decode's
+    Meta-BTS selection (should_use_meta_bts,
+    native/fideslib_stage0/src/stage1_mamba2_config.cpp:69-86): a refresh
+    is two-pass (Meta-BTS, residual amplified by 2^12) for every transient
+    value of a layer with a scheduled normalization, and with Meta-BTS enabled
+    for the carried values (conv FIFO ``xbc`` and recurrent ``state``), the
+    gated norm's polynomial input (``gated_poly_input`` there; here the gated
+    value ``g`` refreshed before its variance is taken, and the variance
+    ``n2_v``) and the layer's residual input (``h``) at the selected layers;
+    every other refresh is one bootstrap."""
+    residual_layers = frozenset(residual_layers)
+
+    def passes(site):
+        site = site or ""
+        if scheduled and site not in CARRIED_SITES:
+            return 2
+        if not enabled:
+            return 1
+        if site in CARRIED_SITES or site in ("g", "n2_v"):
+            return 2
+        return 2 if site == "h" and layer in residual_layers else 1
+
+    return passes
+
+
 class EncryptedChain:
     """The payload's layers on one CryptoContext: the client encrypts a token's
     embedding, every loaded layer runs on ciphertexts (EncryptedMamba2Layer with
@@ -739,10 +768,20 @@ class EncryptedChain:
     a complete chain ends with the final RMSNorm (the reference's run_layer loop
     and final_norm, stage1_mamba2_decode_fideslib.cpp:3634-4520)."""
 
-    def __init__(self, cc, payload: ChainPayload, passes: int = 2, cache_gb: float = 8.0, bounds=None):
+    def __init__(self, cc, payload: ChainPayload, passes: int = 2, cache_gb: float = 8.0, bounds=None,
+                 meta_bts: bool | None = None, meta_bts_residual_layers=()):
+        """passes: every refresh's pass count (2: each refresh is Meta-BTS), or,
+        with meta_bts set (True / False), the reference's selective policy."""
         self.cc, self.p = cc, payload
         self.cache = PlaintextCache(cache_gb * 2 ** 30)
-        self.layers = [EncryptedMamba2Layer(cc, L.weights, L.polys, passes=passes, cache=self.cache)
+
+        def policy(L):
+            if meta_bts is None:
+                return passes
+            scheduled = isinstance(L.polys.rsqrt1, ScheduledInvSqrt) or isinstance(L.polys.rsqrt2, ScheduledInvSqrt)
+            return meta_bts_policy(L.index, meta_bts, meta_bts_residual_layers, scheduled)
+
+        self.layers = [EncryptedMamba2Layer(cc, L.weights, L.polys, passes=policy(L), cache=self.cache)
                        for L in payload.layers]
         self.bounds = bounds if bounds is not None else chain_bounds(payload)
         self.reset()
@@ -758,6 +797,9 @@ class EncryptedChain:
 
     def refreshes(self) -> int:
         return sum(layer.refreshes for layer in self.layers)
+
+    def two_pass_refreshes(self) -> int:
+        return sum(layer.two_pass_refreshes for layer in self.layers)
 
     def step(self, embedding):
         """Server pass for one token: the encrypted final hidden vector (the
@@ -792,7 +834,8 @@ def select_token(payload: ChainPayload, hidden) -> int:
 
 
 def run_chain(cc, payload: ChainPayload, tokens: int, tolerance: float = 5e-2,
-              autoregressive_client_loop: bool = False, passes: int = 2, cache_gb: float = 8.0):
+              autoregressive_client_loop: bool = False, passes: int = 2, cache_gb: float = 8.0,
+              meta_bts: bool | None = None, meta_bts_residual_layers=()):
     """The decode's chain mode: encrypt each test (or client-selected) token's
     embedding, evaluate, decrypt, and compare with the polynomial-circuit
     reference (``chain_expected_poly_final``, or the last layer's
@@ -828,7 +871,8 @@ def run_chain(cc, payload: ChainPayload, tokens: int, tolerance: float = 5e-2,
     has_poly = poly_ref is not None
     reference = poly_ref if has_poly else exact_ref
     t0 = time.perf_counter()
-    chain = EncryptedChain(cc, p, passes=passes, cache_gb=cache_gb)
+    chain = EncryptedChain(cc, p, passes=passes, cache_gb=cache_gb, meta_bts=meta_bts,
+                           meta_bts_residual_layers=meta_bts_residual_layers)
     cc.EvalRotateKeyGen(chain.rotation_steps())
     setup = time.perf_counter() - t0
     per_token, per_token_exact, ok, selected, outputs = [], [], [], [], []
@@ -864,7 +908,8 @@ def run_chain(cc, payload: ChainPayload, tokens: int, tolerance: float = 5e-2,
                        "conv_dim": w.conv_dim, "proj_dim": w.proj_dim, "layers": len(p.layers),
                        "chain_layers": p.n_layers, "tokens": tokens, "ring_dim": cc.n, "slots": cc.slots,
                        "autoregressive_client_loop": autoregressive_client_loop, "tolerance": tolerance,
-                       "refresh_passes": passes},
+                       "refresh_passes": passes if meta_bts is None else None, "meta_bts": meta_bts,
+                       "meta_bts_alpha": 12, "meta_bts_residual_layers": sorted(meta_bts_residual_layers)},
         "measurements": {
             "correctness_reference": "polynomial-circuit" if has_poly else "exact-legacy",
             "max_abs_error": max_error,
@@ -879,6 +924,7 @@ def run_chain(cc, payload: ChainPayload, tokens: int, tolerance: float = 5e-2,
             "token0_expected_sample": [float(v) for v in reference[0][:8]],
             "token0_exact_sample": [float(v) for v in exact_ref[0][:8]],
             "refreshes": chain.refreshes(),
+            "meta_bts_applied": chain.two_pass_refreshes(),
             "setup_seconds": setup,
             "decode_seconds": seconds,
             "seconds_per_token": seconds / tokens,

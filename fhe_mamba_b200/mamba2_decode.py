@@ -10,7 +10,15 @@ stage1_mamba2_config.hpp:20-211):
         [--bootstrap-level-budget-stc 5] [--security 128-classic|not-set]
         [--secret-key-dist uniform-ternary|sparse-encapsulated]
         [--autoregressive-client-loop 0|1] [--tolerance 5e-2] [--refresh-passes 2]
+        [--meta-bts 0|1] [--meta-bts-alpha 12] [--meta-bts-residual-layers 20,21]
         [--pt-cache-gib 5] [--seed 0]
+
+Refreshes: by default every refresh is two-pass (the residual of the first
+bootstrap, amplified by 2^12, bootstrapped again: the reference's Meta-BTS)
+or one bootstrap with --refresh-passes 1; --meta-bts 0|1 selects the
+reference decode's own policy instead (Meta-BTS only for carried values, the
+gated norm's polynomial input, the residual at --meta-bts-residual-layers,
+and the transient values of scheduled-normalization layers).
 
 The result document goes to --output-json; the exit code is 0 when the
 decrypted outputs are within --tolerance of the payload's polynomial-circuit
@@ -59,6 +67,10 @@ def parse_args(argv=None):
     ap.add_argument("--autoregressive-client-loop", type=_bool, default=False)
     ap.add_argument("--tolerance", type=float, default=5e-2)
     ap.add_argument("--refresh-passes", type=int, choices=(1, 2), default=2)
+    ap.add_argument("--meta-bts", type=_bool, default=None)
+    ap.add_argument("--meta-bts-alpha", type=int, default=12)
+    ap.add_argument("--state-meta-bts-alpha", type=int, default=-1)
+    ap.add_argument("--meta-bts-residual-layers", default="")
     ap.add_argument("--pt-cache-gib", type=float, default=5.0)
     ap.add_argument("--seed", type=int, default=0)
     return ap.parse_args(argv)
@@ -69,6 +81,12 @@ def run(args) -> dict:
     from .ckks import CCParams, CryptoContext
     from .program import security_audit
 
+    if args.meta_bts_alpha != 12 or args.state_meta_bts_alpha not in (-1, 12):
+        raise PayloadError("the refresh amplifies the Meta-BTS residual by 2^12 (--meta-bts-alpha 12)")
+    try:
+        residual_layers = {int(t) for t in args.meta_bts_residual_layers.split(",") if t}
+    except ValueError as e:
+        raise PayloadError("--meta-bts-residual-layers expects comma-separated layer indices") from e
     if args.secret_key_dist not in ("uniform-ternary", "sparse-encapsulated"):
         raise PayloadError(f"unsupported --secret-key-dist {args.secret_key_dist} "
                            "(uniform-ternary or sparse-encapsulated)")
@@ -99,7 +117,8 @@ def run(args) -> dict:
                           sparse_hamming_weight=32 if args.secret_key_dist == "sparse-encapsulated" else 0)
     cc.EvalBootstrapKeyGen()
     result = run_chain(cc, payload, args.tokens, args.tolerance, args.autoregressive_client_loop,
-                       passes=args.refresh_passes, cache_gb=args.pt_cache_gib)
+                       passes=args.refresh_passes, cache_gb=args.pt_cache_gib, meta_bts=args.meta_bts,
+                       meta_bts_residual_layers=residual_layers)
     result["parameters"].update({"multiplicative_depth": args.multiplicative_depth,
                                  "scaling_mod_size": args.scaling_mod_size, "first_mod_size": args.first_mod_size,
                                  "num_large_digits": args.num_large_digits, "security": args.security,

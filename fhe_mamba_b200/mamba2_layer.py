@@ -356,7 +356,7 @@ class EncryptedMamba2Layer:
             raise ValueError("packed SSM inputs do not fit the slots")
         self.pm = PackedMamba2(cc, self.layout, b_base=E, c_base=E + S, head_base=self.dt_base,
                                decay_base=self.decay_base)
-        self.refreshes = 0
+        self.refreshes = self.two_pass_refreshes = 0
         self._lin = {}
         n = cc.slots
     # ---- setup --------------------------------------------------------------
@@ -380,14 +380,18 @@ class EncryptedMamba2Layer:
     def _left(self, ct):
         return ct.n_limbs() - 1 - (1 if ct.GetNoiseScaleDeg() >= 2 else 0)
 
-    def _fit(self, ct, need, bound):
+    def _fit(self, ct, need, bound, site=None):
         """Refreshes ct when fewer than need + margin levels remain; the margin keeps
         every stage's output refreshable (a two-pass refresh spends two levels
-        before its second bootstrap, which needs two limbs)."""
+        before its second bootstrap, which needs two limbs).  `passes` is the
+        refresh's pass count, or a function of the refresh site's name (a
+        refresh policy such as the reference's selective Meta-BTS)."""
         if self._left(ct) >= need + self.margin:
             return ct
+        passes = self.passes(site) if callable(self.passes) else self.passes
         self.refreshes += 1
-        return self.cc.refresh(ct, bound, passes=self.passes)
+        self.two_pass_refreshes += passes == 2
+        return self.cc.refresh(ct, bound, passes=passes)
 
     def _rotation_sum(self, x, count, stride):
         c = self.cc
@@ -434,13 +438,14 @@ class EncryptedMamba2Layer:
         (``encrypted_inv_sqrt``) runs its own iteration on the variance, which
         refreshes its iterates through bounds[prefix_*] as their levels run out."""
         if hasattr(seed, "encrypted_inv_sqrt"):
-            x = self._fit(x, 2 + seed.levels, bounds[key])
+            x = self._fit(x, 2 + seed.levels, bounds[key], key)
             v = self.pm.mean_square(x, width, eps, seed.fill)
-            y = seed.encrypted_inv_sqrt(self.cc, v, lambda ct, need, name: self._fit(ct, need, bounds[prefix + "_" + name]))
-            x = self._fit(x, 2, bounds[key])
-            y = self._fit(y, 2, bounds[prefix + "_y"])
+            y = seed.encrypted_inv_sqrt(
+                self.cc, v, lambda ct, need, name: self._fit(ct, need, bounds[prefix + "_" + name], prefix + "_" + name))
+            x = self._fit(x, 2, bounds[key], key)
+            y = self._fit(y, 2, bounds[prefix + "_y"], prefix + "_y")
             return self.pm.scale_rows(x, y, width, weight)
-        x = self._fit(x, 14, bounds[key])
+        x = self._fit(x, 14, bounds[key], key)
         return self.pm.rms_norm(x, width, weight, eps, (seed.lo, seed.hi), degree=len(seed.coeffs) - 1)
 
     # ---- one token ------------------------------------------------------------
@@ -457,12 +462,12 @@ class EncryptedMamba2Layer:
         E, S, H, Dm = W.d_inner, W.d_state, W.heads, W.d_model
         cd = W.conv_dim
         u = self._rms(h, Dm, W["norm_w"], P.rsqrt1, bounds, "h", "n1", W.eps)
-        u = self._fit(u, 2, bounds["u"])
+        u = self._fit(u, 2, bounds["u"], "u")
         proj = self._linear(u, "w_in")
-        proj = self._fit(proj, 19, bounds["proj"])
+        proj = self._fit(proj, 19, bounds["proj"], "proj")
         # xBC stream at [0, conv_dim) and the causal conv
         xbc = self.pm._mul_mask(c.EvalRotate(proj, E), self.pm._block_mask(0, cd))
-        window = [self._fit(w, 2, bounds["xbc"]) if w is not None else None for w in conv_state] + [xbc]
+        window = [self._fit(w, 2, bounds["xbc"], "xbc") if w is not None else None for w in conv_state] + [xbc]
         taps = []
         for k in range(W.conv_kernel):
             t = np.zeros(c.slots)
@@ -471,7 +476,7 @@ class EncryptedMamba2Layer:
         bias = np.zeros(c.slots)
         bias[:cd] = W["conv_b"]
         xc = self.pm.conv(window, taps, bias)
-        xc = self._fit(xc, self._need(P.silu_x), bounds["xc"])
+        xc = self._fit(xc, self._need(P.silu_x), bounds["xc"], "xc")
         xa = self._poly(xc, P.silu_x, 0, cd)
         # dt and decay at [0, heads)
         dtv = self.pm._mul_mask(c.EvalRotate(proj, E + cd), self.pm._block_mask(0, H))
@@ -481,7 +486,7 @@ class EncryptedMamba2Layer:
         bias_dt[:H] = W["dt_bias"]
         dtv = c.EvalAdd(dtv, c.MakeCKKSPackedPlaintext(bias_dt, level=c.n_q - dtv.n_limbs(),
                                                         scale=dtv.GetScalingFactor()))
-        dtv = self._fit(dtv, self._need(P.softplus), bounds["dt"])
+        dtv = self._fit(dtv, self._need(P.softplus), bounds["dt"], "dt")
         dts = self._poly(dtv, P.softplus, 0, H)
         pack = c.EvalAdd(xa, c.EvalRotate(dts, -self.dt_base))
         if ssm_state is not None:
@@ -490,25 +495,25 @@ class EncryptedMamba2Layer:
             mask = getattr(P.exp, "head_mask", None)
             avec = np.zeros(c.slots)
             avec[:H] = W["a"] if mask is None else W["a"] * mask
-            adt = self._fit(self.pm._mul_mask(dts, avec), self._need(P.exp), bounds["adt"])
+            adt = self._fit(self.pm._mul_mask(dts, avec), self._need(P.exp), bounds["adt"], "adt")
             decay = self._poly(adt, P.exp, 0, H)
             pack = c.EvalAdd(pack, c.EvalRotate(decay, -self.decay_base))
-        pack = self._fit(pack, 8, bounds["pack"])
+        pack = self._fit(pack, 8, bounds["pack"], "pack")
         # state update and readout from the packed inputs
         if ssm_state is not None:
-            ssm_state = [self._fit(st, 4, bounds["state"]) for st in ssm_state]
+            ssm_state = [self._fit(st, 4, bounds["state"], "state") for st in ssm_state]
         states, y = self.pm.step(ssm_state, pack, pack, pack if ssm_state is not None else None)
         dvec = np.zeros(c.slots)
         dvec[:E] = np.repeat(W["d"], W.head_dim)
         y = c.EvalAdd(y, self.pm._mul_mask(pack, dvec))
         # gate
         z = self.pm._mul_mask(proj, self.pm._block_mask(0, E))
-        z = self._fit(z, self._need(P.silu_z), bounds["z"])
+        z = self._fit(z, self._need(P.silu_z), bounds["z"], "z")
         sz = self._poly(z, P.silu_z, 0, E)
-        y = self._fit(y, 2, bounds["y"])
+        y = self._fit(y, 2, bounds["y"], "y")
         g = c.EvalMult(y, sz)
         gn = self._rms(g, E, W["gn_w"], P.rsqrt2, bounds, "g", "n2", getattr(W, "gated_eps", W.eps))
-        gn = self._fit(gn, 2, bounds["gn"])
+        gn = self._fit(gn, 2, bounds["gn"], "gn")
         out = self._linear(gn, "w_out")
         h_out = c.EvalAdd(h, out)
         return h_out, window[1:], states

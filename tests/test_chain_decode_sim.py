@@ -80,3 +80,46 @@ def test_simulator_catches_missing_keys_and_bounds():
         x = cc.EvalMult(x, 1.5)
     with pytest.raises(SimError, match="underflow"):
         cc.EvalMult(x, 1.5)
+
+
+class _CountingContext(SlotContext):
+    """Records the pass count of every refresh by the bound it was given."""
+
+    def __init__(self, *a, **k):
+        super().__init__(*a, **k)
+        self.passes_seen = []
+
+    def refresh(self, ct, bound=1.0, passes=2, merge=False):
+        self.passes_seen.append(passes)
+        return super().refresh(ct, bound, passes)
+
+
+@pytest.mark.parametrize("meta_bts,residual_layers", [(False, ()), (True, ()), (True, (1,))])
+def test_meta_bts_policy(payload, meta_bts, residual_layers):
+    """The reference decode's selective Meta-BTS: with it off every refresh is
+    one bootstrap (this payload has no scheduled normalization); with it on,
+    only carried values, the gated norm's polynomial input and the selected
+    layers' residual refreshes are two-pass (here: the gated values, 6 of the
+    ~25 refreshes; the carried values never run out of levels)."""
+    from fhe_mamba_b200.chain_payload import meta_bts_policy
+    cc = _CountingContext(2048, refresh_noise=0.0)
+    r = run_chain(cc, payload, 3, 1e-4, meta_bts=meta_bts, meta_bts_residual_layers=residual_layers)
+    m = r["measurements"]
+    assert r["passed"] and m["refreshes"] == len(cc.passes_seen)
+    assert m["meta_bts_applied"] == cc.passes_seen.count(2)
+    if not meta_bts:
+        assert m["meta_bts_applied"] == 0
+    else:
+        assert 0 < m["meta_bts_applied"] < m["refreshes"]
+    policy = meta_bts_policy(1, meta_bts, residual_layers)
+    assert policy("state") == policy("xbc") == policy("g") == policy("n2_v") == (2 if meta_bts else 1)
+    assert policy("proj") == policy("n1_y") == 1
+    assert policy("h") == (2 if 1 in residual_layers else 1)
+    assert meta_bts_policy(0, False, (), scheduled=True)("proj") == 2
+    assert meta_bts_policy(0, False, (), scheduled=True)("state") == 1
+
+
+def test_every_refresh_two_pass_by_default(payload):
+    cc = _CountingContext(2048, refresh_noise=0.0)
+    r = run_chain(cc, payload, 2, 1e-4)
+    assert set(cc.passes_seen) == {2} and r["measurements"]["meta_bts_applied"] == r["measurements"]["refreshes"]

@@ -249,6 +249,8 @@ def test_cli_reports_errors_without_a_gpu(tmp_path):
     rc = mamba2_decode.main(["--input-chain", str(tmp_path / "missing"), "--output-json", str(out),
                              "--security", "not-set"])
     assert rc == 2 and "failed to open" in json.loads(out.read_text())["error"]
+    rc = mamba2_decode.main(["--input-chain", CHAIN, "--output-json", str(out), "--meta-bts-alpha", "16"])
+    assert rc == 2 and "2^12" in json.loads(out.read_text())["error"]
     # 128-classic over a ring too small for the chain is refused by the audit
     rc = mamba2_decode.main(["--input-chain", CHAIN, "--output-json", str(out), "--ring-dim", "4096"])
     assert rc == 2 and "classical-128" in json.loads(out.read_text())["error"]

@@ -49,3 +49,23 @@ def test_cli_client_loop(tmp_path):
     assert rc == 0 and r["passed"], r
     assert r["measurements"]["autoregressive_selected_ids"] == [80, 117]
     assert r["parameters"]["num_large_digits"] == 3
+
+
+def test_reference_refresh_policy():
+    """The reference decode's own refresh policy (--meta-bts 1: two-pass only
+    for carried values and the gated norm's input, single bootstraps
+    elsewhere).  Measured on a B200: 2.4e-4 (3.2e-4 with Meta-BTS off) against
+    2.5e-6 when every refresh is two-pass; the bound keeps an 8x margin."""
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    from fhe_mamba_b200.chain_payload import read_chain_payload, run_chain
+    p = read_chain_payload(CHAIN)
+    cc = CryptoContext(CCParams(ring_dim=1 << 12, multiplicative_depth=44, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3))
+    cc.KeyGen(67)
+    cc.EvalBootstrapSetup((4, 4))
+    cc.EvalBootstrapKeyGen()
+    r = run_chain(cc, p, 3, 2e-3, meta_bts=True)
+    m = r["measurements"]
+    print("meta-bts policy", m["max_abs_error"], m["refreshes"], m["meta_bts_applied"])
+    assert r["passed"], m
+    assert 0 < m["meta_bts_applied"] < m["refreshes"]
