@@ -37,7 +37,9 @@ ciphertexts through the device library:
   y <- y (a_i - b_i u), u <- u (a_i - b_i u)^2 from a public seed, then one
   Newton step recomputed from v.
 
-The Mamba-2 joint-gate format (``fhemamba-m1-joint-v1``) is refused.
+The joint formats (``fhemamba-m2-chain-joint-v1`` / ``fhemamba-m1-joint-v1``)
+add shared-dissipation-factor gates (``JointGate``) that replace the softplus
+and decay sites.
 """
 from __future__ import annotations
 
@@ -52,7 +54,9 @@ import numpy as np
 from .mamba2_layer import EncryptedMamba2Layer, PlaintextCache, plain_rms, poly_step_record
 
 CHAIN_FORMAT = "fhemamba-m2-chain-v1"
+JOINT_CHAIN_FORMAT = "fhemamba-m2-chain-joint-v1"
 LAYER_FORMAT = "fhemamba-m1-v1"
+JOINT_LAYER_FORMAT = "fhemamba-m1-joint-v1"
 SITES = ("conv_silu", "gate_silu", "dt_softplus", "decay_exp", "rms_invsqrt", "gated_rms_invsqrt")
 NORM_SITES = ("rms_invsqrt", "gated_rms_invsqrt")
 
@@ -303,7 +307,10 @@ class ScheduledInvSqrt(_InvSqrt):
 
     @property
     def fill(self) -> float:
-        return 0.5 * (self.lo + self.hi)
+        # the geometric mean: inside the interval and, for the wide public
+        # intervals these schedules cover (lo ~ 1e-6), near the variances
+        # themselves, so that it does not set the refresh bound of v
+        return math.sqrt(self.lo * self.hi)
 
     levels = 2
 
@@ -313,28 +320,143 @@ class ScheduledInvSqrt(_InvSqrt):
         y = self.seed
         last = len(self.coefficients) - 1
         for i, (a, b) in enumerate(self.coefficients):
+            if trace:
+                trace(f"u{i}", u)
             f = a - b * u
             y = y * f
             if trace:
-                trace("y", y)
+                trace(f"y{i}", y)
             if i < last:
                 u = u * (f * f)
-                if trace:
-                    trace("u", u)
         return self._newton(v, y, trace)
 
     def encrypted_inv_sqrt(self, c, v, fit):
+        """u and y move over orders of magnitude during the schedule (u from
+        v s^2 towards 1), so each step's refreshes have their own bounds
+        (``u<i>``, ``y<i>``): a refresh's error is relative to its bound."""
         s = self.seed
         u = c.EvalMult(v, s * s)
         y = None
         last = len(self.coefficients) - 1
         for i, (a, b) in enumerate(self.coefficients):
-            u = fit(u, 3, "u")
+            u = fit(u, 3, f"u{i}")
             f = c.EvalAdd(c.EvalMult(u, -b), a)
-            y = c.EvalMult(f, s) if y is None else c.EvalMult(fit(y, 2, "y"), f)
+            y = c.EvalMult(f, s) if y is None else c.EvalMult(fit(y, 2, f"y{i - 1}"), f)
             if i < last:
                 u = c.EvalMult(u, c.EvalMult(f, f))
         return self._encrypted_newton(c, v, y, fit)
+
+
+@dataclass(frozen=True)
+class JointGate:
+    """Shared-dissipation-factor gates of the joint format (DissipativeGate,
+    src/fhemamba/selective_gates.py:82-135, built by gate_from_spec,
+    src/fhemamba/payload_surrogate.py:79-92): per head h a Chebyshev domain
+    [lo_h, hi_h] and coefficient columns p[:, h], q[:, h]; for z = dt + dt_bias,
+    write (the step size) = p(z)^2 q(z)^2 and decay = 1 - p(z)^2.  They replace
+    the softplus and decay sites.  On ciphertexts the per-head coefficients
+    are plaintext slot vectors over one shared Chebyshev basis T_1..T_D of the
+    per-head affine map, zero outside the heads."""
+
+    lo: np.ndarray
+    hi: np.ndarray
+    p: np.ndarray  # (degree + 1, heads)
+    q: np.ndarray
+    rates: np.ndarray
+
+    def _series(self, coeffs, t):
+        b1 = np.zeros_like(t)
+        b2 = np.zeros_like(t)
+        for c in coeffs[:0:-1]:
+            b1, b2 = 2.0 * t * b1 - b2 + c, b1
+        return t * b1 - b2 + coeffs[0]
+
+    def __call__(self, z):
+        z = np.asarray(z, dtype=np.float64)
+        t = (2.0 * z - (self.lo + self.hi)) / (self.hi - self.lo)
+        p, q = self._series(self.p, t), self._series(self.q, t)
+        d = p * p
+        return d * q * q, 1.0 - d
+
+    @property
+    def degree(self) -> int:
+        return max(self.p.shape[0], self.q.shape[0]) - 1
+
+    @property
+    def levels(self) -> int:
+        # affine map, the basis, the coefficient products, p^2 and p^2 q^2
+        return 1 + max(0, math.ceil(math.log2(max(1, self.degree)))) + 1 + 2
+
+    def encrypted(self, pm, z, heads):
+        """(write, decay) ciphertexts at [0, heads) from z at [0, heads)."""
+        c, n = pm.cc, pm.L.slots
+        a = np.zeros(n)
+        b = np.zeros(n)
+        a[:heads] = 2.0 / (self.hi - self.lo)
+        b[:heads] = -(self.lo + self.hi) / (self.hi - self.lo)
+        t = pm._mul_mask(z, a)
+        if t.GetNoiseScaleDeg() >= 2:
+            c.RescaleInPlace(t)
+        t = c.EvalAdd(t, c.MakeCKKSPackedPlaintext(b, level=c.n_q - t.n_limbs(), scale=t.GetScalingFactor()))
+        basis = {1: t}
+
+        def T(i):  # T_2k = 2 T_k^2 - 1, T_2k+1 = 2 T_k+1 T_k - T_1
+            if i not in basis:
+                if i % 2 == 0:
+                    sq = c.EvalMult(T(i // 2), T(i // 2))
+                    basis[i] = c.EvalAdd(c.EvalAdd(sq, sq), -1.0)
+                else:
+                    pr = c.EvalMult(T(i // 2 + 1), T(i // 2))
+                    basis[i] = c.EvalSub(c.EvalAdd(pr, pr), T(1))
+            return basis[i]
+
+        def series(coeffs):
+            acc = None
+            for i in range(1, coeffs.shape[0]):
+                vec = np.zeros(n)
+                vec[:heads] = coeffs[i]
+                term = pm._mul_mask(T(i), vec)
+                acc = term if acc is None else c.EvalAdd(acc, term)
+            if acc is None:  # a constant: 0 * t carries it as a ciphertext
+                acc = pm._mul_mask(t, np.zeros(n))
+            if acc.GetNoiseScaleDeg() >= 2:
+                c.RescaleInPlace(acc)
+            const = np.zeros(n)
+            const[:heads] = coeffs[0]
+            return c.EvalAdd(acc, c.MakeCKKSPackedPlaintext(const, level=c.n_q - acc.n_limbs(),
+                                                             scale=acc.GetScalingFactor()))
+
+        p, q = series(self.p), series(self.q)
+        d = c.EvalMult(p, p)
+        if d.GetNoiseScaleDeg() >= 2:
+            c.RescaleInPlace(d)
+        write = c.EvalMult(d, c.EvalMult(q, q))
+        ones = np.zeros(n)
+        ones[:heads] = 1.0
+        decay = c.EvalAdd(c.EvalNegate(d), c.MakeCKKSPackedPlaintext(ones, level=c.n_q - d.n_limbs(),
+                                                                     scale=d.GetScalingFactor()))
+        return write, decay
+
+
+def parse_joint_gate(spec: dict, heads: int, a_log: np.ndarray) -> JointGate:
+    """parse_joint_gate (native/fideslib_stage0/src/stage1_mamba2_payload.cpp:206-231)
+    plus the rate check of PolyOps.mamba2_gates (src/fhemamba/ops.py:548-556)."""
+    if spec.get("kind") != "shared-dissipation-factor-v1" or \
+            spec.get("coefficient_layout") != "degree-major-head-minor":
+        raise PayloadError("unsupported joint gate recipe")
+    try:
+        arr = {k: np.asarray(spec[k], dtype=np.float64) for k in ("lo", "hi", "p", "q", "rates")}
+    except (KeyError, TypeError, ValueError) as e:
+        raise PayloadError("invalid joint gate numeric array") from e
+    if any(not np.all(np.isfinite(v)) or v.ndim != 1 for v in arr.values()):
+        raise PayloadError("invalid joint gate numeric array")
+    if arr["lo"].size != heads or arr["hi"].size != heads or arr["rates"].size != heads or \
+            np.any(arr["lo"] >= arr["hi"]) or arr["p"].size % heads or arr["q"].size % heads or \
+            not arr["p"].size or not arr["q"].size or np.any(arr["rates"] <= 0):
+        raise PayloadError("joint gate needs one domain, one positive rate and whole coefficient rows per head")
+    if not np.allclose(arr["rates"], np.exp(a_log), rtol=1e-6, atol=0):
+        raise PayloadError("joint gate checkpoint rates differ from the layer's A")
+    return JointGate(arr["lo"], arr["hi"], arr["p"].reshape(-1, heads), arr["q"].reshape(-1, heads), arr["rates"])
 
 
 def parse_poly_spec(spec: dict, site: str, heads: int | None = None):
@@ -434,6 +556,7 @@ class PayloadPolys:
     exp: object      # decay_exp
     rsqrt1: object   # rms_invsqrt (block norm)
     rsqrt2: object   # gated_rms_invsqrt
+    gates: object = None  # JointGate (joint format): replaces softplus and exp
 
 
 @dataclass
@@ -509,12 +632,13 @@ def read_layer_payload(dirpath, index: int = 0) -> LayerPayload:
     d = Path(dirpath)
     meta = _read_json(d / "meta.json")
     fmt = meta.get("format")
-    if fmt == "fhemamba-m1-joint-v1":
-        raise PayloadError("joint gate payloads (fhemamba-m1-joint-v1) are not supported")
-    if fmt != LAYER_FORMAT:
+    joint = fmt == JOINT_LAYER_FORMAT
+    if not joint and fmt != LAYER_FORMAT:
         raise PayloadError("unexpected payload format (want fhemamba-m1-v1)")
-    if "joint_gates" in meta:
+    if not joint and "joint_gates" in meta:
         raise PayloadError("joint gate payload requires the versioned joint format")
+    if joint and "joint_gates" not in meta:
+        raise PayloadError("meta.json key not found: joint_gates")
     try:
         dims = {k: int(meta["dims"][k]) for k in ("d_model", "d_inner", "num_heads", "head_dim", "state_size",
                                                    "n_groups", "conv_kernel", "conv_dim")}
@@ -570,8 +694,15 @@ def read_layer_payload(dirpath, index: int = 0) -> LayerPayload:
     W.arrays = {"norm_w": tensors["block_norm_w"], "w_in": tensors["in_proj_w"], "conv_w": tensors["conv_w"],
                 "conv_b": tensors["conv_b"], "dt_bias": tensors["dt_bias"], "a": -np.exp(tensors["a_log"]),
                 "d": tensors["d_skip"], "gn_w": tensors["gated_norm_w"], "w_out": tensors["out_proj_w"]}
+    gates = None
+    if joint:
+        gates = parse_joint_gate(meta["joint_gates"], H, tensors["a_log"])
+        mask = sites["decay_exp"].head_mask if isinstance(sites["decay_exp"], ResquaredExp) else None
+        if mask is not None and np.any(mask != 1.0):
+            raise PayloadError("joint gates retain all heads")
     P = PayloadPolys(silu_x=sites["conv_silu"], silu_z=sites["gate_silu"], softplus=sites["dt_softplus"],
-                     exp=sites["decay_exp"], rsqrt1=sites["rms_invsqrt"], rsqrt2=sites["gated_rms_invsqrt"])
+                     exp=sites["decay_exp"], rsqrt1=sites["rms_invsqrt"], rsqrt2=sites["gated_rms_invsqrt"],
+                     gates=gates)
     for name in ("silu_x", "silu_z", "softplus", "exp"):
         if isinstance(getattr(P, name), _InvSqrt):
             raise PayloadError(f"an inverse square root is not a valid {name} nonlinearity")
@@ -590,9 +721,7 @@ def read_chain_payload(dirpath, max_layers: int = 0, autoregressive: bool = True
     layer loading (stage1_mamba2_decode_fideslib.cpp:765-800) do."""
     d = Path(dirpath)
     meta = _read_json(d / "chain.json")
-    if meta.get("format") == "fhemamba-m2-chain-joint-v1":
-        raise PayloadError("joint gate payloads (fhemamba-m2-chain-joint-v1) are not supported")
-    if meta.get("format") != CHAIN_FORMAT:
+    if meta.get("format") not in (CHAIN_FORMAT, JOINT_CHAIN_FORMAT):
         raise PayloadError("unexpected chain payload format (want fhemamba-m2-chain-v1)")
     n_layers = int(meta["n_layers"])
     dirs = meta.get("layer_dirs") or []
@@ -709,7 +838,10 @@ def chain_bounds(payload: ChainPayload, sequences=None):
     """Refresh bounds per layer (and for the final norm, index len(layers)):
     2 x the largest magnitude each refreshed intermediate reaches in the
     polynomial circuit over `sequences` (default: the payload's own input
-    sequences) or in the layer's calibration-text carried bounds, at least 1."""
+    sequences) or in the layer's calibration-text carried bounds.  There is no
+    floor: a refresh's error is relative to its bound, and small values (the
+    gated variance, the first steps of a scheduled inverse square root) keep
+    their precision only under a bound of their own size."""
     if sequences is None:
         sequences = [payload.input_embeddings]
         if payload.ar_embeddings is not None:
@@ -725,7 +857,7 @@ def chain_bounds(payload: ChainPayload, sequences=None):
     for L, m in zip(payload.layers, mags):
         for k, v in _carried_keys(L.carried):
             m[k] = max(m.get(k, 0.0), v)
-    return [{k: max(1.0, 2.0 * v) for k, v in m.items()} for m in mags]
+    return [{k: max(1e-9, 2.0 * v) for k, v in m.items()} for m in mags]
 
 
 # ---------------------------------------------------------------------------

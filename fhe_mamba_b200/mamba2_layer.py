@@ -206,8 +206,11 @@ def plain_step(W: Mamba2Weights, P: Mamba2Polys, h, conv_state, ssm_state):
     xc = sum(W["conv_w"][:, k] * window[k] for k in range(W.conv_kernel)) + W["conv_b"]
     xa = P.silu_x(xc)
     x, B, C = xa[:E].reshape(H, Pd), xa[E:E + S], xa[E + S:]
-    dts = P.softplus(dt + W["dt_bias"])
-    decay = P.exp(W["a"] * dts)
+    if getattr(P, "gates", None) is not None:  # joint gates: (write, decay) from one factorisation
+        dts, decay = P.gates(dt + W["dt_bias"])
+    else:
+        dts = P.softplus(dt + W["dt_bias"])
+        decay = P.exp(W["a"] * dts)
     upd = (dts[:, None] * x)[:, :, None] * B[None, None, :]
     st = upd if ssm_state is None else decay[:, None, None] * ssm_state + upd
     y = (st * C[None, None, :]).sum(-1) + W["d"][:, None] * x
@@ -486,10 +489,18 @@ class EncryptedMamba2Layer:
         bias_dt[:H] = W["dt_bias"]
         dtv = c.EvalAdd(dtv, c.MakeCKKSPackedPlaintext(bias_dt, level=c.n_q - dtv.n_limbs(),
                                                         scale=dtv.GetScalingFactor()))
-        dtv = self._fit(dtv, self._need(P.softplus), bounds["dt"], "dt")
-        dts = self._poly(dtv, P.softplus, 0, H)
-        pack = c.EvalAdd(xa, c.EvalRotate(dts, -self.dt_base))
-        if ssm_state is not None:
+        gates = getattr(P, "gates", None)
+        if gates is not None:  # joint gates: write and decay from one shared factor
+            dtv = self._fit(dtv, gates.levels, bounds["dt"], "dt")
+            dts, decay = gates.encrypted(self.pm, dtv, H)
+            pack = c.EvalAdd(xa, c.EvalRotate(dts, -self.dt_base))
+            if ssm_state is not None:
+                pack = c.EvalAdd(pack, c.EvalRotate(decay, -self.decay_base))
+        else:
+            dtv = self._fit(dtv, self._need(P.softplus), bounds["dt"], "dt")
+            dts = self._poly(dtv, P.softplus, 0, H)
+            pack = c.EvalAdd(xa, c.EvalRotate(dts, -self.dt_base))
+        if gates is None and ssm_state is not None:
             # heads a payload prunes (head mask 0) get input 0, inside the
             # decay polynomial's domain; the polynomial's output mask zeroes them
             mask = getattr(P.exp, "head_mask", None)
@@ -536,15 +547,22 @@ def poly_step_record(W: Mamba2Weights, P: Mamba2Polys, h, conv, st, rec):
     xa = P.silu_x(xc)
     rec("xa", xa)
     rec("dt", dt + W["dt_bias"])
-    dts = P.softplus(dt + W["dt_bias"])
+    gates = getattr(P, "gates", None)
+    if gates is not None:
+        dts, decay = gates(dt + W["dt_bias"])
+    else:
+        dts = P.softplus(dt + W["dt_bias"])
+        decay = None
+        rec("adt", W["a"] * dts)
     rec("dts", dts)
-    rec("adt", W["a"] * dts)
     rec("pack", xa)
     rec("pack", dts)
     rec("pack", [1.0])
     x, B, C = xa[:E].reshape(H, Pd), xa[E:E + S], xa[E + S:]
     upd_ = (dts[:, None] * x)[:, :, None] * B[None, None, :]
-    st = upd_ if st is None else P.exp(W["a"] * dts)[:, None, None] * st + upd_
+    if st is not None:
+        decay = P.exp(W["a"] * dts) if decay is None else decay
+    st = upd_ if st is None else decay[:, None, None] * st + upd_
     rec("state", st)
     y = (st * C[None, None, :]).sum(-1) + W["d"][:, None] * x
     rec("y", y)

@@ -17,7 +17,9 @@ not available here, so the weights are synthetic and the tokenizer maps each
 byte of the text to ``byte mod 128``; the payload layout is the exporter's.
 Writes ``mamba2_chain/`` next to this script, and
 ``mamba2_nonlinearities.json``: every exported nonlinearity kind evaluated
-by the reference's own evaluators on a grid.
+by the reference's own evaluators on a grid, and ``mamba2_chain_joint/``: the
+same model in the joint format (scheduled normalizations, dedicated final
+norm, shared-dissipation-factor gates; see ``write_joint``).
 """
 import json
 import shutil
@@ -65,16 +67,63 @@ def main(reference: str) -> None:
     export_chain_payload(model, ByteTokenizer(cfg.vocab_size), OUT, n_test_tokens=3, cal_tokens=128,
                          bound_cal_tokens=128, autoregressive_prompt_tokens=2,
                          autoregressive_generate_tokens=2)
+    write_joint(model, cfg)
     write_nonlinearities()
+
+
+def write_joint(model, cfg) -> None:
+    """The same model exported in the joint format (``fhemamba-m2-chain-joint-v1``):
+    scheduled inverse square roots at every norm site, a dedicated final norm
+    (``plan_invsqrt`` on public variance intervals, as the reference's
+    scheduled-payload tests plan them) and shared-dissipation-factor gates on
+    the public gate domains with degree-2 dissipation and degree-1
+    equilibrium roots per head (certified: |p| <= 0.8)."""
+    from fhemamba.m1_payload import export_chain_payload
+    from fhemamba.normalization import plan_invsqrt
+    from fhemamba.payload_surrogate import public_gate_domains
+
+    work = HERE / "_joint_inputs"
+    if work.exists():
+        shutil.rmtree(work)
+    work.mkdir()
+    his = {(0, "rms_invsqrt"): 50, (0, "gated_rms_invsqrt"): 100, (1, "rms_invsqrt"): 50,
+           (1, "gated_rms_invsqrt"): 100, (2, "rms_invsqrt"): 200}
+    bundle = {"format": "fhemamba-normalization-schedules-v1",
+              "operators": [{"layer": layer, "site": site, "recipe": plan_invsqrt(1e-6, hi).recipe()}
+                            for (layer, site), hi in his.items()]}
+    (work / "schedules.json").write_text(json.dumps(bundle))
+    arrays = {}
+    heads = cfg.num_heads
+    for layer, block in enumerate(model.backbone.layers):
+        lo, hi = public_gate_domains(block)
+        shade = np.linspace(0.0, 1.0, heads)
+        arrays.update({f"layer_{layer}_lo": lo, f"layer_{layer}_hi": hi,
+                       f"layer_{layer}_p": np.stack([0.5 - 0.2 * shade, 0.2 + 0.05 * shade, np.full(heads, 0.1)]),
+                       f"layer_{layer}_q": np.stack([0.75 + 0.1 * shade, np.full(heads, -0.15)]),
+                       f"layer_{layer}_rates": block.mixer.A_log.detach().exp().double().numpy()})
+    arrays["manifest"] = np.array(json.dumps({"format": "dissipative-mamba2-gates-v1", "layers": [0, 1],
+                                              "input_payload_sha256": "0" * 64}))
+    np.savez(work / "gates.npz", **arrays)
+    out = HERE / "mamba2_chain_joint"
+    if out.exists():
+        shutil.rmtree(out)
+    try:
+        export_chain_payload(model, ByteTokenizer(cfg.vocab_size), out, n_test_tokens=3, cal_tokens=128,
+                             bound_cal_tokens=128, normalization_bundle=work / "schedules.json",
+                             stabilized_gate_bundle=work / "gates.npz")
+    finally:
+        shutil.rmtree(work)
 
 
 def write_nonlinearities() -> None:
     """Every exported nonlinearity kind evaluated by the reference's own
-    evaluators (``_poly_from_export_spec``) in float64 on a grid: the layer
-    specs of the payload above, plus a ``const-newton`` and a
+    evaluators (``_poly_from_export_spec``, ``gate_from_spec``) in float64 on a
+    grid: the layer specs of both payloads (the joint payload's scheduled
+    inverse square roots and its gates), plus a ``const-newton`` and a
     ``scaled-goldschmidt-invsqrt-v1`` spec (coupled Newton coefficient pairs)
-    that the default exporter does not emit."""
+    that the exporters do not emit."""
     from fhemamba.m1_payload import _poly_from_export_spec
+    from fhemamba.payload_surrogate import gate_from_spec
 
     metas = [json.loads((OUT / f"layer_{i:02d}" / "meta.json").read_text()) for i in (0, 1)]
     cases = []
@@ -94,6 +143,18 @@ def write_nonlinearities() -> None:
             else:
                 x = np.linspace(spec["lo"], spec["hi"], 9)
             add(f"layer{li}.{site}", spec, x)
+    joint = HERE / "mamba2_chain_joint"
+    for li in (0, 1):
+        meta = json.loads((joint / f"layer_{li:02d}" / "meta.json").read_text())
+        for site in ("rms_invsqrt", "gated_rms_invsqrt"):
+            spec = meta["polys"][site]
+            add(f"joint{li}.{site}", spec, np.geomspace(spec["lo"] * 10, spec["hi"] / 10, 9))
+        gate, _ = gate_from_spec(meta["joint_gates"])
+        lo, hi = np.asarray(meta["joint_gates"]["lo"]), np.asarray(meta["joint_gates"]["hi"])
+        z = lo[None, :] + np.linspace(0.0, 1.0, 7)[:, None] * (hi - lo)[None, :]
+        write, decay = gate(torch.tensor(z, dtype=torch.float64))
+        cases.append({"name": f"joint{li}.gates", "spec": meta["joint_gates"], "x": z.tolist(),
+                      "y": [write.numpy().tolist(), decay.numpy().tolist()]})
     add("const-newton", {"kind": "const-newton", "guess": 2.0, "iterations": 7}, np.geomspace(0.02, 0.2, 9))
     add("scheduled", {"kind": "scaled-goldschmidt-invsqrt-v1", "lo": 0.05, "hi": 1.0, "seed": 1.0,
                       "coefficients": [[1.5, 0.5]] * 6, "tolerance": 1e-7, "final_recomputed_newton": True,

@@ -151,6 +151,9 @@ class SlotContext:
             return self.EvalAdd(a, neg)
         return self.EvalAdd(a, -float(b))
 
+    def EvalNegate(self, a):
+        return SimCiphertext(-a.values, a.left, a.deg)
+
     def EvalMult(self, a, b):
         if isinstance(b, SimCiphertext):
             return SimCiphertext(a.values * b.values, min(a.left, b.left) - 1, 2)

@@ -15,6 +15,7 @@ from fhe_mamba_b200.chain_payload import read_chain_payload, run_chain
 from slot_sim import SimError, SlotContext
 
 CHAIN = os.path.join(GOLDEN, "mamba2_chain")
+JOINT = os.path.join(GOLDEN, "mamba2_chain_joint")
 
 
 @pytest.fixture(scope="module")
@@ -123,3 +124,24 @@ def test_every_refresh_two_pass_by_default(payload):
     cc = _CountingContext(2048, refresh_noise=0.0)
     r = run_chain(cc, payload, 2, 1e-4)
     assert set(cc.passes_seen) == {2} and r["measurements"]["meta_bts_applied"] == r["measurements"]["refreshes"]
+
+
+def test_joint_payload_schedule():
+    """Joint gates (a per-head coefficient basis), degree-768/384 SiLU fits and
+    scheduled inverse square roots (12-13 coupled steps, per-step refresh
+    bounds) through the same layer."""
+    p = read_chain_payload(JOINT)
+    cc = SlotContext(2048, refresh_noise=0.0)
+    r = run_chain(cc, p, 3, 1e-4)
+    assert r["passed"] and r["measurements"]["max_abs_error"] < 1e-5 and cc.max_refresh_ratio <= 1.0
+    r = run_chain(SlotContext(2048, refresh_noise=1e-6), p, 3, 1e-3)
+    assert r["passed"], r["measurements"]["max_abs_error"]
+
+
+def test_joint_payload_reference_policy():
+    """Scheduled-normalization layers make every transient refresh two-pass
+    under the reference's policy, even with Meta-BTS off."""
+    p = read_chain_payload(JOINT)
+    cc = _CountingContext(2048, refresh_noise=0.0)
+    r = run_chain(cc, p, 2, 1e-4, meta_bts=False)
+    assert r["passed"] and r["measurements"]["meta_bts_applied"] == cc.passes_seen.count(2) > 0

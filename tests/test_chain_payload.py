@@ -16,12 +16,14 @@ import numpy as np
 import pytest
 
 from conftest import GOLDEN
-from fhe_mamba_b200.chain_payload import (ChebSeries, ConstNewton, PayloadError, PolyNewton, ResquaredExp,
-                                          ScheduledInvSqrt, SquaredPolyNewton, SquaredSeries, chain_bounds,
-                                          chebyshev_levels, initial_state, parse_poly_spec, plain_decode,
-                                          plain_token, read_chain_payload, select_token)
+from fhe_mamba_b200.chain_payload import (ChebSeries, ConstNewton, JointGate, PayloadError, PolyNewton,
+                                          ResquaredExp, ScheduledInvSqrt, SquaredPolyNewton, SquaredSeries,
+                                          chain_bounds, chebyshev_levels, initial_state, parse_joint_gate,
+                                          parse_poly_spec, plain_decode, plain_token, read_chain_payload,
+                                          select_token)
 
 CHAIN = os.path.join(GOLDEN, "mamba2_chain")
+JOINT = os.path.join(GOLDEN, "mamba2_chain_joint")
 FP32 = 2e-5  # float32 evaluation of the exporter vs float64 here
 
 
@@ -60,13 +62,17 @@ def test_nonlinearities_match_reference_evaluators():
     kinds = set()
     for case in cases:
         site = case["name"].split(".")[-1] if "." in case["name"] else "rms_invsqrt"
-        spec = parse_poly_spec(case["spec"], site)
         x, want = np.array(case["x"]), np.array(case["y"])
-        got = spec.inv_sqrt(x) if hasattr(spec, "inv_sqrt") else spec(x)
+        if site == "gates":
+            rates = np.asarray(case["spec"]["rates"])
+            got = np.array(parse_joint_gate(case["spec"], rates.size, np.log(rates))(x))
+        else:
+            spec = parse_poly_spec(case["spec"], site)
+            got = spec.inv_sqrt(x) if hasattr(spec, "inv_sqrt") else spec(x)
         assert np.allclose(got, want, rtol=1e-12, atol=1e-12 * np.max(np.abs(want))), case["name"]
         kinds.add(case["spec"]["kind"])
     assert kinds == {"cheb", "cheb-squared", "cheb-resquared", "poly-newton", "sq-poly-newton", "const-newton",
-                     "scaled-goldschmidt-invsqrt-v1"}
+                     "scaled-goldschmidt-invsqrt-v1", "shared-dissipation-factor-v1"}
 
 
 def test_chain_poly_final(payload):
@@ -117,7 +123,9 @@ def test_refresh_bounds(payload):
     for m in b[:2]:
         for k in ("h", "u", "proj", "xbc", "xc", "dt", "adt", "pack", "state", "y", "z", "g", "gn",
                   "n1_v", "n1_y", "n2_v", "n2_y"):
-            assert m[k] >= 1.0, k
+            assert m[k] > 0, k
+    # no floor: the gated variance (~0.004-0.04) keeps a bound of its own size
+    assert b[0]["n2_v"] < 0.5
     assert {"h", "nf_v", "nf_y"} <= set(b[2])
     # the calibration-text bounds the exporter carries only widen the circuit's own
     carried = payload.layers[0].carried["checkpoint_abs_max"]
@@ -170,7 +178,7 @@ def _edit(path, fn):
 
 @pytest.mark.parametrize("case,message", [
     ("chain_format", "unexpected chain payload format"),
-    ("joint", "joint gate payloads"),
+    ("joint_without_format", "requires the versioned joint format"),
     ("layer_format", "unexpected payload format"),
     ("groups", "only n_groups == 1"),
     ("kind", "unsupported exported polynomial kind"),
@@ -190,7 +198,7 @@ def test_payload_errors(tmp_path, case, message):
              "oracle_workspace_dtype": "float64"}
     edits = {
         "chain_format": (chain, lambda m: m.update(format="fhemamba-m2-chain-v0")),
-        "joint": (chain, lambda m: m.update(format="fhemamba-m2-chain-joint-v1")),
+        "joint_without_format": (layer, lambda m: m.update(joint_gates={})),
         "layer_format": (layer, lambda m: m.update(format="fhemamba-m1-v0")),
         "groups": (layer, lambda m: m["dims"].update(n_groups=2)),
         "kind": (layer, lambda m: m["polys"]["conv_silu"].update(kind="taylor")),
@@ -216,7 +224,7 @@ def test_scheduled_final_norm(tmp_path):
              "oracle_workspace_dtype": "float64"}
     _edit(d / "chain.json", lambda m: m.update(final_norm_poly=sched))
     p = read_chain_payload(d)
-    assert isinstance(p.final_norm, ScheduledInvSqrt) and p.final_norm.fill == pytest.approx(2.025)
+    assert isinstance(p.final_norm, ScheduledInvSqrt) and p.final_norm.fill == pytest.approx(math.sqrt(0.2))
     v = np.geomspace(0.5, 4.0, 7)
     assert np.allclose(p.final_norm.inv_sqrt(v), 1 / np.sqrt(v), rtol=1e-6)
     _edit(d / "chain.json", lambda m: m.update(final_norm_poly={"kind": "poly-newton", "coeffs": [1.0],
@@ -254,3 +262,53 @@ def test_cli_reports_errors_without_a_gpu(tmp_path):
     # 128-classic over a ring too small for the chain is refused by the audit
     rc = mamba2_decode.main(["--input-chain", CHAIN, "--output-json", str(out), "--ring-dim", "4096"])
     assert rc == 2 and "classical-128" in json.loads(out.read_text())["error"]
+
+
+def test_joint_payload():
+    """The joint format (fhemamba-m2-chain-joint-v1): scheduled inverse square
+    roots at every norm site and a dedicated final norm, public-envelope SiLU
+    fits (degrees 768 / 384) and shared-dissipation-factor gates in place of
+    the softplus and decay sites; the fp64 circuit against the exporter's
+    polynomial references."""
+    p = read_chain_payload(JOINT)
+    assert isinstance(p.final_norm, ScheduledInvSqrt)
+    for L in p.layers:
+        P = L.polys
+        assert isinstance(P.gates, JointGate) and P.gates.degree == 2 and P.gates.p.shape == (3, 16)
+        assert isinstance(P.rsqrt1, ScheduledInvSqrt) and isinstance(P.rsqrt2, ScheduledInvSqrt)
+        assert P.silu_x.degree == 768 and P.silu_z.degree == 384
+    out = plain_decode(p, p.input_embeddings)
+    assert np.max(np.abs(out - p.expected_poly_final)) < FP32 * np.max(np.abs(p.expected_poly_final))
+    from fhe_mamba_b200.mamba2_layer import plain_step
+    st = initial_state(p)
+    for t in range(p.n_test_tokens):
+        h = p.input_embeddings[t]
+        for i, L in enumerate(p.layers):
+            conv, s = st[i]
+            h, conv, s = plain_step(L.weights, L.polys, h, conv, s)
+            st[i] = (conv, s)
+            assert np.max(np.abs(h - L.tensors["test_layer_output_poly"][t])) < FP32 * 10, (t, i)
+            assert np.max(np.abs(s - L.tensors["test_state_output_poly"][t])) < FP32, (t, i)
+
+
+@pytest.mark.parametrize("case,message", [
+    ("recipe", "unsupported joint gate recipe"),
+    ("rates", "rates differ"),
+    ("rows", "whole coefficient rows per head"),
+    ("pruned", "joint gates retain all heads"),
+    ("missing", "key not found: joint_gates"),
+])
+def test_joint_payload_errors(tmp_path, case, message):
+    d = tmp_path / "joint"
+    shutil.copytree(JOINT, d)
+    layer = d / "layer_00" / "meta.json"
+    edits = {
+        "recipe": lambda m: m["joint_gates"].update(coefficient_layout="head-major-degree-minor"),
+        "rates": lambda m: m["joint_gates"].update(rates=[2.0 * r for r in m["joint_gates"]["rates"]]),
+        "rows": lambda m: m["joint_gates"].update(p=m["joint_gates"]["p"][:-1]),
+        "pruned": lambda m: m["polys"]["decay_exp"].update(head_mask=[0.0] + [1.0] * 15),
+        "missing": lambda m: m.pop("joint_gates"),
+    }
+    _edit(layer, edits[case])
+    with pytest.raises(PayloadError, match=message):
+        read_chain_payload(d)

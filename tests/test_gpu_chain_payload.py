@@ -69,3 +69,23 @@ def test_reference_refresh_policy():
     print("meta-bts policy", m["max_abs_error"], m["refreshes"], m["meta_bts_applied"])
     assert r["passed"], m
     assert 0 < m["meta_bts_applied"] < m["refreshes"]
+
+
+def test_joint_payload_decode():
+    """The joint format (tests/golden/mamba2_chain_joint): shared-dissipation
+    gates on a per-head coefficient basis, degree-768/384 SiLU fits, scheduled
+    inverse square roots with a dedicated final norm.  Measured on a B200:
+    5.5e-6 (the references' float32 floor), 81 refreshes over 3 tokens."""
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    from fhe_mamba_b200.chain_payload import read_chain_payload, run_chain
+    p = read_chain_payload(os.path.join(GOLDEN, "mamba2_chain_joint"))
+    cc = CryptoContext(CCParams(ring_dim=1 << 12, multiplicative_depth=44, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3))
+    cc.KeyGen(71)
+    cc.EvalBootstrapSetup((4, 4))
+    cc.EvalBootstrapKeyGen()
+    r = run_chain(cc, p, 3, TOL)
+    m = r["measurements"]
+    print("joint decode", m["per_token_max_abs_error"], "refreshes", m["refreshes"], "s/token",
+          m["seconds_per_token"])
+    assert r["passed"], m
