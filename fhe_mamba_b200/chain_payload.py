@@ -196,10 +196,14 @@ class _InvSqrt:
         return y
 
     def _encrypted_newton(self, c, v, y, fit):
+        """Newton steps on ciphertexts.  Each step starts with four levels on
+        y and -v/2: a refresh before a step costs no precision (the step
+        squares the relative error), one after the last step would, so the
+        last step leaves the two levels the final x y w products need."""
         vh = c.EvalMult(v, -0.5)
         for _ in range(self.iterations):
-            y = fit(y, 2, "y")
-            vh = fit(vh, 2, "v")
+            y = fit(y, 4, "y")
+            vh = fit(vh, 4, "v")
             y = _newton_step(c, y, vh)
         return y
 
@@ -312,7 +316,10 @@ class ScheduledInvSqrt(_InvSqrt):
         # themselves, so that it does not set the refresh bound of v
         return math.sqrt(self.lo * self.hi)
 
-    levels = 2
+    # v keeps enough levels for u = v s^2 and the final Newton step's -v/2,
+    # so that neither is refreshed (v spans the whole public interval, whose
+    # bound would swamp the variances themselves)
+    levels = 8
 
     def inv_sqrt(self, v, trace=None):
         v = np.asarray(v, dtype=np.float64)
@@ -834,19 +841,96 @@ def _carried_keys(carried: dict):
     return [(k, float(v)) for k, v in pairs if v is not None]
 
 
-def chain_bounds(payload: ChainPayload, sequences=None):
-    """Refresh bounds per layer (and for the final norm, index len(layers)):
-    2 x the largest magnitude each refreshed intermediate reaches in the
-    polynomial circuit over `sequences` (default: the payload's own input
-    sequences) or in the layer's calibration-text carried bounds.  There is no
-    floor: a refresh's error is relative to its bound, and small values (the
-    gated variance, the first steps of a scheduled inverse square root) keep
-    their precision only under a bound of their own size."""
+# Fallback magnitudes for refresh sites the payload gives no number for (the
+# reference decode's checkpoint_bound table,
+# native/fideslib_stage0/src/stage1_mamba2_decode_fideslib.cpp:174-214).
+FALLBACK_BOUNDS = {"h": 8.0, "proj": 6.0, "xbc": 6.0, "y": 24.0, "state": 24.0}
+
+
+def calibration_sequences(payload: ChainPayload, count: int = 8, length: int = 4, seed: int = 0):
+    """Seeded random token sequences embedded with the payload's client
+    embedding table (present with the client-loop assets), or none."""
+    if payload.client_embedding_w is None:
+        return []
+    r = np.random.default_rng(seed)
+    vocab = payload.client_embedding_w.shape[0]
+    return [payload.client_embedding_w[r.integers(0, vocab, length)] for _ in range(count)]
+
+
+def _inv_sqrt_domain(spec):
+    if isinstance(spec, ScheduledInvSqrt):
+        lo, hi = spec.lo, spec.hi
+    elif isinstance(spec, ConstNewton):
+        lo, hi = 0.01 * spec.fill, spec.fill
+    else:
+        lo, hi = spec.base.lo, spec.base.hi
+    return (lo if lo > 0 else 1e-4 * hi), hi
+
+
+def domain_bounds(L: LayerPayload | None, norms) -> dict:
+    """Magnitudes that follow from the exported domains alone: activation
+    inputs within their fitted intervals, activation outputs over them, every
+    inverse-square-root iterate over its variance interval (and the fill),
+    normalised vectors at most sqrt(width) x max |weight|."""
+    out = {}
+
+    def put(k, v):
+        out[k] = max(out.get(k, 0.0), float(np.max(np.abs(v))))
+
+    if L is not None:
+        P, W = L.polys, L.weights
+        put("xc", [P.silu_x.lo, P.silu_x.hi])
+        put("z", [P.silu_z.lo, P.silu_z.hi])
+        xa = P.silu_x(np.linspace(P.silu_x.lo, P.silu_x.hi, 513))
+        put("xa", xa)
+        put("pack", xa)
+        out["silu_z_max"] = float(np.max(np.abs(P.silu_z(np.linspace(P.silu_z.lo, P.silu_z.hi, 513)))))
+        if P.gates is not None:
+            g = P.gates
+            put("dt", [g.lo, g.hi])
+            write, decay = g(g.lo[None, :] + np.linspace(0.0, 1.0, 257)[:, None] * (g.hi - g.lo)[None, :])
+            put("dts", write)
+            put("pack", write)
+            put("pack", decay)
+        else:
+            b = P.softplus.base
+            put("dt", [b.lo, b.hi])
+            dts = P.softplus(np.linspace(b.lo, b.hi, 513))
+            put("dts", dts)
+            put("pack", dts)
+            put("adt", [P.exp.lo])
+            put("pack", 1.0)
+        put("u", math.sqrt(W.d_model) * np.max(np.abs(W["norm_w"])))
+        put("gn", math.sqrt(W.d_inner) * np.max(np.abs(W["gn_w"])))
+    for prefix, spec in norms:
+        lo, hi = _inv_sqrt_domain(spec)
+        v = np.concatenate([np.geomspace(lo, hi, 257), [spec.fill]])
+        put(prefix + "_v", v)
+        spec.inv_sqrt(v, trace=lambda name, val, pre=prefix: put(pre + "_" + name, val))
+    return out
+
+
+def chain_bounds(payload: ChainPayload, sequences=None, margin: float = 2.0):
+    """Refresh bounds per layer (and for the final norm, index len(layers)),
+    as the reference decode derives them: never from the inputs it is tested
+    on.  Per refreshed intermediate, `margin` x the largest of
+
+    * its magnitude in the fp64 circuit over calibration `sequences` (default:
+      seeded random token sequences from the client embedding table, when the
+      payload has one) and in the layer's calibration-text carried bounds;
+    * for activation inputs and outputs, their extent over the exported
+      polynomial domains;
+
+    and, for a site none of these reaches, its domain-derived magnitude
+    (inverse-square-root iterates, normalised vectors, the gated value from
+    the carried gated-variance range) or the reference's fallback constant.  There is no floor: a refresh's error is relative to
+    its bound, and small values (the gated variance, the first steps of a
+    scheduled inverse square root) keep their precision only under a bound of
+    their own size."""
     if sequences is None:
-        sequences = [payload.input_embeddings]
-        if payload.ar_embeddings is not None:
-            sequences.append(payload.ar_embeddings)
-    mags = [dict() for _ in range(len(payload.layers) + 1)]
+        sequences = calibration_sequences(payload)
+    n = len(payload.layers)
+    mags = [dict() for _ in range(n + 1)]
 
     def rec(i, k, v):
         m = mags[i]
@@ -857,7 +941,28 @@ def chain_bounds(payload: ChainPayload, sequences=None):
     for L, m in zip(payload.layers, mags):
         for k, v in _carried_keys(L.carried):
             m[k] = max(m.get(k, 0.0), v)
-    return [{k: max(1e-9, 2.0 * v) for k, v in m.items()} for m in mags]
+        dom = domain_bounds(L, [("n1", L.polys.rsqrt1), ("n2", L.polys.rsqrt2)])
+        for k in ("xc", "z", "dt", "adt", "xa", "dts", "pack"):
+            if k in dom:
+                m[k] = max(m.get(k, 0.0), dom[k])
+        for k, v in dom.items():
+            if k != "silu_z_max":
+                m.setdefault(k, v)
+        for k, v in FALLBACK_BOUNDS.items():
+            m.setdefault(k, v)
+        gv = L.carried.get("gated_variance_range")
+        if "g" not in m and gv:  # mean(g^2) <= var_hi gives |g_i| <= sqrt(width var_hi)
+            m["g"] = math.sqrt(L.weights.d_inner * float(gv[1]))
+        m.setdefault("g", m["y"] * dom["silu_z_max"])
+    if payload.full_chain:
+        final = mags[n]
+        last = payload.layers[-1].carried.get("checkpoint_abs_max", {}) or {}
+        if last.get("output") is not None:
+            final["h"] = max(final.get("h", 0.0), float(last["output"]))
+        for k, v in domain_bounds(None, [("nf", payload.final_norm)]).items():
+            final.setdefault(k, v)
+        final.setdefault("h", FALLBACK_BOUNDS["h"])
+    return [{k: max(1e-9, margin * v) for k, v in m.items()} for m in mags]
 
 
 # ---------------------------------------------------------------------------

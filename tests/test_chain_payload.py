@@ -118,6 +118,12 @@ def test_max_layers_cuts_the_chain():
 
 
 def test_refresh_bounds(payload):
+    """Bounds never come from the test inputs: calibration sequences from the
+    embedding table, carried calibration-text bounds, exported domains."""
+    from fhe_mamba_b200.chain_payload import FALLBACK_BOUNDS, calibration_sequences
+    seqs = calibration_sequences(payload)
+    assert len(seqs) == 8 and not any(np.allclose(s[0], e) for s in seqs for e in payload.input_embeddings[:1])
+    assert chain_bounds(payload) == chain_bounds(payload, seqs)
     b = chain_bounds(payload)
     assert len(b) == 3
     for m in b[:2]:
@@ -126,6 +132,17 @@ def test_refresh_bounds(payload):
             assert m[k] > 0, k
     # no floor: the gated variance (~0.004-0.04) keeps a bound of its own size
     assert b[0]["n2_v"] < 0.5
+    # exported domains widen the activation inputs' bounds
+    assert b[0]["xc"] >= 2 * max(abs(payload.layers[0].polys.silu_x.lo), payload.layers[0].polys.silu_x.hi)
+    # without calibration data: domains, carried bounds and the fallback table
+    d = chain_bounds(payload, sequences=[])
+    assert d[0]["u"] == pytest.approx(2 * 8 * np.max(np.abs(payload.layers[0].weights["norm_w"])))
+    assert d[0]["proj"] == pytest.approx(2 * payload.layers[0].carried["checkpoint_abs_max"]["proj"])
+    joint = read_chain_payload(JOINT)
+    dj = chain_bounds(joint)
+    assert joint.client_embedding_w is None and dj[0]["g"] == pytest.approx(
+        2 * np.sqrt(128 * joint.layers[0].carried["gated_variance_range"][1]))
+    assert FALLBACK_BOUNDS["state"] == 24.0
     assert {"h", "nf_v", "nf_y"} <= set(b[2])
     # the calibration-text bounds the exporter carries only widen the circuit's own
     carried = payload.layers[0].carried["checkpoint_abs_max"]

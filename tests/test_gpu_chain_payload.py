@@ -54,8 +54,8 @@ def test_cli_client_loop(tmp_path):
 def test_reference_refresh_policy():
     """The reference decode's own refresh policy (--meta-bts 1: two-pass only
     for carried values and the gated norm's input, single bootstraps
-    elsewhere).  Measured on a B200: 2.4e-4 (3.2e-4 with Meta-BTS off) against
-    2.5e-6 when every refresh is two-pass; the bound keeps an 8x margin."""
+    elsewhere).  Measured on a B200: 2.8e-4 (8.4e-4 with Meta-BTS off) against
+    2.6e-6 when every refresh is two-pass; the bound keeps a 7x margin."""
     from fhe_mamba_b200 import CCParams, CryptoContext
     from fhe_mamba_b200.chain_payload import read_chain_payload, run_chain
     p = read_chain_payload(CHAIN)
@@ -75,7 +75,7 @@ def test_joint_payload_decode():
     """The joint format (tests/golden/mamba2_chain_joint): shared-dissipation
     gates on a per-head coefficient basis, degree-768/384 SiLU fits, scheduled
     inverse square roots with a dedicated final norm.  Measured on a B200:
-    5.5e-6 (the references' float32 floor), 81 refreshes over 3 tokens."""
+    5.6e-6 (the references' float32 floor), 75 refreshes over 3 tokens."""
     from fhe_mamba_b200 import CCParams, CryptoContext
     from fhe_mamba_b200.chain_payload import read_chain_payload, run_chain
     p = read_chain_payload(os.path.join(GOLDEN, "mamba2_chain_joint"))
