@@ -1038,11 +1038,19 @@ class EncryptedChain:
     def two_pass_refreshes(self) -> int:
         return sum(layer.two_pass_refreshes for layer in self.layers)
 
-    def step(self, embedding):
-        """Server pass for one token: the encrypted final hidden vector (the
-        last loaded layer's output when the chain is cut by max_layers)."""
+    def encrypt(self, embedding):
+        """Client: the token's embedding at slots [0, d_model)."""
         c, D = self.cc, self.p.d_model
-        h = c.Encrypt(c.MakeCKKSPackedPlaintext(np.pad(np.asarray(embedding, dtype=np.float64), (0, c.slots - D))))
+        return c.Encrypt(c.MakeCKKSPackedPlaintext(np.pad(np.asarray(embedding, dtype=np.float64), (0, c.slots - D))))
+
+    def step(self, embedding):
+        """One token from its embedding (client encryption + server pass)."""
+        return self.step_ct(self.encrypt(embedding))
+
+    def step_ct(self, h):
+        """Server pass for one encrypted token: the encrypted final hidden
+        vector (the last loaded layer's output when max_layers cuts the chain)."""
+        c, D = self.cc, self.p.d_model
         new = []
         for layer, (conv, st), bounds in zip(self.layers, self.state, self.bounds):
             h, conv, st = layer.step(h, conv, st, bounds)

@@ -12,6 +12,7 @@ stage1_mamba2_config.hpp:20-211):
         [--autoregressive-client-loop 0|1] [--tolerance 5e-2] [--refresh-passes 2]
         [--meta-bts 0|1] [--meta-bts-alpha 12] [--meta-bts-residual-layers 20,21]
         [--pt-cache-gib 5] [--seed 0]
+        [--process-role inline|client-init|server-eval|client-decrypt --handoff-dir DIR]
 
 Refreshes: by default every refresh is two-pass (the residual of the first
 bootstrap, amplified by 2^12, bootstrapped again: the reference's Meta-BTS)
@@ -19,6 +20,13 @@ or one bootstrap with --refresh-passes 1; --meta-bts 0|1 selects the
 reference decode's own policy instead (Meta-BTS only for carried values, the
 gated norm's polynomial input, the residual at --meta-bts-residual-layers,
 and the transient values of scheduled-normalization layers).
+
+Process separation (--process-role, the reference's handoff protocol):
+client-init keeps the secret key in DIR/client, writes the evaluation keys to
+DIR/server and the encrypted test inputs to DIR/exchange; server-eval loads
+only DIR/server, evaluates and writes DIR/exchange/output_t*.ct; client-decrypt
+decrypts them and checks them against the payload's reference.  Each role is
+its own process with the same parameter flags.
 
 The result document goes to --output-json; the exit code is 0 when the
 decrypted outputs are within --tolerance of the payload's polynomial-circuit
@@ -39,6 +47,9 @@ from __future__ import annotations
 import argparse
 import json
 import sys
+from pathlib import Path
+
+import numpy as np
 
 
 def _bool(v: str) -> bool:
@@ -73,10 +84,36 @@ def parse_args(argv=None):
     ap.add_argument("--meta-bts-residual-layers", default="")
     ap.add_argument("--pt-cache-gib", type=float, default=5.0)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--process-role", choices=ROLES, default="inline")
+    ap.add_argument("--handoff-dir", default="")
     return ap.parse_args(argv)
 
 
-def run(args) -> dict:
+ROLES = ("inline", "client-init", "server-eval", "client-decrypt")
+
+
+def handoff_paths(root):
+    """client/ (the secret), server/ (evaluation keys only), exchange/
+    (ciphertexts), as the reference's handoff_paths
+    (native/fideslib_stage0/src/stage1_mamba2_process.cpp:28-35)."""
+    root = Path(root)
+    return {"root": root, "client": root / "client", "server": root / "server", "exchange": root / "exchange"}
+
+
+def server_secret_files(paths) -> int:
+    """Files under server/ that could hold a secret (the server must have none)."""
+    if not paths["server"].is_dir():
+        return 0
+    return sum(1 for f in paths["server"].iterdir() if "secret" in f.name or f.name == CLIENT_KEYS)
+
+
+CLIENT_KEYS = "client.keys"   # public, evaluation and secret key (client/)
+SERVER_KEYS = "eval.keys"     # public and evaluation keys (server/)
+
+
+def run(args, context_factory=None) -> dict:
+    """One invocation; `context_factory` makes the CryptoContext (default: the
+    device library with the command line's parameters)."""
     from .chain_payload import PayloadError, read_chain_payload, run_chain
     from .ckks import CCParams, CryptoContext
     from .program import security_audit
@@ -109,26 +146,133 @@ def run(args) -> dict:
     elif args.num_large_digits == 0:
         args.num_large_digits = 3
     payload = read_chain_payload(args.input_chain, args.max_layers, args.autoregressive_client_loop)
-    cc = CryptoContext(CCParams(ring_dim=args.ring_dim, multiplicative_depth=args.multiplicative_depth,
-                                scaling_mod_size=args.scaling_mod_size, first_mod_size=args.first_mod_size,
-                                num_large_digits=args.num_large_digits))
-    cc.KeyGen(args.seed)
-    cc.EvalBootstrapSetup((args.bootstrap_level_budget_cts, args.bootstrap_level_budget_stc),
-                          sparse_hamming_weight=32 if args.secret_key_dist == "sparse-encapsulated" else 0)
-    cc.EvalBootstrapKeyGen()
-    result = run_chain(cc, payload, args.tokens, args.tolerance, args.autoregressive_client_loop,
-                       passes=args.refresh_passes, cache_gb=args.pt_cache_gib, meta_bts=args.meta_bts,
-                       meta_bts_residual_layers=residual_layers)
+    if args.process_role != "inline":
+        if not args.handoff_dir:
+            raise PayloadError(f"--process-role {args.process_role} needs --handoff-dir")
+        if args.autoregressive_client_loop:
+            raise PayloadError("the autoregressive client loop runs inline only")
+        if args.secret_key_dist == "sparse-encapsulated":
+            raise PayloadError("sparse-secret bootstrapping keys are not serialized; use uniform-ternary")
+        if args.tokens < 1 or args.tokens > payload.n_test_tokens:
+            raise PayloadError("--tokens exceeds n_test_tokens in the chain payload")
+    factory = context_factory or (lambda: CryptoContext(CCParams(
+        ring_dim=args.ring_dim, multiplicative_depth=args.multiplicative_depth,
+        scaling_mod_size=args.scaling_mod_size, first_mod_size=args.first_mod_size,
+        num_large_digits=args.num_large_digits)))
+    budget = (args.bootstrap_level_budget_cts, args.bootstrap_level_budget_stc)
+    chain_options = dict(passes=args.refresh_passes, cache_gb=args.pt_cache_gib, meta_bts=args.meta_bts,
+                         meta_bts_residual_layers=residual_layers)
+    if args.process_role == "inline":
+        cc = factory()
+        cc.KeyGen(args.seed)
+        cc.EvalBootstrapSetup(budget, sparse_hamming_weight=32 if args.secret_key_dist == "sparse-encapsulated"
+                              else 0)
+        cc.EvalBootstrapKeyGen()
+        result = run_chain(cc, payload, args.tokens, args.tolerance, args.autoregressive_client_loop,
+                           **chain_options)
+    else:
+        result = run_role(args, payload, factory, budget, chain_options)
     result["parameters"].update({"multiplicative_depth": args.multiplicative_depth,
                                  "scaling_mod_size": args.scaling_mod_size, "first_mod_size": args.first_mod_size,
                                  "num_large_digits": args.num_large_digits, "security": args.security,
                                  "secret_key_dist": args.secret_key_dist,
                                  "bootstrap_level_budget": [args.bootstrap_level_budget_cts,
                                                             args.bootstrap_level_budget_stc],
-                                 "max_layers": args.max_layers, "input_chain": str(args.input_chain)})
+                                 "max_layers": args.max_layers, "input_chain": str(args.input_chain),
+                                 "process_role": args.process_role})
     if audit is not None:
         result["security_audit"] = audit
     return result
+
+
+def run_role(args, payload, factory, budget, chain_options) -> dict:
+    """The process-separated protocol of the reference's decode
+    (stage1_mamba2_decode_fideslib.cpp:879-977, 1248-1275, 1446-1520,
+    4646-4700): client-init makes the keys, keeps the secret in client/,
+    puts the evaluation keys in server/ and the encrypted test inputs in
+    exchange/; server-eval loads only server/ (it cannot decrypt or make
+    keys), runs the layers and writes the encrypted outputs; client-decrypt
+    loads client/ and checks the outputs against the payload's reference."""
+    import os
+    import time
+
+    from .chain_payload import EncryptedChain, PayloadError
+
+    paths = handoff_paths(args.handoff_dir)
+    ex = paths["exchange"]
+    role = args.process_role
+    params = {"process_role": role, "tokens": args.tokens, "layers": len(payload.layers)}
+    scope = {"client_server_process_separation": True, "server_secret_key_loaded": False}
+    if role == "client-init":
+        root = paths["root"]
+        if root.exists() and (not root.is_dir() or any(root.iterdir())):
+            raise PayloadError(f"refusing to reuse non-empty handoff root: {root}")
+        for k in ("client", "server", "exchange"):
+            paths[k].mkdir(parents=True, exist_ok=True)
+        for k in ("root", "client", "server", "exchange"):
+            os.chmod(paths[k], 0o700)
+        cc = factory()
+        cc.KeyGen(args.seed)
+        cc.EvalBootstrapSetup(budget)
+        cc.EvalBootstrapKeyGen()
+        chain = EncryptedChain(cc, payload, **chain_options)
+        cc.EvalRotateKeyGen(chain.rotation_steps())
+        cc.SerializeKeys(paths["server"] / SERVER_KEYS)
+        cc.SerializeKeys(paths["client"] / CLIENT_KEYS, include_secret=True)
+        os.chmod(paths["client"] / CLIENT_KEYS, 0o600)
+        for t in range(args.tokens):
+            cc.SerializeCiphertext(chain.encrypt(payload.input_embeddings[t]), ex / f"input_t{t}.ct")
+        return {"status": "passed", "passed": True, "parameters": params,
+                "measurements": {"encrypted_inputs_written": args.tokens},
+                "measurement_scope": dict(scope, full_model_correctness_claimed=False)}
+    if role == "server-eval":
+        if server_secret_files(paths):
+            raise PayloadError("the server directory holds secret-key files")
+        cc = factory()
+        cc.DeserializeKeys(paths["server"] / SERVER_KEYS)
+        cc.EvalBootstrapSetup(budget)
+        cc.EvalBootstrapKeyGen()  # every key is in the bundle: nothing is generated
+        chain = EncryptedChain(cc, payload, **chain_options)
+        steps = []
+        for t in range(args.tokens):
+            ct = cc.DeserializeCiphertext(ex / f"input_t{t}.ct")
+            t0 = time.perf_counter()
+            out = chain.step_ct(ct)
+            steps.append(time.perf_counter() - t0)
+            cc.SerializeCiphertext(out, ex / f"output_t{t}.ct")
+        return {"status": "passed", "passed": True, "parameters": params,
+                "measurements": {"encrypted_outputs_written": args.tokens, "server_secret_key_files": 0,
+                                 "eval_seconds": sum(steps), "token_step_seconds": steps,
+                                 "refreshes": chain.refreshes(), "meta_bts_applied": chain.two_pass_refreshes()},
+                "measurement_scope": dict(scope, encrypted_full_layer_chain_evaluated=payload.full_chain,
+                                          full_model_correctness_claimed=False)}
+    # client-decrypt
+    cc = factory()
+    cc.DeserializeKeys(paths["client"] / CLIENT_KEYS)
+    last = payload.layers[-1].tensors
+    exact = payload.expected_final if payload.full_chain else last["test_layer_output"]
+    poly = payload.expected_poly_final if payload.full_chain else last.get("test_layer_output_poly")
+    reference = poly if poly is not None else exact
+    errors, ok = [], []
+    for t in range(args.tokens):
+        try:
+            got = cc.Decrypt(cc.DeserializeCiphertext(ex / f"output_t{t}.ct")).GetRealPackedValue()
+            got = np.asarray(got[:payload.d_model])
+            err = float(np.max(np.abs(got - reference[t])))
+            errors.append(err if np.isfinite(err) else float("inf"))
+            ok.append(1)
+        except Exception:  # a missing or corrupt output fails its token, as in the reference
+            errors.append(float("inf"))
+            ok.append(0)
+    secret_files = server_secret_files(paths)
+    max_error = max(errors)
+    passed = max_error <= args.tolerance and secret_files == 0
+    return {"status": "passed" if passed else "failed", "passed": passed,
+            "parameters": dict(params, tolerance=args.tolerance),
+            "measurements": {"correctness_reference": "polynomial-circuit" if poly is not None else "exact-legacy",
+                             "max_abs_error": max_error, "per_token_max_abs_error": errors,
+                             "per_token_decrypt_ok": ok, "server_secret_key_files": secret_files},
+            "measurement_scope": dict(scope, full_model_correctness_claimed=payload.full_chain)}
 
 
 def main(argv=None) -> int:

@@ -100,10 +100,43 @@ class SlotContext:
         self.rng = np.random.default_rng(seed)
         self.refresh_count = 0
         self.max_refresh_ratio = 0.0
+        self.has_secret = True
 
-    # -- keys
+    # -- keys and files (a pickled stand-in for the library's key bundles and
+    # ciphertext files: a bundle without the secret makes an evaluation-only
+    # context that refuses to decrypt or to generate keys)
+    def KeyGen(self, seed=0):
+        self.has_secret = True
+
     def EvalRotateKeyGen(self, steps):
-        self.keys |= {int(s) % self.slots for s in steps}
+        steps = {int(s) % self.slots for s in steps} - {0}
+        if steps - self.keys and not self.has_secret:
+            raise SimError("this context holds no secret key")
+        self.keys |= steps
+
+    def EvalBootstrapSetup(self, *_, **__):
+        pass
+
+    def EvalBootstrapKeyGen(self, *_):
+        pass
+
+    def SerializeKeys(self, path, include_secret=False):
+        import pickle
+        with open(path, "wb") as f:
+            pickle.dump({"keys": sorted(self.keys), "secret": bool(include_secret and self.has_secret)}, f)
+
+    def DeserializeKeys(self, path):
+        import pickle
+        with open(path, "rb") as f:
+            d = pickle.load(f)
+        self.keys, self.has_secret = set(d["keys"]), d["secret"]
+
+    def SerializeCiphertext(self, ct, path):
+        np.savez(path, values=ct.values, meta=np.array([ct.left, ct.deg]))
+
+    def DeserializeCiphertext(self, path):
+        with np.load(path if str(path).endswith(".npz") else str(path) + ".npz") as d:
+            return SimCiphertext(d["values"], int(d["meta"][0]), int(d["meta"][1]))
 
     def _rot(self, values, k):
         k = int(k) % self.slots
@@ -125,6 +158,8 @@ class SlotContext:
         return SimCiphertext(pt.values.copy(), self.n_q - 1)
 
     def Decrypt(self, ct, _unused=None):
+        if not self.has_secret:
+            raise SimError("this context holds no secret key")
         return _Decrypted(ct.values)
 
     # -- arithmetic

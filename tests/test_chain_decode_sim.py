@@ -150,3 +150,39 @@ def test_joint_payload_reference_policy():
     cc = _CountingContext(2048, refresh_noise=0.0)
     r = run_chain(cc, p, 2, 1e-4, meta_bts=False)
     assert r["passed"] and r["measurements"]["meta_bts_applied"] == cc.passes_seen.count(2) > 0
+
+
+def test_process_separated_roles(tmp_path):
+    """client-init / server-eval / client-decrypt through the handoff directory
+    (the reference's protocol): the server loads only evaluation keys and
+    cannot decrypt; the client checks the outputs; a second client-init into a
+    used directory is refused."""
+    from fhe_mamba_b200 import mamba2_decode
+    root = tmp_path / "handoff"
+    servers = []
+
+    def factory():
+        cc = SlotContext(2048, refresh_noise=0.0)
+        servers.append(cc)
+        return cc
+
+    base = ["--input-chain", CHAIN, "--output-json", str(tmp_path / "r.json"), "--ring-dim", "4096",
+            "--security", "not-set", "--tokens", "3", "--tolerance", "1e-4", "--handoff-dir", str(root)]
+    init = mamba2_decode.run(mamba2_decode.parse_args(base + ["--process-role", "client-init"]), factory)
+    assert init["passed"] and init["measurements"]["encrypted_inputs_written"] == 3
+    assert sorted(p.name for p in (root / "exchange").iterdir()) == [f"input_t{t}.ct.npz" for t in range(3)]
+    assert oct((root / "client").stat().st_mode & 0o777) == "0o700"
+    server = mamba2_decode.run(mamba2_decode.parse_args(base + ["--process-role", "server-eval"]), factory)
+    assert server["passed"] and not servers[-1].has_secret and server["measurements"]["refreshes"] > 0
+    with pytest.raises(SimError, match="no secret"):
+        servers[-1].Decrypt(servers[-1].DeserializeCiphertext(root / "exchange" / "output_t0.ct"))
+    client = mamba2_decode.run(mamba2_decode.parse_args(base + ["--process-role", "client-decrypt"]), factory)
+    m = client["measurements"]
+    assert client["passed"] and m["max_abs_error"] < 1e-5 and m["per_token_decrypt_ok"] == [1, 1, 1]
+    assert m["server_secret_key_files"] == 0
+    with pytest.raises(ValueError, match="non-empty handoff root"):
+        mamba2_decode.run(mamba2_decode.parse_args(base + ["--process-role", "client-init"]), factory)
+    # a secret that leaks into server/ fails the check
+    (root / "server" / "client.keys").write_bytes(b"x")
+    leaked = mamba2_decode.run(mamba2_decode.parse_args(base + ["--process-role", "client-decrypt"]), factory)
+    assert not leaked["passed"] and leaked["measurements"]["server_secret_key_files"] == 1

@@ -89,3 +89,27 @@ def test_joint_payload_decode():
     print("joint decode", m["per_token_max_abs_error"], "refreshes", m["refreshes"], "s/token",
           m["seconds_per_token"])
     assert r["passed"], m
+
+
+def test_process_separated_decode(tmp_path):
+    """The reference's three-process protocol, each role its own process:
+    client-init (keys, encrypted inputs), server-eval (evaluation keys only),
+    client-decrypt (checks the outputs against the polynomial circuit)."""
+    import subprocess
+    import sys
+    root = tmp_path / "handoff"
+    base = [sys.executable, "-m", "fhe_mamba_b200.mamba2_decode", "--input-chain", CHAIN, "--ring-dim", "4096",
+            "--security", "not-set", "--bootstrap-level-budget-cts", "4", "--bootstrap-level-budget-stc", "4",
+            "--tokens", "2", "--tolerance", str(TOL), "--handoff-dir", str(root), "--seed", "73"]
+    results = {}
+    for role in ("client-init", "server-eval", "client-decrypt"):
+        out = tmp_path / f"{role}.json"
+        proc = subprocess.run(base + ["--process-role", role, "--output-json", str(out)], capture_output=True,
+                              text=True, timeout=600)
+        results[role] = json.loads(out.read_text())
+        assert proc.returncode == 0, (role, results[role], proc.stderr[-2000:])
+    m = results["client-decrypt"]["measurements"]
+    print("process-separated decode", m["per_token_max_abs_error"],
+          results["server-eval"]["measurements"]["token_step_seconds"])
+    assert m["max_abs_error"] < TOL and m["per_token_decrypt_ok"] == [1, 1] and m["server_secret_key_files"] == 0
+    assert results["server-eval"]["measurement_scope"]["server_secret_key_loaded"] is False
