@@ -595,6 +595,7 @@ class ChainPayload:
     ar_embeddings: np.ndarray | None = None
     ar_expected_poly_final: np.ndarray | None = None
     ar_expected_exact_final: np.ndarray | None = None
+    chain_mode: bool = True  # False: one m1 layer payload (--input), no final norm
 
     @property
     def d_model(self) -> int:
@@ -602,7 +603,7 @@ class ChainPayload:
 
     @property
     def full_chain(self) -> bool:
-        return len(self.layers) == self.n_layers
+        return self.chain_mode and len(self.layers) == self.n_layers
 
 
 def _read_json(path: Path) -> dict:
@@ -790,6 +791,18 @@ def read_chain_payload(dirpath, max_layers: int = 0, autoregressive: bool = True
             chain.ar_expected_exact_final = _tensor(d, "autoregressive_exact_expected_final",
                                                     manifest["autoregressive_exact_expected_final"])
     return chain
+
+
+def read_layer_as_chain(dirpath) -> ChainPayload:
+    """One m1 layer payload as the decode's single-layer mode reads it
+    (``--input``, stage1_mamba2_decode_fideslib.cpp:781-783): the layer's test
+    inputs in, its test outputs as the reference, no final norm."""
+    L = read_layer_payload(dirpath, 0)
+    t = L.tensors
+    return ChainPayload(path=Path(dirpath), n_layers=1, n_test_tokens=t["test_layer_input"].shape[0], layers=[L],
+                        final_norm_w=np.zeros(0), final_norm_eps=0.0, final_norm=L.polys.rsqrt1,
+                        input_embeddings=t["test_layer_input"], expected_final=t["test_layer_output"],
+                        expected_poly_final=t.get("test_layer_output_poly"), chain_mode=False)
 
 
 # ---------------------------------------------------------------------------
@@ -1047,14 +1060,17 @@ class EncryptedChain:
         """One token from its embedding (client encryption + server pass)."""
         return self.step_ct(self.encrypt(embedding))
 
-    def step_ct(self, h):
+    def step_ct(self, h, on_layer=None):
         """Server pass for one encrypted token: the encrypted final hidden
-        vector (the last loaded layer's output when max_layers cuts the chain)."""
+        vector (the last loaded layer's output when max_layers cuts the chain).
+        on_layer(i, ct) sees every layer's output (debug attribution)."""
         c, D = self.cc, self.p.d_model
         new = []
-        for layer, (conv, st), bounds in zip(self.layers, self.state, self.bounds):
+        for i, (layer, (conv, st), bounds) in enumerate(zip(self.layers, self.state, self.bounds)):
             h, conv, st = layer.step(h, conv, st, bounds)
             new.append((conv, st))
+            if on_layer is not None:
+                on_layer(i, h)
         self.state = new
         if not self.p.full_chain:
             return h
@@ -1080,14 +1096,16 @@ def select_token(payload: ChainPayload, hidden) -> int:
 
 def run_chain(cc, payload: ChainPayload, tokens: int, tolerance: float = 5e-2,
               autoregressive_client_loop: bool = False, passes: int = 2, cache_gb: float = 8.0,
-              meta_bts: bool | None = None, meta_bts_residual_layers=()):
+              meta_bts: bool | None = None, meta_bts_residual_layers=(), debug_layer_errors: bool = False):
     """The decode's chain mode: encrypt each test (or client-selected) token's
     embedding, evaluate, decrypt, and compare with the polynomial-circuit
     reference (``chain_expected_poly_final``, or the last layer's
     ``test_layer_output_poly`` when max_layers cuts the chain) and with the
     exact model.  `cc` holds the secret, relinearisation and bootstrapping
-    keys; the layers' rotation keys are generated here.  Returns the result
-    document of the reference's decode (stage1_mamba2_decode_fideslib.cpp:
+    keys; the layers' rotation keys are generated here.  debug_layer_errors
+    also decrypts every layer's output and compares it with that layer's
+    polynomial reference (the decode's --debug-layer-errors).  Returns the
+    result document of the reference's decode (stage1_mamba2_decode_fideslib.cpp:
     4823-5060, the fields this backend has)."""
     p = payload
     if tokens < 1:
@@ -1120,7 +1138,7 @@ def run_chain(cc, payload: ChainPayload, tokens: int, tolerance: float = 5e-2,
                            meta_bts_residual_layers=meta_bts_residual_layers)
     cc.EvalRotateKeyGen(chain.rotation_steps())
     setup = time.perf_counter() - t0
-    per_token, per_token_exact, ok, selected, outputs = [], [], [], [], []
+    per_token, per_token_exact, ok, selected, outputs, per_layer = [], [], [], [], [], []
     next_embedding = None
     t1 = time.perf_counter()
     for t in range(tokens):
@@ -1128,7 +1146,17 @@ def run_chain(cc, payload: ChainPayload, tokens: int, tolerance: float = 5e-2,
             emb = p.ar_embeddings[t] if t < prompt or next_embedding is None else next_embedding
         else:
             emb = p.input_embeddings[t]
-        got = chain.decrypt(chain.step(emb))
+        layer_errors = []
+
+        def on_layer(i, ct, t=t):
+            key = "autoregressive_poly_layer_output" if autoregressive_client_loop else "test_layer_output_poly"
+            ref = p.layers[i].tensors.get(key)
+            if ref is not None and t < ref.shape[0]:
+                layer_errors.append(float(np.max(np.abs(chain.decrypt(ct) - ref[t]))))
+
+        got = chain.decrypt(chain.step_ct(chain.encrypt(emb), on_layer if debug_layer_errors else None))
+        if debug_layer_errors:
+            per_layer.append(layer_errors)
         outputs.append(got)
         finite = bool(np.all(np.isfinite(got)))
         ok.append(int(finite))
@@ -1170,6 +1198,7 @@ def run_chain(cc, payload: ChainPayload, tokens: int, tolerance: float = 5e-2,
             "token0_exact_sample": [float(v) for v in exact_ref[0][:8]],
             "refreshes": chain.refreshes(),
             "meta_bts_applied": chain.two_pass_refreshes(),
+            "per_token_layer_max_abs_error": per_layer if debug_layer_errors else None,
             "setup_seconds": setup,
             "decode_seconds": seconds,
             "seconds_per_token": seconds / tokens,

@@ -3,7 +3,7 @@ flags of the reference's stage-1 decode binary that apply to this backend
 (native/fideslib_stage0/src/stage1_mamba2_config.cpp:100-250, defaults from
 stage1_mamba2_config.hpp:20-211):
 
-    python -m fhe_mamba_b200.mamba2_decode --input-chain DIR --output-json PATH
+    python -m fhe_mamba_b200.mamba2_decode (--input-chain DIR | --input LAYER_DIR) --output-json PATH
         [--max-layers 0] [--tokens 4] [--ring-dim 131072]
         [--multiplicative-depth 44] [--scaling-mod-size 59] [--first-mod-size 60]
         [--num-large-digits 0] [--bootstrap-level-budget-cts 5]
@@ -11,7 +11,7 @@ stage1_mamba2_config.hpp:20-211):
         [--secret-key-dist uniform-ternary|sparse-encapsulated]
         [--autoregressive-client-loop 0|1] [--tolerance 5e-2] [--refresh-passes 2]
         [--meta-bts 0|1] [--meta-bts-alpha 12] [--meta-bts-residual-layers 20,21]
-        [--pt-cache-gib 5] [--seed 0]
+        [--pt-cache-gib 5] [--seed 0] [--debug-layer-errors 0|1]
         [--process-role inline|client-init|server-eval|client-decrypt --handoff-dir DIR]
 
 Refreshes: by default every refresh is two-pass (the residual of the first
@@ -62,7 +62,9 @@ def _bool(v: str) -> bool:
 
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(prog="mamba2_decode", description=__doc__.split("\n\n")[0])
-    ap.add_argument("--input-chain", required=True)
+    src = ap.add_mutually_exclusive_group(required=True)
+    src.add_argument("--input-chain")
+    src.add_argument("--input")
     ap.add_argument("--output-json", required=True)
     ap.add_argument("--max-layers", type=int, default=0)
     ap.add_argument("--tokens", type=int, default=4)
@@ -84,6 +86,7 @@ def parse_args(argv=None):
     ap.add_argument("--meta-bts-residual-layers", default="")
     ap.add_argument("--pt-cache-gib", type=float, default=5.0)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--debug-layer-errors", type=_bool, default=False)
     ap.add_argument("--process-role", choices=ROLES, default="inline")
     ap.add_argument("--handoff-dir", default="")
     return ap.parse_args(argv)
@@ -114,7 +117,7 @@ SERVER_KEYS = "eval.keys"     # public and evaluation keys (server/)
 def run(args, context_factory=None) -> dict:
     """One invocation; `context_factory` makes the CryptoContext (default: the
     device library with the command line's parameters)."""
-    from .chain_payload import PayloadError, read_chain_payload, run_chain
+    from .chain_payload import PayloadError, read_chain_payload, read_layer_as_chain, run_chain
     from .ckks import CCParams, CryptoContext
     from .program import security_audit
 
@@ -145,7 +148,12 @@ def run(args, context_factory=None) -> dict:
             raise PayloadError("parameters exceed the classical-128 bound: " + json.dumps(audit))
     elif args.num_large_digits == 0:
         args.num_large_digits = 3
-    payload = read_chain_payload(args.input_chain, args.max_layers, args.autoregressive_client_loop)
+    if args.input_chain:
+        payload = read_chain_payload(args.input_chain, args.max_layers, args.autoregressive_client_loop)
+    else:
+        if args.autoregressive_client_loop:
+            raise PayloadError("autoregressive-client-loop needs --input-chain")
+        payload = read_layer_as_chain(args.input)
     if args.process_role != "inline":
         if not args.handoff_dir:
             raise PayloadError(f"--process-role {args.process_role} needs --handoff-dir")
@@ -169,7 +177,7 @@ def run(args, context_factory=None) -> dict:
                               else 0)
         cc.EvalBootstrapKeyGen()
         result = run_chain(cc, payload, args.tokens, args.tolerance, args.autoregressive_client_loop,
-                           **chain_options)
+                           debug_layer_errors=args.debug_layer_errors, **chain_options)
     else:
         result = run_role(args, payload, factory, budget, chain_options)
     result["parameters"].update({"multiplicative_depth": args.multiplicative_depth,
@@ -178,7 +186,8 @@ def run(args, context_factory=None) -> dict:
                                  "secret_key_dist": args.secret_key_dist,
                                  "bootstrap_level_budget": [args.bootstrap_level_budget_cts,
                                                             args.bootstrap_level_budget_stc],
-                                 "max_layers": args.max_layers, "input_chain": str(args.input_chain),
+                                 "max_layers": args.max_layers, "input_chain": args.input_chain,
+                                 "input": args.input,
                                  "process_role": args.process_role})
     if audit is not None:
         result["security_audit"] = audit

@@ -186,3 +186,22 @@ def test_process_separated_roles(tmp_path):
     (root / "server" / "client.keys").write_bytes(b"x")
     leaked = mamba2_decode.run(mamba2_decode.parse_args(base + ["--process-role", "client-decrypt"]), factory)
     assert not leaked["passed"] and leaked["measurements"]["server_secret_key_files"] == 1
+
+
+def test_single_layer_mode_and_layer_errors(tmp_path):
+    """--input LAYER_DIR (one m1 payload: its test inputs in, its test outputs
+    as the reference, no final norm) and --debug-layer-errors (every layer's
+    decrypted output against that layer's polynomial reference)."""
+    from fhe_mamba_b200 import mamba2_decode
+    from fhe_mamba_b200.chain_payload import read_layer_as_chain
+    p = read_layer_as_chain(os.path.join(CHAIN, "layer_01"))
+    assert not p.full_chain and not p.chain_mode and p.n_test_tokens == 3
+    r = run_chain(SlotContext(2048, refresh_noise=0.0), p, 3, 1e-4)
+    assert r["passed"] and r["measurements"]["correctness_reference"] == "polynomial-circuit"
+    args = mamba2_decode.parse_args(["--input", os.path.join(CHAIN, "layer_00"), "--output-json",
+                                     str(tmp_path / "r.json"), "--security", "not-set", "--tokens", "2"])
+    assert mamba2_decode.run(args, lambda: SlotContext(2048, refresh_noise=0.0))["passed"]
+    full = read_chain_payload(CHAIN)
+    r = run_chain(SlotContext(2048, refresh_noise=0.0), full, 3, 1e-4, debug_layer_errors=True)
+    per_layer = r["measurements"]["per_token_layer_max_abs_error"]
+    assert len(per_layer) == 3 and all(len(row) == 2 and max(row) < 1e-4 for row in per_layer)
