@@ -11,7 +11,7 @@ stage1_mamba2_config.hpp:20-211):
         [--secret-key-dist uniform-ternary|sparse-encapsulated]
         [--autoregressive-client-loop 0|1] [--tolerance 5e-2] [--refresh-passes 2]
         [--meta-bts 0|1] [--meta-bts-alpha 12] [--meta-bts-residual-layers 20,21]
-        [--pt-cache-gib 5] [--seed 0] [--debug-layer-errors 0|1]
+        [--pt-cache-gib 5] [--seed S] [--debug-layer-errors 0|1]
         [--process-role inline|client-init|server-eval|client-decrypt --handoff-dir DIR]
 
 Refreshes: by default every refresh is two-pass (the residual of the first
@@ -41,6 +41,8 @@ or 3 with --security not-set.  The main secret is
 uniform ternary; ``sparse-encapsulated`` switches bootstrapping to a sparse
 secret of Hamming weight 32 (the reference's SPARSE_ENCAPSULATED); a sparse
 main secret (``sparse-ternary``, the reference's default) is not supported.
+Keys derive from --seed (reproducible runs); without it the seed is drawn
+from the operating system, and it is never written to the result.
 """
 from __future__ import annotations
 
@@ -85,7 +87,7 @@ def parse_args(argv=None):
     ap.add_argument("--state-meta-bts-alpha", type=int, default=-1)
     ap.add_argument("--meta-bts-residual-layers", default="")
     ap.add_argument("--pt-cache-gib", type=float, default=5.0)
-    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--seed", type=int, default=None)
     ap.add_argument("--debug-layer-errors", type=_bool, default=False)
     ap.add_argument("--process-role", choices=ROLES, default="inline")
     ap.add_argument("--handoff-dir", default="")
@@ -167,6 +169,9 @@ def run(args, context_factory=None) -> dict:
         ring_dim=args.ring_dim, multiplicative_depth=args.multiplicative_depth,
         scaling_mod_size=args.scaling_mod_size, first_mod_size=args.first_mod_size,
         num_large_digits=args.num_large_digits)))
+    if args.seed is None:  # keys derive from the seed: without one, draw it from the OS
+        import secrets
+        args.seed = secrets.randbits(63) | 1
     budget = (args.bootstrap_level_budget_cts, args.bootstrap_level_budget_stc)
     chain_options = dict(passes=args.refresh_passes, cache_gb=args.pt_cache_gib, meta_bts=args.meta_bts,
                          meta_bts_residual_layers=residual_layers)
