@@ -1019,9 +1019,12 @@ class EncryptedChain:
     and final_norm, stage1_mamba2_decode_fideslib.cpp:3634-4520)."""
 
     def __init__(self, cc, payload: ChainPayload, passes: int = 2, cache_gb: float = 8.0, bounds=None,
-                 meta_bts: bool | None = None, meta_bts_residual_layers=()):
+                 meta_bts: bool | None = None, meta_bts_residual_layers=(), rotation_keys: str = "full",
+                 rotation_key_gib: float = 45.0):
         """passes: every refresh's pass count (2: each refresh is Meta-BTS), or,
-        with meta_bts set (True / False), the reference's selective policy."""
+        with meta_bts set (True / False), the reference's selective policy.
+        rotation_keys: full | compact | balanced key plan (rotation_keys.py),
+        balanced under rotation_key_gib GiB of rotation keys."""
         self.cc, self.p = cc, payload
         self.cache = PlaintextCache(cache_gb * 2 ** 30)
 
@@ -1034,12 +1037,28 @@ class EncryptedChain:
         self.layers = [EncryptedMamba2Layer(cc, L.weights, L.polys, passes=policy(L), cache=self.cache)
                        for L in payload.layers]
         self.bounds = bounds if bounds is not None else chain_bounds(payload)
+        self.plan = None
+        if rotation_keys != "full":
+            from .rotation_keys import ComposedRotations, key_bytes, plan_keys
+            steps, required = set(), set()
+            for layer in self.layers:
+                steps |= set(layer.rotation_steps())
+                required |= set(layer.transform_steps())
+            per_key = key_bytes(cc.n, cc.n_q + cc.n_p, cc.dnum)
+            self.plan = plan_keys({s: 1.0 for s in steps}, cc.slots, rotation_keys, rotation_key_gib * 2 ** 30,
+                                  per_key, required)
+            self.cc = ComposedRotations(cc, self.plan)
+            for layer in self.layers:
+                layer.cc = layer.pm.cc = self.cc
         self.reset()
 
     def reset(self):
         self.state = [([None] * (L.weights.conv_kernel - 1), None) for L in self.p.layers]
 
     def rotation_steps(self):
+        """The rotation keys to generate (the plan's, under a key plan)."""
+        if self.plan is not None:
+            return sorted(k % self.cc.slots for k in self.plan.keys)
         s = set()
         for layer in self.layers:
             s |= set(layer.rotation_steps())
@@ -1096,7 +1115,8 @@ def select_token(payload: ChainPayload, hidden) -> int:
 
 def run_chain(cc, payload: ChainPayload, tokens: int, tolerance: float = 5e-2,
               autoregressive_client_loop: bool = False, passes: int = 2, cache_gb: float = 8.0,
-              meta_bts: bool | None = None, meta_bts_residual_layers=(), debug_layer_errors: bool = False):
+              meta_bts: bool | None = None, meta_bts_residual_layers=(), debug_layer_errors: bool = False,
+              rotation_keys: str = "full", rotation_key_gib: float = 45.0):
     """The decode's chain mode: encrypt each test (or client-selected) token's
     embedding, evaluate, decrypt, and compare with the polynomial-circuit
     reference (``chain_expected_poly_final``, or the last layer's
@@ -1135,7 +1155,8 @@ def run_chain(cc, payload: ChainPayload, tokens: int, tolerance: float = 5e-2,
     reference = poly_ref if has_poly else exact_ref
     t0 = time.perf_counter()
     chain = EncryptedChain(cc, p, passes=passes, cache_gb=cache_gb, meta_bts=meta_bts,
-                           meta_bts_residual_layers=meta_bts_residual_layers)
+                           meta_bts_residual_layers=meta_bts_residual_layers, rotation_keys=rotation_keys,
+                           rotation_key_gib=rotation_key_gib)
     cc.EvalRotateKeyGen(chain.rotation_steps())
     setup = time.perf_counter() - t0
     per_token, per_token_exact, ok, selected, outputs, per_layer = [], [], [], [], [], []
@@ -1199,6 +1220,9 @@ def run_chain(cc, payload: ChainPayload, tokens: int, tolerance: float = 5e-2,
             "refreshes": chain.refreshes(),
             "meta_bts_applied": chain.two_pass_refreshes(),
             "per_token_layer_max_abs_error": per_layer if debug_layer_errors else None,
+            "rotation_keys": len(chain.rotation_steps()),
+            "rotation_key_plan": chain.plan.stats if chain.plan is not None else {"mode": "full"},
+            "composite_rotation_applications": getattr(chain.cc, "composite_applications", 0),
             "setup_seconds": setup,
             "decode_seconds": seconds,
             "seconds_per_token": seconds / tokens,

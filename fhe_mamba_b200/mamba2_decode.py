@@ -12,6 +12,7 @@ stage1_mamba2_config.hpp:20-211):
         [--autoregressive-client-loop 0|1] [--tolerance 5e-2] [--refresh-passes 2]
         [--meta-bts 0|1] [--meta-bts-alpha 12] [--meta-bts-residual-layers 20,21]
         [--pt-cache-gib 5] [--seed S] [--debug-layer-errors 0|1]
+        [--rotation-keys full|compact|balanced] [--rotation-key-gib 45]
         [--process-role inline|client-init|server-eval|client-decrypt --handoff-dir DIR]
 
 Refreshes: by default every refresh is two-pass (the residual of the first
@@ -89,6 +90,8 @@ def parse_args(argv=None):
     ap.add_argument("--pt-cache-gib", type=float, default=5.0)
     ap.add_argument("--seed", type=int, default=None)
     ap.add_argument("--debug-layer-errors", type=_bool, default=False)
+    ap.add_argument("--rotation-keys", choices=("full", "compact", "balanced"), default="full")
+    ap.add_argument("--rotation-key-gib", type=float, default=45.0)
     ap.add_argument("--process-role", choices=ROLES, default="inline")
     ap.add_argument("--handoff-dir", default="")
     return ap.parse_args(argv)
@@ -173,8 +176,11 @@ def run(args, context_factory=None) -> dict:
         import secrets
         args.seed = secrets.randbits(63) | 1
     budget = (args.bootstrap_level_budget_cts, args.bootstrap_level_budget_stc)
+    if args.rotation_key_gib <= 0:
+        raise PayloadError("--rotation-key-gib must be positive")
     chain_options = dict(passes=args.refresh_passes, cache_gb=args.pt_cache_gib, meta_bts=args.meta_bts,
-                         meta_bts_residual_layers=residual_layers)
+                         meta_bts_residual_layers=residual_layers, rotation_keys=args.rotation_keys,
+                         rotation_key_gib=args.rotation_key_gib)
     if args.process_role == "inline":
         cc = factory()
         cc.KeyGen(args.seed)

@@ -374,6 +374,19 @@ class EncryptedMamba2Layer:
         s |= {W.d_inner, W.d_inner + W.conv_dim, -self.dt_base, -self.decay_base}
         return sorted(v % n for v in s if v % n)
 
+    def transform_steps(self):
+        """The baby and giant steps of this layer's fused linear transforms
+        (the replicated matvecs and the state-block placement): the library
+        switches keys per step there, so they need keys of their own."""
+        n = self.cc.slots
+        s = set()
+        for lay in self.rep.values():
+            s |= set(range(1, lay.b)) | {g * lay.b for g in range(1, lay.G)}
+        stride = -(self.layout.group_block - 1)
+        b, G = self.pm._state_baby, self.pm._state_giant
+        s |= {j * stride for j in range(1, b)} | {g * b * stride for g in range(1, G)}
+        return sorted(v % n for v in s if v % n)
+
     def _diags(self, name):
         if name not in self._lin:
             self._lin[name] = self.rep[name].diagonals(self.W[name], self.cc.slots)

@@ -64,6 +64,9 @@ class SimCiphertext:
     def n_limbs(self):
         return self.left + 1 + (1 if self.deg >= 2 else 0)
 
+    def Clone(self):
+        return SimCiphertext(self.values.copy(), self.left, self.deg)
+
     def GetNoiseScaleDeg(self):
         return self.deg
 
@@ -95,6 +98,7 @@ class SlotContext:
     def __init__(self, slots: int, depth: int = 44, refresh_left: int = 21, refresh_noise: float = 1e-4,
                  seed: int = 0):
         self.slots, self.n, self.n_q = slots, 2 * slots, depth + 1
+        self.n_p, self.dnum = 12, 4  # key-size bookkeeping only
         self.refresh_left, self.refresh_noise = refresh_left, refresh_noise
         self.keys = set()
         self.rng = np.random.default_rng(seed)
