@@ -846,10 +846,12 @@ def plain_decode(payload: ChainPayload, embeddings, rec=None):
 
 
 def _carried_keys(carried: dict):
-    """(refresh-bound key, value) pairs from a layer's calibration-text bounds."""
+    """(refresh-bound key, value) pairs from a layer's calibration-text bounds.
+    The exporter's ``y`` checkpoint is the gated value y * silu(z)
+    (mixer2_forward, src/fhemamba/reference.py:290), ``g`` here."""
     cp = carried.get("checkpoint_abs_max", {}) or {}
     pairs = [("h", cp.get("residual")), ("proj", cp.get("proj")), ("pack", cp.get("conv_silu")),
-             ("pack", cp.get("dt")), ("y", cp.get("y")), ("xbc", carried.get("fifo_abs_max")),
+             ("pack", cp.get("dt")), ("g", cp.get("y")), ("xbc", carried.get("fifo_abs_max")),
              ("state", carried.get("state_abs_max"))]
     return [(k, float(v)) for k, v in pairs if v is not None]
 

@@ -140,8 +140,13 @@ def test_refresh_bounds(payload):
     assert d[0]["proj"] == pytest.approx(2 * payload.layers[0].carried["checkpoint_abs_max"]["proj"])
     joint = read_chain_payload(JOINT)
     dj = chain_bounds(joint)
+    # the exporter's "y" checkpoint is the gated value: its calibration-text maximum bounds g
     assert joint.client_embedding_w is None and dj[0]["g"] == pytest.approx(
-        2 * np.sqrt(128 * joint.layers[0].carried["gated_variance_range"][1]))
+        2 * joint.layers[0].carried["checkpoint_abs_max"]["y"])
+    # without it, the carried gated-variance range does: |g_i| <= sqrt(width var_hi)
+    carried = dict(joint.layers[0].carried, checkpoint_abs_max={})
+    joint.layers[0].carried = carried
+    assert chain_bounds(joint)[0]["g"] == pytest.approx(2 * np.sqrt(128 * carried["gated_variance_range"][1]))
     assert FALLBACK_BOUNDS["state"] == 24.0
     assert {"h", "nf_v", "nf_y"} <= set(b[2])
     # the calibration-text bounds the exporter carries only widen the circuit's own
