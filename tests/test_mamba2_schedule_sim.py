@@ -1,0 +1,47 @@
+"""The synthetic Mamba-2 layer and token loop (mamba2_layer.py: BASELINE
+configs 4 and 5, the bench's token loop) on the slot-level model of the
+CryptoContext API (tests/slot_sim.py): masks, rotations, replicated BSGS
+layouts, level budgeting and refresh bounds of the host schedule, at the
+config-4 shape (d_model 768, 24 heads x 64, d_state 128, 2^15 slots).
+Without bootstrap noise the schedule reproduces the fp64 polynomial path to
+rounding; every rotation must find a generated key and every refresh input
+must sit inside its bound.  No GPU."""
+import numpy as np
+
+from slot_sim import SlotContext
+
+
+def test_config4_layer_schedule():
+    from fhe_mamba_b200.mamba2_layer import (EncryptedMamba2Layer, Mamba2Polys, Mamba2Weights, calibrate_bounds,
+                                             plain_step)
+    W = Mamba2Weights(d_model=768, d_state=128, heads=24)
+    P = Mamba2Polys(W, samples=2)
+    bounds = calibrate_bounds(W, P, samples=2)
+    cc = SlotContext(1 << 15, refresh_noise=0.0)
+    layer = EncryptedMamba2Layer(cc, W, P)
+    cc.EvalRotateKeyGen(layer.rotation_steps())
+    rng = np.random.default_rng(12)
+    conv_p = [np.zeros(W.conv_dim) for _ in range(W.conv_kernel - 1)]
+    conv_c = [None] * (W.conv_kernel - 1)
+    st_p = st_c = None
+    for _ in range(2):
+        h = rng.normal(0, 1, W.d_model)
+        want, conv_p, st_p = plain_step(W, P, h, conv_p, st_p)
+        out, conv_c, st_c = layer.step(cc.Encrypt(cc.MakeCKKSPackedPlaintext(h)), conv_c, st_c, bounds)
+        assert np.max(np.abs(cc.Decrypt(out).GetRealPackedValue()[:W.d_model] - want)) < 1e-10
+    assert layer.refreshes >= 1 and cc.max_refresh_ratio <= 1.0
+
+
+def test_token_loop_schedule():
+    """The 2-layer greedy loop of the GPU test at its shape: same tokens, same hidden vectors."""
+    from fhe_mamba_b200.mamba2_layer import EncryptedMamba2Model, Mamba2Model
+    m = Mamba2Model(layers=2, d_model=64, d_state=32, heads=16, vocab=128, std=0.1)
+    cc = SlotContext(2048, refresh_noise=0.0)
+    em = EncryptedMamba2Model(cc, m)
+    cc.EvalRotateKeyGen(em.rotation_steps())
+    state = m.initial_state()
+    for tok in (3, 17, 5):
+        hf, logits, state = m.plain_token(tok, state)
+        picked, ehf = em.select(em.step(tok))
+        assert picked == int(np.argmax(logits)) and np.max(np.abs(ehf - hf)) < 1e-10
+    assert em.refreshes() >= 1 and cc.max_refresh_ratio <= 1.0
