@@ -363,12 +363,12 @@ def measure_sharded_keyswitch(local, world, reps=20):
 class TokenLoop:
     """The 24-layer encrypted greedy loop: client encrypt -> server layers -> client select."""
 
-    def __init__(self, local, layers=24, passes=2, seed=6, sparse_h=0, classical128=False):
+    def __init__(self, local, layers=24, passes=2, seed=6, sparse_h=0, classical128=False, fused_decay=False):
         from fhe_mamba_b200 import CCParams, CryptoContext
         from fhe_mamba_b200.mamba2_layer import EncryptedMamba2Model, Mamba2Model
         t0 = time.perf_counter()
         self.model = Mamba2Model(layers=layers, d_model=768, d_state=128, heads=24, vocab=50280, seed=seed,
-                                 calib_sequences=4)
+                                 calib_sequences=4, fused_decay=fused_decay)
         # 128-classic as the reference's executable sets it up: ring 2^17, four
         # digits, 2^15 slots sparsely packed (packed_fideslib.cpp:1060-1076)
         ring, dnum = (1 << 17, 4) if classical128 else (1 << 16, 3)
@@ -468,7 +468,7 @@ def config_dict(args):
                         f"({args.layers} layers, d_model 768, d_state 128, 24 heads, vocab 50280)",
             "ring_dim": 1 << 17 if args.security == "128-classic" else 1 << 16, "slots": 1 << 15, "depth": 44,
             "scale_bits": 59, "dnum": 4 if args.security == "128-classic" else 3, "security": args.security,
-            "bootstrap_passes": args.passes,
+            "bootstrap_passes": args.passes, "decay": "fused per-head series" if args.fused_decay else "exp(a softplus)",
             "secret_key_dist": f"sparse-encapsulated h={args.sparse_h}" if args.sparse_h else "uniform-ternary",
             "l2": "inputs larger than L2 (keys ~36 GB, cached diagonals)",
             "parallelism": "one token-loop replica per GPU"}
@@ -531,6 +531,8 @@ def main():
                     help="bootstrap by sparse-secret encapsulation with this Hamming weight (0: uniform ternary)")
     ap.add_argument("--security", default="not-set", choices=["not-set", "128-classic"],
                     help="128-classic: ring 2^17, dnum 4, 2^15 sparsely packed slots, Q*P audited")
+    ap.add_argument("--fused-decay", action="store_true",
+                    help="decay as one per-head series of the raw dt (no refresh of a*dt); off by default")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ckks", action="store_true", help="skip the key-switch, matvec and bootstrap side measurements")
@@ -585,7 +587,7 @@ def main():
         side["sharded_keyswitch"] = measure_sharded_keyswitch(local, world)
 
     loop = TokenLoop(local, layers=args.layers, passes=args.passes, seed=6 + rank, sparse_h=args.sparse_h,
-                     classical128=args.security == "128-classic")
+                     classical128=args.security == "128-classic", fused_decay=args.fused_decay)
     stream = torch.cuda.ExternalStream(loop.cc.stream_ptr(), device=torch.device("cuda", local))
     tok = loop.token
     for _ in range(args.warmup):

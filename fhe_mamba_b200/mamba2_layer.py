@@ -137,6 +137,76 @@ def range_updater(ranges):
     return upd
 
 
+@dataclass
+class HeadPoly:
+    """One Chebyshev series per head on a shared domain [lo, hi]: coeffs[i, h]
+    is head h's coefficient of T_i.  On ciphertexts the heads sit at slots
+    [0, heads): one basis T_1..T_D of the slot-masked affine map is weighted by
+    plaintext coefficient vectors (zero outside the heads, so the result is
+    too), the way the reference's joint gates evaluate per-head polynomials."""
+
+    coeffs: np.ndarray
+    lo: float
+    hi: float
+
+    @classmethod
+    def fit(cls, fn, params, lo, hi, degree):
+        """Head h interpolates t -> fn(params[h], t) at Chebyshev nodes."""
+        return cls(np.stack([cheb_fit(lambda t, q=q: fn(q, t), lo, hi, degree) for q in params], axis=1), lo, hi)
+
+    def __call__(self, x):
+        t = (2.0 * np.asarray(x, dtype=np.float64) - self.lo - self.hi) / (self.hi - self.lo)
+        b1 = np.zeros_like(t)
+        b2 = np.zeros_like(t)
+        for c in self.coeffs[:0:-1]:
+            b1, b2 = 2.0 * t * b1 - b2 + c, b1
+        return t * b1 - b2 + self.coeffs[0]
+
+    @property
+    def degree(self) -> int:
+        return self.coeffs.shape[0] - 1
+
+    @property
+    def levels(self) -> int:
+        # the affine map, the basis up to T_D, the coefficient products
+        return 2 + max(0, int(np.ceil(np.log2(max(1, self.degree)))))
+
+    def encrypted(self, pm, z, heads):
+        c, n = pm.cc, pm.L.slots
+        a = np.zeros(n)
+        b = np.zeros(n)
+        a[:heads] = 2.0 / (self.hi - self.lo)
+        b[:heads] = -(self.lo + self.hi) / (self.hi - self.lo)
+        t = pm._mul_mask(z, a)
+        if t.GetNoiseScaleDeg() >= 2:
+            c.RescaleInPlace(t)
+        t = c.EvalAdd(t, c.MakeCKKSPackedPlaintext(b, level=c.n_q - t.n_limbs(), scale=t.GetScalingFactor()))
+        basis = {1: t}
+
+        def T(i):  # T_2k = 2 T_k^2 - 1, T_2k+1 = 2 T_k+1 T_k - T_1
+            if i not in basis:
+                if i % 2 == 0:
+                    sq = c.EvalMult(T(i // 2), T(i // 2))
+                    basis[i] = c.EvalAdd(c.EvalAdd(sq, sq), -1.0)
+                else:
+                    pr = c.EvalMult(T(i // 2 + 1), T(i // 2))
+                    basis[i] = c.EvalSub(c.EvalAdd(pr, pr), T(1))
+            return basis[i]
+
+        acc = None
+        for i in range(1, self.coeffs.shape[0]):
+            vec = np.zeros(n)
+            vec[:heads] = self.coeffs[i]
+            term = pm._mul_mask(T(i), vec)
+            acc = term if acc is None else c.EvalAdd(acc, term)
+        if acc.GetNoiseScaleDeg() >= 2:
+            c.RescaleInPlace(acc)
+        const = np.zeros(n)
+        const[:heads] = self.coeffs[0]
+        return c.EvalAdd(acc, c.MakeCKKSPackedPlaintext(const, level=c.n_q - acc.n_limbs(),
+                                                         scale=acc.GetScalingFactor()))
+
+
 class Mamba2Polys:
     """Polynomial domains calibrated on exact-function trajectories (random
     residual inputs over a few tokens, recurrent state U[-1, 1]), widened by half
@@ -144,7 +214,7 @@ class Mamba2Polys:
     calibration when the layer sits inside a model."""
 
     def __init__(self, W: Mamba2Weights, degree: int = 31, seed_degree: int = 15, samples: int = 16,
-                 tokens: int = 3, seed: int = 9, ranges=None):
+                 tokens: int = 3, seed: int = 9, ranges=None, fused_decay: bool = False):
         if ranges is None:
             r = np.random.default_rng(seed)
             ranges = new_ranges()
@@ -170,6 +240,11 @@ class Mamba2Polys:
         self.rsqrt1 = self._fit(lambda t: 1 / np.sqrt(t), *self.v1, seed_degree)
         self.rsqrt2 = self._fit(lambda t: 1 / np.sqrt(t), *self.v2, seed_degree)
         self.seed_degree = seed_degree
+        # fused_decay: decay = exp(a_h softplus(x)) as one per-head series of the
+        # raw dt input x on the softplus domain, instead of exp of a * softplus
+        # (which needs a * dt on the exp domain, and a refresh before it)
+        self.decay = HeadPoly.fit(lambda a, t: np.exp(a * _softplus(t)), W["a"], self.softplus.lo,
+                                  self.softplus.hi, degree) if fused_decay else None
 
     @staticmethod
     def _fit(fn, lo, hi, degree):
@@ -210,7 +285,8 @@ def plain_step(W: Mamba2Weights, P: Mamba2Polys, h, conv_state, ssm_state):
         dts, decay = P.gates(dt + W["dt_bias"])
     else:
         dts = P.softplus(dt + W["dt_bias"])
-        decay = P.exp(W["a"] * dts)
+        fused = getattr(P, "decay", None)
+        decay = fused(dt + W["dt_bias"]) if fused is not None else P.exp(W["a"] * dts)
     upd = (dts[:, None] * x)[:, :, None] * B[None, None, :]
     st = upd if ssm_state is None else decay[:, None, None] * ssm_state + upd
     y = (st * C[None, None, :]).sum(-1) + W["d"][:, None] * x
@@ -509,11 +585,17 @@ class EncryptedMamba2Layer:
             pack = c.EvalAdd(xa, c.EvalRotate(dts, -self.dt_base))
             if ssm_state is not None:
                 pack = c.EvalAdd(pack, c.EvalRotate(decay, -self.decay_base))
+        elif getattr(P, "decay", None) is not None:  # fused decay: dts and decay both from dt
+            dtv = self._fit(dtv, max(self._need(P.softplus), P.decay.levels), bounds["dt"], "dt")
+            dts = self._poly(dtv, P.softplus, 0, H)
+            pack = c.EvalAdd(xa, c.EvalRotate(dts, -self.dt_base))
+            if ssm_state is not None:
+                pack = c.EvalAdd(pack, c.EvalRotate(P.decay.encrypted(self.pm, dtv, H), -self.decay_base))
         else:
             dtv = self._fit(dtv, self._need(P.softplus), bounds["dt"], "dt")
             dts = self._poly(dtv, P.softplus, 0, H)
             pack = c.EvalAdd(xa, c.EvalRotate(dts, -self.dt_base))
-        if gates is None and ssm_state is not None:
+        if gates is None and getattr(P, "decay", None) is None and ssm_state is not None:
             # heads a payload prunes (head mask 0) get input 0, inside the
             # decay polynomial's domain; the polynomial's output mask zeroes them
             mask = getattr(P.exp, "head_mask", None)
@@ -566,7 +648,10 @@ def poly_step_record(W: Mamba2Weights, P: Mamba2Polys, h, conv, st, rec):
     else:
         dts = P.softplus(dt + W["dt_bias"])
         decay = None
-        rec("adt", W["a"] * dts)
+        if getattr(P, "decay", None) is not None:
+            decay = P.decay(dt + W["dt_bias"])
+        else:
+            rec("adt", W["a"] * dts)
     rec("dts", dts)
     rec("pack", xa)
     rec("pack", dts)
@@ -615,7 +700,7 @@ class Mamba2Model:
     native/fideslib_stage0/src/packed_fideslib.cpp:842-880)."""
 
     def __init__(self, layers: int, d_model: int, d_state: int, heads: int, vocab: int, std: float = 0.02,
-                 seed: int = 6, calib_sequences: int = 8):
+                 seed: int = 6, calib_sequences: int = 8, fused_decay: bool = False):
         self.layers = [Mamba2Weights(d_model=d_model, d_state=d_state, heads=heads, std=std, seed=seed * 1000 + i)
                        for i in range(layers)]
         r = np.random.default_rng(seed)
@@ -637,7 +722,7 @@ class Mamba2Model:
                     h, c_, s_ = exact_step(W, h, state[li][0], state[li][1], range_updater(ranges[li]))
                     state[li] = (c_, s_)
                 finals.append(np.mean(h * h) + eps)
-        self.polys = [Mamba2Polys(W, ranges=rg) for W, rg in zip(self.layers, ranges)]
+        self.polys = [Mamba2Polys(W, ranges=rg, fused_decay=fused_decay) for W, rg in zip(self.layers, ranges)]
         lo, hi = 0.25 * min(finals), 4.0 * max(finals)
         self.rsqrt_f = Poly(cheb_fit(lambda t: 1 / np.sqrt(t), lo, hi, 15), lo, hi)
         # ... and the polynomial path's magnitudes give the refresh bounds

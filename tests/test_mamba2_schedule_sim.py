@@ -45,3 +45,32 @@ def test_token_loop_schedule():
         picked, ehf = em.select(em.step(tok))
         assert picked == int(np.argmax(logits)) and np.max(np.abs(ehf - hf)) < 1e-10
     assert em.refreshes() >= 1 and cc.max_refresh_ratio <= 1.0
+
+
+def test_fused_decay():
+    """decay = exp(a_h softplus(x)) as one per-head series of the raw dt input
+    (HeadPoly, off by default): accurate over the whole softplus domain, exact
+    against its own plaintext circuit on the slot model, and one refresh per
+    layer and token fewer than exp of a * softplus (no refresh of a * dt)."""
+    from fhe_mamba_b200.mamba2_layer import (EncryptedMamba2Model, HeadPoly, Mamba2Model, Mamba2Polys,
+                                             Mamba2Weights, _softplus)
+    W = Mamba2Weights(d_model=768, d_state=128, heads=24, seed=6000)
+    P = Mamba2Polys(W, samples=2, fused_decay=True)
+    assert isinstance(P.decay, HeadPoly) and P.decay.coeffs.shape == (32, 24) and P.decay.levels == 7
+    x = np.linspace(P.softplus.lo, P.softplus.hi, 2001)
+    want = np.exp(W["a"][None, :] * _softplus(x)[:, None])
+    assert np.max(np.abs(P.decay(x[:, None]) - want)) < 1e-4
+    counts = {}
+    for fused in (False, True):
+        m = Mamba2Model(layers=2, d_model=64, d_state=32, heads=16, vocab=128, std=0.1, fused_decay=fused)
+        cc = SlotContext(2048, refresh_noise=0.0)
+        em = EncryptedMamba2Model(cc, m)
+        cc.EvalRotateKeyGen(em.rotation_steps())
+        state = m.initial_state()
+        for tok in (3, 17, 5):
+            hf, logits, state = m.plain_token(tok, state)
+            picked, ehf = em.select(em.step(tok))
+            assert picked == int(np.argmax(logits)) and np.max(np.abs(ehf - hf)) < 1e-10
+        assert cc.max_refresh_ratio <= 1.0
+        counts[fused] = em.refreshes()
+    assert counts[True] < counts[False]
