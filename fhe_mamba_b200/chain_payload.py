@@ -466,6 +466,16 @@ def parse_joint_gate(spec: dict, heads: int, a_log: np.ndarray) -> JointGate:
     return JointGate(arr["lo"], arr["hi"], arr["p"].reshape(-1, heads), arr["q"].reshape(-1, heads), arr["rates"])
 
 
+def _count(spec: dict, key: str, default=None) -> int:
+    """A non-negative integer field of a spec (squarings, iterations)."""
+    value = spec.get(key, default)
+    if value is None:
+        raise PayloadError(f"meta.json key not found: {key}")
+    if int(value) != value or int(value) < 0 or int(value) > 64:
+        raise PayloadError(f"{key} must be an integer in [0, 64]")
+    return int(value)
+
+
 def parse_poly_spec(spec: dict, site: str, heads: int | None = None):
     """One exported nonlinearity (parse_poly_spec,
     native/fideslib_stage0/src/stage1_mamba2_payload.cpp:153-204, and
@@ -512,16 +522,19 @@ def parse_poly_spec(spec: dict, site: str, heads: int | None = None):
                 raise PayloadError("decay_exp head_mask must contain one value per head")
             if np.any((mask != 0.0) & (mask != 1.0)):
                 raise PayloadError("decay_exp head_mask values must be zero or one")
-        return ResquaredExp(need_base(), int(spec.get("squarings", 0)), mask)
+        return ResquaredExp(need_base(), _count(spec, "squarings", 0), mask)
     if kind == "const-newton":
         guess = float(spec["guess"])
         if guess <= 0.0:
             raise PayloadError("const-newton guess must be positive")
-        return ConstNewton(guess, int(spec["iterations"]))
+        return ConstNewton(guess, _count(spec, "iterations"))
     if kind == "poly-newton":
-        return PolyNewton(need_base(), int(spec["iterations"]))
+        return PolyNewton(need_base(), _count(spec, "iterations"))
     if kind == "sq-poly-newton":
-        return SquaredPolyNewton(need_base(), int(spec["iterations"]), float(spec["damping"]))
+        damping = float(spec["damping"])
+        if not 0.0 < damping <= 1.0:
+            raise PayloadError("sq-poly-newton damping must be in (0, 1]")
+        return SquaredPolyNewton(need_base(), _count(spec, "iterations"), damping)
     raise PayloadError(f"unsupported exported polynomial kind: {kind}")
 
 
@@ -653,6 +666,8 @@ def read_layer_payload(dirpath, index: int = 0) -> LayerPayload:
         eps_block, eps_gated = float(meta["eps"]["block_norm"]), float(meta["eps"]["gated_norm"])
         specs = meta["polys"]
         manifest = meta["tensors"]
+        if meta.get("dtype", "float32-le") != "float32-le":
+            raise PayloadError("tensor dtype must be float32-le")
     except KeyError as e:
         raise PayloadError(f"meta.json key not found: {e.args[0]}") from e
     H = dims["num_heads"]
@@ -741,6 +756,8 @@ def read_chain_payload(dirpath, max_layers: int = 0, autoregressive: bool = True
         if not isinstance(final_spec, ScheduledInvSqrt):
             raise PayloadError("dedicated final norm requires a scheduled normalization recipe")
     manifest = meta["tensors"]
+    if meta.get("dtype", "float32-le") != "float32-le":
+        raise PayloadError("tensor dtype must be float32-le")
     for name in ("final_norm_w", "chain_input_embeddings", "chain_expected_final"):
         if name not in manifest:
             raise PayloadError(f"chain.json key not found: {name}")

@@ -211,6 +211,10 @@ def _edit(path, fn):
     ("tensor", "tensor size mismatch for conv_b"),
     ("protocol", "unsupported autoregressive payload protocol"),
     ("time_step", "time_step_limit"),
+    ("dtype", "float32-le"),
+    ("squarings", "squarings must be an integer"),
+    ("iterations", "iterations must be an integer"),
+    ("damping", "damping must be in"),
 ])
 def test_payload_errors(tmp_path, case, message):
     d = _copy(tmp_path)
@@ -231,6 +235,10 @@ def test_payload_errors(tmp_path, case, message):
         "tensor": (layer, lambda m: m["tensors"].update(conv_b=[193])),
         "protocol": (chain, lambda m: m["autoregressive"].update(protocol="server-side")),
         "time_step": (layer, lambda m: m.update(time_step_limit=[0.0, 100.0])),
+        "dtype": (chain, lambda m: m.update(dtype="float16-le")),
+        "squarings": (layer, lambda m: m["polys"]["decay_exp"].update(squarings=-1)),
+        "iterations": (layer, lambda m: m["polys"]["rms_invsqrt"].update(iterations=2.5)),
+        "damping": (layer, lambda m: m["polys"]["gated_rms_invsqrt"].update(damping=1.5)),
     }
     path, fn = edits[case]
     _edit(path, fn)
