@@ -418,10 +418,19 @@ class PlaintextCache:
 class EncryptedMamba2Layer:
     """The layer on ciphertexts of one CryptoContext (full packing)."""
 
+    # Levels each refresh point must leave for what follows it (plus the
+    # margin): the layer input before a Chebyshev-seeded norm (rms), the normed
+    # input before in_proj (u), the projection feeding the conv, dt and gate
+    # branches (proj), the conv FIFO entries (xbc), the packed SSM inputs
+    # (pack), the carried states (state), the readout before the gate (y) and
+    # the normed gated value before out_proj (gn).
+    NEEDS = {"rms": 14, "u": 2, "proj": 19, "xbc": 2, "pack": 8, "state": 4, "y": 2, "gn": 2}
+
     def __init__(self, cc, W: Mamba2Weights, P: Mamba2Polys, passes: int = 2, margin: int = 4,
-                 cache: PlaintextCache | None = None):
+                 cache: PlaintextCache | None = None, needs: dict | None = None):
         self.cc, self.W, self.P = cc, W, P
         self.passes, self.margin = passes, margin
+        self.needs = dict(self.NEEDS, **(needs or {}))
         self.cache = cache if cache is not None else PlaintextCache(0)
         self.rep = {"w_in": ReplicatedLayout(W.proj_dim, W.d_model, cc.slots),
                     "w_out": ReplicatedLayout(W.d_model, W.d_inner, cc.slots)}
@@ -537,7 +546,7 @@ class EncryptedMamba2Layer:
             x = self._fit(x, 2, bounds[key], key)
             y = self._fit(y, 2, bounds[prefix + "_y"], prefix + "_y")
             return self.pm.scale_rows(x, y, width, weight)
-        x = self._fit(x, 14, bounds[key], key)
+        x = self._fit(x, self.needs["rms"], bounds[key], key)
         return self.pm.rms_norm(x, width, weight, eps, (seed.lo, seed.hi), degree=len(seed.coeffs) - 1)
 
     # ---- one token ------------------------------------------------------------
@@ -554,12 +563,13 @@ class EncryptedMamba2Layer:
         E, S, H, Dm = W.d_inner, W.d_state, W.heads, W.d_model
         cd = W.conv_dim
         u = self._rms(h, Dm, W["norm_w"], P.rsqrt1, bounds, "h", "n1", W.eps)
-        u = self._fit(u, 2, bounds["u"], "u")
+        u = self._fit(u, self.needs["u"], bounds["u"], "u")
         proj = self._linear(u, "w_in")
-        proj = self._fit(proj, 19, bounds["proj"], "proj")
+        proj = self._fit(proj, self.needs["proj"], bounds["proj"], "proj")
         # xBC stream at [0, conv_dim) and the causal conv
         xbc = self.pm._mul_mask(c.EvalRotate(proj, E), self.pm._block_mask(0, cd))
-        window = [self._fit(w, 2, bounds["xbc"], "xbc") if w is not None else None for w in conv_state] + [xbc]
+        window = [self._fit(w, self.needs["xbc"], bounds["xbc"], "xbc") if w is not None else None
+                  for w in conv_state] + [xbc]
         taps = []
         for k in range(W.conv_kernel):
             t = np.zeros(c.slots)
@@ -604,10 +614,10 @@ class EncryptedMamba2Layer:
             adt = self._fit(self.pm._mul_mask(dts, avec), self._need(P.exp), bounds["adt"], "adt")
             decay = self._poly(adt, P.exp, 0, H)
             pack = c.EvalAdd(pack, c.EvalRotate(decay, -self.decay_base))
-        pack = self._fit(pack, 8, bounds["pack"], "pack")
+        pack = self._fit(pack, self.needs["pack"], bounds["pack"], "pack")
         # state update and readout from the packed inputs
         if ssm_state is not None:
-            ssm_state = [self._fit(st, 4, bounds["state"], "state") for st in ssm_state]
+            ssm_state = [self._fit(st, self.needs["state"], bounds["state"], "state") for st in ssm_state]
         states, y = self.pm.step(ssm_state, pack, pack, pack if ssm_state is not None else None)
         dvec = np.zeros(c.slots)
         dvec[:E] = np.repeat(W["d"], W.head_dim)
@@ -616,10 +626,10 @@ class EncryptedMamba2Layer:
         z = self.pm._mul_mask(proj, self.pm._block_mask(0, E))
         z = self._fit(z, self._need(P.silu_z), bounds["z"], "z")
         sz = self._poly(z, P.silu_z, 0, E)
-        y = self._fit(y, 2, bounds["y"], "y")
+        y = self._fit(y, self.needs["y"], bounds["y"], "y")
         g = c.EvalMult(y, sz)
         gn = self._rms(g, E, W["gn_w"], P.rsqrt2, bounds, "g", "n2", getattr(W, "gated_eps", W.eps))
-        gn = self._fit(gn, 2, bounds["gn"], "gn")
+        gn = self._fit(gn, self.needs["gn"], bounds["gn"], "gn")
         out = self._linear(gn, "w_out")
         h_out = c.EvalAdd(h, out)
         return h_out, window[1:], states
@@ -756,10 +766,11 @@ class EncryptedMamba2Model:
     """The model's layers on one CryptoContext; client-side encryption and
     selection around them."""
 
-    def __init__(self, cc, model: Mamba2Model, passes: int = 2, cache_gb: float = 40.0):
+    def __init__(self, cc, model: Mamba2Model, passes: int = 2, cache_gb: float = 40.0, margin: int = 4,
+                 needs: dict | None = None):
         self.cc, self.m = cc, model
         self.cache = PlaintextCache(cache_gb * 2 ** 30)
-        self.layers = [EncryptedMamba2Layer(cc, W, P, passes=passes, cache=self.cache)
+        self.layers = [EncryptedMamba2Layer(cc, W, P, passes=passes, margin=margin, cache=self.cache, needs=needs)
                        for W, P in zip(model.layers, model.polys)]
         self.state = [([None] * (W.conv_kernel - 1), None) for W in model.layers]
         self.tokens, self.margins = [], []
