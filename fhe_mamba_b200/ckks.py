@@ -339,6 +339,17 @@ class CryptoContext:
         call("fhe_ctx_counters", self.h, ctypes.cast(a, vp), int(reset))
         return dict(zip(self._COUNTERS, (int(v) for v in a)))
 
+    def level_counts(self):
+        """The ModUps, key inner products, rescales and tensor products since the
+        last counter reset, by the number of live Q limbs they ran at:
+        {kind: {nq: count}} for the non-zero entries."""
+        out = {}
+        for kind, name in enumerate(("modup", "key_inner", "rescale", "tensor")):
+            a = (ctypes.c_uint64 * 64)()
+            call("fhe_ctx_level_counts", self.h, kind, ctypes.cast(a, vp), 64)
+            out[name] = {i: int(v) for i, v in enumerate(a) if v}
+        return out
+
     def bootstrap_info(self):
         c, d, k = ctypes.c_int32(), ctypes.c_uint32(), ctypes.c_uint32()
         call("fhe_bootstrap_info", self.h, ctypes.byref(c), ctypes.byref(d), ctypes.byref(k))

@@ -712,6 +712,18 @@ int fhe_ctx_counters(fhe_ctx* ctx, fhe_counters* out, int32_t reset) {
   });
 }
 
+int fhe_ctx_level_counts(fhe_ctx* ctx, int32_t kind, uint64_t* out, uint32_t n) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(out != nullptr, "null level counts");
+    const fhe::Counters& c = k.counters;
+    const uint64_t* src = kind == 0 ? c.modup_at : kind == 1 ? c.key_inner_at : kind == 2 ? c.rescale_at
+                          : kind == 3 ? c.tensor_at : nullptr;
+    fhe::require(src != nullptr, "level count kind must be 0 (ModUp), 1 (key inner product), 2 (rescale) or 3 (tensor)");
+    for (uint32_t i = 0; i < n; ++i) out[i] = i < fhe::Counters::kLevels ? src[i] : 0;
+  });
+}
+
 int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, uint32_t slots,
                         int32_t correction, int32_t s2c_first, uint32_t sparse_h) {
   return guarded([&] {

@@ -625,6 +625,7 @@ void Ckks::modup(const uint64_t* d, uint32_t nq, uint64_t* ext) {
   launch_modup(coef, d, ext, nq, ctx.K, n, T.digits.as<ModUpDigit>(), T.D, ctx.alpha, ctx.d_mod.as<Modulus>(),
                ctx.stream, ctx.max_prime() < (uint64_t(1) << 60));
   ++counters.modup;
+  ++counters.modup_at[Counters::slot(nq)];
   if (T.ntt_list_len) {
     counters.ntt_limbs += T.ntt_list_len;
     NttArgs a = ctx.ntt_args(ext, 1, 0, T.ntt_list_len, 0);
@@ -664,6 +665,7 @@ void Ckks::keyswitch(const uint64_t* d, uint32_t nq, const uint64_t* evk, uint64
   uint64_t* acc = ws(2, (size_t)2 * (ctx.L + K) * n);
   modup(d, nq, ext);
   ++counters.key_inner;
+  ++counters.key_inner_at[Counters::slot(nq)];
   launch_key_inner(ext, T.D, w, evk, ctx.L + K, PrimeMap{nq, ctx.L}, acc, n, ctx.d_mod.as<Modulus>(), ctx.stream);
   moddown_pair(acc, nq, out, so, add_c0);
 }
@@ -714,6 +716,7 @@ std::vector<std::unique_ptr<Ct>> Ckks::rotate_hoisted(const Ct& a, const std::ve
   for (uint64_t g : gs) {
     ++counters.rotations;
     ++counters.key_inner;
+    ++counters.key_inner_at[Counters::slot(nq)];
     launch_key_inner(ext, T.D, w, rot_.at(g).as<uint64_t>(), ctx.L + K, PrimeMap{nq, ctx.L}, acc, n,
                      ctx.d_mod.as<Modulus>(), ctx.stream);
     moddown_pair(acc, nq, u, so, a.data());
@@ -931,6 +934,7 @@ std::unique_ptr<Ct> Ckks::tensor(const Ct& a, const Ct& b) {
   const uint32_t nq = a.nq, n = ctx.n;
   auto d = alloc(nq, 3);
   ++counters.tensor;
+  ++counters.tensor_at[Counters::slot(nq)];
   launch_tensor(a.data(), (size_t)a.cap * n, b.data(), (size_t)b.cap * n, d->data(), (size_t)nq * n, nq, n,
                 ctx.d_mod.as<Modulus>(), ctx.stream);
   d->scale = a.scale * b.scale;
@@ -955,6 +959,7 @@ void Ckks::rescale_into(const Ct& a, Ct& o) {
   const uint32_t nq = a.nq, n = ctx.n, nc = a.ncomp;
   const size_t cs = (size_t)a.cap * n, os = (size_t)o.cap * n;
   ++counters.rescales;
+  ++counters.rescale_at[Counters::slot(nq)];
   uint64_t* last = ws(6, (size_t)nc * n);
   {  // last[c] = INTT(limb nq-1 of component c), out of place
     counters.ntt_limbs += nc;

@@ -49,6 +49,13 @@ struct LevelTables {
 struct Counters {
   uint64_t tensor = 0, relin = 0, rotations = 0, modup = 0, moddown = 0, key_inner = 0, rescales = 0,
            ntt_limbs = 0, bootstraps = 0;
+  // The same work by the number of live Q limbs it ran at (index nq, the
+  // last slot collects nq >= kLevels - 1): ModUps, key inner products (each
+  // followed by its ModDown), rescales and tensor products.  A cost model of
+  // another implementation multiplies these by its own per-level times.
+  static constexpr uint32_t kLevels = 64;
+  uint64_t modup_at[kLevels] = {}, key_inner_at[kLevels] = {}, rescale_at[kLevels] = {}, tensor_at[kLevels] = {};
+  static uint32_t slot(uint32_t nq) { return nq < kLevels ? nq : kLevels - 1; }
 };
 
 class Ckks {

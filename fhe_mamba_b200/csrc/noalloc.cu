@@ -15,6 +15,7 @@
 #include "../../include/fhe_b200.h"
 #include "ckks_kernels.h"
 #include "context.h"
+#include "launch_count.h"
 
 namespace fhe {
 namespace {
@@ -43,6 +44,21 @@ uint64_t* scratch_for(int device) {
   return g_ptr[device];
 }
 
+// out[i] = q_last^{-1} mod q_i with its Shoup companion, for i < count
+// (q_last = mods[last].q): Fermat's inverse (every q_i is prime) by square
+// and multiply, computed on the device so that no host buffer is involved.
+__global__ void k_qinv_table(const Modulus* mods, uint32_t last, uint32_t count, Shoup* out) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= count) return;
+  const Modulus& m = mods[i];
+  uint64_t base = mods[last].q % m.q, v = 1;
+  for (uint64_t e = m.q - 2; e; e >>= 1) {
+    if (e & 1) v = mul_mod(v, base, m);
+    base = mul_mod(base, base, m);
+  }
+  out[i] = Shoup{v, (uint64_t)(((unsigned __int128)v << 64) / m.q)};
+}
+
 }  // namespace
 
 // Words of scratch a rescale of ncomp x n_limbs needs.
@@ -55,6 +71,11 @@ void rescale_noalloc(Context& c, const uint64_t* in, uint32_t ncomp, uint32_t nq
   require(ncomp >= 1 && ncomp <= 3, "ncomp must be 1, 2 or 3");
   require(nq >= 2 && nq <= c.L && nq <= 64, "n_limbs must be in [2, min(number of Q primes, 64)]");
   const uint32_t n = c.n;
+  {  // limb i of `out` is written while later limbs of `in` are still to be read
+    const uintptr_t i0 = reinterpret_cast<uintptr_t>(in), i1 = i0 + (size_t)ncomp * nq * n * 8;
+    const uintptr_t o0 = reinterpret_cast<uintptr_t>(out), o1 = o0 + (size_t)ncomp * (nq - 1) * n * 8;
+    require(o1 <= i0 || i1 <= o0, "fhe_rescale_noalloc: out must not overlap in");
+  }
   const size_t need = noalloc_rescale_words(ncomp, nq, n);
   require(need <= kScratchWords,
           "fhe_rescale_noalloc: needs " + std::to_string(need * 8) + " bytes of scratch, above the fixed " +
@@ -66,15 +87,10 @@ void rescale_noalloc(Context& c, const uint64_t* in, uint32_t ncomp, uint32_t nq
   uint64_t* last = base + 2 * (size_t)(nq - 1);
   uint64_t* lifted = last + (size_t)ncomp * n;
   const uint64_t ql = c.primes[nq - 1];
-  Shoup tab[63];
-  for (uint32_t i = 0; i + 1 < nq; ++i) {
-    const uint64_t q = c.primes[i];
-    const uint64_t v = nt::invmod(ql % q, q);
-    tab[i] = Shoup{v, nt::shoup(v, q)};
-  }
-  // Every scratch word below is written before it is read; nothing needs to
-  // start at zero.
-  FHE_CUDA(cudaMemcpyAsync(qinv, tab, sizeof(Shoup) * (nq - 1), cudaMemcpyHostToDevice, c.stream));
+  // Every scratch word below is written before it is read, on the caller's
+  // context stream; nothing needs to start at zero.
+  k_qinv_table<<<1, 64, 0, c.stream>>>(c.d_mod.as<Modulus>(), nq - 1, nq - 1, qinv);
+  note_launch();
   const size_t is = (size_t)nq * n, os = (size_t)(nq - 1) * n;
   FHE_CUDA(cudaMemcpy2DAsync(last, (size_t)n * 8, in + (size_t)(nq - 1) * n, is * 8, (size_t)n * 8, ncomp,
                              cudaMemcpyDeviceToDevice, c.stream));

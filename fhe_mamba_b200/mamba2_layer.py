@@ -46,8 +46,12 @@ class Poly:
     lo: float
     hi: float
 
+    def position(self, x):
+        """Where x falls on the interval: -1 at lo, 1 at hi."""
+        return (2 * np.asarray(x, dtype=np.float64) - self.lo - self.hi) / (self.hi - self.lo)
+
     def __call__(self, x):
-        return np.polynomial.chebyshev.chebval((2 * x - self.lo - self.hi) / (self.hi - self.lo), self.coeffs)
+        return np.polynomial.chebyshev.chebval(self.position(x), self.coeffs)
 
 
 @dataclass
@@ -98,17 +102,36 @@ class Mamba2Weights:
 
 
 def _rms(x, w, eps):
-    return x / np.sqrt(np.mean(x * x) + eps) * w
+    return x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps) * w
+
+
+def _split_proj(W: Mamba2Weights, proj):
+    E = W.d_inner
+    return proj[..., :E], proj[..., E:E + W.conv_dim], proj[..., E + W.conv_dim:]
+
+
+def _split_xa(W: Mamba2Weights, xa):
+    E, S = W.d_inner, W.d_state
+    return xa[..., :E].reshape(xa.shape[:-1] + (W.heads, W.head_dim)), xa[..., E:E + S], xa[..., E + S:]
+
+
+def _ssm(st, decay, dts, x, B, C, d):
+    """S <- decay S + (dt x) (x) B (S = update when there is no state yet) and
+    y = S C + D x, over any leading batch axes."""
+    upd = np.einsum("...hp,...n->...hpn", dts[..., :, None] * x, B)
+    if st is not None:
+        upd += decay[..., :, None, None] * st
+    return upd, np.einsum("...hpn,...n->...hp", upd, C) + d[:, None] * x
 
 
 def exact_step(W: Mamba2Weights, h, conv, st, upd=lambda k, v: None):
     """The layer with the exact nonlinearities (calibration); upd(site, values)
-    observes the inputs of every polynomial and inverse square root."""
-    E, S, H, K, Pd = W.d_inner, W.d_state, W.heads, W.conv_kernel, W.head_dim
-    upd("v1", [np.mean(h * h) + W.eps])
+    observes the inputs of every polynomial and inverse square root.  h may
+    carry leading batch axes (one row per calibration sequence)."""
+    K = W.conv_kernel
+    upd("v1", np.mean(h * h, axis=-1) + W.eps)
     u = _rms(h, W["norm_w"], W.eps)
-    proj = W["w_in"] @ u
-    z, xbc, dt = proj[:E], proj[E:E + W.conv_dim], proj[E + W.conv_dim:]
+    z, xbc, dt = _split_proj(W, u @ W["w_in"].T)
     window = list(conv) + [xbc]
     xc = sum(W["conv_w"][:, k] * window[k] for k in range(K)) + W["conv_b"]
     upd("xc", xc)
@@ -117,12 +140,11 @@ def exact_step(W: Mamba2Weights, h, conv, st, upd=lambda k, v: None):
     dts = _softplus(dt + W["dt_bias"])
     upd("adt", W["a"] * dts)
     upd("z", z)
-    x, B, C = xa[:E].reshape(H, Pd), xa[E:E + S], xa[E + S:]
-    st = np.exp(W["a"] * dts)[:, None, None] * st + (dts[:, None] * x)[:, :, None] * B[None, None, :]
-    y = (st * C[None, None, :]).sum(-1) + W["d"][:, None] * x
-    g = y.reshape(E) * _silu(z)
-    upd("v2", [np.mean(g * g) + W.eps])
-    out = W["w_out"] @ _rms(g, W["gn_w"], W.eps)
+    x, B, C = _split_xa(W, xa)
+    st, y = _ssm(st, np.exp(W["a"] * dts), dts, x, B, C, W["d"])
+    g = y.reshape(y.shape[:-2] + (W.d_inner,)) * _silu(z)
+    upd("v2", np.mean(g * g, axis=-1) + W.eps)
+    out = _rms(g, W["gn_w"], W.eps) @ W["w_out"].T
     return h + out, window[1:], st
 
 
@@ -154,8 +176,11 @@ class HeadPoly:
         """Head h interpolates t -> fn(params[h], t) at Chebyshev nodes."""
         return cls(np.stack([cheb_fit(lambda t, q=q: fn(q, t), lo, hi, degree) for q in params], axis=1), lo, hi)
 
+    def position(self, x):
+        return (2.0 * np.asarray(x, dtype=np.float64) - self.lo - self.hi) / (self.hi - self.lo)
+
     def __call__(self, x):
-        t = (2.0 * np.asarray(x, dtype=np.float64) - self.lo - self.hi) / (self.hi - self.lo)
+        t = self.position(x)
         b1 = np.zeros_like(t)
         b2 = np.zeros_like(t)
         for c in self.coeffs[:0:-1]:
@@ -251,49 +276,32 @@ class Mamba2Polys:
         return Poly(cheb_fit(fn, lo, hi, degree), lo, hi)
 
 
-def plain_rms(x, w, eps, seed, newton=2, rec=None, key=None):
+def plain_rms(x, w, eps, seed, newton=2, rec=None, key=None, dom=None):
     """x * rsqrt(mean(x^2) + eps) * w.  `seed` is a Chebyshev seed refined by
     `newton` Newton steps, or an inverse square root with its own refinement
     (an object with ``inv_sqrt``, as a chain payload exports them); rec(key_*)
     then observes the variance and every iterate, at the variance and at the
-    value that fills the slots outside the vector."""
-    v = np.mean(x * x) + eps
+    value that fills the slots outside the vector.  dom(key, t) observes where
+    the variance falls on a Chebyshev seed's interval (t in [-1, 1] inside)."""
+    v = np.mean(x * x, axis=-1) + eps
     if hasattr(seed, "inv_sqrt"):
         if rec is not None:
             probe = np.array([v, seed.fill])
             rec(key + "_v", probe)
             seed.inv_sqrt(probe, trace=lambda name, val: rec(key + "_" + name, val))
-        return x * seed.inv_sqrt(v) * w
+        return x * np.expand_dims(seed.inv_sqrt(v), -1) * w
+    if dom is not None:
+        dom(key, seed.position(v))
     y = seed(v)
     for _ in range(newton):
         y = 1.5 * y - 0.5 * v * y ** 3
-    return x * y * w
+    return x * np.expand_dims(y, -1) * w
 
 
 def plain_step(W: Mamba2Weights, P: Mamba2Polys, h, conv_state, ssm_state):
     """The layer on plaintext with the same polynomials.  conv_state: list of the
     last conv_kernel-1 xBC vectors (oldest first); ssm_state: [H, P, S] or None."""
-    E, S, H, Pd = W.d_inner, W.d_state, W.heads, W.head_dim
-    u = plain_rms(h, W["norm_w"], W.eps, P.rsqrt1)
-    proj = W["w_in"] @ u
-    z, xbc, dt = proj[:E], proj[E:E + W.conv_dim], proj[E + W.conv_dim:]
-    window = list(conv_state) + [xbc]
-    xc = sum(W["conv_w"][:, k] * window[k] for k in range(W.conv_kernel)) + W["conv_b"]
-    xa = P.silu_x(xc)
-    x, B, C = xa[:E].reshape(H, Pd), xa[E:E + S], xa[E + S:]
-    if getattr(P, "gates", None) is not None:  # joint gates: (write, decay) from one factorisation
-        dts, decay = P.gates(dt + W["dt_bias"])
-    else:
-        dts = P.softplus(dt + W["dt_bias"])
-        fused = getattr(P, "decay", None)
-        decay = fused(dt + W["dt_bias"]) if fused is not None else P.exp(W["a"] * dts)
-    upd = (dts[:, None] * x)[:, :, None] * B[None, None, :]
-    st = upd if ssm_state is None else decay[:, None, None] * ssm_state + upd
-    y = (st * C[None, None, :]).sum(-1) + W["d"][:, None] * x
-    g = y.reshape(E) * P.silu_z(z)
-    gn = plain_rms(g, W["gn_w"], getattr(W, "gated_eps", W.eps), P.rsqrt2)
-    out = W["w_out"] @ gn
-    return h + out, window[1:], st
+    return poly_step_record(W, P, h, conv_state, ssm_state, lambda k, v: None)
 
 
 def rect_diagonals(Wm: np.ndarray, baby: int, giant: int, slots: int):
@@ -635,50 +643,55 @@ class EncryptedMamba2Layer:
         return h_out, window[1:], states
 
 
-def poly_step_record(W: Mamba2Weights, P: Mamba2Polys, h, conv, st, rec):
-    """plain_step that reports the magnitude of every refreshed intermediate."""
-    E, S, H, Pd = W.d_inner, W.d_state, W.heads, W.head_dim
+def poly_step_record(W: Mamba2Weights, P: Mamba2Polys, h, conv, st, rec, dom=None):
+    """The layer on plaintext with the polynomials, reporting the magnitude of
+    every refreshed intermediate (rec(site, values)) and, when dom is given,
+    where every Chebyshev input falls on its interval (dom(name, t), |t| <= 1
+    inside).  h may carry leading batch axes."""
+    def at(name, p, x):
+        if dom is not None and isinstance(p, (Poly, HeadPoly)):
+            dom(name, p.position(x))
+        return x
+
     rec("h", h)
-    u = plain_rms(h, W["norm_w"], W.eps, P.rsqrt1, rec=rec, key="n1")
+    u = plain_rms(h, W["norm_w"], W.eps, P.rsqrt1, rec=rec, key="n1", dom=dom)
     rec("u", u)
-    proj = W["w_in"] @ u
+    proj = u @ W["w_in"].T
     rec("proj", proj)
-    z, xbc, dt = proj[:E], proj[E:E + W.conv_dim], proj[E + W.conv_dim:]
+    z, xbc, dt = _split_proj(W, proj)
     rec("xbc", xbc)
     rec("z", z)
     window = list(conv) + [xbc]
     xc = sum(W["conv_w"][:, k] * window[k] for k in range(W.conv_kernel)) + W["conv_b"]
     rec("xc", xc)
-    xa = P.silu_x(xc)
+    xa = P.silu_x(at("silu_x", P.silu_x, xc))
     rec("xa", xa)
     rec("dt", dt + W["dt_bias"])
     gates = getattr(P, "gates", None)
-    if gates is not None:
+    if gates is not None:  # joint gates: (write, decay) from one factorisation
         dts, decay = gates(dt + W["dt_bias"])
     else:
-        dts = P.softplus(dt + W["dt_bias"])
+        dts = P.softplus(at("softplus", P.softplus, dt + W["dt_bias"]))
         decay = None
         if getattr(P, "decay", None) is not None:
-            decay = P.decay(dt + W["dt_bias"])
+            decay = P.decay(at("decay", P.decay, dt + W["dt_bias"]))
         else:
             rec("adt", W["a"] * dts)
     rec("dts", dts)
     rec("pack", xa)
     rec("pack", dts)
     rec("pack", [1.0])
-    x, B, C = xa[:E].reshape(H, Pd), xa[E:E + S], xa[E + S:]
-    upd_ = (dts[:, None] * x)[:, :, None] * B[None, None, :]
-    if st is not None:
-        decay = P.exp(W["a"] * dts) if decay is None else decay
-    st = upd_ if st is None else decay[:, None, None] * st + upd_
+    x, B, C = _split_xa(W, xa)
+    if st is not None and decay is None:
+        decay = P.exp(at("exp", P.exp, W["a"] * dts))
+    st, y = _ssm(st, decay, dts, x, B, C, W["d"])
     rec("state", st)
-    y = (st * C[None, None, :]).sum(-1) + W["d"][:, None] * x
     rec("y", y)
-    g = y.reshape(E) * P.silu_z(z)
+    g = y.reshape(y.shape[:-2] + (W.d_inner,)) * P.silu_z(at("silu_z", P.silu_z, z))
     rec("g", g)
-    gn = plain_rms(g, W["gn_w"], getattr(W, "gated_eps", W.eps), P.rsqrt2, rec=rec, key="n2")
+    gn = plain_rms(g, W["gn_w"], getattr(W, "gated_eps", W.eps), P.rsqrt2, rec=rec, key="n2", dom=dom)
     rec("gn", gn)
-    out = W["w_out"] @ gn
+    out = gn @ W["w_out"].T
     return h + out, window[1:], st
 
 
@@ -710,7 +723,8 @@ class Mamba2Model:
     native/fideslib_stage0/src/packed_fideslib.cpp:842-880)."""
 
     def __init__(self, layers: int, d_model: int, d_state: int, heads: int, vocab: int, std: float = 0.02,
-                 seed: int = 6, calib_sequences: int = 8, fused_decay: bool = False):
+                 seed: int = 6, calib_sequences: int = 8, calib_tokens: int = 32, calib_prompt: int = 8,
+                 bound_factor: float = 3.0, fused_decay: bool = False):
         self.layers = [Mamba2Weights(d_model=d_model, d_state=d_state, heads=heads, std=std, seed=seed * 1000 + i)
                        for i in range(layers)]
         r = np.random.default_rng(seed)
@@ -718,35 +732,88 @@ class Mamba2Model:
         self.norm_f = 1.0 + r.normal(0, 0.02, d_model)
         eps = self.layers[0].eps
         self.d_model = d_model
-        # calibration through the whole stack: exact-function trajectories from
-        # random prompts give every layer's polynomial domains ...
+        # Calibration through the whole stack, never on the inputs a run is
+        # checked on: calib_sequences token sequences of calib_tokens tokens
+        # from this model's own seed, each a random prompt of calib_prompt
+        # tokens; half continue greedily (the generation protocol, whose
+        # repeated tokens drive the slowly decaying state heads furthest), half
+        # with random tokens.  The horizon must cover the run: the recurrent
+        # state keeps growing for about 1 / (1 - decay) tokens.
+        B, T = calib_sequences, calib_tokens
+        toks = r.integers(0, vocab, (B, T))
+        greedy = np.arange(B) % 2 == 0
         ranges = [new_ranges() for _ in self.layers]
         finals = []
-        seqs = [r.integers(0, vocab, 4) for _ in range(calib_sequences)]
-        for seq in seqs:
-            state = [([np.zeros(W.conv_dim) for _ in range(W.conv_kernel - 1)],
-                      np.zeros((W.heads, W.head_dim, W.d_state))) for W in self.layers]
-            for tok in seq:
-                h = self.embedding[tok]
-                for li, W in enumerate(self.layers):
-                    h, c_, s_ = exact_step(W, h, state[li][0], state[li][1], range_updater(ranges[li]))
-                    state[li] = (c_, s_)
-                finals.append(np.mean(h * h) + eps)
+        state = [([np.zeros((B, W.conv_dim)) for _ in range(W.conv_kernel - 1)],
+                  np.zeros((B, W.heads, W.head_dim, W.d_state))) for W in self.layers]
+        for t in range(T):  # exact-function trajectories give the polynomial domains ...
+            h = self.embedding[toks[:, t]]
+            for li, W in enumerate(self.layers):
+                h, c_, s_ = exact_step(W, h, state[li][0], state[li][1], range_updater(ranges[li]))
+                state[li] = (c_, s_)
+            finals.append(np.mean(h * h, axis=-1) + eps)
+            if calib_prompt <= t + 1 < T:
+                nxt = np.argmax(_rms(h, self.norm_f, eps) @ self.embedding.T, axis=-1)
+                toks[greedy, t + 1] = nxt[greedy]
         self.polys = [Mamba2Polys(W, ranges=rg, fused_decay=fused_decay) for W, rg in zip(self.layers, ranges)]
-        lo, hi = 0.25 * min(finals), 4.0 * max(finals)
+        finals = np.concatenate(finals)
+        lo, hi = 0.25 * float(finals.min()), 4.0 * float(finals.max())
         self.rsqrt_f = Poly(cheb_fit(lambda t: 1 / np.sqrt(t), lo, hi, 15), lo, hi)
-        # ... and the polynomial path's magnitudes give the refresh bounds
+        # ... and the polynomial path's magnitudes over the same tokens the
+        # refresh bounds (bound_factor x the largest magnitude, at least 1:
+        # single random tokens reach almost twice the largest value of a few
+        # hundred calibration tokens)
         mags = [{} for _ in self.layers]
-        for seq in seqs:
-            state = self.initial_state()
-            for tok in seq:
-                h = self.embedding[tok]
-                for li, (W, P) in enumerate(zip(self.layers, self.polys)):
-                    def rec(k, v, m=mags[li]):
-                        m[k] = max(m.get(k, 0.0), float(np.max(np.abs(v))))
-                    h, c_, s_ = poly_step_record(W, P, h, state[li][0], state[li][1], rec)
-                    state[li] = (c_, s_)
-        self.bounds = [{k: max(1.0, 2.0 * v) for k, v in m.items()} for m in mags]
+        final = 0.0
+        state = [([np.zeros((B, W.conv_dim)) for _ in range(W.conv_kernel - 1)], None) for W in self.layers]
+        for t in range(T):
+            h = self.embedding[toks[:, t]]
+            for li, (W, P) in enumerate(zip(self.layers, self.polys)):
+                def rec(k, v, m=mags[li]):
+                    m[k] = max(m.get(k, 0.0), float(np.max(np.abs(v))))
+                h, c_, s_ = poly_step_record(W, P, h, state[li][0], state[li][1], rec)
+                state[li] = (c_, s_)
+            final = max(final, float(np.max(np.abs(h))))
+        self.bounds = [{k: max(1.0, bound_factor * v) for k, v in m.items()} for m in mags]
+        self.final_bound = max(1.0, bound_factor * final)
+        self.calibration = {"sequences": B, "tokens": T, "prompt": calib_prompt, "greedy_sequences": int(greedy.sum()),
+                            "bound_factor": bound_factor, "seed": seed}
+
+    def audit(self, inputs):
+        """The plaintext polynomial path over one sequence of input tokens, as
+        the encrypted loop runs it: for every refresh site the largest
+        |value| / bound (above 1 the refresh leaves its interval), and for every
+        Chebyshev series the largest |position| of its input on its interval
+        (above 1 the series extrapolates), each with the evaluation and layer
+        where it falls.  The final hidden vector's refresh counts as layer
+        len(layers)."""
+        ratio, dom = {}, {}
+
+        def keep(table, k, r, e, li):
+            if r > table.get(k, {"max": -1.0})["max"]:
+                table[k] = {"max": r, "eval": e, "layer": li}
+
+        state = self.initial_state()
+        for e, tok in enumerate(inputs):
+            h = self.embedding[tok].copy()
+            for li, (W, P) in enumerate(zip(self.layers, self.polys)):
+                b = self.bounds[li]
+
+                def rec(k, v, li=li, b=b):
+                    if k in b:
+                        keep(ratio, k, float(np.max(np.abs(v))) / b[k], e, li)
+
+                def dm(k, t, li=li):
+                    keep(dom, k, float(np.max(np.abs(t))), e, li)
+
+                h, c_, s_ = poly_step_record(W, P, h, state[li][0], state[li][1], rec, dm)
+                state[li] = (c_, s_)
+            keep(ratio, "final", float(np.max(np.abs(h))) / self.final_bound, e, len(self.layers))
+            keep(dom, "rsqrt_f", float(np.max(np.abs(self.rsqrt_f.position(np.mean(h * h) + self.layers[0].eps)))),
+                 e, len(self.layers))
+        return {"bound_ratio": ratio, "domain": dom,
+                "max_bound_ratio": max(v["max"] for v in ratio.values()),
+                "max_domain_position": max(v["max"] for v in dom.values())}
 
     def initial_state(self):
         return [([np.zeros(W.conv_dim) for _ in range(W.conv_kernel - 1)], None) for W in self.layers]
@@ -791,7 +858,7 @@ class EncryptedMamba2Model:
             new.append((conv, st))
         self.state = new
         last = self.layers[-1]
-        h = last._fit(h, 14, m.bounds[-1]["h"] * 2)
+        h = last._fit(h, 14, m.final_bound)
         return last.pm.rms_norm(h, m.d_model, m.norm_f, m.layers[0].eps, (m.rsqrt_f.lo, m.rsqrt_f.hi),
                                 degree=len(m.rsqrt_f.coeffs) - 1)
 

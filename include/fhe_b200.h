@@ -300,6 +300,13 @@ typedef struct fhe_counters {
   uint64_t tensor, relin, rotations, modup, moddown, key_inner, rescales, ntt_limbs, bootstraps;
 } fhe_counters;
 int fhe_ctx_counters(fhe_ctx* ctx, fhe_counters* out, int32_t reset);
+/* The same counters by the number of live Q limbs the work ran at: out[nq]
+ * for nq < n (the last of 64 entries collects nq >= 63).  kind 0 = ModUps,
+ * 1 = key inner products (each followed by one ModDown), 2 = rescales,
+ * 3 = tensor products.  Reset together with fhe_ctx_counters(reset).  No
+ * counterpart call in the reference: its native.json reports totals only
+ * (packed_fideslib.cpp:1239-1396); these weight a CPU cost model by level. */
+int fhe_ctx_level_counts(fhe_ctx* ctx, int32_t kind, uint64_t* out, uint32_t n);
 
 /* Bootstrapping of the context's slots (full packing N/2, or sparse packing:
  * a power of two below N/2, where ModRaise is followed by the trace over the
@@ -412,15 +419,16 @@ int fhe_chebyshev(fhe_ctx* ctx, const fhe_ct* a, const double* coeffs, uint32_t 
  * device memory when they rescale — code working inside a memory budget
  * reserved in advance, or a host framework that owns every device allocation.
  * `in` holds device residues [ncomp][n_limbs][N] (NTT form), `out` receives
- * [ncomp][n_limbs-1][N] (must not overlap `in`); the result equals
- * fhe_rescale word for word.  Scratch comes from one fixed 32 MiB device
- * array that every GPU loading this library keeps until the process exits;
- * sizes needing more (2(n_limbs-1) + ncomp*N*n_limbs words) are rejected with
- * FHE_ERR_INVALID.  The first call on each device looks up that array's
- * device address, so make it before any stream capture.  All calls share the
- * one array, so calls whose GPU work overlaps (other contexts, other streams)
- * race; the array keeps the last call's contents, and every word a call reads
- * was written earlier by the same call. */
+ * [ncomp][n_limbs-1][N] and must not overlap `in` (rejected with
+ * FHE_ERR_INVALID); the result equals fhe_rescale word for word.  Scratch
+ * comes from one fixed 32 MiB device array that every GPU loading this
+ * library keeps until the process exits; sizes needing more (2(n_limbs-1) +
+ * ncomp*N*n_limbs words) are rejected with FHE_ERR_INVALID.  The first call
+ * on each device looks up that array's device address (set-up once per
+ * device), so make that first call before any stream capture.  All calls
+ * share the one array, so calls whose GPU work overlaps (other contexts,
+ * other streams) race; the array keeps the last call's contents, and every
+ * word a call reads was written earlier by the same call. */
 int fhe_rescale_noalloc(fhe_ctx* ctx, const uint64_t* in, uint32_t ncomp, uint32_t n_limbs, uint64_t* out);
 
 #ifdef __cplusplus

@@ -299,3 +299,27 @@ def test_library_refresh_matches_host_refresh(boot_ctx):
     host = cc.Decrypt(cc.host_refresh(ct, 8.0, passes=2)).GetRealPackedValue()
     assert np.max(np.abs(two - x)) < 1e-5 and np.max(np.abs(two - x)) < np.max(np.abs(one - x)) / 10
     assert np.max(np.abs(two - host)) < 1e-5
+
+
+def test_bootstrap_at_token_loop_parameters():
+    """The token loop's own parameter set (N = 2^16, 2^15 slots, depth 44,
+    59/60-bit primes, dnum 3, level budget {4, 4}, uniform ternary secret): a
+    2-limb input comes back with 24 limbs within 5e-4 (one bootstrap), and a
+    two-pass refresh of values up to a bound of 4 within 1e-5."""
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    cc = CryptoContext(CCParams(ring_dim=1 << 16, multiplicative_depth=44, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3))
+    cc.KeyGen(SEED)
+    cc.EvalBootstrapSetup((4, 4))
+    cc.EvalBootstrapKeyGen()
+    x = np.random.default_rng(16).uniform(-1, 1, cc.slots)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    cc.LevelReduceInPlace(ct, cc.n_q - 2)
+    out = cc.EvalBootstrap(ct)
+    assert out.n_limbs() == 24
+    assert np.max(np.abs(cc.Decrypt(out).GetRealPackedValue() - x)) < 5e-4
+    ct4 = cc.Encrypt(cc.MakeCKKSPackedPlaintext(4 * x))
+    cc.LevelReduceInPlace(ct4, cc.n_q - 3)
+    two = cc.Decrypt(cc.EvalRefresh(ct4, 4.0, passes=2)).GetRealPackedValue()
+    assert np.max(np.abs(two - 4 * x)) < 1e-5
+    cc.close()

@@ -121,6 +121,27 @@ def test_rotation_and_hoisting_match_oracle(cfg1):
             assert np.array_equal(h.residues(), want), (nq, st)
 
 
+def test_config1_rotation_sweep_matches_oracle(cfg1):
+    """BASELINE config 1's HRotate by {1, 2, 4, ..., 4096}: every rotation key
+    and every rotated ciphertext word for word against the oracle at the top
+    level, and the decrypted slots equal the rotated message."""
+    cc, oc, s, sn = cfg1
+    steps = [1 << k for k in range(13)]
+    cc.EvalRotateKeyGen(steps)
+    a = _rand_ct(oc, oc.L, 4096)
+    ga = cc.upload(a)
+    x = _msg(cc.slots, 4097)
+    cx = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    for st in steps:
+        g = cc.galois_element(st)
+        assert g == oc.galois(st)
+        rk = oc.rot_key(SEED, s, sn, g)
+        assert np.array_equal(cc.key(3, g).reshape(rk.shape), rk), st
+        assert np.array_equal(cc.EvalRotate(ga, st).residues(), oc.rotate(a, g, rk)), st
+        got = cc.Decrypt(cc.EvalRotate(cx, st)).GetRealPackedValue()
+        assert np.max(np.abs(got - np.roll(x, -st))) < 1e-4, st
+
+
 def test_conjugate_matches_oracle(cfg1):
     cc, oc, s, sn = cfg1
     cc.EvalConjugateKeyGen()

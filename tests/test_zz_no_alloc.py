@@ -50,6 +50,35 @@ def test_noalloc_rescale_matches_fhe_rescale_twice():
         assert np.array_equal(got, want), f"call {call}"
 
 
+@pytest.mark.parametrize("ncomp", [1, 3])
+def test_noalloc_rescale_one_and_three_components(ncomp):
+    """A single residue polynomial (compared with component 0 of a two-component
+    rescale: rescaling works on each component alone) and a 3-component
+    product before relinearisation."""
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    cc = CryptoContext(CCParams(ring_dim=1 << 14, multiplicative_depth=8, scaling_mod_size=50,
+                                first_mod_size=60, num_large_digits=2))
+    x = _rand_ct(cc.q, cc.n_q, cc.n, 200 + ncomp)
+    if ncomp == 3:
+        x = np.concatenate([x, _rand_ct(cc.q, cc.n_q, cc.n, 300)[:1]])
+    ref = cc.upload(x, noise_deg=2 if ncomp == 3 else 1)
+    cc.RescaleInPlace(ref)
+    want = ref.residues()[:ncomp]
+    for _ in range(2):
+        assert np.array_equal(_noalloc(cc, x[:ncomp]), want)
+
+
+def test_noalloc_rejects_overlapping_output():
+    import torch
+    from fhe_mamba_b200 import CCParams, CryptoContext, InvalidArgument, _lib
+    cc = CryptoContext(CCParams(ring_dim=1 << 14, multiplicative_depth=8, scaling_mod_size=50,
+                                first_mod_size=60, num_large_digits=2))
+    buf = torch.zeros(2 * cc.n_q * cc.n, dtype=torch.int64, device="cuda")
+    shifted = ctypes.c_void_p(buf.data_ptr() + cc.n * 8)
+    with pytest.raises(InvalidArgument, match="overlap"):
+        _lib.call("fhe_rescale_noalloc", cc.h, ctypes.c_void_p(buf.data_ptr()), 2, cc.n_q, shifted)
+
+
 def test_noalloc_rejects_sizes_above_its_fixed_scratch():
     import torch
     from fhe_mamba_b200 import CCParams, CryptoContext, InvalidArgument, _lib
