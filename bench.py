@@ -468,7 +468,7 @@ class TokenLoop:
         self.cc.synchronize()
         self.setup_seconds = time.perf_counter() - t0
         self.stream = torch.cuda.ExternalStream(self.cc.stream_ptr(), device=torch.device("cuda", local))
-        self.inputs, self.hidden, self.eval_ms = [], [], []
+        self.inputs, self.hidden, self.eval_ms, self.eval_stats = [], [], [], []
         self.layers, self.passes = layers, passes
 
     def encrypt(self, token):
@@ -498,6 +498,7 @@ class TokenLoop:
         the server's device time (CUDA events on the context stream) is kept."""
         import torch
         self.inputs.append(int(token))
+        cache, before = self.em.cache, (self.em.cache.hits, self.em.cache.misses, self.em.refreshes())
         ct = self.encrypt(token)                    # client
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(self.stream)
@@ -505,6 +506,8 @@ class TokenLoop:
         e1.record(self.stream)
         e1.synchronize()
         self.eval_ms.append(e0.elapsed_time(e1))
+        self.eval_stats.append({"cache_hits": cache.hits - before[0], "cache_misses": cache.misses - before[1],
+                                "refreshes": self.em.refreshes() - before[2]})
         return self.select(hidden)                  # client
 
     def plaintext_check(self):
@@ -798,7 +801,8 @@ def main():
             "clocks": clocks,
             "per_token": {"operations": per_token, "refreshes": loop.em.refreshes() / max(1, len(loop.eval_ms)),
                           "setup_seconds": loop.setup_seconds, "calibration_seconds": loop.calibration_seconds,
-                          "eval_ms": loop.eval_ms, "tokens": loop.em.tokens, "check": check,
+                          "eval_ms": loop.eval_ms, "eval_stats": loop.eval_stats, "tokens": loop.em.tokens,
+                          "check": check, "diagonal_cache_gb": loop.em.cache.bytes / 2 ** 30,
                           "level_counts": level_counts},
             "config5": config5,
             "security_audit": loop.audit,

@@ -121,6 +121,8 @@ SIGNATURES = {
     "fhe_linear_transform": [vp, vp, ctypes.POINTER(vp), u32, u32, i32, i32, ctypes.POINTER(vp)],
     "fhe_ctx_counters": [vp, vp, i32],
     "fhe_ctx_level_counts": [vp, i32, vp, u32],
+    "fhe_ctx_set_conversion": [vp, i32],
+    "fhe_tc_timeouts": [vp],
     "fhe_kernel_launches": [ctypes.POINTER(ctypes.c_uint64)],
     "fhe_ntt_butterfly_ceiling": [vp, ctypes.POINTER(ctypes.c_double)],
     "fhe_refresh": [vp, vp, f64, i32, ctypes.POINTER(vp)],

@@ -339,6 +339,11 @@ class CryptoContext:
         call("fhe_ctx_counters", self.h, ctypes.cast(a, vp), int(reset))
         return dict(zip(self._COUNTERS, (int(v) for v in a)))
 
+    def SetConversionKernel(self, kernel: str):
+        """'cuda' (64-bit multiply-accumulates) or 'tensor' (tcgen05 int8 MMA)
+        for the key switches' basis conversions; the results are identical."""
+        call("fhe_ctx_set_conversion", self.h, {"cuda": 0, "tensor": 1}[kernel])
+
     def level_counts(self):
         """The ModUps, key inner products, rescales and tensor products since the
         last counter reset, by the number of live Q limbs they ran at:

@@ -712,6 +712,21 @@ int fhe_ctx_counters(fhe_ctx* ctx, fhe_counters* out, int32_t reset) {
   });
 }
 
+int fhe_ctx_set_conversion(fhe_ctx* ctx, int32_t kernel) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(kernel == 0 || kernel == 1, "conversion kernel must be 0 (CUDA cores) or 1 (tensor cores)");
+    k.tc_conversion = kernel == 1;
+  });
+}
+
+int fhe_tc_timeouts(uint64_t* count) {
+  return guarded([&] {
+    fhe::require(count != nullptr, "null count");
+    *count = fhe::tc_conversion_timeouts();
+  });
+}
+
 int fhe_ctx_level_counts(fhe_ctx* ctx, int32_t kind, uint64_t* out, uint32_t n) {
   return guarded([&] {
     fhe::Ckks& k = ckks(ctx);

@@ -146,6 +146,8 @@ void Ckks::build_static_tables() {
     std::memcpy(blob.data() + b2, hatinv.data(), K * sizeof(Shoup));
     std::memcpy(blob.data() + b3, hat.data(), hat.size() * sizeof(Shoup));
     mdtab_blob_ = upload(blob);
+    if (tc_conversion_supported(ctx.n, K, ctx.max_prime() < (uint64_t(1) << 60)))
+      mdtab_tc_ = upload(tc_conversion_table(hat.data(), K, L));
   }
   // Special FFT twiddles: inverse in OpenFHE FFTSpecialInv order, forward in
   // FFTSpecialForward order, computed with the host C library's cos/sin.
@@ -229,6 +231,21 @@ LevelTables& Ckks::level(uint32_t nq) {
     }
   }
   T.blob = upload(blob);
+  // tensor-core operand tables of every digit, when all digits qualify
+  const bool small = ctx.max_prime() < (uint64_t(1) << 60);
+  T.tc_modup = true;
+  for (uint32_t j = 0; j < T.D; ++j) T.tc_modup &= tc_conversion_supported(ctx.n, offs[j].ns, small);
+  std::vector<size_t> tc_off(T.D, 0);
+  if (T.tc_modup) {
+    std::vector<uint8_t> tcb;
+    for (uint32_t j = 0; j < T.D; ++j) {
+      const Off& o = offs[j];
+      tc_off[j] = tcb.size();
+      const auto t = tc_conversion_table(reinterpret_cast<const Shoup*>(blob.data() + o.h), o.ns, o.nt);
+      tcb.insert(tcb.end(), t.begin(), t.end());
+    }
+    T.tc_blob = upload(tcb);
+  }
   std::vector<ModUpDigit> digs(T.D);
   const char* base = T.blob.as<char>();
   for (uint32_t j = 0; j < T.D; ++j) {
@@ -238,6 +255,7 @@ LevelTables& Ckks::level(uint32_t nq) {
     digs[j].conv = ConvTable{o.ns, o.nt, reinterpret_cast<const uint32_t*>(base + o.sp),
                              reinterpret_cast<const uint32_t*>(base + o.dp),
                              reinterpret_cast<const Shoup*>(base + o.hi), reinterpret_cast<const Shoup*>(base + o.h)};
+    if (T.tc_modup) digs[j].conv.tc_b = T.tc_blob.as<uint8_t>() + tc_off[j];
   }
   T.digits = upload(digs);
   T.ntt_list = upload(list);
@@ -248,6 +266,7 @@ LevelTables& Ckks::level(uint32_t nq) {
     const size_t b1 = a16b(K * 4), b2 = a16b(b1 + L * 4), b3 = b2 + K * sizeof(Shoup);
     ConvTable md{K, nq, reinterpret_cast<const uint32_t*>(mb), reinterpret_cast<const uint32_t*>(mb + b1),
                  reinterpret_cast<const Shoup*>(mb + b2), reinterpret_cast<const Shoup*>(mb + b3)};
+    md.tc_b = mdtab_tc_.as<uint8_t>();
     T.moddown = upload(std::vector<ConvTable>{md});
   }
   return T;
@@ -622,8 +641,12 @@ void Ckks::modup(const uint64_t* d, uint32_t nq, uint64_t* ext) {
     a.src_limb_stride = nq;
     FHE_CUDA(ntt_inverse(a));
   }
-  launch_modup(coef, d, ext, nq, ctx.K, n, T.digits.as<ModUpDigit>(), T.D, ctx.alpha, ctx.d_mod.as<Modulus>(),
-               ctx.stream, ctx.max_prime() < (uint64_t(1) << 60));
+  if (tc_conversion && T.tc_modup)
+    launch_modup_tc(coef, d, ext, nq, ctx.K, n, T.digits.as<ModUpDigit>(), T.D, ctx.alpha, ctx.d_mod.as<Modulus>(),
+                    ctx.stream);
+  else
+    launch_modup(coef, d, ext, nq, ctx.K, n, T.digits.as<ModUpDigit>(), T.D, ctx.alpha, ctx.d_mod.as<Modulus>(),
+                 ctx.stream, ctx.max_prime() < (uint64_t(1) << 60));
   ++counters.modup;
   ++counters.modup_at[Counters::slot(nq)];
   if (T.ntt_list_len) {
@@ -642,8 +665,12 @@ void Ckks::moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, co
   ++counters.moddown;
   ntt_dense(acc + (size_t)nq * n, 2, K, w, ctx.L, true);
   uint64_t* conv = ws(3, (size_t)2 * ctx.L * n);
-  launch_convert(acc + (size_t)nq * n, (size_t)w * n, conv, (size_t)nq * n, 2, T.moddown.as<ConvTable>(), K, nq, n,
-                 ctx.d_mod.as<Modulus>(), ctx.stream, ctx.max_prime() < (uint64_t(1) << 60));
+  if (tc_conversion && mdtab_tc_.as<uint8_t>())
+    launch_convert_tc(acc + (size_t)nq * n, (size_t)w * n, conv, (size_t)nq * n, 2, T.moddown.as<ConvTable>(), nq,
+                      n, ctx.d_mod.as<Modulus>(), ctx.stream);
+  else
+    launch_convert(acc + (size_t)nq * n, (size_t)w * n, conv, (size_t)nq * n, 2, T.moddown.as<ConvTable>(), K, nq,
+                   n, ctx.d_mod.as<Modulus>(), ctx.stream, ctx.max_prime() < (uint64_t(1) << 60));
   // NTT of the conversion with the combine fused into its last pass:
   // out = (acc - NTT(conv)) * P^{-1} (+ c0 on component 0).
   counters.ntt_limbs += 2ull * nq;

@@ -42,6 +42,8 @@ struct LevelTables {
   DevMem ntt_list;  // uint2[]: ext limbs that need a forward NTT after ModUp
   uint32_t ntt_list_len = 0;
   DevMem moddown;   // ConvTable (P -> Q_nq)
+  DevMem tc_blob;   // tensor-core operand tables of the ModUp digits
+  bool tc_modup = false;  // every digit has a tensor-core table
 };
 
 // Operation counters (the reference's native.json ct_ct / rotations /
@@ -63,6 +65,10 @@ class Ckks {
   explicit Ckks(Context& c);
   Context& ctx;
   Counters counters;
+
+  // Basis conversions on the tensor cores (conv_tc.cu) where supported,
+  // else on the CUDA cores; both give the same words.
+  bool tc_conversion = false;
 
   // FLEXIBLEAUTO scaling factor of a fresh ciphertext with nq live limbs.
   double level_scale(uint32_t nq) const { return sf_[ctx.L - nq]; }
@@ -170,6 +176,7 @@ class Ckks {
   DevMem qinv_;        // Shoup[L][L]: q_last^{-1} mod q_i
   DevMem pmod_;        // Shoup[L+K]: P mod q_i (0 for P primes)
   DevMem mdtab_blob_;  // P -> Q conversion arrays (shared by all levels)
+  DevMem mdtab_tc_;    // their tensor-core operand table (empty when not supported)
   std::vector<Modulus> mods_host_;
   DevMem fft_inv_tw_, fft_fwd_tw_;
   bool keyed_ = false;

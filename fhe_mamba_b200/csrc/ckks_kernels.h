@@ -5,6 +5,7 @@
 // (p_base = L, the first special prime), described by a PrimeMap.
 #pragma once
 #include <cstdint>
+#include <vector>
 #include <cuda_runtime.h>
 
 #include "modarith.cuh"
@@ -32,6 +33,9 @@ struct ConvTable {
   // of its component, target t is written to row dst_row[t].
   const uint32_t* src_row = nullptr;
   const uint32_t* dst_row = nullptr;
+  // Optional tensor-core operand table (conv_tc.cu): hat split into bytes in
+  // the MMA's shared-memory layout, one 32 KiB tile per 16 targets.
+  const uint8_t* tc_b = nullptr;
 };
 
 // ---- randomness (ChaCha20, same streams as the oracle) ----
@@ -110,6 +114,19 @@ void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_
                       cudaStream_t s);
 // Basis conversion of ncomp polys: src limbs (coefficient form) -> dst (coefficient form).
 // ns / nt must equal the table's source / target counts (ns <= 24).
+// ---- basis conversion on the tensor cores (conv_tc.cu), same results ----
+// Whether the tensor-core conversion handles ns source limbs at ring n.
+bool tc_conversion_supported(uint32_t n, uint32_t ns, bool primes_below_2_60);
+// Operand table for ConvTable::tc_b from hat[nt][ns].
+std::vector<uint8_t> tc_conversion_table(const Shoup* hat, uint32_t ns, uint32_t nt);
+void launch_convert_tc(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp, uint32_t ncomp,
+                       const ConvTable* t_dev, uint32_t nt, uint32_t n, const Modulus* mods, cudaStream_t s);
+void launch_modup_tc(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t nq, uint32_t K,
+                     uint32_t n, const ModUpDigit* digits_dev, uint32_t D, uint32_t alpha, const Modulus* mods,
+                     cudaStream_t s);
+// Waits for an MMA that ran out of their iteration limit (0 when healthy).
+unsigned tc_conversion_timeouts();
+
 void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp, uint32_t ncomp,
                     const ConvTable* t_dev, uint32_t ns, uint32_t nt, uint32_t n, const Modulus* mods,
                     cudaStream_t s, bool primes_below_2_60);

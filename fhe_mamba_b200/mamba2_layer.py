@@ -18,6 +18,8 @@ output is compared with it directly.
 """
 from __future__ import annotations
 
+import os
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -99,6 +101,17 @@ class Mamba2Weights:
 
     def __getitem__(self, k):
         return self.arrays[k]
+
+
+def _single_threaded_blas():
+    """One BLAS thread per calling thread while the calibration runs its own
+    thread pool (nested pools oversubscribe the cores)."""
+    try:
+        from threadpoolctl import threadpool_limits
+        return threadpool_limits(1)
+    except ImportError:  # pragma: no cover - threadpoolctl ships with the image
+        import contextlib
+        return contextlib.nullcontext()
 
 
 def _rms(x, w, eps):
@@ -742,38 +755,71 @@ class Mamba2Model:
         B, T = calib_sequences, calib_tokens
         toks = r.integers(0, vocab, (B, T))
         greedy = np.arange(B) % 2 == 0
+        # Sequences run in chunks on a thread pool (numpy releases the GIL in
+        # its array loops); the reductions below do not depend on the split.
+        workers = max(1, min(B, os.cpu_count() or 1, 8))
+        step = -(-B // workers)
+        chunks = [slice(i, min(B, i + step)) for i in range(0, B, step)]
+
+        def exact_chunk(sl):  # exact-function trajectories give the polynomial domains ...
+            tk, gr = toks[sl], greedy[sl]
+            ranges = [new_ranges() for _ in self.layers]
+            finals = []
+            b = tk.shape[0]
+            state = [([np.zeros((b, W.conv_dim)) for _ in range(W.conv_kernel - 1)],
+                      np.zeros((b, W.heads, W.head_dim, W.d_state))) for W in self.layers]
+            for t in range(T):
+                h = self.embedding[tk[:, t]]
+                for li, W in enumerate(self.layers):
+                    h, c_, s_ = exact_step(W, h, state[li][0], state[li][1], range_updater(ranges[li]))
+                    state[li] = (c_, s_)
+                finals.append(np.mean(h * h, axis=-1) + eps)
+                if calib_prompt <= t + 1 < T:
+                    nxt = np.argmax(_rms(h, self.norm_f, eps) @ self.embedding.T, axis=-1)
+                    tk[gr, t + 1] = nxt[gr]
+            return ranges, np.concatenate(finals)
+
+        with _single_threaded_blas(), ThreadPoolExecutor(workers) as ex:
+            parts = list(ex.map(exact_chunk, chunks))
         ranges = [new_ranges() for _ in self.layers]
-        finals = []
-        state = [([np.zeros((B, W.conv_dim)) for _ in range(W.conv_kernel - 1)],
-                  np.zeros((B, W.heads, W.head_dim, W.d_state))) for W in self.layers]
-        for t in range(T):  # exact-function trajectories give the polynomial domains ...
-            h = self.embedding[toks[:, t]]
-            for li, W in enumerate(self.layers):
-                h, c_, s_ = exact_step(W, h, state[li][0], state[li][1], range_updater(ranges[li]))
-                state[li] = (c_, s_)
-            finals.append(np.mean(h * h, axis=-1) + eps)
-            if calib_prompt <= t + 1 < T:
-                nxt = np.argmax(_rms(h, self.norm_f, eps) @ self.embedding.T, axis=-1)
-                toks[greedy, t + 1] = nxt[greedy]
+        for part, _ in parts:
+            for li, rg in enumerate(part):
+                for k, (lo, hi) in rg.items():
+                    ranges[li][k][0] = min(ranges[li][k][0], lo)
+                    ranges[li][k][1] = max(ranges[li][k][1], hi)
+        finals = np.concatenate([f for _, f in parts])
         self.polys = [Mamba2Polys(W, ranges=rg, fused_decay=fused_decay) for W, rg in zip(self.layers, ranges)]
-        finals = np.concatenate(finals)
         lo, hi = 0.25 * float(finals.min()), 4.0 * float(finals.max())
         self.rsqrt_f = Poly(cheb_fit(lambda t: 1 / np.sqrt(t), lo, hi, 15), lo, hi)
+
         # ... and the polynomial path's magnitudes over the same tokens the
         # refresh bounds (bound_factor x the largest magnitude, at least 1:
         # single random tokens reach almost twice the largest value of a few
         # hundred calibration tokens)
+        def poly_chunk(sl):
+            tk = toks[sl]
+            mags = [{} for _ in self.layers]
+            final = 0.0
+            state = [([np.zeros((tk.shape[0], W.conv_dim)) for _ in range(W.conv_kernel - 1)], None)
+                     for W in self.layers]
+            for t in range(T):
+                h = self.embedding[tk[:, t]]
+                for li, (W, P) in enumerate(zip(self.layers, self.polys)):
+                    def rec(k, v, m=mags[li]):
+                        m[k] = max(m.get(k, 0.0), float(np.max(np.abs(v))))
+                    h, c_, s_ = poly_step_record(W, P, h, state[li][0], state[li][1], rec)
+                    state[li] = (c_, s_)
+                final = max(final, float(np.max(np.abs(h))))
+            return mags, final
+
+        with _single_threaded_blas(), ThreadPoolExecutor(workers) as ex:
+            parts = list(ex.map(poly_chunk, chunks))
         mags = [{} for _ in self.layers]
-        final = 0.0
-        state = [([np.zeros((B, W.conv_dim)) for _ in range(W.conv_kernel - 1)], None) for W in self.layers]
-        for t in range(T):
-            h = self.embedding[toks[:, t]]
-            for li, (W, P) in enumerate(zip(self.layers, self.polys)):
-                def rec(k, v, m=mags[li]):
-                    m[k] = max(m.get(k, 0.0), float(np.max(np.abs(v))))
-                h, c_, s_ = poly_step_record(W, P, h, state[li][0], state[li][1], rec)
-                state[li] = (c_, s_)
-            final = max(final, float(np.max(np.abs(h))))
+        for part, _ in parts:
+            for li, m in enumerate(part):
+                for k, v in m.items():
+                    mags[li][k] = max(mags[li].get(k, 0.0), v)
+        final = max(f for _, f in parts)
         self.bounds = [{k: max(1.0, bound_factor * v) for k, v in m.items()} for m in mags]
         self.final_bound = max(1.0, bound_factor * final)
         self.calibration = {"sequences": B, "tokens": T, "prompt": calib_prompt, "greedy_sequences": int(greedy.sum()),

@@ -308,6 +308,17 @@ int fhe_ctx_counters(fhe_ctx* ctx, fhe_counters* out, int32_t reset);
  * (packed_fideslib.cpp:1239-1396); these weight a CPU cost model by level. */
 int fhe_ctx_level_counts(fhe_ctx* ctx, int32_t kind, uint64_t* out, uint32_t n);
 
+/* Kernel of the context's HYBRID basis conversions (ModUp and ModDown, the
+ * FIDESlib ModUp / base-extension kernels behind every key switch): 0 = CUDA
+ * cores (64-bit integer multiply-accumulates), 1 = tensor cores
+ * (tcgen05.mma kind::i8 on the residues split into bytes; needs every prime
+ * below 2^60 and at most 16 source limbs, else the CUDA-core kernel runs).
+ * Both produce identical words.  No counterpart call in the reference. */
+int fhe_ctx_set_conversion(fhe_ctx* ctx, int32_t kernel);
+/* Number of tensor-core conversion blocks whose bounded wait for their MMA
+ * ran out (their outputs were skipped); 0 on a healthy device. */
+int fhe_tc_timeouts(uint64_t* count);
+
 /* Bootstrapping of the context's slots (full packing N/2, or sparse packing:
  * a power of two below N/2, where ModRaise is followed by the trace over the
  * rotations by multiples of the slot count, as OpenFHE does for

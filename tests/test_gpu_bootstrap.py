@@ -319,7 +319,7 @@ def test_bootstrap_at_token_loop_parameters():
     assert out.n_limbs() == 24
     assert np.max(np.abs(cc.Decrypt(out).GetRealPackedValue() - x)) < 5e-4
     ct4 = cc.Encrypt(cc.MakeCKKSPackedPlaintext(4 * x))
-    cc.LevelReduceInPlace(ct4, cc.n_q - 3)
+    cc.LevelReduceInPlace(ct4, cc.n_q - 6)  # 6 limbs: the scaling by 1 / bound and two passes
     two = cc.Decrypt(cc.EvalRefresh(ct4, 4.0, passes=2)).GetRealPackedValue()
     assert np.max(np.abs(two - 4 * x)) < 1e-5
     cc.close()

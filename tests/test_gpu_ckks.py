@@ -6,6 +6,8 @@ identical inputs.  Shapes: BASELINE config 1 (N=2^14, 1x60 + 8x50-bit Q,
 dnum 2) and the config-3 key-switch shape (N=2^16, 20 limbs, dnum 3).
 Decrypted values are checked against plaintext math as a second level.
 """
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -237,3 +239,43 @@ def test_wide_digit_keyswitch(oracle):
         assert np.array_equal(got, oc.relinearize(a, rlk)), nq
         b = _rand_ct(oc, nq, 400 + nq)
         assert np.array_equal(cc.EvalRotate(cc.upload(b), 3).residues(), oc.rotate(b, g, rk)), nq
+
+
+@pytest.mark.parametrize("shape", ["config1", "config3", "depth44"])
+def test_tensor_core_conversion_matches_oracle(oracle, shape):
+    """The key switch with its ModUp and ModDown basis conversions on the
+    tensor cores (tcgen05 int8 MMA over byte-split residues): relinearisation,
+    a rotation and hoisted rotations word for word against the oracle and
+    against the CUDA-core conversion, at config 1 (5 + 5 limbs), the config-3
+    shape (digits of 7 and 6 limbs) and the token loop's 45 + 15 limbs."""
+    from fhe_mamba_b200 import _lib
+    args = {"config1": (14, 8, 50, 60, 2), "config3": (16, 19, 59, 60, 3), "depth44": (16, 44, 59, 60, 3)}[shape]
+    cc, oc, s, sn = _setup(oracle, *args)
+    rng = np.random.default_rng(77)
+    nq = cc.n_q if shape != "depth44" else 31
+    d = np.empty((3, nq, cc.n), dtype=np.uint64)
+    for l in range(nq):
+        d[:, l, :] = rng.integers(0, cc.q[l], size=(3, cc.n), dtype=np.uint64)
+    steps = [1, -3]
+    cc.EvalRotateKeyGen(steps)
+    out = {}
+    for kernel in ("cuda", "tensor"):
+        cc.SetConversionKernel(kernel)
+        ct2 = cc.upload(d[:2])
+        out[kernel] = [cc.Relinearize(cc.upload(d, noise_deg=2)).residues(),
+                       cc.EvalRotate(ct2, 1).residues()] + [h.residues() for h in cc.EvalFastRotation(ct2, steps)]
+    cc.SetConversionKernel("cuda")
+    for a, b in zip(out["cuda"], out["tensor"]):
+        assert np.array_equal(a, b)
+    assert np.array_equal(out["tensor"][0], oc.relinearize(d, oc.relin_key(SEED, sn)))
+    g = cc.galois_element(1)
+    assert np.array_equal(out["tensor"][1], oc.rotate(d[:2], g, oc.rot_key(SEED, s, sn, g)))
+    n = ctypes_u64()
+    _lib.call("fhe_tc_timeouts", ctypes.byref(n))
+    assert n.value == 0
+    cc.close()
+
+
+def ctypes_u64():
+    import ctypes
+    return ctypes.c_uint64()
