@@ -53,6 +53,10 @@ LOG_N, LIMBS, POLYS, BITS = 16, 36, 4, 59
 LEVEL_COUNTS = os.path.join(ROOT, "profiles", "token_level_counts.json")
 ALG_BYTES_PER_TRANSFORM = 16 * POLYS * LIMBS * (1 << LOG_N)  # read + write every word once
 N_ROTATE = 4
+# Kernel of the key switches' basis conversions in the token loop and the
+# side measurements ("tensor": tcgen05 int8 MMA, "cuda": 64-bit CUDA-core
+# multiply-accumulates; identical words).  Set from --conversion.
+CONVERSION = "tensor"
 
 
 _JSON_OUT = None
@@ -253,20 +257,27 @@ def measure_ckks(local, reps=20, matvec=True):
     for l, q in enumerate(cc.q):
         d3[:, l, :] = rng.integers(0, q, size=(3, n), dtype=np.uint64)
     ct3 = cc.upload(d3, noise_deg=2)
-    for _ in range(3):
-        cc.Relinearize(ct3)
-    cc.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
-        cc.Relinearize(ct3)  # output freed on the stream right away, as in the evaluator
-    e1.record(stream)
-    e1.synchronize()
-    ks_ms = e0.elapsed_time(e1) / reps
+    per_kernel = {}
+    for kernel in ("cuda", "tensor-all"):
+        cc.SetConversionKernel(kernel)
+        for _ in range(3):
+            cc.Relinearize(ct3)
+        cc.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            cc.Relinearize(ct3)  # output freed on the stream right away, as in the evaluator
+        e1.record(stream)
+        e1.synchronize()
+        per_kernel[kernel] = e0.elapsed_time(e1) / reps
+    cc.SetConversionKernel(CONVERSION)
+    # 7 sources per digit at this shape: the "tensor" choice keeps the CUDA cores here
+    ks_ms = per_kernel["cuda"]
     ks_bytes = (L + 2 * L + 2 * L) * n * 8 + D * 2 * (L + K) * n * 8
     peak, kind = peaks()
     ks = {"workload": "relinearisation (HYBRID key switch), N=2^16, 20 Q limbs, 7 P limbs, dnum 3",
-          "ms": ks_ms, "alg_bytes": ks_bytes, "achieved_gbs": ks_bytes / (ks_ms / 1e3) / 1e9,
+          "ms": ks_ms, "conversion_kernel": "cuda", "ms_by_conversion_kernel": per_kernel,
+          "alg_bytes": ks_bytes, "achieved_gbs": ks_bytes / (ks_ms / 1e3) / 1e9,
           "frac": ks_bytes / (ks_ms / 1e3) / 1e9 / peak, "peak_gbs": peak, "peak_source": kind}
 
     if not matvec:
@@ -301,6 +312,38 @@ def measure_ckks(local, reps=20, matvec=True):
     del pts, ct, out, ct3
     cc.close()
     return ks, mv
+
+
+def measure_keyswitch_levels(cc, levels=(45, 31, 16), reps=20):
+    """Relinearisation on the token loop's context (N = 2^16, depth 44, dnum 3:
+    15 P limbs, digits of 15) at several levels, with the basis conversions on
+    the CUDA cores and on the tensor cores; CUDA events on the context stream."""
+    import torch
+    stream = torch.cuda.ExternalStream(cc.stream_ptr())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    rng = np.random.default_rng(45)
+    out = []
+    for nq in levels:
+        d = np.empty((3, nq, cc.n), dtype=np.uint64)
+        for l in range(nq):
+            d[:, l, :] = rng.integers(0, cc.q[l], size=(3, cc.n), dtype=np.uint64)
+        ct = cc.upload(d, noise_deg=2)
+        row = {"limbs": nq}
+        for kernel in ("cuda", "tensor"):
+            cc.SetConversionKernel(kernel)
+            for _ in range(3):
+                cc.Relinearize(ct)
+            cc.synchronize()
+            e0.record(stream)
+            for _ in range(reps):
+                cc.Relinearize(ct)
+            e1.record(stream)
+            e1.synchronize()
+            row[kernel + "_ms"] = e0.elapsed_time(e1) / reps
+        out.append(row)
+        del ct
+    cc.SetConversionKernel(CONVERSION)
+    return out
 
 
 def measure_bootstrap(cc, reps=3):
@@ -457,6 +500,7 @@ class TokenLoop:
             self.audit = {"ring_dimension": ring, "qp_bits": qp, "guideline_max_qp_bits": 3523,
                           "q_towers": self.cc.n_q, "p_towers": self.cc.n_p, "hybrid_digits": dnum,
                           "uniform_ternary": not sparse_h}
+        self.cc.SetConversionKernel(CONVERSION)
         self.cc.KeyGen(41 + seed)
         self.cc.EvalBootstrapSetup((4, 4), sparse_hamming_weight=sparse_h)
         self.cc.EvalBootstrapKeyGen()
@@ -586,7 +630,7 @@ def config_dict(args):
                         f"({args.layers} layers, d_model 768, d_state 128, 24 heads, vocab 50280)",
             "ring_dim": 1 << 17 if args.security == "128-classic" else 1 << 16, "slots": 1 << 15, "depth": 44,
             "scale_bits": 59, "dnum": 4 if args.security == "128-classic" else 3, "security": args.security,
-            "bootstrap_passes": args.passes, "decay": "fused per-head series" if args.fused_decay else "exp(a softplus)",
+            "bootstrap_passes": args.passes, "conversion_kernel": args.conversion, "decay": "fused per-head series" if args.fused_decay else "exp(a softplus)",
             "secret_key_dist": f"sparse-encapsulated h={args.sparse_h}" if args.sparse_h else "uniform-ternary",
             "l2": "inputs larger than L2 (keys ~36 GB, cached diagonals)",
             "parallelism": "one token-loop replica per GPU"}
@@ -651,6 +695,8 @@ def main():
                     help="128-classic: ring 2^17, dnum 4, 2^15 sparsely packed slots, Q*P audited")
     ap.add_argument("--fused-decay", action="store_true",
                     help="decay as one per-head series of the raw dt (no refresh of a*dt); off by default")
+    ap.add_argument("--conversion", default="tensor", choices=["tensor", "cuda"],
+                    help="basis conversions of the key switches on the tensor cores or the CUDA cores")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ckks", action="store_true", help="skip the key-switch, matvec and bootstrap side measurements")
@@ -661,6 +707,8 @@ def main():
     ap.add_argument("--kernel-shares", action="store_true",
                     help="after the warm-up, record one token's kernels (CUPTI) and print their time shares")
     args = ap.parse_args()
+    global CONVERSION
+    CONVERSION = args.conversion
     if args.warmup < 3:
         ap.error("warmup must be >= 3")
     json_stdout()
@@ -682,7 +730,12 @@ def main():
         return
     if args.ckks_only and world == 1:
         ks, _ = measure_ckks(local, matvec=False)
-        emit({"keyswitch": ks})
+        from fhe_mamba_b200 import CCParams, CryptoContext
+        cc = CryptoContext(CCParams(ring_dim=1 << 16, multiplicative_depth=44, scaling_mod_size=59,
+                                    first_mod_size=60, num_large_digits=3, device=local))
+        cc.KeyGen(7)
+        emit({"keyswitch": ks, "keyswitch_by_level": measure_keyswitch_levels(cc)})
+        cc.close()
         return
     if world > 1:
         from datetime import timedelta
@@ -815,6 +868,7 @@ def main():
         line.update(side)
         if world == 1 and not args.no_ckks:
             line["bootstrap"] = measure_bootstrap(loop.cc)
+            line["keyswitch_by_level"] = measure_keyswitch_levels(loop.cc)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(level_counts, host_threads())
         emit(line)

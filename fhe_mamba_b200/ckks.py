@@ -340,9 +340,10 @@ class CryptoContext:
         return dict(zip(self._COUNTERS, (int(v) for v in a)))
 
     def SetConversionKernel(self, kernel: str):
-        """'cuda' (64-bit multiply-accumulates) or 'tensor' (tcgen05 int8 MMA)
-        for the key switches' basis conversions; the results are identical."""
-        call("fhe_ctx_set_conversion", self.h, {"cuda": 0, "tensor": 1}[kernel])
+        """'cuda' (64-bit multiply-accumulates), 'tensor' (tcgen05 int8 MMA for
+        bases of 12+ limbs, where it is faster) or 'tensor-all' (every base;
+        tests) for the key switches' basis conversions; identical results."""
+        call("fhe_ctx_set_conversion", self.h, {"cuda": 0, "tensor": 1, "tensor-all": 2}[kernel])
 
     def level_counts(self):
         """The ModUps, key inner products, rescales and tensor products since the

@@ -715,8 +715,9 @@ int fhe_ctx_counters(fhe_ctx* ctx, fhe_counters* out, int32_t reset) {
 int fhe_ctx_set_conversion(fhe_ctx* ctx, int32_t kernel) {
   return guarded([&] {
     fhe::Ckks& k = ckks(ctx);
-    fhe::require(kernel == 0 || kernel == 1, "conversion kernel must be 0 (CUDA cores) or 1 (tensor cores)");
-    k.tc_conversion = kernel == 1;
+    fhe::require(kernel >= 0 && kernel <= 2,
+                 "conversion kernel must be 0 (CUDA cores), 1 (tensor cores where faster) or 2 (tensor cores)");
+    k.tc_conversion = kernel;
   });
 }
 

@@ -630,6 +630,14 @@ std::unique_ptr<Pt> Ckks::decrypt(const Ct& c) {
 // ---------------------------------------------------------------------------
 // key switching
 
+// Source limbs from which the tensor-core conversion is used when enabled:
+// its epilogue (15 byte-shift sums per output, assembled and reduced once)
+// costs the same for any source count, while the CUDA-core conversion's
+// multiply-accumulates grow with it.  Measured on a B200 (relinearisation,
+// N = 2^16): 7 sources 0.324 vs 0.313 ms (CUDA cores faster), 15 sources at
+// 45 limbs 0.613 vs 0.703 ms (tensor cores faster).
+constexpr uint32_t kTcMinSources = 12;
+
 void Ckks::modup(const uint64_t* d, uint32_t nq, uint64_t* ext) {
   const uint32_t n = ctx.n;
   LevelTables& T = level(nq);
@@ -641,7 +649,7 @@ void Ckks::modup(const uint64_t* d, uint32_t nq, uint64_t* ext) {
     a.src_limb_stride = nq;
     FHE_CUDA(ntt_inverse(a));
   }
-  if (tc_conversion && T.tc_modup)
+  if (tc_conversion && T.tc_modup && (tc_conversion == 2 || ctx.alpha >= kTcMinSources))
     launch_modup_tc(coef, d, ext, nq, ctx.K, n, T.digits.as<ModUpDigit>(), T.D, ctx.alpha, ctx.d_mod.as<Modulus>(),
                     ctx.stream);
   else
@@ -665,7 +673,7 @@ void Ckks::moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, co
   ++counters.moddown;
   ntt_dense(acc + (size_t)nq * n, 2, K, w, ctx.L, true);
   uint64_t* conv = ws(3, (size_t)2 * ctx.L * n);
-  if (tc_conversion && mdtab_tc_.as<uint8_t>())
+  if (tc_conversion && mdtab_tc_.as<uint8_t>() && (tc_conversion == 2 || K >= kTcMinSources))
     launch_convert_tc(acc + (size_t)nq * n, (size_t)w * n, conv, (size_t)nq * n, 2, T.moddown.as<ConvTable>(), nq,
                       n, ctx.d_mod.as<Modulus>(), ctx.stream);
   else

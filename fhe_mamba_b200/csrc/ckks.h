@@ -66,9 +66,10 @@ class Ckks {
   Context& ctx;
   Counters counters;
 
-  // Basis conversions on the tensor cores (conv_tc.cu) where supported,
-  // else on the CUDA cores; both give the same words.
-  bool tc_conversion = false;
+  // Basis conversions: 0 = CUDA cores, 1 = tensor cores (conv_tc.cu) for
+  // bases where they are faster, 2 = tensor cores wherever supported (for
+  // tests); every choice gives the same words.
+  int tc_conversion = 0;
 
   // FLEXIBLEAUTO scaling factor of a fresh ciphertext with nq live limbs.
   double level_scale(uint32_t nq) const { return sf_[ctx.L - nq]; }

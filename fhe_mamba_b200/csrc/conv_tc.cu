@@ -34,15 +34,17 @@ namespace fhe {
 namespace {
 
 constexpr uint32_t kRows = 128;      // coefficients per CTA (MMA M)
-constexpr uint32_t kTgt = 16;        // target limbs per CTA
+constexpr uint32_t kTgt = 8;         // target limbs per tile
 constexpr uint32_t kCols = 16 * kTgt;  // MMA N: 16 columns per target (15 shifts + 1 zero)
 constexpr uint32_t kK = 128;         // MMA K in bytes (16 sources x 8 bytes)
 constexpr uint32_t kBytesA = kRows * kK;   // 16 KiB
-constexpr uint32_t kBytesB = kCols * kK;   // 32 KiB
-constexpr uint32_t kSmem = kBytesA + kBytesB + 64;
+constexpr uint32_t kBytesB = kCols * kK;   // 16 KiB per tile, two buffers
+constexpr uint32_t kSmem = kBytesA + 2 * kBytesB + 64;
+constexpr uint32_t kTmemCols = 2 * kCols;  // two accumulator buffers
 // Dynamic shared memory requested per CTA: above a third of the SM's 228 KiB,
-// so at most two CTAs are resident and their two 256-column tensor-memory
-// allocations always fit the SM's 512 columns (no CTA waits in tcgen05.alloc).
+// so at most two CTAs are resident and their tensor-memory allocations
+// (2 x 256 columns) always fit the SM's 512 columns (no CTA waits in
+// tcgen05.alloc).
 constexpr uint32_t kSmemLaunch = 96 * 1024;
 static_assert(kSmem <= kSmemLaunch, "operands exceed the requested shared memory");
 // Bound on the wait for the MMA's completion: far above its microseconds;
@@ -82,14 +84,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t addr, uint32_t parity) {
   return false;
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
       "%14, %15}, [%16];"
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
         "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // sum_{s<15} 2^(8s) p[s] (exact, below 2^124) as (hi, lo), from four groups
@@ -122,13 +123,45 @@ struct TcArgs {
   const Modulus* mods;
 };
 
+// One CTA = 128 coefficients of one component (MODE 0) or digit (MODE 1),
+// all tiles of 8 targets.  A (the bytes of y) is formed once.  Thread 0 is
+// the producer: it fetches B tiles with bulk asynchronous copies into two
+// shared buffers and issues each tile's MMA group into one of two
+// tensor-memory accumulators, so the copy of tile t + 2 and the MMA of tile
+// t + 1 run while the 8 warps read tile t back (warps w and w + 4 share lane
+// quarter w % 4 and take targets 0-3 and 4-7 of the tile).
+constexpr uint32_t kThreads = 256;
+
+__device__ __forceinline__ void issue_mma(uint32_t tmem, uint32_t a0, uint32_t b0, uint32_t mbar) {
+#pragma unroll
+  for (uint32_t s = 0; s < kK / 32; ++s) {
+    const uint64_t da = smem_desc(a0 + s * 256), db = smem_desc(b0 + s * 256);
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+        "l"(da), "l"(db), "r"(kIdesc), "r"(s));
+  }
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
+               : "memory");
+}
+
+// Bulk asynchronous copy of one B tile (16-byte aligned, a multiple of 16
+// bytes) from global to shared memory, completing on mbar.
+__device__ __forceinline__ void fetch_b(uint32_t dst, const uint8_t* src, uint32_t mbar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(kBytesB) : "memory");
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(kBytesB), "r"(mbar)
+               : "memory");
+}
+
 template <int MODE>
-__global__ void __launch_bounds__(kRows, 1) k_conv_tc(const TcArgs g) {
+__global__ void __launch_bounds__(kThreads, 2) k_conv_tc(const TcArgs g) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* sa = smem;
-  uint8_t* sb = smem + kBytesA;
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + kBytesA + kBytesB);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + kBytesA + kBytesB + 8);
+  uint8_t* sb = smem + kBytesA;  // two tiles
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kBytesA + 2 * kBytesB);  // B full [2], MMA done [2]
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + kBytesA + 2 * kBytesB + 32);
 
   ConvTable t;
   uint32_t lo = 0, j = 0;
@@ -140,111 +173,156 @@ __global__ void __launch_bounds__(kRows, 1) k_conv_tc(const TcArgs g) {
   } else {
     t = *g.tab;
   }
-  const uint32_t t0 = blockIdx.z * kTgt;
-  if (t0 >= t.nt) return;  // uniform across the block, before any tensor memory is held
-  const uint32_t nt = min(kTgt, t.nt - t0);
-  const uint32_t ns = t.ns;
-  const uint32_t n = g.n, r = threadIdx.x, k = blockIdx.x * kRows + r;
+  const uint32_t ns = t.ns, n = g.n;
   const uint32_t warp = threadIdx.x >> 5;
+  const uint32_t r = threadIdx.x & (kRows - 1), half = threadIdx.x / kRows;
+  const uint32_t k = blockIdx.x * kRows + r;
+  const uint32_t tiles = (t.nt + kTgt - 1) / kTgt;
+  const uint32_t a0 = smem_u32(sa), b0 = smem_u32(sb), bb = smem_u32(bar), bm = bb + 16;
+  const bool producer = threadIdx.x == 0;
+  // producer bookkeeping: copies and MMA groups issued / waited per buffer
+  uint32_t b_issued[2] = {0, 0}, b_waited[2] = {0, 0}, m_issued[2] = {0, 0};
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
-                 "r"(kCols));
+                 "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  if (threadIdx.x == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(mbar)));
+  if (producer) {
+    for (uint32_t i = 0; i < 4; ++i) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bb + 8 * i));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    fetch_b(b0, t.tc_b, bb);
+    ++b_issued[0];
+    if (tiles > 1) {
+      fetch_b(b0 + kBytesB, t.tc_b + kBytesB, bb + 8);
+      ++b_issued[1];
+    }
   }
 
-  // A: row r = coefficient k, bytes 8i..8i+7 = y_i (zero for i >= ns).
+  // A: row r = coefficient k, bytes 8i..8i+7 = y_i (zero for i >= ns); the
+  // two halves of the block form sources 0-7 and 8-15.  All loads first.
   const uint64_t* src;
   if constexpr (MODE == 1) src = g.src + (size_t)lo * n;
   else src = g.src + (size_t)blockIdx.y * g.s_comp;
+  uint64_t* dst;
+  if constexpr (MODE == 1) dst = g.dst + (size_t)j * g.w * n;
+  else dst = g.dst + (size_t)blockIdx.y * g.d_comp;
+  uint64_t x[8];
 #pragma unroll
-  for (uint32_t i = 0; i < 16; ++i) {
-    uint64_t y = 0;
+  for (uint32_t ii = 0; ii < 8; ++ii) {
+    const uint32_t i = half * 8 + ii;
+    x[ii] = 0;
     if (i < ns) {
       const size_t row = MODE == 1 ? i : (t.src_row ? t.src_row[i] : i);
-      const uint64_t x = src[row * n + k];
+      x[ii] = src[row * n + k];
+    }
+  }
+#pragma unroll
+  for (uint32_t ii = 0; ii < 8; ++ii) {
+    const uint32_t i = half * 8 + ii;
+    uint64_t y = 0;
+    if (i < ns) {
       const Shoup h = t.hatinv[i];
-      y = shoup_mul(x, h.w, h.wp, g.mods[t.src_prime[i]].q);
-      if constexpr (MODE == 1) {
-        if (blockIdx.z == 0) {
-          uint64_t* e = g.dst + (size_t)j * g.w * n;
-          e[(size_t)(lo + i) * n + k] = g.dntt[(size_t)(lo + i) * n + k];
-        }
-      }
+      y = shoup_mul(x[ii], h.w, h.wp, g.mods[t.src_prime[i]].q);
+      if constexpr (MODE == 1) dst[(size_t)(lo + i) * n + k] = g.dntt[(size_t)(lo + i) * n + k];
     }
     *reinterpret_cast<uint64_t*>(sa + (r >> 3) * 1024 + (i >> 1) * 128 + (r & 7) * 16 + (i & 1) * 8) = y;
-  }
-  // B: this target tile of the table, stored by the host in the operand layout.
-  {
-    const uint4* bsrc = reinterpret_cast<const uint4*>(t.tc_b + (size_t)blockIdx.z * kBytesB);
-    uint4* bdst = reinterpret_cast<uint4*>(sb);
-#pragma unroll 4
-    for (uint32_t v = threadIdx.x; v < kBytesB / 16; v += kRows) bdst[v] = __ldg(bsrc + v);
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tslot;
-
-  if (threadIdx.x == 0) {
-    const uint32_t a0 = smem_u32(sa), b0 = smem_u32(sb);
-#pragma unroll
-    for (uint32_t s = 0; s < kK / 32; ++s) {
-      const uint64_t da = smem_desc(a0 + s * 256), db = smem_desc(b0 + s * 256);
-      asm volatile(
-          "{\n\t.reg .pred p;\n\t"
-          "setp.ne.b32 p, %4, 0;\n\t"
-          "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-          "l"(da), "l"(db), "r"(kIdesc), "r"(s));
-    }
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(mbar))
-                 : "memory");
-  }
-  const bool ok = mbar_wait(smem_u32(mbar), 0);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (!ok) {
-    if (threadIdx.x == 0) atomicAdd(&g_tc_timeouts, 1u);
-  } else {
-    uint64_t* dst;
-    if constexpr (MODE == 1) dst = g.dst + (size_t)j * g.w * n;
-    else dst = g.dst + (size_t)blockIdx.y * g.d_comp;
-    const uint32_t lane_base = (warp * 32) << 16;
-    for (uint32_t u = 0; u < nt; ++u) {
-      uint32_t p[16];
-      tmem_ld16(tmem + lane_base + 16 * u, p);
-      uint64_t hi, lo64;
-      assemble(p, hi, lo64);
-      const uint32_t tt = t0 + u;
-      const uint64_t v = reduce_u128(hi, lo64, g.mods[t.dst_prime[tt]]);
-      size_t row;
-      if constexpr (MODE == 1) row = tt < lo ? tt : tt + ns;
-      else row = t.dst_row ? t.dst_row[tt] : tt;
-      dst[row * n + k] = v;
+  bool ok = true;
+  if (producer) {
+    ok = mbar_wait(bb, 0);
+    b_waited[0] = 1;
+    if (ok) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      issue_mma(tmem, a0, b0, bm);
+      ++m_issued[0];
     }
   }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  if (warp == 0) {
+  ok = __syncthreads_and(ok);
+  const uint32_t lane_base = ((warp & 3) * 32) << 16;
+  uint32_t tile = 0;
+  for (; tile < tiles && ok; ++tile) {
+    const uint32_t buf = tile & 1, nb = buf ^ 1;
+    if (producer && tile + 1 < tiles) {  // MMA of the next tile once its B tile has landed
+      ok = mbar_wait(bb + 8 * nb, b_waited[nb] & 1);
+      ++b_waited[nb];
+      if (ok) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        issue_mma(tmem + nb * kCols, a0, b0 + nb * kBytesB, bm + 8 * nb);
+        ++m_issued[nb];
+      }
+    }
+    const bool mok = mbar_wait(bm + 8 * buf, (tile >> 1) & 1);  // this tile's MMA is done
+    ok = ok && mok;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
+    if (producer && ok && tile + 2 < tiles) {  // B buffer `buf` is free again
+      fetch_b(b0 + buf * kBytesB, t.tc_b + (size_t)(tile + 2) * kBytesB, bb + 8 * buf);
+      ++b_issued[buf];
+    }
+    if (ok) {
+      const uint32_t t0 = tile * kTgt + half * 4;
+      uint32_t p[4][16];
+      const uint32_t col = tmem + lane_base + buf * kCols + 16 * half * 4;
+      tmem_ld16_nowait(col, p[0]);
+      tmem_ld16_nowait(col + 16, p[1]);
+      tmem_ld16_nowait(col + 32, p[2]);
+      tmem_ld16_nowait(col + 48, p[3]);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (uint32_t u = 0; u < 4; ++u) {
+        const uint32_t tt = t0 + u;
+        if (tt < t.nt) {
+          uint64_t hi, lo64;
+          assemble(p[u], hi, lo64);
+          const uint64_t v = reduce_u128(hi, lo64, g.mods[t.dst_prime[tt]]);
+          size_t row;
+          if constexpr (MODE == 1) row = tt < lo ? tt : tt + ns;
+          else row = t.dst_row ? t.dst_row[tt] : tt;
+          dst[row * n + k] = v;
+        }
+      }
+    }
+    // every warp's reads of accumulator `buf` are done before the MMA of
+    // tile + 2 overwrites it
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    ok = __syncthreads_and(ok);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  }
+  if (!ok) {
+    // A wait ran out: record it, then let every copy and MMA group the
+    // producer issued finish (bounded waits) before the tensor memory goes.
+    if (producer) {
+      atomicAdd(&g_tc_timeouts, 1u);
+      // phases complete in order and at most one per barrier is outstanding,
+      // so the last issued phase of each barrier covers the rest
+      for (uint32_t q = 0; q < 2; ++q) {
+        if (b_issued[q] > b_waited[q]) mbar_wait(bb + 8 * q, (b_issued[q] - 1) & 1);
+        if (m_issued[q]) mbar_wait(bm + 8 * q, (m_issued[q] - 1) & 1);
+      }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
 }
 
 template <int MODE>
-void launch_tc(const TcArgs& a, uint32_t ny, uint32_t nt_max, cudaStream_t s) {
+void launch_tc(const TcArgs& a, uint32_t ny, cudaStream_t s) {
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_conv_tc<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLaunch);
     attr = true;
   }
-  const dim3 grid(a.n / kRows, ny, (nt_max + kTgt - 1) / kTgt);
-  k_conv_tc<MODE><<<grid, kRows, kSmemLaunch, s>>>(a);
+  const dim3 grid(a.n / kRows, ny);
+  k_conv_tc<MODE><<<grid, kThreads, kSmemLaunch, s>>>(a);
   note_launch();
 }
 
@@ -285,7 +363,8 @@ void launch_convert_tc(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t
   a.tab = t_dev;
   a.n = n;
   a.mods = mods;
-  launch_tc<0>(a, ncomp, nt, s);
+  (void)nt;
+  launch_tc<0>(a, ncomp, s);
 }
 
 void launch_modup_tc(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uint32_t nq, uint32_t K,
@@ -300,10 +379,8 @@ void launch_modup_tc(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, 
   a.dntt = dntt;
   a.n = n;
   a.mods = mods;
-  // every digit has at most nq + K - (nq - (D-1) alpha) targets; blocks past a
-  // digit's own target count return at once
-  const uint32_t shortest = nq - (D - 1) * alpha;
-  launch_tc<1>(a, D, nq + K - shortest, s);
+  (void)alpha;
+  launch_tc<1>(a, D, s);
 }
 
 unsigned tc_conversion_timeouts() {

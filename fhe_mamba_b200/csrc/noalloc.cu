@@ -71,15 +71,15 @@ void rescale_noalloc(Context& c, const uint64_t* in, uint32_t ncomp, uint32_t nq
   require(ncomp >= 1 && ncomp <= 3, "ncomp must be 1, 2 or 3");
   require(nq >= 2 && nq <= c.L && nq <= 64, "n_limbs must be in [2, min(number of Q primes, 64)]");
   const uint32_t n = c.n;
+  const size_t need = noalloc_rescale_words(ncomp, nq, n);
+  require(need <= kScratchWords,
+          "fhe_rescale_noalloc: needs " + std::to_string(need * 8) + " bytes of scratch, above the fixed " +
+              std::to_string(kScratchWords * 8) + "-byte maximum (use fhe_rescale)");
   {  // limb i of `out` is written while later limbs of `in` are still to be read
     const uintptr_t i0 = reinterpret_cast<uintptr_t>(in), i1 = i0 + (size_t)ncomp * nq * n * 8;
     const uintptr_t o0 = reinterpret_cast<uintptr_t>(out), o1 = o0 + (size_t)ncomp * (nq - 1) * n * 8;
     require(o1 <= i0 || i1 <= o0, "fhe_rescale_noalloc: out must not overlap in");
   }
-  const size_t need = noalloc_rescale_words(ncomp, nq, n);
-  require(need <= kScratchWords,
-          "fhe_rescale_noalloc: needs " + std::to_string(need * 8) + " bytes of scratch, above the fixed " +
-              std::to_string(kScratchWords * 8) + "-byte maximum (use fhe_rescale)");
   c.make_current();
   uint64_t* base = scratch_for(c.device);
   // Layout: [Shoup q_last^{-1} mod q_i, i < nq-1][last limb per comp][lifted].

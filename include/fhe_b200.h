@@ -311,8 +311,10 @@ int fhe_ctx_level_counts(fhe_ctx* ctx, int32_t kind, uint64_t* out, uint32_t n);
 /* Kernel of the context's HYBRID basis conversions (ModUp and ModDown, the
  * FIDESlib ModUp / base-extension kernels behind every key switch): 0 = CUDA
  * cores (64-bit integer multiply-accumulates), 1 = tensor cores
- * (tcgen05.mma kind::i8 on the residues split into bytes; needs every prime
- * below 2^60 and at most 16 source limbs, else the CUDA-core kernel runs).
+ * (tcgen05.mma kind::i8 on the residues split into bytes) for bases of 12 to
+ * 16 source limbs with every prime below 2^60, where they are faster, 2 =
+ * tensor cores for every base of 1 to 16 limbs (tests); the CUDA-core kernel
+ * runs wherever the tensor cores are not used.
  * Both produce identical words.  No counterpart call in the reference. */
 int fhe_ctx_set_conversion(fhe_ctx* ctx, int32_t kernel);
 /* Number of tensor-core conversion blocks whose bounded wait for their MMA

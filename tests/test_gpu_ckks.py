@@ -259,17 +259,17 @@ def test_tensor_core_conversion_matches_oracle(oracle, shape):
     steps = [1, -3]
     cc.EvalRotateKeyGen(steps)
     out = {}
-    for kernel in ("cuda", "tensor"):
+    for kernel in ("cuda", "tensor-all"):
         cc.SetConversionKernel(kernel)
         ct2 = cc.upload(d[:2])
         out[kernel] = [cc.Relinearize(cc.upload(d, noise_deg=2)).residues(),
                        cc.EvalRotate(ct2, 1).residues()] + [h.residues() for h in cc.EvalFastRotation(ct2, steps)]
     cc.SetConversionKernel("cuda")
-    for a, b in zip(out["cuda"], out["tensor"]):
+    for a, b in zip(out["cuda"], out["tensor-all"]):
         assert np.array_equal(a, b)
-    assert np.array_equal(out["tensor"][0], oc.relinearize(d, oc.relin_key(SEED, sn)))
+    assert np.array_equal(out["tensor-all"][0], oc.relinearize(d, oc.relin_key(SEED, sn)))
     g = cc.galois_element(1)
-    assert np.array_equal(out["tensor"][1], oc.rotate(d[:2], g, oc.rot_key(SEED, s, sn, g)))
+    assert np.array_equal(out["tensor-all"][1], oc.rotate(d[:2], g, oc.rot_key(SEED, s, sn, g)))
     n = ctypes_u64()
     _lib.call("fhe_tc_timeouts", ctypes.byref(n))
     assert n.value == 0
