@@ -478,12 +478,12 @@ class TokenLoop:
     the checks after the timed region."""
 
     def __init__(self, local, layers=24, passes=2, seed=6, sparse_h=0, classical128=False, fused_decay=False,
-                 horizon=32, cache_gb=None):
+                 horizon=32, cache_gb=None, model=None):
         from fhe_mamba_b200 import CCParams, CryptoContext
         from fhe_mamba_b200.mamba2_layer import EncryptedMamba2Model
         import torch
         t0 = time.perf_counter()
-        self.model = synthetic_model(seed, horizon, layers, fused_decay)
+        self.model = model if model is not None else synthetic_model(seed, horizon, layers, fused_decay)
         self.calibration_seconds = time.perf_counter() - t0
         # 128-classic as the reference's executable sets it up: ring 2^17, four
         # digits, 2^15 slots sparsely packed (packed_fideslib.cpp:1060-1076)
@@ -581,6 +581,27 @@ class TokenLoop:
                 "outside_domain": out_of_domain, "calibration": m.calibration}
 
 
+def run_classical128(local, model, evaluations, passes):
+    """The same model's loop under classical-128 parameters as the reference's
+    executable sets them up (ring 2^17, four digits, 45 Q + 12 P primes with
+    the Q*P audit, 2^15 sparsely packed slots, uniform ternary secret) over
+    the first `evaluations` prompt tokens of the config-5 protocol, with its
+    own plaintext-path check; device time per evaluation (CUDA events)."""
+    loop = TokenLoop(local, passes=passes, classical128=True, model=model, cache_gb=8)
+    prompt = config5_prompt()
+    for t in prompt[:evaluations]:
+        loop.evaluate(t)
+    check = loop.plaintext_check()
+    out = {"workload": "config-5 loop, first prompt tokens, classical-128 (ring 2^17, dnum 4)",
+           "evaluations": len(loop.eval_ms), "s_per_evaluation": sum(loop.eval_ms[1:]) / 1e3 / max(1, len(loop.eval_ms) - 1),
+           "eval_ms": loop.eval_ms, "refreshes_per_evaluation": loop.em.refreshes() / len(loop.eval_ms),
+           "security_audit": loop.audit, "setup_seconds": loop.setup_seconds,
+           "check": {k: check[k] for k in ("tokens_equal_plaintext", "max_hidden_error", "tolerance", "passed",
+                                           "max_refresh_bound_ratio", "max_domain_position")}}
+    loop.cc.close()
+    return out
+
+
 def host_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -630,7 +651,7 @@ def config_dict(args):
                         f"({args.layers} layers, d_model 768, d_state 128, 24 heads, vocab 50280)",
             "ring_dim": 1 << 17 if args.security == "128-classic" else 1 << 16, "slots": 1 << 15, "depth": 44,
             "scale_bits": 59, "dnum": 4 if args.security == "128-classic" else 3, "security": args.security,
-            "bootstrap_passes": args.passes, "conversion_kernel": args.conversion, "decay": "fused per-head series" if args.fused_decay else "exp(a softplus)",
+            "bootstrap_passes": args.passes, "conversion_kernel": args.conversion, "decay": "fused per-head series" if args.decay == "fused" else "exp(a softplus)",
             "secret_key_dist": f"sparse-encapsulated h={args.sparse_h}" if args.sparse_h else "uniform-ternary",
             "l2": "inputs larger than L2 (keys ~36 GB, cached diagonals)",
             "parallelism": "one token-loop replica per GPU"}
@@ -693,8 +714,12 @@ def main():
                     help="bootstrap by sparse-secret encapsulation with this Hamming weight (0: uniform ternary)")
     ap.add_argument("--security", default="not-set", choices=["not-set", "128-classic"],
                     help="128-classic: ring 2^17, dnum 4, 2^15 sparsely packed slots, Q*P audited")
-    ap.add_argument("--fused-decay", action="store_true",
-                    help="decay as one per-head series of the raw dt (no refresh of a*dt); off by default")
+    ap.add_argument("--decay", default="fused", choices=["fused", "separate"],
+                    help="fused: decay = one per-head series of the raw dt (no refresh of a*dt); "
+                         "separate: exp of a times the softplus series")
+    ap.add_argument("--classical128-evaluations", type=int, default=3,
+                    help="after the headline (not-set) run, this many timed evaluations of the same loop under "
+                         "classical-128 parameters (0: none)")
     ap.add_argument("--conversion", default="tensor", choices=["tensor", "cuda"],
                     help="basis conversions of the key switches on the tensor cores or the CUDA cores")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -763,7 +788,7 @@ def main():
     extra_warmup = max(0, args.warmup - PROMPT_TOKENS)
     horizon = PROMPT_TOKENS + extra_warmup + args.steps
     loop = TokenLoop(local, layers=args.layers, passes=args.passes, seed=6 + rank, sparse_h=args.sparse_h,
-                     classical128=args.security == "128-classic", fused_decay=args.fused_decay, horizon=horizon)
+                     classical128=args.security == "128-classic", fused_decay=args.decay == "fused", horizon=horizon)
     prompt = config5_prompt()
     tok = None
     for t in prompt:
@@ -871,9 +896,14 @@ def main():
             line["keyswitch_by_level"] = measure_keyswitch_levels(loop.cc)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(level_counts, host_threads())
-        emit(line)
 
+    model = loop.model
     loop.cc.close()
+    if rank == 0:
+        if world == 1 and args.security == "not-set" and args.classical128_evaluations > 0:
+            # the first evaluation also builds its level tables: the mean skips it
+            line["classical128"] = run_classical128(local, model, args.classical128_evaluations + 1, args.passes)
+        emit(line)
     if world > 1:
         dist.destroy_process_group()
     if failed:
