@@ -57,6 +57,8 @@ N_ROTATE = 4
 # side measurements ("tensor": tcgen05 int8 MMA, "cuda": 64-bit CUDA-core
 # multiply-accumulates; identical words).  Set from --conversion.
 CONVERSION = "tensor"
+# Key inner product of the Q limbs inside ModDown's last NTT pass (--keyswitch-fusion).
+FUSED_KEY_INNER = False
 
 
 _JSON_OUT = None
@@ -259,8 +261,9 @@ def measure_ckks(local, reps=20, matvec=True):
     ct3 = cc.upload(d3, noise_deg=2)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     per_kernel = {}
-    for kernel in ("cuda", "tensor-all"):
+    for kernel, fused in (("cuda", False), ("tensor-all", False), ("cuda", True)):
         cc.SetConversionKernel(kernel)
+        cc.SetKeySwitchFusion(fused)
         for _ in range(3):
             cc.Relinearize(ct3)
         cc.synchronize()
@@ -269,14 +272,16 @@ def measure_ckks(local, reps=20, matvec=True):
             cc.Relinearize(ct3)  # output freed on the stream right away, as in the evaluator
         e1.record(stream)
         e1.synchronize()
-        per_kernel[kernel] = e0.elapsed_time(e1) / reps
+        per_kernel[kernel + ("_fused" if fused else "")] = e0.elapsed_time(e1) / reps
     cc.SetConversionKernel(CONVERSION)
+    cc.SetKeySwitchFusion(FUSED_KEY_INNER)
     # 7 sources per digit at this shape: the "tensor" choice keeps the CUDA cores here
-    ks_ms = per_kernel["cuda"]
+    ks_ms = per_kernel["cuda_fused" if FUSED_KEY_INNER else "cuda"]
     ks_bytes = (L + 2 * L + 2 * L) * n * 8 + D * 2 * (L + K) * n * 8
     peak, kind = peaks()
     ks = {"workload": "relinearisation (HYBRID key switch), N=2^16, 20 Q limbs, 7 P limbs, dnum 3",
-          "ms": ks_ms, "conversion_kernel": "cuda", "ms_by_conversion_kernel": per_kernel,
+          "ms": ks_ms, "conversion_kernel": "cuda", "fused_key_inner": FUSED_KEY_INNER,
+          "ms_by_variant": per_kernel,
           "alg_bytes": ks_bytes, "achieved_gbs": ks_bytes / (ks_ms / 1e3) / 1e9,
           "frac": ks_bytes / (ks_ms / 1e3) / 1e9 / peak, "peak_gbs": peak, "peak_source": kind}
 
@@ -329,8 +334,9 @@ def measure_keyswitch_levels(cc, levels=(45, 31, 16), reps=20):
             d[:, l, :] = rng.integers(0, cc.q[l], size=(3, cc.n), dtype=np.uint64)
         ct = cc.upload(d, noise_deg=2)
         row = {"limbs": nq}
-        for kernel in ("cuda", "tensor"):
+        for kernel, fused in (("cuda", False), ("tensor", False), ("tensor", True)):
             cc.SetConversionKernel(kernel)
+            cc.SetKeySwitchFusion(fused)
             for _ in range(3):
                 cc.Relinearize(ct)
             cc.synchronize()
@@ -339,10 +345,11 @@ def measure_keyswitch_levels(cc, levels=(45, 31, 16), reps=20):
                 cc.Relinearize(ct)
             e1.record(stream)
             e1.synchronize()
-            row[kernel + "_ms"] = e0.elapsed_time(e1) / reps
+            row[kernel + ("_fused" if fused else "") + "_ms"] = e0.elapsed_time(e1) / reps
         out.append(row)
         del ct
     cc.SetConversionKernel(CONVERSION)
+    cc.SetKeySwitchFusion(FUSED_KEY_INNER)
     return out
 
 
@@ -411,6 +418,15 @@ def measure_sharded_keyswitch(local, world, reps=20):
         e1.record(sk.stream)
         e1.synchronize()
         ms = e0.elapsed_time(e1) / reps
+        # per-step breakdown (device time on the context stream; a gather's
+        # step includes waiting for the slowest rank to reach it)
+        steps = {k: 0.0 for k in sk.STAGES}
+        for _ in range(reps):
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+            sk.relinearize(own, nq, events=evs)
+            evs[5].synchronize()
+            for i, k in enumerate(sk.STAGES):
+                steps[k] += evs[i].elapsed_time(evs[i + 1]) / reps
         for _ in range(3):
             cc.Relinearize(full)
         cc.synchronize()
@@ -420,13 +436,16 @@ def measure_sharded_keyswitch(local, world, reps=20):
         e1.record(sk.stream)
         e1.synchronize()
         single = e0.elapsed_time(e1) / reps
-        t = torch.tensor([ms, single, 0.0 if exact else 1.0], dtype=torch.float64, device=dev)
+        t = torch.tensor([ms, single, 0.0 if exact else 1.0] + [steps[k] for k in sk.STAGES], dtype=torch.float64,
+                         device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         pl = sk.plan
         gather = (world - 1) * (pl.q_chunk(nq) + 2 * pl.p_chunk) * cc.n * 8
+        breakdown = {k: float(t[3 + i]) for i, k in enumerate(sk.STAGES)}
         cases.append({"limbs": nq, "ms": float(t[0]), "single_gpu_ms": float(t[1]),
                       "speedup": float(t[1] / t[0]), "bit_exact_all_ranks": bool(t[2] == 0.0),
-                      "received_bytes_per_rank": gather})
+                      "received_bytes_per_rank": gather, "step_ms_max_over_ranks": breakdown,
+                      "largest_step": max(breakdown, key=breakdown.get)})
         del full
     cc.close()
     return {"world": world, "layout": "round-robin RNS limbs, NCCL all-gathers of the ModUp and ModDown limbs",
@@ -446,14 +465,15 @@ def config5_prompt():
     return [int(t) for t in np.random.default_rng(PROMPT_SEED).integers(0, VOCAB, PROMPT_TOKENS)]
 
 
-def synthetic_model(seed, horizon, layers=24, fused_decay=False):
+def synthetic_model(seed, horizon, layers=24, fused_decay=False, threads=None):
     """The BASELINE config-5 model (Mamba-2-130M shape, tied embedding, seeded
     random weights), calibrated on 16 token sequences of its own seed that
     cover at least the run's `horizon` evaluations (the recurrent state keeps
     growing for many tokens)."""
     from fhe_mamba_b200.mamba2_layer import Mamba2Model
     return Mamba2Model(layers=layers, d_model=768, d_state=128, heads=24, vocab=VOCAB, seed=seed,
-                       calib_sequences=16, calib_tokens=max(32, horizon + 4), fused_decay=fused_decay)
+                       calib_sequences=16, calib_tokens=max(32, horizon + 4), fused_decay=fused_decay,
+                       calib_threads=threads)
 
 
 def plaintext_protocol(model, evaluations):
@@ -483,7 +503,9 @@ class TokenLoop:
         from fhe_mamba_b200.mamba2_layer import EncryptedMamba2Model
         import torch
         t0 = time.perf_counter()
-        self.model = model if model is not None else synthetic_model(seed, horizon, layers, fused_decay)
+        # ranks of one node share the host cores for the calibration
+        threads = max(1, host_threads() // int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
+        self.model = model if model is not None else synthetic_model(seed, horizon, layers, fused_decay, threads)
         self.calibration_seconds = time.perf_counter() - t0
         # 128-classic as the reference's executable sets it up: ring 2^17, four
         # digits, 2^15 slots sparsely packed (packed_fideslib.cpp:1060-1076)
@@ -501,6 +523,7 @@ class TokenLoop:
                           "q_towers": self.cc.n_q, "p_towers": self.cc.n_p, "hybrid_digits": dnum,
                           "uniform_ternary": not sparse_h}
         self.cc.SetConversionKernel(CONVERSION)
+        self.cc.SetKeySwitchFusion(FUSED_KEY_INNER)
         self.cc.KeyGen(41 + seed)
         self.cc.EvalBootstrapSetup((4, 4), sparse_hamming_weight=sparse_h)
         self.cc.EvalBootstrapKeyGen()
@@ -651,7 +674,8 @@ def config_dict(args):
                         f"({args.layers} layers, d_model 768, d_state 128, 24 heads, vocab 50280)",
             "ring_dim": 1 << 17 if args.security == "128-classic" else 1 << 16, "slots": 1 << 15, "depth": 44,
             "scale_bits": 59, "dnum": 4 if args.security == "128-classic" else 3, "security": args.security,
-            "bootstrap_passes": args.passes, "conversion_kernel": args.conversion, "decay": "fused per-head series" if args.decay == "fused" else "exp(a softplus)",
+            "bootstrap_passes": args.passes, "conversion_kernel": args.conversion,
+            "keyswitch_fusion": args.keyswitch_fusion, "decay": "fused per-head series" if args.decay == "fused" else "exp(a softplus)",
             "secret_key_dist": f"sparse-encapsulated h={args.sparse_h}" if args.sparse_h else "uniform-ternary",
             "l2": "inputs larger than L2 (keys ~36 GB, cached diagonals)",
             "parallelism": "one token-loop replica per GPU"}
@@ -722,18 +746,22 @@ def main():
                          "classical-128 parameters (0: none)")
     ap.add_argument("--conversion", default="tensor", choices=["tensor", "cuda"],
                     help="basis conversions of the key switches on the tensor cores or the CUDA cores")
+    ap.add_argument("--keyswitch-fusion", default="off", choices=["on", "off"],
+                    help="form the Q limbs' key inner product inside ModDown's last NTT pass")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ckks", action="store_true", help="skip the key-switch, matvec and bootstrap side measurements")
     ap.add_argument("--ckks-only", action="store_true",
-                    help="print only the key-switch measurement: config 3 on one GPU, limb-sharded under torchrun")
+                    help="print only the key-switch and config-3 matvec measurements on one GPU, the "
+                         "limb-sharded key switch under torchrun")
     ap.add_argument("--ntt-only", action="store_true",
                     help="print only the config-2 NTT roofline measurement (profiling runs)")
     ap.add_argument("--kernel-shares", action="store_true",
                     help="after the warm-up, record one token's kernels (CUPTI) and print their time shares")
     args = ap.parse_args()
-    global CONVERSION
+    global CONVERSION, FUSED_KEY_INNER
     CONVERSION = args.conversion
+    FUSED_KEY_INNER = args.keyswitch_fusion == "on"
     if args.warmup < 3:
         ap.error("warmup must be >= 3")
     json_stdout()
@@ -754,12 +782,12 @@ def main():
         emit({"roofline": measure_ntt(local, steps=20, warmup=5)})
         return
     if args.ckks_only and world == 1:
-        ks, _ = measure_ckks(local, matvec=False)
+        ks, mv = measure_ckks(local, matvec=True)
         from fhe_mamba_b200 import CCParams, CryptoContext
         cc = CryptoContext(CCParams(ring_dim=1 << 16, multiplicative_depth=44, scaling_mod_size=59,
                                     first_mod_size=60, num_large_digits=3, device=local))
         cc.KeyGen(7)
-        emit({"keyswitch": ks, "keyswitch_by_level": measure_keyswitch_levels(cc)})
+        emit({"keyswitch": ks, "bsgs_matvec": mv, "keyswitch_by_level": measure_keyswitch_levels(cc)})
         cc.close()
         return
     if world > 1:
@@ -899,10 +927,22 @@ def main():
 
     model = loop.model
     loop.cc.close()
+    del loop
     if rank == 0:
         if world == 1 and args.security == "not-set" and args.classical128_evaluations > 0:
-            # the first evaluation also builds its level tables: the mean skips it
-            line["classical128"] = run_classical128(local, model, args.classical128_evaluations + 1, args.passes)
+            # every ciphertext and cached plaintext of the ring-2^16 loop goes
+            # back to the driver first: the ring-2^17 keys need large blocks
+            import gc
+            gc.collect()
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+            _lib.call("fhe_device_trim", local)
+            try:
+                # the first evaluation also builds its level tables: the mean skips it
+                line["classical128"] = run_classical128(local, model, args.classical128_evaluations + 1,
+                                                        args.passes)
+            except Exception as e:  # reported, the headline stands on its own
+                line["classical128"] = {"error": f"{type(e).__name__}: {e}"}
         emit(line)
     if world > 1:
         dist.destroy_process_group()

@@ -122,6 +122,8 @@ SIGNATURES = {
     "fhe_ctx_counters": [vp, vp, i32],
     "fhe_ctx_level_counts": [vp, i32, vp, u32],
     "fhe_ctx_set_conversion": [vp, i32],
+    "fhe_ctx_set_keyswitch_fusion": [vp, i32],
+    "fhe_device_trim": [i32],
     "fhe_tc_timeouts": [vp],
     "fhe_kernel_launches": [ctypes.POINTER(ctypes.c_uint64)],
     "fhe_ntt_butterfly_ceiling": [vp, ctypes.POINTER(ctypes.c_double)],

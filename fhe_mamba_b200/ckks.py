@@ -345,6 +345,11 @@ class CryptoContext:
         tests) for the key switches' basis conversions; identical results."""
         call("fhe_ctx_set_conversion", self.h, {"cuda": 0, "tensor": 1, "tensor-all": 2}[kernel])
 
+    def SetKeySwitchFusion(self, fused: bool):
+        """Form the Q limbs' key inner product inside ModDown's last NTT pass
+        (True) or in a separate kernel (False); the results are identical."""
+        call("fhe_ctx_set_keyswitch_fusion", self.h, int(bool(fused)))
+
     def level_counts(self):
         """The ModUps, key inner products, rescales and tensor products since the
         last counter reset, by the number of live Q limbs they ran at:

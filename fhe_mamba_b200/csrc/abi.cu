@@ -721,6 +721,23 @@ int fhe_ctx_set_conversion(fhe_ctx* ctx, int32_t kernel) {
   });
 }
 
+int fhe_device_trim(int32_t device) {
+  return guarded([&] {
+    int count = 0;
+    FHE_CUDA(cudaGetDeviceCount(&count));
+    fhe::require(device >= 0 && device < count, "device ordinal out of range");
+    FHE_CUDA(cudaSetDevice(device));
+    FHE_CUDA(cudaDeviceSynchronize());
+    cudaMemPool_t pool;
+    FHE_CUDA(cudaDeviceGetDefaultMemPool(&pool, device));
+    FHE_CUDA(cudaMemPoolTrimTo(pool, 0));
+  });
+}
+
+int fhe_ctx_set_keyswitch_fusion(fhe_ctx* ctx, int32_t fused) {
+  return guarded([&] { ckks(ctx).fused_key_inner = fused != 0; });
+}
+
 int fhe_tc_timeouts(uint64_t* count) {
   return guarded([&] {
     fhe::require(count != nullptr, "null count");

@@ -667,7 +667,8 @@ void Ckks::modup(const uint64_t* d, uint32_t nq, uint64_t* ext) {
 }
 
 // acc = [2][w][N] (NTT form, clobbered) -> out[c] = ModDown(acc[c]) (+ add_c0 on component 0).
-void Ckks::moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, const uint64_t* add_c0) {
+void Ckks::moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, const uint64_t* add_c0,
+                        const uint64_t* ext, const uint64_t* evk) {
   const uint32_t n = ctx.n, K = ctx.K, w = nq + K;
   LevelTables& T = level(nq);
   ++counters.moddown;
@@ -689,7 +690,33 @@ void Ckks::moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, co
   a.epi_out_comp = so;
   a.epi_w = pinv_.as<Shoup>();
   a.epi_add = add_c0;
+  if (ext) {  // acc's Q rows formed in the epilogue from the digits and the key
+    a.epi_ext = ext;
+    a.epi_key = evk;
+    a.epi_digits = T.D;
+    a.epi_w_rows = w;
+    a.epi_key_limbs = ctx.L + K;
+    a.epi_mods = ctx.d_mod.as<Modulus>();
+  }
   FHE_CUDA(ntt_forward(a));
+}
+
+void Ckks::key_moddown(const uint64_t* ext, const uint64_t* evk, uint32_t nq, uint64_t* out, size_t so,
+                       const uint64_t* add_c0) {
+  const uint32_t n = ctx.n, K = ctx.K, w = nq + K;
+  LevelTables& T = level(nq);
+  uint64_t* acc = ws(2, (size_t)2 * (ctx.L + K) * n);
+  ++counters.key_inner;
+  ++counters.key_inner_at[Counters::slot(nq)];
+  if (fused_key_inner) {  // only the P limbs go through the accumulator
+    launch_key_inner(ext, T.D, w, evk, ctx.L + K, PrimeMap{nq, ctx.L}, acc, n, ctx.d_mod.as<Modulus>(), ctx.stream,
+                     nq, K);
+    moddown_pair(acc, nq, out, so, add_c0, ext, evk);
+  } else {
+    launch_key_inner(ext, T.D, w, evk, ctx.L + K, PrimeMap{nq, ctx.L}, acc, n, ctx.d_mod.as<Modulus>(),
+                     ctx.stream);
+    moddown_pair(acc, nq, out, so, add_c0);
+  }
 }
 
 void Ckks::keyswitch(const uint64_t* d, uint32_t nq, const uint64_t* evk, uint64_t* out, size_t so,
@@ -697,12 +724,8 @@ void Ckks::keyswitch(const uint64_t* d, uint32_t nq, const uint64_t* evk, uint64
   const uint32_t n = ctx.n, K = ctx.K, w = nq + K;
   LevelTables& T = level(nq);
   uint64_t* ext = ws(0, (size_t)T.D * w * n);
-  uint64_t* acc = ws(2, (size_t)2 * (ctx.L + K) * n);
   modup(d, nq, ext);
-  ++counters.key_inner;
-  ++counters.key_inner_at[Counters::slot(nq)];
-  launch_key_inner(ext, T.D, w, evk, ctx.L + K, PrimeMap{nq, ctx.L}, acc, n, ctx.d_mod.as<Modulus>(), ctx.stream);
-  moddown_pair(acc, nq, out, so, add_c0);
+  key_moddown(ext, evk, nq, out, so, add_c0);
 }
 
 std::unique_ptr<Ct> Ckks::relinearize(const Ct& d) {
@@ -746,15 +769,10 @@ std::vector<std::unique_ptr<Ct>> Ckks::rotate_hoisted(const Ct& a, const std::ve
   uint64_t* ext = ws(5, (size_t)T.D * w * n);  // one ModUp shared by every rotation
   modup(a.data() + cs, nq, ext);
   std::vector<std::unique_ptr<Ct>> outs;
-  uint64_t* acc = ws(2, (size_t)2 * (ctx.L + K) * n);
   uint64_t* u = ws(4, 2 * so);
   for (uint64_t g : gs) {
     ++counters.rotations;
-    ++counters.key_inner;
-    ++counters.key_inner_at[Counters::slot(nq)];
-    launch_key_inner(ext, T.D, w, rot_.at(g).as<uint64_t>(), ctx.L + K, PrimeMap{nq, ctx.L}, acc, n,
-                     ctx.d_mod.as<Modulus>(), ctx.stream);
-    moddown_pair(acc, nq, u, so, a.data());
+    key_moddown(ext, rot_.at(g).as<uint64_t>(), nq, u, so, a.data());
     auto out = alloc(nq, 2);
     launch_automorphism(u, so, out->data(), so, 2, nq, ctx.log_n, g, ctx.stream);
     out->scale = a.scale;

@@ -70,6 +70,9 @@ class Ckks {
   // bases where they are faster, 2 = tensor cores wherever supported (for
   // tests); every choice gives the same words.
   int tc_conversion = 0;
+  // Key inner product of the Q limbs folded into ModDown's combine epilogue
+  // (the accumulator's Q rows are never written and re-read); same words.
+  bool fused_key_inner = false;
 
   // FLEXIBLEAUTO scaling factor of a fresh ciphertext with nq live limbs.
   double level_scale(uint32_t nq) const { return sf_[ctx.L - nq]; }
@@ -161,7 +164,13 @@ class Ckks {
   void keyswitch(const uint64_t* d, uint32_t nq, const uint64_t* evk, uint64_t* out, size_t so,
                  const uint64_t* add_c0);
   void modup(const uint64_t* d, uint32_t nq, uint64_t* ext);
-  void moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, const uint64_t* add_c0);
+  void moddown_pair(uint64_t* acc, uint32_t nq, uint64_t* out, size_t so, const uint64_t* add_c0,
+                    const uint64_t* ext = nullptr, const uint64_t* evk = nullptr);
+  // Key inner product of the ModUp digits `ext` with `evk` followed by the
+  // ModDown pair into out (+ add_c0): with fused_key_inner the Q limbs'
+  // inner product is formed inside ModDown's last NTT pass.
+  void key_moddown(const uint64_t* ext, const uint64_t* evk, uint32_t nq, uint64_t* out, size_t so,
+                   const uint64_t* add_c0);
   void switch_keygen(uint64_t key_id, const uint64_t* s_new, const uint64_t* s_old, DevMem& out);
   void ntt_dense(uint64_t* d, uint32_t polys, uint32_t limbs, uint32_t stride, uint32_t prime0, bool inv);
   uint64_t* ws(size_t idx, size_t words);

@@ -317,10 +317,10 @@ __global__ void k_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ex
 
 __global__ void k_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_t* evk,
                             uint32_t key_limbs, PrimeMap pm, uint64_t* acc, uint32_t n,
-                            const Modulus* mods) {
+                            const Modulus* mods, uint32_t first_limb) {
   const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
   if (k >= n) return;
-  const uint32_t l = blockIdx.y;
+  const uint32_t l = first_limb + blockIdx.y;
   const uint32_t p = pm(l);
   const Modulus m = mods[p];
   // 128-bit sums of the D products (each < q^2 < 2^122 / D), one reduction each
@@ -552,32 +552,52 @@ constexpr int kGiantChunk = 8;  // giants per CTA: neighbouring CTAs share the b
 // Block (x = giant chunk, y = coefficient tile, z = limb).  Each thread owns
 // one coefficient and accumulates every giant of its chunk in 128 bits; the
 // babies are re-read per giant from L1/L2, the diagonals stream from HBM once.
+// The chunk's diagonal pointers and the baby pointers sit in shared memory and
+// every load of a batch of 8 babies is issued before its products (an absent
+// diagonal reads a zero word instead of branching), so each thread keeps 24
+// loads in flight: the stream is bound by HBM, not by load latency.
+__device__ const uint64_t g_zero_word = 0;
+
 __global__ void __launch_bounds__(128) k_bsgs_dot(const uint64_t* const* babies, const uint64_t* const* diags,
                                                   uint64_t* out, uint32_t b, uint32_t G, uint32_t nq, uint32_t n,
                                                   const Modulus* mods) {
+  constexpr uint32_t kBatch = 8;
+  __shared__ const uint64_t* s_diag[kGiantChunk * kMaxBaby];
+  __shared__ const uint64_t* s_baby[kMaxBaby];
+  const uint32_t g0 = blockIdx.x * kGiantChunk, g1 = min(G, g0 + kGiantChunk);
+  for (uint32_t i = threadIdx.x; i < (g1 - g0) * b; i += blockDim.x) s_diag[i] = diags[g0 * b + i];
+  for (uint32_t i = threadIdx.x; i < b; i += blockDim.x) s_baby[i] = babies[i];
+  __syncthreads();
   const uint32_t k = blockIdx.y * blockDim.x + threadIdx.x;
   if (k >= n) return;
   const uint32_t l = blockIdx.z;
   const Modulus m = mods[l];
   const uint64_t r64 = barrett_reduce(1, 0, m);
   const size_t off = (size_t)l * n + k, cs = (size_t)nq * n;
-  const uint32_t g0 = blockIdx.x * kGiantChunk, g1 = min(G, g0 + kGiantChunk);
   for (uint32_t g = g0; g < g1; ++g) {
+    const uint64_t* const* dg = s_diag + (g - g0) * b;
     uint64_t h0 = 0, l0 = 0, h1 = 0, l1 = 0;
-#pragma unroll 4
-    for (uint32_t j = 0; j < b; ++j) {
-      const uint64_t* dp = diags[g * b + j];
-      if (!dp) continue;
-      const uint64_t d = __ldcs(dp + off);  // streamed once: evict first
-      const uint64_t* bj = babies[j];
-      const uint64_t x0 = __ldg(bj + off), x1 = __ldg(bj + cs + off);
-      uint64_t lo = x0 * d, hi = __umul64hi(x0, d);
-      l0 += lo;
-      h0 += hi + (l0 < lo);
-      lo = x1 * d;
-      hi = __umul64hi(x1, d);
-      l1 += lo;
-      h1 += hi + (l1 < lo);
+    for (uint32_t jb = 0; jb < b; jb += kBatch) {
+      uint64_t d[kBatch], x0[kBatch], x1[kBatch];
+#pragma unroll
+      for (uint32_t u = 0; u < kBatch; ++u) {
+        const uint32_t j = jb + u;
+        const uint64_t* dp = j < b ? dg[j] : nullptr;
+        const uint64_t* bj = j < b ? s_baby[j] : nullptr;
+        d[u] = __ldcs(dp ? dp + off : &g_zero_word);  // streamed once: evict first
+        x0[u] = bj ? __ldg(bj + off) : 0;
+        x1[u] = bj ? __ldg(bj + cs + off) : 0;
+      }
+#pragma unroll
+      for (uint32_t u = 0; u < kBatch; ++u) {
+        uint64_t lo = x0[u] * d[u], hi = __umul64hi(x0[u], d[u]);
+        l0 += lo;
+        h0 += hi + (l0 < lo);
+        lo = x1[u] * d[u];
+        hi = __umul64hi(x1[u], d[u]);
+        l1 += lo;
+        h1 += hi + (l1 < lo);
+      }
     }
     uint64_t* o = out + (size_t)g * 2 * cs;
     o[off] = reduce128(h0, l0, m, r64);
@@ -704,8 +724,11 @@ void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uin
 }
 
 void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_t* evk, uint32_t key_limbs,
-                      PrimeMap pm, uint64_t* acc, uint32_t n, const Modulus* mods, cudaStream_t s) {
-  k_key_inner<<<grid1(n, w), kTpb, 0, s>>>(ext, D, w, evk, key_limbs, pm, acc, n, mods); note_launch();
+                      PrimeMap pm, uint64_t* acc, uint32_t n, const Modulus* mods, cudaStream_t s, uint32_t l0,
+                      uint32_t count) {
+  const uint32_t rows = l0 >= w ? 0 : (count < w - l0 ? count : w - l0);
+  if (!rows) return;
+  k_key_inner<<<grid1(n, rows), kTpb, 0, s>>>(ext, D, w, evk, key_limbs, pm, acc, n, mods, l0); note_launch();
 }
 
 void launch_convert(const uint64_t* src, size_t s_comp, uint64_t* dst, size_t d_comp, uint32_t ncomp,

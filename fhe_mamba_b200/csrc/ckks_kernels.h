@@ -109,9 +109,10 @@ void launch_modup(const uint64_t* coef, const uint64_t* dntt, uint64_t* ext, uin
                   uint32_t n, const ModUpDigit* digits_dev, uint32_t D, uint32_t alpha, const Modulus* mods,
                   cudaStream_t s, bool primes_below_2_60);
 // acc[2][w][N] = sum_j ext[j] * evk[j][0/1][key limb]; key limb of ext limb l is pm(l).
+// Only the limbs [l0, l0 + count) when given (the rest of acc is left alone).
 void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_t* evk,
                       uint32_t key_limbs, PrimeMap pm, uint64_t* acc, uint32_t n, const Modulus* mods,
-                      cudaStream_t s);
+                      cudaStream_t s, uint32_t l0 = 0, uint32_t count = ~0u);
 // Basis conversion of ncomp polys: src limbs (coefficient form) -> dst (coefficient form).
 // ns / nt must equal the table's source / target counts (ns <= 24).
 // ---- basis conversion on the tensor cores (conv_tc.cu), same results ----

@@ -7,11 +7,11 @@
 // 8 bytes, y_i = sum_a 2^(8a) y_{i,a} and h = sum_b 2^(8b) h_b, and
 //   sum_i y_i h_{i,t} = sum_{s=0..14} 2^(8s) P_{s,t},
 //   P_{s,t} = sum_i sum_{a+b=s} y_{i,a} h_{i,t,b}.
-// One unsigned 8-bit MMA per CTA forms every P_{s,t}: A = the 128 coefficients'
-// bytes (K = 16 sources x 8 bytes = 128), B = for each of 16 targets and each
-// shift s the row of bytes h_{i,t,s-a} at K index (i, a) (zero where s - a is
-// outside [0, 8)), so D[row][16 t + s] = P_{s,t} with int32 accumulation
-// (P < 16 * 8 * 255^2 < 2^23).  The epilogue reads each target's 15 shift
+// One unsigned 8-bit MMA group per tile of 8 targets forms every P_{s,t}:
+// A = the 128 coefficients' bytes (K = 16 sources x 8 bytes = 128), B = for
+// each target and each shift s the row of bytes h_{i,t,s-a} at K index (i, a)
+// (zero where s - a is outside [0, 8)), so D[row][16 t + s] = P_{s,t} with
+// int32 accumulation (P < 16 * 8 * 255^2 < 2^23).  The epilogue reads each target's 15 shift
 // sums from tensor memory, assembles the exact sum (below 16 * 2^120) in 128
 // bits with shifts and adds, and reduces it once.  The multiply-accumulates
 // leave the 64-bit integer multiply pipe, which bounds the CUDA-core
@@ -22,7 +22,13 @@
 // core matrices of 8 rows x 16 bytes (128 contiguous bytes), the 8 K-chunks
 // of one 8-row group adjacent (leading byte offset 128), 8-row groups 1024
 // bytes apart (stride byte offset).  The B table is stored in that layout by
-// the host (one 32 KiB tile per 16 targets), so a CTA copies it verbatim.
+// the host (one 16 KiB tile per 8 targets), so a bulk copy moves it verbatim.
+//
+// Measured on a B200 (relinearisation at N = 2^16, depth 44, dnum 3, 15
+// source limbs): 0.614 ms at 45 limbs against 0.702 ms with the CUDA-core
+// conversion, 0.479 vs 0.514 at 31, 0.285 vs 0.294 at 16; with 7 source
+// limbs the CUDA cores stay faster (0.312 vs 0.324 ms),
+// since the epilogue costs the same for any source count.
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -108,8 +114,8 @@ __device__ __forceinline__ void assemble(const uint32_t (&p)[16], uint64_t& hi, 
 // src_row(i)*n, targets at dst + y*d_comp + dst_row(t)*n (ConvTable maps).
 // MODE 1 (ModUp): blockIdx.y = digit - digit0; sources are the digit's own
 // rows lo..hi-1 of coef, targets the other rows of ext (row t < lo: t, else
-// t + ns) of digit j at ext + j*w*n; the z == 0 blocks also copy the digit's
-// own rows from the NTT-form input.
+// t + ns) of digit j at ext + j*w*n; every block also copies the digit's own
+// rows (its 128 coefficients) from the NTT-form input.
 struct TcArgs {
   const uint64_t* src;
   size_t s_comp;

@@ -193,7 +193,9 @@ __device__ __forceinline__ int rpad(int k) { return k + (k >> 4); }
 // With LZ > 0 the column pass leaves values below lz_bound_after(LZ, 1, LA) q;
 // this pass continues the greedy schedule and reduces the output with one
 // Shoup multiplication by 1 and a conditional subtraction.
-template <int LA, int LB, int ROWS, int LZ, bool EPI>
+// EPI: 0 = store the transform, 1 = combine epilogue with epi_x, 2 = combine
+// epilogue with the key inner product formed in place of epi_x.
+template <int LA, int LB, int ROWS, int LZ, int EPI>
 __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, min_blocks<LB, ROWS>())
     ntt_fwd_rows(const NttArgs g) {
   using P = PassShape<LB>;
@@ -270,7 +272,7 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, min_blocks<LB, ROWS>(
     for (int u = 0; u < P::R; ++u) srow[rpad(t + P::T * u)] = fwd_final(x[u], q, q2, mu);
   }
   __syncthreads();
-  if constexpr (EPI) {
+  if constexpr (EPI == 1) {
     // combine epilogue: (x - v) * w (+ add on component 0), same coalesced layout
     const size_t off = (size_t)blockIdx.z * n + ((size_t)blockIdx.x * ROWS + rr) * P::S;
     const uint64_t* ex = g.epi_x + blockIdx.y * g.epi_x_comp + off;
@@ -281,6 +283,32 @@ __global__ void __launch_bounds__(ROWS * PassShape<LB>::T, min_blocks<LB, ROWS>(
     for (int u = 0; u < P::R; ++u) {
       const int k = t + P::T * u;
       uint64_t r = shoup_mul(sub_mod(ex[k], srow[rpad(k)], q), w.w, w.wp, q);
+      if (ea) r = add_mod(r, ea[k], q);
+      eo[k] = r;
+    }
+  } else if constexpr (EPI == 2) {
+    // key-switching combine: x = sum_j ext[j][l] key[j][c][l] (128-bit sum,
+    // each product below q^2 and at most 15 digits), then (x - v) w (+ add)
+    const size_t row_off = ((size_t)blockIdx.x * ROWS + rr) * P::S;
+    const size_t off = (size_t)blockIdx.z * n + row_off;
+    uint64_t* eo = g.epi_out + blockIdx.y * g.epi_out_comp + off;
+    const uint64_t* ea = (g.epi_add && blockIdx.y == 0) ? g.epi_add + off : nullptr;
+    const Twiddle w = g.epi_w[pidx];
+    const Modulus m = g.epi_mods[pidx];
+    const size_t ext_stride = (size_t)g.epi_w_rows * n, key_stride = (size_t)2 * g.epi_key_limbs * n;
+    const uint64_t* e0 = g.epi_ext + off;
+    const uint64_t* k0 = g.epi_key + ((size_t)blockIdx.y * g.epi_key_limbs + pidx) * n + row_off;
+#pragma unroll
+    for (int u = 0; u < P::R; ++u) {
+      const int k = t + P::T * u;
+      uint64_t hi = 0, lo = 0;
+      for (uint32_t j = 0; j < g.epi_digits; ++j) {
+        const uint64_t a = e0[j * ext_stride + k], b = k0[j * key_stride + k];
+        const uint64_t pl = a * b;
+        lo += pl;
+        hi += __umul64hi(a, b) + (lo < pl);
+      }
+      uint64_t r = shoup_mul(sub_mod(reduce_u128(hi, lo, m), srow[rpad(k)], q), w.w, w.wp, q);
       if (ea) r = add_mod(r, ea[k], q);
       eo[k] = r;
     }
@@ -445,7 +473,7 @@ size_t cols_smem() {
 // the config-2 batch against 16 and 32 with several register caps: small
 // CTAs with ~100 registers keep the integer pipes busiest.
 
-template <int LA, int LB, int LZ, int TW, bool EPI>
+template <int LA, int LB, int LZ, int TW, int EPI>
 cudaError_t launch_fwd_impl(const NttArgs& g) {
   using PA = PassShape<LA>;
   using PB = PassShape<LB>;
@@ -463,7 +491,7 @@ cudaError_t launch_fwd_impl(const NttArgs& g) {
   return cudaGetLastError();
 }
 
-template <int LA, int LB, int TW, bool EPI>
+template <int LA, int LB, int TW, int EPI>
 cudaError_t launch_fwd_lz(const NttArgs& g) {
   switch (g.lazy) {
     case 32: return launch_fwd_impl<LA, LB, 32, TW, EPI>(g);
@@ -474,11 +502,17 @@ cudaError_t launch_fwd_lz(const NttArgs& g) {
 
 template <int LA, int LB, int TW>
 cudaError_t launch_fwd_tw(const NttArgs& g) {
+  if (g.epi_out && g.epi_ext) {
+    if (g.list || !g.epi_key || !g.epi_w || !g.epi_mods || g.epi_digits == 0 || g.epi_digits > 15 ||
+        g.n_polys != 2)
+      return cudaErrorInvalidValue;
+    return launch_fwd_lz<LA, LB, TW, 2>(g);
+  }
   if (g.epi_out) {
     if (g.list || !g.epi_x || !g.epi_w) return cudaErrorInvalidValue;
-    return launch_fwd_lz<LA, LB, TW, true>(g);
+    return launch_fwd_lz<LA, LB, TW, 1>(g);
   }
-  return launch_fwd_lz<LA, LB, TW, false>(g);
+  return launch_fwd_lz<LA, LB, TW, 0>(g);
 }
 
 template <int LA, int LB>

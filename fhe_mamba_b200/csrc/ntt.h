@@ -45,6 +45,15 @@ struct NttArgs {
   size_t epi_out_comp = 0;
   const Twiddle* epi_w = nullptr;
   const uint64_t* epi_add = nullptr;
+  // Optional key-switching form of that epilogue: epi_x[c][l] is not read but
+  // formed as the key inner product sum_j ext[j][l] * key[j][c][l] (128-bit
+  // sum, one reduction), so the Q rows of the accumulator are never written
+  // and re-read.  ext: [epi_digits][epi_w_rows][N]; key: [digits][2][key_limbs][N]
+  // with Q limb l on key row l; mods: per-prime Barrett constants.
+  const uint64_t* epi_ext = nullptr;
+  const uint64_t* epi_key = nullptr;
+  uint32_t epi_digits = 0, epi_w_rows = 0, epi_key_limbs = 0;
+  const Modulus* epi_mods = nullptr;
   cudaStream_t stream;
 };
 

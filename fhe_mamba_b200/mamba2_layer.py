@@ -737,7 +737,7 @@ class Mamba2Model:
 
     def __init__(self, layers: int, d_model: int, d_state: int, heads: int, vocab: int, std: float = 0.02,
                  seed: int = 6, calib_sequences: int = 8, calib_tokens: int = 32, calib_prompt: int = 8,
-                 bound_factor: float = 3.0, fused_decay: bool = False):
+                 bound_factor: float = 3.0, fused_decay: bool = False, calib_threads: int | None = None):
         self.layers = [Mamba2Weights(d_model=d_model, d_state=d_state, heads=heads, std=std, seed=seed * 1000 + i)
                        for i in range(layers)]
         r = np.random.default_rng(seed)
@@ -757,7 +757,7 @@ class Mamba2Model:
         greedy = np.arange(B) % 2 == 0
         # Sequences run in chunks on a thread pool (numpy releases the GIL in
         # its array loops); the reductions below do not depend on the split.
-        workers = max(1, min(B, os.cpu_count() or 1, 8))
+        workers = max(1, min(B, calib_threads or os.cpu_count() or 1, 8))
         step = -(-B // workers)
         chunks = [slice(i, min(B, i + step)) for i in range(0, B, step)]
 

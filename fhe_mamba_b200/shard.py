@@ -151,26 +151,41 @@ class ShardedKeySwitch:
              self._p(out))
         return out
 
-    def keyswitch(self, d_own, nq: int, kind: int, galois: int = 0, add0=None, add1=None):
-        """[2][q_own][N]: KS(d) (+ add0 on component 0, + add1 on component 1)."""
+    STAGES = ("modup_prepare", "gather_modup_rows", "modup_inner", "gather_p_rows", "moddown")
+
+    def keyswitch(self, d_own, nq: int, kind: int, galois: int = 0, add0=None, add1=None, events=None):
+        """[2][q_own][N]: KS(d) (+ add0 on component 0, + add1 on component 1).
+        events: optional list of 6 CUDA timing events, recorded on the context
+        stream around the five steps (STAGES), for a per-step breakdown."""
         import torch
         q_own = len(self.plan.q_limbs(nq))
         assert tuple(d_own.shape) == (q_own, self.cc.n) and d_own.dtype == torch.int64
         caller = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(caller)
+
+        def mark(i):
+            if events is not None:
+                events[i].record(self.stream)
+
         with torch.cuda.stream(self.stream):
+            mark(0)
             send = self.stage_prepare(d_own, nq)
+            mark(1)
             gathered = all_gather_rows(send, self.group)
+            mark(2)
             acc, p_send = self.stage_inner(nq, kind, galois, gathered, d_own)
+            mark(3)
             p_gathered = all_gather_rows(p_send, self.group)
+            mark(4)
             out = self.stage_moddown(nq, acc, p_gathered, add0, add1)
+            mark(5)
         caller.wait_stream(self.stream)
         return out
 
-    def relinearize(self, ct_own, nq: int):
+    def relinearize(self, ct_own, nq: int, events=None):
         """(d0, d1, d2) own rows -> (d0 + KS0(d2), d1 + KS1(d2)) with the relinearisation key."""
         self.load_key(2)
-        return self.keyswitch(ct_own[2], nq, 2, 0, ct_own[0], ct_own[1])
+        return self.keyswitch(ct_own[2], nq, 2, 0, ct_own[0], ct_own[1], events)
 
     def rotate(self, ct_own, nq: int, step: int):
         """EvalRotate of own rows: KS(c1) + (c0, 0), then the automorphism."""

@@ -317,6 +317,18 @@ int fhe_ctx_level_counts(fhe_ctx* ctx, int32_t kind, uint64_t* out, uint32_t n);
  * runs wherever the tensor cores are not used.
  * Both produce identical words.  No counterpart call in the reference. */
 int fhe_ctx_set_conversion(fhe_ctx* ctx, int32_t kernel);
+/* Returns the device's freed library memory (kept in its stream-ordered
+ * pool between contexts for reuse) to the driver, after a device
+ * synchronisation: for a caller that switches to parameters with differently
+ * sized buffers (ring 2^16 to 2^17).  No counterpart in the reference. */
+int fhe_device_trim(int32_t device);
+/* fused != 0: the key inner product of the Q limbs is formed inside the
+ * ModDown's last NTT pass (its combine epilogue reads the ModUp digits and
+ * the key), so the accumulator's Q rows are never written and re-read; the P
+ * limbs keep the separate inner product.  The FIDESlib counterpart is its
+ * NTT's KSK_DOT / KSK_DOT_ACC modes (experiments/ntt_warp_tail/probe.cu:70-73),
+ * which fuse the product into the ModUp side instead.  Identical words. */
+int fhe_ctx_set_keyswitch_fusion(fhe_ctx* ctx, int32_t fused);
 /* Number of tensor-core conversion blocks whose bounded wait for their MMA
  * ran out (their outputs were skipped); 0 on a healthy device. */
 int fhe_tc_timeouts(uint64_t* count);

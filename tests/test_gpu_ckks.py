@@ -244,10 +244,12 @@ def test_wide_digit_keyswitch(oracle):
 @pytest.mark.parametrize("shape", ["config1", "config3", "depth44"])
 def test_tensor_core_conversion_matches_oracle(oracle, shape):
     """The key switch with its ModUp and ModDown basis conversions on the
-    tensor cores (tcgen05 int8 MMA over byte-split residues): relinearisation,
-    a rotation and hoisted rotations word for word against the oracle and
-    against the CUDA-core conversion, at config 1 (5 + 5 limbs), the config-3
-    shape (digits of 7 and 6 limbs) and the token loop's 45 + 15 limbs."""
+    tensor cores (tcgen05 int8 MMA over byte-split residues) and with the Q
+    limbs' key inner product fused into ModDown's last NTT pass:
+    relinearisation, a rotation and hoisted rotations word for word against
+    the oracle and against the CUDA-core, unfused key switch, at config 1
+    (5 + 5 limbs), the config-3 shape (digits of 7 and 6 limbs) and the token
+    loop's 45 + 15 limbs."""
     from fhe_mamba_b200 import _lib
     args = {"config1": (14, 8, 50, 60, 2), "config3": (16, 19, 59, 60, 3), "depth44": (16, 44, 59, 60, 3)}[shape]
     cc, oc, s, sn = _setup(oracle, *args)
@@ -260,13 +262,19 @@ def test_tensor_core_conversion_matches_oracle(oracle, shape):
     cc.EvalRotateKeyGen(steps)
     out = {}
     for kernel in ("cuda", "tensor-all"):
-        cc.SetConversionKernel(kernel)
-        ct2 = cc.upload(d[:2])
-        out[kernel] = [cc.Relinearize(cc.upload(d, noise_deg=2)).residues(),
-                       cc.EvalRotate(ct2, 1).residues()] + [h.residues() for h in cc.EvalFastRotation(ct2, steps)]
+        for fused in (False, True):
+            cc.SetConversionKernel(kernel)
+            cc.SetKeySwitchFusion(fused)
+            ct2 = cc.upload(d[:2])
+            out[kernel, fused] = ([cc.Relinearize(cc.upload(d, noise_deg=2)).residues(),
+                                   cc.EvalRotate(ct2, 1).residues()] +
+                                  [h.residues() for h in cc.EvalFastRotation(ct2, steps)])
     cc.SetConversionKernel("cuda")
-    for a, b in zip(out["cuda"], out["tensor-all"]):
-        assert np.array_equal(a, b)
+    cc.SetKeySwitchFusion(False)
+    for key in out:
+        for a, b in zip(out["cuda", False], out[key]):
+            assert np.array_equal(a, b), key
+    out["tensor-all"] = out["tensor-all", True]
     assert np.array_equal(out["tensor-all"][0], oc.relinearize(d, oc.relin_key(SEED, sn)))
     g = cc.galois_element(1)
     assert np.array_equal(out["tensor-all"][1], oc.rotate(d[:2], g, oc.rot_key(SEED, s, sn, g)))
