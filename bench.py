@@ -418,6 +418,17 @@ def measure_sharded_keyswitch(local, world, reps=20):
         e1.record(sk.stream)
         e1.synchronize()
         ms = e0.elapsed_time(e1) / reps
+        for _ in range(3):
+            sk.relinearize(own, nq, split=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(sk.stream)
+        for _ in range(reps):
+            sk.relinearize(own, nq, split=True)
+        e1.record(sk.stream)
+        e1.synchronize()
+        ms_split = e0.elapsed_time(e1) / reps
+        exact_split = np.array_equal(to_host_rows(sk.relinearize(own, nq, split=True)), sk.plan.own_rows(want, nq))
         # per-step breakdown (device time on the context stream; a gather's
         # step includes waiting for the slowest rank to reach it)
         steps = {k: 0.0 for k in sk.STAGES}
@@ -436,14 +447,15 @@ def measure_sharded_keyswitch(local, world, reps=20):
         e1.record(sk.stream)
         e1.synchronize()
         single = e0.elapsed_time(e1) / reps
-        t = torch.tensor([ms, single, 0.0 if exact else 1.0] + [steps[k] for k in sk.STAGES], dtype=torch.float64,
-                         device=dev)
+        t = torch.tensor([ms, single, 0.0 if exact and exact_split else 1.0, ms_split] +
+                         [steps[k] for k in sk.STAGES], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         pl = sk.plan
         gather = (world - 1) * (pl.q_chunk(nq) + 2 * pl.p_chunk) * cc.n * 8
-        breakdown = {k: float(t[3 + i]) for i, k in enumerate(sk.STAGES)}
+        breakdown = {k: float(t[4 + i]) for i, k in enumerate(sk.STAGES)}
         cases.append({"limbs": nq, "ms": float(t[0]), "single_gpu_ms": float(t[1]),
                       "speedup": float(t[1] / t[0]), "bit_exact_all_ranks": bool(t[2] == 0.0),
+                      "ms_digit_split_exchange": float(t[3]), "speedup_digit_split": float(t[1] / t[3]),
                       "received_bytes_per_rank": gather, "step_ms_max_over_ranks": breakdown,
                       "largest_step": max(breakdown, key=breakdown.get)})
         del full

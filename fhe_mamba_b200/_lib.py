@@ -138,6 +138,8 @@ SIGNATURES = {
     "fhe_shard_load_key": [vp, i32, u64],
     "fhe_shard_modup_prepare": [vp, u32, vp, vp],
     "fhe_shard_inner": [vp, u32, i32, u64, vp, vp, vp, vp],
+    "fhe_shard_inner_digit": [vp, u32, u32, vp, vp],
+    "fhe_shard_inner_tail": [vp, u32, i32, u64, vp, vp],
     "fhe_shard_moddown": [vp, u32, vp, vp, vp, vp, vp],
     "fhe_shard_automorphism": [vp, u32, u64, vp, vp],
     "fhe_bootstrap_setup": [vp, u32, u32, u32, i32, i32, u32],

@@ -614,6 +614,24 @@ int fhe_shard_inner(fhe_ctx* ctx, uint32_t n_limbs, int32_t kind, uint64_t galoi
   });
 }
 
+int fhe_shard_inner_digit(fhe_ctx* ctx, uint32_t n_limbs, uint32_t digit, const uint64_t* gathered_digit,
+                          const uint64_t* d_own) {
+  return guarded([&] {
+    const fhe::ShardPlan p = shard_of(ctx).plan(n_limbs);
+    fhe::require(gathered_digit != nullptr && (d_own != nullptr || p.q_own == 0), "null buffer");
+    shard_of(ctx).inner_digit(n_limbs, digit, gathered_digit, d_own);
+  });
+}
+
+int fhe_shard_inner_tail(fhe_ctx* ctx, uint32_t n_limbs, int32_t kind, uint64_t galois, uint64_t* acc,
+                         uint64_t* p_send) {
+  return guarded([&] {
+    const fhe::ShardPlan p = shard_of(ctx).plan(n_limbs);
+    fhe::require((acc != nullptr || p.rows == 0) && (p_send != nullptr || p.p_chunk == 0), "null buffer");
+    shard_of(ctx).inner_tail(n_limbs, kind, galois, acc, p_send);
+  });
+}
+
 int fhe_shard_moddown(fhe_ctx* ctx, uint32_t n_limbs, const uint64_t* acc, const uint64_t* p_gathered,
                       const uint64_t* add0, const uint64_t* add1, uint64_t* out) {
   return guarded([&] {

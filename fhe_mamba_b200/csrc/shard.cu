@@ -134,7 +134,12 @@ ShardKeySwitch::Level& ShardKeySwitch::level(uint32_t nq) {
     if (bytes) std::memcpy(blob.data() + off, src, bytes);
     return off;
   };
-  struct Tab { size_t sp, dp, sr, dr, hi, h; uint32_t ns, nt; };
+  struct Tab { size_t sp, dp, sr, dr, hi, h, srs; uint32_t ns, nt; };
+  // Per-digit exchange: digit j's own rows of every rank, padded to dchunk
+  // rows, gathered into [W][dchunk][N]; limb l of digit j at row
+  // (l % W) * dchunk + (index of l among rank l % W's limbs of the digit).
+  const uint32_t dchunk = (a + W - 1) / W;
+  T.dchunk = dchunk;
   std::vector<Tab> dig(pl.digits);
   std::vector<uint2> ext_list;
   T.digit_ns.resize(pl.digits);
@@ -143,12 +148,14 @@ ShardKeySwitch::Level& ShardKeySwitch::level(uint32_t nq) {
   T.digit_own_hi.resize(pl.digits);
   for (uint32_t j = 0; j < pl.digits; ++j) {
     const uint32_t lo = j * a, hi = std::min(lo + a, nq), ns = hi - lo;
-    std::vector<uint32_t> sp(ns), sr(ns), dp, dr;
+    std::vector<uint32_t> sp(ns), sr(ns), srs(ns), dp, dr;
     std::vector<Shoup> hinv(ns), hat;
     for (uint32_t i = 0; i < ns; ++i) {
       const uint32_t l = lo + i;
       sp[i] = l;
       sr[i] = (l % W) * pl.q_chunk + l / W;
+      const uint32_t first = lo + (l % W + W - lo % W) % W;  // rank l % W's first limb of the digit
+      srs[i] = (l % W) * dchunk + (l - first) / W;
       const uint64_t qi = P[l];
       uint64_t h = 1 % qi;
       for (uint32_t m = lo; m < hi; ++m)
@@ -185,6 +192,7 @@ ShardKeySwitch::Level& ShardKeySwitch::level(uint32_t nq) {
     tb.sp = put(sp.data(), sp.size() * 4);
     tb.dp = put(dp.data(), dp.size() * 4);
     tb.sr = put(sr.data(), sr.size() * 4);
+    tb.srs = put(srs.data(), srs.size() * 4);
     tb.dr = put(dr.data(), dr.size() * 4);
     tb.hi = put(hinv.data(), hinv.size() * sizeof(Shoup));
     tb.h = put(hat.data(), hat.size() * sizeof(Shoup));
@@ -241,10 +249,12 @@ ShardKeySwitch::Level& ShardKeySwitch::level(uint32_t nq) {
   const char* base = T.blob.as<char>();
   auto u32 = [base](size_t o) { return reinterpret_cast<const uint32_t*>(base + o); };
   auto sh = [base](size_t o) { return reinterpret_cast<const Shoup*>(base + o); };
-  std::vector<ConvTable> tabs(pl.digits);
+  std::vector<ConvTable> tabs(2 * pl.digits);  // whole-gather tables, then per-digit-gather tables
   for (uint32_t j = 0; j < pl.digits; ++j) {
     const Tab& tb = dig[j];
     tabs[j] = ConvTable{tb.ns, tb.nt, u32(tb.sp), u32(tb.dp), sh(tb.hi), sh(tb.h), u32(tb.sr), u32(tb.dr)};
+    tabs[pl.digits + j] = ConvTable{tb.ns, tb.nt, u32(tb.sp), u32(tb.dp), sh(tb.hi), sh(tb.h), u32(tb.srs),
+                                    u32(tb.dr)};
   }
   T.digit_tabs = DevMem(std::max<size_t>(tabs.size() * sizeof(ConvTable), 16));
   if (!tabs.empty())
@@ -284,6 +294,42 @@ void ShardKeySwitch::modup_prepare(uint32_t nq, const uint64_t* d_own, uint64_t*
 void ShardKeySwitch::inner(uint32_t nq, int kind, uint64_t g, const uint64_t* gathered, const uint64_t* d_own,
                            uint64_t* acc, uint64_t* p_send) {
   Level& T = level(nq);
+  require(keys_.count(key_id(kind, g)) != 0, "shard key not loaded (fhe_shard_load_key)", -4);
+  ++ck_.counters.modup;
+  for (uint32_t j = 0; j < T.pl.digits; ++j) convert_digit(T, j, gathered, false, d_own);
+  inner_tail(nq, kind, g, acc, p_send);
+}
+
+void ShardKeySwitch::convert_digit(Level& T, uint32_t j, const uint64_t* gathered, bool split,
+                                   const uint64_t* d_own) {
+  const ShardPlan& pl = T.pl;
+  const Context& c = ck_.ctx;
+  const uint32_t n = c.n;
+  const size_t ext_words = (size_t)pl.digits * pl.rows * n;
+  if (ext_.bytes < ext_words * 8) {
+    FHE_CUDA(cudaStreamSynchronize(c.stream));
+    ext_ = DevMem(ext_words * 8);
+  }
+  uint64_t* e = ext_.as<uint64_t>() + (size_t)j * pl.rows * n;
+  const uint32_t lo = T.digit_own_lo[j], hi = T.digit_own_hi[j];
+  if (hi > lo)
+    FHE_CUDA(cudaMemcpyAsync(e + (size_t)lo * n, d_own + (size_t)lo * n, (size_t)(hi - lo) * n * 8,
+                             cudaMemcpyDeviceToDevice, c.stream));
+  if (T.digit_nt[j])
+    launch_convert(gathered, 0, e, 0, 1, T.digit_tabs.as<ConvTable>() + (split ? pl.digits : 0) + j,
+                   T.digit_ns[j], T.digit_nt[j], n, c.d_mod.as<Modulus>(), c.stream,
+                   c.max_prime() < (uint64_t(1) << 60));
+}
+
+void ShardKeySwitch::inner_digit(uint32_t nq, uint32_t j, const uint64_t* gathered_j, const uint64_t* d_own) {
+  Level& T = level(nq);
+  require(j < T.pl.digits, "digit index out of range", -1);
+  if (j == 0) ++ck_.counters.modup;
+  convert_digit(T, j, gathered_j, true, d_own);
+}
+
+void ShardKeySwitch::inner_tail(uint32_t nq, int kind, uint64_t g, uint64_t* acc, uint64_t* p_send) {
+  Level& T = level(nq);
   const ShardPlan& pl = T.pl;
   const Context& c = ck_.ctx;
   const uint32_t n = c.n;
@@ -295,17 +341,6 @@ void ShardKeySwitch::inner(uint32_t nq, int kind, uint64_t g, const uint64_t* ga
     ext_ = DevMem(ext_words * 8);
   }
   uint64_t* ext = ext_.as<uint64_t>();
-  ++ck_.counters.modup;
-  for (uint32_t j = 0; j < pl.digits; ++j) {
-    uint64_t* e = ext + (size_t)j * pl.rows * n;
-    const uint32_t lo = T.digit_own_lo[j], hi = T.digit_own_hi[j];
-    if (hi > lo)
-      FHE_CUDA(cudaMemcpyAsync(e + (size_t)lo * n, d_own + (size_t)lo * n, (size_t)(hi - lo) * n * 8,
-                               cudaMemcpyDeviceToDevice, c.stream));
-    if (T.digit_nt[j])
-      launch_convert(gathered, 0, e, 0, 1, T.digit_tabs.as<ConvTable>() + j, T.digit_ns[j], T.digit_nt[j], n,
-                     c.d_mod.as<Modulus>(), c.stream, c.max_prime() < (uint64_t(1) << 60));
-  }
   ntt_list(ext, T.ext_list, T.ext_len, false);
   ++ck_.counters.key_inner;
   if (pl.rows) {

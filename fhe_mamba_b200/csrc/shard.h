@@ -41,6 +41,13 @@ class ShardKeySwitch {
   void modup_prepare(uint32_t nq, const uint64_t* d_own, uint64_t* send);
   void inner(uint32_t nq, int kind, uint64_t g, const uint64_t* gathered, const uint64_t* d_own, uint64_t* acc,
              uint64_t* p_send);
+  // The same stage with the first exchange split by digit, so the caller can
+  // overlap digit j + 1's all-gather with digit j's conversion:
+  // inner_digit for every digit j (gathered_j = digit j's own rows of every
+  // rank, [W][dchunk][N], dchunk = ceil(alpha / W); rank r sends its digit-j
+  // rows padded to dchunk), then inner_tail.
+  void inner_digit(uint32_t nq, uint32_t j, const uint64_t* gathered_j, const uint64_t* d_own);
+  void inner_tail(uint32_t nq, int kind, uint64_t g, uint64_t* acc, uint64_t* p_send);
   void moddown(uint32_t nq, const uint64_t* acc, const uint64_t* p_gathered, const uint64_t* add0,
                const uint64_t* add1, uint64_t* out);
   // Slot permutation of 2 components of q_own rows each (limb-local).
@@ -59,9 +66,10 @@ class ShardKeySwitch {
     const uint32_t* row_prime = nullptr;  // prime index of each own extended row
     const Shoup* pinv_rows = nullptr;     // P^{-1} mod q of each own Q row
     const uint64_t* q_rows = nullptr;     // q of each own Q row
-    uint32_t ext_len = 0;
+    uint32_t ext_len = 0, dchunk = 0;
     std::vector<uint32_t> digit_ns, digit_nt, digit_own_lo, digit_own_hi;
   };
+  void convert_digit(Level& T, uint32_t j, const uint64_t* gathered, bool split, const uint64_t* d_own);
   Level& level(uint32_t nq);
   uint64_t key_id(int kind, uint64_t g) const;
   uint32_t q_own(uint32_t nq) const { return nq > rank ? (nq - 1 - rank) / world + 1 : 0; }

@@ -67,6 +67,25 @@ class ShardPlan:
         """Row of P limb p, component comp, in the second all-gather's output [W][2][p_chunk][N]."""
         return ((p % self.world) * 2 + comp) * self.p_chunk + p // self.world
 
+    # per-digit exchange (fhe_shard_inner_digit)
+    @property
+    def digit_chunk(self) -> int:
+        """Rows per rank in a digit's all-gather: ceil(alpha / world)."""
+        return -(-self.alpha // self.world)
+
+    def digit_rows(self, nq: int, j: int) -> tuple[int, int]:
+        """[lo, hi): this rank's own rows (send-buffer rows) of HYBRID digit j."""
+        lo, hi = j * self.alpha, min((j + 1) * self.alpha, nq)
+        rows = [i for i, l in enumerate(self.q_limbs(nq)) if lo <= l < hi]
+        return (rows[0], rows[-1] + 1) if rows else (0, 0)
+
+    def split_row(self, l: int) -> int:
+        """Row of Q limb l in its digit's all-gather output [W][digit_chunk][N]
+        (the library's source-row map of fhe_shard_inner_digit)."""
+        lo = (l // self.alpha) * self.alpha
+        first = lo + (l % self.world - lo % self.world) % self.world
+        return (l % self.world) * self.digit_chunk + (l - first) // self.world
+
     # host-side packing (numpy or torch arrays of rows)
     def own_rows(self, full, nq: int):
         """The own Q rows of a [..., nq, N] array."""
@@ -144,6 +163,34 @@ class ShardedKeySwitch:
              self._p(p_send))
         return acc, p_send
 
+    def digit_rows(self, nq: int, j: int) -> tuple[int, int]:
+        return self.plan.digit_rows(nq, j)
+
+    def stage_inner_split(self, nq: int, kind: int, galois: int, send, d_own):
+        """The inner stage with the first exchange split by digit: digit j + 1's
+        all-gather (asynchronous, NCCL's own stream) overlaps digit j's
+        conversion on the context stream."""
+        import torch
+        import torch.distributed as dist
+        pl, n, W = self.plan, self.cc.n, self.world
+        D = pl.digits(nq)
+        dchunk = pl.digit_chunk
+        gathered = torch.empty((D, W * dchunk, n), dtype=torch.int64, device=self.device)
+        works = []
+        for j in range(D):
+            lo, hi = self.digit_rows(nq, j)
+            part = torch.zeros((dchunk, n), dtype=torch.int64, device=self.device)
+            if hi > lo:
+                part[: hi - lo] = send[lo:hi]
+            works.append(dist.all_gather_into_tensor(gathered[j], part, group=self.group, async_op=True))
+        for j in range(D):
+            works[j].wait()  # the context stream waits for digit j's rows only
+            call("fhe_shard_inner_digit", self.cc.h, nq, j, self._p(gathered[j]), self._p(d_own))
+        acc = torch.empty((2, pl.rows(nq), n), dtype=torch.int64, device=self.device)
+        p_send = torch.empty((2, pl.p_chunk, n), dtype=torch.int64, device=self.device)
+        call("fhe_shard_inner_tail", self.cc.h, nq, kind, galois, self._p(acc), self._p(p_send))
+        return acc, p_send
+
     def stage_moddown(self, nq: int, acc, p_gathered, add0=None, add1=None):
         import torch
         out = torch.empty((2, len(self.plan.q_limbs(nq)), self.cc.n), dtype=torch.int64, device=self.device)
@@ -153,10 +200,14 @@ class ShardedKeySwitch:
 
     STAGES = ("modup_prepare", "gather_modup_rows", "modup_inner", "gather_p_rows", "moddown")
 
-    def keyswitch(self, d_own, nq: int, kind: int, galois: int = 0, add0=None, add1=None, events=None):
+    def keyswitch(self, d_own, nq: int, kind: int, galois: int = 0, add0=None, add1=None, events=None,
+                  split: bool = False):
         """[2][q_own][N]: KS(d) (+ add0 on component 0, + add1 on component 1).
         events: optional list of 6 CUDA timing events, recorded on the context
-        stream around the five steps (STAGES), for a per-step breakdown."""
+        stream around the five steps (STAGES), for a per-step breakdown.
+        split: the first exchange runs per digit, overlapped with the
+        conversions (its events then bracket the gathers and conversions
+        together)."""
         import torch
         q_own = len(self.plan.q_limbs(nq))
         assert tuple(d_own.shape) == (q_own, self.cc.n) and d_own.dtype == torch.int64
@@ -171,9 +222,13 @@ class ShardedKeySwitch:
             mark(0)
             send = self.stage_prepare(d_own, nq)
             mark(1)
-            gathered = all_gather_rows(send, self.group)
-            mark(2)
-            acc, p_send = self.stage_inner(nq, kind, galois, gathered, d_own)
+            if split:
+                acc, p_send = self.stage_inner_split(nq, kind, galois, send, d_own)
+                mark(2)
+            else:
+                gathered = all_gather_rows(send, self.group)
+                mark(2)
+                acc, p_send = self.stage_inner(nq, kind, galois, gathered, d_own)
             mark(3)
             p_gathered = all_gather_rows(p_send, self.group)
             mark(4)
@@ -182,10 +237,10 @@ class ShardedKeySwitch:
         caller.wait_stream(self.stream)
         return out
 
-    def relinearize(self, ct_own, nq: int, events=None):
+    def relinearize(self, ct_own, nq: int, events=None, split: bool = False):
         """(d0, d1, d2) own rows -> (d0 + KS0(d2), d1 + KS1(d2)) with the relinearisation key."""
         self.load_key(2)
-        return self.keyswitch(ct_own[2], nq, 2, 0, ct_own[0], ct_own[1], events)
+        return self.keyswitch(ct_own[2], nq, 2, 0, ct_own[0], ct_own[1], events, split)
 
     def rotate(self, ct_own, nq: int, step: int):
         """EvalRotate of own rows: KS(c1) + (c0, 0), then the automorphism."""

@@ -259,6 +259,17 @@ int fhe_shard_load_key(fhe_ctx* ctx, int32_t kind, uint64_t galois);
 int fhe_shard_modup_prepare(fhe_ctx* ctx, uint32_t n_limbs, const uint64_t* d_own, uint64_t* send);
 int fhe_shard_inner(fhe_ctx* ctx, uint32_t n_limbs, int32_t kind, uint64_t galois, const uint64_t* gathered,
                     const uint64_t* d_own, uint64_t* acc, uint64_t* p_send);
+/* fhe_shard_inner with the first exchange split by HYBRID digit, so that
+ * digit j + 1's all-gather overlaps digit j's conversion: for every digit j,
+ * rank r sends its own rows of digit j (send rows of limbs in
+ * [j*alpha, min((j+1)*alpha, n_limbs)), in limb order) padded with zero rows
+ * to dchunk = ceil(alpha / world) rows, the caller all-gathers them into
+ * gathered_digit [W][dchunk][N] and calls fhe_shard_inner_digit; then
+ * fhe_shard_inner_tail (NTT, key inner product, own P rows into p_send). */
+int fhe_shard_inner_digit(fhe_ctx* ctx, uint32_t n_limbs, uint32_t digit, const uint64_t* gathered_digit,
+                          const uint64_t* d_own);
+int fhe_shard_inner_tail(fhe_ctx* ctx, uint32_t n_limbs, int32_t kind, uint64_t galois, uint64_t* acc,
+                         uint64_t* p_send);
 int fhe_shard_moddown(fhe_ctx* ctx, uint32_t n_limbs, const uint64_t* acc, const uint64_t* p_gathered,
                       const uint64_t* add0, const uint64_t* add1, uint64_t* out);
 /* Slot permutation of both components of the own rows ([2][q_own][N]). */

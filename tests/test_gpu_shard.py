@@ -114,6 +114,59 @@ def test_sharded_relinearize_and_rotate_equal_single_gpu(setup, world, nq):
         assert np.array_equal(host(rot), sk.plan.own_rows(want, nq)), (world, nq, sk.rank)
 
 
+@pytest.mark.parametrize("world,nq", [(2, 12), (3, 12), (4, 9), (3, 2)])
+def test_split_exchange_equals_single_gpu(setup, world, nq):
+    """The first exchange split by HYBRID digit (fhe_shard_inner_digit /
+    fhe_shard_inner_tail, what ShardedKeySwitch(split=True) overlaps with the
+    conversions): each digit's padded rows of every rank concatenated, the
+    result equal to the single-GPU relinearisation word for word."""
+    import torch
+    from fhe_mamba_b200._lib import call
+    from fhe_mamba_b200.shard import ShardedKeySwitch, to_device_rows, to_host_rows
+    ref = setup
+    dev = torch.device("cuda", 0)
+    ranks = [ShardedKeySwitch(_ctx(), rank=r, world=world) for r in range(world)]
+    d = _rand_ct(ref, nq, 3, 300 + world * 16 + nq)
+    want = ref.Relinearize(ref.upload(d, noise_deg=2)).residues()
+    for sk in ranks:
+        sk.load_key(2)
+    own = [to_device_rows(sk.plan.own_rows(d[2], nq), dev) for sk in ranks]
+    torch.cuda.synchronize()
+    sends = [sk.stage_prepare(x, nq) for sk, x in zip(ranks, own)]
+    for sk in ranks:
+        sk.cc.synchronize()
+    pl = ranks[0].plan
+    dchunk = -(-pl.alpha // world)
+    for j in range(pl.digits(nq)):
+        parts = []
+        for sk, snd in zip(ranks, sends):
+            lo, hi = sk.digit_rows(nq, j)
+            part = torch.zeros((dchunk, ref.n), dtype=torch.int64, device=dev)
+            if hi > lo:
+                part[: hi - lo] = snd[lo:hi]
+            parts.append(part)
+        gathered = torch.cat(parts)
+        torch.cuda.synchronize()
+        for sk, x in zip(ranks, own):
+            call("fhe_shard_inner_digit", sk.cc.h, nq, j, sk._p(gathered), sk._p(x))
+            sk.cc.synchronize()
+    inner = []
+    for sk in ranks:
+        acc = torch.empty((2, sk.plan.rows(nq), ref.n), dtype=torch.int64, device=dev)
+        p_send = torch.empty((2, sk.plan.p_chunk, ref.n), dtype=torch.int64, device=dev)
+        call("fhe_shard_inner_tail", sk.cc.h, nq, 2, 0, sk._p(acc), sk._p(p_send))
+        sk.cc.synchronize()
+        inner.append((acc, p_send))
+    p_gathered = torch.cat([ps for _, ps in inner])
+    torch.cuda.synchronize()
+    for sk, (acc, _) in zip(ranks, inner):
+        a0 = to_device_rows(sk.plan.own_rows(d[0], nq), dev)
+        a1 = to_device_rows(sk.plan.own_rows(d[1], nq), dev)
+        out = sk.stage_moddown(nq, acc, p_gathered, a0, a1)
+        sk.cc.synchronize()
+        assert np.array_equal(to_host_rows(out), sk.plan.own_rows(want, nq)), (world, nq, sk.rank)
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -144,6 +197,9 @@ def _nccl_worker(rank, world, port, results):
         out = sk.relinearize(own, nq)
         torch.cuda.synchronize()
         ok = np.array_equal(to_host_rows(out), sk.plan.own_rows(want, nq))
+        out = sk.relinearize(own, nq, split=True)  # per-digit exchange overlapped with the conversions
+        torch.cuda.synchronize()
+        ok = ok and np.array_equal(to_host_rows(out), sk.plan.own_rows(want, nq))
         cc.EvalRotateKeyGen([5])
         c = _rand_ct(cc, nq, 2, 4343)
         want = cc.EvalRotate(cc.upload(c), 5).residues()

@@ -87,3 +87,23 @@ def test_gloo_exchange_reassembles_limbs(world, nq):
         p.join(120)
         assert p.exitcode == 0
     assert all(results[r] for r in range(world))
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+@pytest.mark.parametrize("nq,alpha", [(45, 15), (20, 7), (31, 15), (9, 4), (2, 15)])
+def test_digit_split_exchange_places_every_limb(world, nq, alpha):
+    """Per-digit exchange: every rank's own rows of digit j, padded to
+    ceil(alpha / W) rows and gathered in rank order, put Q limb l of the digit
+    at the row the library's conversion reads (ShardPlan.split_row)."""
+    from fhe_mamba_b200.shard import ShardPlan
+    plans = [ShardPlan(n_q=45, n_p=15, alpha=alpha, rank=r, world=world) for r in range(world)]
+    dc = plans[0].digit_chunk
+    for j in range(plans[0].digits(nq)):
+        gathered = []
+        for pl in plans:
+            lo, hi = pl.digit_rows(nq, j)
+            rows = [pl.q_limbs(nq)[i] for i in range(lo, hi)]
+            assert len(rows) <= dc
+            gathered += rows + [None] * (dc - len(rows))
+        for l in range(j * alpha, min((j + 1) * alpha, nq)):
+            assert gathered[plans[0].split_row(l)] == l, (j, l)
