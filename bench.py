@@ -57,6 +57,10 @@ N_ROTATE = 4
 # side measurements ("tensor": tcgen05 int8 MMA, "cuda": 64-bit CUDA-core
 # multiply-accumulates; identical words).  Set from --conversion.
 CONVERSION = "tensor"
+# Byte budget of the encoded-diagonal cache of the layers' matvecs (--diagonal-cache-gb;
+# None: 40 GB at ring 2^16, 8 GB at 2^17).  The diagonals are generated on the device
+# from the weights, so a cache only saves their encoding.
+DIAGONAL_CACHE_GB = None
 # Key inner product of the Q limbs inside ModDown's last NTT pass (--keyswitch-fusion).
 FUSED_KEY_INNER = False
 
@@ -541,7 +545,7 @@ class TokenLoop:
         self.cc.EvalBootstrapKeyGen()
         # ring 2^17 doubles every key and ciphertext: a smaller diagonal cache
         if cache_gb is None:
-            cache_gb = 8 if classical128 else 40
+            cache_gb = DIAGONAL_CACHE_GB if DIAGONAL_CACHE_GB is not None else (8 if classical128 else 40)
         self.em = EncryptedMamba2Model(self.cc, self.model, passes=passes, cache_gb=cache_gb)
         self.cc.EvalRotateKeyGen(self.em.rotation_steps())
         self.cc.synchronize()
@@ -690,7 +694,8 @@ def config_dict(args):
             "bootstrap_passes": args.passes, "conversion_kernel": args.conversion,
             "keyswitch_fusion": args.keyswitch_fusion, "decay": "fused per-head series" if args.decay == "fused" and args.security == "not-set" else "exp(a softplus)",
             "secret_key_dist": f"sparse-encapsulated h={args.sparse_h}" if args.sparse_h else "uniform-ternary",
-            "l2": "inputs larger than L2 (keys ~36 GB, cached diagonals)",
+            "l2": "inputs larger than L2 (keys ~36 GB, diagonals generated on the device)",
+            "diagonal_cache_gb": args.diagonal_cache_gb,
             "parallelism": "one token-loop replica per GPU"}
 
 
@@ -762,6 +767,8 @@ def main():
                          "freshly calibrated model")
     ap.add_argument("--conversion", default="tensor", choices=["tensor", "cuda"],
                     help="basis conversions of the key switches on the tensor cores or the CUDA cores")
+    ap.add_argument("--diagonal-cache-gb", type=float, default=None,
+                    help="encoded-diagonal cache budget (default 40 at ring 2^16, 8 at 2^17; 0: encode every time)")
     ap.add_argument("--keyswitch-fusion", default="off", choices=["on", "off"],
                     help="form the Q limbs' key inner product inside ModDown's last NTT pass")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -775,8 +782,9 @@ def main():
     ap.add_argument("--kernel-shares", action="store_true",
                     help="after the warm-up, record one token's kernels (CUPTI) and print their time shares")
     args = ap.parse_args()
-    global CONVERSION, FUSED_KEY_INNER
+    global CONVERSION, FUSED_KEY_INNER, DIAGONAL_CACHE_GB
     CONVERSION = args.conversion
+    DIAGONAL_CACHE_GB = args.diagonal_cache_gb
     FUSED_KEY_INNER = args.keyswitch_fusion == "on"
     if args.warmup < 3:
         ap.error("warmup must be >= 3")

@@ -118,6 +118,7 @@ SIGNATURES = {
     "fhe_rotate_hoisted": [vp, vp, PI32, u32, ctypes.POINTER(vp)],
     "fhe_rescale_noalloc": [vp, vp, u32, u32, vp],
     "fhe_encode_batch": [vp, PD, PD, u32, u32, u32, f64, ctypes.POINTER(vp)],
+    "fhe_encode_replicated_diagonals": [vp, vp, u32, u32, u32, u32, u32, u32, u32, f64, vp],
     "fhe_linear_transform": [vp, vp, ctypes.POINTER(vp), u32, u32, i32, i32, ctypes.POINTER(vp)],
     "fhe_ctx_counters": [vp, vp, i32],
     "fhe_ctx_level_counts": [vp, i32, vp, u32],

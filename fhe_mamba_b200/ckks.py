@@ -150,6 +150,7 @@ class CryptoContext:
         h = vp()
         call("fhe_ctx_create", ctypes.byref(p), ctypes.byref(h))
         self.h = h
+        self.device = params.device
         info = (ctypes.c_uint32 * 8)()
         call("fhe_ctx_info", h, ctypes.cast(info, vp))
         self.log_n, self.n_q, self.n_p, self.dnum, self.alpha, self.slots = list(info)[:6]
@@ -228,6 +229,15 @@ class CryptoContext:
         outs = (vp * arr.shape[0])()
         call("fhe_encode_batch", self.h, re.ctypes.data_as(PD), im.ctypes.data_as(PD), arr.shape[0],
              arr.shape[1], self.n_q - level, float(scale), outs)
+        return [Plaintext(self, vp(o)) for o in outs]
+
+    def MakeReplicatedDiagonals(self, w_dev_ptr: int, m: int, cols: int, R: int, T: int, win: int, baby: int,
+                                level=0, scale=0.0):
+        """The T diagonal plaintexts of a replicated BSGS layout generated on the
+        device from W (m x cols, fp64, row-major, device pointer w_dev_ptr)."""
+        outs = (vp * T)()
+        call("fhe_encode_replicated_diagonals", self.h, vp(w_dev_ptr), m, cols, R, T, win, baby, self.n_q - level,
+             float(scale), outs)
         return [Plaintext(self, vp(o)) for o in outs]
 
     def EvalLinearTransform(self, ct, diagonals, baby: int, giant: int, stride: int = 1, giant_offset: int = 0):

@@ -548,6 +548,19 @@ int fhe_encode_batch(fhe_ctx* ctx, const double* re, const double* im, uint32_t 
   });
 }
 
+int fhe_encode_replicated_diagonals(fhe_ctx* ctx, const double* w_dev, uint32_t m, uint32_t cols, uint32_t R,
+                                    uint32_t T, uint32_t win, uint32_t baby, uint32_t n_limbs, double scale,
+                                    fhe_pt** outs) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(outs != nullptr, "null outputs");
+    const uint32_t nq = n_limbs ? n_limbs : ctx->c.L;
+    fhe::require(nq <= ctx->c.L, "n_limbs above the number of Q primes");
+    auto v = k.encode_replicated_diagonals(w_dev, m, cols, R, T, win, baby, nq, scale > 0 ? scale : k.level_scale(nq));
+    for (uint32_t i = 0; i < T; ++i) outs[i] = new fhe_pt{std::move(v[i])};
+  });
+}
+
 int fhe_linear_transform(fhe_ctx* ctx, const fhe_ct* a, const fhe_pt* const* diags, uint32_t baby,
                          uint32_t giant, int32_t stride, int32_t giant_offset, fhe_ct** out) {
   return guarded([&] {

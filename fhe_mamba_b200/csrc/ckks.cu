@@ -504,27 +504,53 @@ std::vector<std::unique_ptr<Pt>> Ckks::encode_batch(const double* re, const doub
       }
     double2* dv = reinterpret_cast<double2*>(ws(18, 2 * (size_t)nb * slots));
     FHE_CUDA(cudaMemcpyAsync(dv, v.data(), (size_t)nb * slots * sizeof(double2), cudaMemcpyHostToDevice, ctx.stream));
-    launch_fft_special_inv(dv, fft_inv_tw_.as<double2>(), slots, nb, ctx.stream);
-    double* coef = reinterpret_cast<double*>(ws(19, (size_t)nb * n));
-    FHE_CUDA(cudaMemsetAsync(coef, 0, (size_t)nb * n * 8, ctx.stream));
-    FHE_CUDA(cudaMemsetAsync(status_.p, 0, sizeof(unsigned), ctx.stream));
-    launch_encode_round_batch(dv, coef, slots, n, scale, nb, status_.as<unsigned>(), ctx.stream);
-    uint64_t* res = ws(20, (size_t)nb * nq * n);
-    launch_lift_double(coef, res, n, nq, PrimeMap{nq, ctx.L}, ctx.d_mod.as<Modulus>(), nb, ctx.stream);
-    ntt_dense(res, nb, nq, nq, 0, false);
-    for (uint32_t b = 0; b < nb; ++b) {
-      auto p = std::make_unique<Pt>();
-      p->buf = DevMem((size_t)nq * n * 8, ctx.sh);
-      p->nq = nq;
-      p->scale = scale;
-      FHE_CUDA(cudaMemcpyAsync(p->data(), res + (size_t)b * nq * n, (size_t)nq * n * 8, cudaMemcpyDeviceToDevice,
-                               ctx.stream));
-      out.push_back(std::move(p));
-    }
-    unsigned st = 0;
-    FHE_CUDA(cudaMemcpyAsync(&st, status_.p, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx.stream));
-    FHE_CUDA(cudaStreamSynchronize(ctx.stream));
-    require(st == 0, "encode: a scaled value is not finite or reaches 2^126", -1);
+    encode_slots_on_device(dv, nb, nq, scale, out);
+  }
+  return out;
+}
+
+// Encodes nb slot vectors already on the device (dv, [nb][slots], clobbered):
+// special inverse FFT, scale and round, RNS lift, NTT; appends the plaintexts.
+void Ckks::encode_slots_on_device(double2* dv, uint32_t nb, uint32_t nq, double scale,
+                                  std::vector<std::unique_ptr<Pt>>& out) {
+  const uint32_t slots = ctx.slots, n = ctx.n;
+  launch_fft_special_inv(dv, fft_inv_tw_.as<double2>(), slots, nb, ctx.stream);
+  double* coef = reinterpret_cast<double*>(ws(19, (size_t)nb * n));
+  FHE_CUDA(cudaMemsetAsync(coef, 0, (size_t)nb * n * 8, ctx.stream));
+  FHE_CUDA(cudaMemsetAsync(status_.p, 0, sizeof(unsigned), ctx.stream));
+  launch_encode_round_batch(dv, coef, slots, n, scale, nb, status_.as<unsigned>(), ctx.stream);
+  uint64_t* res = ws(20, (size_t)nb * nq * n);
+  launch_lift_double(coef, res, n, nq, PrimeMap{nq, ctx.L}, ctx.d_mod.as<Modulus>(), nb, ctx.stream);
+  ntt_dense(res, nb, nq, nq, 0, false);
+  for (uint32_t b = 0; b < nb; ++b) {
+    auto p = std::make_unique<Pt>();
+    p->buf = DevMem((size_t)nq * n * 8, ctx.sh);
+    p->nq = nq;
+    p->scale = scale;
+    FHE_CUDA(cudaMemcpyAsync(p->data(), res + (size_t)b * nq * n, (size_t)nq * n * 8, cudaMemcpyDeviceToDevice,
+                             ctx.stream));
+    out.push_back(std::move(p));
+  }
+  unsigned st = 0;
+  FHE_CUDA(cudaMemcpyAsync(&st, status_.p, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx.stream));
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  require(st == 0, "encode: a scaled value is not finite or reaches 2^126", -1);
+}
+
+std::vector<std::unique_ptr<Pt>> Ckks::encode_replicated_diagonals(const double* w_dev, uint32_t m, uint32_t cols,
+                                                                   uint32_t R, uint32_t T, uint32_t win,
+                                                                   uint32_t baby, uint32_t nq, double scale) {
+  const uint32_t slots = ctx.slots;
+  require(w_dev != nullptr && m >= 1 && cols >= 1 && R >= 1 && T >= 1 && baby >= 1, "bad diagonal layout", -1);
+  require(win >= m && (uint64_t)(R - 1) * win + m <= slots, "the windows do not fit the slots", -1);
+  require(nq >= 1 && nq <= ctx.L, "limb count out of range", -1);
+  std::vector<std::unique_ptr<Pt>> out;
+  const uint32_t chunk = std::max(1u, std::min(T, (uint32_t)((64u << 20) / (16ull * slots))));
+  for (uint32_t t0 = 0; t0 < T; t0 += chunk) {
+    const uint32_t nb = std::min(chunk, T - t0);
+    double2* dv = reinterpret_cast<double2*>(ws(18, 2 * (size_t)nb * slots));
+    launch_replicated_diagonals(dv, w_dev, m, cols, R, T, win, baby, slots, t0, nb, ctx.stream);
+    encode_slots_on_device(dv, nb, nq, scale, out);
   }
   return out;
 }

@@ -102,6 +102,13 @@ class Ckks {
   std::unique_ptr<Pt> encode(const double* re, const double* im, uint32_t count, uint32_t nq, double scale);
   void decode(const Pt& p, double* re, double* im, uint32_t count);
   // Encodes B vectors of `count` values (values[b*count + i]) at nq limbs.
+  // Diagonal plaintexts t = 0..T-1 of the replicated BSGS layout of y = W x
+  // (W: m x cols, row-major fp64 on this device): window r < R of `win`
+  // slots holds W[i][(i + r T + t) % cols] at slot r win + i (i < m), the
+  // vector rotated by (t / baby) * baby slots (pre-rotated for its giant step).
+  std::vector<std::unique_ptr<Pt>> encode_replicated_diagonals(const double* w_dev, uint32_t m, uint32_t cols,
+                                                               uint32_t R, uint32_t T, uint32_t win, uint32_t baby,
+                                                               uint32_t nq, double scale);
   std::vector<std::unique_ptr<Pt>> encode_batch(const double* re, const double* im, uint32_t B, uint32_t count,
                                                 uint32_t nq, double scale);
   std::unique_ptr<Ct> encrypt(const Pt& p);
@@ -173,6 +180,8 @@ class Ckks {
                    const uint64_t* add_c0);
   void switch_keygen(uint64_t key_id, const uint64_t* s_new, const uint64_t* s_old, DevMem& out);
   void ntt_dense(uint64_t* d, uint32_t polys, uint32_t limbs, uint32_t stride, uint32_t prime0, bool inv);
+  void encode_slots_on_device(double2* dv, uint32_t nb, uint32_t nq, double scale,
+                              std::vector<std::unique_ptr<Pt>>& out);
   uint64_t* ws(size_t idx, size_t words);
   std::vector<uint64_t> scalar_residues(long double v, uint32_t nq) const;
   std::unique_ptr<Ct> prepare_mult_input(const Ct& a);

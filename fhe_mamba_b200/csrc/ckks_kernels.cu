@@ -768,6 +768,30 @@ void launch_rescale_lift(const uint64_t* last, size_t sl, uint64_t* lifted, size
   k_rescale_lift<<<grid1(n, nlimbs, ncomp), kTpb, 0, s>>>(last, sl, lifted, sd, n, q_last, mods); note_launch();
 }
 
+// dv[u][s] = W[i][(i + r T + t) % cols] with t = t0 + u, p = (s - (t / baby) baby) mod slots,
+// r = p / win, i = p % win (r < R, i < m), else 0: the numpy construction of
+// the replicated layout's diagonal t followed by np.roll by its giant step.
+__global__ void k_replicated_diagonals(double2* dv, const double* w, uint32_t m, uint32_t cols, uint32_t R,
+                                       uint32_t T, uint32_t win, uint32_t baby, uint32_t slots, uint32_t t0) {
+  const uint32_t sl = blockIdx.x * blockDim.x + threadIdx.x;
+  if (sl >= slots) return;
+  const uint32_t u = blockIdx.y, t = t0 + u;
+  const uint32_t shift = (t / baby) * baby % slots;
+  const uint32_t p = (sl + slots - shift) % slots;
+  const uint32_t r = p / win, i = p - r * win;
+  double v = 0.0;
+  if (r < R && i < m) v = w[(size_t)i * cols + ((uint64_t)i + (uint64_t)r * T + t) % cols];
+  dv[(size_t)u * slots + sl] = make_double2(v, 0.0);
+}
+
+void launch_replicated_diagonals(double2* dv, const double* w, uint32_t m, uint32_t cols, uint32_t R, uint32_t T,
+                                 uint32_t win, uint32_t baby, uint32_t slots, uint32_t t0, uint32_t nb,
+                                 cudaStream_t s) {
+  if (!nb) return;
+  k_replicated_diagonals<<<grid1(slots, nb), kTpb, 0, s>>>(dv, w, m, cols, R, T, win, baby, slots, t0);
+  note_launch();
+}
+
 void launch_fft_special_inv(double2* v, const double2* tw, uint32_t slots, uint32_t batch, cudaStream_t s) {
   for (uint32_t len = slots; len >= 2; len >>= 1)
     { k_fft_inv_stage<<<grid1(slots / 2, batch), kTpb, 0, s>>>(v, tw, slots, len); note_launch(); }

@@ -115,6 +115,12 @@ void launch_key_inner(const uint64_t* ext, uint32_t D, uint32_t w, const uint64_
                       cudaStream_t s, uint32_t l0 = 0, uint32_t count = ~0u);
 // Basis conversion of ncomp polys: src limbs (coefficient form) -> dst (coefficient form).
 // ns / nt must equal the table's source / target counts (ns <= 24).
+// Slot vectors of replicated-BSGS diagonals t0..t0+nb-1 into dv [nb][slots]
+// (real parts; see Ckks::encode_replicated_diagonals).
+void launch_replicated_diagonals(double2* dv, const double* w, uint32_t m, uint32_t cols, uint32_t R, uint32_t T,
+                                 uint32_t win, uint32_t baby, uint32_t slots, uint32_t t0, uint32_t nb,
+                                 cudaStream_t s);
+
 // ---- basis conversion on the tensor cores (conv_tc.cu), same results ----
 // Whether the tensor-core conversion handles ns source limbs at ring n.
 bool tc_conversion_supported(uint32_t n, uint32_t ns, bool primes_below_2_60);

@@ -448,8 +448,13 @@ class EncryptedMamba2Layer:
     NEEDS = {"rms": 14, "u": 2, "proj": 19, "xbc": 2, "pack": 8, "state": 4, "y": 2, "gn": 2}
 
     def __init__(self, cc, W: Mamba2Weights, P: Mamba2Polys, passes: int = 2, margin: int = 4,
-                 cache: PlaintextCache | None = None, needs: dict | None = None):
+                 cache: PlaintextCache | None = None, needs: dict | None = None, device_diagonals: bool = True):
         self.cc, self.W, self.P = cc, W, P
+        # Diagonal plaintexts generated on the device from the weights (the
+        # context's MakeReplicatedDiagonals) instead of built on the host and
+        # uploaded; identical words.  Contexts without it use the host path.
+        self.device_diagonals = device_diagonals and hasattr(cc, "MakeReplicatedDiagonals")
+        self._wdev = {}
         self.passes, self.margin = passes, margin
         self.needs = dict(self.NEEDS, **(needs or {}))
         self.cache = cache if cache is not None else PlaintextCache(0)
@@ -493,6 +498,16 @@ class EncryptedMamba2Layer:
         s |= {j * stride for j in range(1, b)} | {g * b * stride for g in range(1, G)}
         return sorted(v % n for v in s if v % n)
 
+    def _weights_on_device(self, name):
+        """The layer's weight matrix as a row-major fp64 tensor on the context's
+        device (uploaded once per layer and matrix)."""
+        if name not in self._wdev:
+            import torch
+            self._wdev[name] = torch.from_numpy(np.ascontiguousarray(self.W[name], dtype=np.float64)).to(
+                torch.device("cuda", self.cc.device))
+            torch.cuda.synchronize(self.cc.device)
+        return self._wdev[name]
+
     def _diags(self, name):
         if name not in self._lin:
             self._lin[name] = self.rep[name].diagonals(self.W[name], self.cc.slots)
@@ -529,14 +544,19 @@ class EncryptedMamba2Layer:
         lay = self.rep[name]
         x = self._rotation_sum(x, lay.copies, -lay.n)
         nq = x.n_limbs() - (1 if x.GetNoiseScaleDeg() >= 2 else 0)
-        diags = self._diags(name)
 
         def build():
+            if self.device_diagonals:
+                w = self._weights_on_device(name)
+                pts = c.MakeReplicatedDiagonals(w.data_ptr(), lay.m, lay.n, lay.R, lay.T, lay.w, lay.b,
+                                                level=c.n_q - nq)
+                return [pts[t] if t < lay.T else None for t in range(lay.G * lay.b)]
+            diags = self._diags(name)
             dense = [d for d in diags if d is not None]
             pts = iter(c.MakeCKKSPackedPlaintexts(np.array(dense), level=c.n_q - nq))
             return [next(pts) if d is not None else None for d in diags]
 
-        nbytes = sum(d is not None for d in diags) * nq * c.n * 8
+        nbytes = lay.T * nq * c.n * 8
         plist = self.cache.get((id(self), name, nq), nbytes, build)
         y = c.EvalLinearTransform(x, plist, lay.b, lay.G)
         y = self._rotation_sum(y, lay.R, lay.w)
@@ -880,10 +900,11 @@ class EncryptedMamba2Model:
     selection around them."""
 
     def __init__(self, cc, model: Mamba2Model, passes: int = 2, cache_gb: float = 40.0, margin: int = 4,
-                 needs: dict | None = None):
+                 needs: dict | None = None, device_diagonals: bool = True):
         self.cc, self.m = cc, model
         self.cache = PlaintextCache(cache_gb * 2 ** 30)
-        self.layers = [EncryptedMamba2Layer(cc, W, P, passes=passes, margin=margin, cache=self.cache, needs=needs)
+        self.layers = [EncryptedMamba2Layer(cc, W, P, passes=passes, margin=margin, cache=self.cache, needs=needs,
+                                            device_diagonals=device_diagonals)
                        for W, P in zip(model.layers, model.polys)]
         self.state = [([None] * (W.conv_kernel - 1), None) for W in model.layers]
         self.tokens, self.margins = [], []

@@ -215,6 +215,18 @@ int fhe_rotate_hoisted(fhe_ctx* ctx, const fhe_ct* a, const int32_t* steps, uint
  * per-diagonal host encoding (src/fideslib_plaintext_encoder.cpp:264-410). */
 int fhe_encode_batch(fhe_ctx* ctx, const double* re, const double* im, uint32_t batch, uint32_t count,
                      uint32_t n_limbs, double scale, fhe_pt** outs);
+/* Diagonal plaintexts of the replicated BSGS layout of y = W x generated on
+ * the device from the weights (the device-side diagonal generation of the
+ * reference's GPU special FFT + RNS encoder, src/gpu_special_fft.cu:12-113 and
+ * src/fideslib_plaintext_rns.cu:119-139, for this layout): w_dev is W, m x
+ * cols, row-major fp64 in device memory; diagonal t < T holds
+ * W[i][(i + r*T + t) % cols] at slot r*win + i (r < R, i < m), rotated by
+ * (t / baby) * baby slots; outs[t] receives its plaintext over n_limbs limbs
+ * at `scale` (0: the level's scale).  The words equal fhe_encode_batch of the
+ * same vectors built on the host. */
+int fhe_encode_replicated_diagonals(fhe_ctx* ctx, const double* w_dev, uint32_t m, uint32_t cols, uint32_t R,
+                                    uint32_t T, uint32_t win, uint32_t baby, uint32_t n_limbs, double scale,
+                                    fhe_pt** outs);
 
 /* BSGS plaintext-ciphertext matrix-vector product (PackedEvaluator::linear,
  * packed_fideslib.cpp:447-532; LinearTransformInPlace of the reference's

@@ -94,3 +94,28 @@ def test_config5_protocol_horizon_matches_plaintext():
         assert enc_tok == token, (i, em.margins[-1])
     assert max(errs) < 1e-4, errs
     assert m.audit(inputs)["max_bound_ratio"] <= 1.0
+
+
+def test_device_diagonals_equal_host_diagonals():
+    """The replicated BSGS diagonals generated on the device from the weights
+    (fhe_encode_replicated_diagonals) equal the host-built, uploaded and encoded
+    ones word for word, for both matvecs of a config-4-shape layer (in_proj
+    3352 x 768, out_proj 768 x 1536) at two levels."""
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    from fhe_mamba_b200.mamba2_layer import EncryptedMamba2Layer, Mamba2Polys, Mamba2Weights
+    W = Mamba2Weights(d_model=768, d_state=128, heads=24)
+    P = Mamba2Polys(W, samples=1, tokens=1)
+    cc = CryptoContext(CCParams(ring_dim=1 << 16, multiplicative_depth=7, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3))
+    layer = EncryptedMamba2Layer(cc, W, P)
+    for name in ("w_in", "w_out"):
+        lay = layer.rep[name]
+        for nq in (cc.n_q, 3):
+            dev = cc.MakeReplicatedDiagonals(layer._weights_on_device(name).data_ptr(), lay.m, lay.n, lay.R, lay.T,
+                                             lay.w, lay.b, level=cc.n_q - nq)
+            diags = layer._diags(name)
+            host = cc.MakeCKKSPackedPlaintexts(np.array([d for d in diags if d is not None]), level=cc.n_q - nq)
+            assert len(dev) == len(host) == lay.T
+            for t in (0, 1, lay.b, lay.T - 1):
+                assert np.array_equal(dev[t].residues(), host[t].residues()), (name, nq, t)
+    cc.close()
