@@ -899,7 +899,7 @@ class EncryptedMamba2Model:
     """The model's layers on one CryptoContext; client-side encryption and
     selection around them."""
 
-    def __init__(self, cc, model: Mamba2Model, passes: int = 2, cache_gb: float = 40.0, margin: int = 4,
+    def __init__(self, cc, model: Mamba2Model, passes: int = 2, cache_gb: float = 0.0, margin: int = 4,
                  needs: dict | None = None, device_diagonals: bool = True):
         self.cc, self.m = cc, model
         self.cache = PlaintextCache(cache_gb * 2 ** 30)
