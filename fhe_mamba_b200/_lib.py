@@ -129,6 +129,7 @@ SIGNATURES = {
     "fhe_kernel_launches": [ctypes.POINTER(ctypes.c_uint64)],
     "fhe_ntt_butterfly_ceiling": [vp, ctypes.POINTER(ctypes.c_double)],
     "fhe_refresh": [vp, vp, f64, i32, ctypes.POINTER(vp)],
+    "fhe_refresh_support": [vp, vp, f64, i32, u32, ctypes.POINTER(vp)],
     "fhe_security_audit": [u32, u32, u32, u32, u32, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(i32)],
     "fhe_ct_save": [vp, vp, ctypes.c_char_p],
     "fhe_ct_load": [vp, ctypes.c_char_p, ctypes.POINTER(vp)],
@@ -144,6 +145,7 @@ SIGNATURES = {
     "fhe_shard_moddown": [vp, u32, vp, vp, vp, vp, vp],
     "fhe_shard_automorphism": [vp, u32, u64, vp, vp],
     "fhe_bootstrap_setup": [vp, u32, u32, u32, i32, i32, u32],
+    "fhe_bootstrap_subslot_setup": [vp, u32, u32, u32, i32],
     "fhe_bootstrap_keygen": [vp],
     "fhe_bootstrap": [vp, vp, ctypes.POINTER(vp)],
     "fhe_bootstrap_stage": [vp, i32, vp, ctypes.POINTER(vp)],

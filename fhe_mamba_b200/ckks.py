@@ -151,6 +151,7 @@ class CryptoContext:
         call("fhe_ctx_create", ctypes.byref(p), ctypes.byref(h))
         self.h = h
         self.device = params.device
+        self.subslot_sizes = ()  # sub-slot refresh setups (slot counts)
         info = (ctypes.c_uint32 * 8)()
         call("fhe_ctx_info", h, ctypes.cast(info, vp))
         self.log_n, self.n_q, self.n_p, self.dnum, self.alpha, self.slots = list(info)[:6]
@@ -256,6 +257,15 @@ class CryptoContext:
         call("fhe_bootstrap_setup", self.h, int(level_budget[0]), int(level_budget[1]), int(slots),
              int(correction_factor), int(bool(slots_to_coeffs_first)), int(sparse_hamming_weight))
 
+    def EvalBootstrapSubslotSetup(self, slots: int, level_budget=(4, 4), correction_factor: int = 0):
+        """A sub-slot refresh for inputs zero outside slots [0, slots) (a power of
+        two <= N/4): one EvalMod instead of two, the same levels as the full
+        bootstrap, output zero outside [0, slots).  EvalBootstrapKeyGen
+        generates its keys; refresh(..., support=) picks it."""
+        call("fhe_bootstrap_subslot_setup", self.h, int(slots), int(level_budget[0]), int(level_budget[1]),
+             int(correction_factor))
+        self.subslot_sizes = tuple(sorted(set(self.subslot_sizes) | {int(slots)}))
+
     def bootstrap_components(self, ct, passes: int = 2, merge: bool = False):
         """The reference's two-pass refresh (PackedEvaluator::bootstrap_components,
         packed_fideslib.cpp:235-270): first = bootstrap(x); the residual
@@ -292,12 +302,14 @@ class CryptoContext:
             return self.EvalAdd(self.MultByInteger(first, 4096), second), None, 4096.0
         return first, second, 1.0
 
-    def refresh(self, ct, bound: float = 1.0, passes: int = 2, merge: bool = False):
+    def refresh(self, ct, bound: float = 1.0, passes: int = 2, merge: bool = False, support: int = 0):
         """PackedEvaluator::refresh (packed_fideslib.cpp:271-281): bootstrap x / bound
         (one or two passes) and scale back by bound.  Without merge this is one
-        library call (fhe_refresh); the merge variant composes the host steps."""
+        library call (fhe_refresh); the merge variant composes the host steps.
+        support > 0 declares ct zero outside slots [0, support): a sub-slot
+        refresh set up for at least that many slots then runs it."""
         if not merge:
-            return self.EvalRefresh(ct, bound, passes)
+            return self.EvalRefresh(ct, bound, passes, support)
         return self.host_refresh(ct, bound, passes, merge)
 
     def host_refresh(self, ct, bound: float = 1.0, passes: int = 2, merge: bool = False):
@@ -325,9 +337,12 @@ class CryptoContext:
         cannot decrypt or generate keys (a server)."""
         call("fhe_keys_load", self.h, os.fsencode(str(path)))
 
-    def EvalRefresh(self, ct, bound: float = 1.0, passes: int = 2):
+    def EvalRefresh(self, ct, bound: float = 1.0, passes: int = 2, support: int = 0):
         """One library call for the reference's refresh (fhe_refresh): the same
-        arithmetic as refresh() without the host round trips."""
+        arithmetic as refresh() without the host round trips (fhe_refresh_support
+        with a support)."""
+        if support:
+            return self._ct("fhe_refresh_support", ct.handle, float(bound), int(passes), int(support))
         return self._ct("fhe_refresh", ct.handle, float(bound), int(passes))
 
     def EvalBootstrapKeyGen(self, secret_key=None, slots: int = 0):

@@ -5,6 +5,7 @@
 #include <fstream>
 #include <iomanip>
 #include <iostream>
+#include <map>
 #include <memory>
 #include <new>
 #include <sstream>
@@ -27,6 +28,7 @@ struct fhe_ctx {
   fhe::Context c;
   std::unique_ptr<fhe::Ckks> ck;
   std::unique_ptr<fhe::Bootstrapper> boot;
+  std::map<uint32_t, std::unique_ptr<fhe::Bootstrapper>> sub;  // sub-slot refreshes by slot count
   std::unique_ptr<fhe::ShardKeySwitch> shard;
 };
 struct fhe_ct {
@@ -803,11 +805,26 @@ int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, 
   });
 }
 
+int fhe_bootstrap_subslot_setup(fhe_ctx* ctx, uint32_t slots, uint32_t budget_cts, uint32_t budget_stc,
+                                int32_t correction) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    fhe::require(slots >= 2 && slots < ctx->c.slots, "sub-slot refresh slots must be below the context's", -1);
+    fhe::BootParams p;
+    p.budget_cts = budget_cts;
+    p.budget_stc = budget_stc;
+    p.correction = correction;
+    p.slots = slots;
+    ctx->sub[slots] = std::make_unique<fhe::Bootstrapper>(k, p);
+  });
+}
+
 int fhe_bootstrap_keygen(fhe_ctx* ctx) {
   return guarded([&] {
     ckks(ctx);
-    fhe::require(ctx->boot != nullptr, "bootstrap keygen before bootstrap setup", -4);
-    ctx->boot->keygen();
+    fhe::require(ctx->boot != nullptr || !ctx->sub.empty(), "bootstrap keygen before bootstrap setup", -4);
+    if (ctx->boot) ctx->boot->keygen();
+    for (auto& [n, b] : ctx->sub) b->keygen();
   });
 }
 
@@ -819,30 +836,56 @@ int fhe_bootstrap(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out) {
   });
 }
 
+namespace {
+
+// PackedEvaluator::refresh / bootstrap_components (packed_fideslib.cpp:235-281):
+// bootstrap x / bound; with two passes the residual (x - first) * 4096 is
+// bootstrapped again and added back / 4096; the result is scaled by bound.
+// A sub-slot bootstrapper gets each input replicated with period n first
+// (its inputs are zero outside [0, n)); its outputs are zero there again.
+std::unique_ptr<fhe::Ct> refresh_with(fhe::Ckks& k, fhe::Bootstrapper& b, bool sub, const fhe::Ct& a, double bound,
+                                      int32_t passes) {
+  fhe::require(passes == 1 || passes == 2, "refresh passes must be 1 or 2");
+  fhe::require(std::isfinite(bound) && bound > 0, "refresh bound must be positive");
+  auto boot = [&](const fhe::Ct& v) { return sub ? b.bootstrap(*b.replicate(v)) : b.bootstrap(v); };
+  auto x = k.mul_scalar(a, 1.0 / bound);
+  if (x->noise_deg > 1) x = k.rescaled(*x);
+  auto first = boot(*x);
+  std::unique_ptr<fhe::Ct> r;
+  if (passes == 1) {
+    r = k.mul_scalar(*first, bound);
+  } else {
+    auto residual = k.mul_scalar(*k.add(*x, *first, true), 4096.0);
+    if (residual->noise_deg > 1) residual = k.rescaled(*residual);
+    auto second = boot(*residual);
+    r = k.mul_scalar(*k.add(*first, *k.mul_scalar(*second, 1.0 / 4096.0), false), bound);
+  }
+  if (r->noise_deg > 1) r = k.rescaled(*r);
+  return r;
+}
+
+}  // namespace
+
 int fhe_refresh(fhe_ctx* ctx, const fhe_ct* a, double bound, int32_t passes, fhe_ct** out) {
   return guarded([&] {
     fhe::Ckks& k = ckks(ctx);
     fhe::require(ctx->boot != nullptr, "refresh before bootstrap setup", -4);
-    fhe::require(passes == 1 || passes == 2, "refresh passes must be 1 or 2");
-    fhe::require(std::isfinite(bound) && bound > 0, "refresh bound must be positive");
-    fhe::Bootstrapper& b = *ctx->boot;
-    // PackedEvaluator::refresh / bootstrap_components (packed_fideslib.cpp:235-281):
-    // bootstrap x / bound; with two passes the residual (x - first) * 4096 is
-    // bootstrapped again and added back / 4096; the result is scaled by bound.
-    auto x = k.mul_scalar(ct_of(a), 1.0 / bound);
-    if (x->noise_deg > 1) x = k.rescaled(*x);
-    auto first = b.bootstrap(*x);
-    std::unique_ptr<fhe::Ct> r;
-    if (passes == 1) {
-      r = k.mul_scalar(*first, bound);
-    } else {
-      auto residual = k.mul_scalar(*k.add(*x, *first, true), 4096.0);
-      if (residual->noise_deg > 1) residual = k.rescaled(*residual);
-      auto second = b.bootstrap(*residual);
-      r = k.mul_scalar(*k.add(*first, *k.mul_scalar(*second, 1.0 / 4096.0), false), bound);
+    put_ct(out, refresh_with(k, *ctx->boot, false, ct_of(a), bound, passes));
+  });
+}
+
+int fhe_refresh_support(fhe_ctx* ctx, const fhe_ct* a, double bound, int32_t passes, uint32_t support,
+                        fhe_ct** out) {
+  return guarded([&] {
+    fhe::Ckks& k = ckks(ctx);
+    // the smallest sub-slot bootstrapper covering [0, support), else the full one
+    auto it = support ? ctx->sub.lower_bound(support) : ctx->sub.end();
+    if (it != ctx->sub.end()) {
+      put_ct(out, refresh_with(k, *it->second, true, ct_of(a), bound, passes));
+      return;
     }
-    if (r->noise_deg > 1) r = k.rescaled(*r);
-    put_ct(out, std::move(r));
+    fhe::require(ctx->boot != nullptr, "refresh before bootstrap setup", -4);
+    put_ct(out, refresh_with(k, *ctx->boot, false, ct_of(a), bound, passes));
   });
 }
 

@@ -92,9 +92,17 @@ std::vector<double> cheb_fit(const std::function<double(double)>& f, int d) {
 
 Bootstrapper::Bootstrapper(Ckks& ck, const BootParams& p) : ck_(ck), p_(p) {
   Context& ctx = ck.ctx;
-  const uint32_t n = ctx.slots;
+  n_ = p_.slots ? p_.slots : ctx.slots;
+  const uint32_t n = n_;
   require(n >= 2 && n <= ctx.n / 2 && (n & (n - 1)) == 0, "bootstrapping needs a power-of-two slot count <= N/2",
           -1);
+  if (p_.slots) {
+    require(ctx.slots == ctx.n / 2, "a sub-slot refresh needs a fully packed context", -1);
+    require(n <= ctx.n / 4, "sub-slot refresh slots must be a power of two <= N/4", -1);
+    require(!p_.s2c_first && !p_.sparse_h, "a sub-slot refresh combines with neither S2C-first nor a sparse secret",
+            -1);
+    single_ = true;
+  }
   // Sparse packing (n < N/2): the plaintext lives in Z[X^g'], g' = N/(2n);
   // after ModRaise the trace over the g = N/(2n) automorphisms fixing that
   // subring (rotations by multiples of n) keeps g times its part of
@@ -105,6 +113,7 @@ Bootstrapper::Bootstrapper(Ckks& ck, const BootParams& p) : ck_(ck), p_(p) {
   require(p_.budget_cts >= 1 && p_.budget_stc >= 1, "level budgets must be >= 1", -1);
   p_.budget_cts = std::min(p_.budget_cts, logn);
   p_.budget_stc = std::min(p_.budget_stc, logn);
+  require(!single_ || p_.budget_stc >= 2, "a sub-slot refresh needs at least two SlotToCoeff groups", -1);
   if (p_.sparse_h) {
     require(p_.sparse_h <= ctx.n / 2, "sparse Hamming weight out of range", -1);
     p_.K = std::ceil((p_.sparse_h + 1) / 2.0) + 2.0;  // |I| <= (h + 1) / 2
@@ -125,11 +134,13 @@ Bootstrapper::Bootstrapper(Ckks& ck, const BootParams& p) : ck_(ck), p_(p) {
   const double alpha = S / (2.0 * p_.K * (double)ctx.primes[0] * (double)trace_);
   std::vector<uint32_t> halves;
   for (uint32_t h = n / 2; h >= 1; h /= 2) halves.push_back(h);
-  build_groups(cts_, halves, p_.budget_cts, true, std::pow(alpha, 1.0 / p_.budget_cts));
+  build_groups(cts_, halves, p_.budget_cts, true, std::pow(alpha, 1.0 / p_.budget_cts), Edit::None,
+               single_ ? Edit::Split : Edit::None);
   // SlotToCoeff: BR(w') -> U0 w' / (2 pi); the 2^correction factor is an exact
   // integer multiplication afterwards.
   std::reverse(halves.begin(), halves.end());
-  build_groups(stc_, halves, p_.budget_stc, false, std::pow(1.0 / (2.0 * M_PI), 1.0 / p_.budget_stc));
+  build_groups(stc_, halves, p_.budget_stc, false, std::pow(1.0 / (2.0 * M_PI), 1.0 / p_.budget_stc),
+               single_ ? Edit::Merge : Edit::None, single_ ? Edit::Mask : Edit::None);
 
   // EvalMod cosine: p(u) ~ cos(2 pi (K u - 1/4) / 2^r) on [-1, 1], truncated
   // where every remaining coefficient is below 2^-48.
@@ -143,8 +154,8 @@ Bootstrapper::Bootstrapper(Ckks& ck, const BootParams& p) : ck_(ck), p_(p) {
 }
 
 void Bootstrapper::build_groups(std::vector<Group>& out, const std::vector<uint32_t>& halves, uint32_t budget,
-                                bool inverse, double factor) {
-  const uint32_t n = ck_.ctx.slots;
+                                bool inverse, double factor, Edit first, Edit last) {
+  const uint32_t n = n_, S = ck_.ctx.slots;
   const uint32_t stages = (uint32_t)halves.size();
   size_t pos = 0;
   for (uint32_t gi = 0; gi < budget; ++gi) {
@@ -172,21 +183,57 @@ void Bootstrapper::build_groups(std::vector<Group>& out, const std::vector<uint3
     // giant offset: a multiple of b, so one giant step is the identity
     g.offset = top ? 0 : ((T + g.b - 1) / g.b) * g.b;
     g.G = top ? (uint32_t)((count + g.b - 1) / g.b) : (uint32_t)((g.offset + T + g.b) / g.b);
+    // (with one group a CoeffToSlot split, which is always `last`, wins)
+    Edit edit = gi == 0 ? first : Edit::None;
+    if (gi + 1 == budget && last != Edit::None) edit = last;
+    g.aux = edit == Edit::Split ? 1 : edit == Edit::Merge ? 2 : 0;
     g.diags.resize((size_t)g.b * g.G);
+    if (g.aux) g.diags2.resize((size_t)g.b * g.G);
+    const cd I(0, 1);
+    // Over 2n slots (k mod 2n < n: the real parts' half, else the imaginary
+    // parts'): z = P x + Q conj(x) splits CoeffToSlot's output x into re / im,
+    // w = R1 e + R2 rot(e, n) merges EvalMod's output e back.
+    auto lower = [n](int64_t k) { return ((k % (2 * (int64_t)n)) + 2 * (int64_t)n) % (2 * (int64_t)n) < n; };
     for (uint32_t gg = 0; gg < g.G; ++gg)
       for (uint32_t j = 0; j < g.b; ++j) {
         const int64_t t = (int64_t)gg * g.b + j - g.offset;
         if (top ? (t < 0 || t >= count) : (t < -T || t > T)) continue;
-        const uint32_t d = (uint32_t)(((t * (int64_t)hmin) % (int64_t)n + n) % n);
+        const int64_t amount = t * (int64_t)hmin;  // the diagonal's rotation (signed)
+        const uint32_t d = (uint32_t)((amount % (int64_t)n + n) % n);
         auto it = M.find(d);
         if (it == M.end()) continue;
         const auto& v = it->second;
         if (std::all_of(v.begin(), v.end(), [](const cd& x) { return x == cd(0, 0); })) continue;
-        // pre-rotate by the giant amount r: D'[i] = D[(i - r) mod n]
-        const int64_t r = ((((int64_t)gg * g.b - g.offset) * (int64_t)hmin) % (int64_t)n + n) % n;
-        std::vector<cd> rv(n);
-        for (uint32_t i = 0; i < n; ++i) rv[i] = v[(i + n - (uint32_t)r) % n];
-        g.diags[(size_t)gg * g.b + j] = std::move(rv);
+        // The diagonal over its period P (n, 2n, or S for the masked output).
+        const uint32_t P = edit == Edit::None ? n : edit == Edit::Mask ? S : 2 * n;
+        std::vector<cd> D(P), D2;
+        if (g.aux) D2.resize(P);
+        for (uint32_t i = 0; i < P; ++i) {
+          const cd x = v[i % n];
+          switch (edit) {
+            case Edit::None: D[i] = x; break;
+            case Edit::Mask: D[i] = i < n ? x : cd(0, 0); break;
+            case Edit::Split:
+              D[i] = lower(i) ? x : -I * x;
+              D2[i] = lower(i) ? std::conj(x) : I * std::conj(x);
+              break;
+            case Edit::Merge:
+              D[i] = x * (lower(i + amount) ? cd(1, 0) : I);
+              D2[i] = x * (lower(i + amount) ? I : cd(1, 0));
+              break;
+          }
+        }
+        // pre-rotate by the giant amount r over the period, D'[i] = D[(i - r) mod P],
+        // then lay the period out over the context's S slots
+        const int64_t r = (int64_t)gg * g.b - g.offset;
+        const int64_t rr = ((r * (int64_t)hmin) % (int64_t)P + P) % P;
+        auto place = [&](const std::vector<cd>& src) {
+          std::vector<cd> o(S);
+          for (uint32_t i = 0; i < S; ++i) o[i] = src[(i % P + P - (uint32_t)rr) % P];
+          return o;
+        };
+        g.diags[(size_t)gg * g.b + j] = place(D);
+        if (g.aux) g.diags2[(size_t)gg * g.b + j] = place(D2);
       }
     out.push_back(std::move(g));
   }
@@ -194,10 +241,10 @@ void Bootstrapper::build_groups(std::vector<Group>& out, const std::vector<uint3
 
 std::vector<int64_t> Bootstrapper::rotation_steps() const {
   std::vector<int64_t> s;
-  const int64_t n = ck_.ctx.slots;
   for (const auto* gs : {&cts_, &stc_})
     for (const Group& g : *gs) {
-      for (uint32_t j = 1; j < g.b; ++j) s.push_back(((int64_t)j * g.stride) % n);
+      // baby steps j*stride < n
+      for (uint32_t j = 1; j < g.b; ++j) s.push_back((int64_t)j * g.stride);
       // giant steps exactly as linear_transform asks for them (signed): with
       // sparse packing a step and its residue mod n are different keys
       for (uint32_t gg = 0; gg < g.G; ++gg) {
@@ -218,8 +265,8 @@ void Bootstrapper::keygen() {
   }
   const uint64_t conj = 2ull * ck_.ctx.n - 1;
   if (!ck_.has_rotation_key(conj)) ck_.rotation_keygen(conj);
-  for (uint32_t j = 1; j < trace_; j *= 2) {  // sparse-packing trace
-    const uint64_t g = ck_.galois_for_full_step((int64_t)j * ck_.ctx.slots);
+  for (uint32_t j = 1; j < trace_; j *= 2) {  // sparse-packing trace (and the sub-slot replication and merge)
+    const uint64_t g = ck_.galois_for_full_step((int64_t)j * n_);
     if (!ck_.has_rotation_key(g)) ck_.rotation_keygen(g);
   }
   if (p_.sparse_h) ck_.sparse_keygen(p_.sparse_h);
@@ -227,7 +274,7 @@ void Bootstrapper::keygen() {
 
 std::unique_ptr<Ct> Bootstrapper::transform(std::vector<Group>& groups, std::unique_ptr<Ct> x) {
   Context& ctx = ck_.ctx;
-  const uint32_t n = ctx.slots;
+  const uint32_t n = ctx.slots;  // diagonal vectors span the context's slots
   for (Group& g : groups) {
     const uint32_t nq = x->nq;
     require(nq >= 2, "bootstrapping ran out of levels", -4);
@@ -241,26 +288,38 @@ std::unique_ptr<Ct> Bootstrapper::transform(std::vector<Group>& groups, std::uni
       g.enc.erase(it);
       it = g.enc.end();
     }
-    if (it == g.enc.end()) {
+    auto encode = [&](const std::vector<std::vector<cd>>& diags) {
       std::vector<double> re, im;
       std::vector<size_t> which;
-      for (size_t i = 0; i < g.diags.size(); ++i)
-        if (!g.diags[i].empty()) {
+      for (size_t i = 0; i < diags.size(); ++i)
+        if (!diags[i].empty()) {
           which.push_back(i);
-          for (const cd& v : g.diags[i]) {
+          for (const cd& v : diags[i]) {
             re.push_back(v.real());
             im.push_back(v.imag());
           }
         }
       auto pts = ck_.encode_batch(re.data(), im.data(), (uint32_t)which.size(), n, nq, dscale);
-      std::vector<std::unique_ptr<Pt>> enc(g.diags.size());
+      std::vector<std::unique_ptr<Pt>> enc(diags.size());
       for (size_t i = 0; i < which.size(); ++i) enc[which[i]] = std::move(pts[i]);
-      it = g.enc.emplace(nq, std::move(enc)).first;
+      return enc;
+    };
+    if (it == g.enc.end()) {
+      it = g.enc.emplace(nq, encode(g.diags)).first;
+      if (g.aux) g.enc2[nq] = encode(g.diags2);
       g.enc_scale[nq] = dscale;
     }
-    std::vector<const Pt*> d(g.diags.size());
-    for (size_t i = 0; i < d.size(); ++i) d[i] = it->second[i].get();
-    auto y = ck_.linear_transform(*x, d, g.b, g.G, g.stride, g.offset);
+    auto ptrs = [](const std::vector<std::unique_ptr<Pt>>& enc) {
+      std::vector<const Pt*> d(enc.size());
+      for (size_t i = 0; i < d.size(); ++i) d[i] = enc[i].get();
+      return d;
+    };
+    auto y = ck_.linear_transform(*x, ptrs(it->second), g.b, g.G, g.stride, g.offset);
+    if (g.aux) {  // the companion: the same transform shape on conj(x) or rot(x, n)
+      auto x2 = g.aux == 1 ? ck_.rotate(*x, 2ull * ctx.n - 1) : ck_.rotate(*x, ck_.galois_for_full_step((int64_t)n_));
+      auto y2 = ck_.linear_transform(*x2, ptrs(g.enc2.at(nq)), g.b, g.G, g.stride, g.offset);
+      y = ck_.add(*y, *y2, false);
+    }
     ck_.rescale_inplace(*y);
     y->scale = target;  // equal to the computed scale up to its last bit
     x = std::move(y);
@@ -299,7 +358,7 @@ std::unique_ptr<Ct> Bootstrapper::raise(const Ct& a) {
   if (p_.sparse_h) raised = ck_.switch_to_dense(*raised);
   // Sparse packing: sum of the rotations by j*n, j < g (log2 g doublings).
   for (uint32_t j = 1; j < trace_; j *= 2) {
-    auto r = ck_.rotate(*raised, ck_.galois_for_full_step((int64_t)j * ctx.slots));
+    auto r = ck_.rotate(*raised, ck_.galois_for_full_step((int64_t)j * n_));
     raised = ck_.add(*raised, *r, false);
   }
   raised->scale = ck_.level_scale(ctx.L);
@@ -314,7 +373,22 @@ std::unique_ptr<Ct> Bootstrapper::coeff_to_slot(const Ct& raised) {
   return x;
 }
 
+std::unique_ptr<Ct> Bootstrapper::replicate(const Ct& x) {
+  auto r = ck_.clone(x);
+  for (uint32_t j = 1; j < trace_; j *= 2) {
+    auto t = ck_.rotate(*r, ck_.galois_for_full_step((int64_t)j * n_));
+    r = ck_.add(*r, *t, false);
+  }
+  return r;
+}
+
 std::unique_ptr<Ct> Bootstrapper::eval_mod_full(const Ct& x) {
+  if (single_) {  // the real and imaginary parts already sit side by side (2n slots)
+    auto w = eval_mod(x);
+    if (w->noise_deg > 1) ck_.rescale_inplace(*w);
+    levels_[2] = w->nq;
+    return w;
+  }
   // real / imaginary split: re = x + conj(x), im = -i (x - conj(x))
   auto cj = ck_.rotate(x, 2ull * ck_.ctx.n - 1);
   auto re = ck_.add(x, *cj, false);

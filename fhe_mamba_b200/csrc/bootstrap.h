@@ -38,6 +38,15 @@ struct BootParams {
   // ModRaise and back right after it, so |I| <= (h + 1) / 2 and EvalMod needs
   // a far smaller interval, degree and depth.
   uint32_t sparse_h = 0;
+  // Sub-slot refresh in a fully packed context: 0 bootstraps all of the
+  // context's slots; a power of two n <= N/4 bootstraps inputs whose values
+  // sit in slots [0, n) (zeros elsewhere), replicated with period n by the
+  // caller: the sparse-packing pipeline on n slots with ONE EvalMod (the real
+  // and imaginary parts of CoeffToSlot's output side by side in 2n slots;
+  // the split is folded into the last CoeffToSlot group, the merge into the
+  // first SlotToCoeff group) and the output masked to [0, n) inside the last
+  // SlotToCoeff group.  No extra level.
+  uint32_t slots = 0;
 };
 
 class Bootstrapper {
@@ -53,6 +62,11 @@ class Bootstrapper {
   // s2c_first) whose slots are bounded by 1 in magnitude.  The output
   // decrypts to the same slots with fresh levels.
   std::unique_ptr<Ct> bootstrap(const Ct& a);
+  // Slots this bootstrapper covers (the context's, or the sub-slot count).
+  uint32_t slots() const { return n_; }
+  // x replicated with period slots() over the context's slots (x zero
+  // outside [0, slots())): log2(N / (2 slots)) rotate-and-add doublings.
+  std::unique_ptr<Ct> replicate(const Ct& x);
 
   // The four steps of bootstrap(), each on its own (the pieces that
   // EvalCoeffsToSlots / EvalSlotsToCoeffs expose in OpenFHE):
@@ -78,18 +92,28 @@ class Bootstrapper {
   struct Group {
     uint32_t b = 0, G = 0;
     int64_t stride = 0, offset = 0;
-    std::vector<std::vector<std::complex<double>>> diags;       // [b*G], pre-rotated; empty = zero
-    std::map<uint32_t, std::vector<std::unique_ptr<Pt>>> enc;  // encodings by limb count
-    std::map<uint32_t, double> enc_scale;                      // their encoding scale
+    // Diagonal vectors over the context's slots, pre-rotated; empty = zero.
+    // With a companion (aux != 0) the group computes LT(x, diags) +
+    // LT(aux(x), diags2), aux 1 = conjugate, 2 = rotation by n slots.
+    std::vector<std::vector<std::complex<double>>> diags, diags2;
+    int aux = 0;
+    std::map<uint32_t, std::vector<std::unique_ptr<Pt>>> enc, enc2;  // encodings by limb count
+    std::map<uint32_t, double> enc_scale;                            // their encoding scale
   };
+  // Edits applied to a group's matrix before its diagonals are laid out:
+  // none, the CoeffToSlot split (companion on the conjugate), the
+  // SlotToCoeff merge (companion on the rotation by n), the output mask.
+  enum class Edit { None, Split, Merge, Mask };
   void build_groups(std::vector<Group>& out, const std::vector<uint32_t>& halves, uint32_t budget, bool inverse,
-                    double factor);
+                    double factor, Edit first, Edit last);
   std::unique_ptr<Ct> transform(std::vector<Group>& groups, std::unique_ptr<Ct> x);
   std::unique_ptr<Ct> eval_mod(const Ct& x);
 
   Ckks& ck_;
   BootParams p_;
   int corr_ = 0;
+  uint32_t n_ = 0;      // slots bootstrapped
+  bool single_ = false;  // one EvalMod over 2n slots (sub-slot refresh)
   uint32_t trace_ = 1;  // N / (2 slots): automorphisms summed after ModRaise (sparse packing)
   std::vector<Group> cts_, stc_;
   std::vector<double> cheb_;

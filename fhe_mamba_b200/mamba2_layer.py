@@ -517,17 +517,21 @@ class EncryptedMamba2Layer:
     def _left(self, ct):
         return ct.n_limbs() - 1 - (1 if ct.GetNoiseScaleDeg() >= 2 else 0)
 
-    def _fit(self, ct, need, bound, site=None):
+    def _fit(self, ct, need, bound, site=None, support=0):
         """Refreshes ct when fewer than need + margin levels remain; the margin keeps
         every stage's output refreshable (a two-pass refresh spends two levels
         before its second bootstrap, which needs two limbs).  `passes` is the
         refresh's pass count, or a function of the refresh site's name (a
-        refresh policy such as the reference's selective Meta-BTS)."""
+        refresh policy such as the reference's selective Meta-BTS).  support > 0
+        says ct is zero outside slots [0, support): a context with sub-slot
+        refreshes (``subslot_sizes``) then refreshes it over fewer slots."""
         if self._left(ct) >= need + self.margin:
             return ct
         passes = self.passes(site) if callable(self.passes) else self.passes
         self.refreshes += 1
         self.two_pass_refreshes += passes == 2
+        if support and getattr(self.cc, "subslot_sizes", ()):
+            return self.cc.refresh(ct, bound, passes=passes, support=support)
         return self.cc.refresh(ct, bound, passes=passes)
 
     def _rotation_sum(self, x, count, stride):
@@ -580,14 +584,14 @@ class EncryptedMamba2Layer:
         (``encrypted_inv_sqrt``) runs its own iteration on the variance, which
         refreshes its iterates through bounds[prefix_*] as their levels run out."""
         if hasattr(seed, "encrypted_inv_sqrt"):
-            x = self._fit(x, 2 + seed.levels, bounds[key], key)
+            x = self._fit(x, 2 + seed.levels, bounds[key], key, width)
             v = self.pm.mean_square(x, width, eps, seed.fill)
             y = seed.encrypted_inv_sqrt(
                 self.cc, v, lambda ct, need, name: self._fit(ct, need, bounds[prefix + "_" + name], prefix + "_" + name))
-            x = self._fit(x, 2, bounds[key], key)
+            x = self._fit(x, 2, bounds[key], key, width)
             y = self._fit(y, 2, bounds[prefix + "_y"], prefix + "_y")
             return self.pm.scale_rows(x, y, width, weight)
-        x = self._fit(x, self.needs["rms"], bounds[key], key)
+        x = self._fit(x, self.needs["rms"], bounds[key], key, width)
         return self.pm.rms_norm(x, width, weight, eps, (seed.lo, seed.hi), degree=len(seed.coeffs) - 1)
 
     # ---- one token ------------------------------------------------------------
@@ -604,12 +608,12 @@ class EncryptedMamba2Layer:
         E, S, H, Dm = W.d_inner, W.d_state, W.heads, W.d_model
         cd = W.conv_dim
         u = self._rms(h, Dm, W["norm_w"], P.rsqrt1, bounds, "h", "n1", W.eps)
-        u = self._fit(u, self.needs["u"], bounds["u"], "u")
+        u = self._fit(u, self.needs["u"], bounds["u"], "u", Dm)
         proj = self._linear(u, "w_in")
-        proj = self._fit(proj, self.needs["proj"], bounds["proj"], "proj")
+        proj = self._fit(proj, self.needs["proj"], bounds["proj"], "proj", W.proj_dim)
         # xBC stream at [0, conv_dim) and the causal conv
         xbc = self.pm._mul_mask(c.EvalRotate(proj, E), self.pm._block_mask(0, cd))
-        window = [self._fit(w, self.needs["xbc"], bounds["xbc"], "xbc") if w is not None else None
+        window = [self._fit(w, self.needs["xbc"], bounds["xbc"], "xbc", cd) if w is not None else None
                   for w in conv_state] + [xbc]
         taps = []
         for k in range(W.conv_kernel):
@@ -619,7 +623,7 @@ class EncryptedMamba2Layer:
         bias = np.zeros(c.slots)
         bias[:cd] = W["conv_b"]
         xc = self.pm.conv(window, taps, bias)
-        xc = self._fit(xc, self._need(P.silu_x), bounds["xc"], "xc")
+        xc = self._fit(xc, self._need(P.silu_x), bounds["xc"], "xc", cd)
         xa = self._poly(xc, P.silu_x, 0, cd)
         # dt and decay at [0, heads)
         dtv = self.pm._mul_mask(c.EvalRotate(proj, E + cd), self.pm._block_mask(0, H))
@@ -631,19 +635,19 @@ class EncryptedMamba2Layer:
                                                         scale=dtv.GetScalingFactor()))
         gates = getattr(P, "gates", None)
         if gates is not None:  # joint gates: write and decay from one shared factor
-            dtv = self._fit(dtv, gates.levels, bounds["dt"], "dt")
+            dtv = self._fit(dtv, gates.levels, bounds["dt"], "dt", H)
             dts, decay = gates.encrypted(self.pm, dtv, H)
             pack = c.EvalAdd(xa, c.EvalRotate(dts, -self.dt_base))
             if ssm_state is not None:
                 pack = c.EvalAdd(pack, c.EvalRotate(decay, -self.decay_base))
         elif getattr(P, "decay", None) is not None:  # fused decay: dts and decay both from dt
-            dtv = self._fit(dtv, max(self._need(P.softplus), P.decay.levels), bounds["dt"], "dt")
+            dtv = self._fit(dtv, max(self._need(P.softplus), P.decay.levels), bounds["dt"], "dt", H)
             dts = self._poly(dtv, P.softplus, 0, H)
             pack = c.EvalAdd(xa, c.EvalRotate(dts, -self.dt_base))
             if ssm_state is not None:
                 pack = c.EvalAdd(pack, c.EvalRotate(P.decay.encrypted(self.pm, dtv, H), -self.decay_base))
         else:
-            dtv = self._fit(dtv, self._need(P.softplus), bounds["dt"], "dt")
+            dtv = self._fit(dtv, self._need(P.softplus), bounds["dt"], "dt", H)
             dts = self._poly(dtv, P.softplus, 0, H)
             pack = c.EvalAdd(xa, c.EvalRotate(dts, -self.dt_base))
         if gates is None and getattr(P, "decay", None) is None and ssm_state is not None:
@@ -652,10 +656,10 @@ class EncryptedMamba2Layer:
             mask = getattr(P.exp, "head_mask", None)
             avec = np.zeros(c.slots)
             avec[:H] = W["a"] if mask is None else W["a"] * mask
-            adt = self._fit(self.pm._mul_mask(dts, avec), self._need(P.exp), bounds["adt"], "adt")
+            adt = self._fit(self.pm._mul_mask(dts, avec), self._need(P.exp), bounds["adt"], "adt", H)
             decay = self._poly(adt, P.exp, 0, H)
             pack = c.EvalAdd(pack, c.EvalRotate(decay, -self.decay_base))
-        pack = self._fit(pack, self.needs["pack"], bounds["pack"], "pack")
+        pack = self._fit(pack, self.needs["pack"], bounds["pack"], "pack", self.decay_base + H)
         # state update and readout from the packed inputs
         if ssm_state is not None:
             ssm_state = [self._fit(st, self.needs["state"], bounds["state"], "state") for st in ssm_state]
@@ -665,12 +669,12 @@ class EncryptedMamba2Layer:
         y = c.EvalAdd(y, self.pm._mul_mask(pack, dvec))
         # gate
         z = self.pm._mul_mask(proj, self.pm._block_mask(0, E))
-        z = self._fit(z, self._need(P.silu_z), bounds["z"], "z")
+        z = self._fit(z, self._need(P.silu_z), bounds["z"], "z", E)
         sz = self._poly(z, P.silu_z, 0, E)
-        y = self._fit(y, self.needs["y"], bounds["y"], "y")
+        y = self._fit(y, self.needs["y"], bounds["y"], "y", E)
         g = c.EvalMult(y, sz)
         gn = self._rms(g, E, W["gn_w"], P.rsqrt2, bounds, "g", "n2", getattr(W, "gated_eps", W.eps))
-        gn = self._fit(gn, self.needs["gn"], bounds["gn"], "gn")
+        gn = self._fit(gn, self.needs["gn"], bounds["gn"], "gn", E)
         out = self._linear(gn, "w_out")
         h_out = c.EvalAdd(h, out)
         return h_out, window[1:], states
@@ -925,7 +929,7 @@ class EncryptedMamba2Model:
             new.append((conv, st))
         self.state = new
         last = self.layers[-1]
-        h = last._fit(h, 14, m.final_bound)
+        h = last._fit(h, 14, m.final_bound, support=m.d_model)
         return last.pm.rms_norm(h, m.d_model, m.norm_f, m.layers[0].eps, (m.rsqrt_f.lo, m.rsqrt_f.hi),
                                 degree=len(m.rsqrt_f.coeffs) - 1)
 

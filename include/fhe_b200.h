@@ -379,6 +379,19 @@ int fhe_tc_timeouts(uint64_t* count);
  * secret throughout. */
 int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, uint32_t slots,
                         int32_t correction, int32_t s2c_first, uint32_t sparse_h);
+/* Sub-slot refresh for a fully packed context (no reference counterpart: the
+ * reference bootstraps every refresh over all N/2 slots, packed_fideslib.cpp:1084):
+ * a bootstrapper for inputs whose values sit in slots [0, slots) with zeros
+ * elsewhere, slots a power of two <= N/4.  It bootstraps the input replicated
+ * with period `slots` as a sparsely packed ciphertext (trace after ModRaise)
+ * with ONE EvalMod (the real and imaginary parts side by side in 2*slots
+ * slots; the split folded into the last CoeffToSlot group, the merge into the
+ * first SlotToCoeff group) and returns zeros outside [0, slots) (a mask folded
+ * into the last SlotToCoeff group): the same levels as the full bootstrap.
+ * Several sizes may be set up; fhe_bootstrap_keygen generates the keys of
+ * every setup made before it. */
+int fhe_bootstrap_subslot_setup(fhe_ctx* ctx, uint32_t slots, uint32_t budget_cts, uint32_t budget_stc,
+                                int32_t correction);
 int fhe_bootstrap_keygen(fhe_ctx* ctx);
 int fhe_bootstrap(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
 /* The reference's refresh (PackedEvaluator::refresh / bootstrap_components,
@@ -386,6 +399,11 @@ int fhe_bootstrap(fhe_ctx* ctx, const fhe_ct* a, fhe_ct** out);
  * bound]); with passes == 2 the residual (x - first) * 4096 is bootstrapped
  * again and added back / 4096; the result is scaled by bound. */
 int fhe_refresh(fhe_ctx* ctx, const fhe_ct* a, double bound, int32_t passes, fhe_ct** out);
+/* fhe_refresh for an input known to be zero outside slots [0, support): the
+ * smallest sub-slot bootstrapper with slots >= support runs it (the output is
+ * zero outside [0, slots)), else the full bootstrapper; support 0 = full. */
+int fhe_refresh_support(fhe_ctx* ctx, const fhe_ct* a, double bound, int32_t passes, uint32_t support,
+                        fhe_ct** out);
 /* One step of fhe_bootstrap (EvalCoeffsToSlots / EvalSlotsToCoeffs and their
  * neighbours in OpenFHE's FHECKKSRNS): stage 0 = scale down to one limb and
  * ModRaise, 1 = CoeffToSlot, 2 = EvalMod (real and imaginary parts), 3 =

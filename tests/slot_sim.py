@@ -105,6 +105,8 @@ class SlotContext:
         self.refresh_count = 0
         self.max_refresh_ratio = 0.0
         self.has_secret = True
+        self.subslot_sizes = ()
+        self.subslot_refreshes = 0
 
     # -- keys and files (a pickled stand-in for the library's key bundles and
     # ciphertext files: a bundle without the secret makes an evaluation-only
@@ -120,6 +122,11 @@ class SlotContext:
 
     def EvalBootstrapSetup(self, *_, **__):
         pass
+
+    def EvalBootstrapSubslotSetup(self, slots, *_, **__):
+        if slots & (slots - 1) or not 2 <= slots <= self.slots // 2:
+            raise SimError("sub-slot refresh slots must be a power of two <= N/4")
+        self.subslot_sizes = tuple(sorted(set(self.subslot_sizes) | {int(slots)}))
 
     def EvalBootstrapKeyGen(self, *_):
         pass
@@ -235,7 +242,11 @@ class SlotContext:
         coeffs = np.polynomial.chebyshev.chebfit(t, func(0.5 * (t + 1) * (b - a) + a), degree)
         return self.EvalChebyshevSeries(ct, coeffs, a, b)
 
-    def refresh(self, ct, bound: float = 1.0, passes: int = 2, merge: bool = False):
+    def refresh(self, ct, bound: float = 1.0, passes: int = 2, merge: bool = False, support: int = 0):
+        """support > 0 with a sub-slot setup of n >= support slots: the device
+        replicates the input with period n and bootstraps it, so slot i < n
+        comes back as the sum of the input's slots i + j n and every slot from
+        n on as 0; the input must be zero (up to noise) outside [0, support)."""
         ratio = float(np.max(np.abs(ct.values))) / bound
         self.max_refresh_ratio = max(self.max_refresh_ratio, ratio)
         if ratio > 1.0:
@@ -243,7 +254,19 @@ class SlotContext:
         if ct.left < 2:
             raise SimError("too few levels left to refresh")
         self.refresh_count += 1
-        noise = self.rng.uniform(-1, 1, self.slots) * self.refresh_noise * bound
-        return SimCiphertext(ct.values + noise, self.refresh_left + (1 if passes == 1 else 0), 1)
+        left = self.refresh_left + (1 if passes == 1 else 0)
+        sizes = [n for n in self.subslot_sizes if n >= support] if support else []
+        if not sizes:
+            noise = self.rng.uniform(-1, 1, self.slots) * self.refresh_noise * bound
+            return SimCiphertext(ct.values + noise, left, 1)
+        n = sizes[0]
+        outside = float(np.max(np.abs(ct.values[support:]))) / bound if support < self.slots else 0.0
+        if outside > 1e-3:
+            raise SimError(f"sub-slot refresh input is {outside:.3g} x its bound outside [0, {support})")
+        self.subslot_refreshes += 1
+        out = np.zeros(self.slots, dtype=ct.values.dtype)
+        out[:n] = ct.values.reshape(-1, n).sum(axis=0)
+        out[:n] += self.rng.uniform(-1, 1, n) * self.refresh_noise * bound
+        return SimCiphertext(out, left, 1)
 
     EvalRefresh = refresh

@@ -301,6 +301,45 @@ def test_library_refresh_matches_host_refresh(boot_ctx):
     assert np.max(np.abs(two - host)) < 1e-5
 
 
+def test_subslot_refresh():
+    """Sub-slot refreshes (n = 256, 512 of 2048 slots): an input zero outside
+    [0, support) is replicated with period n, bootstrapped with one EvalMod
+    (split and merge folded into the edge CoeffToSlot / SlotToCoeff groups)
+    and masked back: the same limbs as the full refresh, the values on
+    [0, support) within the full refresh's precision, zeros from n on; real
+    and complex values; a support above every sub-slot size takes the full
+    refresh."""
+    from fhe_mamba_b200 import CCParams, CryptoContext
+    cc = CryptoContext(CCParams(ring_dim=1 << 12, multiplicative_depth=25, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3))
+    cc.KeyGen(SEED)
+    cc.EvalBootstrapSetup((4, 4))
+    cc.EvalBootstrapSubslotSetup(512, (4, 4))
+    cc.EvalBootstrapSubslotSetup(256, (4, 4))
+    cc.EvalBootstrapKeyGen()
+    assert cc.subslot_sizes == (256, 512)
+    r = np.random.default_rng(41)
+    for support, n, cplx in ((200, 256, False), (512, 512, False), (300, 512, True), (1000, 0, False)):
+        x = np.zeros(cc.slots, dtype=complex)
+        x[:support] = r.uniform(-5, 5, support) + (1j * r.uniform(-5, 5, support) if cplx else 0)
+        ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x if cplx else x.real))
+        cc.LevelReduceInPlace(ct, cc.n_q - 4)
+        full = cc.EvalRefresh(ct, 8.0, passes=2)
+        for passes, tol in ((1, 1e-3), (2, 1e-5)):
+            out = cc.EvalRefresh(ct, 8.0, passes=passes, support=support)
+            ref = cc.EvalRefresh(ct, 8.0, passes=passes)
+            assert out.n_limbs() == ref.n_limbs(), (support, passes)
+            y = cc.Decrypt(out).GetCKKSPackedValue()
+            if not cplx:
+                y = y.real
+            assert np.max(np.abs(y[:support] - x[:support])) < tol, (support, passes)
+            if n:
+                assert np.max(np.abs(y[n:])) < tol, (support, passes)
+        yf = cc.Decrypt(full).GetCKKSPackedValue()
+        assert np.max(np.abs((yf if cplx else yf.real) - x)) < 1e-5
+    cc.close()
+
+
 def test_bootstrap_at_token_loop_parameters():
     """The token loop's own parameter set (N = 2^16, 2^15 slots, depth 44,
     59/60-bit primes, dnum 3, level budget {4, 4}, uniform ternary secret): a
@@ -311,6 +350,7 @@ def test_bootstrap_at_token_loop_parameters():
                                 first_mod_size=60, num_large_digits=3))
     cc.KeyGen(SEED)
     cc.EvalBootstrapSetup((4, 4))
+    cc.EvalBootstrapSubslotSetup(4096, (4, 4))
     cc.EvalBootstrapKeyGen()
     x = np.random.default_rng(16).uniform(-1, 1, cc.slots)
     ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
@@ -320,6 +360,16 @@ def test_bootstrap_at_token_loop_parameters():
     assert np.max(np.abs(cc.Decrypt(out).GetRealPackedValue() - x)) < 5e-4
     ct4 = cc.Encrypt(cc.MakeCKKSPackedPlaintext(4 * x))
     cc.LevelReduceInPlace(ct4, cc.n_q - 6)  # 6 limbs: the scaling by 1 / bound and two passes
-    two = cc.Decrypt(cc.EvalRefresh(ct4, 4.0, passes=2)).GetRealPackedValue()
+    two_ct = cc.EvalRefresh(ct4, 4.0, passes=2)
+    two = cc.Decrypt(two_ct).GetRealPackedValue()
     assert np.max(np.abs(two - 4 * x)) < 1e-5
+    # the sub-slot refresh of the same values cut to the in_proj width
+    v = np.zeros(cc.slots)
+    v[:3352] = 4 * x[:3352]
+    cv = cc.Encrypt(cc.MakeCKKSPackedPlaintext(v))
+    cc.LevelReduceInPlace(cv, cc.n_q - 6)
+    out = cc.EvalRefresh(cv, 4.0, passes=2, support=3352)
+    assert out.n_limbs() == two_ct.n_limbs()
+    sub = cc.Decrypt(out).GetRealPackedValue()
+    assert np.max(np.abs(sub[:3352] - v[:3352])) < 1e-5 and np.max(np.abs(sub[4096:])) < 1e-5
     cc.close()

@@ -74,3 +74,44 @@ def test_fused_decay():
         assert cc.max_refresh_ratio <= 1.0
         counts[fused] = em.refreshes()
     assert counts[True] < counts[False]
+
+
+def test_subslot_refresh_schedule():
+    """Refreshes over fewer slots (EvalBootstrapSubslotSetup): every site that
+    declares a support is zero outside it (the slot model raises otherwise and
+    returns the sum of the input's n-periodic copies, as the device's
+    replicate-then-bootstrap does), so the loop still reproduces the fp64
+    polynomial path to rounding; the carried states keep the full refresh."""
+    from fhe_mamba_b200.mamba2_layer import (EncryptedMamba2Layer, EncryptedMamba2Model, Mamba2Model, Mamba2Polys,
+                                             Mamba2Weights, calibrate_bounds, plain_step)
+    W = Mamba2Weights(d_model=768, d_state=128, heads=24)
+    P = Mamba2Polys(W, samples=2)
+    bounds = calibrate_bounds(W, P, samples=2)
+    cc = SlotContext(1 << 15, refresh_noise=0.0)
+    cc.EvalBootstrapSubslotSetup(4096)
+    cc.EvalBootstrapSubslotSetup(2048)
+    layer = EncryptedMamba2Layer(cc, W, P)
+    cc.EvalRotateKeyGen(layer.rotation_steps())
+    rng = np.random.default_rng(12)
+    conv_p = [np.zeros(W.conv_dim) for _ in range(W.conv_kernel - 1)]
+    conv_c = [None] * (W.conv_kernel - 1)
+    st_p = st_c = None
+    for _ in range(2):
+        h = rng.normal(0, 1, W.d_model)
+        want, conv_p, st_p = plain_step(W, P, h, conv_p, st_p)
+        out, conv_c, st_c = layer.step(cc.Encrypt(cc.MakeCKKSPackedPlaintext(h)), conv_c, st_c, bounds)
+        assert np.max(np.abs(cc.Decrypt(out).GetRealPackedValue()[:W.d_model] - want)) < 1e-10
+    assert cc.subslot_refreshes >= 1 and cc.max_refresh_ratio <= 1.0
+
+    for fused in (False, True):
+        m = Mamba2Model(layers=2, d_model=64, d_state=32, heads=16, vocab=128, std=0.1, fused_decay=fused)
+        cc = SlotContext(2048, refresh_noise=0.0)
+        cc.EvalBootstrapSubslotSetup(512)
+        em = EncryptedMamba2Model(cc, m)
+        cc.EvalRotateKeyGen(em.rotation_steps())
+        state = m.initial_state()
+        for tok in (3, 17, 5, 9):
+            hf, logits, state = m.plain_token(tok, state)
+            picked, ehf = em.select(em.step(tok))
+            assert picked == int(np.argmax(logits)) and np.max(np.abs(ehf - hf)) < 1e-10
+        assert 1 <= cc.subslot_refreshes <= em.refreshes()
