@@ -69,6 +69,12 @@ FUSED_KEY_INNER = False
 # Two-pass refresh at N = 2^16: 158 ms over all slots, 115 ms over 4096, 105 ms
 # over 2048; the steady evaluation 15.8 s with (4096, 2048) against 20.1 s.
 SUBSLOT_SIZES = (4096, 2048)
+# Their level budget {CoeffToSlot, SlotToCoeff} (--subslot-budget).  {3, 3}
+# returns two more limbs, which drops the packed-input refresh; but the
+# carried states, updated from that input, then run out of levels every 4
+# tokens instead of every 12 (slot model, 36 tokens: 76.8 sub-slot + 35.4
+# full refreshes per token against 96.5 + 14.7), so {4, 4} stays.
+SUBSLOT_BUDGET = (4, 4)
 
 
 _JSON_OUT = None
@@ -575,7 +581,7 @@ class TokenLoop:
         # sub-slot refreshes need a fully packed context and the uniform secret
         self.subslot = () if (classical128 or sparse_h) else tuple(SUBSLOT_SIZES)
         for n in self.subslot:
-            self.cc.EvalBootstrapSubslotSetup(n, (4, 4))
+            self.cc.EvalBootstrapSubslotSetup(n, SUBSLOT_BUDGET)
         self.cc.EvalBootstrapKeyGen()
         # ring 2^17 doubles every key and ciphertext: a smaller diagonal cache
         if cache_gb is None:
@@ -731,6 +737,7 @@ def config_dict(args):
             "l2": "inputs larger than L2 (keys ~36 GB, diagonals generated on the device)",
             "diagonal_cache_gb": args.diagonal_cache_gb,
             "subslot_refresh": [] if args.security == "128-classic" or args.sparse_h else list(SUBSLOT_SIZES),
+            "subslot_budget": list(SUBSLOT_BUDGET),
             "parallelism": "one token-loop replica per GPU"}
 
 
@@ -781,7 +788,7 @@ def measure_ntt(local, steps, warmup):
 
 
 def main():
-    global CONVERSION, FUSED_KEY_INNER, DIAGONAL_CACHE_GB, SUBSLOT_SIZES
+    global CONVERSION, FUSED_KEY_INNER, DIAGONAL_CACHE_GB, SUBSLOT_SIZES, SUBSLOT_BUDGET
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2, help="timed tokens")
@@ -811,6 +818,8 @@ def main():
     ap.add_argument("--subslot-refresh", default=",".join(map(str, SUBSLOT_SIZES)),
                     help="comma-separated slot counts of sub-slot refreshes for values known to be zero outside "
                          "[0, n) (one EvalMod over n slots instead of two over all); 0: every refresh over all slots")
+    ap.add_argument("--subslot-budget", default=",".join(map(str, SUBSLOT_BUDGET)),
+                    help="level budget CoeffToSlot,SlotToCoeff of the sub-slot refreshes")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ckks", action="store_true", help="skip the key-switch, matvec and bootstrap side measurements")
@@ -824,6 +833,9 @@ def main():
     args = ap.parse_args()
     CONVERSION = args.conversion
     SUBSLOT_SIZES = tuple(int(v) for v in args.subslot_refresh.split(",") if int(v))
+    SUBSLOT_BUDGET = tuple(int(v) for v in args.subslot_budget.split(","))
+    if len(SUBSLOT_BUDGET) != 2:
+        ap.error("--subslot-budget takes two numbers")
     DIAGONAL_CACHE_GB = args.diagonal_cache_gb
     FUSED_KEY_INNER = args.keyswitch_fusion == "on"
     if args.warmup < 3:

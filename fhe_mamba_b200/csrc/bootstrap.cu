@@ -265,6 +265,15 @@ void Bootstrapper::keygen() {
   }
   const uint64_t conj = 2ull * ck_.ctx.n - 1;
   if (!ck_.has_rotation_key(conj)) ck_.rotation_keygen(conj);
+  // companion babies: sigma_aux o rot(j * stride), j < b
+  for (const auto* gs : {&cts_, &stc_})
+    for (const Group& g : *gs)
+      if (g.aux)
+        for (uint32_t j = 0; j < g.b; ++j) {
+          const uint64_t a = aux_galois(g);
+          const uint64_t e = j ? nt::mulmod(a, ck_.galois_for_step((int64_t)j * g.stride), 2ull * ck_.ctx.n) : a;
+          if (!ck_.has_rotation_key(e)) ck_.rotation_keygen(e);
+        }
   for (uint32_t j = 1; j < trace_; j *= 2) {  // sparse-packing trace (and the sub-slot replication and merge)
     const uint64_t g = ck_.galois_for_full_step((int64_t)j * n_);
     if (!ck_.has_rotation_key(g)) ck_.rotation_keygen(g);
@@ -314,11 +323,20 @@ std::unique_ptr<Ct> Bootstrapper::transform(std::vector<Group>& groups, std::uni
       for (size_t i = 0; i < d.size(); ++i) d[i] = enc[i].get();
       return d;
     };
-    auto y = ck_.linear_transform(*x, ptrs(it->second), g.b, g.G, g.stride, g.offset);
-    if (g.aux) {  // the companion: the same transform shape on conj(x) or rot(x, n)
-      auto x2 = g.aux == 1 ? ck_.rotate(*x, 2ull * ctx.n - 1) : ck_.rotate(*x, ck_.galois_for_full_step((int64_t)n_));
-      auto y2 = ck_.linear_transform(*x2, ptrs(g.enc2.at(nq)), g.b, g.G, g.stride, g.offset);
-      y = ck_.add(*y, *y2, false);
+    std::unique_ptr<Ct> y;
+    if (!g.aux) {
+      y = ck_.linear_transform(*x, ptrs(it->second), g.b, g.G, g.stride, g.offset);
+    } else {
+      // the companion on conj(x) or rot(x, n) shares the ModUp and the giant
+      // steps: diagonals [giant][main b | companion b]
+      const auto& e2 = g.enc2.at(nq);
+      std::vector<const Pt*> d;
+      d.reserve(2 * it->second.size());
+      for (uint32_t gg = 0; gg < g.G; ++gg) {
+        for (uint32_t j = 0; j < g.b; ++j) d.push_back(it->second[(size_t)gg * g.b + j].get());
+        for (uint32_t j = 0; j < g.b; ++j) d.push_back(e2[(size_t)gg * g.b + j].get());
+      }
+      y = ck_.linear_transform(*x, d, g.b, g.G, g.stride, g.offset, aux_galois(g));
     }
     ck_.rescale_inplace(*y);
     y->scale = target;  // equal to the computed scale up to its last bit
@@ -371,6 +389,10 @@ std::unique_ptr<Ct> Bootstrapper::coeff_to_slot(const Ct& raised) {
   auto x = transform(cts_, ck_.clone(raised));
   levels_[1] = x->nq;
   return x;
+}
+
+uint64_t Bootstrapper::aux_galois(const Group& g) const {
+  return g.aux == 1 ? 2ull * ck_.ctx.n - 1 : ck_.galois_for_full_step((int64_t)n_);
 }
 
 std::unique_ptr<Ct> Bootstrapper::replicate(const Ct& x) {

@@ -107,6 +107,7 @@ class Bootstrapper {
   void build_groups(std::vector<Group>& out, const std::vector<uint32_t>& halves, uint32_t budget, bool inverse,
                     double factor, Edit first, Edit last);
   std::unique_ptr<Ct> transform(std::vector<Group>& groups, std::unique_ptr<Ct> x);
+  uint64_t aux_galois(const Group& g) const;  // conjugation (aux 1) or rotation by n (aux 2)
   std::unique_ptr<Ct> eval_mod(const Ct& x);
 
   Ckks& ck_;

@@ -809,13 +809,15 @@ std::vector<std::unique_ptr<Ct>> Ckks::rotate_hoisted(const Ct& a, const std::ve
 }
 
 std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a_in, const std::vector<const Pt*>& diags, uint32_t b,
-                                           uint32_t G, int64_t stride, int64_t giant_offset) {
+                                           uint32_t G, int64_t stride, int64_t giant_offset, uint64_t aux_galois) {
   require(a_in.ncomp == 2, "linear transform expects a 2-component ciphertext", -1);
   std::unique_ptr<Ct> pre;
   if (a_in.noise_deg >= 2) pre = prepare_mult_input(a_in);
   const Ct& a = pre ? *pre : a_in;
-  require(b >= 1 && b <= 32 && G >= 1, "baby step must be in [1, 32], giant step >= 1", -1);
-  require(diags.size() == (size_t)b * G, "need baby*giant diagonal entries", -1);
+  const uint32_t nb = aux_galois ? 2 * b : b;  // babies of the dot product
+  require(b >= 1 && nb <= 32 && G >= 1, "baby step must be in [1, 32] (16 with a companion), giant step >= 1", -1);
+  require(diags.size() == (size_t)nb * G, "need baby*giant diagonal entries (twice that with a companion)", -1);
+  require(aux_galois == 0 || (aux_galois & 1), "the companion's Galois element must be odd", -1);
   require(stride != 0, "stride must be non-zero", -1);
   const uint32_t nq = a.nq, n = ctx.n;
   double pscale = 0.0;
@@ -829,6 +831,10 @@ std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a_in, const std::vector<con
   // Babies: j = 0 is the input itself, 1..b-1 (rotations by j*stride) share one ModUp.
   std::vector<uint64_t> gs;
   for (uint32_t j = 1; j < b; ++j) gs.push_back(galois_for_step((int64_t)j * stride));
+  // companion babies sigma_aux o sigma_{5^{j stride}} = sigma_{aux 5^{j stride} mod 2N}
+  if (aux_galois)
+    for (uint32_t j = 0; j < b; ++j)
+      gs.push_back(j ? nt::mulmod(aux_galois, galois_for_step((int64_t)j * stride), 2ull * n) : aux_galois);
   auto rot = rotate_hoisted(a, gs);
   auto base = clone(a);  // cap == nq, component stride nq*N like the rotations
   std::vector<const uint64_t*> tab{base->data()};
@@ -838,7 +844,7 @@ std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a_in, const std::vector<con
       static_cast<const uint64_t* const*>(stage_pointers(tab.data(), tab.size() * sizeof(void*), 23));
   const size_t cs = (size_t)nq * n;
   uint64_t* inner = ws(21, (size_t)G * 2 * cs);
-  launch_bsgs_dot(d_tab, d_tab + b, inner, b, G, nq, n, ctx.d_mod.as<Modulus>(), ctx.stream);
+  launch_bsgs_dot(d_tab, d_tab + nb, inner, nb, G, nq, n, ctx.d_mod.as<Modulus>(), ctx.stream);
   auto out = alloc(nq, 2);
   out->scale = a.scale * pscale;
   out->noise_deg = a.noise_deg + 1;

@@ -142,8 +142,12 @@ class Ckks {
   // with the same scale; babies share one ModUp.
   // General form: baby j rotates by j*stride, giant g by (g*b - giant_offset)*stride,
   // so diagonal (g*b + j - giant_offset)*stride is pre-rotated by the giant amount.
+  // aux_galois != 0 adds a companion transform of the same shape on
+  // sigma_aux(a): diags then has 2b*G entries, [g][0, b) on a and [g][b, 2b) on
+  // sigma_aux(a); the companion's babies sigma_aux o rot(j*stride) share the
+  // ModUp and every giant step with the main transform.
   std::unique_ptr<Ct> linear_transform(const Ct& a, const std::vector<const Pt*>& diags, uint32_t b, uint32_t G,
-                                       int64_t stride = 1, int64_t giant_offset = 0);
+                                       int64_t stride = 1, int64_t giant_offset = 0, uint64_t aux_galois = 0);
 
   // ModRaise for bootstrapping: the centred coefficients of limb 0 lifted to
   // every Q limb (the plaintext becomes m + q_0 I).

@@ -471,6 +471,7 @@ class EncryptedMamba2Layer:
         self.pm = PackedMamba2(cc, self.layout, b_base=E, c_base=E + S, head_base=self.dt_base,
                                decay_base=self.decay_base)
         self.refreshes = self.two_pass_refreshes = 0
+        self.site_refreshes = {}  # refreshes by site name
         self._lin = {}
         n = cc.slots
     # ---- setup --------------------------------------------------------------
@@ -530,6 +531,7 @@ class EncryptedMamba2Layer:
         passes = self.passes(site) if callable(self.passes) else self.passes
         self.refreshes += 1
         self.two_pass_refreshes += passes == 2
+        self.site_refreshes[site] = self.site_refreshes.get(site, 0) + 1
         if support and getattr(self.cc, "subslot_sizes", ()):
             return self.cc.refresh(ct, bound, passes=passes, support=support)
         return self.cc.refresh(ct, bound, passes=passes)

@@ -106,6 +106,7 @@ class SlotContext:
         self.max_refresh_ratio = 0.0
         self.has_secret = True
         self.subslot_sizes = ()
+        self.subslot_extra = {}
         self.subslot_refreshes = 0
 
     # -- keys and files (a pickled stand-in for the library's key bundles and
@@ -123,10 +124,13 @@ class SlotContext:
     def EvalBootstrapSetup(self, *_, **__):
         pass
 
-    def EvalBootstrapSubslotSetup(self, slots, *_, **__):
+    def EvalBootstrapSubslotSetup(self, slots, level_budget=(4, 4), *_, **__):
+        """The levels a sub-slot refresh returns follow its level budget: each
+        transform level below the full refresh's {4, 4} is one more left."""
         if slots & (slots - 1) or not 2 <= slots <= self.slots // 2:
             raise SimError("sub-slot refresh slots must be a power of two <= N/4")
         self.subslot_sizes = tuple(sorted(set(self.subslot_sizes) | {int(slots)}))
+        self.subslot_extra[int(slots)] = 8 - int(level_budget[0]) - int(level_budget[1])
 
     def EvalBootstrapKeyGen(self, *_):
         pass
@@ -267,6 +271,6 @@ class SlotContext:
         out = np.zeros(self.slots, dtype=ct.values.dtype)
         out[:n] = ct.values.reshape(-1, n).sum(axis=0)
         out[:n] += self.rng.uniform(-1, 1, n) * self.refresh_noise * bound
-        return SimCiphertext(out, left, 1)
+        return SimCiphertext(out, left + self.subslot_extra[n], 1)
 
     EvalRefresh = refresh

@@ -88,8 +88,8 @@ def test_subslot_refresh_schedule():
     P = Mamba2Polys(W, samples=2)
     bounds = calibrate_bounds(W, P, samples=2)
     cc = SlotContext(1 << 15, refresh_noise=0.0)
-    cc.EvalBootstrapSubslotSetup(4096)
-    cc.EvalBootstrapSubslotSetup(2048)
+    cc.EvalBootstrapSubslotSetup(4096, (3, 3))
+    cc.EvalBootstrapSubslotSetup(2048, (3, 3))
     layer = EncryptedMamba2Layer(cc, W, P)
     cc.EvalRotateKeyGen(layer.rotation_steps())
     rng = np.random.default_rng(12)
