@@ -54,31 +54,77 @@ Ckks::Ckks(Context& c) : ctx(c) {
   FHE_CUDA(cudaMemcpy(mods_host_.data(), c.d_mod.p, mods_host_.size() * sizeof(Modulus), cudaMemcpyDeviceToHost));
   build_static_tables();
   status_ = DevMem(sizeof(unsigned));
+  FHE_CUDA(cudaMemset(status_.p, 0, sizeof(unsigned)));
+  stage_ring_.resize(kStageSlots);
 }
 
 Ckks::~Ckks() {
-  if (ptr_event_) cudaEventDestroy(ptr_event_);
-  if (pinned_) cudaFreeHost(pinned_);
+  for (StageSlot& s : stage_ring_) {
+    if (s.pending) cudaEventSynchronize(s.done);
+    if (s.done) cudaEventDestroy(s.done);
+    if (s.host) cudaFreeHost(s.host);
+  }
+}
+
+// Copies host data to device memory without blocking the host: through the
+// next pinned slot of the ring, which is reused once its previous copy ran.
+void Ckks::stage_upload(void* dev, const void* host, size_t bytes) {
+  StageSlot& s = stage_ring_[stage_next_];
+  stage_next_ = (stage_next_ + 1) % stage_ring_.size();
+  if (!s.done) FHE_CUDA(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+  if (s.pending) FHE_CUDA(cudaEventSynchronize(s.done));
+  s.pending = false;
+  if (s.bytes < bytes) {
+    if (s.host) FHE_CUDA(cudaFreeHost(s.host));
+    s.host = nullptr;
+    s.bytes = 0;
+    const size_t want = std::max<size_t>(bytes, 4096);
+    FHE_CUDA(cudaMallocHost(&s.host, want));
+    s.bytes = want;
+  }
+  std::memcpy(s.host, host, bytes);
+  FHE_CUDA(cudaMemcpyAsync(dev, s.host, bytes, cudaMemcpyHostToDevice, ctx.stream));
+  FHE_CUDA(cudaEventRecord(s.done, ctx.stream));
+  s.pending = true;
 }
 
 // Copies a small host table (pointers) to a device scratch buffer without
-// blocking the host: the data goes through pinned memory, reused once the
-// previous copy has finished.
+// blocking the host.
 const void* Ckks::stage_pointers(const void* host, size_t bytes, size_t ws_idx) {
-  if (!ptr_event_) FHE_CUDA(cudaEventCreateWithFlags(&ptr_event_, cudaEventDisableTiming));
-  else FHE_CUDA(cudaEventSynchronize(ptr_event_));
-  if (pinned_bytes_ < bytes) {
-    if (pinned_) FHE_CUDA(cudaFreeHost(pinned_));
-    pinned_ = nullptr;
-    FHE_CUDA(cudaMallocHost(&pinned_, bytes));
-    pinned_bytes_ = bytes;
-  }
-  std::memcpy(pinned_, host, bytes);
   uint64_t* d = ws(ws_idx, (bytes + 7) / 8);
-  FHE_CUDA(cudaMemcpyAsync(d, pinned_, bytes, cudaMemcpyHostToDevice, ctx.stream));
-  FHE_CUDA(cudaEventRecord(ptr_event_, ctx.stream));
+  stage_upload(d, host, bytes);
   return d;
 }
+
+void Ckks::check_encode_status() {
+  unsigned st = 0;
+  FHE_CUDA(cudaMemcpyAsync(&st, status_.p, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx.stream));
+  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  if (st) {
+    FHE_CUDA(cudaMemsetAsync(status_.p, 0, sizeof(unsigned), ctx.stream));
+    FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  }
+  require(st == 0, "encode: a scaled value is not finite or reaches 2^126", -1);
+}
+
+namespace {
+
+// True when the rounding kernel cannot flag these values: all finite and
+// (max |re| + max |im|) * scale < 2^120.  Every coefficient of the encoding is
+// bounded by the largest slot magnitude (an average of the slots times roots
+// of unity), which leaves 2^6 of room below the kernel's 2^126 limit.
+bool encode_in_range(const double* re, const double* im, size_t count, double scale) {
+  double mr = 0.0, mi = 0.0;
+  for (size_t i = 0; i < count; ++i) {
+    const double a = re ? std::fabs(re[i]) : 0.0, b = im ? std::fabs(im[i]) : 0.0;
+    if (!(a <= 1e300) || !(b <= 1e300)) return false;  // NaN or infinite
+    mr = std::max(mr, a);
+    mi = std::max(mi, b);
+  }
+  return std::isfinite(scale) && (mr + mi) * scale < 0x1p120;
+}
+
+}  // namespace
 
 // Context-owned scratch buffers, reused across calls (one stream orders all use).
 uint64_t* Ckks::ws(size_t idx, size_t words) {
@@ -467,11 +513,10 @@ std::unique_ptr<Pt> Ckks::encode(const double* re, const double* im, uint32_t co
   std::vector<double2> v(slots, make_double2(0.0, 0.0));
   for (uint32_t i = 0; i < count; ++i) v[i] = make_double2(re ? re[i] : 0.0, im ? im[i] : 0.0);
   double2* dv = reinterpret_cast<double2*>(ws(13, 2 * (size_t)slots));
-  FHE_CUDA(cudaMemcpyAsync(dv, v.data(), slots * sizeof(double2), cudaMemcpyHostToDevice, ctx.stream));
+  stage_upload(dv, v.data(), slots * sizeof(double2));
   launch_fft_special_inv(dv, fft_inv_tw_.as<double2>(), slots, 1, ctx.stream);
   double* coef = reinterpret_cast<double*>(ws(14, n));
   FHE_CUDA(cudaMemsetAsync(coef, 0, (size_t)n * 8, ctx.stream));
-  FHE_CUDA(cudaMemsetAsync(status_.p, 0, sizeof(unsigned), ctx.stream));
   launch_encode_round(dv, coef, slots, n, scale, status_.as<unsigned>(), ctx.stream);
   auto p = std::make_unique<Pt>();
   p->buf = DevMem((size_t)nq * n * 8, ctx.sh);
@@ -479,10 +524,8 @@ std::unique_ptr<Pt> Ckks::encode(const double* re, const double* im, uint32_t co
   p->scale = scale;
   launch_lift_double(coef, p->data(), n, nq, PrimeMap{nq, ctx.L}, ctx.d_mod.as<Modulus>(), 1, ctx.stream);
   ntt_dense(p->data(), 1, nq, nq, 0, false);
-  unsigned st = 0;
-  FHE_CUDA(cudaMemcpyAsync(&st, status_.p, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx.stream));
-  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
-  require(st == 0, "encode: a scaled value is not finite or reaches 2^126", -1);
+  // values the rounding cannot reject return without waiting for the device
+  if (!encode_in_range(re, im, count, scale)) check_encode_status();
   return p;
 }
 
@@ -504,20 +547,21 @@ std::vector<std::unique_ptr<Pt>> Ckks::encode_batch(const double* re, const doub
       }
     double2* dv = reinterpret_cast<double2*>(ws(18, 2 * (size_t)nb * slots));
     FHE_CUDA(cudaMemcpyAsync(dv, v.data(), (size_t)nb * slots * sizeof(double2), cudaMemcpyHostToDevice, ctx.stream));
-    encode_slots_on_device(dv, nb, nq, scale, out);
+    const bool in_range = encode_in_range(re ? re + (size_t)b0 * count : nullptr, im ? im + (size_t)b0 * count : nullptr,
+                                          (size_t)nb * count, scale);
+    encode_slots_on_device(dv, nb, nq, scale, !in_range, out);
   }
   return out;
 }
 
 // Encodes nb slot vectors already on the device (dv, [nb][slots], clobbered):
 // special inverse FFT, scale and round, RNS lift, NTT; appends the plaintexts.
-void Ckks::encode_slots_on_device(double2* dv, uint32_t nb, uint32_t nq, double scale,
+void Ckks::encode_slots_on_device(double2* dv, uint32_t nb, uint32_t nq, double scale, bool check,
                                   std::vector<std::unique_ptr<Pt>>& out) {
   const uint32_t slots = ctx.slots, n = ctx.n;
   launch_fft_special_inv(dv, fft_inv_tw_.as<double2>(), slots, nb, ctx.stream);
   double* coef = reinterpret_cast<double*>(ws(19, (size_t)nb * n));
   FHE_CUDA(cudaMemsetAsync(coef, 0, (size_t)nb * n * 8, ctx.stream));
-  FHE_CUDA(cudaMemsetAsync(status_.p, 0, sizeof(unsigned), ctx.stream));
   launch_encode_round_batch(dv, coef, slots, n, scale, nb, status_.as<unsigned>(), ctx.stream);
   uint64_t* res = ws(20, (size_t)nb * nq * n);
   launch_lift_double(coef, res, n, nq, PrimeMap{nq, ctx.L}, ctx.d_mod.as<Modulus>(), nb, ctx.stream);
@@ -531,10 +575,8 @@ void Ckks::encode_slots_on_device(double2* dv, uint32_t nb, uint32_t nq, double 
                              ctx.stream));
     out.push_back(std::move(p));
   }
-  unsigned st = 0;
-  FHE_CUDA(cudaMemcpyAsync(&st, status_.p, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx.stream));
-  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
-  require(st == 0, "encode: a scaled value is not finite or reaches 2^126", -1);
+  // otherwise the sticky status is read at the next decode
+  if (check) check_encode_status();
 }
 
 std::vector<std::unique_ptr<Pt>> Ckks::encode_replicated_diagonals(const double* w_dev, uint32_t m, uint32_t cols,
@@ -550,7 +592,7 @@ std::vector<std::unique_ptr<Pt>> Ckks::encode_replicated_diagonals(const double*
     const uint32_t nb = std::min(chunk, T - t0);
     double2* dv = reinterpret_cast<double2*>(ws(18, 2 * (size_t)nb * slots));
     launch_replicated_diagonals(dv, w_dev, m, cols, R, T, win, baby, slots, t0, nb, ctx.stream);
-    encode_slots_on_device(dv, nb, nq, scale, out);
+    encode_slots_on_device(dv, nb, nq, scale, false, out);
   }
   return out;
 }
@@ -569,7 +611,7 @@ void Ckks::decode(const Pt& p, double* re, double* im, uint32_t count) {
   launch_fft_special_fwd(dv, fft_fwd_tw_.as<double2>(), slots, 1, ctx.stream);
   std::vector<double2> v(slots);
   FHE_CUDA(cudaMemcpyAsync(v.data(), dv, slots * sizeof(double2), cudaMemcpyDeviceToHost, ctx.stream));
-  FHE_CUDA(cudaStreamSynchronize(ctx.stream));
+  check_encode_status();  // also waits for the copy
   for (uint32_t i = 0; i < count; ++i) {
     if (re) re[i] = v[i].x;
     if (im) im[i] = v[i].y;

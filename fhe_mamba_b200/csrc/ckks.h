@@ -184,7 +184,7 @@ class Ckks {
                    const uint64_t* add_c0);
   void switch_keygen(uint64_t key_id, const uint64_t* s_new, const uint64_t* s_old, DevMem& out);
   void ntt_dense(uint64_t* d, uint32_t polys, uint32_t limbs, uint32_t stride, uint32_t prime0, bool inv);
-  void encode_slots_on_device(double2* dv, uint32_t nb, uint32_t nq, double scale,
+  void encode_slots_on_device(double2* dv, uint32_t nb, uint32_t nq, double scale, bool check,
                               std::vector<std::unique_ptr<Pt>>& out);
   uint64_t* ws(size_t idx, size_t words);
   std::vector<uint64_t> scalar_residues(long double v, uint32_t nq) const;
@@ -211,12 +211,23 @@ class Ckks {
   std::unique_ptr<Ct> switch_with(const Ct& a, const DevMem& key);
   std::map<uint64_t, DevMem> rot_;
   std::vector<DevMem> ws_;
+  // Sticky status of the encoders' rounding kernels (non-finite or >= 2^126
+  // values); read and cleared by check_encode_status().
   DevMem status_;
-  // Pinned staging for per-call pointer tables, reused once the previous
-  // copy (ptr_event_) has completed.
-  void* pinned_ = nullptr;
-  size_t pinned_bytes_ = 0;
-  cudaEvent_t ptr_event_ = nullptr;
+  void check_encode_status();
+  // Ring of pinned host buffers for host -> device uploads that must not
+  // block the host: a slot is rewritten only after the copy that read it
+  // (its event) has run, so the host can run up to kStageSlots uploads ahead.
+  struct StageSlot {
+    void* host = nullptr;
+    size_t bytes = 0;
+    cudaEvent_t done = nullptr;
+    bool pending = false;
+  };
+  static constexpr size_t kStageSlots = 16;
+  std::vector<StageSlot> stage_ring_;
+  size_t stage_next_ = 0;
+  void stage_upload(void* dev, const void* host, size_t bytes);
   const void* stage_pointers(const void* host, size_t bytes, size_t ws_idx);
 
  public:

@@ -504,6 +504,8 @@ class EncryptedMamba2Layer:
         device (uploaded once per layer and matrix)."""
         if name not in self._wdev:
             import torch
+            if not np.all(np.isfinite(self.W[name])):  # the device encoder checks only at the next decode
+                raise ValueError(f"weight matrix {name} holds non-finite values")
             self._wdev[name] = torch.from_numpy(np.ascontiguousarray(self.W[name], dtype=np.float64)).to(
                 torch.device("cuda", self.cc.device))
             torch.cuda.synchronize(self.cc.device)

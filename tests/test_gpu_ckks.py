@@ -190,6 +190,18 @@ def test_errors_are_reported(cfg1):
         cc.RescaleInPlace(y)
     with pytest.raises(FheError):
         cc.MakeCKKSPackedPlaintext(np.full(4, 1e30))
+    # encodes return without waiting for the device unless a value could be
+    # rejected: non-finite values still raise at the call, batched ones too,
+    # and the next encode after an error is clean
+    for bad in (np.inf, -np.inf, np.nan):
+        v = np.zeros(8)
+        v[3] = bad
+        with pytest.raises(FheError):
+            cc.MakeCKKSPackedPlaintext(v)
+        with pytest.raises(FheError):
+            cc.MakeCKKSPackedPlaintexts(np.stack([np.zeros(8), v]))
+    z = _msg(cc.slots, 2)
+    assert np.max(np.abs(cc.MakeCKKSPackedPlaintext(z).GetRealPackedValue() - z)) < 1e-9
 
 
 def test_config3_keyswitch_shape(oracle):
