@@ -64,6 +64,9 @@ CONVERSION = "tensor"
 DIAGONAL_CACHE_GB = 0.0
 # Key inner product of the Q limbs inside ModDown's last NTT pass (--keyswitch-fusion).
 FUSED_KEY_INNER = False
+# Budget of the memo of the layers' constant plaintexts (masks, taps, biases
+# by level and scale; --constant-memo-gb, 0: encode at every use).
+MEMO_GB = 4.0
 # Slot counts of the sub-slot refreshes (--subslot-refresh): a refresh of a
 # value known to be zero outside [0, n) bootstraps n slots with one EvalMod.
 # Two-pass refresh at N = 2^16: 158 ms over all slots, 115 ms over 4096, 105 ms
@@ -586,7 +589,7 @@ class TokenLoop:
         # ring 2^17 doubles every key and ciphertext: a smaller diagonal cache
         if cache_gb is None:
             cache_gb = DIAGONAL_CACHE_GB
-        self.em = EncryptedMamba2Model(self.cc, self.model, passes=passes, cache_gb=cache_gb)
+        self.em = EncryptedMamba2Model(self.cc, self.model, passes=passes, cache_gb=cache_gb, memo_gb=MEMO_GB)
         self.cc.EvalRotateKeyGen(self.em.rotation_steps())
         self.cc.synchronize()
         self.setup_seconds = time.perf_counter() - t0
@@ -621,7 +624,8 @@ class TokenLoop:
         the server's device time (CUDA events on the context stream) is kept."""
         import torch
         self.inputs.append(int(token))
-        cache, before = self.em.cache, (self.em.cache.hits, self.em.cache.misses, self.em.refreshes())
+        cache, memo = self.em.cache, self.em.memo
+        before = (cache.hits, cache.misses, self.em.refreshes(), memo.hits if memo else 0, memo.misses if memo else 0)
         ct = self.encrypt(token)                    # client
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(self.stream)
@@ -630,7 +634,9 @@ class TokenLoop:
         e1.synchronize()
         self.eval_ms.append(e0.elapsed_time(e1))
         self.eval_stats.append({"cache_hits": cache.hits - before[0], "cache_misses": cache.misses - before[1],
-                                "refreshes": self.em.refreshes() - before[2]})
+                                "refreshes": self.em.refreshes() - before[2],
+                                "constant_encodes": (memo.misses - before[4]) if memo else None,
+                                "constant_memo_hits": (memo.hits - before[3]) if memo else None})
         return self.select(hidden)                  # client
 
     def plaintext_check(self):
@@ -737,7 +743,7 @@ def config_dict(args):
             "l2": "inputs larger than L2 (keys ~36 GB, diagonals generated on the device)",
             "diagonal_cache_gb": args.diagonal_cache_gb,
             "subslot_refresh": [] if args.security == "128-classic" or args.sparse_h else list(SUBSLOT_SIZES),
-            "subslot_budget": list(SUBSLOT_BUDGET),
+            "subslot_budget": list(SUBSLOT_BUDGET), "constant_memo_gb": args.constant_memo_gb,
             "parallelism": "one token-loop replica per GPU"}
 
 
@@ -788,7 +794,7 @@ def measure_ntt(local, steps, warmup):
 
 
 def main():
-    global CONVERSION, FUSED_KEY_INNER, DIAGONAL_CACHE_GB, SUBSLOT_SIZES, SUBSLOT_BUDGET
+    global CONVERSION, FUSED_KEY_INNER, DIAGONAL_CACHE_GB, SUBSLOT_SIZES, SUBSLOT_BUDGET, MEMO_GB
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2, help="timed tokens")
@@ -820,6 +826,8 @@ def main():
                          "[0, n) (one EvalMod over n slots instead of two over all); 0: every refresh over all slots")
     ap.add_argument("--subslot-budget", default=",".join(map(str, SUBSLOT_BUDGET)),
                     help="level budget CoeffToSlot,SlotToCoeff of the sub-slot refreshes")
+    ap.add_argument("--constant-memo-gb", type=float, default=MEMO_GB,
+                    help="budget of the memo of the layers' constant plaintexts in GB (0: encode at every use)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ckks", action="store_true", help="skip the key-switch, matvec and bootstrap side measurements")
@@ -834,6 +842,7 @@ def main():
     CONVERSION = args.conversion
     SUBSLOT_SIZES = tuple(int(v) for v in args.subslot_refresh.split(",") if int(v))
     SUBSLOT_BUDGET = tuple(int(v) for v in args.subslot_budget.split(","))
+    MEMO_GB = args.constant_memo_gb
     if len(SUBSLOT_BUDGET) != 2:
         ap.error("--subslot-budget takes two numbers")
     DIAGONAL_CACHE_GB = args.diagonal_cache_gb

@@ -89,6 +89,41 @@ class StateLayout:
         return v.reshape(self.heads, self.head_dim, self.state_size)
 
 
+class PlaintextMemo:
+    """Device plaintexts of constant slot vectors (masks, conv taps, biases,
+    per-head coefficients) kept across calls, keyed by the vector's non-zero
+    positions and values, the limb count and the scale: an encode of the same
+    vector at the same level and scale gives the same words, so a hit returns
+    the earlier plaintext.  Least recently used entries go beyond
+    `budget_bytes` of plaintext words."""
+
+    def __init__(self, cc, budget_bytes: float):
+        from collections import OrderedDict
+        self.cc, self.budget = cc, float(budget_bytes)
+        self.entries, self.bytes, self.hits, self.misses = OrderedDict(), 0, 0, 0
+
+    def get(self, values, level: int = 0, scale: float = 0.0):
+        c = self.cc
+        v = np.asarray(values, dtype=float)
+        nz = np.flatnonzero(v)
+        key = (v.shape[0], nz.tobytes(), v[nz].tobytes(), int(level), float(scale))
+        pt = self.entries.get(key)
+        if pt is not None:
+            self.entries.move_to_end(key)
+            self.hits += 1
+            return pt
+        self.misses += 1
+        pt = c.MakeCKKSPackedPlaintext(v, level=level, scale=scale)
+        nbytes = (c.n_q - level) * c.n * 8
+        if nbytes <= self.budget:
+            self.entries[key] = pt
+            self.bytes += nbytes
+            while self.bytes > self.budget:
+                (_, _, _, lv, _), _ = self.entries.popitem(last=False)
+                self.bytes -= (c.n_q - lv) * c.n * 8
+        return pt
+
+
 class PackedMamba2:
     """Encrypted Mamba-2 state update / readout / conv / RMSNorm over one CryptoContext.
 
@@ -111,6 +146,8 @@ class PackedMamba2:
         self._state_giant = L.state_size // self._state_baby
         self._mask_cache = {}
         self._state_diags = None
+        # a PlaintextMemo shared by the caller (None: encode every constant)
+        self.memo = None
 
     # ---- keys -------------------------------------------------------------
     def rotation_steps(self, norm_width: int = 0) -> list[int]:
@@ -142,11 +179,17 @@ class PackedMamba2:
             self._mask_cache[key] = m
         return self._mask_cache[key]
 
+    def plain(self, values, level: int = 0, scale: float = 0.0):
+        """A constant slot vector as a plaintext (through the memo when set)."""
+        if self.memo is not None:
+            return self.memo.get(values, level, scale)
+        return self.cc.MakeCKKSPackedPlaintext(np.asarray(values, dtype=float), level=level, scale=scale)
+
     def _plain_for(self, ct, values):
         """Plaintext at the level `ct` multiplies on (after its pending rescale)."""
         c = self.cc
         nq = ct.n_limbs() - (1 if ct.GetNoiseScaleDeg() >= 2 else 0)
-        return c.MakeCKKSPackedPlaintext(np.asarray(values, dtype=float), level=c.n_q - nq)
+        return self.plain(values, level=c.n_q - nq)
 
     def _mul_mask(self, ct, mask):
         return self.cc.EvalMult(ct, self._plain_for(ct, mask))
@@ -260,8 +303,8 @@ class PackedMamba2:
         if bias is not None:
             if acc.GetNoiseScaleDeg() >= 2:
                 c.RescaleInPlace(acc)
-            acc = c.EvalAdd(acc, c.MakeCKKSPackedPlaintext(np.asarray(bias, dtype=float), level=c.n_q - acc.n_limbs(),
-                                                           scale=acc.GetScalingFactor()))
+            acc = c.EvalAdd(acc, self.plain(np.asarray(bias, dtype=float), level=c.n_q - acc.n_limbs(),
+                                            scale=acc.GetScalingFactor()))
         return acc
 
     # ---- polynomial gates -------------------------------------------------
@@ -278,7 +321,7 @@ class PackedMamba2:
         u = self._mul_mask(x, a)
         if u.GetNoiseScaleDeg() >= 2:
             c.RescaleInPlace(u)
-        u = c.EvalAdd(u, c.MakeCKKSPackedPlaintext(b, level=c.n_q - u.n_limbs(), scale=u.GetScalingFactor()))
+        u = c.EvalAdd(u, self.plain(b, level=c.n_q - u.n_limbs(), scale=u.GetScalingFactor()))
         out = c.EvalChebyshevSeries(u, coeffs, -1.0, 1.0)
         return self._mul_mask(out, self._block_mask(lo_slot, hi_slot) if out_mask is None else out_mask)
 
@@ -300,7 +343,7 @@ class PackedMamba2:
             c.RescaleInPlace(v)
         shift = np.full(self.L.slots, fill)
         shift[:width] = eps
-        return c.EvalAdd(v, c.MakeCKKSPackedPlaintext(shift, level=c.n_q - v.n_limbs(), scale=v.GetScalingFactor()))
+        return c.EvalAdd(v, self.plain(shift, level=c.n_q - v.n_limbs(), scale=v.GetScalingFactor()))
 
     def scale_rows(self, x, y, width: int, weight):
         """x * y * weight on [0, width): the normalised, weighted vector."""

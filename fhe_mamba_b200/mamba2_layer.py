@@ -24,7 +24,7 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
-from .mamba import PackedMamba2, StateLayout
+from .mamba import PackedMamba2, PlaintextMemo, StateLayout
 
 
 def _silu(x):
@@ -218,7 +218,7 @@ class HeadPoly:
         t = pm._mul_mask(z, a)
         if t.GetNoiseScaleDeg() >= 2:
             c.RescaleInPlace(t)
-        t = c.EvalAdd(t, c.MakeCKKSPackedPlaintext(b, level=c.n_q - t.n_limbs(), scale=t.GetScalingFactor()))
+        t = c.EvalAdd(t, pm.plain(b, level=c.n_q - t.n_limbs(), scale=t.GetScalingFactor()))
         basis = {1: t}
 
         def T(i):  # T_2k = 2 T_k^2 - 1, T_2k+1 = 2 T_k+1 T_k - T_1
@@ -241,8 +241,7 @@ class HeadPoly:
             c.RescaleInPlace(acc)
         const = np.zeros(n)
         const[:heads] = self.coeffs[0]
-        return c.EvalAdd(acc, c.MakeCKKSPackedPlaintext(const, level=c.n_q - acc.n_limbs(),
-                                                         scale=acc.GetScalingFactor()))
+        return c.EvalAdd(acc, pm.plain(const, level=c.n_q - acc.n_limbs(), scale=acc.GetScalingFactor()))
 
 
 class Mamba2Polys:
@@ -448,7 +447,8 @@ class EncryptedMamba2Layer:
     NEEDS = {"rms": 14, "u": 2, "proj": 19, "xbc": 2, "pack": 8, "state": 4, "y": 2, "gn": 2}
 
     def __init__(self, cc, W: Mamba2Weights, P: Mamba2Polys, passes: int = 2, margin: int = 4,
-                 cache: PlaintextCache | None = None, needs: dict | None = None, device_diagonals: bool = True):
+                 cache: PlaintextCache | None = None, needs: dict | None = None, device_diagonals: bool = True,
+                 memo=None):
         self.cc, self.W, self.P = cc, W, P
         # Diagonal plaintexts generated on the device from the weights (the
         # context's MakeReplicatedDiagonals) instead of built on the host and
@@ -470,6 +470,7 @@ class EncryptedMamba2Layer:
             raise ValueError("packed SSM inputs do not fit the slots")
         self.pm = PackedMamba2(cc, self.layout, b_base=E, c_base=E + S, head_base=self.dt_base,
                                decay_base=self.decay_base)
+        self.pm.memo = memo  # constant plaintexts (masks, taps, biases) shared across layers and tokens
         self.refreshes = self.two_pass_refreshes = 0
         self.site_refreshes = {}  # refreshes by site name
         self._lin = {}
@@ -635,8 +636,7 @@ class EncryptedMamba2Layer:
             c.RescaleInPlace(dtv)
         bias_dt = np.zeros(c.slots)
         bias_dt[:H] = W["dt_bias"]
-        dtv = c.EvalAdd(dtv, c.MakeCKKSPackedPlaintext(bias_dt, level=c.n_q - dtv.n_limbs(),
-                                                        scale=dtv.GetScalingFactor()))
+        dtv = c.EvalAdd(dtv, self.pm.plain(bias_dt, level=c.n_q - dtv.n_limbs(), scale=dtv.GetScalingFactor()))
         gates = getattr(P, "gates", None)
         if gates is not None:  # joint gates: write and decay from one shared factor
             dtv = self._fit(dtv, gates.levels, bounds["dt"], "dt", H)
@@ -908,11 +908,13 @@ class EncryptedMamba2Model:
     selection around them."""
 
     def __init__(self, cc, model: Mamba2Model, passes: int = 2, cache_gb: float = 0.0, margin: int = 4,
-                 needs: dict | None = None, device_diagonals: bool = True):
+                 needs: dict | None = None, device_diagonals: bool = True, memo_gb: float = 4.0):
         self.cc, self.m = cc, model
         self.cache = PlaintextCache(cache_gb * 2 ** 30)
+        # the layers' constant slot vectors, encoded once per level and scale
+        self.memo = PlaintextMemo(cc, memo_gb * 2 ** 30) if memo_gb > 0 else None
         self.layers = [EncryptedMamba2Layer(cc, W, P, passes=passes, margin=margin, cache=self.cache, needs=needs,
-                                            device_diagonals=device_diagonals)
+                                            device_diagonals=device_diagonals, memo=self.memo)
                        for W, P in zip(model.layers, model.polys)]
         self.state = [([None] * (W.conv_kernel - 1), None) for W in model.layers]
         self.tokens, self.margins = [], []

@@ -115,3 +115,33 @@ def test_subslot_refresh_schedule():
             picked, ehf = em.select(em.step(tok))
             assert picked == int(np.argmax(logits)) and np.max(np.abs(ehf - hf)) < 1e-10
         assert 1 <= cc.subslot_refreshes <= em.refreshes()
+
+
+def test_plaintext_memo():
+    """The model's constant slot vectors (masks, taps, biases) come from the
+    shared memo after the first token: same results to rounding, most lookups
+    hits, and a budget too small for any entry only encodes."""
+    from fhe_mamba_b200.mamba import PlaintextMemo
+    from fhe_mamba_b200.mamba2_layer import EncryptedMamba2Model, Mamba2Model
+    m = Mamba2Model(layers=2, d_model=64, d_state=32, heads=16, vocab=128, std=0.1, fused_decay=True)
+    outs = {}
+    for memo_gb in (0.0, 4.0):
+        cc = SlotContext(2048, refresh_noise=0.0)
+        em = EncryptedMamba2Model(cc, m, memo_gb=memo_gb)
+        cc.EvalRotateKeyGen(em.rotation_steps())
+        outs[memo_gb] = [em.select(em.step(tok))[1] for tok in (3, 17, 5)]
+        if memo_gb:
+            assert em.memo.hits > 2 * em.memo.misses and 0 < em.memo.bytes <= memo_gb * 2 ** 30
+        else:
+            assert em.memo is None
+    for a, b in zip(outs[0.0], outs[4.0]):
+        assert np.max(np.abs(a - b)) < 1e-12
+    cc = SlotContext(2048, refresh_noise=0.0)
+    tiny = PlaintextMemo(cc, 1.0)
+    v = np.zeros(cc.slots)
+    v[:5] = 1.0
+    assert tiny.get(v, 3) is not tiny.get(v, 3) and tiny.misses == 2 and not tiny.entries
+    memo = PlaintextMemo(cc, 2 * (cc.n_q - 3) * cc.n * 8)
+    a = memo.get(v, 3)
+    assert memo.get(v.copy(), 3) is a and memo.get(v, 4) is not a and memo.get(v, 3, scale=2.0) is not a
+    assert len(memo.entries) == 2 and memo.bytes <= 2 * (cc.n_q - 3) * cc.n * 8
