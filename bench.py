@@ -66,7 +66,7 @@ DIAGONAL_CACHE_GB = 0.0
 FUSED_KEY_INNER = False
 # Budget of the memo of the layers' constant plaintexts (masks, taps, biases
 # by level and scale; --constant-memo-gb, 0: encode at every use).
-MEMO_GB = 4.0
+MEMO_GB = 16.0
 # Slot counts of the sub-slot refreshes (--subslot-refresh): a refresh of a
 # value known to be zero outside [0, n) bootstraps n slots with one EvalMod.
 # Two-pass refresh at N = 2^16: 158 ms over all slots, 115 ms over 4096, 105 ms

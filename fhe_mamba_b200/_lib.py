@@ -124,6 +124,7 @@ SIGNATURES = {
     "fhe_ctx_level_counts": [vp, i32, vp, u32],
     "fhe_ctx_set_conversion": [vp, i32],
     "fhe_ctx_set_keyswitch_fusion": [vp, i32],
+    "fhe_ctx_set_giant_hoisting": [vp, i32],
     "fhe_device_trim": [i32],
     "fhe_tc_timeouts": [vp],
     "fhe_kernel_launches": [ctypes.POINTER(ctypes.c_uint64)],

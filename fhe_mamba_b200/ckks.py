@@ -375,6 +375,12 @@ class CryptoContext:
         (True) or in a separate kernel (False); the results are identical."""
         call("fhe_ctx_set_keyswitch_fusion", self.h, int(bool(fused)))
 
+    def SetGiantStepHoisting(self, on: bool):
+        """Giant steps of a linear transform share one ModDown (True, the
+        default) or each take a full key switch (False); the results agree
+        within the key switching noise."""
+        call("fhe_ctx_set_giant_hoisting", self.h, int(bool(on)))
+
     def level_counts(self):
         """The ModUps, key inner products, rescales and tensor products since the
         last counter reset, by the number of live Q limbs they ran at:

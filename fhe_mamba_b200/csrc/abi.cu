@@ -771,6 +771,10 @@ int fhe_ctx_set_keyswitch_fusion(fhe_ctx* ctx, int32_t fused) {
   return guarded([&] { ckks(ctx).fused_key_inner = fused != 0; });
 }
 
+int fhe_ctx_set_giant_hoisting(fhe_ctx* ctx, int32_t on) {
+  return guarded([&] { ckks(ctx).hoist_giant_moddown = on != 0; });
+}
+
 int fhe_tc_timeouts(uint64_t* count) {
   return guarded([&] {
     fhe::require(count != nullptr, "null count");

@@ -891,6 +891,62 @@ std::unique_ptr<Ct> Ckks::linear_transform(const Ct& a_in, const std::vector<con
   out->scale = a.scale * pscale;
   out->noise_deg = a.noise_deg + 1;
   const PrimeMap pm{nq, ctx.L};
+  uint32_t rotating = 0;
+  for (uint32_t g = 0; g < G; ++g) rotating += galois_for_step(((int64_t)g * b - giant_offset) * stride) != 1;
+  if (hoist_giant_moddown && rotating >= 2) {
+    // sum_g sigma_g(KS(c1_g)) = ModDown(sum_g sigma_g(inner_g)) + sum_g sigma_g(c0_g):
+    // the key inner products accumulate in the extended basis (Q and P limbs)
+    const uint32_t K = ctx.K, w = nq + K;
+    LevelTables& T = level(nq);
+    uint64_t* ext = ws(0, (size_t)T.D * w * n);
+    uint64_t* acc = ws(2, (size_t)2 * (ctx.L + K) * n);   // one giant's inner product [2][w][N]
+    uint64_t* sum = ws(25, (size_t)2 * w * n);            // their automorphisms summed [2][w][N]
+    uint64_t* c0 = ws(26, cs);                            // sum of sigma_g(c0_g) [nq][N]
+    uint64_t* t = ws(27, (size_t)2 * w * n);              // one permuted inner product
+    const PrimeMap pe{nq, ctx.L};                         // extended limbs: Q then P primes
+    bool first = true, first_id = true;
+    for (uint32_t g = 0; g < G; ++g) {
+      const uint64_t* ig = inner + (size_t)g * 2 * cs;
+      const int64_t amount = ((int64_t)g * b - giant_offset) * stride;
+      const uint64_t gal = galois_for_step(amount);
+      if (gal == 1) {  // the identity giant joins the output directly
+        if (first_id)
+          FHE_CUDA(cudaMemcpyAsync(out->data(), ig, 2 * cs * 8, cudaMemcpyDeviceToDevice, ctx.stream));
+        else
+          launch_ew(Ew::Add, out->data(), cs, ig, cs, out->data(), cs, 2, nq, n, pm, ctx.d_mod.as<Modulus>(),
+                    ctx.stream);
+        first_id = false;
+        continue;
+      }
+      auto it = rot_.find(gal);
+      require(it != rot_.end(), "missing rotation key for giant step " + std::to_string(amount), -4);
+      ++counters.rotations;
+      modup(ig + cs, nq, ext);
+      ++counters.key_inner;
+      ++counters.key_inner_at[Counters::slot(nq)];
+      launch_key_inner(ext, T.D, w, it->second.as<uint64_t>(), ctx.L + K, pe, acc, n, ctx.d_mod.as<Modulus>(),
+                       ctx.stream);
+      if (first) {
+        launch_automorphism(acc, (size_t)w * n, sum, (size_t)w * n, 2, w, ctx.log_n, gal, ctx.stream);
+        launch_automorphism(ig, cs, c0, cs, 1, nq, ctx.log_n, gal, ctx.stream);
+      } else {
+        launch_automorphism(acc, (size_t)w * n, t, (size_t)w * n, 2, w, ctx.log_n, gal, ctx.stream);
+        launch_ew(Ew::Add, sum, (size_t)w * n, t, (size_t)w * n, sum, (size_t)w * n, 2, w, n, pe,
+                  ctx.d_mod.as<Modulus>(), ctx.stream);
+        launch_automorphism(ig, cs, t, cs, 1, nq, ctx.log_n, gal, ctx.stream);
+        launch_ew(Ew::Add, c0, cs, t, cs, c0, cs, 1, nq, n, pm, ctx.d_mod.as<Modulus>(), ctx.stream);
+      }
+      first = false;
+    }
+    uint64_t* u = ws(4, 2 * cs);
+    moddown_pair(sum, nq, u, cs, c0);
+    if (first_id)
+      FHE_CUDA(cudaMemcpyAsync(out->data(), u, 2 * cs * 8, cudaMemcpyDeviceToDevice, ctx.stream));
+    else
+      launch_ew(Ew::Add, out->data(), cs, u, cs, out->data(), cs, 2, nq, n, pm, ctx.d_mod.as<Modulus>(),
+                ctx.stream);
+    return out;
+  }
   for (uint32_t g = 0; g < G; ++g) {
     const uint64_t* ig = inner + (size_t)g * 2 * cs;
     const int64_t amount = ((int64_t)g * b - giant_offset) * stride;

@@ -73,6 +73,12 @@ class Ckks {
   // Key inner product of the Q limbs folded into ModDown's combine epilogue
   // (the accumulator's Q rows are never written and re-read); same words.
   bool fused_key_inner = false;
+  // Giant steps of a linear transform share ONE ModDown: each rotating giant's
+  // key inner product is permuted by its automorphism in the extended basis
+  // and summed there (ModDown is linear and commutes with automorphisms up
+  // to its rounding), instead of a ModDown per giant.  Different words than
+  // a ModDown per giant; the same noise bound.
+  bool hoist_giant_moddown = true;
 
   // FLEXIBLEAUTO scaling factor of a fresh ciphertext with nq live limbs.
   double level_scale(uint32_t nq) const { return sf_[ctx.L - nq]; }

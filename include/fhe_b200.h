@@ -352,6 +352,16 @@ int fhe_device_trim(int32_t device);
  * NTT's KSK_DOT / KSK_DOT_ACC modes (experiments/ntt_warp_tail/probe.cu:70-73),
  * which fuse the product into the ModUp side instead.  Identical words. */
 int fhe_ctx_set_keyswitch_fusion(fhe_ctx* ctx, int32_t fused);
+/* on != 0 (the default): the rotating giant steps of fhe_linear_transform
+ * (and of bootstrapping's CoeffToSlot / SlotToCoeff groups) share one
+ * ModDown: each giant's key inner product is permuted by its automorphism
+ * in the extended Q*P basis and summed there, the way OpenFHE's
+ * EvalFastRotationExt / KeySwitchDown pair hoists them in its bootstrapping
+ * linear transforms; the sum is brought down once.  on == 0: a full key
+ * switch (with its ModDown) per giant, the composition the reference's
+ * EvalLinearTransform performs.  Results agree within the key switching
+ * noise, not word for word. */
+int fhe_ctx_set_giant_hoisting(fhe_ctx* ctx, int32_t on);
 /* Number of tensor-core conversion blocks whose bounded wait for their MMA
  * ran out (their outputs were skipped); 0 on a healthy device. */
 int fhe_tc_timeouts(uint64_t* count);

@@ -16,7 +16,17 @@ pytestmark = pytest.mark.gpu
 SEED = 99
 
 
-def test_linear_transform_matches_oracle_small(oracle):
+def _ext_add(a, b, q, p):
+    """a + b over extended limbs ([..., nq + K, N]: Q primes, then P primes)."""
+    primes = np.array(list(q[:a.shape[-2] - len(p)]) + list(p), dtype=np.uint64)[:, None]
+    return (a + b) % primes
+
+
+@pytest.mark.parametrize("hoist", [False, True])
+def test_linear_transform_matches_oracle_small(oracle, hoist):
+    """hoist False: a full key switch per giant step; True (the default): the
+    rotating giants' key inner products permuted and summed in the extended
+    basis, one ModDown for all of them plus the permuted c0 parts."""
     from fhe_mamba_b200 import CCParams, CryptoContext
     log_n, depth, sb, fb, dnum = 12, 6, 45, 55, 2
     cc = CryptoContext(CCParams(ring_dim=1 << log_n, multiplicative_depth=depth, scaling_mod_size=sb,
@@ -41,12 +51,15 @@ def test_linear_transform_matches_oracle_small(oracle):
     for d, p in zip(diags, dpts):
         if d is not None:
             assert np.array_equal(p.residues(), oc.encode(d, cc.level_scale(), cc.n_q))
+    cc.SetGiantStepHoisting(hoist)
     out = cc.EvalLinearTransform(ct, dpts, baby, giant)
+    cc.SetGiantStepHoisting(True)
     # oracle composition of the same schedule
     a = ct.residues()
+    nq = a.shape[1]
     keys = {st: oc.rot_key(SEED, s, sn, oc.galois(st)) for st in steps}
     babies = [a] + [oc.rotate(a, oc.galois(j), keys[j]) for j in range(1, baby)]
-    total = None
+    total, ext_sum, c0_sum = None, None, None
     for g in range(giant):
         inner = None
         for j in range(baby):
@@ -55,9 +68,20 @@ def test_linear_transform_matches_oracle_small(oracle):
                 continue
             t = oc.mul_plain(babies[j], p.residues())
             inner = t if inner is None else oc.add(inner, t)
+        if g and hoist:
+            gal = oc.galois(g * baby)
+            acc = oc.automorphism(oc.key_inner(oc.modup(inner[1], nq), nq, keys[g * baby]), gal)
+            c0 = oc.automorphism(inner[0], gal)
+            ext_sum = acc if ext_sum is None else _ext_add(ext_sum, acc, cc.q, cc.p)
+            c0_sum = c0 if c0_sum is None else oc.add(c0_sum[None], c0[None])[0]
+            continue
         if g:
             inner = oc.rotate(inner, oc.galois(g * baby), keys[g * baby])
         total = inner if total is None else oc.add(total, inner)
+    if hoist:
+        u = np.stack([oc.moddown(ext_sum[0], nq), oc.moddown(ext_sum[1], nq)])
+        u[0] = oc.add(u[0][None], c0_sum[None])[0]
+        total = oc.add(total, u)
     assert np.array_equal(out.residues(), total)
     y = cc.Decrypt(out).GetRealPackedValue()
     assert np.max(np.abs(y[:m] - W @ x)) < 1e-4
