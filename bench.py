@@ -581,8 +581,10 @@ class TokenLoop:
         self.cc.SetKeySwitchFusion(FUSED_KEY_INNER)
         self.cc.KeyGen(41 + seed)
         self.cc.EvalBootstrapSetup((4, 4), sparse_hamming_weight=sparse_h)
-        # sub-slot refreshes need a fully packed context and the uniform secret
-        self.subslot = () if (classical128 or sparse_h) else tuple(SUBSLOT_SIZES)
+        # sub-slot refreshes run with the uniform secret; at ring 2^17 (keys of
+        # 478 MB) only the largest size, whose keys cover every refresh site
+        sizes = SUBSLOT_SIZES[:1] if classical128 else SUBSLOT_SIZES
+        self.subslot = () if sparse_h else tuple(n for n in sizes if n <= self.cc.slots // 2)
         for n in self.subslot:
             self.cc.EvalBootstrapSubslotSetup(n, SUBSLOT_BUDGET)
         self.cc.EvalBootstrapKeyGen()
@@ -742,7 +744,8 @@ def config_dict(args):
             "secret_key_dist": f"sparse-encapsulated h={args.sparse_h}" if args.sparse_h else "uniform-ternary",
             "l2": "inputs larger than L2 (keys ~36 GB, diagonals generated on the device)",
             "diagonal_cache_gb": args.diagonal_cache_gb,
-            "subslot_refresh": [] if args.security == "128-classic" or args.sparse_h else list(SUBSLOT_SIZES),
+            "subslot_refresh": [] if args.sparse_h else list(SUBSLOT_SIZES[:1] if args.security == "128-classic"
+                                                              else SUBSLOT_SIZES),
             "subslot_budget": list(SUBSLOT_BUDGET), "constant_memo_gb": args.constant_memo_gb,
             "parallelism": "one token-loop replica per GPU"}
 

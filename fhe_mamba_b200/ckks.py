@@ -258,10 +258,10 @@ class CryptoContext:
              int(correction_factor), int(bool(slots_to_coeffs_first)), int(sparse_hamming_weight))
 
     def EvalBootstrapSubslotSetup(self, slots: int, level_budget=(4, 4), correction_factor: int = 0):
-        """A sub-slot refresh for inputs zero outside slots [0, slots) (a power of
-        two <= N/4): one EvalMod instead of two, the same levels as the full
-        bootstrap, output zero outside [0, slots).  EvalBootstrapKeyGen
-        generates its keys; refresh(..., support=) picks it."""
+        """A sub-slot refresh for inputs zero outside slots [0, slots) (a power
+        of two <= half the context's slots): one EvalMod instead of two, the
+        same levels as the full bootstrap, output zero outside [0, slots).
+        EvalBootstrapKeyGen generates its keys; refresh(..., support=) picks it."""
         call("fhe_bootstrap_subslot_setup", self.h, int(slots), int(level_budget[0]), int(level_budget[1]),
              int(correction_factor))
         self.subslot_sizes = tuple(sorted(set(self.subslot_sizes) | {int(slots)}))

@@ -97,8 +97,8 @@ Bootstrapper::Bootstrapper(Ckks& ck, const BootParams& p) : ck_(ck), p_(p) {
   require(n >= 2 && n <= ctx.n / 2 && (n & (n - 1)) == 0, "bootstrapping needs a power-of-two slot count <= N/2",
           -1);
   if (p_.slots) {
-    require(ctx.slots == ctx.n / 2, "a sub-slot refresh needs a fully packed context", -1);
-    require(n <= ctx.n / 4, "sub-slot refresh slots must be a power of two <= N/4", -1);
+    // 2n of the context's slots hold the real and imaginary halves
+    require(n <= ctx.slots / 2, "sub-slot refresh slots must be a power of two <= half the context's slots", -1);
     require(!p_.s2c_first && !p_.sparse_h, "a sub-slot refresh combines with neither S2C-first nor a sparse secret",
             -1);
     single_ = true;
@@ -396,8 +396,10 @@ uint64_t Bootstrapper::aux_galois(const Group& g) const {
 }
 
 std::unique_ptr<Ct> Bootstrapper::replicate(const Ct& x) {
+  // copies over the context's own slots: a sparsely packed context's vector
+  // already repeats with period ctx.slots over the N/2 slots of the ring
   auto r = ck_.clone(x);
-  for (uint32_t j = 1; j < trace_; j *= 2) {
+  for (uint32_t j = 1; j < ck_.ctx.slots / n_; j *= 2) {
     auto t = ck_.rotate(*r, ck_.galois_for_full_step((int64_t)j * n_));
     r = ck_.add(*r, *t, false);
   }

@@ -38,8 +38,8 @@ struct BootParams {
   // ModRaise and back right after it, so |I| <= (h + 1) / 2 and EvalMod needs
   // a far smaller interval, degree and depth.
   uint32_t sparse_h = 0;
-  // Sub-slot refresh in a fully packed context: 0 bootstraps all of the
-  // context's slots; a power of two n <= N/4 bootstraps inputs whose values
+  // Sub-slot refresh: 0 bootstraps all of the context's slots; a power of
+  // two n <= half the context's slots bootstraps inputs whose values
   // sit in slots [0, n) (zeros elsewhere), replicated with period n by the
   // caller: the sparse-packing pipeline on n slots with ONE EvalMod (the real
   // and imaginary parts of CoeffToSlot's output side by side in 2n slots;
@@ -65,7 +65,8 @@ class Bootstrapper {
   // Slots this bootstrapper covers (the context's, or the sub-slot count).
   uint32_t slots() const { return n_; }
   // x replicated with period slots() over the context's slots (x zero
-  // outside [0, slots())): log2(N / (2 slots)) rotate-and-add doublings.
+  // outside [0, slots())): log2(context slots / slots()) rotate-and-add
+  // doublings.
   std::unique_ptr<Ct> replicate(const Ct& x);
 
   // The four steps of bootstrap(), each on its own (the pieces that

@@ -389,11 +389,12 @@ int fhe_tc_timeouts(uint64_t* count);
  * secret throughout. */
 int fhe_bootstrap_setup(fhe_ctx* ctx, uint32_t budget_cts, uint32_t budget_stc, uint32_t slots,
                         int32_t correction, int32_t s2c_first, uint32_t sparse_h);
-/* Sub-slot refresh for a fully packed context (no reference counterpart: the
- * reference bootstraps every refresh over all N/2 slots, packed_fideslib.cpp:1084):
- * a bootstrapper for inputs whose values sit in slots [0, slots) with zeros
- * elsewhere, slots a power of two <= N/4.  It bootstraps the input replicated
- * with period `slots` as a sparsely packed ciphertext (trace after ModRaise)
+/* Sub-slot refresh (no reference counterpart: the reference bootstraps every
+ * refresh over all of the context's slots, packed_fideslib.cpp:1084): a
+ * bootstrapper for inputs whose values sit in slots [0, slots) with zeros
+ * elsewhere, slots a power of two <= half the context's slot count (fully or
+ * sparsely packed).  It bootstraps the input replicated with period `slots`
+ * as a sparsely packed ciphertext (trace after ModRaise)
  * with ONE EvalMod (the real and imaginary parts side by side in 2*slots
  * slots; the split folded into the last CoeffToSlot group, the merge into the
  * first SlotToCoeff group) and returns zeros outside [0, slots) (a mask folded

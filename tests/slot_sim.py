@@ -128,7 +128,7 @@ class SlotContext:
         """The levels a sub-slot refresh returns follow its level budget: each
         transform level below the full refresh's {4, 4} is one more left."""
         if slots & (slots - 1) or not 2 <= slots <= self.slots // 2:
-            raise SimError("sub-slot refresh slots must be a power of two <= N/4")
+            raise SimError("sub-slot refresh slots must be a power of two <= half the slots")
         self.subslot_sizes = tuple(sorted(set(self.subslot_sizes) | {int(slots)}))
         self.subslot_extra[int(slots)] = 8 - int(level_budget[0]) - int(level_budget[1])
 

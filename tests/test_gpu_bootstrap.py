@@ -340,6 +340,32 @@ def test_subslot_refresh():
     cc.close()
 
 
+def test_subslot_refresh_in_sparse_context():
+    """A sparsely packed context (1024 of N/2 = 2048 slots, the classical-128
+    layout at a small ring) takes sub-slot refreshes too: 256 slots, values
+    back on [0, support) within the two-pass precision, zeros from 256 on,
+    the limbs of the context's own refresh."""
+    from fhe_mamba_b200 import CCParams, CryptoContext, InvalidArgument
+    cc = CryptoContext(CCParams(ring_dim=1 << 12, multiplicative_depth=25, scaling_mod_size=59,
+                                first_mod_size=60, num_large_digits=3, batch_size=1024))
+    assert cc.slots == 1024
+    cc.KeyGen(SEED)
+    cc.EvalBootstrapSetup((4, 4))
+    cc.EvalBootstrapSubslotSetup(256, (4, 4))
+    with pytest.raises(InvalidArgument):
+        cc.EvalBootstrapSubslotSetup(1024, (4, 4))  # above half the slots
+    cc.EvalBootstrapKeyGen()
+    x = np.zeros(cc.slots)
+    x[:200] = np.random.default_rng(43).uniform(-5, 5, 200)
+    ct = cc.Encrypt(cc.MakeCKKSPackedPlaintext(x))
+    cc.LevelReduceInPlace(ct, cc.n_q - 4)
+    out = cc.EvalRefresh(ct, 8.0, passes=2, support=200)
+    assert out.n_limbs() == cc.EvalRefresh(ct, 8.0, passes=2).n_limbs()
+    y = cc.Decrypt(out).GetRealPackedValue()
+    assert np.max(np.abs(y[:200] - x[:200])) < 1e-5 and np.max(np.abs(y[256:])) < 1e-5
+    cc.close()
+
+
 def test_bootstrap_at_token_loop_parameters():
     """The token loop's own parameter set (N = 2^16, 2^15 slots, depth 44,
     59/60-bit primes, dnum 3, level budget {4, 4}, uniform ternary secret): a
