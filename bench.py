@@ -581,17 +581,19 @@ class TokenLoop:
         self.cc.SetKeySwitchFusion(FUSED_KEY_INNER)
         self.cc.KeyGen(41 + seed)
         self.cc.EvalBootstrapSetup((4, 4), sparse_hamming_weight=sparse_h)
-        # sub-slot refreshes run with the uniform secret; at ring 2^17 (keys of
-        # 478 MB) only the largest size, whose keys cover every refresh site
-        sizes = SUBSLOT_SIZES[:1] if classical128 else SUBSLOT_SIZES
-        self.subslot = () if sparse_h else tuple(n for n in sizes if n <= self.cc.slots // 2)
+        # sub-slot refreshes run with the uniform secret; not at ring 2^17, where
+        # their keys (478 MB each) next to the loop's ran the B200 out of memory
+        self.subslot = () if (sparse_h or classical128) else tuple(SUBSLOT_SIZES)
         for n in self.subslot:
             self.cc.EvalBootstrapSubslotSetup(n, SUBSLOT_BUDGET)
         self.cc.EvalBootstrapKeyGen()
         # ring 2^17 doubles every key and ciphertext: a smaller diagonal cache
         if cache_gb is None:
             cache_gb = DIAGONAL_CACHE_GB
-        self.em = EncryptedMamba2Model(self.cc, self.model, passes=passes, cache_gb=cache_gb, memo_gb=MEMO_GB)
+        # ring 2^17 doubles every plaintext: the memo takes the 8 GB the former
+        # diagonal cache held there
+        self.em = EncryptedMamba2Model(self.cc, self.model, passes=passes, cache_gb=cache_gb,
+                                       memo_gb=min(MEMO_GB, 8.0) if classical128 else MEMO_GB)
         self.cc.EvalRotateKeyGen(self.em.rotation_steps())
         self.cc.synchronize()
         self.setup_seconds = time.perf_counter() - t0
@@ -744,8 +746,7 @@ def config_dict(args):
             "secret_key_dist": f"sparse-encapsulated h={args.sparse_h}" if args.sparse_h else "uniform-ternary",
             "l2": "inputs larger than L2 (keys ~36 GB, diagonals generated on the device)",
             "diagonal_cache_gb": args.diagonal_cache_gb,
-            "subslot_refresh": [] if args.sparse_h else list(SUBSLOT_SIZES[:1] if args.security == "128-classic"
-                                                              else SUBSLOT_SIZES),
+            "subslot_refresh": [] if args.sparse_h or args.security == "128-classic" else list(SUBSLOT_SIZES),
             "subslot_budget": list(SUBSLOT_BUDGET), "constant_memo_gb": args.constant_memo_gb,
             "parallelism": "one token-loop replica per GPU"}
 
