@@ -145,3 +145,26 @@ def test_plaintext_memo():
     a = memo.get(v, 3)
     assert memo.get(v.copy(), 3) is a and memo.get(v, 4) is not a and memo.get(v, 3, scale=2.0) is not a
     assert len(memo.entries) == 2 and memo.bytes <= 2 * (cc.n_q - 3) * cc.n * 8
+
+
+def test_subslot_supports_over_the_horizon():
+    """28 greedy tokens of the small loop with sub-slot refreshes over 256 and
+    512 of 2048 slots: every declared support holds on every token, through
+    the carried states' own (full-slot) refreshes, and the loop stays equal to
+    the fp64 polynomial path."""
+    from fhe_mamba_b200.mamba2_layer import EncryptedMamba2Model, Mamba2Model
+    m = Mamba2Model(layers=2, d_model=64, d_state=32, heads=16, vocab=128, std=0.1, fused_decay=True)
+    cc = SlotContext(2048, refresh_noise=0.0)
+    cc.EvalBootstrapSubslotSetup(512)
+    cc.EvalBootstrapSubslotSetup(256)
+    em = EncryptedMamba2Model(cc, m)
+    cc.EvalRotateKeyGen(em.rotation_steps())
+    state, tok = m.initial_state(), 3
+    for _ in range(28):
+        hf, logits, state = m.plain_token(tok, state)
+        picked, ehf = em.select(em.step(tok))
+        assert picked == int(np.argmax(logits)) and np.max(np.abs(ehf - hf)) < 1e-9
+        tok = picked
+    full = em.refreshes() - cc.subslot_refreshes
+    assert cc.subslot_refreshes > 0 and full > 0  # the states refresh over all slots
+    assert sum(layer.site_refreshes.get("state", 0) for layer in em.layers) == full
